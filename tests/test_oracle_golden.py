@@ -1,0 +1,145 @@
+"""Pins the CPU oracle against outputs of the reference's own code (fixtures made by golden/make_golden.py)."""
+import numpy as np
+
+from conftest import golden_groups
+from oracle import folded_moe_oracle as O
+
+
+def test_e4m3_table_roundtrip():
+    codes = np.arange(256, dtype=np.uint8)
+    vals = O.e4m3_to_f32(codes)
+    ok = ~np.isnan(vals)
+    back = O.f32_to_e4m3(vals[ok])
+    # -0 and +0 keep their sign bit; every finite code round-trips
+    assert np.array_equal(back, codes[ok])
+    assert vals[0x7E] == 448.0 and vals[0x01] == 2.0 ** -9
+
+
+def test_dequant_bit_exact(golden):
+    g0 = golden_groups(golden)[0]
+    for tag, sfx in (("gu", "s_gu"), ("down", "s_down")):
+        got = O.unpack_nvfp4(g0[f"{sfx}.weight"], g0[f"{sfx}.weight_scale"], g0[f"{sfx}.weight_scale_2"])
+        ref = golden[f"ref.dequant_{tag}_g0"]
+        assert got.dtype == np.float32
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"{tag}: fp32 bit patterns differ"
+
+
+def test_pack_known_answer(golden):
+    p, s, s2 = O.pack_nvfp4(golden["ref.pack.in"])
+    assert np.array_equal(p, golden["ref.pack.packed"])
+    assert np.array_equal(s, golden["ref.pack.scale"])
+    assert np.float32(s2) == golden["ref.pack.scale2"]
+    dq = O.unpack_nvfp4(p, s, s2)
+    assert np.array_equal(dq.view(np.uint32), golden["ref.pack.dequant"].view(np.uint32))
+    # the tiny block quantises to a zero scale code with saturated nibbles: signed zeros are legal values
+    assert np.all(golden["ref.pack.scale"][3, 1] == 0) and np.all(dq[3, 16:32] == 0.0)
+
+
+def test_keys_match_reference(golden):
+    names = ("r_s1", "r_perm", "r_inv", "r_s2", "c_s1", "c_perm", "c_inv", "c_s2")
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    seen = 0
+    for key in golden:
+        if not key.startswith("ref.keys.") or not key.endswith(".r_s1"):
+            continue
+        _, _, tag, gs, ms, _ = key.split(".")
+        g, m = int(gs[1:]), int(ms[1:])
+        rows, cols = (2 * i, h) if tag == "gu" else (h, i)
+        sb = O.group_seed_bases(g)[0 if tag == "gu" else 1]
+        keys = O.expert_keys(rows, cols, m, sb)
+        for nm, arr in zip(names, keys):
+            assert np.array_equal(arr.astype(np.int64), golden[f"ref.keys.{tag}.g{g}.m{m}.{nm}"].astype(np.int64)), (key, nm)
+        seen += 1
+    assert seen == 4
+
+
+def test_fold_unbind_roundtrip():
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((256, 128)).astype(np.float32)
+    keys = O.expert_keys(256, 128, 2, 101)
+    back = O.unbind_2d(O.fold_2d(w, keys), keys)
+    assert np.abs(back - w).max() < 1e-5
+
+
+def test_reconstruction_matches_reference(golden):
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    groups = golden_groups(golden)
+    seen = 0
+    for key in golden:
+        if not key.startswith("ref.recon_") or not key.endswith(".gu"):
+            continue
+        tg, gs, ms, _ = key[len("ref.recon_"):].split(".")
+        g, m = int(gs[1:]), int(ms[1:])
+        gu, dn = O.reconstruct_expert(groups[g], g, m, h, i, include_tail=(tg == "tail"))
+        for got, ref in ((gu, golden[key]), (dn, golden[key[:-3] + ".down"])):
+            # same fp32 expression; only the BLAS summation order inside the H_128 / U.V matmuls may differ
+            assert np.abs(got - ref).max() <= 2e-6 * max(1.0, np.abs(ref).max()) + 1e-7
+        seen += 1
+    assert seen == 3
+
+
+def test_activation_space_equals_weight_space(golden):
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    groups = golden_groups(golden)
+    x = golden["x"]
+    g, m = len(groups) - 1, k - 1
+    gu, dn = O.reconstruct_expert(groups[g], g, m, h, i)
+    z = x @ gu.T
+    y_w = (O.silu(z[:, :i]) * z[:, i:]) @ dn.T
+    y_a = O.expert_forward_activation_space(x, groups[g], g, m, h, i)
+    assert np.linalg.norm(y_a - y_w) <= 1e-5 * np.linalg.norm(y_w)
+
+
+def test_router_matches_reference(golden):
+    top_k = int(golden["meta"][5])
+    for logits in (golden["ref.router.logits"], O.router_logits_fixed(golden["x"], golden["router_w"])):
+        ids, gates = O.router_softmax_topk(logits, top_k)
+        assert np.array_equal(ids, golden["ref.router.softmax_ids"])
+        assert np.allclose(gates, golden["ref.router.softmax_gates"], rtol=1e-5, atol=1e-7)
+        ids, gates = O.router_sigmoid_topk(logits, golden["e_bias"], top_k)
+        assert np.array_equal(ids, golden["ref.router.sigmoid_ids"])
+        assert np.allclose(gates, golden["ref.router.sigmoid_gates"], rtol=1e-5, atol=1e-7)
+    assert np.abs(O.router_logits_fixed(golden["x"], golden["router_w"]) - golden["ref.router.logits"]).max() < 1e-5
+
+
+def test_router_fixed_order_is_the_stated_order():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((2, 96)).astype(np.float32)
+    w = rng.standard_normal((3, 96)).astype(np.float32)
+    got = O.router_logits_fixed(x, w)
+    for t in range(2):
+        for e in range(3):
+            p = np.zeros(32, dtype=np.float32)
+            for l in range(32):
+                acc = np.float64(0)  # fma = exact product + single rounding: emulate in fp64 (exact for fp32 inputs)
+                a32 = np.float32(0)
+                for kk in range(l, 96, 32):
+                    a32 = np.float32(np.float64(x[t, kk]) * np.float64(w[e, kk]) + np.float64(a32))
+                p[l] = a32
+            for off in (16, 8, 4, 2, 1):
+                p = (p + p[np.arange(32) ^ off]).astype(np.float32)
+            assert got[t, e] == p[0]
+
+
+def test_layer_output_matches_reference(golden):
+    h, i, e, k, r, top_k, n_tok = (int(v) for v in golden["meta"])
+    groups = golden_groups(golden)
+    for tag in ("softmax", "sigmoid"):
+        y = O.moe_layer_forward(golden["x"], groups, golden["router_w"], top_k, h, i, k, router=tag,
+                                e_bias=golden["e_bias"], logits=golden["ref.router.logits"])
+        ref = golden[f"ref.layer_y.{tag}"]
+        assert np.linalg.norm(y - ref) <= 1e-5 * np.linalg.norm(ref)
+
+
+def test_synthetic_fold_is_valid_format():
+    rng = np.random.default_rng(1)
+    k, i, h, r = 4, 128, 256, 8
+    gate, up = (rng.standard_normal((k, i, h)).astype(np.float32) * 0.02 for _ in range(2))
+    down = rng.standard_normal((k, h, i)).astype(np.float32) * 0.02
+    g = O.fold_group_synthetic(gate, up, down, 1, r)
+    assert g["s_gu.weight"].shape == (2 * i, h // 2) and g["s_gu.weight_scale"].shape == (2 * i, h // 16)
+    assert g["healer.u_down"].shape == (k, h, r) and g["healer.v_down"].shape == (k, r, i)
+    gu, dn = O.reconstruct_expert(g, 1, 2, h, i)
+    ref = np.concatenate([gate[2], up[2]], 0)
+    cos = float((gu * ref).sum() / (np.linalg.norm(gu) * np.linalg.norm(ref)))
+    assert cos > 0.4  # a K=4 fold keeps ~1/sqrt(K) of each expert before healing
