@@ -1,0 +1,181 @@
+// extern "C" entry points of libchronos_b200.so: argument validation on the host, then stream-ordered launches.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace chronos {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int check_launch(const char* what) {
+    const cudaError_t rc = cudaGetLastError();
+    if (rc == cudaSuccess) return CHRONOS_OK;
+    set_error("%s: %s", what, cudaGetErrorString(rc));
+    return CHRONOS_E_LAUNCH;
+}
+
+static bool aligned16(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int validate_layer(const chronos_layer_t* L, bool need_router) {
+    if (!L) { set_error("layer is NULL"); return CHRONOS_E_ALIGN; }
+    if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128 || L->hidden > 32768 || 2 * L->inter > 32768) {
+        set_error("hidden (%d) and inter (%d) must be positive multiples of 128 with hidden, 2*inter <= 32768", L->hidden, L->inter);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->group_size <= 0 || L->n_slots <= 0 || L->n_experts != L->n_slots * L->group_size || L->n_experts > 1024) {
+        set_error("n_experts (%d) must equal n_slots (%d) * group_size (%d) and be <= 1024", L->n_experts, L->n_slots, L->group_size);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->rank <= 0 || L->rank % 16 || L->rank > kMaxRank) {
+        set_error("healer rank (%d) must be a multiple of 16 in [16, %d]", L->rank, kMaxRank);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->top_k <= 0 || L->top_k > kMaxTopK || L->top_k > L->n_experts) {
+        set_error("top_k (%d) must be in [1, min(%d, n_experts)]", L->top_k, kMaxTopK);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->shared_inter != 0 && L->shared_inter != L->inter) {
+        set_error("shared_inter (%d) must be 0 or equal to inter (%d)", L->shared_inter, L->inter);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->router_kind != CHRONOS_ROUTER_SOFTMAX_TOPK && L->router_kind != CHRONOS_ROUTER_SIGMOID_NOAUX) {
+        set_error("router_kind %d is not a CHRONOS_ROUTER_* value", L->router_kind);
+        return CHRONOS_E_ARG;
+    }
+    const void* need[] = {L->gu_w, L->gu_s, L->gu_s2, L->gu_beta, L->dn_w, L->dn_s, L->dn_s2, L->dn_beta, L->u_gu, L->v_gu,
+                          L->u_dn, L->v_dn_t, L->gu_cin, L->gu_cs2, L->gu_rout, L->gu_rs2, L->dn_cin, L->dn_cs2, L->dn_rout,
+                          L->dn_rs2};
+    const char* names[] = {"gu_w", "gu_s", "gu_s2", "gu_beta", "dn_w", "dn_s", "dn_s2", "dn_beta", "u_gu", "v_gu",
+                           "u_dn", "v_dn_t", "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout",
+                           "dn_rs2"};
+    for (size_t i = 0; i < sizeof(need) / sizeof(need[0]); ++i) {
+        const bool scalar_table = (i == 2 || i == 3 || i == 6 || i == 7);
+        if (need[i] == nullptr || (!scalar_table && !aligned16(need[i]))) {
+            set_error("layer.%s is NULL or not 16-byte aligned", names[i]);
+            return CHRONOS_E_ALIGN;
+        }
+    }
+    if (need_router && L->router_w == nullptr) { set_error("layer.router_w is NULL"); return CHRONOS_E_ALIGN; }
+    if (L->shared_inter > 0) {
+        const void* sh[] = {L->sh_gu_w, L->sh_gu_s, L->sh_dn_w, L->sh_dn_s};
+        for (const void* q : sh)
+            if (!aligned16(q)) { set_error("a shared-expert bank pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
+        if (!L->sh_gu_s2 || !L->sh_dn_s2) { set_error("a shared-expert scale_2 pointer is NULL"); return CHRONOS_E_ALIGN; }
+    }
+    return CHRONOS_OK;
+}
+
+static int validate_io(const void* x, int x_dtype, int n_tokens, const void* y, int y_dtype) {
+    if (n_tokens < 0 || n_tokens > (1 << 20)) { set_error("n_tokens (%d) out of range", n_tokens); return CHRONOS_E_SHAPE; }
+    if ((x_dtype != CHRONOS_DTYPE_F32 && x_dtype != CHRONOS_DTYPE_BF16) ||
+        (y_dtype != CHRONOS_DTYPE_F32 && y_dtype != CHRONOS_DTYPE_BF16)) {
+        set_error("dtype must be CHRONOS_DTYPE_F32 or CHRONOS_DTYPE_BF16");
+        return CHRONOS_E_ARG;
+    }
+    if (n_tokens > 0 && (!aligned16(x) || !aligned16(y))) { set_error("x or y is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
+    return CHRONOS_OK;
+}
+
+static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
+                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, cudaStream_t st) {
+    if (int rc = launch_plan(L, ids, n_tokens, with_shared, p, st)) return rc;
+    if (int rc = launch_pre_gu(L, x, x_dtype, p, st)) return rc;
+    if (int rc = launch_bank_stream(L, 0, p, st)) return rc;
+    if (int rc = launch_mid(L, p, st)) return rc;
+    if (int rc = launch_bank_stream(L, 1, p, st)) return rc;
+    return launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+}
+
+}  // namespace chronos
+
+using namespace chronos;
+
+extern "C" {
+
+int chronos_b200_abi_version(void) { return 1; }
+
+const char* chronos_b200_last_error(void) { return g_err; }
+
+int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, const float* scale_2, float* out, int rows,
+                               int cols, void* stream) {
+    if (rows <= 0 || cols <= 0 || cols % 16) { set_error("dequant: rows (%d) > 0 and cols (%d) a positive multiple of 16 required", rows, cols); return CHRONOS_E_SHAPE; }
+    if (!packed || !scale || !scale_2 || !out || (reinterpret_cast<uintptr_t>(out) & 7u)) { set_error("dequant: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
+    return launch_dequant(packed, scale, scale_2, out, rows, cols, (cudaStream_t)stream);
+}
+
+int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, int which, float* out, float* scratch,
+                                    void* stream) {
+    if (int rc = validate_layer(layer, false)) return rc;
+    if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
+    if (!out || !scratch) { set_error("unfold: out or scratch is NULL"); return CHRONOS_E_ALIGN; }
+    return launch_unfold(*layer, expert, which, out, scratch, (cudaStream_t)stream);
+}
+
+int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
+                             float* gates, float* logits, void* stream) {
+    if (int rc = validate_layer(layer, true)) return rc;
+    if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
+    if (!ids || !gates || !logits) { set_error("router: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
+    return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, (cudaStream_t)stream);
+}
+
+size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens) {
+    if (validate_layer(layer, false) != CHRONOS_OK || n_tokens < 0 || n_tokens > (1 << 20)) return 0;
+    return plan_layout(*layer, n_tokens).total;
+}
+
+long chronos_b200_workspace_status_offset(const chronos_layer_t* layer, int n_tokens) {
+    if (validate_layer(layer, false) != CHRONOS_OK || n_tokens < 0 || n_tokens > (1 << 20)) return -1;
+    return (long)plan_layout(*layer, n_tokens).off_counters + 2 * (long)sizeof(int32_t);
+}
+
+int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = validate_layer(layer, true)) return rc;
+    if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
+    if (n_tokens == 0) return CHRONOS_OK;
+    const PlanLayout lay = plan_layout(*layer, n_tokens);
+    if (!aligned16(workspace) || workspace_bytes < lay.total) {
+        set_error("workspace of %zu bytes is too small or misaligned (%zu needed)", workspace_bytes, lay.total);
+        return CHRONOS_E_WORKSPACE;
+    }
+    const Plan p = plan_bind(lay, workspace);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, st)) return rc;
+    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, st);
+}
+
+int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
+                                   const int32_t* ids, const float* gates, int with_shared, void* y, int y_dtype,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = validate_layer(layer, false)) return rc;
+    if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
+    if (n_tokens == 0) return CHRONOS_OK;
+    if (!ids || !gates) { set_error("routed: ids or gates is NULL"); return CHRONOS_E_ALIGN; }
+    const PlanLayout lay = plan_layout(*layer, n_tokens);
+    if (!aligned16(workspace) || workspace_bytes < lay.total) {
+        set_error("workspace of %zu bytes is too small or misaligned (%zu needed)", workspace_bytes, lay.total);
+        return CHRONOS_E_WORKSPACE;
+    }
+    const Plan p = plan_bind(lay, workspace);
+    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, (cudaStream_t)stream);
+}
+
+int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,
+                                  int hidden, float eps, void* stream) {
+    if (dtype != CHRONOS_DTYPE_F32 && dtype != CHRONOS_DTYPE_BF16) { set_error("rmsnorm: bad dtype"); return CHRONOS_E_ARG; }
+    if (n_tokens < 0 || hidden <= 0) { set_error("rmsnorm: bad shape"); return CHRONOS_E_SHAPE; }
+    if (n_tokens > 0 && (!h || !x_norm)) { set_error("rmsnorm: NULL pointer"); return CHRONOS_E_ALIGN; }
+    return launch_residual_rmsnorm(h, y, weight, x_norm, dtype, n_tokens, hidden, eps, (cudaStream_t)stream);
+}
+
+}  // extern "C"

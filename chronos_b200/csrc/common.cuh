@@ -1,0 +1,179 @@
+// Shared device helpers and the workspace plan of the folded-MoE forward (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "chronos_b200.h"
+
+namespace chronos {
+
+constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
+constexpr int kMaxTopK = 32;
+constexpr int kMaxRank = 128;
+
+// Device-side view of the caller's workspace for one forward call. All offsets are 256-byte aligned.
+struct Plan {
+    float* logits;         // [T, E]
+    int32_t* ids;          // [T, top_k]
+    float* gates;          // [T, top_k]
+    int32_t* offsets;      // [E + 2]  first sorted pair of expert e; entry E = shared expert; entry E+1 = total
+    int32_t* pair_token;   // [P]      token of sorted pair p
+    int32_t* pair_expert;  // [P]      expert of sorted pair p (E = shared expert)
+    int32_t* pos_of;       // [T * top_k] sorted position of routing entry (t, j); -1 when skipped
+    int32_t* item_start;   // [max_items] first sorted pair of work item
+    int32_t* item_cnt;     // [max_items] 1..8 pairs
+    int32_t* item_slot;    // [max_items] slot whose bank the item streams (n_slots = shared expert)
+    int32_t* counters;     // [0] = number of items, [1] = number of pairs, [2] = device status word
+    __half* xc;            // [P, H]   transformed gate_up inputs
+    float* hmid;           // [P, r]   V_gu . x
+    float* z1;             // [P, 2I]  H_r(r_s2 * (S_gu . x_c)) * scale_2
+    __half* ac;            // [P, I]   transformed down inputs
+    float* hpart;          // [P, I/128, r] partial V_down . act per 128-block
+    float* y1;             // [P, H]   H_r(r_s2 * (S_down . a_c)) * scale_2
+    int max_pairs;
+    int max_items;
+};
+
+struct PlanLayout {
+    size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
+        off_item_cnt, off_item_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, total;
+    int max_pairs, max_items;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
+    PlanLayout p{};
+    const size_t T = (size_t)n_tokens, E = (size_t)L.n_experts, k = (size_t)L.top_k, H = (size_t)L.hidden,
+                 I = (size_t)L.inter, r = (size_t)L.rank;
+    const size_t P = T * k + (L.shared_inter > 0 ? T : 0);
+    p.max_pairs = (int)P;
+    p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
+    p.off_logits = take(T * E * 4);
+    p.off_ids = take(T * k * 4);
+    p.off_gates = take(T * k * 4);
+    p.off_offsets = take((E + 2) * 4);
+    p.off_pair_token = take(P * 4);
+    p.off_pair_expert = take(P * 4);
+    p.off_pos_of = take(T * k * 4);
+    p.off_item_start = take((size_t)p.max_items * 4);
+    p.off_item_cnt = take((size_t)p.max_items * 4);
+    p.off_item_slot = take((size_t)p.max_items * 4);
+    p.off_counters = take(64);
+    p.off_xc = take(P * H * 2);
+    p.off_hmid = take(P * r * 4);
+    p.off_z1 = take(P * 2 * I * 4);
+    p.off_ac = take(P * I * 2);
+    p.off_hpart = take(P * (I / 128) * r * 4);
+    p.off_y1 = take(P * H * 4);
+    p.total = o;
+    return p;
+}
+
+inline Plan plan_bind(const PlanLayout& l, void* ws) {
+    char* b = (char*)ws;
+    Plan p{};
+    p.logits = (float*)(b + l.off_logits);
+    p.ids = (int32_t*)(b + l.off_ids);
+    p.gates = (float*)(b + l.off_gates);
+    p.offsets = (int32_t*)(b + l.off_offsets);
+    p.pair_token = (int32_t*)(b + l.off_pair_token);
+    p.pair_expert = (int32_t*)(b + l.off_pair_expert);
+    p.pos_of = (int32_t*)(b + l.off_pos_of);
+    p.item_start = (int32_t*)(b + l.off_item_start);
+    p.item_cnt = (int32_t*)(b + l.off_item_cnt);
+    p.item_slot = (int32_t*)(b + l.off_item_slot);
+    p.counters = (int32_t*)(b + l.off_counters);
+    p.xc = (__half*)(b + l.off_xc);
+    p.hmid = (float*)(b + l.off_hmid);
+    p.z1 = (float*)(b + l.off_z1);
+    p.ac = (__half*)(b + l.off_ac);
+    p.hpart = (float*)(b + l.off_hpart);
+    p.y1 = (float*)(b + l.off_y1);
+    p.max_pairs = l.max_pairs;
+    p.max_items = l.max_items;
+    return p;
+}
+
+// ---- host-side launch wrappers (one per .cu file) -------------------------------------------------------------
+int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2, float* out, int rows, int cols,
+                   cudaStream_t st);
+int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, float* scratch, cudaStream_t st);
+int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
+                  float* logits, cudaStream_t st);
+int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const Plan& p,
+                cudaStream_t st);
+int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
+int launch_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                   int y_dtype, cudaStream_t st);
+int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, int dtype, int n_tokens, int hidden,
+                            float eps, cudaStream_t st);
+
+void set_error(const char* fmt, ...);
+int check_launch(const char* what);
+
+#ifdef __CUDACC__
+// ---- device helpers ---------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float ld_act(const void* x, int dtype, size_t i) {
+    return dtype == CHRONOS_DTYPE_BF16 ? __bfloat162float(((const __nv_bfloat16*)x)[i]) : ((const float*)x)[i];
+}
+
+// Two e4m3 bytes (low byte first) -> two fp32 values. Exact: every e4m3 value is representable in fp16.
+__device__ __forceinline__ float2 e4m3x2_to_f32(uint16_t v) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(v));
+    return __half22float2(*reinterpret_cast<__half2*>(&h2));
+}
+__device__ __forceinline__ float e4m3_to_f32(uint8_t v) { return e4m3x2_to_f32((uint16_t)v).x; }
+
+// Four bytes = eight e2m1 nibbles -> four f16x2 registers; low nibble of each byte lands in the low half.
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t& h0, uint32_t& h1, uint32_t& h2, uint32_t& h3) {
+    asm("{\n"
+        ".reg .b8 b0, b1, b2, b3;\n"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+        "}\n"
+        : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+        : "r"(w));
+}
+
+// Orthonormal 128-point Walsh-Hadamard transform (Sylvester order, scale 1/sqrt(128)) of a vector spread over a
+// warp: lane l holds elements 4l .. 4l+3. Same matrix as build_hadamard_128
+// (chronos_1t/converter/convert_glm53_flash_colab.py:41-45).
+__device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
+    float a = v[0] + v[1], b = v[0] - v[1], c = v[2] + v[3], d = v[2] - v[3];
+    v[0] = a + c; v[1] = b + d; v[2] = a - c; v[3] = b - d;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = hi ? (o - v[i]) : (v[i] + o);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] *= 0.08838834764831845f;
+}
+
+__device__ __forceinline__ float silu_f32(float z) { return z / (1.0f + expf(-z)); }
+
+__device__ __forceinline__ __half f32_to_f16_sat(float v) {
+    unsigned short r;
+    asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(r) : "f"(v));
+    return __ushort_as_half(r);
+}
+#endif  // __CUDACC__
+
+}  // namespace chronos

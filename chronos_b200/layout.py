@@ -1,0 +1,303 @@
+"""Device-resident packed layout of one folded MoE layer and its `chronos_layer_t` view.
+
+The bank and healer bytes are the converter's on-disk bytes (chronos_1t/models/glm53_holo.py:291-302), stacked
+over slots / experts; nothing is re-quantised. Two load-time rearrangements that do not touch the file format:
+`healer.v_down` is stored transposed ([I, r] per expert) and the seeded keys are compacted into gather tables.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Iterable, Mapping
+
+import numpy as np
+import torch
+
+from . import _lib, keys
+
+GROUP_TENSOR_SUFFIXES = (  # chronos_1t/models/glm53_holo.py:45-51
+    "s_gu.weight", "s_gu.weight_scale", "s_gu.weight_scale_2", "s_gu.beta",
+    "s_down.weight", "s_down.weight_scale", "s_down.weight_scale_2", "s_down.beta",
+    "healer.u_gu", "healer.v_gu", "healer.u_down", "healer.v_down",
+    "tail.gu_bits", "tail.gu_packed", "tail.gu_scale",
+    "tail.down_bits", "tail.down_packed", "tail.down_scale",
+)
+_REQUIRED = GROUP_TENSOR_SUFFIXES[:12]  # the tail lattice is carried by the format but not read by this path
+
+
+@dataclass
+class FoldedLayerConfig:
+    """Shape and router description of a folded layer (mirrors the `chronos_holographic_moe` block of config.json,
+    chronos_1t/converter/convert_glm53_chronos.py:544-561, plus the router fields of the model config)."""
+
+    hidden: int
+    inter: int
+    n_experts: int
+    group_size: int
+    rank: int
+    top_k: int
+    router: str = "softmax"        # "softmax" (top-k then softmax) or "sigmoid" (noaux_tc)
+    norm_topk_prob: bool = True
+    routed_scaling_factor: float = 2.5
+    seed_stride: int = keys.SEED_GROUP_STRIDE
+    key_generator: str = "torch_cpu_v1"
+
+    @property
+    def n_slots(self) -> int:
+        return self.n_experts // self.group_size
+
+    def validate(self) -> None:
+        if self.hidden % 128 or self.inter % 128:
+            raise ValueError("hidden and inter must be multiples of 128 (chronos_1t/models/glm53_chronos_spec.py:149-151)")
+        if self.n_experts % self.group_size:
+            raise ValueError("n_experts must be a multiple of group_size")
+        if self.router not in ("softmax", "sigmoid"):
+            raise ValueError(f"unknown router flavour {self.router!r}")
+        if self.key_generator != "torch_cpu_v1":
+            raise ValueError("only key_generator = 'torch_cpu_v1' checkpoints can be read")
+
+    def bank_bytes_per_slot(self) -> int:
+        h, i = self.hidden, self.inter
+        return 2 * i * h // 2 + 2 * i * h // 16 + h * i // 2 + h * i // 16
+
+    def healer_bytes_per_expert(self) -> int:
+        return self.rank * (2 * self.inter + self.hidden + self.hidden + self.inter)
+
+
+def _u8(t: Any) -> torch.Tensor:
+    """Tensor or array -> CPU uint8 torch tensor holding the same bytes (fp8 is reinterpreted, not converted)."""
+    if isinstance(t, np.ndarray):
+        t = torch.from_numpy(np.ascontiguousarray(t))
+    if t.dtype == torch.float8_e4m3fn:
+        t = t.view(torch.uint8)
+    if t.dtype != torch.uint8:
+        raise TypeError(f"expected uint8 / float8_e4m3fn bytes, got {t.dtype}")
+    return t.contiguous()
+
+
+def _f32(t: Any) -> torch.Tensor:
+    if isinstance(t, (np.ndarray, np.generic, float)):
+        t = torch.from_numpy(np.ascontiguousarray(np.asarray(t, dtype=np.float32)))
+    return t.detach().to(torch.float32).contiguous()
+
+
+_KEY_TABLE_CACHE: dict[tuple, dict[str, torch.Tensor]] = {}
+
+
+def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.Tensor]:
+    """Compact key tables of all experts of a layer shape. Keys depend on (slot, member, dims) only - not on the
+    layer index - so one set per shape and device is shared by every layer (the reference caches them the same way,
+    chronos_1t/models/glm53_holo.py:53,68-71)."""
+    ck = (cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.seed_stride, str(device))
+    hit = _KEY_TABLE_CACHE.get(ck)
+    if hit is not None:
+        return hit
+    h, i, e, k = cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size
+    acc: dict[str, list[np.ndarray]] = {n: [] for n in ("gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2")}
+    for eid in range(e):
+        g, m = divmod(eid, k)
+        sg, sd = keys.group_seed_bases(g, cfg.seed_stride)
+        for pre, rows, cols, sb in (("gu", 2 * i, h, sg), ("dn", h, i, sd)):
+            t = keys.compact_tables(rows, cols, m, sb)
+            for n in ("cin", "cs2", "rout", "rs2"):
+                acc[f"{pre}_{n}"].append(t[n])
+    out: dict[str, torch.Tensor] = {}
+    for n, parts in acc.items():
+        arr = np.stack(parts)
+        view = arr.view(np.int16) if arr.dtype == np.uint16 else arr.view(np.int32)
+        out[n] = torch.from_numpy(view.copy()).to(device)
+    _KEY_TABLE_CACHE[ck] = out
+    return out
+
+
+class PackedLayer:
+    """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
+
+    def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device):
+        cfg.validate()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.t = tensors
+        self.struct = _lib.LayerStruct()
+        s = self.struct
+        s.hidden, s.inter, s.n_experts, s.group_size, s.n_slots = cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.n_slots
+        s.rank, s.top_k = cfg.rank, cfg.top_k
+        s.router_kind = _lib.ROUTER_SOFTMAX_TOPK if cfg.router == "softmax" else _lib.ROUTER_SIGMOID_NOAUX
+        s.renorm = int(cfg.norm_topk_prob)
+        s.routed_scaling = float(cfg.routed_scaling_factor)
+        s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
+        for name, _ in _lib.LayerStruct._fields_:
+            if name in tensors:
+                setattr(s, name, tensors[name].data_ptr())
+        self._check_shapes()
+
+    # -- shape checks: wrong or short tensors are rejected here, before any launch ---------------------------------
+    def _check_shapes(self) -> None:
+        c, t = self.cfg, self.t
+        h, i, e, ns, r = c.hidden, c.inter, c.n_experts, c.n_slots, c.rank
+        want = {
+            "gu_w": (ns, 2 * i, h // 2), "gu_s": (ns, 2 * i, h // 16), "gu_s2": (ns,), "gu_beta": (e,),
+            "dn_w": (ns, h, i // 2), "dn_s": (ns, h, i // 16), "dn_s2": (ns,), "dn_beta": (e,),
+            "u_gu": (e, 2 * i, r), "v_gu": (e, r, h), "u_dn": (e, h, r), "v_dn_t": (e, i, r),
+            "gu_cin": (e, h), "gu_cs2": (e, h // 32), "gu_rout": (e, 2 * i), "gu_rs2": (e, 2 * i // 32),
+            "dn_cin": (e, i), "dn_cs2": (e, i // 32), "dn_rout": (e, h), "dn_rs2": (e, h // 32),
+        }
+        if "router_w" in t:
+            want["router_w"] = (e, h)
+        if "e_bias" in t:
+            want["e_bias"] = (e,)
+        if "sh_gu_w" in t:
+            want.update({"sh_gu_w": (2 * i, h // 2), "sh_gu_s": (2 * i, h // 16), "sh_gu_s2": (2,),
+                         "sh_dn_w": (h, i // 2), "sh_dn_s": (h, i // 16), "sh_dn_s2": (1,)})
+        for name, shape in want.items():
+            if name not in t:
+                raise ValueError(f"packed layer is missing tensor {name!r}")
+            if tuple(t[name].shape) != shape:
+                raise ValueError(f"packed tensor {name!r} has shape {tuple(t[name].shape)}, expected {shape}")
+            if not t[name].is_contiguous() or t[name].device != self.device:
+                raise ValueError(f"packed tensor {name!r} must be contiguous on {self.device}")
+        for name in ("gu_s2", "dn_s2", "gu_beta", "dn_beta"):
+            if not bool(torch.isfinite(t[name]).all()):
+                raise ValueError(f"packed tensor {name!r} holds a non-finite value")
+
+    @property
+    def ptr(self):
+        return C.byref(self.struct)
+
+    def resident_bytes(self) -> int:
+        return sum(v.numel() * v.element_size() for v in self.t.values())
+
+    # -- constructors ---------------------------------------------------------------------------------------------
+    @classmethod
+    def from_groups(cls, cfg: FoldedLayerConfig, groups: Iterable[Mapping[str, Any]], router_w: Any = None,
+                    e_bias: Any = None, shared: Mapping[str, Any] | None = None,
+                    device: torch.device | str = "cuda") -> "PackedLayer":
+        """`groups[g]` maps the on-disk suffixes to tensors/arrays (fp8 either as float8_e4m3fn or raw uint8).
+        `shared` (optional) holds a plain-NVFP4 expert: `{gate,up,down}_proj.{weight,weight_scale,weight_scale_2}`."""
+        device = torch.device(device)
+        groups = list(groups)
+        if len(groups) != cfg.n_slots:
+            raise ValueError(f"{len(groups)} slot dicts for {cfg.n_slots} slots")
+        for g, d in enumerate(groups):
+            for sfx in _REQUIRED:
+                if sfx not in d:
+                    raise ValueError(f"slot {g} is missing tensor {sfx!r}")
+            kk = int(np.asarray(_f32(d["s_gu.beta"])).shape[0])
+            if kk != cfg.group_size:
+                raise ValueError(f"slot {g} folds {kk} experts, config says {cfg.group_size}")
+
+        def stack_u8(sfx: str) -> torch.Tensor:
+            return torch.stack([_u8(d[sfx]) for d in groups])
+
+        t: dict[str, torch.Tensor] = {
+            "gu_w": stack_u8("s_gu.weight"), "gu_s": stack_u8("s_gu.weight_scale"),
+            "dn_w": stack_u8("s_down.weight"), "dn_s": stack_u8("s_down.weight_scale"),
+            "gu_s2": torch.stack([_f32(d["s_gu.weight_scale_2"]).reshape(()) for d in groups]),
+            "dn_s2": torch.stack([_f32(d["s_down.weight_scale_2"]).reshape(()) for d in groups]),
+            "gu_beta": torch.cat([_f32(d["s_gu.beta"]) for d in groups]),
+            "dn_beta": torch.cat([_f32(d["s_down.beta"]) for d in groups]),
+            "u_gu": torch.cat([_u8(d["healer.u_gu"]) for d in groups]),
+            "v_gu": torch.cat([_u8(d["healer.v_gu"]) for d in groups]),
+            "u_dn": torch.cat([_u8(d["healer.u_down"]) for d in groups]),
+            "v_dn_t": torch.cat([_u8(d["healer.v_down"]) for d in groups]).transpose(1, 2).contiguous(),
+        }
+        if router_w is not None:
+            t["router_w"] = _f32(router_w)
+        if e_bias is not None:
+            t["e_bias"] = _f32(e_bias)
+        if shared is not None:
+            t["sh_gu_w"] = torch.cat([_u8(shared["gate_proj.weight"]), _u8(shared["up_proj.weight"])])
+            t["sh_gu_s"] = torch.cat([_u8(shared["gate_proj.weight_scale"]), _u8(shared["up_proj.weight_scale"])])
+            t["sh_gu_s2"] = torch.stack([_f32(shared["gate_proj.weight_scale_2"]).reshape(()), _f32(shared["up_proj.weight_scale_2"]).reshape(())])
+            t["sh_dn_w"], t["sh_dn_s"] = _u8(shared["down_proj.weight"]), _u8(shared["down_proj.weight_scale"])
+            t["sh_dn_s2"] = _f32(shared["down_proj.weight_scale_2"]).reshape(1)
+        t = {n: v.to(device).contiguous() for n, v in t.items()}
+        t.update(key_tables(cfg, device))
+        return cls(cfg, t, device)
+
+    @classmethod
+    def from_safetensors(cls, path: str | Path, cfg: FoldedLayerConfig, prefix: str, device: torch.device | str = "cuda",
+                         shared_prefix: str | None = None) -> "PackedLayer":
+        """Reads `{prefix}.chronos_groups.{g}.{suffix}` (chronos_1t/models/glm53_chronos_spec.py:186-191) and
+        `{prefix}.gate.weight` (+ `.gate.e_score_correction_bias`) from a converter shard."""
+        from safetensors import safe_open
+
+        with safe_open(str(path), framework="pt", device="cpu") as fh:
+            names = set(fh.keys())
+            groups = []
+            for g in range(cfg.n_slots):
+                gp = f"{prefix}.chronos_groups.{g}."
+                missing = [s for s in _REQUIRED if gp + s not in names]
+                if missing:
+                    raise ValueError(f"{path}: slot {g} is missing {missing}")
+                groups.append({s: fh.get_tensor(gp + s) for s in _REQUIRED})
+            router_w = fh.get_tensor(f"{prefix}.gate.weight") if f"{prefix}.gate.weight" in names else None
+            bias_key = f"{prefix}.gate.e_score_correction_bias"
+            e_bias = fh.get_tensor(bias_key) if bias_key in names else None
+            shared = None
+            if shared_prefix is not None and f"{shared_prefix}.gate_proj.weight" in names:
+                shared = {f"{p}.{s}": fh.get_tensor(f"{shared_prefix}.{p}.{s}")
+                          for p in ("gate_proj", "up_proj", "down_proj") for s in ("weight", "weight_scale", "weight_scale_2")}
+        return cls.from_groups(cfg, groups, router_w, e_bias, shared, device)
+
+    @classmethod
+    def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda", with_shared: bool = False,
+                  slots: range | None = None) -> "PackedLayer":
+        """Seeded random layer in the converter's byte format, generated on the device (for benchmarks: the real
+        converter takes seconds per slot). Value ranges follow what the converter emits for N(0, 0.02) weights:
+        uniform nibbles, e4m3 block-scale codes 0x58..0x77, scale_2 = amax / 2688, beta ~ 0.5, healer ~ N(0, 0.05)."""
+        device = torch.device(device)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        h, i, e, ns, r = cfg.hidden, cfg.inter, cfg.n_experts, cfg.n_slots, cfg.rank
+
+        def rnd_u8(shape, lo=0, hi=256):
+            return torch.randint(lo, hi, shape, generator=gen, device=device, dtype=torch.uint8)
+
+        def rnd_fp8(shape, std):
+            return (torch.randn(shape, generator=gen, device=device) * std).to(torch.float8_e4m3fn).view(torch.uint8)
+
+        t = {
+            "gu_w": rnd_u8((ns, 2 * i, h // 2)), "gu_s": rnd_u8((ns, 2 * i, h // 16), 0x58, 0x78),
+            "dn_w": rnd_u8((ns, h, i // 2)), "dn_s": rnd_u8((ns, h, i // 16), 0x58, 0x78),
+            "gu_s2": torch.full((ns,), 0.08 / 2688.0, device=device), "dn_s2": torch.full((ns,), 0.08 / 2688.0, device=device),
+            "gu_beta": torch.rand(e, generator=gen, device=device) * 0.4 + 0.3,
+            "dn_beta": torch.rand(e, generator=gen, device=device) * 0.4 + 0.3,
+            "u_gu": rnd_fp8((e, 2 * i, r), 0.05), "v_gu": rnd_fp8((e, r, h), 0.05),
+            "u_dn": rnd_fp8((e, h, r), 0.05), "v_dn_t": rnd_fp8((e, i, r), 0.05),
+            "router_w": torch.randn(e, h, generator=gen, device=device) * 0.02,
+        }
+        if cfg.router == "sigmoid":
+            t["e_bias"] = torch.zeros(e, device=device)
+        if with_shared:
+            t.update({
+                "sh_gu_w": rnd_u8((2 * i, h // 2)), "sh_gu_s": rnd_u8((2 * i, h // 16), 0x58, 0x78),
+                "sh_gu_s2": torch.full((2,), 0.08 / 2688.0, device=device),
+                "sh_dn_w": rnd_u8((h, i // 2)), "sh_dn_s": rnd_u8((h, i // 16), 0x58, 0x78),
+                "sh_dn_s2": torch.full((1,), 0.08 / 2688.0, device=device),
+            })
+        t.update(key_tables(cfg, device))
+        return cls(cfg, t, device)
+
+    def to_groups_numpy(self) -> tuple[list[dict[str, np.ndarray]], dict[str, np.ndarray]]:
+        """Back to per-slot dicts of on-disk suffixes (numpy, fp8 as uint8) + extras: what a checker needs."""
+        c, t = self.cfg, {n: v.cpu().numpy() for n, v in self.t.items()}
+        k = c.group_size
+        groups = []
+        for g in range(c.n_slots):
+            sl = slice(g * k, (g + 1) * k)
+            groups.append({
+                "s_gu.weight": t["gu_w"][g], "s_gu.weight_scale": t["gu_s"][g], "s_gu.weight_scale_2": t["gu_s2"][g],
+                "s_gu.beta": t["gu_beta"][sl], "s_down.weight": t["dn_w"][g], "s_down.weight_scale": t["dn_s"][g],
+                "s_down.weight_scale_2": t["dn_s2"][g], "s_down.beta": t["dn_beta"][sl],
+                "healer.u_gu": t["u_gu"][sl], "healer.v_gu": t["v_gu"][sl], "healer.u_down": t["u_dn"][sl],
+                "healer.v_down": np.ascontiguousarray(t["v_dn_t"][sl].transpose(0, 2, 1)),
+            })
+        extras = {n: t[n] for n in ("router_w", "e_bias", "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2") if n in t}
+        return groups, extras
+
+
+def layer_index_from_prefix(prefix: str) -> int | None:
+    m = re.search(r"layers\.(\d+)", str(prefix))
+    return int(m.group(1)) if m else None

@@ -1,0 +1,147 @@
+/* chronos_b200 — C ABI of the B200 (sm_100a) folded-expert MoE forward.
+ *
+ * Plain pointers and sizes only; every pointer inside `chronos_layer_t` and every buffer argument is a DEVICE
+ * pointer owned by the caller (PyTorch in the shipped host layer).  The library allocates nothing, keeps no
+ * global state besides immutable constant tables and a per-thread error string, launches on the stream it is
+ * given and never synchronises, so the routed forward can be captured in a CUDA graph.  Every entry point
+ * returns 0 on success and a negative `CHRONOS_E_*` code otherwise; `chronos_b200_last_error()` describes the
+ * last failure of the calling thread.  Shape and alignment violations are rejected on the host before any
+ * launch.  There is no CPU fallback.
+ *
+ * "Replaces" comments name the reference interface (path within the Chronos project : line) whose role the
+ * entry point takes over.
+ */
+#ifndef CHRONOS_B200_H
+#define CHRONOS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHRONOS_OK 0
+#define CHRONOS_E_SHAPE (-1)     /* a dimension violates the layout rules below               */
+#define CHRONOS_E_ALIGN (-2)     /* a pointer is NULL or not 16-byte aligned                  */
+#define CHRONOS_E_WORKSPACE (-3) /* workspace smaller than chronos_b200_workspace_bytes()     */
+#define CHRONOS_E_LAUNCH (-4)    /* the CUDA runtime refused a launch (message has the cause) */
+#define CHRONOS_E_ARG (-5)       /* an enum-like argument is out of range                     */
+
+#define CHRONOS_DTYPE_F32 0
+#define CHRONOS_DTYPE_BF16 1
+
+#define CHRONOS_ROUTER_SOFTMAX_TOPK 0 /* chronos_1t/models/vllm_chronos_moe.py:310-314     */
+#define CHRONOS_ROUTER_SIGMOID_NOAUX 1 /* chronos_1t/models/glm53_chronos_moe.py:392-399    */
+
+/* One folded MoE layer resident in HBM.
+ *
+ * Dimensions: hidden H and inter I are multiples of 128 and at most 32768; n_experts = n_slots * group_size;
+ * expert e lives in slot e / group_size as member e % group_size (chronos_1t/models/glm5_chronos_moe.py:439-440).
+ * rank r is a multiple of 16, at most 128.  top_k <= 32.
+ *
+ * Banks and healers hold the on-disk bytes of the converter unchanged (suffix names from
+ * chronos_1t/models/glm53_holo.py:45-51), stacked over slots / experts:
+ *   gu_w   u8   [n_slots, 2I, H/2]   "s_gu.weight"      e2m1 nibbles, even column in the low nibble
+ *   gu_s   e4m3 [n_slots, 2I, H/16]  "s_gu.weight_scale"
+ *   gu_s2  f32  [n_slots]            "s_gu.weight_scale_2"
+ *   gu_beta f32 [n_experts]          "s_gu.beta"
+ *   dn_*   the same for "s_down.*" with shape [H, I/2] / [H, I/16]
+ *   u_gu   e4m3 [n_experts, 2I, r]   "healer.u_gu"
+ *   v_gu   e4m3 [n_experts, r, H]    "healer.v_gu"
+ *   u_dn   e4m3 [n_experts, H, r]    "healer.u_down"
+ *   v_dn_t e4m3 [n_experts, I, r]    "healer.v_down" TRANSPOSED once at load (on disk it is [r, I])
+ *
+ * Key tables are built on the host at load time from torch's CPU generator exactly as
+ * chronos_1t/models/glm53_holo.py:66-86 draws them, then compacted:
+ *   *_cin  u16 [n_experts, cols]     bits 0-14 = c_perm[j], bit 15 = (c_s1[c_perm[j]] < 0)
+ *   *_cs2  u32 [n_experts, cols/32]  bit j%32 of word j/32 = (c_s2[j] < 0)
+ *   *_rout u16 [n_experts, rows]     bits 0-14 = r_inv[i],  bit 15 = (r_s1[i] < 0)
+ *   *_rs2  u32 [n_experts, rows/32]  bit = (r_s2[i] < 0)
+ * with (rows, cols) = (2I, H) for gu and (H, I) for down.
+ *
+ * Optional always-on shared expert in plain (unfolded) NVFP4, the hub-expert format of
+ * chronos_1t/models/vllm_chronos_moe.py:131-141: sh_gu_* [2*shared_inter, H/2|H/16], sh_dn_* [H, shared_inter/2|/16];
+ * sh_gu_s2 f32 [2] = (gate_proj, up_proj) weight_scale_2, sh_dn_s2 f32 [1].
+ * shared_inter == 0 disables it.  shared_inter must equal inter when non-zero.
+ */
+typedef struct chronos_layer {
+    int32_t hidden, inter, n_experts, group_size, n_slots, rank, top_k;
+    int32_t router_kind;   /* CHRONOS_ROUTER_* */
+    int32_t renorm;        /* sigmoid router: divide weights by their sum (norm_topk_prob) */
+    float routed_scaling;  /* sigmoid router: routed_scaling_factor */
+    int32_t shared_inter;
+    int32_t reserved_;
+    const float* router_w; /* [n_experts, H] */
+    const float* e_bias;   /* [n_experts] or NULL (sigmoid router's e_score_correction_bias) */
+    const uint8_t* gu_w; const uint8_t* gu_s; const float* gu_s2; const float* gu_beta;
+    const uint8_t* dn_w; const uint8_t* dn_s; const float* dn_s2; const float* dn_beta;
+    const uint8_t* u_gu; const uint8_t* v_gu; const uint8_t* u_dn; const uint8_t* v_dn_t;
+    const uint16_t* gu_cin; const uint32_t* gu_cs2; const uint16_t* gu_rout; const uint32_t* gu_rs2;
+    const uint16_t* dn_cin; const uint32_t* dn_cs2; const uint16_t* dn_rout; const uint32_t* dn_rs2;
+    const uint8_t* sh_gu_w; const uint8_t* sh_gu_s; const float* sh_gu_s2;
+    const uint8_t* sh_dn_w; const uint8_t* sh_dn_s; const float* sh_dn_s2;
+} chronos_layer_t;
+
+/* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated
+ * in fp32 in exactly that order (bit-exact target).
+ * Replaces: unpack_nvfp4, chronos_1t/converter/convert_glm53_flash_colab.py:81-89
+ *           (= chronos_1t/models/chronos_moe_block.py:109-119 with dtype=float32). */
+int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, const float* scale_2, float* out,
+                               int rows, int cols, void* stream);
+
+/* Weight-space reconstruction probe of ONE expert: out f32 = beta * unbind(bank) + U.V  (no tail).
+ * which = 0: gate_up [2I, H]; which = 1: down [H, I].  `scratch` holds rows*cols floats.
+ * Replaces: reconstruct_group_experts(include_tail=False), chronos_1t/models/glm53_holo.py:336-368. */
+int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, int which, float* out, float* scratch,
+                                    void* stream);
+
+/* Router: fp32 logits in the fixed summation order (lane l of 32 sums k = l, l+32, ... with FMAs, then the xor
+ * butterfly 16,8,4,2,1), top-k descending with ties to the lower index, gate weights per router_kind.
+ * ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k], logits f32 [n_tokens, n_experts] (scratch, also returned).
+ * Replaces: the router blocks at chronos_1t/models/vllm_chronos_moe.py:310-314 and
+ *           chronos_1t/models/glm53_chronos_moe.py:392-399. */
+int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
+                             float* gates, float* logits, void* stream);
+
+/* Bytes of caller-owned scratch the forward entry points need for n_tokens tokens (0 on bad arguments). */
+size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens);
+
+/* Whole layer, streaming regime (HBM-bound; any n_tokens, meant for decode-shaped batches):
+ * y[n_tokens, H] = sum_k gate_k * Expert_{id_k}(x) (+ shared expert), router included.  Each distinct slot's
+ * bank is read from HBM once per call for up to 8 (token, expert) pairs that hit it.
+ * Replaces: ChronosGlm53SparseMoeBlock.forward_impl, chronos_1t/models/glm53_chronos_moe.py:474-483, with the
+ *           experts evaluated as ChronosGlm5HolographicExpertGroup.forward_cold_fast does
+ *           (chronos_1t/models/glm5_chronos_moe.py:149-195). */
+int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same, with routing supplied by the caller (ids < 0 are skipped; used by the expert-parallel host layer where
+ * a rank only owns some slots).  ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k].  with_shared != 0 adds
+ * the shared expert.
+ * Replaces: ChronosGlm53SparseMoeBlock.routed_forward, chronos_1t/models/glm53_chronos_moe.py:441-472. */
+int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
+                                   const int32_t* ids, const float* gates, int with_shared, void* y, int y_dtype,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* h[n_tokens, H] += y (when y != NULL); x_norm = h * rsqrt(mean(h^2) + eps) * (weight or 1), fp32 math.
+ * Replaces: rms_norm + residual wiring, chronos_1t/models/glm53_engine.py:71-73 and :200-204. */
+int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,
+                                  int hidden, float eps, void* stream);
+
+/* Byte offset, inside a workspace laid out for n_tokens, of the int32 device status word that the forward entry
+ * points clear at the start of a call and kernels raise on a device-side anomaly (bit 0x10: a bounded wait in the
+ * streaming bank kernel expired).  Read it after synchronising the stream.  Returns -1 on bad arguments.
+ * No counterpart in the reference (its kernels have no device-side waits). */
+long chronos_b200_workspace_status_offset(const chronos_layer_t* layer, int n_tokens);
+
+/* Message for the last non-zero status returned to the calling thread ("" if none). */
+const char* chronos_b200_last_error(void);
+
+/* Library/ABI version: increases whenever a signature or struct layout above changes. */
+int chronos_b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHRONOS_B200_H */

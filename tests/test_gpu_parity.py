@@ -1,0 +1,259 @@
+"""Parity of the CUDA path (through the C ABI) against the CPU oracle and the reference-generated golden files.
+
+Bars: NVFP4 dequantisation bit-exact; router logits bit-exact against the oracle's stated summation order and
+top-k ids exact (against the oracle everywhere, against the reference's own torch router on the golden cases);
+weight-space reconstruction within fp32 round-off; layer output rel-L2 <= 1e-2 against the fp32 reconstruction.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_groups
+from oracle import folded_moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LAYER_TOL = 1e-2  # relative L2 of the layer output, the tolerance stated for this path
+
+
+def _rel_l2(a, b):
+    a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _cfg(meta, router="softmax"):
+    from chronos_b200 import FoldedLayerConfig
+
+    h, i, e, k, r, top_k, _ = (int(v) for v in meta)
+    return FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k, router=router)
+
+
+def _golden_layer(golden, router="softmax", register=False):
+    from chronos_b200 import FoldedMoELayer, PackedLayer
+
+    packed = PackedLayer.from_groups(_cfg(golden["meta"], router), golden_groups(golden), golden["router_w"],
+                                     golden["e_bias"] if router == "sigmoid" else None, device="cuda")
+    return FoldedMoELayer(layer_idx=0, packed=packed, register=register)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def test_dequant_bit_exact_vs_reference(golden):
+    from chronos_b200 import codec
+
+    g0 = golden_groups(golden)[0]
+    for tag, sfx in (("gu", "s_gu"), ("down", "s_down")):
+        out = codec.unpack_nvfp4(torch.from_numpy(g0[f"{sfx}.weight"]).cuda(), torch.from_numpy(g0[f"{sfx}.weight_scale"]).cuda(),
+                                 torch.tensor(float(g0[f"{sfx}.weight_scale_2"])))
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), golden[f"ref.dequant_{tag}_g0"].view(np.uint32))
+
+
+def test_dequant_bit_exact_all_codes():
+    from chronos_b200 import codec
+
+    rng = np.random.default_rng(0)
+    rows, cols = 64, 512
+    packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    scale = rng.integers(0, 0x7F, (rows, cols // 16), dtype=np.uint8)  # every finite non-negative e4m3 code, incl. 0
+    packed[0, :8] = 0xFF  # saturated nibbles under a zero scale: legal input, dequantises to signed zeros
+    scale[0, 0] = 0
+    s2 = np.float32(3.1e-5)
+    ref = O.unpack_nvfp4(packed, scale, s2)
+    out = codec.unpack_nvfp4(torch.from_numpy(packed).cuda(), torch.from_numpy(scale).cuda(), torch.tensor(float(s2)))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    assert np.all(np.signbit(out.cpu().numpy()[0, :16]))  # -0.0 keeps its sign
+
+
+def test_reconstruction_matches_reference(golden):
+    from chronos_b200 import codec
+
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    groups = golden_groups(golden)
+    seen = 0
+    for key in golden:
+        if not key.startswith("ref.recon_notail.") or not key.endswith(".gu"):
+            continue
+        _, gs, ms, _ = key[len("ref.recon_"):].split(".")
+        g, m = int(gs[1:]), int(ms[1:])
+        gt = {s: torch.from_numpy(np.ascontiguousarray(v)) for s, v in groups[g].items()}
+        gu, dn = codec.reconstruct_group_experts(gt, g, [m], h, i, include_tail=False)[0]
+        for got, ref in ((gu, golden[key]), (dn, golden[key[:-3] + ".down"])):
+            err = np.abs(got.cpu().numpy() - ref).max()
+            assert err <= 4e-6 * max(1.0, np.abs(ref).max()), (key, err)
+        seen += 1
+    assert seen == 2
+
+
+def test_router_matches_reference_and_oracle(golden):
+    top_k = int(golden["meta"][5])
+    x = torch.from_numpy(golden["x"]).cuda()
+    for flavour in ("softmax", "sigmoid"):
+        layer = _golden_layer(golden, flavour)
+        ids, w = layer.route(x)
+        assert np.array_equal(ids.cpu().numpy(), golden[f"ref.router.{flavour}_ids"])
+        assert np.allclose(w.cpu().numpy(), golden[f"ref.router.{flavour}_gates"], rtol=2e-5, atol=1e-7)
+        fixed = O.router_logits_fixed(golden["x"], golden["router_w"])
+        assert np.array_equal(layer.last_logits.cpu().numpy().view(np.uint32), fixed.view(np.uint32))
+
+
+@pytest.mark.parametrize("n_tok,dtype", [(1, "f32"), (37, "bf16"), (256, "bf16")])
+def test_router_bit_exact_large(n_tok, dtype):
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=1024, inter=128, n_experts=288, group_size=4, rank=16, top_k=8)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=5), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(n_tok)
+    x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda")
+    if dtype == "bf16":
+        x = x.to(torch.bfloat16)
+    ids, w = layer.route(x)
+    logits = O.router_logits_fixed(x.float().cpu().numpy(), layer.packed.t["router_w"].cpu().numpy())
+    assert np.array_equal(layer.last_logits.cpu().numpy().view(np.uint32), logits.view(np.uint32))
+    ref_ids, ref_w = O.router_softmax_topk(logits, cfg.top_k)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    assert np.allclose(w.cpu().numpy(), ref_w, rtol=2e-5, atol=1e-7)
+
+
+def test_layer_output_matches_reference(golden):
+    for flavour in ("softmax", "sigmoid"):
+        layer = _golden_layer(golden, flavour)
+        ref = golden[f"ref.layer_y.{flavour}"]
+        y32 = layer(torch.from_numpy(golden["x"]).cuda())
+        assert y32.dtype == torch.float32 and layer.device_status() == 0
+        assert _rel_l2(y32.cpu().numpy(), ref) <= LAYER_TOL, flavour
+        # bf16 activations: compare with the oracle fed the same rounded activations
+        xb = torch.from_numpy(golden["x"]).cuda().to(torch.bfloat16)
+        h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+        ref_b = O.moe_layer_forward(xb.float().cpu().numpy(), golden_groups(golden), golden["router_w"], top_k, h, i, k,
+                                    router=flavour, e_bias=golden["e_bias"])
+        yb = layer(xb)
+        assert yb.dtype == torch.bfloat16
+        assert _rel_l2(yb.float().cpu().numpy(), ref_b) <= LAYER_TOL, flavour
+
+
+def _oracle_layer(layer, x_np, with_shared=True):
+    groups, extras = layer.packed.to_groups_numpy()
+    c = layer.cfg
+    shared = None
+    if with_shared and "sh_gu_w" in extras:
+        i = c.inter
+        gate = O.unpack_nvfp4(extras["sh_gu_w"][:i], extras["sh_gu_s"][:i], extras["sh_gu_s2"][0])
+        up = O.unpack_nvfp4(extras["sh_gu_w"][i:], extras["sh_gu_s"][i:], extras["sh_gu_s2"][1])
+        shared = (np.concatenate([gate, up]), O.unpack_nvfp4(extras["sh_dn_w"], extras["sh_dn_s"], extras["sh_dn_s2"][0]))
+    return O.moe_layer_forward(x_np, groups, extras["router_w"], c.top_k, c.hidden, c.inter, c.group_size, router=c.router,
+                               e_bias=extras.get("e_bias"), routed_scaling=c.routed_scaling_factor, shared=shared,
+                               return_routing=True)
+
+
+def test_config0_layer_with_folded_weights():
+    """CPU-runnable case: hidden 2048, 64 experts, top-8 softmax router, inter 768, fold 4, rank 32, 3 tokens fp32."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=2048, inter=768, n_experts=64, group_size=4, rank=32, top_k=8)
+    rng = np.random.default_rng(0)
+    router_w = (rng.standard_normal((64, 2048)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((3, 2048)).astype(np.float32)
+    logits = O.router_logits_fixed(x, router_w)
+    ids, _ = O.router_softmax_topk(logits, 8)
+    used = sorted({int(e) // 4 for e in ids.reshape(-1)})
+    groups = []
+    for g in range(16):
+        if g in used:  # fold real N(0, 0.02) experts for the slots this batch touches; untouched slots get random bytes
+            gate, up = (rng.standard_normal((4, 768, 2048)).astype(np.float32) * 0.02 for _ in range(2))
+            down = rng.standard_normal((4, 2048, 768)).astype(np.float32) * 0.02
+            groups.append(O.fold_group_synthetic(gate, up, down, g, 32))
+        else:
+            groups.append(O.random_group(rng, 4, 2048, 768, 32))
+    layer = FoldedMoELayer(packed=PackedLayer.from_groups(cfg, groups, router_w, device="cuda"), register=False)
+    y = layer(torch.from_numpy(x).cuda())
+    ref, ref_ids, ref_w = _oracle_layer(layer, x)
+    got_ids, got_w = layer.route(torch.from_numpy(x).cuda())
+    assert np.array_equal(got_ids.cpu().numpy(), ref_ids)
+    assert layer.device_status() == 0
+    assert _rel_l2(y.cpu().numpy(), ref) <= LAYER_TOL
+
+
+@pytest.mark.parametrize("streams", [1, 4])
+def test_decode_shaped_layer(streams):
+    """Decode-shaped layer: hidden 4096, 288 experts + shared, top-8, inter 1536, fold 4, rank 64, bf16, 3 tokens/stream."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=4096, inter=1536, n_experts=288, group_size=4, rank=64, top_k=8)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=1, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    base = torch.randn(streams, 1, cfg.hidden, generator=gen, device="cuda")
+    x = (0.55 * base + 0.84 * torch.randn(streams, 3, cfg.hidden, generator=gen, device="cuda")).reshape(-1, cfg.hidden).to(torch.bfloat16)
+    y1 = layer(x)
+    y2 = layer(x)
+    assert torch.equal(y1, y2), "two runs on the same input must be bit-identical"
+    assert layer.device_status() == 0
+    ref, ref_ids, _ = _oracle_layer(layer, x.float().cpu().numpy())
+    ids, _ = layer.route(x)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    assert _rel_l2(y1.float().cpu().numpy(), ref) <= LAYER_TOL
+
+
+def test_many_tokens_on_one_slot_and_skipped_entries():
+    """More than 8 pairs on a slot (several work items per slot), entries with id -1, routing supplied by the caller."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=2)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=7), register=False)
+    n = 21
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(n, cfg.hidden, generator=gen, device="cuda")
+    ids = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    ids[:, 0] = 5                      # 21 pairs on expert 5 (slot 1)
+    ids[:, 1] = torch.arange(n, device="cuda", dtype=torch.int32) % 4 + 4   # the other members of slot 1
+    ids[::2, 1] = 6
+    ids[3, 1] = -1                     # skipped entry
+    w = torch.rand((n, 2), generator=gen, device="cuda")
+    y = layer.routed_forward(x, ids, w)
+    assert layer.device_status() == 0
+    groups, _ = layer.packed.to_groups_numpy()
+    ref = np.zeros((n, cfg.hidden), dtype=np.float32)
+    xn, idn, wn = x.cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy()
+    for e in np.unique(idn[idn >= 0]):
+        gu, dn = O.reconstruct_expert(groups[e // 4], int(e) // 4, int(e) % 4, cfg.hidden, cfg.inter)
+        for t, j in zip(*np.nonzero(idn == e)):
+            z = xn[t] @ gu.T
+            ref[t] += wn[t, j] * ((O.silu(z[:cfg.inter]) * z[cfg.inter:]) @ dn.T)
+    assert _rel_l2(y.cpu().numpy(), ref) <= LAYER_TOL
+    # all entries skipped -> exact zeros; zero tokens -> empty output
+    y0 = layer.routed_forward(x, torch.full_like(ids, -1), w)
+    assert torch.count_nonzero(y0) == 0
+    assert layer(torch.empty(0, cfg.hidden, device="cuda")).shape == (0, cfg.hidden)
+
+
+def test_residual_rmsnorm_matches_oracle():
+    from chronos_b200 import residual_rmsnorm
+
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    h = torch.randn(5, 1024, generator=gen, device="cuda")
+    y = torch.randn(5, 1024, generator=gen, device="cuda")
+    ref_h = (h + y).cpu().numpy()
+    out = residual_rmsnorm(h, y, None, 1e-6)
+    assert np.allclose(h.cpu().numpy(), ref_h)
+    assert np.allclose(out.cpu().numpy(), O.rms_norm(ref_h, 1e-6), rtol=2e-5, atol=1e-6)
+
+
+def test_custom_op_equals_direct_call(golden):
+    from chronos_b200 import vllm_plugin as VP
+
+    layer = _golden_layer(golden, register=True)
+    VP.register_custom_op()
+    x = torch.from_numpy(golden["x"]).cuda()
+    assert torch.equal(torch.ops.chronos_b200.moe_forward(x, 0), layer.forward_impl(x))
+
+
+def test_bad_arguments_raise(golden):
+    from chronos_b200 import _lib
+
+    layer = _golden_layer(golden)
+    with pytest.raises(_lib.ChronosError):
+        layer(torch.from_numpy(golden["x"]))  # CPU tensor
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    x = torch.from_numpy(golden["x"]).cuda()
+    y = torch.empty_like(x)
+    rc = _lib.lib().chronos_b200_folded_moe_decode(layer.packed.ptr, x.data_ptr(), 0, x.shape[0], y.data_ptr(), 0,
+                                                   ws.data_ptr(), ws.numel(), None)
+    assert rc == -3 and b"workspace" in _lib.lib().chronos_b200_last_error()

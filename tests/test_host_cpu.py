@@ -1,0 +1,195 @@
+"""CPU-side checks: the C-ABI library loads and exports what the header declares, host logic (keys, layout
+validation, plugin hook with stub vLLM modules) behaves, and nothing computes without a GPU."""
+import re
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT, golden_groups, load_golden
+from oracle import folded_moe_oracle as O
+
+import chronos_b200
+from chronos_b200 import _lib, keys
+from chronos_b200.layout import FoldedLayerConfig, PackedLayer
+
+
+@pytest.fixture(scope="module", autouse=True)
+def built_library():
+    from chronos_b200 import build
+
+    build.build()
+
+
+def test_library_exports_every_declared_symbol():
+    header = (ROOT / "include" / "chronos_b200.h").read_text()
+    declared = set(re.findall(r"\b(chronos_b200_\w+)\s*\(", header))
+    assert {"chronos_b200_dequant_nvfp4", "chronos_b200_unfold_expert_fp32", "chronos_b200_router_topk",
+            "chronos_b200_workspace_bytes", "chronos_b200_folded_moe_decode", "chronos_b200_folded_moe_routed",
+            "chronos_b200_last_error"} <= declared
+    handle = _lib.lib()
+    for name in declared:
+        assert hasattr(handle, name), f"{name} is declared in the header but not exported"
+    assert declared == set(_lib.EXPORTS), "ctypes table and header disagree"
+    assert handle.chronos_b200_abi_version() == _lib.ABI_VERSION
+
+
+def test_layer_struct_matches_header_layout():
+    # 12 four-byte scalars then 28 pointers, no padding surprises
+    import ctypes
+
+    assert ctypes.sizeof(_lib.LayerStruct) == 12 * 4 + 28 * 8
+    header = (ROOT / "include" / "chronos_b200.h").read_text()
+    body = header[header.index("typedef struct chronos_layer {"):header.index("} chronos_layer_t;")]
+    names = re.findall(r"(\w+)\s*[;,]", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
+    assert names == [n for n, _ in _lib.LayerStruct._fields_]
+
+
+def test_host_rejects_bad_layer_without_a_gpu():
+    s = _lib.LayerStruct()
+    assert _lib.lib().chronos_b200_workspace_bytes(s, 4) == 0
+    s.hidden, s.inter, s.n_experts, s.group_size, s.n_slots, s.rank, s.top_k = 256, 100, 8, 4, 2, 16, 2
+    assert _lib.lib().chronos_b200_workspace_bytes(s, 4) == 0  # inter not a multiple of 128
+    rc = _lib.lib().chronos_b200_dequant_nvfp4(None, None, None, None, 4, 30, None)
+    assert rc == -1 and b"multiple of 16" in _lib.lib().chronos_b200_last_error()
+    with pytest.raises(_lib.ChronosError):
+        _lib.check(rc)
+
+
+def test_compact_key_tables_match_reference_keys(golden):
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    g, m = e // k - 1, k - 1
+    sg, sd = keys.group_seed_bases(g)
+    for tag, rows, cols, sb in (("gu", 2 * i, h, sg), ("down", h, i, sd)):
+        t = keys.compact_tables(rows, cols, m, sb)
+        ref = {n: golden[f"ref.keys.{tag}.g{g}.m{m}.{n}"].astype(np.int64)
+               for n in ("r_s1", "r_perm", "r_inv", "r_s2", "c_s1", "c_perm", "c_inv", "c_s2")}
+        assert np.array_equal(t["cin"] & 0x7FFF, ref["c_perm"])
+        assert np.array_equal(t["cin"] >> 15, (ref["c_s1"][ref["c_perm"]] < 0))
+        assert np.array_equal(t["rout"] & 0x7FFF, ref["r_inv"])
+        assert np.array_equal(t["rout"] >> 15, ref["r_s1"] < 0)
+        for name, sign in (("cs2", ref["c_s2"]), ("rs2", ref["r_s2"])):
+            bits = (t[name][np.arange(len(sign)) // 32] >> (np.arange(len(sign)) % 32)) & 1
+            assert np.array_equal(bits, sign < 0)
+
+
+def test_packed_layer_validation_on_cpu(golden):
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    cfg = FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k)
+    groups = golden_groups(golden)
+    layer = PackedLayer.from_groups(cfg, groups, golden["router_w"], device="cpu")
+    assert layer.struct.n_slots == e // k and layer.struct.shared_inter == 0
+    # v_down is stored transposed; everything else byte-identical
+    assert np.array_equal(layer.t["v_dn_t"][1].numpy(), groups[0]["healer.v_down"][1].T)
+    back, _ = layer.to_groups_numpy()
+    for sfx in ("s_gu.weight", "s_down.weight_scale", "healer.v_down", "healer.u_gu"):
+        assert np.array_equal(back[1][sfx], groups[1][sfx])
+    # failure injection on the host: missing tensor, short tensor, wrong fold factor, NaN scale
+    bad = [dict(g) for g in groups]
+    del bad[0]["healer.u_gu"]
+    with pytest.raises(ValueError, match="missing"):
+        PackedLayer.from_groups(cfg, bad, device="cpu")
+    bad = [dict(g) for g in groups]
+    bad[1]["s_gu.weight"] = bad[1]["s_gu.weight"][:-1]
+    with pytest.raises((ValueError, RuntimeError)):
+        PackedLayer.from_groups(cfg, bad, device="cpu")
+    with pytest.raises(ValueError, match="folds"):
+        PackedLayer.from_groups(FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k // 2, rank=r, top_k=top_k),
+                                groups + groups, device="cpu")
+    bad = [dict(g) for g in groups]
+    bad[0]["s_gu.weight_scale_2"] = np.float32("nan")
+    with pytest.raises(ValueError, match="non-finite"):
+        PackedLayer.from_groups(cfg, bad, device="cpu")
+
+
+def test_no_cpu_compute_path(golden):
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    cfg = FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k)
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only behaviour")
+    with pytest.raises(_lib.ChronosError):
+        chronos_b200.FoldedMoELayer(packed=PackedLayer.from_groups(cfg, golden_groups(golden), golden["router_w"], device="cpu"))
+    from chronos_b200 import codec
+
+    with pytest.raises(_lib.ChronosError):
+        codec.unpack_nvfp4(torch.zeros(4, 8, dtype=torch.uint8), torch.zeros(4, 1, dtype=torch.uint8), torch.tensor(1.0))
+
+
+def test_safetensors_loader_reads_converter_layout(tmp_path, golden):
+    from safetensors.torch import save_file
+
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    cfg = FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k, router="sigmoid")
+    prefix = "model.layers.3.mlp"
+    tensors = {}
+    for g, grp in enumerate(golden_groups(golden)):
+        for sfx, arr in grp.items():
+            t = torch.from_numpy(np.ascontiguousarray(arr))
+            if sfx.split(".")[-1] in ("weight_scale", "u_gu", "v_gu", "u_down", "v_down", "gu_scale", "down_scale"):
+                t = t.view(torch.float8_e4m3fn)
+            tensors[f"{prefix}.chronos_groups.{g}.{sfx}"] = t
+    tensors[f"{prefix}.gate.weight"] = torch.from_numpy(golden["router_w"])
+    tensors[f"{prefix}.gate.e_score_correction_bias"] = torch.from_numpy(golden["e_bias"])
+    path = tmp_path / "chronos-glm53-layer-00003-of-00005.safetensors"
+    save_file(tensors, str(path))
+    layer = PackedLayer.from_safetensors(path, cfg, prefix, device="cpu")
+    ref = PackedLayer.from_groups(cfg, golden_groups(golden), golden["router_w"], golden["e_bias"], device="cpu")
+    for n in ref.t:
+        assert torch.equal(layer.t[n], ref.t[n]), n
+    # a shard with a slot cut out is refused
+    del tensors[f"{prefix}.chronos_groups.1.healer.v_down"]
+    save_file(tensors, str(path))
+    with pytest.raises(ValueError, match="missing"):
+        PackedLayer.from_safetensors(path, cfg, prefix, device="cpu")
+
+
+def test_vllm_hook_with_stub_modules(tmp_path, monkeypatch):
+    """Stub `vllm.*` modules mirroring the import sites (the pattern of the reference's hook self-test,
+    benchmarks/glm53_vllm_hook_selftest.py:21-63): class swap, fallback to the stock class, isinstance."""
+    from chronos_b200 import vllm_plugin as VP
+
+    class StockMoE(torch.nn.Module):
+        def __init__(self, *a, **kw):
+            super().__init__()
+            self.kw = kw
+
+    pkg = types.ModuleType("vllm")
+    me = types.ModuleType("vllm.model_executor")
+    models = types.ModuleType("vllm.model_executor.models")
+    dsv2 = types.ModuleType("vllm.model_executor.models.deepseek_v2")
+    dsv2.DeepseekV2MoE = StockMoE
+    for name, mod in (("vllm", pkg), ("vllm.model_executor", me), ("vllm.model_executor.models", models),
+                      ("vllm.model_executor.models.deepseek_v2", dsv2)):
+        monkeypatch.setitem(sys.modules, name, mod)
+    monkeypatch.setenv("CHRONOS_B200_CKPT", str(tmp_path))
+    assert VP.enable_chronos_b200_vllm_hook() is True
+    hooked = dsv2.DeepseekV2MoE
+    assert isinstance(hooked, type) and hooked is not StockMoE and hooked._orig_moe_cls is StockMoE
+    assert VP.enable_chronos_b200_vllm_hook() is True and dsv2.DeepseekV2MoE is hooked  # idempotent
+    # no config.json / shard in the checkpoint dir -> stock class comes back
+    obj = dsv2.DeepseekV2MoE(config=None, prefix="model.layers.7.mlp")
+    assert type(obj) is StockMoE and obj.kw["prefix"] == "model.layers.7.mlp"
+    # the operator exists and traces through its fake implementation
+    assert hasattr(torch.ops.chronos_b200, "moe_forward")
+    VP.register()  # never raises
+
+
+def test_config_from_checkpoint(tmp_path):
+    import json
+
+    from chronos_b200 import vllm_plugin as VP
+
+    assert VP.config_from_checkpoint(tmp_path) is None
+    (tmp_path / "config.json").write_text(json.dumps({
+        "hidden_size": 4096, "moe_intermediate_size": 1536, "n_routed_experts": 288, "num_experts_per_tok": 8,
+        "scoring_func": "sigmoid", "routed_scaling_factor": 2.5, "norm_topk_prob": True,
+        "chronos_holographic_moe": {"group_size": 4, "svd_rank": 64, "key_generator": "torch_cpu_v1"}}))
+    cfg = VP.config_from_checkpoint(tmp_path)
+    assert (cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.rank, cfg.top_k, cfg.router) == (4096, 1536, 288, 4, 64, 8, "sigmoid")
+    assert cfg.bank_bytes_per_slot() == 10_616_832 and cfg.healer_bytes_per_expert() == 819_200
+    assert VP.find_layer_shard(tmp_path, 3) is None
+    (tmp_path / "chronos-glm53-layer-00003-of-00046.safetensors").write_bytes(b"")
+    assert VP.find_layer_shard(tmp_path, 3).name.endswith("00003-of-00046.safetensors")
