@@ -85,14 +85,30 @@ static int validate_io(const void* x, int x_dtype, int n_tokens, const void* y, 
     return CHRONOS_OK;
 }
 
+// Profiling aid: events recorded between the launches of a forward call (see chronos_b200_set_stage_events).
+static thread_local cudaEvent_t g_stage_events[kStageEvents];
+static thread_local int g_n_stage_events = 0;
+
+static void stage_mark(int idx, cudaStream_t st) {
+    if (idx < g_n_stage_events) cudaEventRecord(g_stage_events[idx], st);
+}
+
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
                           const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, cudaStream_t st) {
+    stage_mark(1, st);
     if (int rc = launch_plan(L, ids, n_tokens, with_shared, p, st)) return rc;
+    stage_mark(2, st);
     if (int rc = launch_pre_gu(L, x, x_dtype, p, st)) return rc;
+    stage_mark(3, st);
     if (int rc = launch_bank_stream(L, 0, p, st)) return rc;
+    stage_mark(4, st);
     if (int rc = launch_mid(L, p, st)) return rc;
+    stage_mark(5, st);
     if (int rc = launch_bank_stream(L, 1, p, st)) return rc;
-    return launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    stage_mark(6, st);
+    const int rc = launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    stage_mark(7, st);
+    return rc;
 }
 
 }  // namespace chronos
@@ -150,6 +166,7 @@ int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, 
     }
     const Plan p = plan_bind(lay, workspace);
     cudaStream_t st = (cudaStream_t)stream;
+    stage_mark(0, st);
     if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, st)) return rc;
     return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, st);
 }
@@ -168,6 +185,13 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
     }
     const Plan p = plan_bind(lay, workspace);
     return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, (cudaStream_t)stream);
+}
+
+int chronos_b200_set_stage_events(void** events, int n_events) {
+    if (n_events < 0 || n_events > kStageEvents || (n_events > 0 && !events)) { set_error("set_stage_events: 0..%d events expected", kStageEvents); return CHRONOS_E_ARG; }
+    for (int i = 0; i < n_events; ++i) g_stage_events[i] = (cudaEvent_t)events[i];
+    g_n_stage_events = n_events;
+    return CHRONOS_OK;
 }
 
 int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,

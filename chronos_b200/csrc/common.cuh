@@ -13,6 +13,7 @@ namespace chronos {
 constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
 constexpr int kMaxTopK = 32;
 constexpr int kMaxRank = 128;
+constexpr int kStageEvents = 8;   // stage boundaries of one forward call that can carry a profiling event
 
 // Device-side view of the caller's workspace for one forward call. All offsets are 256-byte aligned.
 struct Plan {

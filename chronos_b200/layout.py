@@ -66,6 +66,14 @@ class FoldedLayerConfig:
         return self.rank * (2 * self.inter + self.hidden + self.hidden + self.inter)
 
 
+def _norm_device(device: torch.device | str) -> torch.device:
+    """'cuda' -> 'cuda:<current index>' so that device comparisons with tensors are exact."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return device
+
+
 def _u8(t: Any) -> torch.Tensor:
     """Tensor or array -> CPU uint8 torch tensor holding the same bytes (fp8 is reinterpreted, not converted)."""
     if isinstance(t, np.ndarray):
@@ -118,7 +126,7 @@ class PackedLayer:
     def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device):
         cfg.validate()
         self.cfg = cfg
-        self.device = torch.device(device)
+        self.device = _norm_device(device)
         self.t = tensors
         self.struct = _lib.LayerStruct()
         s = self.struct
@@ -176,7 +184,7 @@ class PackedLayer:
                     device: torch.device | str = "cuda") -> "PackedLayer":
         """`groups[g]` maps the on-disk suffixes to tensors/arrays (fp8 either as float8_e4m3fn or raw uint8).
         `shared` (optional) holds a plain-NVFP4 expert: `{gate,up,down}_proj.{weight,weight_scale,weight_scale_2}`."""
-        device = torch.device(device)
+        device = _norm_device(device)
         groups = list(groups)
         if len(groups) != cfg.n_slots:
             raise ValueError(f"{len(groups)} slot dicts for {cfg.n_slots} slots")
@@ -248,7 +256,7 @@ class PackedLayer:
         """Seeded random layer in the converter's byte format, generated on the device (for benchmarks: the real
         converter takes seconds per slot). Value ranges follow what the converter emits for N(0, 0.02) weights:
         uniform nibbles, e4m3 block-scale codes 0x58..0x77, scale_2 = amax / 2688, beta ~ 0.5, healer ~ N(0, 0.05)."""
-        device = torch.device(device)
+        device = _norm_device(device)
         gen = torch.Generator(device=device).manual_seed(seed)
         h, i, e, ns, r = cfg.hidden, cfg.inter, cfg.n_experts, cfg.n_slots, cfg.rank
 

@@ -129,6 +129,15 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
 int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,
                                   int hidden, float eps, void* stream);
 
+/* Profiling aid for the calling thread: with n_events = 8 CUDA events (cudaEvent_t handles, timing enabled) the
+ * forward entry points record events[i] on the call's stream at their stage boundaries:
+ *   0 start | 1 after router (2 launches) | 2 after plan | 3 after gate_up input transform | 4 after gate_up bank pass
+ *   | 5 after SwiGLU / down input transform | 6 after down bank pass | 7 after combine.
+ * (folded_moe_routed starts at boundary 1.)  n_events = 0 switches it off.  Events are not recorded otherwise.
+ * No counterpart in the reference (it times whole calls with torch.cuda.Event,
+ * benchmarks/dgx_spark_gb10_experiments.py:70-71). */
+int chronos_b200_set_stage_events(void** events, int n_events);
+
 /* Byte offset, inside a workspace laid out for n_tokens, of the int32 device status word that the forward entry
  * points clear at the start of a call and kernels raise on a device-side anomaly (bit 0x10: a bounded wait in the
  * streaming bank kernel expired).  Read it after synchronising the stream.  Returns -1 on bad arguments.

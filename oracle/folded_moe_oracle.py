@@ -198,12 +198,19 @@ def unbind_2d(s_mat: np.ndarray, keys) -> np.ndarray:
 # ---------------------------------------------------------------------------------------------
 # Expert reconstruction (the "fp32 reconstruction" the layer tolerance refers to)
 # ---------------------------------------------------------------------------------------------
-def reconstruct_expert(g: dict, g_idx: int, m: int, hidden: int, inter: int, include_tail: bool = False):
+def unpack_banks(g: dict):
+    """Both banks of a slot dequantised once (chronos_1t/models/glm53_holo.py:350-351)."""
+    return (unpack_nvfp4(g["s_gu.weight"], g["s_gu.weight_scale"], g["s_gu.weight_scale_2"]),
+            unpack_nvfp4(g["s_down.weight"], g["s_down.weight_scale"], g["s_down.weight_scale_2"]))
+
+
+def reconstruct_expert(g: dict, g_idx: int, m: int, hidden: int, inter: int, include_tail: bool = False, banks=None):
     """chronos_1t/models/glm53_holo.py:336-368 for one member `m` of group `g_idx`.
-    `g` maps the on-disk suffixes (glm53_holo.py:45-51) to numpy arrays (fp8 as uint8). Returns (gu [2I,H], down [H,I])."""
+    `g` maps the on-disk suffixes (glm53_holo.py:45-51) to numpy arrays (fp8 as uint8). `banks` = `unpack_banks(g)`
+    when the caller handles several members of a slot (the reference unpacks once per group call, :350-351).
+    Returns (gu [2I,H], down [H,I])."""
     seed_gu, seed_dn = group_seed_bases(g_idx)
-    s_gu = unpack_nvfp4(g["s_gu.weight"], g["s_gu.weight_scale"], g["s_gu.weight_scale_2"])
-    s_dn = unpack_nvfp4(g["s_down.weight"], g["s_down.weight_scale"], g["s_down.weight_scale_2"])
+    s_gu, s_dn = banks if banks is not None else unpack_banks(g)
     kg = expert_keys(2 * inter, hidden, m, seed_gu)
     kd = expert_keys(hidden, inter, m, seed_dn)
     h_gu = unbind_2d(s_gu, kg)
@@ -327,10 +334,13 @@ def moe_layer_forward(x, groups, router_w, top_k, hidden, inter, group_size, rou
     flat_ids = ids.reshape(-1)
     flat_w = w.reshape(-1)
     tok_of = np.repeat(np.arange(n_tok), top_k)
+    bank_cache: tuple = (-1, None)  # each distinct slot is dequantised once (chronos_1t/models/glm5_chronos_moe.py:530-539)
     for eid in np.unique(flat_ids):
         sel = np.nonzero(flat_ids == eid)[0]
         g_idx, m = int(eid) // group_size, int(eid) % group_size
-        gu_w, dn_w = reconstruct_expert(groups[g_idx], g_idx, m, hidden, inter, include_tail=include_tail)
+        if bank_cache[0] != g_idx:
+            bank_cache = (g_idx, unpack_banks(groups[g_idx]))
+        gu_w, dn_w = reconstruct_expert(groups[g_idx], g_idx, m, hidden, inter, include_tail=include_tail, banks=bank_cache[1])
         xs = x[tok_of[sel]]
         gu = xs @ gu_w.T
         act = silu(gu[:, :inter]) * gu[:, inter:]
