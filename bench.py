@@ -324,6 +324,7 @@ def main() -> None:
     ap.add_argument("--workload", default=None, choices=(None, "decode", "ep_stack"))
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=EP_LAYERS, help="depth of the ep_stack workload")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -338,7 +339,7 @@ def main() -> None:
         return
     from chronos_b200 import ep_bench
 
-    res = ep_bench.run(args, EP_LAYERS, EP_TOKENS, DECODE)
+    res = ep_bench.run(args, args.layers, EP_TOKENS, DECODE, ClockSampler)
     if rank == 0:
         print(json.dumps(res), flush=True)
 

@@ -12,7 +12,8 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX = 0, 1
-ABI_VERSION = 1
+ABI_VERSION = 2
+REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR = 0, 1, 2
 
 
 class ChronosError(RuntimeError):
@@ -45,7 +46,9 @@ EXPORTS = {
     "chronos_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int]),
     "chronos_b200_workspace_status_offset": (C.c_long, [C.POINTER(LayerStruct), C.c_int]),
     "chronos_b200_folded_moe_decode": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
-    "chronos_b200_folded_moe_routed": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "chronos_b200_folded_moe_prefill": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "chronos_b200_folded_moe_forward": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "chronos_b200_folded_moe_routed": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
     "chronos_b200_residual_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p]),
 }
 

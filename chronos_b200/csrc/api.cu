@@ -74,6 +74,20 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
     return CHRONOS_OK;
 }
 
+// The router entry point reads only the router fields, so an expert-parallel shard can route over the full
+// (replicated) router table while its bank tables hold the local slots.
+static int validate_router(const chronos_layer_t* L) {
+    if (!L) { set_error("layer is NULL"); return CHRONOS_E_ALIGN; }
+    if (L->hidden <= 0 || L->hidden % 128 || L->hidden > 32768) { set_error("router: hidden (%d) must be a positive multiple of 128", L->hidden); return CHRONOS_E_SHAPE; }
+    if (L->n_experts <= 0 || L->n_experts > 1024 || L->top_k <= 0 || L->top_k > kMaxTopK || L->top_k > L->n_experts) {
+        set_error("router: n_experts (%d) in [1, 1024] and top_k (%d) in [1, min(%d, n_experts)] required", L->n_experts, L->top_k, kMaxTopK);
+        return CHRONOS_E_SHAPE;
+    }
+    if (L->router_kind != CHRONOS_ROUTER_SOFTMAX_TOPK && L->router_kind != CHRONOS_ROUTER_SIGMOID_NOAUX) { set_error("router_kind %d is not a CHRONOS_ROUTER_* value", L->router_kind); return CHRONOS_E_ARG; }
+    if (!L->router_w) { set_error("layer.router_w is NULL"); return CHRONOS_E_ALIGN; }
+    return CHRONOS_OK;
+}
+
 static int validate_io(const void* x, int x_dtype, int n_tokens, const void* y, int y_dtype) {
     if (n_tokens < 0 || n_tokens > (1 << 20)) { set_error("n_tokens (%d) out of range", n_tokens); return CHRONOS_E_SHAPE; }
     if ((x_dtype != CHRONOS_DTYPE_F32 && x_dtype != CHRONOS_DTYPE_BF16) ||
@@ -93,18 +107,27 @@ static void stage_mark(int idx, cudaStream_t st) {
     if (idx < g_n_stage_events) cudaEventRecord(g_stage_events[idx], st);
 }
 
+// Regime choice when the caller leaves it open: the tensor-core pass pays off once a slot sees enough pairs to
+// fill MMA tiles; below that the bank bytes dominate and the streaming pass reads each of them exactly once.
+static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime) {
+    if (regime == CHRONOS_REGIME_STREAM || regime == CHRONOS_REGIME_TENSOR) return regime;
+    return (long)n_tokens * L.top_k >= 16L * L.n_slots ? CHRONOS_REGIME_TENSOR : CHRONOS_REGIME_STREAM;
+}
+
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
-                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, cudaStream_t st) {
+                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, int regime,
+                          cudaStream_t st) {
+    const bool tensor = pick_regime(L, n_tokens, regime) == CHRONOS_REGIME_TENSOR;
     stage_mark(1, st);
     if (int rc = launch_plan(L, ids, n_tokens, with_shared, p, st)) return rc;
     stage_mark(2, st);
     if (int rc = launch_pre_gu(L, x, x_dtype, p, st)) return rc;
     stage_mark(3, st);
-    if (int rc = launch_bank_stream(L, 0, p, st)) return rc;
+    if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : launch_bank_stream(L, 0, p, st)) return rc;
     stage_mark(4, st);
     if (int rc = launch_mid(L, p, st)) return rc;
     stage_mark(5, st);
-    if (int rc = launch_bank_stream(L, 1, p, st)) return rc;
+    if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : launch_bank_stream(L, 1, p, st)) return rc;
     stage_mark(6, st);
     const int rc = launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     stage_mark(7, st);
@@ -117,7 +140,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 1; }
+int chronos_b200_abi_version(void) { return 2; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -138,7 +161,7 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
 
 int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
                              float* gates, float* logits, void* stream) {
-    if (int rc = validate_layer(layer, true)) return rc;
+    if (int rc = validate_router(layer)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
     if (!ids || !gates || !logits) { set_error("router: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
     return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, (cudaStream_t)stream);
@@ -154,10 +177,11 @@ long chronos_b200_workspace_status_offset(const chronos_layer_t* layer, int n_to
     return (long)plan_layout(*layer, n_tokens).off_counters + 2 * (long)sizeof(int32_t);
 }
 
-int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
-                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y, int y_dtype,
+                        void* workspace, size_t workspace_bytes, int regime, void* stream) {
     if (int rc = validate_layer(layer, true)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (n_tokens == 0) return CHRONOS_OK;
     const PlanLayout lay = plan_layout(*layer, n_tokens);
     if (!aligned16(workspace) || workspace_bytes < lay.total) {
@@ -168,13 +192,29 @@ int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, 
     cudaStream_t st = (cudaStream_t)stream;
     stage_mark(0, st);
     if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, st)) return rc;
-    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, st);
+    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, st);
+}
+
+int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_STREAM, stream);
+}
+
+int chronos_b200_folded_moe_prefill(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_TENSOR, stream);
+}
+
+int chronos_b200_folded_moe_forward(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_AUTO, stream);
 }
 
 int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
-                                   const int32_t* ids, const float* gates, int with_shared, void* y, int y_dtype,
-                                   void* workspace, size_t workspace_bytes, void* stream) {
+                                   const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
+                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
     if (n_tokens == 0) return CHRONOS_OK;
     if (!ids || !gates) { set_error("routed: ids or gates is NULL"); return CHRONOS_E_ALIGN; }
@@ -184,7 +224,7 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
         return CHRONOS_E_WORKSPACE;
     }
     const Plan p = plan_bind(lay, workspace);
-    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, (cudaStream_t)stream);
+    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, (cudaStream_t)stream);
 }
 
 int chronos_b200_set_stage_events(void** events, int n_events) {

@@ -21,7 +21,6 @@ namespace chronos {
 constexpr int kRowsPerStage = 16;
 constexpr int kStagesPerTile = 128 / kRowsPerStage;
 constexpr int kRedStride = 132;           // floats per (warp, pair) row of the reduction buffer (bank-conflict pad)
-constexpr uint32_t kWaitLimit = 1u << 22;  // polls of a ~1 us bounded try_wait before giving up
 constexpr int kStatusBankTimeout = 0x10;
 
 struct BankArgs {
@@ -44,47 +43,11 @@ struct BankArgs {
     int nib_stride, sc_stride, stage_bytes, n_stages, n_warps;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-// Bounded wait: returns false when the phase did not complete within the poll limit.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{\n.reg .pred p;\n"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n"
-            "selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
 }
 __device__ __forceinline__ void consumer_barrier(int n_threads) {
     asm volatile("bar.sync 1, %0;" ::"r"(n_threads) : "memory");
@@ -105,6 +68,8 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
     const int RB = R / 128;
     const int n_chunks = K / 128;
     const long n_tiles = (long)a.counters[0] * RB;
+    // each CTA takes a contiguous run of tiles: consecutive row blocks of one item share their B fragments
+    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
@@ -121,44 +86,50 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
 
     if (warp == NW) {
         // ---------------- producer warp ----------------
-        if (lane == 0) {
-            uint32_t it = 0;
-            bool live = true;
-            for (long tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
-                const int item = (int)(tile / RB), rb = (int)(tile % RB);
-                const int slot = a.item_slot[item];
-                const bool sh = slot >= a.n_slots;
-                const uint8_t* wsrc = (sh ? a.sh_w : a.w + (size_t)slot * R * (K / 2)) + (size_t)rb * 128 * (K / 2);
-                const uint8_t* ssrc = (sh ? a.sh_s : a.s + (size_t)slot * R * (K / 16)) + (size_t)rb * 128 * (K / 16);
-                for (int rt = 0; rt < kStagesPerTile; ++rt, ++it) {
-                    const int s = (int)(it % (uint32_t)S);
-                    const uint32_t ph = (it / (uint32_t)S) & 1u;
-                    if (!mbar_wait(smem_u32(&bars[S + s]), ph ^ 1u)) {
-                        // consumers stopped releasing stages: stop feeding; they run into their own bounded waits
-                        atomicOr(a.counters + 2, kStatusBankTimeout);
-                        live = false;
-                        break;
-                    }
-                    const uint32_t full = smem_u32(&bars[s]);
-                    mbar_expect_tx(full, stage_tx);
-                    const uint32_t dst = smem_u32(stage0 + (size_t)s * a.stage_bytes);
-                    const uint8_t* wr = wsrc + (size_t)rt * kRowsPerStage * (K / 2);
-                    const uint8_t* sr = ssrc + (size_t)rt * kRowsPerStage * (K / 16);
+        // Lane 0 runs the ring protocol; the row copies of a stage are issued by 32 lanes at once (lanes 0-15 one
+        // nibble row each, lanes 16-31 one scale row each) because a single thread issues bulk copies too slowly
+        // to keep HBM busy with 16 + 16 small copies per stage.
+        uint32_t it = 0;
+        bool live = true;
+        for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
+            const int item = (int)(tile / RB), rb = (int)(tile % RB);
+            const int slot = a.item_slot[item];
+            const bool sh = slot >= a.n_slots;
+            const uint8_t* wsrc = (sh ? a.sh_w : a.w + (size_t)slot * R * (K / 2)) + (size_t)rb * 128 * (K / 2);
+            const uint8_t* ssrc = (sh ? a.sh_s : a.s + (size_t)slot * R * (K / 16)) + (size_t)rb * 128 * (K / 16);
+            for (int rt = 0; rt < kStagesPerTile; ++rt, ++it) {
+                const int s = (int)(it % (uint32_t)S);
+                const uint32_t ph = (it / (uint32_t)S) & 1u;
+                const uint32_t full = smem_u32(&bars[s]);
+                int ok = 1;
+                if (lane == 0) {
+                    ok = mbar_wait(smem_u32(&bars[S + s]), ph ^ 1u) ? 1 : 0;
+                    if (ok) mbar_expect_tx(full, stage_tx);
+                    else atomicOr(a.counters + 2, kStatusBankTimeout);  // consumers stopped releasing stages
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) { live = false; break; }
+                const uint32_t dst = smem_u32(stage0 + (size_t)s * a.stage_bytes);
+                const uint8_t* wr = wsrc + (size_t)rt * kRowsPerStage * (K / 2);
+                const uint8_t* sr = ssrc + (size_t)rt * kRowsPerStage * (K / 16);
+                if (lane < 16) {
                     if (a.nib_stride == K / 2) {
-                        bulk_g2s(dst, wr, (uint32_t)(kRowsPerStage * (K / 2)), full);
+                        if (lane == 0) bulk_g2s(dst, wr, (uint32_t)(kRowsPerStage * (K / 2)), full);
                     } else {
-                        for (int rr = 0; rr < kRowsPerStage; ++rr)
-                            bulk_g2s(dst + rr * a.nib_stride, wr + (size_t)rr * (K / 2), (uint32_t)(K / 2), full);
+                        bulk_g2s(dst + lane * a.nib_stride, wr + (size_t)lane * (K / 2), (uint32_t)(K / 2), full);
                     }
+                } else {
+                    const int rr = lane - 16;
                     if (a.sc_stride == K / 16) {
-                        bulk_g2s(dst + sc_off, sr, (uint32_t)(kRowsPerStage * (K / 16)), full);
+                        if (rr == 0) bulk_g2s(dst + sc_off, sr, (uint32_t)(kRowsPerStage * (K / 16)), full);
                     } else {
-                        for (int rr = 0; rr < kRowsPerStage; ++rr)
-                            bulk_g2s(dst + sc_off + rr * a.sc_stride, sr + (size_t)rr * (K / 16), (uint32_t)(K / 16), full);
+                        bulk_g2s(dst + sc_off + rr * a.sc_stride, sr + (size_t)rr * (K / 16), (uint32_t)(K / 16), full);
                     }
                 }
             }
-            // drain: every stage handed to the copy engine must land (or be consumed) before the CTA may exit
+        }
+        // drain: every stage handed to the copy engine must land (or be consumed) before the CTA may exit
+        if (lane == 0) {
             const uint32_t issued = it;
             for (uint32_t back = 0; back < (uint32_t)S && back < issued; ++back) {
                 const uint32_t j = issued - 1 - back;
@@ -176,13 +147,17 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
     const int g = lane >> 2, q = lane & 3;
     const int consumer_threads = NW * 32;
     uint32_t it = 0;
-    for (long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    int cur_item = -1;
+    uint32_t bfrag[CPW][16];
+    for (long tile = tile_lo; tile < tile_hi; ++tile) {
         const int item = (int)(tile / RB), rb = (int)(tile % RB);
         const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
         const bool sh = slot >= a.n_slots;
 
-        // B fragments: x_c[start + g][k-slice of this warp], 32 consecutive halves per chunk for lane (g, q)
-        uint32_t bfrag[CPW][16];
+        // B fragments: x_c[start + g][k-slice of this warp], 32 consecutive halves per chunk for lane (g, q);
+        // kept across the row blocks of an item
+        if (item != cur_item) {
+        cur_item = item;
 #pragma unroll
         for (int c = 0; c < CPW; ++c) {
             const int chunk = warp * CPW + c;
@@ -198,6 +173,7 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
 #pragma unroll
                 for (int v = 0; v < 16; ++v) bfrag[c][v] = 0u;
             }
+        }
         }
         float acc[kStagesPerTile][4];
 #pragma unroll

@@ -11,6 +11,7 @@
 namespace chronos {
 
 constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
+constexpr int kPairsPerGemmItem = 128;  // pairs of ONE expert per tensor-core work item (= MMA M)
 constexpr int kMaxTopK = 32;
 constexpr int kMaxRank = 128;
 constexpr int kStageEvents = 8;   // stage boundaries of one forward call that can carry a profiling event
@@ -27,7 +28,10 @@ struct Plan {
     int32_t* item_start;   // [max_items] first sorted pair of work item
     int32_t* item_cnt;     // [max_items] 1..8 pairs
     int32_t* item_slot;    // [max_items] slot whose bank the item streams (n_slots = shared expert)
-    int32_t* counters;     // [0] = number of items, [1] = number of pairs, [2] = device status word
+    int32_t* gitem_start;  // [max_gitems] tensor-core work items: up to 128 sorted pairs of one expert
+    int32_t* gitem_cnt;
+    int32_t* gitem_slot;
+    int32_t* counters;     // [0] = number of items, [1] = number of pairs, [2] = device status word, [3] = number of gemm items
     __half* xc;            // [P, H]   transformed gate_up inputs
     float* hmid;           // [P, r]   V_gu . x
     float* z1;             // [P, 2I]  H_r(r_s2 * (S_gu . x_c)) * scale_2
@@ -36,12 +40,13 @@ struct Plan {
     float* y1;             // [P, H]   H_r(r_s2 * (S_down . a_c)) * scale_2
     int max_pairs;
     int max_items;
+    int max_gitems;
 };
 
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
-        off_item_cnt, off_item_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, total;
-    int max_pairs, max_items;
+        off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, total;
+    int max_pairs, max_items, max_gitems;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -53,6 +58,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     const size_t P = T * k + (L.shared_inter > 0 ? T : 0);
     p.max_pairs = (int)P;
     p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
+    p.max_gitems = (int)(E + 1 + P / kPairsPerGemmItem + 1);
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
     p.off_logits = take(T * E * 4);
@@ -65,6 +71,9 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_item_start = take((size_t)p.max_items * 4);
     p.off_item_cnt = take((size_t)p.max_items * 4);
     p.off_item_slot = take((size_t)p.max_items * 4);
+    p.off_gitem_start = take((size_t)p.max_gitems * 4);
+    p.off_gitem_cnt = take((size_t)p.max_gitems * 4);
+    p.off_gitem_slot = take((size_t)p.max_gitems * 4);
     p.off_counters = take(64);
     p.off_xc = take(P * H * 2);
     p.off_hmid = take(P * r * 4);
@@ -89,6 +98,9 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.item_start = (int32_t*)(b + l.off_item_start);
     p.item_cnt = (int32_t*)(b + l.off_item_cnt);
     p.item_slot = (int32_t*)(b + l.off_item_slot);
+    p.gitem_start = (int32_t*)(b + l.off_gitem_start);
+    p.gitem_cnt = (int32_t*)(b + l.off_gitem_cnt);
+    p.gitem_slot = (int32_t*)(b + l.off_gitem_slot);
     p.counters = (int32_t*)(b + l.off_counters);
     p.xc = (__half*)(b + l.off_xc);
     p.hmid = (float*)(b + l.off_hmid);
@@ -98,6 +110,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.y1 = (float*)(b + l.off_y1);
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
+    p.max_gitems = l.max_gitems;
     return p;
 }
 
@@ -114,6 +127,7 @@ int launch_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                    int y_dtype, cudaStream_t st);
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, int dtype, int n_tokens, int hidden,
                             float eps, cudaStream_t st);
 
@@ -125,6 +139,27 @@ int check_launch(const char* what);
 
 __device__ __forceinline__ float ld_act(const void* x, int dtype, size_t i) {
     return dtype == CHRONOS_DTYPE_BF16 ? __bfloat162float(((const __nv_bfloat16*)x)[i]) : ((const float*)x)[i];
+}
+
+// 16 consecutive activations starting at element i (i a multiple of 16) as fp32.
+__device__ __forceinline__ void ld_act16(const void* x, int dtype, size_t i, float (&out)[16]) {
+    if (dtype == CHRONOS_DTYPE_BF16) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + i);
+        const uint4 a = src[0], b = src[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            out[2 * q] = __uint_as_float(w[q] << 16);
+            out[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+        }
+    } else {
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = src[q];
+            out[4 * q] = v.x; out[4 * q + 1] = v.y; out[4 * q + 2] = v.z; out[4 * q + 3] = v.w;
+        }
+    }
 }
 
 // Two e4m3 bytes (low byte first) -> two fp32 values. Exact: every e4m3 value is representable in fp16.
@@ -168,12 +203,52 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     for (int i = 0; i < 4; ++i) v[i] *= 0.08838834764831845f;
 }
 
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 __device__ __forceinline__ float silu_f32(float z) { return z / (1.0f + expf(-z)); }
 
 __device__ __forceinline__ __half f32_to_f16_sat(float v) {
     unsigned short r;
     asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(r) : "f"(v));
     return __ushort_as_half(r);
+}
+// ---- mbarrier / bulk-copy primitives (every wait is bounded) ----------------------------------------------------
+constexpr uint32_t kWaitLimit = 1u << 22;  // polls of a ~1 us bounded try_wait before giving up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Bounded wait: returns false when the phase did not complete within the poll limit.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n.reg .pred p;\n"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n"
+            "selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 #endif  // __CUDACC__
 

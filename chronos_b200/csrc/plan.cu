@@ -94,8 +94,39 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         }
         carry += scan[src][kPlanThreads - 1];
     }
+    const int n_items_total = carry;
+    // tensor-core work items: expert e (bin n_experts = shared expert) owns sorted pairs [off[e], off[e+1]), cut into
+    // blocks of 128 so that one MMA tile never mixes experts
+    carry = 0;
+    for (int base = 0; base < n_bins; base += kPlanThreads) {
+        const int e = base + tid;
+        int lo = 0, hi = 0;
+        if (e < n_bins) { lo = off[e]; hi = off[e + 1]; }
+        const int ni = (hi - lo + kPairsPerGemmItem - 1) / kPairsPerGemmItem;
+        int src = 0;
+        __syncthreads();
+        scan[0][tid] = ni;
+        __syncthreads();
+        for (int d = 1; d < kPlanThreads; d <<= 1) {
+            const int a = scan[src][tid] + (tid >= d ? scan[src][tid - d] : 0);
+            scan[src ^ 1][tid] = a;
+            src ^= 1;
+            __syncthreads();
+        }
+        const int first = carry + scan[src][tid] - ni;
+        for (int q = 0; q < ni; ++q) {
+            const int it = first + q;
+            if (it < p.max_gitems) {
+                p.gitem_start[it] = lo + q * kPairsPerGemmItem;
+                p.gitem_cnt[it] = min(kPairsPerGemmItem, hi - lo - q * kPairsPerGemmItem);
+                p.gitem_slot[it] = e < n_experts ? e / group_size : n_slots;
+            }
+        }
+        carry += scan[src][kPlanThreads - 1];
+    }
     if (tid == 0) {
-        p.counters[0] = min(carry, p.max_items);
+        p.counters[3] = min(carry, p.max_gitems);
+        p.counters[0] = min(n_items_total, p.max_items);
         p.counters[1] = off[n_bins];
         p.counters[2] = 0;
     }

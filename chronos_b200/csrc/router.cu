@@ -3,50 +3,62 @@
 
 namespace chronos {
 
-constexpr int kRtTok = 4;  // tokens per warp tile
-constexpr int kRtExp = 4;  // experts per warp tile
-
 // logits[t, e] = sum_k x[t, k] * w[e, k] with lane l accumulating k = l, l+32, ... ascending by FMA from +0,
 // lanes combined by the xor butterfly 16, 8, 4, 2, 1. Any tiling gives the same bits because every (t, e) dot is
-// owned by one warp and walks k in that order. Each warp computes a 4-token x 4-expert tile.
+// owned by one warp and walks k in that order. Each warp computes a TOK-token x EXP-expert tile: (4, 1) spreads
+// decode-sized batches over many warps, (4, 4) reuses loaded operands for prefill-sized ones.
+template <int TOK, int EXP>
 __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int x_dtype,
                                                             const float* __restrict__ w, float* __restrict__ logits,
                                                             int n_tokens, int n_experts, int hidden) {
     const int lane = threadIdx.x & 31;
     const int warp_in_block = threadIdx.x >> 5;
-    const int e_tiles = (n_experts + kRtExp - 1) / kRtExp;
-    const int t_tiles = (n_tokens + kRtTok - 1) / kRtTok;
+    const int e_tiles = (n_experts + EXP - 1) / EXP;
+    const int t_tiles = (n_tokens + TOK - 1) / TOK;
     const long tile = (long)blockIdx.x * 8 + warp_in_block;
     if (tile >= (long)e_tiles * t_tiles) return;
     // consecutive warps of a block share the token tile (x stays in L1) and walk over expert tiles
     const int tt = (int)(tile / e_tiles), et = (int)(tile % e_tiles);
-    const int t0 = tt * kRtTok, e0 = et * kRtExp;
-    float acc[kRtTok][kRtExp];
+    const int t0 = tt * TOK, e0 = et * EXP;
+    float acc[TOK][EXP];
 #pragma unroll
-    for (int a = 0; a < kRtTok; ++a)
+    for (int a = 0; a < TOK; ++a)
 #pragma unroll
-        for (int b = 0; b < kRtExp; ++b) acc[a][b] = 0.0f;
-    for (int k = lane; k < hidden; k += 32) {
-        float xv[kRtTok], wv[kRtExp];
+        for (int b = 0; b < EXP; ++b) acc[a][b] = 0.0f;
+    size_t xoff[TOK], woff[EXP];
 #pragma unroll
-        for (int a = 0; a < kRtTok; ++a) {
-            const int t = min(t0 + a, n_tokens - 1);
-            xv[a] = ld_act(x, x_dtype, (size_t)t * hidden + k);
+    for (int a = 0; a < TOK; ++a) xoff[a] = (size_t)min(t0 + a, n_tokens - 1) * hidden;
+#pragma unroll
+    for (int b = 0; b < EXP; ++b) woff[b] = (size_t)min(e0 + b, n_experts - 1) * hidden;
+    constexpr int UN = 8;  // k-steps whose loads are issued together (the FMA order per dot is unchanged)
+    int k = lane;
+    for (; k + (UN - 1) * 32 < hidden; k += UN * 32) {
+        float xv[UN][TOK], wv[UN][EXP];
+#pragma unroll
+        for (int u = 0; u < UN; ++u) {
+#pragma unroll
+            for (int a = 0; a < TOK; ++a) xv[u][a] = ld_act(x, x_dtype, xoff[a] + k + u * 32);
+#pragma unroll
+            for (int b = 0; b < EXP; ++b) wv[u][b] = w[woff[b] + k + u * 32];
         }
 #pragma unroll
-        for (int b = 0; b < kRtExp; ++b) {
-            const int e = min(e0 + b, n_experts - 1);
-            wv[b] = w[(size_t)e * hidden + k];
-        }
+        for (int u = 0; u < UN; ++u)
 #pragma unroll
-        for (int a = 0; a < kRtTok; ++a)
+            for (int a = 0; a < TOK; ++a)
 #pragma unroll
-            for (int b = 0; b < kRtExp; ++b) acc[a][b] = __fmaf_rn(xv[a], wv[b], acc[a][b]);
+                for (int b = 0; b < EXP; ++b) acc[a][b] = __fmaf_rn(xv[u][a], wv[u][b], acc[a][b]);
+    }
+    for (; k < hidden; k += 32) {
+#pragma unroll
+        for (int a = 0; a < TOK; ++a)
+#pragma unroll
+            for (int b = 0; b < EXP; ++b)
+                acc[a][b] = __fmaf_rn(ld_act(x, x_dtype, xoff[a] + k), w[woff[b] + k], acc[a][b]);
     }
 #pragma unroll
-    for (int a = 0; a < kRtTok; ++a)
+    for (int a = 0; a < TOK; ++a)
 #pragma unroll
-        for (int b = 0; b < kRtExp; ++b) {
+        for (int b = 0; b < EXP; ++b) {
             float v = acc[a][b];
 #pragma unroll
             for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -127,9 +139,15 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
                   float* logits, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
-    const long tiles = (long)((L.n_experts + kRtExp - 1) / kRtExp) * ((n_tokens + kRtTok - 1) / kRtTok);
-    router_logits_kernel<<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
-                                                                     L.n_experts, L.hidden);
+    if (n_tokens <= 64) {
+        const long tiles = (long)L.n_experts * ((n_tokens + 3) / 4);
+        router_logits_kernel<4, 1><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
+                                                                               L.n_experts, L.hidden);
+    } else {
+        const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
+        router_logits_kernel<4, 4><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
+                                                                               L.n_experts, L.hidden);
+    }
     if (int rc = check_launch("router_logits")) return rc;
     router_topk_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(logits, L.e_bias, L.router_kind, L.renorm,
                                                                       L.routed_scaling, n_tokens, L.n_experts,

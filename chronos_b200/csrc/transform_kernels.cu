@@ -47,7 +47,8 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
         *reinterpret_cast<uint2*>(p.xc + (size_t)pair * H + blk * 128 + lane * 4) = o;
         return;
     }
-    // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, 8 rank rows)
+    // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, 8 rank rows).
+    // Lane l owns 16 consecutive columns per 512-column step: one 16-byte load per rank row.
     const long hw = gw - xf_warps;
     const int rgroups = r / 8;
     const int pair = (int)(hw / rgroups), rg = (int)(hw % rgroups);
@@ -58,18 +59,23 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
     const uint8_t* vbase = L.v_gu + ((size_t)e * r + rg * 8) * H;
-    for (int k = lane * 4; k < H; k += 128) {
-        float xv[4];
+    for (int k = lane * 16; k < H; k += 512) {
+        uint4 vw[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = ld_act(x, x_dtype, (size_t)t * H + k + i);
+        for (int c = 0; c < 8; ++c) vw[c] = *reinterpret_cast<const uint4*>(vbase + (size_t)c * H + k);
+        float xv[16];
+        ld_act16(x, x_dtype, (size_t)t * H + k, xv);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(vbase + (size_t)c * H + k);
-            const float2 lo = e4m3x2_to_f32((uint16_t)(w & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(w >> 16));
-            acc[c] = fmaf(lo.x, xv[0], acc[c]);
-            acc[c] = fmaf(lo.y, xv[1], acc[c]);
-            acc[c] = fmaf(hi.x, xv[2], acc[c]);
-            acc[c] = fmaf(hi.y, xv[3], acc[c]);
+            const uint32_t ww[4] = {vw[c].x, vw[c].y, vw[c].z, vw[c].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
+                acc[c] = fmaf(lo.x, xv[q * 4 + 0], acc[c]);
+                acc[c] = fmaf(lo.y, xv[q * 4 + 1], acc[c]);
+                acc[c] = fmaf(hi.x, xv[q * 4 + 2], acc[c]);
+                acc[c] = fmaf(hi.y, xv[q * 4 + 3], acc[c]);
+            }
         }
     }
 #pragma unroll
@@ -158,19 +164,36 @@ __global__ void __launch_bounds__(256) mid_kernel(chronos_layer_t L, Plan p) {
         for (int i = 0; i < 4; ++i)
             if ((sw >> i) & 1u) v[i] = -v[i];
         __syncwarp();
-        // partial down-healer input: hpart[pair, blk, c] = sum_{j in block} V_down^T[e, i(j), c] * act(i(j))
+        // partial down-healer input: hpart[pair, blk, c] = sum_{j in block} V_down^T[e, i(j), c] * act(i(j)).
+        // A row of V_down^T is r bytes = r/16 chunks of 16; lane = (row selector, chunk): 32/(r/16) rows per step.
         const uint8_t* vt = L.v_dn_t + (size_t)e * I * r;
-        for (int cp = lane; cp < r / 2; cp += 32) {
-            float a0 = 0.0f, a1 = 0.0f;
-            for (int jj = 0; jj < 128; ++jj) {
-                const uint16_t w = *reinterpret_cast<const uint16_t*>(vt + (size_t)idx_s[wib][jj] * r + cp * 2);
-                const float2 vv = e4m3x2_to_f32(w);
-                a0 = fmaf(vv.x, act_s[wib][jj], a0);
-                a1 = fmaf(vv.y, act_s[wib][jj], a1);
+        const int cpr = r / 16, rpi = 32 / cpr;
+        const int rsel = lane / cpr, chunk = lane % cpr;
+        float hacc[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) hacc[c] = 0.0f;
+#pragma unroll 4
+        for (int j0 = 0; j0 < 128; j0 += rpi) {
+            const int jj = j0 + rsel;
+            const uint4 w = *reinterpret_cast<const uint4*>(vt + (size_t)idx_s[wib][jj] * r + chunk * 16);
+            const float a = act_s[wib][jj];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
+                hacc[q * 4 + 0] = fmaf(lo.x, a, hacc[q * 4 + 0]);
+                hacc[q * 4 + 1] = fmaf(lo.y, a, hacc[q * 4 + 1]);
+                hacc[q * 4 + 2] = fmaf(hi.x, a, hacc[q * 4 + 2]);
+                hacc[q * 4 + 3] = fmaf(hi.y, a, hacc[q * 4 + 3]);
             }
-            float* hp = p.hpart + ((size_t)pair * nblk + blk) * r + cp * 2;
-            hp[0] = a0;
-            hp[1] = a1;
+        }
+        for (int off = cpr; off < 32; off <<= 1)
+#pragma unroll
+            for (int c = 0; c < 16; ++c) hacc[c] += __shfl_xor_sync(0xffffffffu, hacc[c], off);
+        if (rsel == 0) {
+            float4* hp = reinterpret_cast<float4*>(p.hpart + ((size_t)pair * nblk + blk) * r + chunk * 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) hp[q] = make_float4(hacc[q * 4], hacc[q * 4 + 1], hacc[q * 4 + 2], hacc[q * 4 + 3]);
         }
     }
     __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
@@ -191,63 +214,79 @@ int launch_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
 // ---------------------------------------------------------------------------------------------------------------
 // Combine: y[t, i] = sum_j gate[t, j] * (beta_d * r_s1[i] * y1[p_j, r_inv[i]] + U_down[e_j, i, :] . hd[p_j, :])
 //                    (+ shared expert row), summed over j = 0..top_k-1 in that order.
-// One block per (token, 256 output rows).
+// One block per (token, 128 output rows): warp w evaluates routing entries j = w, w+8, ...; lane l owns rows 4l..4l+3;
+// the per-entry terms meet in shared memory and are added in index order (deterministic).
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p, const float* __restrict__ gates,
                                                       int with_shared, void* __restrict__ y, int y_dtype) {
-    __shared__ float hd[kMaxTopK][kMaxRank];
-    __shared__ int pos_s[kMaxTopK];
-    const int t = blockIdx.x, i = blockIdx.y * 256 + threadIdx.x;
+    __shared__ float hd[8][kMaxRank];
+    __shared__ __align__(16) float terms[kMaxTopK][128];
+    const int t = blockIdx.x, rb = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int H = L.hidden, I = L.inter, E = L.n_experts, r = L.rank, k = L.top_k;
     const int nblk = I / 128;
-    if (threadIdx.x < k) pos_s[threadIdx.x] = p.pos_of[t * k + threadIdx.x];
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < k * r; idx += 256) {
-        const int j = idx / r, c = idx % r;
-        float s = 0.0f;
-        if (pos_s[j] >= 0)
-            for (int b = 0; b < nblk; ++b) s += p.hpart[((size_t)pos_s[j] * nblk + b) * r + c];
-        hd[j][c] = s;
-    }
-    __syncthreads();
-    if (i >= H) return;
-    float acc = 0.0f;
-    for (int j = 0; j < k; ++j) {
-        const int pos = pos_s[j];
-        if (pos < 0) continue;
-        const int e = p.pair_expert[pos];
-        const uint16_t ro = L.dn_rout[(size_t)e * H + i];
-        float yb = p.y1[(size_t)pos * H + (ro & 0x7fff)];
-        if (ro >> 15) yb = -yb;
-        float heal = 0.0f;
-        const uint4* urow = reinterpret_cast<const uint4*>(L.u_dn + ((size_t)e * H + i) * r);
-        for (int c16 = 0; c16 < r / 16; ++c16) {
-            const uint4 u = urow[c16];
-            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+    const int row0 = rb * 128 + lane * 4;
+    for (int j = warp; j < k; j += 8) {
+        const int pos = p.pos_of[t * k + j];
+        float out[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (pos >= 0) {
+            for (int c = lane; c < r; c += 32) {
+                float s = 0.0f;
+                for (int b = 0; b < nblk; ++b) s += p.hpart[((size_t)pos * nblk + b) * r + c];
+                hd[warp][c] = s;
+            }
+            __syncwarp();
+            const int e = p.pair_expert[pos];
+            const float g = gates[t * k + j], beta = L.dn_beta[e];
+            const uint2 ro2 = *reinterpret_cast<const uint2*>(L.dn_rout + (size_t)e * H + row0);
+            const uint32_t ro[4] = {ro2.x & 0xffffu, ro2.x >> 16, ro2.y & 0xffffu, ro2.y >> 16};
+            float yb[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float2 lo = e4m3x2_to_f32((uint16_t)(uw[q] & 0xffffu));
-                const float2 hi = e4m3x2_to_f32((uint16_t)(uw[q] >> 16));
-                const float* hp = &hd[j][c16 * 16 + q * 4];
-                heal = fmaf(lo.x, hp[0], heal);
-                heal = fmaf(lo.y, hp[1], heal);
-                heal = fmaf(hi.x, hp[2], heal);
-                heal = fmaf(hi.y, hp[3], heal);
+                const float v = p.y1[(size_t)pos * H + (ro[q] & 0x7fffu)];
+                yb[q] = (ro[q] >> 15) ? -v : v;
             }
+            const uint4* urow = reinterpret_cast<const uint4*>(L.u_dn + ((size_t)e * H + row0) * r);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float heal = 0.0f;
+                for (int c16 = 0; c16 < r / 16; ++c16) {
+                    const uint4 u = urow[q * (r / 16) + c16];
+                    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int w4 = 0; w4 < 4; ++w4) {
+                        const float2 lo = e4m3x2_to_f32((uint16_t)(uw[w4] & 0xffffu));
+                        const float2 hi = e4m3x2_to_f32((uint16_t)(uw[w4] >> 16));
+                        const float* hp = &hd[warp][c16 * 16 + w4 * 4];
+                        heal = fmaf(lo.x, hp[0], heal);
+                        heal = fmaf(lo.y, hp[1], heal);
+                        heal = fmaf(hi.x, hp[2], heal);
+                        heal = fmaf(hi.y, hp[3], heal);
+                    }
+                }
+                out[q] = g * fmaf(beta, yb[q], heal);
+            }
+            __syncwarp();
         }
-        acc = fmaf(gates[t * k + j], fmaf(L.dn_beta[e], yb, heal), acc);
+        *reinterpret_cast<float4*>(&terms[j][lane * 4]) = make_float4(out[0], out[1], out[2], out[3]);
     }
-    if (with_shared) acc += p.y1[(size_t)(p.offsets[E] + t) * H + i];
-    if (y_dtype == CHRONOS_DTYPE_BF16)
-        reinterpret_cast<__nv_bfloat16*>(y)[(size_t)t * H + i] = __float2bfloat16(acc);
-    else
-        reinterpret_cast<float*>(y)[(size_t)t * H + i] = acc;
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int i = rb * 128 + threadIdx.x;
+        float acc = 0.0f;
+        for (int j = 0; j < k; ++j) acc += terms[j][threadIdx.x];
+        if (with_shared) acc += p.y1[(size_t)(p.offsets[E] + t) * H + i];
+        if (y_dtype == CHRONOS_DTYPE_BF16)
+            reinterpret_cast<__nv_bfloat16*>(y)[(size_t)t * H + i] = __float2bfloat16(acc);
+        else
+            reinterpret_cast<float*>(y)[(size_t)t * H + i] = acc;
+    }
 }
 
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                    int y_dtype, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
-    dim3 grid((unsigned)n_tokens, (unsigned)((L.hidden + 255) / 256));
+    dim3 grid((unsigned)n_tokens, (unsigned)(L.hidden / 128));
     combine_kernel<<<grid, 256, 0, st>>>(L, p, gates, with_shared && L.shared_inter > 0, y, y_dtype);
     return check_launch("combine");
 }

@@ -1,0 +1,90 @@
+"""Expert-parallel stack benchmark (driven by bench.py): 42 folded layers, experts sharded over the ranks,
+4096 tokens per step split evenly over the ranks, residual + RMSNorm between layers."""
+from __future__ import annotations
+
+import os
+import statistics
+
+import torch
+import torch.distributed as dist
+
+from . import FoldedLayerConfig
+from .ep import ExpertParallelMoE, ExpertParallelStack, build_local_layer
+
+
+def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> dict:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29531")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        cfg = FoldedLayerConfig(**layer_kw)
+        layers = [ExpertParallelMoE(build_local_layer(cfg, 3 + l, world, rank, dev, with_shared=True), cfg) for l in range(n_layers)]
+        stack = ExpertParallelStack(layers)
+        tl = tokens // world
+        gen = torch.Generator(device=dev).manual_seed(3 + 1000 * rank)
+        h0 = torch.randn(tl, cfg.hidden, generator=gen, device=dev).to(torch.bfloat16)
+        K, W = args.steps, max(args.warmup, 3)
+        sampler = sampler_cls(local) if (sampler_cls and rank == 0) else None
+        st = torch.cuda.current_stream()
+        h = h0.clone()
+        for _ in range(W):
+            h.copy_(h0)
+            stack(h)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(K):
+            h.copy_(h0)
+            stack(h)
+        e1.record(st)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        status = max(l.layer.device_status() for l in layers[-1:])
+        # end to end: pinned host tokens -> device -> stack -> pinned host result
+        host_in = h0.cpu().pin_memory()
+        host_out = torch.empty_like(host_in).pin_memory()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(K):
+            h.copy_(host_in, non_blocking=True)
+            stack(h)
+            host_out.copy_(h, non_blocking=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms_e2e = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+        clocks = sampler.stop() if sampler else None
+        step_s = float(ms.item()) * 1e-3 / K
+        pairs = tokens * cfg.top_k
+        bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
+        healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
+        useful = n_layers * (pairs * (bank_flops + healer_flops) + tokens * bank_flops)
+        launches_per_layer = 1 + 2 + 7 + 6  # rmsnorm, router (2), routed pass (plan..combine), shared pass (plan..combine)
+        return {
+            "metric": "folded_moe_ep_stack_tokens_per_s", "value": tokens / step_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": float(ms.item()) / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 (NVFP4 weights exact in f16; fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": "ep_stack", "layers": n_layers, "tokens_per_step": tokens, "hidden": cfg.hidden,
+                       "routed_experts": cfg.n_experts, "experts_per_gpu": cfg.n_experts // world, "shared_experts": 1,
+                       "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
+                       "parallelism": f"ep{world}", "activations": "bf16", "rmsnorm_eps": 1e-6,
+                       "l2_policy": f"each rank streams {n_layers * (cfg.n_slots // world) * cfg.bank_bytes_per_slot() / 1e9:.1f} GB of banks per step (> 126 MB L2)"},
+            "e2e": {"value": tokens / (float(ms_e2e.item()) * 1e-3 / K), "unit": "tokens/s",
+                    "h2d_bytes_per_step": tokens * cfg.hidden * 2, "d2h_bytes_per_step": tokens * cfg.hidden * 2},
+            "gpu_launches": launches_per_layer * n_layers * K,
+            "clocks": clocks,
+            "useful_tflops": useful / step_s / 1e12,
+            "device_status": status,
+        }
+    finally:
+        dist.destroy_process_group()

@@ -43,6 +43,12 @@ class FoldedLayerConfig:
     routed_scaling_factor: float = 2.5
     seed_stride: int = keys.SEED_GROUP_STRIDE
     key_generator: str = "torch_cpu_v1"
+    first_slot: int = 0                    # expert-parallel shard: global index of local slot 0 (keys are seeded by it)
+    n_router_experts: int | None = None    # rows of the (replicated) router table when it is wider than the local experts
+
+    @property
+    def router_experts(self) -> int:
+        return self.n_router_experts or self.n_experts
 
     @property
     def n_slots(self) -> int:
@@ -98,7 +104,7 @@ def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.
     """Compact key tables of all experts of a layer shape. Keys depend on (slot, member, dims) only - not on the
     layer index - so one set per shape and device is shared by every layer (the reference caches them the same way,
     chronos_1t/models/glm53_holo.py:53,68-71)."""
-    ck = (cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.seed_stride, str(device))
+    ck = (cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.seed_stride, cfg.first_slot, str(device))
     hit = _KEY_TABLE_CACHE.get(ck)
     if hit is not None:
         return hit
@@ -106,7 +112,7 @@ def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.
     acc: dict[str, list[np.ndarray]] = {n: [] for n in ("gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2")}
     for eid in range(e):
         g, m = divmod(eid, k)
-        sg, sd = keys.group_seed_bases(g, cfg.seed_stride)
+        sg, sd = keys.group_seed_bases(cfg.first_slot + g, cfg.seed_stride)
         for pre, rows, cols, sb in (("gu", 2 * i, h, sg), ("dn", h, i, sd)):
             t = keys.compact_tables(rows, cols, m, sb)
             for n in ("cin", "cs2", "rout", "rs2"):
@@ -139,7 +145,19 @@ class PackedLayer:
         for name, _ in _lib.LayerStruct._fields_:
             if name in tensors:
                 setattr(s, name, tensors[name].data_ptr())
+        # the router may be wider than the local expert table (expert-parallel shards replicate the full router)
+        self.router_struct = _lib.LayerStruct()
+        rs = self.router_struct
+        rs.hidden, rs.n_experts, rs.top_k = cfg.hidden, cfg.router_experts, cfg.top_k
+        rs.router_kind, rs.renorm, rs.routed_scaling = s.router_kind, s.renorm, s.routed_scaling
+        for name in ("router_w", "e_bias"):
+            if name in tensors:
+                setattr(rs, name, tensors[name].data_ptr())
         self._check_shapes()
+
+    @property
+    def router_ptr(self):
+        return C.byref(self.router_struct)
 
     # -- shape checks: wrong or short tensors are rejected here, before any launch ---------------------------------
     def _check_shapes(self) -> None:
@@ -153,9 +171,9 @@ class PackedLayer:
             "dn_cin": (e, i), "dn_cs2": (e, i // 32), "dn_rout": (e, h), "dn_rs2": (e, h // 32),
         }
         if "router_w" in t:
-            want["router_w"] = (e, h)
+            want["router_w"] = (c.router_experts, h)
         if "e_bias" in t:
-            want["e_bias"] = (e,)
+            want["e_bias"] = (c.router_experts,)
         if "sh_gu_w" in t:
             want.update({"sh_gu_w": (2 * i, h // 2), "sh_gu_s": (2 * i, h // 16), "sh_gu_s2": (2,),
                          "sh_dn_w": (h, i // 2), "sh_dn_s": (h, i // 16), "sh_dn_s2": (1,)})
@@ -251,13 +269,52 @@ class PackedLayer:
         return cls.from_groups(cfg, groups, router_w, e_bias, shared, device)
 
     @classmethod
-    def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda", with_shared: bool = False,
-                  slots: range | None = None) -> "PackedLayer":
+    def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda",
+                  with_shared: bool = False) -> "PackedLayer":
         """Seeded random layer in the converter's byte format, generated on the device (for benchmarks: the real
         converter takes seconds per slot). Value ranges follow what the converter emits for N(0, 0.02) weights:
         uniform nibbles, e4m3 block-scale codes 0x58..0x77, scale_2 = amax / 2688, beta ~ 0.5, healer ~ N(0, 0.05)."""
         device = _norm_device(device)
         gen = torch.Generator(device=device).manual_seed(seed)
+        t = cls._random_slot_tensors(cfg, gen, device)
+        t["router_w"] = torch.randn(cfg.router_experts, cfg.hidden, generator=gen, device=device) * 0.02
+        if cfg.router == "sigmoid":
+            t["e_bias"] = torch.zeros(cfg.router_experts, device=device)
+        if with_shared:
+            t.update(cls._random_shared_tensors(cfg, gen, device))
+        t.update(key_tables(cfg, device))
+        return cls(cfg, t, device)
+
+    @classmethod
+    def synthetic_sharded(cls, cfg_global: FoldedLayerConfig, seed: int, slots: range, device: torch.device | str = "cuda",
+                          with_shared: bool = False) -> "PackedLayer":
+        """The slots `slots` of the seeded random layer `seed`, plus the replicated router (and shared expert).
+        Every slot is drawn from its own generator seeded by (seed, slot), so a slot holds the same bytes whatever
+        the number of ranks it is sharded over."""
+        import dataclasses
+
+        device = _norm_device(device)
+        k = cfg_global.group_size
+        cfg = dataclasses.replace(cfg_global, n_experts=len(slots) * k, first_slot=slots.start,
+                                  n_router_experts=cfg_global.n_experts)
+        one = dataclasses.replace(cfg_global, n_experts=k, first_slot=0, n_router_experts=None)
+        parts: dict[str, list[torch.Tensor]] = {}
+        for sl in slots:
+            gen = torch.Generator(device=device).manual_seed(seed * 100003 + sl)
+            for n, v in cls._random_slot_tensors(one, gen, device).items():
+                parts.setdefault(n, []).append(v)
+        t = {n: torch.cat(v) for n, v in parts.items()}
+        gen = torch.Generator(device=device).manual_seed(seed * 100003 + 99991)
+        t["router_w"] = torch.randn(cfg_global.n_experts, cfg.hidden, generator=gen, device=device) * 0.02
+        if cfg.router == "sigmoid":
+            t["e_bias"] = torch.zeros(cfg_global.n_experts, device=device)
+        if with_shared:
+            t.update(cls._random_shared_tensors(cfg, gen, device))
+        t.update(key_tables(cfg, device))
+        return cls(cfg, t, device)
+
+    @staticmethod
+    def _random_slot_tensors(cfg: FoldedLayerConfig, gen: torch.Generator, device: torch.device) -> dict[str, torch.Tensor]:
         h, i, e, ns, r = cfg.hidden, cfg.inter, cfg.n_experts, cfg.n_slots, cfg.rank
 
         def rnd_u8(shape, lo=0, hi=256):
@@ -266,7 +323,7 @@ class PackedLayer:
         def rnd_fp8(shape, std):
             return (torch.randn(shape, generator=gen, device=device) * std).to(torch.float8_e4m3fn).view(torch.uint8)
 
-        t = {
+        return {
             "gu_w": rnd_u8((ns, 2 * i, h // 2)), "gu_s": rnd_u8((ns, 2 * i, h // 16), 0x58, 0x78),
             "dn_w": rnd_u8((ns, h, i // 2)), "dn_s": rnd_u8((ns, h, i // 16), 0x58, 0x78),
             "gu_s2": torch.full((ns,), 0.08 / 2688.0, device=device), "dn_s2": torch.full((ns,), 0.08 / 2688.0, device=device),
@@ -274,19 +331,21 @@ class PackedLayer:
             "dn_beta": torch.rand(e, generator=gen, device=device) * 0.4 + 0.3,
             "u_gu": rnd_fp8((e, 2 * i, r), 0.05), "v_gu": rnd_fp8((e, r, h), 0.05),
             "u_dn": rnd_fp8((e, h, r), 0.05), "v_dn_t": rnd_fp8((e, i, r), 0.05),
-            "router_w": torch.randn(e, h, generator=gen, device=device) * 0.02,
         }
-        if cfg.router == "sigmoid":
-            t["e_bias"] = torch.zeros(e, device=device)
-        if with_shared:
-            t.update({
-                "sh_gu_w": rnd_u8((2 * i, h // 2)), "sh_gu_s": rnd_u8((2 * i, h // 16), 0x58, 0x78),
-                "sh_gu_s2": torch.full((2,), 0.08 / 2688.0, device=device),
-                "sh_dn_w": rnd_u8((h, i // 2)), "sh_dn_s": rnd_u8((h, i // 16), 0x58, 0x78),
-                "sh_dn_s2": torch.full((1,), 0.08 / 2688.0, device=device),
-            })
-        t.update(key_tables(cfg, device))
-        return cls(cfg, t, device)
+
+    @staticmethod
+    def _random_shared_tensors(cfg: FoldedLayerConfig, gen: torch.Generator, device: torch.device) -> dict[str, torch.Tensor]:
+        h, i = cfg.hidden, cfg.inter
+
+        def rnd_u8(shape, lo=0, hi=256):
+            return torch.randint(lo, hi, shape, generator=gen, device=device, dtype=torch.uint8)
+
+        return {
+            "sh_gu_w": rnd_u8((2 * i, h // 2)), "sh_gu_s": rnd_u8((2 * i, h // 16), 0x58, 0x78),
+            "sh_gu_s2": torch.full((2,), 0.08 / 2688.0, device=device),
+            "sh_dn_w": rnd_u8((h, i // 2)), "sh_dn_s": rnd_u8((h, i // 16), 0x58, 0x78),
+            "sh_dn_s2": torch.full((1,), 0.08 / 2688.0, device=device),
+        }
 
     def to_groups_numpy(self) -> tuple[list[dict[str, np.ndarray]], dict[str, np.ndarray]]:
         """Back to per-slot dicts of on-disk suffixes (numpy, fp8 as uint8) + extras: what a checker needs."""

@@ -15,7 +15,7 @@ import torch
 from torch import nn
 
 from . import _lib
-from .layout import FoldedLayerConfig, PackedLayer, layer_index_from_prefix
+from .layout import FoldedLayerConfig, PackedLayer, _norm_device, layer_index_from_prefix
 
 LIVE_BLOCKS: dict[int, "FoldedMoELayer"] = {}  # layer index -> block, read by the custom op (glm53_chronos_moe.py:273)
 
@@ -33,6 +33,12 @@ class _DummyExperts(nn.Module):
 
 
 _DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+_REGIMES = {"auto": _lib.REGIME_AUTO, "stream": _lib.REGIME_STREAM, "tensor": _lib.REGIME_TENSOR}
+
+# One scratch buffer per device, shared by every layer on it: layers of a model run one after another on the
+# worker's stream (the reference's blocks are used the same way), so they never need scratch at the same time.
+# Two forwards that overlap on the SAME device from different streams would race on it.
+_WORKSPACE_POOL: dict[torch.device, torch.Tensor] = {}
 
 
 class FoldedMoELayer(nn.Module):
@@ -48,7 +54,7 @@ class FoldedMoELayer(nn.Module):
             if not torch.cuda.is_available():
                 raise _lib.ChronosError("FoldedMoELayer needs a CUDA device: chronos_b200 has no CPU path")
             device = torch.device(f"cuda:{torch.cuda.current_device()}")
-        self.device = torch.device(device)
+        self.device = _norm_device(device)
         if packed is None:
             if shard_path is None or config is None:
                 raise ValueError("either `packed` or (`shard_path` and `config`) is required")
@@ -70,21 +76,27 @@ class FoldedMoELayer(nn.Module):
         self.experts = _DummyExperts()
         self.is_sequence_parallel = False
         self._ws: torch.Tensor | None = None
-        self._ws_tokens = 0
+        self._ws_need: dict[int, int] = {}
         self._last_n = 0
         if register:
             LIVE_BLOCKS[layer_idx] = self
 
     # -- plumbing ---------------------------------------------------------------------------------------------------
     def _workspace(self, n_tokens: int) -> torch.Tensor:
-        """Scratch is allocated once per token-count bucket and then reused, so a captured graph sees fixed pointers."""
-        if self._ws is None or n_tokens > self._ws_tokens:
+        """Scratch from the per-device pool; it only ever grows, so a captured graph keeps seeing a valid pointer as
+        long as the largest batch has been run once before capture."""
+        need = self._ws_need.get(n_tokens)
+        if need is None:
             need = _lib.lib().chronos_b200_workspace_bytes(self.packed.ptr, n_tokens)
             if need == 0:
                 raise _lib.ChronosError("workspace_bytes rejected the layer description")
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
-            self._ws_tokens = n_tokens
-        return self._ws
+            self._ws_need[n_tokens] = need
+        buf = _WORKSPACE_POOL.get(self.device)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(need, dtype=torch.uint8, device=self.device)
+            _WORKSPACE_POOL[self.device] = buf
+        self._ws = buf
+        return buf
 
     def _prep(self, hidden_states: torch.Tensor) -> torch.Tensor:
         if not hidden_states.is_cuda:
@@ -122,15 +134,17 @@ class FoldedMoELayer(nn.Module):
         n = x.shape[0]
         ids = torch.empty((n, self.top_k), dtype=torch.int32, device=self.device)
         w = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
-        logits = torch.empty((n, self.n_experts), dtype=torch.float32, device=self.device)
-        _lib.check(_lib.lib().chronos_b200_router_topk(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, ids.data_ptr(),
+        logits = torch.empty((n, self.cfg.router_experts), dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().chronos_b200_router_topk(self.packed.router_ptr, x.data_ptr(), _DTYPES[x.dtype], n, ids.data_ptr(),
                                                      w.data_ptr(), logits.data_ptr(), self._stream()))
         self.last_logits = logits
         return ids, w
 
+    route_global = route  # expert-parallel shards: ids index the full (replicated) router table
+
     @torch.no_grad()
     def routed_forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, with_shared: bool = False,
-                       out_dtype: torch.dtype | None = None) -> torch.Tensor:
+                       out_dtype: torch.dtype | None = None, regime: str = "auto") -> torch.Tensor:
         """Routed experts for caller-supplied routing (chronos_1t/models/glm53_chronos_moe.py:441-472). Entries with
         ids < 0 are skipped."""
         x = self._prep(x)
@@ -144,14 +158,15 @@ class FoldedMoELayer(nn.Module):
         ws = self._workspace(n)
         self._last_n = n
         _lib.check(_lib.lib().chronos_b200_folded_moe_routed(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, ids.data_ptr(),
-                                                           w.data_ptr(), int(with_shared), y.data_ptr(), _DTYPES[out_dtype],
+                                                           w.data_ptr(), int(with_shared), _REGIMES[regime], y.data_ptr(), _DTYPES[out_dtype],
                                                            ws.data_ptr(), ws.numel(), self._stream()))
         return y
 
     @torch.no_grad()
-    def forward_impl(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    def forward_impl(self, hidden_states: torch.Tensor, regime: str = "auto") -> torch.Tensor:
         """Router + routed experts + shared expert (chronos_1t/models/glm53_chronos_moe.py:474-483). fp32 inputs stay
-        fp32 end to end; anything else is computed from bf16 activations."""
+        fp32 end to end; anything else is computed from bf16 activations. `regime`: "auto" (by batch shape),
+        "stream" (HBM-bound decode pass) or "tensor" (tcgen05 grouped GEMM)."""
         orig_shape, orig_dtype = hidden_states.shape, hidden_states.dtype
         x = self._prep(hidden_states)
         n = x.shape[0]
@@ -159,8 +174,10 @@ class FoldedMoELayer(nn.Module):
         if n:
             ws = self._workspace(n)
             self._last_n = n
-            _lib.check(_lib.lib().chronos_b200_folded_moe_decode(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, y.data_ptr(),
-                                                               _DTYPES[x.dtype], ws.data_ptr(), ws.numel(), self._stream()))
+            fn = {"auto": _lib.lib().chronos_b200_folded_moe_forward, "stream": _lib.lib().chronos_b200_folded_moe_decode,
+                  "tensor": _lib.lib().chronos_b200_folded_moe_prefill}[regime]
+            _lib.check(fn(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, y.data_ptr(),
+                          _DTYPES[x.dtype], ws.data_ptr(), ws.numel(), self._stream()))
         return y.to(orig_dtype).view(orig_shape)
 
     def forward(self, hidden_states: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:

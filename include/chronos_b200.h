@@ -31,6 +31,10 @@ extern "C" {
 #define CHRONOS_DTYPE_F32 0
 #define CHRONOS_DTYPE_BF16 1
 
+#define CHRONOS_REGIME_AUTO 0   /* pick by pairs per slot */
+#define CHRONOS_REGIME_STREAM 1 /* HBM-bound: packed banks streamed once, up to 8 pairs per pass */
+#define CHRONOS_REGIME_TENSOR 2 /* dense: tcgen05 grouped GEMM, 128 pairs of one expert per tile */
+
 #define CHRONOS_ROUTER_SOFTMAX_TOPK 0 /* chronos_1t/models/vllm_chronos_moe.py:310-314     */
 #define CHRONOS_ROUTER_SIGMOID_NOAUX 1 /* chronos_1t/models/glm53_chronos_moe.py:392-399    */
 
@@ -99,6 +103,8 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
 /* Router: fp32 logits in the fixed summation order (lane l of 32 sums k = l, l+32, ... with FMAs, then the xor
  * butterfly 16,8,4,2,1), top-k descending with ties to the lower index, gate weights per router_kind.
  * ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k], logits f32 [n_tokens, n_experts] (scratch, also returned).
+ * Reads only hidden, n_experts, top_k, router_kind, renorm, routed_scaling, router_w and e_bias of `layer`, so an
+ * expert-parallel shard can pass a description whose n_experts is the width of the full router table.
  * Replaces: the router blocks at chronos_1t/models/vllm_chronos_moe.py:310-314 and
  *           chronos_1t/models/glm53_chronos_moe.py:392-399. */
 int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
@@ -116,13 +122,28 @@ size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens);
 int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Whole layer, tensor-core regime (prefill-shaped batches): same result contract as folded_moe_decode; the two bank
+ * passes run as grouped GEMMs on the 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory), with
+ * the NVFP4 bank tiles converted to fp16 operands on the fly (exactly) and the scale_2 / r_s2 / Walsh-Hadamard step
+ * fused into the epilogue.
+ * Replaces: the grouped dense path of ChronosGlm53SparseMoeBlock.routed_forward,
+ *           chronos_1t/models/glm53_chronos_moe.py:452-472. */
+int chronos_b200_folded_moe_prefill(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Whole layer with the regime chosen from the batch shape (tensor regime once n_tokens * top_k >= 16 * n_slots).
+ * Replaces: ChronosGlm53SparseMoeBlock.forward, chronos_1t/models/glm53_chronos_moe.py:485-486 (which picks between
+ *           its GEMV and grouped dense paths by pair count, :445). */
+int chronos_b200_folded_moe_forward(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
+                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Same, with routing supplied by the caller (ids < 0 are skipped; used by the expert-parallel host layer where
  * a rank only owns some slots).  ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k].  with_shared != 0 adds
- * the shared expert.
+ * the shared expert.  regime is a CHRONOS_REGIME_* value.
  * Replaces: ChronosGlm53SparseMoeBlock.routed_forward, chronos_1t/models/glm53_chronos_moe.py:441-472. */
 int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
-                                   const int32_t* ids, const float* gates, int with_shared, void* y, int y_dtype,
-                                   void* workspace, size_t workspace_bytes, void* stream);
+                                   const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
+                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* h[n_tokens, H] += y (when y != NULL); x_norm = h * rsqrt(mean(h^2) + eps) * (weight or 1), fp32 math.
  * Replaces: rms_norm + residual wiring, chronos_1t/models/glm53_engine.py:71-73 and :200-204. */

@@ -224,6 +224,61 @@ def test_many_tokens_on_one_slot_and_skipped_entries():
     assert layer(torch.empty(0, cfg.hidden, device="cuda")).shape == (0, cfg.hidden)
 
 
+def _pairs_reference(layer, x, ids, w):
+    """fp32 oracle of the routed experts for explicit routing (numpy arrays in, [T, H] out)."""
+    c = layer.cfg
+    groups, _ = layer.packed.to_groups_numpy()
+    ref = np.zeros((x.shape[0], c.hidden), dtype=np.float32)
+    for e in np.unique(ids[ids >= 0]):
+        gu, dn = O.reconstruct_expert(groups[e // c.group_size], int(e) // c.group_size, int(e) % c.group_size, c.hidden, c.inter)
+        for t, j in zip(*np.nonzero(ids == e)):
+            z = x[t] @ gu.T
+            ref[t] += w[t, j] * ((O.silu(z[:c.inter]) * z[c.inter:]) @ dn.T)
+    return ref
+
+
+def test_tensor_regime_matches_oracle_and_stream_regime():
+    """The tcgen05 grouped-GEMM path against the fp32 oracle, and against the streaming path on the same batch
+    (the decode-path vs prefill-path equivalence check of benchmarks/glm53_synthetic_e2e_test.py:194-204)."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=16, top_k=2)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=11, with_shared=True), register=False)
+    n = 300  # > 128 pairs on several experts: full tiles, ragged tiles and (expert 7 unused) empty ones
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(n, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, 7, (n, 2), generator=gen, device="cuda", dtype=torch.int32)
+    ids[:, 1] = (ids[:, 0] + 1 + torch.randint(0, 5, (n,), generator=gen, device="cuda", dtype=torch.int32)) % 7
+    ids[5, 0] = -1
+    w = torch.rand((n, 2), generator=gen, device="cuda")
+    y_t = layer.routed_forward(x, ids, w, regime="tensor", out_dtype=torch.float32)
+    assert layer.device_status() == 0
+    y_s = layer.routed_forward(x, ids, w, regime="stream", out_dtype=torch.float32)
+    assert layer.device_status() == 0
+    ref = _pairs_reference(layer, x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy())
+    assert _rel_l2(y_t.cpu().numpy(), ref) <= LAYER_TOL
+    assert _rel_l2(y_s.cpu().numpy(), ref) <= LAYER_TOL
+    assert _rel_l2(y_t.cpu().numpy(), y_s.cpu().numpy()) <= 2e-3
+    y_t2 = layer.routed_forward(x, ids, w, regime="tensor", out_dtype=torch.float32)
+    assert torch.equal(y_t, y_t2), "two runs on the same input must be bit-identical"
+
+
+def test_tensor_regime_whole_layer_with_router_and_shared():
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=1024, inter=384, n_experts=16, group_size=4, rank=32, top_k=4)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(200, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    y = layer.forward_impl(x, regime="tensor")
+    assert layer.device_status() == 0
+    ref, ref_ids, _ = _oracle_layer(layer, x.float().cpu().numpy())
+    ids, _ = layer.route(x)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL
+    assert torch.equal(layer.forward_impl(x, regime="auto"), y)  # 800 pairs on 4 slots: auto picks the tensor regime
+
+
 def test_residual_rmsnorm_matches_oracle():
     from chronos_b200 import residual_rmsnorm
 
