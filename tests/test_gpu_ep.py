@@ -1,0 +1,72 @@
+"""Expert-parallel path on real GPUs (needs >= 2): 2 ranks over NCCL must reproduce the single-GPU layer on the same
+seeded slots, and the 2-layer stack (residual + RMSNorm wiring) must match a single-GPU evaluation of the same stack."""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, ret):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer, residual_rmsnorm
+        from chronos_b200.ep import ExpertParallelMoE, ExpertParallelStack, build_local_layer
+
+        cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=4)
+        n_layers, tokens = 2, 64
+        gen = torch.Generator(device=dev).manual_seed(7)
+        h_all = torch.randn(tokens, cfg.hidden, generator=gen, device=dev).to(torch.bfloat16)
+        tl = tokens // world
+        layers = [ExpertParallelMoE(build_local_layer(cfg, 3 + l, world, rank, dev, with_shared=True), cfg) for l in range(n_layers)]
+        h = h_all[rank * tl:(rank + 1) * tl].clone()
+        ExpertParallelStack(layers)(h)
+        # single-GPU evaluation of the same stack: every slot on this device
+        full = [FoldedMoELayer(packed=PackedLayer.synthetic_sharded(cfg, 3 + l, range(cfg.n_slots), dev, True), register=False)
+                for l in range(n_layers)]
+        href = h_all.clone()
+        y = None
+        for lay in full:
+            x = residual_rmsnorm(href, y, None, 1e-6)
+            y = lay.forward_impl(x)
+        residual_rmsnorm(href, y, None, 1e-6)
+        ref = href[rank * tl:(rank + 1) * tl].float()
+        err = float((h.float() - ref).norm() / ref.norm())
+        ret[rank] = err
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_stack_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, ret)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert ret[r] < 1e-2, (r, ret[r])
