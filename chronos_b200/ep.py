@@ -66,7 +66,7 @@ class ExpertParallelMoE:
             return None
         none = torch.full((x_local.shape[0], self.cfg.top_k), -1, dtype=torch.int32, device=x_local.device)
         zero = torch.zeros((x_local.shape[0], self.cfg.top_k), dtype=torch.float32, device=x_local.device)
-        return self.layer.shared_layer.routed_forward(x_local, none, zero, with_shared=True, out_dtype=torch.float32)
+        return self.layer.routed_forward(x_local, none, zero, with_shared=True, out_dtype=torch.float32)
 
     @torch.no_grad()
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
