@@ -41,6 +41,7 @@ EXPORTS = {
     "chronos_b200_last_error": (C.c_char_p, []),
     "chronos_b200_dequant_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "chronos_b200_unfold_expert_fp32": (C.c_int, [C.POINTER(LayerStruct), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "chronos_b200_unfold_expert_fp32_static": (C.c_int, [C.POINTER(LayerStruct), C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "chronos_b200_router_topk": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_workspace_bytes": (C.c_size_t, [C.POINTER(LayerStruct), C.c_int]),
     "chronos_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int]),

@@ -159,6 +159,13 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
     return launch_unfold(*layer, expert, which, out, scratch, (cudaStream_t)stream);
 }
 
+int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int expert, int which, float* out, void* stream) {
+    if (int rc = validate_layer(layer, false)) return rc;
+    if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold_static: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
+    if (!out) { set_error("unfold_static: out is NULL"); return CHRONOS_E_ALIGN; }
+    return launch_unfold_static(*layer, expert, which, out, (cudaStream_t)stream);
+}
+
 int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
                              float* gates, float* logits, void* stream) {
     if (int rc = validate_router(layer)) return rc;

@@ -118,6 +118,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
 int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2, float* out, int rows, int cols,
                    cudaStream_t st);
 int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, float* scratch, cudaStream_t st);
+int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
                   float* logits, cudaStream_t st);
 int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const Plan& p,

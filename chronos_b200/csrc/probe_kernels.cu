@@ -124,4 +124,49 @@ int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, f
     return check_launch("unfold_cols");
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free variant of the reconstruction probe: the row-axis intermediate lives in a fixed device array that
+// is part of the library image, so the caller hands over nothing but the layer and the output.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr size_t kStaticScratchFloats = size_t(4) << 20;  // 4 Mi floats = 16 MiB: matrices up to rows * cols = 4,194,304
+static __device__ __align__(256) float g_unfold_scratch[kStaticScratchFloats];
+
+constexpr int kMaxDevices = 64;
+static float* g_unfold_scratch_addr[kMaxDevices];  // device address of the array on each device, filled at set-up
+
+// Set-up for the CURRENT device (first call on that device only): the array's name is a host-side handle, not an
+// address a kernel can use, so its device address is looked up once and cached.
+static int static_scratch_for_current_device(float** out) {
+    int dev = -1;
+    cudaError_t rc = cudaGetDevice(&dev);
+    if (rc != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("unfold_static: cannot identify the current device (%s)", rc == cudaSuccess ? "index out of range" : cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    if (g_unfold_scratch_addr[dev] == nullptr) {
+        float* ptr = nullptr;
+        rc = cudaGetSymbolAddress((void**)&ptr, g_unfold_scratch);
+        if (rc != cudaSuccess || ptr == nullptr) {
+            set_error("unfold_static: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(rc));
+            return CHRONOS_E_LAUNCH;
+        }
+        g_unfold_scratch_addr[dev] = ptr;
+    }
+    *out = g_unfold_scratch_addr[dev];
+    return CHRONOS_OK;
+}
+
+int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st) {
+    const size_t rows = which == 0 ? 2 * (size_t)L.inter : (size_t)L.hidden, cols = which == 0 ? (size_t)L.hidden : (size_t)L.inter;
+    if (rows * cols > kStaticScratchFloats) {
+        set_error("unfold_static: a %zu x %zu matrix needs %zu scratch floats, the built-in scratch holds %zu; "
+                  "use chronos_b200_unfold_expert_fp32 with caller-provided scratch", rows, cols, rows * cols, kStaticScratchFloats);
+        return CHRONOS_E_SHAPE;
+    }
+    float* scratch = nullptr;
+    if (int rc = static_scratch_for_current_device(&scratch)) return rc;
+    // every element of scratch[0 .. rows*cols) is written by the first kernel before the second reads it: no clearing needed
+    return launch_unfold(L, expert, which, out, scratch, st);
+}
+
 }  // namespace chronos

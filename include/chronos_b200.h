@@ -100,6 +100,20 @@ int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, cons
 int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, int which, float* out, float* scratch,
                                     void* stream);
 
+/* The same reconstruction probe for callers that cannot provide scratch memory because they cannot allocate any:
+ * code running inside a serving process whose framework has already claimed the GPU's memory for its own pool
+ * (an extra cudaMalloc there can fail or fragment the pool), or code that must not call the allocator at this point
+ * at all (a latency-critical step, a region where allocation calls are forbidden).  The row-axis intermediate is
+ * kept in a 16 MiB array that is part of the library image on every GPU that loads it, so only matrices with
+ * rows * cols <= 4,194,304 are accepted (e.g. 1536 x 2048); larger ones are refused with CHRONOS_E_SHAPE and a
+ * message naming the limit - use the entry point above for those.  The entry point calls no cudaMalloc / cudaFree
+ * and no allocating library routine.  The first call on a device looks up the array's device address (the device
+ * must be current; make that first call outside any stream capture).  All calls on a device share the one array:
+ * its previous contents are simply overwritten (nothing needs clearing), and two calls that overlap on the GPU -
+ * different streams, or a second call issued before the first finished on another stream - race on it.
+ * This entry point has no counterpart in the reference. */
+int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int expert, int which, float* out, void* stream);
+
 /* Router: fp32 logits in the fixed summation order (lane l of 32 sums k = l, l+32, ... with FMAs, then the xor
  * butterfly 16,8,4,2,1), top-k descending with ties to the lower index, gate weights per router_kind.
  * ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k], logits f32 [n_tokens, n_experts] (scratch, also returned).
