@@ -234,6 +234,13 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
     return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, (cudaStream_t)stream);
 }
 
+int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out, int32_t* status,
+                               void* stream) {
+    if (n_stages <= 0 || n_stages > 4096) { set_error("fp4_probe: n_stages (%d) out of range", n_stages); return CHRONOS_E_SHAPE; }
+    if (!aligned16(a_image) || !aligned16(b_image) || !d_out || !status) { set_error("fp4_probe: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
+    return launch_fp4_probe(a_image, b_image, n_stages, d_out, status, (cudaStream_t)stream);
+}
+
 int chronos_b200_set_stage_events(void** events, int n_events) {
     if (n_events < 0 || n_events > kStageEvents || (n_events > 0 && !events)) { set_error("set_stage_events: 0..%d events expected", kStageEvents); return CHRONOS_E_ARG; }
     for (int i = 0; i < n_events; ++i) g_stage_events[i] = (cudaEvent_t)events[i];

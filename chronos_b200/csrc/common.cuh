@@ -129,6 +129,8 @@ int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, 
                    int y_dtype, cudaStream_t st);
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, float* d_out, int32_t* status,
+                     cudaStream_t st);
 int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, int dtype, int n_tokens, int hidden,
                             float eps, cudaStream_t st);
 

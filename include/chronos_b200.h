@@ -164,6 +164,17 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
 int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,
                                   int hidden, float eps, void* stream);
 
+/* Operand-format probe of the block-scaled FP4 tensor-core path (tcgen05.mma kind::mxf4nvf4, e2m1 operands with a
+ * ue4m3 scale per 16 elements): d_out f32 [128, 32] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns.
+ * a_image: n_stages x 18432 bytes, b_image: n_stages x 6144 bytes; per stage the packed nibbles of a 128-row (resp.
+ * 32-row) x 256-column tile in K-major core-matrix order - byte(r, c, b) at c * rows * 16 + r * 16 + b, c = 16-byte
+ * chunk along K - followed by four 512-byte scale blocks (one per 64 columns; byte(r, s) at (r % 32) * 16 +
+ * (r / 32) * 4 + s).  status: one int32 the kernel raises bits in if a bounded wait expires (clear it first).
+ * The values are what unpack_nvfp4 (chronos_1t/converter/convert_glm53_flash_colab.py:81-89) gives with
+ * weight_scale_2 = 1; the reference has no tensor-core path to compare with beyond that. */
+int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out,
+                               int32_t* status, void* stream);
+
 /* Profiling aid for the calling thread: with n_events = 8 CUDA events (cudaEvent_t handles, timing enabled) the
  * forward entry points record events[i] on the call's stream at their stage boundaries:
  *   0 start | 1 after router (2 launches) | 2 after plan | 3 after gate_up input transform | 4 after gate_up bank pass

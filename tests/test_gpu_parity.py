@@ -279,6 +279,32 @@ def test_tensor_regime_whole_layer_with_router_and_shared():
     assert torch.equal(layer.forward_impl(x, regime="auto"), y)  # 800 pairs on 4 slots: auto picks the tensor regime
 
 
+@pytest.mark.parametrize("n_stages", [1, 3])
+def test_fp4_tensor_core_operand_format(n_stages):
+    """tcgen05 block-scaled FP4 MMA on re-tiled operand images == dequantise-and-multiply of the same bytes."""
+    from chronos_b200 import _lib
+    from chronos_b200.fp4_layout import tile_matrix_fp4
+
+    rng = np.random.default_rng(n_stages)
+    k = 256 * n_stages
+    a_p = rng.integers(0, 256, (128, k // 2), dtype=np.uint8)
+    b_p = rng.integers(0, 256, (32, k // 2), dtype=np.uint8)
+    a_s = rng.integers(0x28, 0x48, (128, k // 16), dtype=np.uint8)   # e4m3 2^-2 .. 2^1.9, non-negative
+    b_s = rng.integers(0x28, 0x48, (32, k // 16), dtype=np.uint8)
+    ref = O.unpack_nvfp4(a_p, a_s, 1.0).astype(np.float64) @ O.unpack_nvfp4(b_p, b_s, 1.0).astype(np.float64).T
+    a_img = tile_matrix_fp4(torch.from_numpy(a_p).cuda(), torch.from_numpy(a_s).cuda(), 128)
+    b_img = tile_matrix_fp4(torch.from_numpy(b_p).cuda(), torch.from_numpy(b_s).cuda(), 32)
+    assert a_img.shape == (1, n_stages, 18432) and b_img.shape == (1, n_stages, 6144)
+    d = torch.zeros((128, 32), dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().chronos_b200_fp4_mma_probe(a_img.data_ptr(), b_img.data_ptr(), n_stages, d.data_ptr(),
+                                                    status.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = d.cpu().numpy().astype(np.float64)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max(), np.abs(got - ref).max() / np.abs(ref).max()
+
+
 def test_residual_rmsnorm_matches_oracle():
     from chronos_b200 import residual_rmsnorm
 
