@@ -12,8 +12,8 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX = 0, 1
-ABI_VERSION = 2
-REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR = 0, 1, 2
+ABI_VERSION = 3
+REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4 = 0, 1, 2, 3
 
 
 class ChronosError(RuntimeError):
@@ -32,7 +32,8 @@ class LayerStruct(C.Structure):
             "gu_w", "gu_s", "gu_s2", "gu_beta", "dn_w", "dn_s", "dn_s2", "dn_beta",
             "u_gu", "v_gu", "u_dn", "v_dn_t",
             "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2",
-            "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2")]
+            "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
+            "gu_t", "dn_t", "sh_gu_t", "sh_dn_t")]
     )
 
 

@@ -109,25 +109,32 @@ static void stage_mark(int idx, cudaStream_t st) {
 
 // Regime choice when the caller leaves it open: the tensor-core pass pays off once a slot sees enough pairs to
 // fill MMA tiles; below that the bank bytes dominate and the streaming pass reads each of them exactly once.
-static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime) {
-    if (regime == CHRONOS_REGIME_STREAM || regime == CHRONOS_REGIME_TENSOR) return regime;
-    return (long)n_tokens * L.top_k >= 16L * L.n_slots ? CHRONOS_REGIME_TENSOR : CHRONOS_REGIME_STREAM;
+static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, bool fp4_laid_out) {
+    if (regime == CHRONOS_REGIME_STREAM_FP4 && !fp4_laid_out) regime = CHRONOS_REGIME_STREAM;  // no re-tiled banks / batch too large
+    if (regime != CHRONOS_REGIME_AUTO) return regime;
+    if ((long)n_tokens * L.top_k >= 16L * L.n_slots) return CHRONOS_REGIME_TENSOR;
+    return fp4_laid_out ? CHRONOS_REGIME_STREAM_FP4 : CHRONOS_REGIME_STREAM;
 }
 
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
                           const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, int regime,
-                          cudaStream_t st) {
-    const bool tensor = pick_regime(L, n_tokens, regime) == CHRONOS_REGIME_TENSOR;
+                          bool have_tok_scale, cudaStream_t st) {
+    const int reg = pick_regime(L, n_tokens, regime, p.bq_gu != nullptr);
+    const bool tensor = reg == CHRONOS_REGIME_TENSOR;
+    const int fp4 = reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0;
     stage_mark(1, st);
-    if (int rc = launch_plan(L, ids, n_tokens, with_shared, p, st)) return rc;
+    // token scales come from the router kernel when this call ran it; otherwise from a kernel of their own
+    if (!have_tok_scale)
+        if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, p.tok_scale, st)) return rc;
+    if (int rc = launch_plan(L, ids, n_tokens, with_shared, x, x_dtype, 0, p, st)) return rc;
     stage_mark(2, st);
-    if (int rc = launch_pre_gu(L, x, x_dtype, p, st)) return rc;
+    if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, st)) return rc;
     stage_mark(3, st);
-    if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : launch_bank_stream(L, 0, p, st)) return rc;
+    if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st))) return rc;
     stage_mark(4, st);
-    if (int rc = launch_mid(L, p, st)) return rc;
+    if (int rc = launch_mid(L, p, fp4, st)) return rc;
     stage_mark(5, st);
-    if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : launch_bank_stream(L, 1, p, st)) return rc;
+    if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st))) return rc;
     stage_mark(6, st);
     const int rc = launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     stage_mark(7, st);
@@ -140,7 +147,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 2; }
+int chronos_b200_abi_version(void) { return 3; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -171,7 +178,7 @@ int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_
     if (int rc = validate_router(layer)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
     if (!ids || !gates || !logits) { set_error("router: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
-    return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, (cudaStream_t)stream);
+    return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, nullptr, (cudaStream_t)stream);
 }
 
 size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens) {
@@ -188,7 +195,7 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
                         void* workspace, size_t workspace_bytes, int regime, void* stream) {
     if (int rc = validate_layer(layer, true)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
-    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_STREAM_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (n_tokens == 0) return CHRONOS_OK;
     const PlanLayout lay = plan_layout(*layer, n_tokens);
     if (!aligned16(workspace) || workspace_bytes < lay.total) {
@@ -198,13 +205,13 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
     const Plan p = plan_bind(lay, workspace);
     cudaStream_t st = (cudaStream_t)stream;
     stage_mark(0, st);
-    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, st)) return rc;
-    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, st);
+    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, p.tok_scale, st)) return rc;
+    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, true, st);
 }
 
 int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
-    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_STREAM, stream);
+    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_STREAM_FP4, stream);
 }
 
 int chronos_b200_folded_moe_prefill(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
@@ -221,7 +228,7 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
                                    const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
-    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_STREAM_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
     if (n_tokens == 0) return CHRONOS_OK;
     if (!ids || !gates) { set_error("routed: ids or gates is NULL"); return CHRONOS_E_ALIGN; }
@@ -231,7 +238,7 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
         return CHRONOS_E_WORKSPACE;
     }
     const Plan p = plan_bind(lay, workspace);
-    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, (cudaStream_t)stream);
+    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, false, (cudaStream_t)stream);
 }
 
 int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out, int32_t* status,

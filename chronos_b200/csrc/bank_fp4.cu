@@ -136,6 +136,263 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64u) : "memory");
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Streaming bank pass on the block-scaled FP4 tensor cores (decode regime): no conversion work on the CUDA cores.
+//   z[pair, row] = H_128-blocks( r_s2 * scale_2 * g_pair * sum_t 32^-t * D[row, t*8 + p] ),
+//   D = (bank tile, e2m1 x ue4m3 as stored) x (activation image: 8 pairs x 3 residual e2m1 terms)^T.
+// Persistent, one CTA per SM, 6 warps:
+//   warp 0    producer: per stage two bulk copies (18432 B of re-tiled bank, 6144 B of activation image) into a ring;
+//   warp 1    MMA issuer: per stage 8 scale-block copies to tensor memory (tcgen05.cp) and 4 tcgen05.mma of
+//             128 x 32 x 64; tcgen05.commit frees the stage; two accumulator buffers in tensor memory;
+//   warps 2-5 epilogue: tcgen05.ld (thread = bank row), combine the 3 terms, scale, then per pair r_s2 sign and the
+//             128-point Walsh-Hadamard butterflies over the rows (shared-memory transpose + warp shuffles).
+// Every mbarrier wait is bounded; on expiry the role raises the status word and stops, the others run into their
+// own bounded waits.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kF4MaxStages = 8;
+constexpr int kF4Threads = 192;
+constexpr int kStatusFp4Timeout = 0x80;
+constexpr uint32_t kF4TmemCols = 512;  // 2 x 32 accumulator columns + 8 stages x (16 + 16) scale columns = 320 -> 512
+
+struct Fp4Args {
+    const uint8_t* bank_t;     // [n_slots, RB, NS, 18432]
+    const uint8_t* sh_bank_t;  // [RB, NS, 18432] shared expert (slot == n_slots)
+    const float* s2; const float* sh_s2; int sh_split;
+    const uint32_t* rs2;
+    const uint8_t* bq;         // [items, NS, 6144]
+    const float* pscale;       // [P]
+    float* zout;               // [P, R]
+    const int32_t* item_start; const int32_t* item_cnt; const int32_t* item_slot; const int32_t* pair_expert;
+    int32_t* counters;
+    int R, K, n_slots, n_stages;
+};
+
+// Shared memory: [activation image of the current work item: NS x 6144 B][ring of n_stages bank stages x 18432 B].
+// The activation image is fetched once per work item and stays while the CTA walks the item's row blocks
+// (a CTA owns a contiguous run of tiles, so it changes item only once or twice per launch).
+__global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t bars[2 * kF4MaxStages + 6];  // full[S], empty[S], acc_full[2], acc_empty[2], b_full, b_empty
+    __shared__ uint32_t tmem_base_s;
+    __shared__ __align__(16) float zs[8][132];
+    uint8_t* bimg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int R = a.R, RB = R / 128, NS = a.K / kF4StageK, S = a.n_stages;
+    uint8_t* stages = bimg + (size_t)NS * kF4BStage;  // 6144 * NS is a multiple of 1024 when NS is even; descriptors need 16 B only
+    const long n_tiles = (long)a.counters[0] * RB;
+    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kF4MaxStages;
+    uint64_t* acc_full = bars + 2 * kF4MaxStages;
+    uint64_t* acc_empty = bars + 2 * kF4MaxStages + 2;
+    uint64_t* b_full = bars + 2 * kF4MaxStages + 4;
+    uint64_t* b_empty = bars + 2 * kF4MaxStages + 5;
+
+    if (tid == 0) {
+        for (int s = 0; s < kF4MaxStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&acc_full[b]), 1); mbar_init(smem_u32(&acc_empty[b]), 4); }
+        mbar_init(smem_u32(b_full), 1);
+        mbar_init(smem_u32(b_empty), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)), "r"(kF4TmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_s;
+    const uint32_t tmem_sf0 = tmem + 64;  // per bank stage: 16 columns SFA then 16 columns SFB
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0, n_items_seen = 0;
+            int cur_item = -1;
+            bool live = true;
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
+                const int item = (int)(tile / RB), rb = (int)(tile % RB);
+                if (item != cur_item) {  // new work item: its activation image replaces the previous one
+                    if (!mbar_wait(smem_u32(b_empty), (n_items_seen & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                    mbar_expect_tx(smem_u32(b_full), (uint32_t)NS * kF4BStage);
+                    bulk_g2s(smem_u32(bimg), a.bq + (size_t)item * NS * kF4BStage, (uint32_t)NS * kF4BStage, smem_u32(b_full));
+                    cur_item = item;
+                    ++n_items_seen;
+                }
+                const int slot = a.item_slot[item];
+                const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
+                                      (size_t)rb * NS * kF4AStage;
+                for (int st = 0; st < NS; ++st, ++it) {
+                    const int s = (int)(it % (uint32_t)S);
+                    if (!mbar_wait(smem_u32(&empty[s]), ((it / (uint32_t)S) & 1u) ^ 1u)) {
+                        atomicOr(a.counters + 2, kStatusFp4Timeout);
+                        live = false;
+                        break;
+                    }
+                    mbar_expect_tx(smem_u32(&full[s]), kF4AStage);
+                    bulk_g2s(smem_u32(stages + (size_t)s * kF4AStage), asrc + (size_t)st * kF4AStage, kF4AStage, smem_u32(&full[s]));
+                }
+            }
+            // drain: copies handed to the copy engine must land before the CTA may exit
+            for (uint32_t back = 0; back < (uint32_t)S && back < it; ++back) {
+                const uint32_t j = it - 1 - back;
+                if (!mbar_wait(smem_u32(&full[j % (uint32_t)S]), (j / (uint32_t)S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+            }
+            if (n_items_seen > 0 && !mbar_wait(smem_u32(b_full), (n_items_seen - 1) & 1u)) atomicOr(a.counters + 2, kStatusFp4Timeout);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_nvf4(kF4ARows, kF4BRows);
+            uint32_t it = 0, tcount = 0, n_items_seen = 0;
+            int cur_item = -1;
+            bool live = true;
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
+                const int item = (int)(tile / RB);
+                if (item != cur_item) {
+                    if (!mbar_wait(smem_u32(b_full), n_items_seen & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                    cur_item = item;
+                    ++n_items_seen;
+                }
+                const bool last_of_item = (tile + 1 >= tile_hi) || ((int)((tile + 1) / RB) != item);
+                const uint32_t buf = tcount & 1u;
+                if (!mbar_wait(smem_u32(&acc_empty[buf]), ((tcount >> 1) & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t tmem_d = tmem + buf * 32;
+                for (int st = 0; st < NS; ++st, ++it) {
+                    const int s = (int)(it % (uint32_t)S);
+                    if (!mbar_wait(smem_u32(&full[s]), (it / (uint32_t)S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint8_t* sa = stages + (size_t)s * kF4AStage;
+                    const uint8_t* sb = bimg + (size_t)st * kF4BStage;
+                    const uint32_t sfa = tmem_sf0 + s * 32, sfb = sfa + 16;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        tc_cp_sf(sfa + 4 * j, smem_u32(sa + kF4ANib + 512 * j));
+                        tc_cp_sf(sfb + 4 * j, smem_u32(sb + kF4BNib + 512 * j));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t da = smem_desc_interleaved(smem_u32(sa + 2 * j * (kF4ARows * 16)), kF4ARows * 16);
+                        const uint64_t db = smem_desc_interleaved(smem_u32(sb + 2 * j * (kF4BRows * 16)), kF4BRows * 16);
+                        tc_mma_nvf4(tmem_d, da, db, idesc, sfa + 4 * j, sfb + 4 * j, (st > 0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit_f4(smem_u32(&empty[s]));
+                }
+                if (live) {
+                    tc_commit_f4(smem_u32(&acc_full[buf]));
+                    if (last_of_item) tc_commit_f4(smem_u32(b_empty));  // every MMA that reads this activation image is done
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue warps (TMEM lane quarter = warp % 4) ----------------
+        const int quarter = warp & 3, ew = warp - 2, et = tid - 64;  // ew 0..3, et 0..127
+        const int row = quarter * 32 + lane;
+        uint32_t tcount = 0;
+        for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
+            const int item = (int)(tile / RB), rb = (int)(tile % RB);
+            const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
+            const bool sh = slot >= a.n_slots;
+            // operands of the epilogue, fetched while the tile streams
+            const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
+            uint32_t sw[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int n = ew * 2 + q;
+                sw[q] = 0u;
+                if (n < cnt && !sh)
+                    sw[q] = a.rs2[(size_t)a.pair_expert[start + n] * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
+            }
+            float g8[8];
+#pragma unroll
+            for (int n = 0; n < 8; ++n) g8[n] = n < cnt ? a.pscale[start + n] * s2 : 0.0f;
+            const uint32_t buf = tcount & 1u;
+            // the 128 epilogue threads must take the same branch: a named barrier ORs their verdicts
+            uint32_t fail = mbar_wait(smem_u32(&acc_full[buf]), (tcount >> 1) & 1u) ? 0u : 1u;
+            asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbarrier.red.or.pred p, 2, 128, q;\nselp.u32 %0, 1, 0, p;\n}"
+                         : "=r"(fail) : "r"(fail) : "memory");
+            if (fail) { if (et == 0) atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            uint32_t d[32];
+            tmem_ld32_f4(tmem + buf * 32 + ((uint32_t)(quarter * 32) << 16), d);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));  // accumulator buffer may be overwritten
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                const float v = __uint_as_float(d[n]) + 0.03125f * __uint_as_float(d[8 + n]) + 0.0009765625f * __uint_as_float(d[16 + n]);
+                zs[n][row] = v * g8[n];
+            }
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int n = ew * 2 + q;
+                if (n < cnt) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(&zs[n][lane * 4]);
+                    float v[4] = {t4.x, t4.y, t4.z, t4.w};
+                    if (!sh) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            if ((sw[q] >> i) & 1u) v[i] = -v[i];
+                        fwht128_warp(v, lane);
+                    }
+                    *reinterpret_cast<float4*>(a.zout + (size_t)(start + n) * R + rb * 128 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+                }
+            }
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kF4TmemCols) : "memory");
+}
+
+int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st) {
+    Fp4Args a{};
+    a.K = stage == 0 ? L.hidden : L.inter;
+    a.R = stage == 0 ? 2 * L.inter : L.hidden;
+    a.bank_t = stage == 0 ? L.gu_t : L.dn_t;
+    a.sh_bank_t = stage == 0 ? L.sh_gu_t : L.sh_dn_t;
+    a.s2 = stage == 0 ? L.gu_s2 : L.dn_s2;
+    a.sh_s2 = stage == 0 ? L.sh_gu_s2 : L.sh_dn_s2;
+    a.sh_split = stage == 0 ? L.inter : 0x7fffffff;
+    a.rs2 = stage == 0 ? L.gu_rs2 : L.dn_rs2;
+    a.bq = stage == 0 ? p.bq_gu : p.bq_dn;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
+    a.zout = stage == 0 ? p.z1 : p.y1;
+    a.item_start = p.item_start;
+    a.item_cnt = p.item_cnt;
+    a.item_slot = p.item_slot;
+    a.pair_expert = p.pair_expert;
+    a.counters = p.counters;
+    a.n_slots = L.n_slots;
+    const int ns = a.K / kF4StageK;
+    const size_t bimg = (size_t)ns * kF4BStage;
+    const size_t budget = 218 * 1024;
+    if (bimg + 2 * (size_t)kF4AStage + 1024 > budget) {
+        set_error("bank_fp4: K = %d columns need a %zu-byte activation image, too large for shared memory", a.K, bimg);
+        return CHRONOS_E_SHAPE;
+    }
+    int stages = (int)((budget - 1024 - bimg) / kF4AStage);
+    a.n_stages = stages > kF4MaxStages ? kF4MaxStages : stages;
+    const size_t smem = bimg + (size_t)a.n_stages * kF4AStage + 1024;
+    cudaError_t rc = cudaFuncSetAttribute(bank_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (rc != cudaSuccess) {
+        set_error("bank_fp4: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long max_tiles = (long)p.max_items * (a.R / 128);
+    const int grid = (int)(max_tiles < sms ? max_tiles : sms);
+    bank_fp4_kernel<<<grid, kF4Threads, smem, st>>>(a);
+    return check_launch("bank_fp4");
+}
+
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, float* d_out, int32_t* status,
                      cudaStream_t st) {
     const size_t smem = kF4AStage + kF4BStage + 1024;

@@ -30,6 +30,7 @@ struct GemmArgs {
     const uint32_t* rs2;
     const __half* xin;
     float* zout;
+    const float* pscale;
     const int32_t* item_start; const int32_t* item_cnt; const int32_t* item_slot; const int32_t* pair_expert;
     int32_t* counters;
     int R, K, n_slots;
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(256, 1) bank_gemm_kernel(const GemmArgs a) {
                 for (int i = 0; i < 32; ++i) v[c4 * 32 + i] = __uint_as_float(r[i]);
             }
             if (tid < cnt) {
-                const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
+                const float s2 = (sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot]) * a.pscale[start + tid];
 #pragma unroll
                 for (int i = 0; i < 128; ++i) v[i] *= s2;
                 if (!sh) {
@@ -226,6 +227,7 @@ int launch_bank_gemm(const chronos_layer_t& L, int stage, const Plan& p, cudaStr
     a.rs2 = stage == 0 ? L.gu_rs2 : L.dn_rs2;
     a.xin = stage == 0 ? p.xc : p.ac;
     a.zout = stage == 0 ? p.z1 : p.y1;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
     a.item_start = p.gitem_start;
     a.item_cnt = p.gitem_cnt;
     a.item_slot = p.gitem_slot;

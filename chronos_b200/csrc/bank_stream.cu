@@ -34,6 +34,7 @@ struct BankArgs {
     const uint32_t* rs2;    // [E, R/32]
     const __half* xin;      // [P, K]
     float* zout;            // [P, R]
+    const float* pscale;    // [P] power-of-two scale each pair's activation row was divided by
     const int32_t* item_start;
     const int32_t* item_cnt;
     const int32_t* item_slot;
@@ -244,8 +245,9 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
                 const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)ww * 8 + n) * kRedStride + lane * 4);
                 v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
             }
+            const float sc = s2 * a.pscale[start + n];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] *= s2;
+            for (int i = 0; i < 4; ++i) v[i] *= sc;
             if (!sh) {
                 const int e = a.pair_expert[start + n];
                 const uint32_t sw = a.rs2[(size_t)e * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
@@ -282,6 +284,7 @@ int launch_bank_stream(const chronos_layer_t& L, int stage, const Plan& p, cudaS
     a.rs2 = stage == 0 ? L.gu_rs2 : L.dn_rs2;
     a.xin = stage == 0 ? p.xc : p.ac;
     a.zout = stage == 0 ? p.z1 : p.y1;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
     a.item_start = p.item_start;
     a.item_cnt = p.item_cnt;
     a.item_slot = p.item_slot;

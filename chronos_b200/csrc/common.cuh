@@ -38,6 +38,13 @@ struct Plan {
     __half* ac;            // [P, I]   transformed down inputs
     float* hpart;          // [P, I/128, r] partial V_down . act per 128-block
     float* y1;             // [P, H]   H_r(r_s2 * (S_down . a_c)) * scale_2
+    float* act;            // [P, I]   SwiGLU outputs, natural order
+    float* act_ss;         // [P, I/128] partial sums of squares of act
+    float* tok_scale;      // [T]      power-of-two scale near rms(x[t]) (FP4 streaming regime)
+    float* pscale_gu;      // [P]      scale the pair's gate_up activation image was divided by
+    float* pscale_dn;      // [P]      same for the down image
+    uint8_t* bq_gu;        // [max_items, H/256, 6144] FP4 activation images of the gate_up pass (NULL: not laid out)
+    uint8_t* bq_dn;        // [max_items, I/256, 6144]
     int max_pairs;
     int max_items;
     int max_gitems;
@@ -45,7 +52,9 @@ struct Plan {
 
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
-        off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, total;
+        off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
+        off_pscale_dn, off_bq_gu, off_bq_dn, total;
+    int fp4;
     int max_pairs, max_items, max_gitems;
 };
 
@@ -81,6 +90,17 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_ac = take(P * I * 2);
     p.off_hpart = take(P * (I / 128) * r * 4);
     p.off_y1 = take(P * H * 4);
+    p.off_act = take(P * I * 4);
+    p.off_act_ss = take(P * (I / 128) * 4);
+    p.off_tok_scale = take(T * 4);
+    p.off_pscale_gu = take(P * 4);
+    p.off_pscale_dn = take(P * 4);
+    // FP4 activation images exist only for batch shapes the streaming regime serves and layers that carry re-tiled banks
+    p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
+             T * k < 16 * (size_t)L.n_slots &&
+             (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
+    p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : 0);
+    p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : 0);
     p.total = o;
     return p;
 }
@@ -108,6 +128,13 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.ac = (__half*)(b + l.off_ac);
     p.hpart = (float*)(b + l.off_hpart);
     p.y1 = (float*)(b + l.off_y1);
+    p.act = (float*)(b + l.off_act);
+    p.act_ss = (float*)(b + l.off_act_ss);
+    p.tok_scale = (float*)(b + l.off_tok_scale);
+    p.pscale_gu = (float*)(b + l.off_pscale_gu);
+    p.pscale_dn = (float*)(b + l.off_pscale_dn);
+    p.bq_gu = l.fp4 ? (uint8_t*)(b + l.off_bq_gu) : nullptr;
+    p.bq_dn = l.fp4 ? (uint8_t*)(b + l.off_bq_dn) : nullptr;
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
     p.max_gitems = l.max_gitems;
@@ -120,14 +147,16 @@ int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2,
 int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, float* scratch, cudaStream_t st);
 int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
-                  float* logits, cudaStream_t st);
-int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const Plan& p,
-                cudaStream_t st);
-int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
-int launch_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+                  float* logits, float* tok_scale, cudaStream_t st);
+int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const void* x, int x_dtype,
+                int want_tok_scale, const Plan& p, cudaStream_t st);
+int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st);
+int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st);
+int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st);
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                    int y_dtype, cudaStream_t st);
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+int launch_bank_fp4(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, float* d_out, int32_t* status,
                      cudaStream_t st);

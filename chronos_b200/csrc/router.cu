@@ -10,7 +10,8 @@ namespace chronos {
 template <int TOK, int EXP>
 __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int x_dtype,
                                                             const float* __restrict__ w, float* __restrict__ logits,
-                                                            int n_tokens, int n_experts, int hidden) {
+                                                            int n_tokens, int n_experts, int hidden,
+                                                            float* __restrict__ tok_scale) {
     const int lane = threadIdx.x & 31;
     const int warp_in_block = threadIdx.x >> 5;
     const int e_tiles = (n_experts + EXP - 1) / EXP;
@@ -30,6 +31,12 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
     for (int a = 0; a < TOK; ++a) xoff[a] = (size_t)min(t0 + a, n_tokens - 1) * hidden;
 #pragma unroll
     for (int b = 0; b < EXP; ++b) woff[b] = (size_t)min(e0 + b, n_experts - 1) * hidden;
+    // the warp that owns expert tile 0 of a token tile also produces the tokens' power-of-two activation scales
+    // (near rms(x[t])): it reads every x element anyway
+    const bool do_scale = tok_scale != nullptr && et == 0;
+    float ssq[TOK];
+#pragma unroll
+    for (int a = 0; a < TOK; ++a) ssq[a] = 0.0f;
     constexpr int UN = 8;  // k-steps whose loads are issued together (the FMA order per dot is unchanged)
     int k = lane;
     for (; k + (UN - 1) * 32 < hidden; k += UN * 32) {
@@ -44,16 +51,32 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
 #pragma unroll
         for (int u = 0; u < UN; ++u)
 #pragma unroll
-            for (int a = 0; a < TOK; ++a)
+            for (int a = 0; a < TOK; ++a) {
 #pragma unroll
                 for (int b = 0; b < EXP; ++b) acc[a][b] = __fmaf_rn(xv[u][a], wv[u][b], acc[a][b]);
+                ssq[a] = fmaf(xv[u][a], xv[u][a], ssq[a]);
+            }
     }
     for (; k < hidden; k += 32) {
 #pragma unroll
-        for (int a = 0; a < TOK; ++a)
+        for (int a = 0; a < TOK; ++a) {
+            const float xv1 = ld_act(x, x_dtype, xoff[a] + k);
 #pragma unroll
-            for (int b = 0; b < EXP; ++b)
-                acc[a][b] = __fmaf_rn(ld_act(x, x_dtype, xoff[a] + k), w[woff[b] + k], acc[a][b]);
+            for (int b = 0; b < EXP; ++b) acc[a][b] = __fmaf_rn(xv1, w[woff[b] + k], acc[a][b]);
+            ssq[a] = fmaf(xv1, xv1, ssq[a]);
+        }
+    }
+    if (do_scale) {
+#pragma unroll
+        for (int a = 0; a < TOK; ++a) {
+            float v = ssq[a];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0 && t0 + a < n_tokens) {
+                const float rms = sqrtf(v / (float)hidden);
+                tok_scale[t0 + a] = rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
+            }
+        }
     }
 #pragma unroll
     for (int a = 0; a < TOK; ++a)
@@ -137,16 +160,16 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 }
 
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
-                  float* logits, cudaStream_t st) {
+                  float* logits, float* tok_scale, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
     if (n_tokens <= 64) {
         const long tiles = (long)L.n_experts * ((n_tokens + 3) / 4);
         router_logits_kernel<4, 1><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
-                                                                               L.n_experts, L.hidden);
+                                                                               L.n_experts, L.hidden, tok_scale);
     } else {
         const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
         router_logits_kernel<4, 4><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
-                                                                               L.n_experts, L.hidden);
+                                                                               L.n_experts, L.hidden, tok_scale);
     }
     if (int rc = check_launch("router_logits")) return rc;
     router_topk_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(logits, L.e_bias, L.router_kind, L.renorm,

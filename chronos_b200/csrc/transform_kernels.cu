@@ -8,43 +8,158 @@
 namespace chronos {
 
 // ---------------------------------------------------------------------------------------------------------------
-// gate_up input: one warp per (sorted pair, 128-column block) writes x_c in fp16; further warps compute V_gu . x.
+// FP4 quantiser: a 128-block of activations (lane l holds elements 4l..4l+3, already divided by the pair's scale) is
+// written as three residual e2m1 terms with ue4m3 scales per 16 elements into an activation stage image
+// (csrc/bank_fp4.cu describes the image): term t quantises the residual times 32^t, so the tensor-core column of
+// term t is worth 32^-t. Row of the image = t * 8 + p (p = the pair's position in its work item).
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p) {
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+    uint16_t r;
+    asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\nmov.b16 %0, {t, 0};\n}" : "=h"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {
+    uint32_t h2;
+    asm("{\n.reg .b8 t, z;\nmov.b16 {t, z}, %1;\ncvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(h2) : "h"((uint16_t)byte));
+    return __half22float2(*reinterpret_cast<__half2*>(&h2));
+}
+
+__device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int lane, uint8_t* __restrict__ stage_img,
+                                                     int half, int prow) {
+    float r[4] = {v[0], v[1], v[2], v[3]};
+    const int c = half * 4 + (lane >> 3), b = 2 * (lane & 7);
+    const int j = half * 2 + (lane >> 4), sidx = (lane & 15) >> 2;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        const float up = t == 0 ? 1.0f : (t == 1 ? 32.0f : 1024.0f);
+        float m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const uint32_t sc8 = f32x2_to_e4m3x2(m * up * (1.0f / 6.0f), 0.0f) & 0xffu;
+        const float sdec = e4m3_to_f32((uint8_t)sc8);
+        const float inv = sdec > 0.0f ? up / sdec : 0.0f;
+        const uint32_t b01 = f32x2_to_e2m1x2(r[0] * inv, r[1] * inv) & 0xffu;
+        const uint32_t b23 = f32x2_to_e2m1x2(r[2] * inv, r[3] * inv) & 0xffu;
+        const float2 q01 = e2m1x2_to_f32(b01), q23 = e2m1x2_to_f32(b23);
+        const float back = sdec / up;
+        r[0] = fmaf(-q01.x, back, r[0]); r[1] = fmaf(-q01.y, back, r[1]);
+        r[2] = fmaf(-q23.x, back, r[2]); r[3] = fmaf(-q23.y, back, r[3]);
+        const int n = t * 8 + prow;
+        *reinterpret_cast<uint16_t*>(stage_img + c * 512 + n * 16 + b) = (uint16_t)(b01 | (b23 << 8));
+        if ((lane & 3) == 0) stage_img[4096 + j * 512 + n * 16 + sidx] = (uint8_t)sc8;
+    }
+}
+
+// Power-of-two scale near the root mean square of a vector (1 when the vector is all zero).
+__device__ __forceinline__ float pow2_scale(float sumsq, int n) {
+    const float rms = sqrtf(sumsq / (float)n);
+    return rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
+}
+
+// One 128-block of a gate_up input: gather + sign, Walsh-Hadamard, sign (identity for the shared expert).
+__device__ __forceinline__ void transform_gu_block(const chronos_layer_t& L, const void* __restrict__ x, int x_dtype,
+                                                   int t, int e, int blk, int lane, float (&v)[4]) {
+    const int H = L.hidden;
+    if (e >= L.n_experts) {  // shared expert: plain weights, identity keys
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = ld_act(x, x_dtype, (size_t)t * H + blk * 128 + lane * 4 + i);
+        return;
+    }
+    const uint2 ce = *reinterpret_cast<const uint2*>(L.gu_cin + (size_t)e * H + blk * 128 + lane * 4);
+    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float xv = ld_act(x, x_dtype, (size_t)t * H + (ent[i] & 0x7fffu));
+        v[i] = (ent[i] >> 15) ? -xv : xv;
+    }
+    fwht128_warp(v, lane);
+    const uint32_t sw = L.gu_cs2[(size_t)e * (H / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
+// One 128-block of a down input from the SwiGLU outputs `act` (fp32, natural order) of the pair.
+__device__ __forceinline__ void transform_dn_block(const chronos_layer_t& L, const float* __restrict__ act, int e, int blk,
+                                                   int lane, float (&v)[4]) {
+    const int I = L.inter;
+    if (e >= L.n_experts) {
+        const float4 a = *reinterpret_cast<const float4*>(act + blk * 128 + lane * 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        return;
+    }
+    const uint2 ce = *reinterpret_cast<const uint2*>(L.dn_cin + (size_t)e * I + blk * 128 + lane * 4);
+    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float a = act[ent[i] & 0x7fffu];
+        v[i] = (ent[i] >> 15) ? -a : a;
+    }
+    fwht128_warp(v, lane);
+    const uint32_t sw = L.dn_cs2[(size_t)e * (I / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
+__device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
+    __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
+    __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&h01);
+    o.y = *reinterpret_cast<uint32_t*>(&h23);
+    *reinterpret_cast<uint2*>(dst) = o;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// gate_up input. Transform warps: fp16 mode - one warp per (sorted pair, 128-column block) writes x_c;
+// FP4 mode - one warp per (work item, position in item, 128-column block) writes three e2m1 terms into the item's
+// activation image (positions past the item's pair count are written as zeros). Further warps compute V_gu . x.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p,
+                                                     int fp4) {
     const int lane = threadIdx.x & 31;
     const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int n_pairs = p.counters[1];
     const int H = L.hidden, E = L.n_experts, r = L.rank;
     const int nblk = H / 128;
-    const long xf_warps = (long)p.max_pairs * nblk;
+    const long xf_warps = fp4 ? (long)p.max_items * kPairsPerItem * nblk : (long)p.max_pairs * nblk;
     if (gw < xf_warps) {
-        const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
-        if (pair >= n_pairs) return;
-        const int t = p.pair_token[pair], e = p.pair_expert[pair];
         float v[4];
-        if (e >= E) {  // shared expert: plain weights, identity keys
+        if (!fp4) {
+            const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
+            if (pair >= n_pairs) return;
+            const int t = p.pair_token[pair];
+            const float g = p.tok_scale[t];  // power of two: keeps the fp16 image in range whatever the activation scale
+            transform_gu_block(L, x, x_dtype, t, p.pair_expert[pair], blk, lane, v);
+            const float gi = 1.0f / g;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = ld_act(x, x_dtype, (size_t)t * H + blk * 128 + lane * 4 + i);
-        } else {
-            const uint2 ce = *reinterpret_cast<const uint2*>(L.gu_cin + (size_t)e * H + blk * 128 + lane * 4);
-            const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float xv = ld_act(x, x_dtype, (size_t)t * H + (ent[i] & 0x7fffu));
-                v[i] = (ent[i] >> 15) ? -xv : xv;
-            }
-            fwht128_warp(v, lane);
-            const uint32_t sw = L.gu_cs2[(size_t)e * (H / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if ((sw >> i) & 1u) v[i] = -v[i];
+            for (int i = 0; i < 4; ++i) v[i] *= gi;
+            if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
+            store_half4(p.xc + (size_t)pair * H + blk * 128 + lane * 4, v);
+            return;
         }
-        __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
-        __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));
-        uint2 o;
-        o.x = *reinterpret_cast<uint32_t*>(&h01);
-        o.y = *reinterpret_cast<uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(p.xc + (size_t)pair * H + blk * 128 + lane * 4) = o;
+        const int blk = (int)(gw % nblk);
+        const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
+        if (item >= p.counters[0]) return;
+        v[0] = v[1] = v[2] = v[3] = 0.0f;
+        if (pos < p.item_cnt[item]) {
+            const int pair = p.item_start[item] + pos;
+            const int t = p.pair_token[pair];
+            const float g = p.tok_scale[t];
+            transform_gu_block(L, x, x_dtype, t, p.pair_expert[pair], blk, lane, v);
+            const float gi = 1.0f / g;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] *= gi;
+            if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
+        }
+        uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * 6144;
+        quantize_block_fp4x3(v, lane, img, blk & 1, pos);
         return;
     }
     // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, 8 rank rows).
@@ -87,128 +202,189 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
     }
 }
 
-int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, cudaStream_t st) {
-    const long warps = (long)p.max_pairs * (L.hidden / 128) + (long)p.max_pairs * (L.rank / 8);
-    pre_gu_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, x, x_dtype, p);
+// Per-token power-of-two scale near rms(x[t]); one warp per token, fixed summation order.
+__global__ void __launch_bounds__(256) token_scale_kernel(const void* __restrict__ x, int x_dtype, int n_tokens, int hidden,
+                                                          float* __restrict__ tok_scale) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= n_tokens) return;
+    float ss = 0.0f;
+    for (int k = lane; k < hidden; k += 32) {
+        const float v = ld_act(x, x_dtype, (size_t)t * hidden + k);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) tok_scale[t] = pow2_scale(ss, hidden);
+}
+
+int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st) {
+    if (n_tokens <= 0) return CHRONOS_OK;
+    token_scale_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(x, x_dtype, n_tokens, hidden, tok_scale);
+    return check_launch("token_scale");
+}
+
+int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st) {
+    const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
+    const long warps = xf + (long)p.max_pairs * (L.rank / 8);
+    pre_gu_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, x, x_dtype, p, fp4);
     return check_launch("pre_gu");
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Between the passes: one warp per (sorted pair, 128-block of the down input). Each down-input element needs one
-// SwiGLU output, which needs two gate_up rows (row-inverse gather of z1 + beta + healer U_gu . hmid).
+// Between the passes, part A: SwiGLU outputs in natural order. One warp per (sorted pair, 128 outputs):
+// act[i] = silu(z_gu[i]) * z_gu[I + i] with z_gu[row] = beta * r_s1[row] * z1[r_inv[row]] + U_gu[row, :] . hmid;
+// also the pair's partial sum of squares of the block and the partial down-healer input V_down . act of the block.
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) mid_kernel(chronos_layer_t L, Plan p) {
+__global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p) {
     __shared__ float hs[8][kMaxRank];
     __shared__ float act_s[8][128];
-    __shared__ uint16_t idx_s[8][128];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const long gw = (long)blockIdx.x * 8 + wib;
     const int n_pairs = p.counters[1];
-    const int H = L.hidden, I = L.inter, E = L.n_experts, r = L.rank;
+    const int I = L.inter, E = L.n_experts, r = L.rank;
     const int nblk = I / 128;
     const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
     if (pair >= n_pairs) return;
     const int e = p.pair_expert[pair];
     const float* z1 = p.z1 + (size_t)pair * 2 * I;
-    __half* ac = p.ac + (size_t)pair * I + blk * 128 + lane * 4;
-    float v[4];
+    const int i0 = blk * 128 + lane * 4;
+    float a[4];
     if (e >= E) {  // shared expert: rows in natural order, no healer
-        const float4 zg = *reinterpret_cast<const float4*>(z1 + blk * 128 + lane * 4);
-        const float4 zu = *reinterpret_cast<const float4*>(z1 + I + blk * 128 + lane * 4);
-        v[0] = silu_f32(zg.x) * zu.x; v[1] = silu_f32(zg.y) * zu.y;
-        v[2] = silu_f32(zg.z) * zu.z; v[3] = silu_f32(zg.w) * zu.w;
+        const float4 zg = *reinterpret_cast<const float4*>(z1 + i0);
+        const float4 zu = *reinterpret_cast<const float4*>(z1 + I + i0);
+        a[0] = silu_f32(zg.x) * zu.x; a[1] = silu_f32(zg.y) * zu.y;
+        a[2] = silu_f32(zg.z) * zu.z; a[3] = silu_f32(zg.w) * zu.w;
     } else {
         for (int c = lane; c < r; c += 32) hs[wib][c] = p.hmid[(size_t)pair * r + c];
         __syncwarp();
         const float beta = L.gu_beta[e];
-        const uint2 ce = *reinterpret_cast<const uint2*>(L.dn_cin + (size_t)e * I + blk * 128 + lane * 4);
-        const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
         const uint16_t* rout = L.gu_rout + (size_t)e * 2 * I;
         const uint8_t* ug = L.u_gu + (size_t)e * 2 * I * r;
+        float zz[2][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int src_i = (int)(ent[i] & 0x7fffu);  // SwiGLU index feeding down-input position j
-            float zz[2];
+        for (int half = 0; half < 2; ++half) {
+            const uint2 ro2 = *reinterpret_cast<const uint2*>(rout + half * I + i0);
+            const uint32_t ro[4] = {ro2.x & 0xffffu, ro2.x >> 16, ro2.y & 0xffffu, ro2.y >> 16};
+            float zb[4];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int row = src_i + half * I;
-                const uint16_t ro = rout[row];
-                float zb = z1[ro & 0x7fff];
-                if (ro >> 15) zb = -zb;
+            for (int q = 0; q < 4; ++q) {
+                const float z = z1[ro[q] & 0x7fffu];
+                zb[q] = (ro[q] >> 15) ? -z : z;
+            }
+            const uint4* urow = reinterpret_cast<const uint4*>(ug + (size_t)(half * I + i0) * r);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
                 float heal = 0.0f;
-                const uint4* urow = reinterpret_cast<const uint4*>(ug + (size_t)row * r);
                 for (int c16 = 0; c16 < r / 16; ++c16) {
-                    const uint4 u = urow[c16];
+                    const uint4 u = urow[q * (r / 16) + c16];
                     const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float2 lo = e4m3x2_to_f32((uint16_t)(uw[q] & 0xffffu));
-                        const float2 hi = e4m3x2_to_f32((uint16_t)(uw[q] >> 16));
-                        const float* hp = &hs[wib][c16 * 16 + q * 4];
+                    for (int w4 = 0; w4 < 4; ++w4) {
+                        const float2 lo = e4m3x2_to_f32((uint16_t)(uw[w4] & 0xffffu));
+                        const float2 hi = e4m3x2_to_f32((uint16_t)(uw[w4] >> 16));
+                        const float* hp = &hs[wib][c16 * 16 + w4 * 4];
                         heal = fmaf(lo.x, hp[0], heal);
                         heal = fmaf(lo.y, hp[1], heal);
                         heal = fmaf(hi.x, hp[2], heal);
                         heal = fmaf(hi.y, hp[3], heal);
                     }
                 }
-                zz[half] = fmaf(beta, zb, heal);
+                zz[half][q] = fmaf(beta, zb[q], heal);
             }
-            const float a = silu_f32(zz[0]) * zz[1];
-            act_s[wib][lane * 4 + i] = a;
-            idx_s[wib][lane * 4 + i] = (uint16_t)src_i;
-            v[i] = (ent[i] >> 15) ? -a : a;
         }
-        fwht128_warp(v, lane);
-        const uint32_t sw = L.dn_cs2[(size_t)e * (I / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            if ((sw >> i) & 1u) v[i] = -v[i];
-        __syncwarp();
-        // partial down-healer input: hpart[pair, blk, c] = sum_{j in block} V_down^T[e, i(j), c] * act(i(j)).
-        // A row of V_down^T is r bytes = r/16 chunks of 16; lane = (row selector, chunk): 32/(r/16) rows per step.
-        const uint8_t* vt = L.v_dn_t + (size_t)e * I * r;
-        const int cpr = r / 16, rpi = 32 / cpr;
-        const int rsel = lane / cpr, chunk = lane % cpr;
-        float hacc[16];
+        for (int q = 0; q < 4; ++q) a[q] = silu_f32(zz[0][q]) * zz[1][q];
+    }
+    *reinterpret_cast<float4*>(p.act + (size_t)pair * I + i0) = make_float4(a[0], a[1], a[2], a[3]);
+    float ss = a[0] * a[0] + a[1] * a[1] + a[2] * a[2] + a[3] * a[3];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) hacc[c] = 0.0f;
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) p.act_ss[(size_t)pair * nblk + blk] = ss;
+    if (e >= E) return;
+    // partial down-healer input: hpart[pair, blk, c] = sum_{i in block} V_down^T[e, i, c] * act[i].
+    // A row of V_down^T is r bytes = r/16 chunks of 16; lane = (row selector, chunk): 32/(r/16) rows per step.
+    *reinterpret_cast<float4*>(&act_s[wib][lane * 4]) = make_float4(a[0], a[1], a[2], a[3]);
+    __syncwarp();
+    const uint8_t* vt = L.v_dn_t + ((size_t)e * I + blk * 128) * r;
+    const int cpr = r / 16, rpi = 32 / cpr;
+    const int rsel = lane / cpr, chunk = lane % cpr;
+    float hacc[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) hacc[c] = 0.0f;
 #pragma unroll 4
-        for (int j0 = 0; j0 < 128; j0 += rpi) {
-            const int jj = j0 + rsel;
-            const uint4 w = *reinterpret_cast<const uint4*>(vt + (size_t)idx_s[wib][jj] * r + chunk * 16);
-            const float a = act_s[wib][jj];
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    for (int j0 = 0; j0 < 128; j0 += rpi) {
+        const int jj = j0 + rsel;
+        const uint4 w = *reinterpret_cast<const uint4*>(vt + (size_t)jj * r + chunk * 16);
+        const float av = act_s[wib][jj];
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
-                hacc[q * 4 + 0] = fmaf(lo.x, a, hacc[q * 4 + 0]);
-                hacc[q * 4 + 1] = fmaf(lo.y, a, hacc[q * 4 + 1]);
-                hacc[q * 4 + 2] = fmaf(hi.x, a, hacc[q * 4 + 2]);
-                hacc[q * 4 + 3] = fmaf(hi.y, a, hacc[q * 4 + 3]);
-            }
-        }
-        for (int off = cpr; off < 32; off <<= 1)
-#pragma unroll
-            for (int c = 0; c < 16; ++c) hacc[c] += __shfl_xor_sync(0xffffffffu, hacc[c], off);
-        if (rsel == 0) {
-            float4* hp = reinterpret_cast<float4*>(p.hpart + ((size_t)pair * nblk + blk) * r + chunk * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) hp[q] = make_float4(hacc[q * 4], hacc[q * 4 + 1], hacc[q * 4 + 2], hacc[q * 4 + 3]);
+        for (int q = 0; q < 4; ++q) {
+            const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
+            hacc[q * 4 + 0] = fmaf(lo.x, av, hacc[q * 4 + 0]);
+            hacc[q * 4 + 1] = fmaf(lo.y, av, hacc[q * 4 + 1]);
+            hacc[q * 4 + 2] = fmaf(hi.x, av, hacc[q * 4 + 2]);
+            hacc[q * 4 + 3] = fmaf(hi.y, av, hacc[q * 4 + 3]);
         }
     }
-    __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
-    __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t*>(&h01);
-    o.y = *reinterpret_cast<uint32_t*>(&h23);
-    *reinterpret_cast<uint2*>(ac) = o;
-    (void)H;
+    for (int off = cpr; off < 32; off <<= 1)
+#pragma unroll
+        for (int c = 0; c < 16; ++c) hacc[c] += __shfl_xor_sync(0xffffffffu, hacc[c], off);
+    if (rsel == 0) {
+        float4* hp = reinterpret_cast<float4*>(p.hpart + ((size_t)pair * nblk + blk) * r + chunk * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) hp[q] = make_float4(hacc[q * 4], hacc[q * 4 + 1], hacc[q * 4 + 2], hacc[q * 4 + 3]);
+    }
 }
 
-int launch_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
-    const long warps = (long)p.max_pairs * (L.inter / 128);
-    mid_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, p);
-    return check_launch("mid");
+// Part B: down-input transform of the SwiGLU outputs, fp16 rows (one warp per (pair, block)) or FP4 images
+// (one warp per (work item, position, block); the pair's scale comes from the partial sums of squares of part A).
+__global__ void __launch_bounds__(256) mid_xform_kernel(chronos_layer_t L, Plan p, int fp4) {
+    const int lane = threadIdx.x & 31;
+    const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int I = L.inter, nblk = I / 128;
+    float v[4];
+    if (!fp4) {
+        const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
+        if (pair >= p.counters[1]) return;
+        float ss = 0.0f;
+        for (int b = 0; b < nblk; ++b) ss += p.act_ss[(size_t)pair * nblk + b];
+        const float g = pow2_scale(ss, I);
+        transform_dn_block(L, p.act + (size_t)pair * I, p.pair_expert[pair], blk, lane, v);
+        const float gi = 1.0f / g;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] *= gi;
+        if (blk == 0 && lane == 0) p.pscale_dn[pair] = g;
+        store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+        return;
+    }
+    const int blk = (int)(gw % nblk);
+    const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
+    if (item >= p.counters[0]) return;
+    v[0] = v[1] = v[2] = v[3] = 0.0f;
+    if (pos < p.item_cnt[item]) {
+        const int pair = p.item_start[item] + pos;
+        float ss = 0.0f;
+        for (int b = 0; b < nblk; ++b) ss += p.act_ss[(size_t)pair * nblk + b];  // fixed order: same scale in every warp
+        const float g = pow2_scale(ss, I);
+        transform_dn_block(L, p.act + (size_t)pair * I, p.pair_expert[pair], blk, lane, v);
+        const float gi = 1.0f / g;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] *= gi;
+        if (blk == 0 && lane == 0) p.pscale_dn[pair] = g;
+    }
+    uint8_t* img = p.bq_dn + ((size_t)item * (I / 256) + blk / 2) * 6144;
+    quantize_block_fp4x3(v, lane, img, blk & 1, pos);
+}
+
+int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st) {
+    const int nblk = L.inter / 128;
+    long warps = (long)p.max_pairs * nblk;
+    mid_act_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, p);
+    if (int rc = check_launch("mid_act")) return rc;
+    if (fp4) warps = (long)p.max_items * kPairsPerItem * nblk;
+    mid_xform_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, p, fp4);
+    return check_launch("mid_xform");
 }
 
 // ---------------------------------------------------------------------------------------------------------------

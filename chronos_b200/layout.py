@@ -129,9 +129,11 @@ def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.
 class PackedLayer:
     """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
 
-    def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device):
+    def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device,
+                 fp4_images: bool = True):
         cfg.validate()
         self.cfg = cfg
+        self.fp4_images = fp4_images
         self.device = _norm_device(device)
         self.t = tensors
         self.struct = _lib.LayerStruct()
@@ -142,6 +144,7 @@ class PackedLayer:
         s.renorm = int(cfg.norm_topk_prob)
         s.routed_scaling = float(cfg.routed_scaling_factor)
         s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
+        self._add_fp4_images()
         for name, _ in _lib.LayerStruct._fields_:
             if name in tensors:
                 setattr(s, name, tensors[name].data_ptr())
@@ -154,6 +157,20 @@ class PackedLayer:
             if name in tensors:
                 setattr(rs, name, tensors[name].data_ptr())
         self._check_shapes()
+
+    def _add_fp4_images(self) -> None:
+        """Re-tiled bank copies for the block-scaled FP4 tensor-core pass (a byte permutation done once at load;
+        needs hidden and inter to be multiples of 256; doubles the resident bank bytes)."""
+        from .fp4_layout import tile_matrix_fp4
+
+        c, t = self.cfg, self.t
+        if c.hidden % 256 or c.inter % 256 or self.device.type != "cuda" or not self.fp4_images or "gu_t" in t:
+            return
+        t["gu_t"] = tile_matrix_fp4(t["gu_w"], t["gu_s"], 128)
+        t["dn_t"] = tile_matrix_fp4(t["dn_w"], t["dn_s"], 128)
+        if "sh_gu_w" in t:
+            t["sh_gu_t"] = tile_matrix_fp4(t["sh_gu_w"], t["sh_gu_s"], 128)
+            t["sh_dn_t"] = tile_matrix_fp4(t["sh_dn_w"], t["sh_dn_s"], 128)
 
     @property
     def router_ptr(self):
@@ -361,6 +378,7 @@ class PackedLayer:
                 "healer.u_gu": t["u_gu"][sl], "healer.v_gu": t["v_gu"][sl], "healer.u_down": t["u_dn"][sl],
                 "healer.v_down": np.ascontiguousarray(t["v_dn_t"][sl].transpose(0, 2, 1)),
             })
+        # (the re-tiled FP4 images are derived data and are not exported)
         extras = {n: t[n] for n in ("router_w", "e_bias", "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2") if n in t}
         return groups, extras
 

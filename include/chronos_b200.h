@@ -34,6 +34,8 @@ extern "C" {
 #define CHRONOS_REGIME_AUTO 0   /* pick by pairs per slot */
 #define CHRONOS_REGIME_STREAM 1 /* HBM-bound: packed banks streamed once, up to 8 pairs per pass */
 #define CHRONOS_REGIME_TENSOR 2 /* dense: tcgen05 grouped GEMM, 128 pairs of one expert per tile */
+#define CHRONOS_REGIME_STREAM_FP4 3 /* HBM-bound, banks fed as stored (e2m1 + ue4m3) to tcgen05 block-scaled FP4 MMA;
+                                       needs the re-tiled bank copies (gu_t, dn_t); falls back to STREAM without them */
 
 #define CHRONOS_ROUTER_SOFTMAX_TOPK 0 /* chronos_1t/models/vllm_chronos_moe.py:310-314     */
 #define CHRONOS_ROUTER_SIGMOID_NOAUX 1 /* chronos_1t/models/glm53_chronos_moe.py:392-399    */
@@ -68,6 +70,12 @@ extern "C" {
  * chronos_1t/models/vllm_chronos_moe.py:131-141: sh_gu_* [2*shared_inter, H/2|H/16], sh_dn_* [H, shared_inter/2|/16];
  * sh_gu_s2 f32 [2] = (gate_proj, up_proj) weight_scale_2, sh_dn_s2 f32 [1].
  * shared_inter == 0 disables it.  shared_inter must equal inter when non-zero.
+ *
+ * Optional (NULL when absent; needs H and I multiples of 256): the same bank bytes re-tiled once at load into the
+ * operand images of the block-scaled FP4 tensor-core path - per (slot, 128-row block, 256-column stage) 16384 bytes
+ * of nibbles in K-major core-matrix order followed by four 512-byte scale blocks (see chronos_b200_fp4_mma_probe):
+ *   gu_t u8 [n_slots, 2I/128, H/256, 18432], dn_t u8 [n_slots, H/128, I/256, 18432], sh_gu_t / sh_dn_t without the
+ *   slot axis.  A pure permutation of the "s_gu.weight" + "s_gu.weight_scale" bytes; the file format is untouched.
  */
 typedef struct chronos_layer {
     int32_t hidden, inter, n_experts, group_size, n_slots, rank, top_k;
@@ -85,6 +93,7 @@ typedef struct chronos_layer {
     const uint16_t* dn_cin; const uint32_t* dn_cs2; const uint16_t* dn_rout; const uint32_t* dn_rs2;
     const uint8_t* sh_gu_w; const uint8_t* sh_gu_s; const float* sh_gu_s2;
     const uint8_t* sh_dn_w; const uint8_t* sh_dn_s; const float* sh_dn_s2;
+    const uint8_t* gu_t; const uint8_t* dn_t; const uint8_t* sh_gu_t; const uint8_t* sh_dn_t;
 } chronos_layer_t;
 
 /* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated
@@ -129,7 +138,9 @@ size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens);
 
 /* Whole layer, streaming regime (HBM-bound; any n_tokens, meant for decode-shaped batches):
  * y[n_tokens, H] = sum_k gate_k * Expert_{id_k}(x) (+ shared expert), router included.  Each distinct slot's
- * bank is read from HBM once per call for up to 8 (token, expert) pairs that hit it.
+ * bank is read from HBM once per call for up to 8 (token, expert) pairs that hit it.  Uses the block-scaled FP4
+ * tensor-core pass (CHRONOS_REGIME_STREAM_FP4) when the layer carries re-tiled banks and the workspace was laid
+ * out for it (n_tokens * top_k < 16 * n_slots), otherwise the CUDA-core conversion pass (CHRONOS_REGIME_STREAM).
  * Replaces: ChronosGlm53SparseMoeBlock.forward_impl, chronos_1t/models/glm53_chronos_moe.py:474-483, with the
  *           experts evaluated as ChronosGlm5HolographicExpertGroup.forward_cold_fast does
  *           (chronos_1t/models/glm5_chronos_moe.py:149-195). */

@@ -192,6 +192,27 @@ def test_decode_shaped_layer(streams):
     assert _rel_l2(y1.float().cpu().numpy(), ref) <= LAYER_TOL
 
 
+def test_fp4_streaming_regime_matches_oracle_and_cuda_core_regime():
+    """The same decode-shaped batch through the block-scaled FP4 tensor-core pass and the CUDA-core conversion pass."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=1024, inter=512, n_experts=32, group_size=4, rank=32, top_k=4)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True), register=False)
+    assert layer.packed.struct.gu_t and layer.packed.struct.dn_t
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    for scale in (1.0, 37.0, 0.004):  # the per-pair power-of-two scale must absorb the activation magnitude
+        x = (torch.randn(7, cfg.hidden, generator=gen, device="cuda") * scale).to(torch.bfloat16)
+        y4 = layer.forward_impl(x, regime="stream_fp4")
+        assert layer.device_status() == 0
+        ys = layer.forward_impl(x, regime="stream")
+        assert layer.device_status() == 0
+        ref, _, _ = _oracle_layer(layer, x.float().cpu().numpy())
+        assert _rel_l2(y4.float().cpu().numpy(), ref) <= LAYER_TOL, scale
+        assert _rel_l2(ys.float().cpu().numpy(), ref) <= LAYER_TOL, scale
+        assert torch.equal(y4, layer.forward_impl(x, regime="stream_fp4")), "FP4 pass must be reproducible"
+        assert torch.equal(layer.forward_impl(x, regime="auto"), y4)  # 28 pairs on 8 slots: auto = FP4 streaming
+
+
 def test_many_tokens_on_one_slot_and_skipped_entries():
     """More than 8 pairs on a slot (several work items per slot), entries with id -1, routing supplied by the caller."""
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
