@@ -35,8 +35,8 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
         set_error("n_experts (%d) must equal n_slots (%d) * group_size (%d) and be <= 1024", L->n_experts, L->n_slots, L->group_size);
         return CHRONOS_E_SHAPE;
     }
-    if (L->rank <= 0 || L->rank % 16 || L->rank > kMaxRank) {
-        set_error("healer rank (%d) must be a multiple of 16 in [16, %d]", L->rank, kMaxRank);
+    if (L->rank != 16 && L->rank != 32 && L->rank != 64 && L->rank != 128) {
+        set_error("healer rank (%d) must be 16, 32, 64 or 128", L->rank);
         return CHRONOS_E_SHAPE;
     }
     if (L->top_k <= 0 || L->top_k > kMaxTopK || L->top_k > L->n_experts) {
@@ -126,7 +126,7 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     // token scales come from the router kernel when this call ran it; otherwise from a kernel of their own
     if (!have_tok_scale)
         if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, p.tok_scale, st)) return rc;
-    if (int rc = launch_plan(L, ids, n_tokens, with_shared, x, x_dtype, 0, p, st)) return rc;
+    if (int rc = launch_plan(L, ids, n_tokens, with_shared, x, x_dtype, have_tok_scale ? 0 : 1, p, st)) return rc;
     stage_mark(2, st);
     if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, st)) return rc;
     stage_mark(3, st);
@@ -178,7 +178,7 @@ int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_
     if (int rc = validate_router(layer)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
     if (!ids || !gates || !logits) { set_error("router: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
-    return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, nullptr, (cudaStream_t)stream);
+    return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, nullptr, nullptr, (cudaStream_t)stream);
 }
 
 size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens) {
@@ -205,7 +205,9 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
     const Plan p = plan_bind(lay, workspace);
     cudaStream_t st = (cudaStream_t)stream;
     stage_mark(0, st);
-    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, p.tok_scale, st)) return rc;
+    // the router may raise the status word, so it is cleared here (a memset node, no allocation) and not by the plan kernel
+    if (cudaMemsetAsync(p.counters, 0, 64, st) != cudaSuccess) return check_launch("clear counters");
+    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, p.tok_scale, p.counters + 2, st)) return rc;
     return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, true, st);
 }
 

@@ -62,6 +62,30 @@ __device__ __forceinline__ void tmem_ld32_f4(uint32_t taddr, uint32_t (&r)[32]) 
         : "memory");
 }
 
+// Lean forms for the issuing thread (its instruction stream is the critical path of the streaming kernel): the
+// descriptors' high words are constants, the low words are a base plus a 16-byte-unit offset.
+__device__ __forceinline__ void tc_cp_sf_lo(uint32_t tmem_dst, uint32_t desc_lo) {
+    asm volatile("{\n.reg .b64 d;\nmov.b64 d, {%1, %2};\ntcgen05.cp.cta_group::1.32x128b.warpx4 [%0], d;\n}" ::"r"(tmem_dst),
+                 "r"(desc_lo), "r"(0x00004008u)
+                 : "memory");
+}
+template <bool ACC>
+__device__ __forceinline__ void tc_mma_nvf4_lo(uint32_t tmem_d, uint32_t da_lo, uint32_t da_hi, uint32_t db_lo, uint32_t db_hi,
+                                               uint32_t idesc, uint32_t sfa, uint32_t sfb) {
+    if (ACC)
+        asm volatile(
+            "{\n.reg .b64 a, b;\n.reg .pred p;\nmov.b64 a, {%1, %2};\nmov.b64 b, {%3, %4};\nsetp.eq.u32 p, 0, 0;\n"
+            "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], a, b, %5, [%6], [%7], p;\n}" ::"r"(tmem_d),
+            "r"(da_lo), "r"(da_hi), "r"(db_lo), "r"(db_hi), "r"(idesc), "r"(sfa), "r"(sfb)
+            : "memory");
+    else
+        asm volatile(
+            "{\n.reg .b64 a, b;\n.reg .pred p;\nmov.b64 a, {%1, %2};\nmov.b64 b, {%3, %4};\nsetp.ne.u32 p, 0, 0;\n"
+            "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], a, b, %5, [%6], [%7], p;\n}" ::"r"(tmem_d),
+            "r"(da_lo), "r"(da_hi), "r"(db_lo), "r"(db_hi), "r"(idesc), "r"(sfa), "r"(sfb)
+            : "memory");
+}
+
 // instruction descriptor, block-scaled: A = B = e2m1 (code 1), K-major, scale format ue4m3 (0), N at [17,23), M at [24,29)
 __device__ __forceinline__ uint32_t idesc_nvf4(int m, int n) {
     return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
@@ -203,7 +227,7 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
-    const uint32_t tmem_sf0 = tmem + 64;  // per bank stage: 16 columns SFA then 16 columns SFB
+    const uint32_t tmem_sf0 = tmem + 64;  // bank scales: 16 columns per ring stage; activation scales follow
 
     if (warp == 0) {
         // ---------------- producer ----------------
@@ -211,6 +235,7 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
             uint32_t it = 0, n_items_seen = 0;
             int cur_item = -1;
             bool live = true;
+            const uint64_t pol = l2_policy_evict_first();
             for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
                 const int item = (int)(tile / RB), rb = (int)(tile % RB);
                 if (item != cur_item) {  // new work item: its activation image replaces the previous one
@@ -231,7 +256,7 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
                         break;
                     }
                     mbar_expect_tx(smem_u32(&full[s]), kF4AStage);
-                    bulk_g2s(smem_u32(stages + (size_t)s * kF4AStage), asrc + (size_t)st * kF4AStage, kF4AStage, smem_u32(&full[s]));
+                    bulk_g2s_stream(smem_u32(stages + (size_t)s * kF4AStage), asrc + (size_t)st * kF4AStage, kF4AStage, smem_u32(&full[s]), pol);
                 }
             }
             // drain: copies handed to the copy engine must land before the CTA may exit
@@ -243,15 +268,32 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
+        // Scale blocks travel to tensor memory with tcgen05.cp. An MMA that has to wait for a copy issued just before
+        // it stalls the whole pipe, so the bank scales of stage i+1 are copied before the MMAs of stage i are issued
+        // (when that stage has already landed), and the activation scales of a work item are copied once per item.
         if (lane == 0) {
             const uint32_t idesc = idesc_nvf4(kF4ARows, kF4BRows);
-            uint32_t it = 0, tcount = 0, n_items_seen = 0;
+            const uint32_t total = (uint32_t)((tile_hi - tile_lo) * NS);
+            const bool sfb_resident = 64 + S * 16 + NS * 16 <= (int)kF4TmemCols;
+            const uint32_t tmem_sfb_item = tmem_sf0 + S * 16;  // NS x 16 columns when resident
+            // descriptor words: smem address >> 4 in the low 14 bits; LBO >> 4 at bit 16; SBO = 128 B, version 1 in the high word
+            const uint32_t hi_word = 0x00004008u;
+            const uint32_t a_lo0 = ((smem_u32(stages) >> 4) & 0x3FFFu) | ((uint32_t)(kF4ARows * 16 >> 4) << 16);
+            const uint32_t b_lo0 = ((smem_u32(bimg) >> 4) & 0x3FFFu) | ((uint32_t)(kF4BRows * 16 >> 4) << 16);
+            const uint32_t sfa_lo0 = (smem_u32(stages + kF4ANib) >> 4) & 0x3FFFu;
+            const uint32_t sfb_lo0 = (smem_u32(bimg + kF4BNib) >> 4) & 0x3FFFu;
+            uint32_t it = 0, tcount = 0, n_items_seen = 0, sfa_done = 0;  // sfa_done: stages whose bank scales are in TMEM
+            uint32_t s = 0, ph = 0;                                        // ring slot and phase of stage `it`
             int cur_item = -1;
             bool live = true;
             for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
                 const int item = (int)(tile / RB);
                 if (item != cur_item) {
                     if (!mbar_wait(smem_u32(b_full), n_items_seen & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    if (sfb_resident)
+                        for (int q = 0; q < NS * 4; ++q)
+                            tc_cp_sf_lo(tmem_sfb_item + 4 * q, sfb_lo0 + (uint32_t)(((q >> 2) * kF4BStage + 512 * (q & 3)) >> 4));
                     cur_item = item;
                     ++n_items_seen;
                 }
@@ -261,24 +303,39 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t tmem_d = tmem + buf * 32;
                 for (int st = 0; st < NS; ++st, ++it) {
-                    const int s = (int)(it % (uint32_t)S);
-                    if (!mbar_wait(smem_u32(&full[s]), (it / (uint32_t)S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint8_t* sa = stages + (size_t)s * kF4AStage;
-                    const uint8_t* sb = bimg + (size_t)st * kF4BStage;
-                    const uint32_t sfa = tmem_sf0 + s * 32, sfb = sfa + 16;
+                    if (sfa_done <= it) {  // not copied ahead: wait for the stage and copy now
+                        if (!mbar_wait(smem_u32(&full[s]), ph)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t lo = sfa_lo0 + s * (kF4AStage >> 4);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        tc_cp_sf(sfa + 4 * j, smem_u32(sa + kF4ANib + 512 * j));
-                        tc_cp_sf(sfb + 4 * j, smem_u32(sb + kF4BNib + 512 * j));
+                        for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + s * 16 + 4 * j, lo + j * 32);
+                        sfa_done = it + 1;
                     }
+                    uint32_t sn = s + 1, phn = ph;
+                    if (sn == (uint32_t)S) { sn = 0; phn ^= 1u; }
+                    if (it + 1 < total && sfa_done == it + 1 && mbar_test(smem_u32(&full[sn]), phn)) {  // look one stage ahead
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t lo = sfa_lo0 + sn * (kF4AStage >> 4);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint64_t da = smem_desc_interleaved(smem_u32(sa + 2 * j * (kF4ARows * 16)), kF4ARows * 16);
-                        const uint64_t db = smem_desc_interleaved(smem_u32(sb + 2 * j * (kF4BRows * 16)), kF4BRows * 16);
-                        tc_mma_nvf4(tmem_d, da, db, idesc, sfa + 4 * j, sfb + 4 * j, (st > 0 || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + sn * 16 + 4 * j, lo + j * 32);
+                        sfa_done = it + 2;
                     }
+                    const uint32_t a_lo = a_lo0 + s * (kF4AStage >> 4), b_lo = b_lo0 + (uint32_t)st * (kF4BStage >> 4);
+                    const uint32_t sfa = tmem_sf0 + s * 16;
+                    uint32_t sfb = tmem_sfb_item + st * 16;
+                    if (!sfb_resident) {
+                        sfb = tmem_sf0 + S * 16 + (s & 1) * 16;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) tc_cp_sf_lo(sfb + 4 * j, sfb_lo0 + (uint32_t)((st * kF4BStage + 512 * j) >> 4));
+                    }
+                    if (st == 0) tc_mma_nvf4_lo<false>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sfa, sfb);
+                    else tc_mma_nvf4_lo<true>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sfa, sfb);
+#pragma unroll
+                    for (int j = 1; j < 4; ++j)
+                        tc_mma_nvf4_lo<true>(tmem_d, a_lo + j * (2 * kF4ARows * 16 >> 4), hi_word, b_lo + j * (2 * kF4BRows * 16 >> 4), hi_word,
+                                             idesc, sfa + 4 * j, sfb + 4 * j);
                     tc_commit_f4(smem_u32(&empty[s]));
+                    s = sn; ph = phn;
                 }
                 if (live) {
                     tc_commit_f4(smem_u32(&acc_full[buf]));

@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
         // to keep HBM busy with 16 + 16 small copies per stage.
         uint32_t it = 0;
         bool live = true;
+        const uint64_t pol = l2_policy_evict_first();
         for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
             const int item = (int)(tile / RB), rb = (int)(tile % RB);
             const int slot = a.item_slot[item];
@@ -115,16 +116,16 @@ __global__ void __launch_bounds__(9 * 32, 1) bank_stream_kernel(const BankArgs a
                 const uint8_t* sr = ssrc + (size_t)rt * kRowsPerStage * (K / 16);
                 if (lane < 16) {
                     if (a.nib_stride == K / 2) {
-                        if (lane == 0) bulk_g2s(dst, wr, (uint32_t)(kRowsPerStage * (K / 2)), full);
+                        if (lane == 0) bulk_g2s_stream(dst, wr, (uint32_t)(kRowsPerStage * (K / 2)), full, pol);
                     } else {
-                        bulk_g2s(dst + lane * a.nib_stride, wr + (size_t)lane * (K / 2), (uint32_t)(K / 2), full);
+                        bulk_g2s_stream(dst + lane * a.nib_stride, wr + (size_t)lane * (K / 2), (uint32_t)(K / 2), full, pol);
                     }
                 } else {
                     const int rr = lane - 16;
                     if (a.sc_stride == K / 16) {
-                        if (rr == 0) bulk_g2s(dst + sc_off, sr, (uint32_t)(kRowsPerStage * (K / 16)), full);
+                        if (rr == 0) bulk_g2s_stream(dst + sc_off, sr, (uint32_t)(kRowsPerStage * (K / 16)), full, pol);
                     } else {
-                        bulk_g2s(dst + sc_off + rr * a.sc_stride, sr + (size_t)rr * (K / 16), (uint32_t)(K / 16), full);
+                        bulk_g2s_stream(dst + sc_off + rr * a.sc_stride, sr + (size_t)rr * (K / 16), (uint32_t)(K / 16), full, pol);
                     }
                 }
             }

@@ -147,9 +147,9 @@ int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2,
 int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, float* scratch, cudaStream_t st);
 int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
-                  float* logits, float* tok_scale, cudaStream_t st);
+                  float* logits, float* tok_scale, int32_t* status, cudaStream_t st);
 int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const void* x, int x_dtype,
-                int want_tok_scale, const Plan& p, cudaStream_t st);
+                int reset_status, const Plan& p, cudaStream_t st);
 int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st);
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st);
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st);
@@ -277,9 +277,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     }
     return false;
 }
+// One non-blocking test of a phase.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Streamed-once data (bank bytes) is tagged evict-first in L2 so that it does not push out the small tensors the other
+// kernels of the layer re-read (router weights, key tables, activations, scratch).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_stream(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar), "l"(pol)
                  : "memory");
 }
 #endif  // __CUDACC__

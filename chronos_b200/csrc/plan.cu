@@ -12,7 +12,7 @@ constexpr int kPlanMaxBins = 1024 + 1;  // experts + the shared-expert bin
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ ids, int n_tokens, int top_k,
                                                             int n_experts, int group_size, int n_slots, int with_shared,
                                                             const void* __restrict__ x, int x_dtype, int hidden,
-                                                            int want_tok_scale, Plan p) {
+                                                            int reset_status, Plan p) {
     __shared__ int cnt[kPlanMaxBins + 1];
     __shared__ int off[kPlanMaxBins + 1];
     __shared__ int cur[kPlanMaxBins + 1];
@@ -20,24 +20,6 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
     const int tid = threadIdx.x;
     const int n_bins = n_experts + 1;
     const int n_entries = n_tokens * top_k;
-    if (want_tok_scale) {
-        // per-token power-of-two scale near rms(x[t]) for the FP4 activation images: one warp per token,
-        // lane-strided sum of squares + xor butterfly (a fixed order: the scale is reproducible)
-        const int lane = tid & 31;
-        for (int t = tid >> 5; t < n_tokens; t += kPlanThreads / 32) {
-            float ss = 0.0f;
-            for (int k = lane; k < hidden; k += 32) {
-                const float v = ld_act(x, x_dtype, (size_t)t * hidden + k);
-                ss = fmaf(v, v, ss);
-            }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-            if (lane == 0) {
-                const float rms = sqrtf(ss / (float)hidden);
-                p.tok_scale[t] = rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
-            }
-        }
-    }
     for (int i = tid; i <= n_bins; i += kPlanThreads) { cnt[i] = 0; cur[i] = 0; }
     __syncthreads();
     for (int i = tid; i < n_entries; i += kPlanThreads) {
@@ -147,14 +129,14 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         p.counters[3] = min(carry, p.max_gitems);
         p.counters[0] = min(n_items_total, p.max_items);
         p.counters[1] = off[n_bins];
-        p.counters[2] = 0;
+        if (reset_status) p.counters[2] = 0;  // otherwise the caller cleared it before the router ran
     }
 }
 
 int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const void* x, int x_dtype,
-                int want_tok_scale, const Plan& p, cudaStream_t st) {
+                int reset_status, const Plan& p, cudaStream_t st) {
     plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, n_tokens, L.top_k, L.n_experts, L.group_size, L.n_slots,
-                                           with_shared && L.shared_inter > 0, x, x_dtype, L.hidden, want_tok_scale, p);
+                                           with_shared && L.shared_inter > 0, x, x_dtype, L.hidden, reset_status, p);
     return check_launch("plan");
 }
 

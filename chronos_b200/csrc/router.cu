@@ -1,17 +1,30 @@
 // Router: fp32 logits in a fixed, reproducible summation order + top-k + gate weights.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace chronos {
 
-// logits[t, e] = sum_k x[t, k] * w[e, k] with lane l accumulating k = l, l+32, ... ascending by FMA from +0,
-// lanes combined by the xor butterfly 16, 8, 4, 2, 1. Any tiling gives the same bits because every (t, e) dot is
-// owned by one warp and walks k in that order. Each warp computes a TOK-token x EXP-expert tile: (4, 1) spreads
-// decode-sized batches over many warps, (4, 4) reuses loaded operands for prefill-sized ones.
-template <int TOK, int EXP>
-__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int x_dtype,
-                                                            const float* __restrict__ w, float* __restrict__ logits,
-                                                            int n_tokens, int n_experts, int hidden,
-                                                            float* __restrict__ tok_scale) {
+// logits[t, e] = sum_k x[t, k] * w[e, k] in ONE stated order, so that the CPU oracle can reproduce every bit:
+// lane l (0..31) accumulates, by fused multiply-add starting from +0, the products at k = 128 j + 4 l + i for
+// j = 0, 1, ... and i = 0..3 (j ascending, then i); the 32 lane sums are combined by the xor butterfly 16, 8, 4, 2, 1.
+// Any tiling gives the same bits because every (t, e) dot is owned by one warp and walks k in that order; the order
+// lets a lane fetch its four consecutive columns with one vector load. Each warp computes a TOK-token x EXP-expert
+// tile: (4, 1) spreads decode-sized batches over many warps, (4, 4) reuses loaded operands for prefill-sized ones.
+template <bool BF16>
+__device__ __forceinline__ float4 ld_x4(const void* x, size_t i) {
+    if (BF16) {
+        const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(x) + i);
+        return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                           __uint_as_float(v.y & 0xffff0000u));
+    }
+    return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i);
+}
+
+template <int TOK, int EXP, bool BF16>
+__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                            float* __restrict__ logits, int n_tokens, int n_experts,
+                                                            int hidden, float* __restrict__ tok_scale) {
     const int lane = threadIdx.x & 31;
     const int warp_in_block = threadIdx.x >> 5;
     const int e_tiles = (n_experts + EXP - 1) / EXP;
@@ -22,48 +35,59 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
     const int tt = (int)(tile / e_tiles), et = (int)(tile % e_tiles);
     const int t0 = tt * TOK, e0 = et * EXP;
     float acc[TOK][EXP];
+    float ssq[TOK];
 #pragma unroll
-    for (int a = 0; a < TOK; ++a)
+    for (int a = 0; a < TOK; ++a) {
+        ssq[a] = 0.0f;
 #pragma unroll
         for (int b = 0; b < EXP; ++b) acc[a][b] = 0.0f;
+    }
     size_t xoff[TOK], woff[EXP];
 #pragma unroll
-    for (int a = 0; a < TOK; ++a) xoff[a] = (size_t)min(t0 + a, n_tokens - 1) * hidden;
+    for (int a = 0; a < TOK; ++a) xoff[a] = (size_t)min(t0 + a, n_tokens - 1) * hidden + 4 * lane;
 #pragma unroll
-    for (int b = 0; b < EXP; ++b) woff[b] = (size_t)min(e0 + b, n_experts - 1) * hidden;
+    for (int b = 0; b < EXP; ++b) woff[b] = (size_t)min(e0 + b, n_experts - 1) * hidden + 4 * lane;
     // the warp that owns expert tile 0 of a token tile also produces the tokens' power-of-two activation scales
     // (near rms(x[t])): it reads every x element anyway
     const bool do_scale = tok_scale != nullptr && et == 0;
-    float ssq[TOK];
-#pragma unroll
-    for (int a = 0; a < TOK; ++a) ssq[a] = 0.0f;
-    constexpr int UN = 8;  // k-steps whose loads are issued together (the FMA order per dot is unchanged)
-    int k = lane;
-    for (; k + (UN - 1) * 32 < hidden; k += UN * 32) {
-        float xv[UN][TOK], wv[UN][EXP];
+    constexpr int UN = EXP == 1 ? 8 : 4;  // 128-column steps whose loads are issued together (the FMA order per dot is unchanged)
+    int k = 0;
+    for (; k + UN * 128 <= hidden; k += UN * 128) {
+        float4 xv[UN][TOK], wv[UN][EXP];
 #pragma unroll
         for (int u = 0; u < UN; ++u) {
 #pragma unroll
-            for (int a = 0; a < TOK; ++a) xv[u][a] = ld_act(x, x_dtype, xoff[a] + k + u * 32);
+            for (int a = 0; a < TOK; ++a) xv[u][a] = ld_x4<BF16>(x, xoff[a] + k + u * 128);
 #pragma unroll
-            for (int b = 0; b < EXP; ++b) wv[u][b] = w[woff[b] + k + u * 32];
+            for (int b = 0; b < EXP; ++b) wv[u][b] = *reinterpret_cast<const float4*>(w + woff[b] + k + u * 128);
         }
 #pragma unroll
         for (int u = 0; u < UN; ++u)
 #pragma unroll
             for (int a = 0; a < TOK; ++a) {
 #pragma unroll
-                for (int b = 0; b < EXP; ++b) acc[a][b] = __fmaf_rn(xv[u][a], wv[u][b], acc[a][b]);
-                ssq[a] = fmaf(xv[u][a], xv[u][a], ssq[a]);
+                for (int b = 0; b < EXP; ++b) {
+                    acc[a][b] = __fmaf_rn(xv[u][a].x, wv[u][b].x, acc[a][b]);
+                    acc[a][b] = __fmaf_rn(xv[u][a].y, wv[u][b].y, acc[a][b]);
+                    acc[a][b] = __fmaf_rn(xv[u][a].z, wv[u][b].z, acc[a][b]);
+                    acc[a][b] = __fmaf_rn(xv[u][a].w, wv[u][b].w, acc[a][b]);
+                }
+                ssq[a] = fmaf(xv[u][a].x, xv[u][a].x, fmaf(xv[u][a].y, xv[u][a].y, fmaf(xv[u][a].z, xv[u][a].z, fmaf(xv[u][a].w, xv[u][a].w, ssq[a]))));
             }
     }
-    for (; k < hidden; k += 32) {
+    for (; k < hidden; k += 128) {
 #pragma unroll
         for (int a = 0; a < TOK; ++a) {
-            const float xv1 = ld_act(x, x_dtype, xoff[a] + k);
+            const float4 xq = ld_x4<BF16>(x, xoff[a] + k);
 #pragma unroll
-            for (int b = 0; b < EXP; ++b) acc[a][b] = __fmaf_rn(xv1, w[woff[b] + k], acc[a][b]);
-            ssq[a] = fmaf(xv1, xv1, ssq[a]);
+            for (int b = 0; b < EXP; ++b) {
+                const float4 wq = *reinterpret_cast<const float4*>(w + woff[b] + k);
+                acc[a][b] = __fmaf_rn(xq.x, wq.x, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.y, wq.y, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.z, wq.z, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.w, wq.w, acc[a][b]);
+            }
+            ssq[a] = fmaf(xq.x, xq.x, fmaf(xq.y, xq.y, fmaf(xq.z, xq.z, fmaf(xq.w, xq.w, ssq[a]))));
         }
     }
     if (do_scale) {
@@ -87,6 +111,84 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
             for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
             if (lane == 0 && t0 + a < n_tokens && e0 + b < n_experts) logits[(size_t)(t0 + a) * n_experts + e0 + b] = v;
         }
+}
+
+// Decode-sized batches: the dots are few and every one is a long dependent walk over k, so the time is pure memory
+// latency. One CTA stages EPC router rows and up to 4 activation rows in shared memory with bulk async copies
+// (all bytes requested at once, one wait), then warp w computes expert e0 + w against the 4 tokens in the stated
+// order (lane l: k = 128 j + 4 l + i). Bits are identical to router_logits_kernel.
+template <bool BF16>
+__global__ void __launch_bounds__(256) router_logits_small_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                                  float* __restrict__ logits, int n_tokens, int n_experts,
+                                                                  int hidden, int epc, float* __restrict__ tok_scale,
+                                                                  int32_t* __restrict__ status) {
+    extern __shared__ __align__(128) uint8_t rsm[];
+    __shared__ uint64_t bar;
+    constexpr int XB = BF16 ? 2 : 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e_tiles = (n_experts + epc - 1) / epc;
+    const int tt = blockIdx.x / e_tiles, et = blockIdx.x % e_tiles;
+    const int t0 = tt * 4, e0 = et * epc;
+    const int nt = min(4, n_tokens - t0), ne = min(epc, n_experts - e0);
+    float* ws = reinterpret_cast<float*>(rsm);                       // [epc][hidden]
+    uint8_t* xs = rsm + (size_t)epc * hidden * 4;                    // [4][hidden] in the activation dtype
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(smem_u32(&bar), (uint32_t)(ne * hidden * 4 + nt * hidden * XB));
+        for (int i = 0; i < ne; ++i)
+            bulk_g2s(smem_u32(ws + (size_t)i * hidden), w + (size_t)(e0 + i) * hidden, (uint32_t)hidden * 4, smem_u32(&bar));
+        for (int a = 0; a < nt; ++a)
+            bulk_g2s(smem_u32(xs + (size_t)a * hidden * XB), reinterpret_cast<const uint8_t*>(x) + (size_t)(t0 + a) * hidden * XB,
+                     (uint32_t)hidden * XB, smem_u32(&bar));
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(smem_u32(&bar), 0);
+    if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) atomicOr(status, 0x100);
+        return;
+    }
+    for (int ew = warp; ew < ne; ew += 8) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, ssq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float* wr = ws + (size_t)ew * hidden + 4 * lane;
+        for (int k = 0; k < hidden; k += 128) {
+            const float4 wq = *reinterpret_cast<const float4*>(wr + k);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                if (a < nt) {
+                    float4 xq;
+                    if (BF16) {
+                        const uint2 v = *reinterpret_cast<const uint2*>(xs + ((size_t)a * hidden + k + 4 * lane) * 2);
+                        xq = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                                         __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+                    } else {
+                        xq = *reinterpret_cast<const float4*>(xs + ((size_t)a * hidden + k + 4 * lane) * 4);
+                    }
+                    acc[a] = __fmaf_rn(xq.x, wq.x, acc[a]);
+                    acc[a] = __fmaf_rn(xq.y, wq.y, acc[a]);
+                    acc[a] = __fmaf_rn(xq.z, wq.z, acc[a]);
+                    acc[a] = __fmaf_rn(xq.w, wq.w, acc[a]);
+                    ssq[a] = fmaf(xq.x, xq.x, fmaf(xq.y, xq.y, fmaf(xq.z, xq.z, fmaf(xq.w, xq.w, ssq[a]))));
+                }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            float v = acc[a];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0 && a < nt) logits[(size_t)(t0 + a) * n_experts + e0 + ew] = v;
+            if (tok_scale != nullptr && et == 0 && ew == 0) {
+                float q = ssq[a];
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+                if (lane == 0 && a < nt) {
+                    const float rms = sqrtf(q / (float)hidden);
+                    tok_scale[t0 + a] = rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
+                }
+            }
+        }
+    }
 }
 
 // One warp per token: k rounds of arg-max over the choice scores (ties -> lower index), then the gate weights.
@@ -160,16 +262,29 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 }
 
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
-                  float* logits, float* tok_scale, cudaStream_t st) {
+                  float* logits, float* tok_scale, int32_t* status, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
-    if (n_tokens <= 64) {
+    const bool bf16 = x_dtype == CHRONOS_DTYPE_BF16;
+    const size_t xrow = (size_t)L.hidden * (bf16 ? 2 : 4), wrow = (size_t)L.hidden * 4;
+    const int epc = (int)std::min<size_t>(8, (200 * 1024 - 4 * xrow) / wrow);
+    if (n_tokens <= 64 && epc >= 1 && status != nullptr) {
+        const size_t smem = (size_t)epc * wrow + 4 * xrow;
+        const unsigned grid = (unsigned)(((L.n_experts + epc - 1) / epc) * ((n_tokens + 3) / 4));
+        cudaError_t rc = bf16 ? cudaFuncSetAttribute(router_logits_small_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                              : cudaFuncSetAttribute(router_logits_small_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (rc != cudaSuccess) { set_error("router: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc)); return CHRONOS_E_LAUNCH; }
+        if (bf16) router_logits_small_kernel<true><<<grid, 256, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, epc, tok_scale, status);
+        else router_logits_small_kernel<false><<<grid, 256, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, epc, tok_scale, status);
+    } else if (n_tokens <= 64) {
         const long tiles = (long)L.n_experts * ((n_tokens + 3) / 4);
-        router_logits_kernel<4, 1><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
-                                                                               L.n_experts, L.hidden, tok_scale);
+        const unsigned grid = (unsigned)((tiles + 7) / 8);
+        if (bf16) router_logits_kernel<4, 1, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+        else router_logits_kernel<4, 1, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     } else {
         const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
-        router_logits_kernel<4, 4><<<(unsigned)((tiles + 7) / 8), 256, 0, st>>>(x, x_dtype, L.router_w, logits, n_tokens,
-                                                                               L.n_experts, L.hidden, tok_scale);
+        const unsigned grid = (unsigned)((tiles + 7) / 8);
+        if (bf16) router_logits_kernel<4, 4, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+        else router_logits_kernel<4, 4, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     }
     if (int rc = check_launch("router_logits")) return rc;
     router_topk_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(logits, L.e_bias, L.router_kind, L.renorm,

@@ -162,44 +162,47 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
         quantize_block_fp4x3(v, lane, img, blk & 1, pos);
         return;
     }
-    // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, 8 rank rows).
-    // Lane l owns 16 consecutive columns per 512-column step: one 16-byte load per rank row.
+    // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, rank row): the row's
+    // 16-byte pieces (lane l owns columns 16 l .. 16 l + 15 of every 512-column step) are all requested before use.
     const long hw = gw - xf_warps;
-    const int rgroups = r / 8;
-    const int pair = (int)(hw / rgroups), rg = (int)(hw % rgroups);
+    const int pair = (int)(hw / r), c = (int)(hw % r);
     if (pair >= n_pairs) return;
     const int t = p.pair_token[pair], e = p.pair_expert[pair];
     if (e >= E) return;
-    float acc[8];
+    const uint8_t* vrow = L.v_gu + ((size_t)e * r + c) * H;
+    float acc = 0.0f;
+    for (int k0 = 0; k0 < H; k0 += 4 * 512) {
+        uint4 vw[4];
+        float xv[4][16];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
-    const uint8_t* vbase = L.v_gu + ((size_t)e * r + rg * 8) * H;
-    for (int k = lane * 16; k < H; k += 512) {
-        uint4 vw[8];
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u * 512 + lane * 16;
+            if (k < H) vw[u] = *reinterpret_cast<const uint4*>(vrow + k);
+        }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) vw[c] = *reinterpret_cast<const uint4*>(vbase + (size_t)c * H + k);
-        float xv[16];
-        ld_act16(x, x_dtype, (size_t)t * H + k, xv);
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u * 512 + lane * 16;
+            if (k < H) ld_act16(x, x_dtype, (size_t)t * H + k, xv[u]);
+        }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint32_t ww[4] = {vw[c].x, vw[c].y, vw[c].z, vw[c].w};
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u * 512 + lane * 16;
+            if (k < H) {
+                const uint32_t ww[4] = {vw[u].x, vw[u].y, vw[u].z, vw[u].w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
-                acc[c] = fmaf(lo.x, xv[q * 4 + 0], acc[c]);
-                acc[c] = fmaf(lo.y, xv[q * 4 + 1], acc[c]);
-                acc[c] = fmaf(hi.x, xv[q * 4 + 2], acc[c]);
-                acc[c] = fmaf(hi.y, xv[q * 4 + 3], acc[c]);
+                for (int q = 0; q < 4; ++q) {
+                    const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
+                    acc = fmaf(lo.x, xv[u][q * 4 + 0], acc);
+                    acc = fmaf(lo.y, xv[u][q * 4 + 1], acc);
+                    acc = fmaf(hi.x, xv[u][q * 4 + 2], acc);
+                    acc = fmaf(hi.y, xv[u][q * 4 + 3], acc);
+                }
             }
         }
     }
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        float s = acc[c];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) p.hmid[(size_t)pair * r + rg * 8 + c] = s;
-    }
+    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) p.hmid[(size_t)pair * r + c] = acc;
 }
 
 // Per-token power-of-two scale near rms(x[t]); one warp per token, fixed summation order.
@@ -226,7 +229,7 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
 
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st) {
     const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
-    const long warps = xf + (long)p.max_pairs * (L.rank / 8);
+    const long warps = xf + (long)p.max_pairs * L.rank;
     pre_gu_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, x, x_dtype, p, fp4);
     return check_launch("pre_gu");
 }
@@ -236,13 +239,15 @@ int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Pl
 // act[i] = silu(z_gu[i]) * z_gu[I + i] with z_gu[row] = beta * r_s1[row] * z1[r_inv[row]] + U_gu[row, :] . hmid;
 // also the pair's partial sum of squares of the block and the partial down-healer input V_down . act of the block.
 // ---------------------------------------------------------------------------------------------------------------
+template <int R16>  // healer rank / 16: compile-time so that every 16-byte healer load of a row can be issued up front
 __global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p) {
     __shared__ float hs[8][kMaxRank];
     __shared__ float act_s[8][128];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const long gw = (long)blockIdx.x * 8 + wib;
     const int n_pairs = p.counters[1];
-    const int I = L.inter, E = L.n_experts, r = L.rank;
+    const int I = L.inter, E = L.n_experts;
+    constexpr int r = R16 * 16;
     const int nblk = I / 128;
     const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
     if (pair >= n_pairs) return;
@@ -273,11 +278,15 @@ __global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p)
                 zb[q] = (ro[q] >> 15) ? -z : z;
             }
             const uint4* urow = reinterpret_cast<const uint4*>(ug + (size_t)(half * I + i0) * r);
+            uint4 uall[4 * R16];  // rows i0..i0+3 are contiguous: 4 * r bytes
+#pragma unroll
+            for (int w = 0; w < 4 * R16; ++w) uall[w] = urow[w];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 float heal = 0.0f;
-                for (int c16 = 0; c16 < r / 16; ++c16) {
-                    const uint4 u = urow[q * (r / 16) + c16];
+#pragma unroll
+                for (int c16 = 0; c16 < R16; ++c16) {
+                    const uint4 u = uall[q * R16 + c16];
                     const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
                     for (int w4 = 0; w4 < 4; ++w4) {
@@ -307,12 +316,12 @@ __global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p)
     *reinterpret_cast<float4*>(&act_s[wib][lane * 4]) = make_float4(a[0], a[1], a[2], a[3]);
     __syncwarp();
     const uint8_t* vt = L.v_dn_t + ((size_t)e * I + blk * 128) * r;
-    const int cpr = r / 16, rpi = 32 / cpr;
+    constexpr int cpr = R16, rpi = 32 / cpr;
     const int rsel = lane / cpr, chunk = lane % cpr;
     float hacc[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) hacc[c] = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
     for (int j0 = 0; j0 < 128; j0 += rpi) {
         const int jj = j0 + rsel;
         const uint4 w = *reinterpret_cast<const uint4*>(vt + (size_t)jj * r + chunk * 16);
@@ -380,7 +389,13 @@ __global__ void __launch_bounds__(256) mid_xform_kernel(chronos_layer_t L, Plan 
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st) {
     const int nblk = L.inter / 128;
     long warps = (long)p.max_pairs * nblk;
-    mid_act_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, p);
+    const unsigned grid_a = (unsigned)((warps + 7) / 8);
+    switch (L.rank / 16) {
+        case 1: mid_act_kernel<1><<<grid_a, 256, 0, st>>>(L, p); break;
+        case 2: mid_act_kernel<2><<<grid_a, 256, 0, st>>>(L, p); break;
+        case 4: mid_act_kernel<4><<<grid_a, 256, 0, st>>>(L, p); break;
+        default: mid_act_kernel<8><<<grid_a, 256, 0, st>>>(L, p); break;
+    }
     if (int rc = check_launch("mid_act")) return rc;
     if (fp4) warps = (long)p.max_items * kPairsPerItem * nblk;
     mid_xform_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, p, fp4);
@@ -393,26 +408,34 @@ int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st
 // One block per (token, 128 output rows): warp w evaluates routing entries j = w, w+8, ...; lane l owns rows 4l..4l+3;
 // the per-entry terms meet in shared memory and are added in index order (deterministic).
 // ---------------------------------------------------------------------------------------------------------------
+template <int R16>
 __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p, const float* __restrict__ gates,
                                                       int with_shared, void* __restrict__ y, int y_dtype) {
     __shared__ float hd[8][kMaxRank];
     __shared__ __align__(16) float terms[kMaxTopK][128];
     const int t = blockIdx.x, rb = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int H = L.hidden, I = L.inter, E = L.n_experts, r = L.rank, k = L.top_k;
+    const int H = L.hidden, I = L.inter, E = L.n_experts, k = L.top_k;
+    constexpr int r = R16 * 16;
     const int nblk = I / 128;
     const int row0 = rb * 128 + lane * 4;
     for (int j = warp; j < k; j += 8) {
         const int pos = p.pos_of[t * k + j];
         float out[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (pos >= 0) {
+            const int e = p.pair_expert[pos];
+            // the healer rows of this lane's 4 outputs do not depend on anything computed here: request them first
+            const uint4* urow = reinterpret_cast<const uint4*>(L.u_dn + ((size_t)e * H + row0) * r);
+            uint4 uall[4 * R16];
+#pragma unroll
+            for (int w = 0; w < 4 * R16; ++w) uall[w] = urow[w];
             for (int c = lane; c < r; c += 32) {
                 float s = 0.0f;
+#pragma unroll 4
                 for (int b = 0; b < nblk; ++b) s += p.hpart[((size_t)pos * nblk + b) * r + c];
                 hd[warp][c] = s;
             }
             __syncwarp();
-            const int e = p.pair_expert[pos];
             const float g = gates[t * k + j], beta = L.dn_beta[e];
             const uint2 ro2 = *reinterpret_cast<const uint2*>(L.dn_rout + (size_t)e * H + row0);
             const uint32_t ro[4] = {ro2.x & 0xffffu, ro2.x >> 16, ro2.y & 0xffffu, ro2.y >> 16};
@@ -422,12 +445,12 @@ __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p,
                 const float v = p.y1[(size_t)pos * H + (ro[q] & 0x7fffu)];
                 yb[q] = (ro[q] >> 15) ? -v : v;
             }
-            const uint4* urow = reinterpret_cast<const uint4*>(L.u_dn + ((size_t)e * H + row0) * r);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 float heal = 0.0f;
-                for (int c16 = 0; c16 < r / 16; ++c16) {
-                    const uint4 u = urow[q * (r / 16) + c16];
+#pragma unroll
+                for (int c16 = 0; c16 < R16; ++c16) {
+                    const uint4 u = uall[q * R16 + c16];
                     const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
                     for (int w4 = 0; w4 < 4; ++w4) {
@@ -463,7 +486,13 @@ int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, 
                    int y_dtype, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
     dim3 grid((unsigned)n_tokens, (unsigned)(L.hidden / 128));
-    combine_kernel<<<grid, 256, 0, st>>>(L, p, gates, with_shared && L.shared_inter > 0, y, y_dtype);
+    const int ws = with_shared && L.shared_inter > 0;
+    switch (L.rank / 16) {
+        case 1: combine_kernel<1><<<grid, 256, 0, st>>>(L, p, gates, ws, y, y_dtype); break;
+        case 2: combine_kernel<2><<<grid, 256, 0, st>>>(L, p, gates, ws, y, y_dtype); break;
+        case 4: combine_kernel<4><<<grid, 256, 0, st>>>(L, p, gates, ws, y, y_dtype); break;
+        default: combine_kernel<8><<<grid, 256, 0, st>>>(L, p, gates, ws, y, y_dtype); break;
+    }
     return check_launch("combine");
 }
 

@@ -44,7 +44,7 @@ extern "C" {
  *
  * Dimensions: hidden H and inter I are multiples of 128 and at most 32768; n_experts = n_slots * group_size;
  * expert e lives in slot e / group_size as member e % group_size (chronos_1t/models/glm5_chronos_moe.py:439-440).
- * rank r is a multiple of 16, at most 128.  top_k <= 32.
+ * rank r is 16, 32, 64 or 128.  top_k <= 32.
  *
  * Banks and healers hold the on-disk bytes of the converter unchanged (suffix names from
  * chronos_1t/models/glm53_holo.py:45-51), stacked over slots / experts:
@@ -123,8 +123,9 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
  * This entry point has no counterpart in the reference. */
 int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int expert, int which, float* out, void* stream);
 
-/* Router: fp32 logits in the fixed summation order (lane l of 32 sums k = l, l+32, ... with FMAs, then the xor
- * butterfly 16,8,4,2,1), top-k descending with ties to the lower index, gate weights per router_kind.
+/* Router: fp32 logits in the fixed summation order (lane l of 32 sums k = 128 j + 4 l + i, j ascending then i = 0..3,
+ * with FMAs from +0, then the xor butterfly 16,8,4,2,1), top-k descending with ties to the lower index, gate weights
+ * per router_kind.
  * ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k], logits f32 [n_tokens, n_experts] (scratch, also returned).
  * Reads only hidden, n_experts, top_k, router_kind, renorm, routed_scaling, router_w and e_bias of `layer`, so an
  * expert-parallel shard can pass a description whose n_experts is the width of the full router table.

@@ -277,8 +277,9 @@ def _clib():
 
 def router_logits_fixed(x: np.ndarray, wr: np.ndarray) -> np.ndarray:
     """fp32 logits = x . Wr^T (chronos_1t/models/vllm_chronos_moe.py:311) in ONE stated summation order, so a
-    device kernel can reproduce them bit for bit: lane l of 32 accumulates k = l, l+32, ... ascending with fused
-    multiply-adds starting from +0, then lanes are combined by the xor butterfly 16, 8, 4, 2, 1."""
+    device kernel can reproduce them bit for bit: lane l of 32 accumulates the products at k = 128 j + 4 l + i
+    (j = 0, 1, ...; i = 0..3; j ascending, then i) with fused multiply-adds starting from +0, then lanes are combined by
+    the xor butterfly 16, 8, 4, 2, 1."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     wr = np.ascontiguousarray(wr, dtype=np.float32)
     t, h = x.shape

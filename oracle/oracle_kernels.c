@@ -5,8 +5,9 @@
  * chronos_1t/models/glm53_chronos_moe.py:393); the value of an fp32 dot product depends on the order of its
  * additions, so this file states ONE order and the CUDA router follows the same one.
  *
- * Order: 32 lanes; lane l accumulates k = l, l+32, l+64, ... ascending with fused multiply-adds starting from
- * +0.0f; then lanes are combined with the xor butterfly (offsets 16, 8, 4, 2, 1): p[l] = p[l] + p[l ^ off].
+ * Order: 32 lanes; lane l accumulates the products at k = 128*j + 4*l + i for j = 0, 1, ... and i = 0..3
+ * (j ascending, then i) with fused multiply-adds starting from +0.0f (columns >= h contribute nothing); then
+ * lanes are combined with the xor butterfly (offsets 16, 8, 4, 2, 1): p[l] = p[l] + p[l ^ off].
  * fp32 addition is commutative, so every lane ends with the same value; lane 0 is returned.
  */
 #include <math.h>
@@ -21,7 +22,11 @@ static float dot_fixed(const float* x, const float* w, int h) {
     float p[32];
     for (int l = 0; l < 32; ++l) {
         float acc = 0.0f;
-        for (int k = l; k < h; k += 32) acc = fmaf(x[k], w[k], acc);
+        for (int j = 0; j < h; j += 128)
+            for (int i = 0; i < 4; ++i) {
+                const int k = j + 4 * l + i;
+                if (k < h) acc = fmaf(x[k], w[k], acc);
+            }
         p[l] = acc;
     }
     for (int off = 16; off >= 1; off >>= 1) {

@@ -111,10 +111,11 @@ def test_router_fixed_order_is_the_stated_order():
         for e in range(3):
             p = np.zeros(32, dtype=np.float32)
             for l in range(32):
-                acc = np.float64(0)  # fma = exact product + single rounding: emulate in fp64 (exact for fp32 inputs)
+                # fma = exact product + single rounding: emulate in fp64 (exact for fp32 inputs)
                 a32 = np.float32(0)
-                for kk in range(l, 96, 32):
-                    a32 = np.float32(np.float64(x[t, kk]) * np.float64(w[e, kk]) + np.float64(a32))
+                for kk in (j + 4 * l + i for j in range(0, 96, 128) for i in range(4)):
+                    if kk < 96:
+                        a32 = np.float32(np.float64(x[t, kk]) * np.float64(w[e, kk]) + np.float64(a32))
                 p[l] = a32
             for off in (16, 8, 4, 2, 1):
                 p = (p + p[np.arange(32) ^ off]).astype(np.float32)
