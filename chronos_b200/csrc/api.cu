@@ -118,7 +118,7 @@ static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, bool 
 
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
                           const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, int regime,
-                          bool have_tok_scale, cudaStream_t st) {
+                          bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
     const int reg = pick_regime(L, n_tokens, regime, p.bq_gu != nullptr);
     const bool tensor = reg == CHRONOS_REGIME_TENSOR;
     const int fp4 = reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0;
@@ -126,9 +126,10 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     // token scales come from the router kernel when this call ran it; otherwise from a kernel of their own
     if (!have_tok_scale)
         if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, p.tok_scale, st)) return rc;
-    if (int rc = launch_plan(L, ids, n_tokens, with_shared, x, x_dtype, have_tok_scale ? 0 : 1, p, st)) return rc;
+    if (int rc = launch_plan(L, ids, n_tokens, with_shared, have_tok_scale ? 0 : 1, tk, p, st)) return rc;
     stage_mark(2, st);
-    if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, st)) return rc;
+    const int many = (tensor && p.yt != nullptr) ? 1 : 0;  // many pairs per expert: healer kernels that share rows through L1
+    if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, many, st)) return rc;
     stage_mark(3, st);
     if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st))) return rc;
     stage_mark(4, st);
@@ -136,7 +137,8 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     stage_mark(5, st);
     if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st))) return rc;
     stage_mark(6, st);
-    const int rc = launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    const int rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)
+                        : launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     stage_mark(7, st);
     return rc;
 }
@@ -207,8 +209,16 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
     stage_mark(0, st);
     // the router may raise the status word, so it is cleared here (a memset node, no allocation) and not by the plan kernel
     if (cudaMemsetAsync(p.counters, 0, 64, st) != cudaSuccess) return check_launch("clear counters");
-    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, p.ids, p.gates, p.logits, p.tok_scale, p.counters + 2, st)) return rc;
-    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, true, st);
+    // decode-sized batches: the top-k runs inside the plan launch (one launch less on the critical path)
+    const bool fuse_topk = n_tokens <= 32;
+    TopkArgs tk{};
+    if (fuse_topk)
+        tk = TopkArgs{p.logits, layer->e_bias, layer->router_kind, layer->renorm, layer->routed_scaling, n_tokens,
+                      layer->n_experts, layer->top_k, p.ids, p.gates};
+    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, fuse_topk ? nullptr : p.ids, p.gates, p.logits, p.tok_scale,
+                               p.counters + 2, st))
+        return rc;
+    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, true, tk, st);
 }
 
 int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
@@ -240,7 +250,7 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
         return CHRONOS_E_WORKSPACE;
     }
     const Plan p = plan_bind(lay, workspace);
-    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, false, (cudaStream_t)stream);
+    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, false, TopkArgs{}, (cudaStream_t)stream);
 }
 
 int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out, int32_t* status,

@@ -174,9 +174,9 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
 // own bounded waits.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kF4MaxStages = 8;
-constexpr int kF4Threads = 192;
+constexpr int kF4Threads = 224;  // producer, MMA issuer A, 4 epilogue warps, MMA issuer B
 constexpr int kStatusFp4Timeout = 0x80;
-constexpr uint32_t kF4TmemCols = 512;  // 2 x 32 accumulator columns + 8 stages x (16 + 16) scale columns = 320 -> 512
+constexpr uint32_t kF4TmemCols = 512;  // 2 buffers x 2 accumulators x 32 columns, then bank scales (16 per ring stage), then activation scales
 
 struct Fp4Args {
     const uint8_t* bank_t;     // [n_slots, RB, NS, 18432]
@@ -211,12 +211,16 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
     uint64_t* acc_empty = bars + 2 * kF4MaxStages + 2;
     uint64_t* b_full = bars + 2 * kF4MaxStages + 4;
     uint64_t* b_empty = bars + 2 * kF4MaxStages + 5;
+    // two issuing threads take alternate stages into separate accumulators (the issuing thread's instruction stream is
+    // the critical path); an odd stage count per tile, or activation scales too large to stay in TMEM, keep one issuer
+    const bool sfb_resident = 128 + S * 16 + NS * 16 <= (int)kF4TmemCols;  // activation scales of a whole item fit in TMEM
+    const uint32_t n_issuers = (NS % 2 == 0 && sfb_resident) ? 2u : 1u;   // even NS: a stage keeps its issuer in every tile
 
     if (tid == 0) {
         for (int s = 0; s < kF4MaxStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&acc_full[b]), 1); mbar_init(smem_u32(&acc_empty[b]), 4); }
+        for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&acc_full[b]), n_issuers); mbar_init(smem_u32(&acc_empty[b]), 4); }
         mbar_init(smem_u32(b_full), 1);
-        mbar_init(smem_u32(b_empty), 1);
+        mbar_init(smem_u32(b_empty), n_issuers);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -227,7 +231,7 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
-    const uint32_t tmem_sf0 = tmem + 64;  // bank scales: 16 columns per ring stage; activation scales follow
+    const uint32_t tmem_sf0 = tmem + 128;  // bank scales: 16 columns per ring stage; activation scales follow
 
     if (warp == 0) {
         // ---------------- producer ----------------
@@ -266,15 +270,16 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
             }
             if (n_items_seen > 0 && !mbar_wait(smem_u32(b_full), (n_items_seen - 1) & 1u)) atomicOr(a.counters + 2, kStatusFp4Timeout);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        // Scale blocks travel to tensor memory with tcgen05.cp. An MMA that has to wait for a copy issued just before
-        // it stalls the whole pipe, so the bank scales of stage i+1 are copied before the MMAs of stage i are issued
-        // (when that stage has already landed), and the activation scales of a work item are copied once per item.
-        if (lane == 0) {
+    } else if (warp == 1 || warp == 6) {
+        // ---------------- MMA issuers ----------------
+        // Issuer A (warp 1) takes the even stages of the CTA's stage sequence, issuer B (warp 6) the odd ones; each owns an
+        // accumulator per buffer and the epilogue adds the two. Scale blocks travel to tensor memory with tcgen05.cp:
+        // the bank scales of an issuer's next stage are copied before the MMAs of its current stage are issued (when
+        // that stage has already landed), the activation scales of a work item once per item (each issuer its stages).
+        const uint32_t me = warp == 1 ? 0u : 1u;
+        if (lane == 0 && me < n_issuers) {
             const uint32_t idesc = idesc_nvf4(kF4ARows, kF4BRows);
             const uint32_t total = (uint32_t)((tile_hi - tile_lo) * NS);
-            const bool sfb_resident = 64 + S * 16 + NS * 16 <= (int)kF4TmemCols;
             const uint32_t tmem_sfb_item = tmem_sf0 + S * 16;  // NS x 16 columns when resident
             // descriptor words: smem address >> 4 in the low 14 bits; LBO >> 4 at bit 16; SBO = 128 B, version 1 in the high word
             const uint32_t hi_word = 0x00004008u;
@@ -282,18 +287,22 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
             const uint32_t b_lo0 = ((smem_u32(bimg) >> 4) & 0x3FFFu) | ((uint32_t)(kF4BRows * 16 >> 4) << 16);
             const uint32_t sfa_lo0 = (smem_u32(stages + kF4ANib) >> 4) & 0x3FFFu;
             const uint32_t sfb_lo0 = (smem_u32(bimg + kF4BNib) >> 4) & 0x3FFFu;
-            uint32_t it = 0, tcount = 0, n_items_seen = 0, sfa_done = 0;  // sfa_done: stages whose bank scales are in TMEM
-            uint32_t s = 0, ph = 0;                                        // ring slot and phase of stage `it`
+            uint32_t tcount = 0, n_items_seen = 0;
+            uint32_t sfa_done = 0;  // this issuer's stages below sfa_done have their bank scales in tensor memory
             int cur_item = -1;
             bool live = true;
-            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
+            uint32_t it0 = 0;       // index of the tile's first stage in the CTA's stage sequence
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount, it0 += (uint32_t)NS) {
                 const int item = (int)(tile / RB);
                 if (item != cur_item) {
                     if (!mbar_wait(smem_u32(b_full), n_items_seen & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     if (sfb_resident)
-                        for (int q = 0; q < NS * 4; ++q)
-                            tc_cp_sf_lo(tmem_sfb_item + 4 * q, sfb_lo0 + (uint32_t)(((q >> 2) * kF4BStage + 512 * (q & 3)) >> 4));
+                        for (int st = 0; st < NS; ++st)
+                            if (((it0 + (uint32_t)st) & (n_issuers - 1u)) == me)  // the stages this issuer will multiply
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    tc_cp_sf_lo(tmem_sfb_item + 16 * st + 4 * j, sfb_lo0 + (uint32_t)((st * kF4BStage + 512 * j) >> 4));
                     cur_item = item;
                     ++n_items_seen;
                 }
@@ -301,8 +310,12 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
                 const uint32_t buf = tcount & 1u;
                 if (!mbar_wait(smem_u32(&acc_empty[buf]), ((tcount >> 1) & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t tmem_d = tmem + buf * 32;
-                for (int st = 0; st < NS; ++st, ++it) {
+                const uint32_t tmem_d = tmem + buf * 64 + me * 32;
+                bool first = true;
+                for (int st = 0; st < NS; ++st) {
+                    const uint32_t it = it0 + (uint32_t)st;
+                    if ((it & (n_issuers - 1u)) != me) continue;
+                    const uint32_t s = it % (uint32_t)S, ph = (it / (uint32_t)S) & 1u;
                     if (sfa_done <= it) {  // not copied ahead: wait for the stage and copy now
                         if (!mbar_wait(smem_u32(&full[s]), ph)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -311,41 +324,43 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
                         for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + s * 16 + 4 * j, lo + j * 32);
                         sfa_done = it + 1;
                     }
-                    uint32_t sn = s + 1, phn = ph;
-                    if (sn == (uint32_t)S) { sn = 0; phn ^= 1u; }
-                    if (it + 1 < total && sfa_done == it + 1 && mbar_test(smem_u32(&full[sn]), phn)) {  // look one stage ahead
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t lo = sfa_lo0 + sn * (kF4AStage >> 4);
+                    const uint32_t nx = it + n_issuers;  // this issuer's next stage
+                    if (nx < total && sfa_done <= nx) {
+                        const uint32_t sn = nx % (uint32_t)S, phn = (nx / (uint32_t)S) & 1u;
+                        if (mbar_test(smem_u32(&full[sn]), phn)) {
+                            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                            const uint32_t lo = sfa_lo0 + sn * (kF4AStage >> 4);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + sn * 16 + 4 * j, lo + j * 32);
-                        sfa_done = it + 2;
+                            for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + sn * 16 + 4 * j, lo + j * 32);
+                            sfa_done = nx + 1;
+                        }
                     }
                     const uint32_t a_lo = a_lo0 + s * (kF4AStage >> 4), b_lo = b_lo0 + (uint32_t)st * (kF4BStage >> 4);
                     const uint32_t sfa = tmem_sf0 + s * 16;
                     uint32_t sfb = tmem_sfb_item + st * 16;
                     if (!sfb_resident) {
-                        sfb = tmem_sf0 + S * 16 + (s & 1) * 16;
+                        sfb = tmem_sf0 + S * 16 + (s & 3) * 16;  // 4 small slots: consecutive stages of either issuer never collide
 #pragma unroll
                         for (int j = 0; j < 4; ++j) tc_cp_sf_lo(sfb + 4 * j, sfb_lo0 + (uint32_t)((st * kF4BStage + 512 * j) >> 4));
                     }
-                    if (st == 0) tc_mma_nvf4_lo<false>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sfa, sfb);
+                    if (first) tc_mma_nvf4_lo<false>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sfa, sfb);
                     else tc_mma_nvf4_lo<true>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sfa, sfb);
+                    first = false;
 #pragma unroll
                     for (int j = 1; j < 4; ++j)
                         tc_mma_nvf4_lo<true>(tmem_d, a_lo + j * (2 * kF4ARows * 16 >> 4), hi_word, b_lo + j * (2 * kF4BRows * 16 >> 4), hi_word,
                                              idesc, sfa + 4 * j, sfb + 4 * j);
                     tc_commit_f4(smem_u32(&empty[s]));
-                    s = sn; ph = phn;
                 }
                 if (live) {
                     tc_commit_f4(smem_u32(&acc_full[buf]));
-                    if (last_of_item) tc_commit_f4(smem_u32(b_empty));  // every MMA that reads this activation image is done
+                    if (last_of_item) tc_commit_f4(smem_u32(b_empty));  // every MMA of this issuer that reads the activation image is done
                 }
             }
         }
     } else {
         // ---------------- epilogue warps (TMEM lane quarter = warp % 4) ----------------
-        const int quarter = warp & 3, ew = warp - 2, et = tid - 64;  // ew 0..3, et 0..127
+        const int quarter = warp & 3, ew = warp - 2, et = tid - 64;  // warps 2..5: ew 0..3, et 0..127
         const int row = quarter * 32 + lane;
         uint32_t tcount = 0;
         for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
@@ -373,8 +388,15 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
             if (fail) { if (et == 0) atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             uint32_t d[32];
-            tmem_ld32_f4(tmem + buf * 32 + ((uint32_t)(quarter * 32) << 16), d);
+            tmem_ld32_f4(tmem + buf * 64 + ((uint32_t)(quarter * 32) << 16), d);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (n_issuers == 2) {  // add issuer B's accumulator
+                uint32_t d2[32];
+                tmem_ld32_f4(tmem + buf * 64 + 32 + ((uint32_t)(quarter * 32) << 16), d2);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int n = 0; n < 24; ++n) d[n] = __float_as_uint(__uint_as_float(d[n]) + __uint_as_float(d2[n]));
+            }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));  // accumulator buffer may be overwritten

@@ -45,6 +45,7 @@ struct Plan {
     float* pscale_dn;      // [P]      same for the down image
     uint8_t* bq_gu;        // [max_items, H/256, 6144] FP4 activation images of the gate_up pass (NULL: not laid out)
     uint8_t* bq_dn;        // [max_items, I/256, 6144]
+    float* yt;             // [P, H]   per-pair down outputs in natural row order (tensor regime only, else NULL)
     int max_pairs;
     int max_items;
     int max_gitems;
@@ -53,8 +54,8 @@ struct Plan {
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
-        off_pscale_dn, off_bq_gu, off_bq_dn, total;
-    int fp4;
+        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, total;
+    int fp4, tiled;
     int max_pairs, max_items, max_gitems;
 };
 
@@ -101,6 +102,8 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
              (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
     p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : 0);
     p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : 0);
+    p.tiled = (T * k >= 16 * (size_t)L.n_slots) ? 1 : 0;  // batch shapes the tensor regime serves
+    p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.total = o;
     return p;
 }
@@ -135,11 +138,23 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.pscale_dn = (float*)(b + l.off_pscale_dn);
     p.bq_gu = l.fp4 ? (uint8_t*)(b + l.off_bq_gu) : nullptr;
     p.bq_dn = l.fp4 ? (uint8_t*)(b + l.off_bq_dn) : nullptr;
+    p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
     p.max_gitems = l.max_gitems;
     return p;
 }
+
+// Top-k selection of one routing call (shared by the router kernel and the plan kernel's fused path).
+struct TopkArgs {
+    const float* logits;   // [T, E]; NULL = no top-k to run
+    const float* e_bias;   // [E] or NULL
+    int kind, renorm;
+    float scaling;
+    int n_tokens, n_experts, top_k;
+    int32_t* ids;          // [T, top_k]
+    float* gates;          // [T, top_k]
+};
 
 // ---- host-side launch wrappers (one per .cu file) -------------------------------------------------------------
 int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2, float* out, int rows, int cols,
@@ -148,10 +163,13 @@ int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, f
 int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
                   float* logits, float* tok_scale, int32_t* status, cudaStream_t st);
-int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const void* x, int x_dtype,
-                int reset_status, const Plan& p, cudaStream_t st);
+int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, int reset_status,
+                const TopkArgs& tk, const Plan& p, cudaStream_t st);
 int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st);
-int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st);
+int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
+                  cudaStream_t st);
+int launch_combine_tiled(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                         int y_dtype, cudaStream_t st);
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st);
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                    int y_dtype, cudaStream_t st);
@@ -233,6 +251,70 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] *= 0.08838834764831845f;
+}
+
+// k rounds of warp arg-max for token t (ties -> lower index) and the gate weights; executed by one full warp.
+template <int PL>
+__device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int lane) {
+    float choice[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = i * 32 + lane;
+        float c = -INFINITY;
+        if (e < a.n_experts) {
+            const float lg = a.logits[(size_t)t * a.n_experts + e];
+            c = a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? (1.0f / (1.0f + expf(-lg))) + (a.e_bias ? a.e_bias[e] : 0.0f) : lg;
+        }
+        choice[i] = c;
+    }
+    float my_val = 0.0f;  // lane j keeps the j-th chosen weight source
+    int my_id = -1;
+    for (int j = 0; j < a.top_k; ++j) {
+        float best = -INFINITY;
+        int best_e = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+            const int e = i * 32 + lane;
+            if (e < a.n_experts && (choice[i] > best)) { best = choice[i]; best_e = e; }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+            const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
+            if (ov > best || (ov == best && oe < best_e)) { best = ov; best_e = oe; }
+        }
+#pragma unroll
+        for (int i = 0; i < PL; ++i)
+            if (i * 32 + lane == best_e) choice[i] = -INFINITY;  // remove the winner from its owner lane
+        if (lane == j) {
+            my_id = best_e;
+            const float lg = a.logits[(size_t)t * a.n_experts + best_e];
+            my_val = a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? 1.0f / (1.0f + expf(-lg)) : lg;
+        }
+    }
+    float gate;
+    if (a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX) {
+        const float s = lane < a.top_k ? my_val : 0.0f;
+        float tot = 0.0f;  // sequential sum in index order, the way a row reduction over k values reads
+        for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, s, j);
+        gate = a.renorm ? my_val / (tot + 1e-20f) : my_val;
+        gate *= a.scaling;
+    } else {
+        const float mx = __shfl_sync(0xffffffffu, my_val, 0);  // chosen values are in descending order
+        const float ex = lane < a.top_k ? expf(my_val - mx) : 0.0f;
+        float tot = 0.0f;
+        for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, ex, j);
+        gate = ex / tot;
+    }
+    if (lane < a.top_k) {
+        a.ids[(size_t)t * a.top_k + lane] = my_id;
+        a.gates[(size_t)t * a.top_k + lane] = gate;
+    }
+}
+__device__ __forceinline__ void topk_one_token(const TopkArgs& a, int t, int lane) {
+    if (a.n_experts <= 256) topk_one_token_pl<8>(a, t, lane);
+    else if (a.n_experts <= 512) topk_one_token_pl<16>(a, t, lane);
+    else topk_one_token_pl<32>(a, t, lane);
 }
 
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {

@@ -1,50 +1,78 @@
 // Batch coalescing on the device: sorts (token, expert) routing entries by expert, so that the entries of one slot
-// are contiguous, and cuts them into work items of up to 8 pairs that share one pass over the slot's bank.
+// are contiguous, and cuts them into work items: up to 8 pairs that share one pass over the slot's bank (streaming
+// regimes) and up to 128 pairs of one expert (tensor regime).
 // Takes the role of `torch.unique` + per-expert gathers (chronos_1t/models/glm5_chronos_moe.py:508-522) and of
 // the argsort/unique_consecutive grouping (chronos_1t/models/glm53_chronos_moe.py:456-459) with no host round trip.
+// For decode-sized batches the top-k selection runs inside the same launch (one warp per token).
 #include "common.cuh"
 
 namespace chronos {
 
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanWarps = kPlanThreads / 32;
 constexpr int kPlanMaxBins = 1024 + 1;  // experts + the shared-expert bin
 
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ ids, int n_tokens, int top_k,
+// Exclusive scan over the block: every thread passes its value and gets the sum of the values of lower threads;
+// `total` receives the block sum. Warp shuffles inside the warps, warp 0 scans the warp totals.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot /*[kPlanWarps + 1]*/, int& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += o;
+    }
+    __syncthreads();  // warp_tot may still be read from a previous call
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = warp_tot[lane];
+        int winc = w;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, winc, d);
+            if (lane >= d) winc += o;
+        }
+        warp_tot[lane] = winc - w;  // exclusive prefix of the warp totals
+        if (lane == 31) warp_tot[kPlanWarps] = winc;
+    }
+    __syncthreads();
+    total = warp_tot[kPlanWarps];
+    return warp_tot[warp] + inc - v;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ ids_in, int n_tokens, int top_k,
                                                             int n_experts, int group_size, int n_slots, int with_shared,
-                                                            const void* __restrict__ x, int x_dtype, int hidden,
-                                                            int reset_status, Plan p) {
+                                                            int reset_status, TopkArgs tk, Plan p) {
     __shared__ int cnt[kPlanMaxBins + 1];
     __shared__ int off[kPlanMaxBins + 1];
     __shared__ int cur[kPlanMaxBins + 1];
-    __shared__ int scan[2][kPlanThreads + 1];
+    __shared__ int warp_tot[kPlanWarps + 1];
     const int tid = threadIdx.x;
     const int n_bins = n_experts + 1;
     const int n_entries = n_tokens * top_k;
     for (int i = tid; i <= n_bins; i += kPlanThreads) { cnt[i] = 0; cur[i] = 0; }
-    __syncthreads();
+    const int32_t* ids = ids_in;
+    if (tk.logits != nullptr) {  // fused top-k: one warp per token (decode-sized batches only)
+        for (int t = tid >> 5; t < n_tokens; t += kPlanWarps) topk_one_token(tk, t, tid & 31);
+        ids = tk.ids;
+    }
+    __syncthreads();  // also orders the ids written above (global memory, same block) before they are read back
     for (int i = tid; i < n_entries; i += kPlanThreads) {
         const int e = ids[i];
         if (e >= 0 && e < n_experts) atomicAdd(&cnt[e], 1);
     }
     if (tid == 0 && with_shared) cnt[n_experts] = n_tokens;
     __syncthreads();
-    // exclusive scan of cnt[0 .. n_bins) (n_bins <= 1025): chunked Hillis-Steele over 1024 + carry
+    // exclusive scan of cnt[0 .. n_bins) (n_bins <= 1025): chunks of 1024 with a carry
     int carry = 0;
     for (int base = 0; base < n_bins; base += kPlanThreads) {
         const int idx = base + tid;
         const int v = idx < n_bins ? cnt[idx] : 0;
-        int src = 0;
-        scan[0][tid] = v;
-        __syncthreads();
-        for (int d = 1; d < kPlanThreads; d <<= 1) {
-            const int a = scan[src][tid] + (tid >= d ? scan[src][tid - d] : 0);
-            scan[src ^ 1][tid] = a;
-            src ^= 1;
-            __syncthreads();
-        }
-        if (idx < n_bins) off[idx] = carry + scan[src][tid] - v;
-        carry += scan[src][kPlanThreads - 1];
-        __syncthreads();
+        int total;
+        const int ex = block_exclusive_scan(v, warp_tot, total);
+        if (idx < n_bins) off[idx] = carry + ex;
+        carry += total;
     }
     if (tid == 0) off[n_bins] = carry;
     __syncthreads();
@@ -65,7 +93,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
             p.pair_token[off[n_experts] + t] = t;
             p.pair_expert[off[n_experts] + t] = n_experts;
         }
-    // work items: slot s owns sorted pairs [off[s*K], off[(s+1)*K]); the shared expert is slot n_slots
+    // streaming work items: slot s owns sorted pairs [off[s*K], off[(s+1)*K]); the shared expert is slot n_slots
     carry = 0;
     const int n_vslots = n_slots + 1;
     for (int base = 0; base < n_vslots; base += kPlanThreads) {
@@ -74,17 +102,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         if (s < n_slots) { lo = off[s * group_size]; hi = off[(s + 1) * group_size]; }
         else if (s == n_slots) { lo = off[n_experts]; hi = off[n_bins]; }
         const int ni = (hi - lo + kPairsPerItem - 1) / kPairsPerItem;
-        int src = 0;
-        __syncthreads();
-        scan[0][tid] = ni;
-        __syncthreads();
-        for (int d = 1; d < kPlanThreads; d <<= 1) {
-            const int a = scan[src][tid] + (tid >= d ? scan[src][tid - d] : 0);
-            scan[src ^ 1][tid] = a;
-            src ^= 1;
-            __syncthreads();
-        }
-        const int first = carry + scan[src][tid] - ni;
+        int total;
+        const int first = carry + block_exclusive_scan(ni, warp_tot, total);
         for (int q = 0; q < ni; ++q) {
             const int it = first + q;
             if (it < p.max_items) {
@@ -93,7 +112,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
                 p.item_slot[it] = s;
             }
         }
-        carry += scan[src][kPlanThreads - 1];
+        carry += total;
     }
     const int n_items_total = carry;
     // tensor-core work items: expert e (bin n_experts = shared expert) owns sorted pairs [off[e], off[e+1]), cut into
@@ -104,17 +123,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         int lo = 0, hi = 0;
         if (e < n_bins) { lo = off[e]; hi = off[e + 1]; }
         const int ni = (hi - lo + kPairsPerGemmItem - 1) / kPairsPerGemmItem;
-        int src = 0;
-        __syncthreads();
-        scan[0][tid] = ni;
-        __syncthreads();
-        for (int d = 1; d < kPlanThreads; d <<= 1) {
-            const int a = scan[src][tid] + (tid >= d ? scan[src][tid - d] : 0);
-            scan[src ^ 1][tid] = a;
-            src ^= 1;
-            __syncthreads();
-        }
-        const int first = carry + scan[src][tid] - ni;
+        int total;
+        const int first = carry + block_exclusive_scan(ni, warp_tot, total);
         for (int q = 0; q < ni; ++q) {
             const int it = first + q;
             if (it < p.max_gitems) {
@@ -123,7 +133,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
                 p.gitem_slot[it] = e < n_experts ? e / group_size : n_slots;
             }
         }
-        carry += scan[src][kPlanThreads - 1];
+        carry += total;
     }
     if (tid == 0) {
         p.counters[3] = min(carry, p.max_gitems);
@@ -133,10 +143,10 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
     }
 }
 
-int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, const void* x, int x_dtype,
-                int reset_status, const Plan& p, cudaStream_t st) {
+int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, int reset_status,
+                const TopkArgs& tk, const Plan& p, cudaStream_t st) {
     plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, n_tokens, L.top_k, L.n_experts, L.group_size, L.n_slots,
-                                           with_shared && L.shared_inter > 0, x, x_dtype, L.hidden, reset_status, p);
+                                           with_shared && L.shared_inter > 0, reset_status, tk, p);
     return check_launch("plan");
 }
 

@@ -194,71 +194,11 @@ __global__ void __launch_bounds__(256) router_logits_small_kernel(const void* __
 // One warp per token: k rounds of arg-max over the choice scores (ties -> lower index), then the gate weights.
 // softmax flavour: choice = logit, gate = softmax over the k chosen logits.
 // sigmoid flavour: choice = sigmoid(logit) + bias, weight = sigmoid(logit) (unbiased), optional renorm, * scaling.
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
-                                                          const float* __restrict__ e_bias, int kind, int renorm,
-                                                          float scaling, int n_tokens, int n_experts, int top_k,
-                                                          int32_t* __restrict__ ids, float* __restrict__ gates) {
-    const int lane = threadIdx.x & 31;
+// (topk_one_token lives in common.cuh so that the plan kernel can run it in the same launch.)
+__global__ void __launch_bounds__(256) router_topk_kernel(TopkArgs tk) {
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (t >= n_tokens) return;
-    constexpr int kMaxPerLane = 32;  // n_experts <= 1024
-    float choice[kMaxPerLane];
-    const int per_lane = (n_experts + 31) / 32;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
-        const int e = i * 32 + lane;
-        float c = -INFINITY;
-        if (i < per_lane && e < n_experts) {
-            const float lg = logits[(size_t)t * n_experts + e];
-            c = kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? (1.0f / (1.0f + expf(-lg))) + (e_bias ? e_bias[e] : 0.0f) : lg;
-        }
-        choice[i] = c;
-    }
-    float my_val = 0.0f;  // lane j keeps the j-th chosen weight source
-    int my_id = -1;
-    for (int j = 0; j < top_k; ++j) {
-        float best = -INFINITY;
-        int best_e = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i) {
-            const int e = i * 32 + lane;
-            if (i < per_lane && e < n_experts && (choice[i] > best)) { best = choice[i]; best_e = e; }
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-            const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
-            if (ov > best || (ov == best && oe < best_e)) { best = ov; best_e = oe; }
-        }
-        // remove the winner from its owner lane
-#pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i)
-            if (i * 32 + lane == best_e) choice[i] = -INFINITY;
-        if (lane == j) {
-            my_id = best_e;
-            const float lg = logits[(size_t)t * n_experts + best_e];
-            my_val = kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? 1.0f / (1.0f + expf(-lg)) : lg;
-        }
-    }
-    float gate;
-    if (kind == CHRONOS_ROUTER_SIGMOID_NOAUX) {
-        float s = lane < top_k ? my_val : 0.0f;
-        // sequential sum in index order, the way a row reduction over k values reads
-        float tot = 0.0f;
-        for (int j = 0; j < top_k; ++j) tot += __shfl_sync(0xffffffffu, s, j);
-        gate = renorm ? my_val / (tot + 1e-20f) : my_val;
-        gate *= scaling;
-    } else {
-        const float mx = __shfl_sync(0xffffffffu, my_val, 0);  // chosen values are in descending order
-        const float ex = lane < top_k ? expf(my_val - mx) : 0.0f;
-        float tot = 0.0f;
-        for (int j = 0; j < top_k; ++j) tot += __shfl_sync(0xffffffffu, ex, j);
-        gate = ex / tot;
-    }
-    if (lane < top_k) {
-        ids[(size_t)t * top_k + lane] = my_id;
-        gates[(size_t)t * top_k + lane] = gate;
-    }
+    if (t >= tk.n_tokens) return;
+    topk_one_token(tk, t, threadIdx.x & 31);
 }
 
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
@@ -287,9 +227,9 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
         else router_logits_kernel<4, 4, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     }
     if (int rc = check_launch("router_logits")) return rc;
-    router_topk_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(logits, L.e_bias, L.router_kind, L.renorm,
-                                                                      L.routed_scaling, n_tokens, L.n_experts,
-                                                                      L.top_k, ids, gates);
+    if (ids == nullptr) return CHRONOS_OK;  // the caller runs the top-k inside its plan launch
+    TopkArgs tk{logits, L.e_bias, L.router_kind, L.renorm, L.routed_scaling, n_tokens, L.n_experts, L.top_k, ids, gates};
+    router_topk_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(tk);
     return check_launch("router_topk");
 }
 

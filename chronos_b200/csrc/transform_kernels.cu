@@ -119,7 +119,7 @@ __device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
 // ---------------------------------------------------------------------------------------------------------------
 // gate_up input. Transform warps: fp16 mode - one warp per (sorted pair, 128-column block) writes x_c;
 // FP4 mode - one warp per (work item, position in item, 128-column block) writes three e2m1 terms into the item's
-// activation image (positions past the item's pair count are written as zeros). Further warps compute V_gu . x.
+// activation image (positions past the item's pair count stay unwritten). Further warps compute V_gu . x.
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p,
                                                      int fp4) {
@@ -146,9 +146,10 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
         }
         const int blk = (int)(gw % nblk);
         const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
-        if (item >= p.counters[0]) return;
-        v[0] = v[1] = v[2] = v[3] = 0.0f;
-        if (pos < p.item_cnt[item]) {
+        // positions past the item's pair count are left unwritten: row n of the image only feeds accumulator column n,
+        // and the bank pass never reads the columns of absent pairs
+        if (item >= p.counters[0] || pos >= p.item_cnt[item]) return;
+        {
             const int pair = p.item_start[item] + pos;
             const int t = p.pair_token[pair];
             const float g = p.tok_scale[t];
@@ -205,6 +206,47 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
     if (lane == 0) p.hmid[(size_t)pair * r + c] = acc;
 }
 
+// Healer input factor for batches with many pairs per expert: a block = 8 consecutive sorted pairs x 8 rank rows; warp w
+// computes the 8 dots of pair 8 b + w, and the 8 warps share the 8 rows of V_gu through L1 when they share the expert.
+__global__ void __launch_bounds__(256) healer_in_tile_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p) {
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int H = L.hidden, r = L.rank, rgroups = r / 8;
+    const int pair = (int)(blockIdx.x / rgroups) * 8 + wib, rg = (int)(blockIdx.x % rgroups);
+    if (pair >= p.counters[1]) return;
+    const int t = p.pair_token[pair], e = p.pair_expert[pair];
+    if (e >= L.n_experts) return;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+    const uint8_t* vbase = L.v_gu + ((size_t)e * r + rg * 8) * H;
+    for (int k = lane * 16; k < H; k += 512) {
+        uint4 vw[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) vw[c] = *reinterpret_cast<const uint4*>(vbase + (size_t)c * H + k);
+        float xv[16];
+        ld_act16(x, x_dtype, (size_t)t * H + k, xv);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t ww[4] = {vw[c].x, vw[c].y, vw[c].z, vw[c].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 lo = e4m3x2_to_f32((uint16_t)(ww[q] & 0xffffu)), hi = e4m3x2_to_f32((uint16_t)(ww[q] >> 16));
+                acc[c] = fmaf(lo.x, xv[q * 4 + 0], acc[c]);
+                acc[c] = fmaf(lo.y, xv[q * 4 + 1], acc[c]);
+                acc[c] = fmaf(hi.x, xv[q * 4 + 2], acc[c]);
+                acc[c] = fmaf(hi.y, xv[q * 4 + 3], acc[c]);
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        float sacc = acc[c];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, off);
+        if (lane == 0) p.hmid[(size_t)pair * r + rg * 8 + c] = sacc;
+    }
+}
+
 // Per-token power-of-two scale near rms(x[t]); one warp per token, fixed summation order.
 __global__ void __launch_bounds__(256) token_scale_kernel(const void* __restrict__ x, int x_dtype, int n_tokens, int hidden,
                                                           float* __restrict__ tok_scale) {
@@ -227,11 +269,17 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
     return check_launch("token_scale");
 }
 
-int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, cudaStream_t st) {
+int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
+                  cudaStream_t st) {
     const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
-    const long warps = xf + (long)p.max_pairs * L.rank;
+    // few pairs per expert: healer warps ride along in the same launch, one per (pair, rank row); many pairs per expert:
+    // a second launch whose blocks share healer rows through L1
+    const long warps = xf + (many_pairs ? 0 : (long)p.max_pairs * L.rank);
     pre_gu_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, x, x_dtype, p, fp4);
-    return check_launch("pre_gu");
+    if (int rc = check_launch("pre_gu")) return rc;
+    if (!many_pairs) return CHRONOS_OK;
+    healer_in_tile_kernel<<<(unsigned)(((p.max_pairs + 7) / 8) * (L.rank / 8)), 256, 0, st>>>(L, x, x_dtype, p);
+    return check_launch("healer_in_tile");
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -244,12 +292,13 @@ __global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p)
     __shared__ float hs[8][kMaxRank];
     __shared__ float act_s[8][128];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const long gw = (long)blockIdx.x * 8 + wib;
     const int n_pairs = p.counters[1];
     const int I = L.inter, E = L.n_experts;
     constexpr int r = R16 * 16;
     const int nblk = I / 128;
-    const int pair = (int)(gw / nblk), blk = (int)(gw % nblk);
+    // a block = 8 consecutive sorted pairs x one 128-output block: pairs of one expert sit next to each other, so the
+    // warps of a block mostly read the same healer rows (L1 hits) when an expert has many pairs
+    const int pair = (int)(blockIdx.x / nblk) * 8 + wib, blk = (int)(blockIdx.x % nblk);
     if (pair >= n_pairs) return;
     const int e = p.pair_expert[pair];
     const float* z1 = p.z1 + (size_t)pair * 2 * I;
@@ -369,9 +418,8 @@ __global__ void __launch_bounds__(256) mid_xform_kernel(chronos_layer_t L, Plan 
     }
     const int blk = (int)(gw % nblk);
     const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
-    if (item >= p.counters[0]) return;
-    v[0] = v[1] = v[2] = v[3] = 0.0f;
-    if (pos < p.item_cnt[item]) {
+    if (item >= p.counters[0] || pos >= p.item_cnt[item]) return;  // absent pairs: rows left unwritten (see pre_gu_kernel)
+    {
         const int pair = p.item_start[item] + pos;
         float ss = 0.0f;
         for (int b = 0; b < nblk; ++b) ss += p.act_ss[(size_t)pair * nblk + b];  // fixed order: same scale in every warp
@@ -389,7 +437,7 @@ __global__ void __launch_bounds__(256) mid_xform_kernel(chronos_layer_t L, Plan 
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st) {
     const int nblk = L.inter / 128;
     long warps = (long)p.max_pairs * nblk;
-    const unsigned grid_a = (unsigned)((warps + 7) / 8);
+    const unsigned grid_a = (unsigned)(((p.max_pairs + 7) / 8) * nblk);
     switch (L.rank / 16) {
         case 1: mid_act_kernel<1><<<grid_a, 256, 0, st>>>(L, p); break;
         case 2: mid_act_kernel<2><<<grid_a, 256, 0, st>>>(L, p); break;
@@ -480,6 +528,110 @@ __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p,
         else
             reinterpret_cast<float*>(y)[(size_t)t * H + i] = acc;
     }
+}
+
+// Tensor-regime combine, part 1: yt[pair, i] = beta_d * r_s1[i] * y1[pair, r_inv[i]] + U_down[e, i, :] . hd[pair, :].
+// A block = 8 consecutive sorted pairs x 128 output rows (the warps share the healer rows of an expert through L1).
+template <int R16>
+__global__ void __launch_bounds__(256) down_term_kernel(chronos_layer_t L, Plan p) {
+    __shared__ float hd[8][kMaxRank];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int H = L.hidden, I = L.inter, E = L.n_experts;
+    constexpr int r = R16 * 16;
+    const int nblk = I / 128, nrb = H / 128;
+    const int pos = (int)(blockIdx.x / nrb) * 8 + warp, rb = (int)(blockIdx.x % nrb);
+    if (pos >= p.counters[1]) return;
+    const int e = p.pair_expert[pos];
+    const int row0 = rb * 128 + lane * 4;
+    float4* dst = reinterpret_cast<float4*>(p.yt + (size_t)pos * H + row0);
+    if (e >= E) {  // shared expert: plain rows
+        *dst = *reinterpret_cast<const float4*>(p.y1 + (size_t)pos * H + row0);
+        return;
+    }
+    const uint4* urow = reinterpret_cast<const uint4*>(L.u_dn + ((size_t)e * H + row0) * r);
+    uint4 uall[4 * R16];
+#pragma unroll
+    for (int w = 0; w < 4 * R16; ++w) uall[w] = urow[w];
+    for (int c = lane; c < r; c += 32) {
+        float s = 0.0f;
+#pragma unroll 4
+        for (int b = 0; b < nblk; ++b) s += p.hpart[((size_t)pos * nblk + b) * r + c];
+        hd[warp][c] = s;
+    }
+    __syncwarp();
+    const float beta = L.dn_beta[e];
+    const uint2 ro2 = *reinterpret_cast<const uint2*>(L.dn_rout + (size_t)e * H + row0);
+    const uint32_t ro[4] = {ro2.x & 0xffffu, ro2.x >> 16, ro2.y & 0xffffu, ro2.y >> 16};
+    float out[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float v = p.y1[(size_t)pos * H + (ro[q] & 0x7fffu)];
+        const float yb = (ro[q] >> 15) ? -v : v;
+        float heal = 0.0f;
+#pragma unroll
+        for (int c16 = 0; c16 < R16; ++c16) {
+            const uint4 u = uall[q * R16 + c16];
+            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+                const float2 lo = e4m3x2_to_f32((uint16_t)(uw[w4] & 0xffffu));
+                const float2 hi = e4m3x2_to_f32((uint16_t)(uw[w4] >> 16));
+                const float* hp = &hd[warp][c16 * 16 + w4 * 4];
+                heal = fmaf(lo.x, hp[0], heal);
+                heal = fmaf(lo.y, hp[1], heal);
+                heal = fmaf(hi.x, hp[2], heal);
+                heal = fmaf(hi.y, hp[3], heal);
+            }
+        }
+        out[q] = fmaf(beta, yb, heal);
+    }
+    *dst = make_float4(out[0], out[1], out[2], out[3]);
+}
+
+// Part 2: y[t, i] = sum_j gate[t, j] * yt[pos(t, j), i] (+ shared expert row), j in index order.
+__global__ void __launch_bounds__(256) combine_sum_kernel(chronos_layer_t L, Plan p, const float* __restrict__ gates,
+                                                          int with_shared, void* __restrict__ y, int y_dtype) {
+    const int H = L.hidden, k = L.top_k;
+    const int t = blockIdx.x, i0 = (blockIdx.y * 256 + threadIdx.x) * 4;
+    if (i0 >= H) return;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < k; ++j) {
+        const int pos = p.pos_of[t * k + j];
+        if (pos < 0) continue;
+        const float g = gates[t * k + j];
+        const float4 v = *reinterpret_cast<const float4*>(p.yt + (size_t)pos * H + i0);
+        acc[0] = fmaf(g, v.x, acc[0]); acc[1] = fmaf(g, v.y, acc[1]);
+        acc[2] = fmaf(g, v.z, acc[2]); acc[3] = fmaf(g, v.w, acc[3]);
+    }
+    if (with_shared) {
+        const float4 v = *reinterpret_cast<const float4*>(p.yt + (size_t)(p.offsets[L.n_experts] + t) * H + i0);
+        acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
+    }
+    if (y_dtype == CHRONOS_DTYPE_BF16) {
+        __nv_bfloat162 a01 = __floats2bfloat162_rn(acc[0], acc[1]), a23 = __floats2bfloat162_rn(acc[2], acc[3]);
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t*>(&a01);
+        o.y = *reinterpret_cast<uint32_t*>(&a23);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(y) + (size_t)t * H + i0) = o;
+    } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + (size_t)t * H + i0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+}
+
+int launch_combine_tiled(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                         int y_dtype, cudaStream_t st) {
+    if (n_tokens <= 0) return CHRONOS_OK;
+    const unsigned grid = (unsigned)(((p.max_pairs + 7) / 8) * (L.hidden / 128));
+    switch (L.rank / 16) {
+        case 1: down_term_kernel<1><<<grid, 256, 0, st>>>(L, p); break;
+        case 2: down_term_kernel<2><<<grid, 256, 0, st>>>(L, p); break;
+        case 4: down_term_kernel<4><<<grid, 256, 0, st>>>(L, p); break;
+        default: down_term_kernel<8><<<grid, 256, 0, st>>>(L, p); break;
+    }
+    if (int rc = check_launch("down_term")) return rc;
+    dim3 g2((unsigned)n_tokens, (unsigned)((L.hidden / 4 + 255) / 256));
+    combine_sum_kernel<<<g2, 256, 0, st>>>(L, p, gates, with_shared && L.shared_inter > 0, y, y_dtype);
+    return check_launch("combine_sum");
 }
 
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,

@@ -239,6 +239,10 @@ def test_many_tokens_on_one_slot_and_skipped_entries():
             z = xn[t] @ gu.T
             ref[t] += wn[t, j] * ((O.silu(z[:cfg.inter]) * z[cfg.inter:]) @ dn.T)
     assert _rel_l2(y.cpu().numpy(), ref) <= LAYER_TOL
+    # the tensor-core regime forced onto a batch below its usual threshold (its small-batch healer kernels)
+    y_t = layer.routed_forward(x, ids, w, regime="tensor")
+    assert layer.device_status() == 0
+    assert _rel_l2(y_t.cpu().numpy(), ref) <= LAYER_TOL
     # all entries skipped -> exact zeros; zero tokens -> empty output
     y0 = layer.routed_forward(x, torch.full_like(ids, -1), w)
     assert torch.count_nonzero(y0) == 0
