@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX = 0, 1
-ABI_VERSION = 3
+ABI_VERSION = 4
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4 = 0, 1, 2, 3
 
 
@@ -33,7 +33,7 @@ class LayerStruct(C.Structure):
             "u_gu", "v_gu", "u_dn", "v_dn_t",
             "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2",
             "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
-            "gu_t", "dn_t", "sh_gu_t", "sh_dn_t")]
+            "gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn")]
     )
 
 

@@ -128,17 +128,28 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
         if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, p.tok_scale, st)) return rc;
     if (int rc = launch_plan(L, ids, n_tokens, with_shared, have_tok_scale ? 0 : 1, tk, p, st)) return rc;
     stage_mark(2, st);
-    const int many = (tensor && p.yt != nullptr) ? 1 : 0;  // many pairs per expert: healer kernels that share rows through L1
-    if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, many, st)) return rc;
+    // many pairs per expert (the batch shapes the tensor regime is chosen for): healer products on the tensor cores when
+    // the layer carries healer.v_down in its on-disk orientation, else CUDA-core kernels that share healer rows through L1
+    const int many = (tensor && p.yt != nullptr) ? 1 : 0;
+    const bool hmma = many && healer_mma_fits(L);
+    if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, hmma ? 2 : many, st)) return rc;
+    if (hmma)
+        if (int rc = launch_healer_in_mma(L, 0, x, x_dtype, p, st)) return rc;
     stage_mark(3, st);
     if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st))) return rc;
     stage_mark(4, st);
-    if (int rc = launch_mid(L, p, fp4, st)) return rc;
+    if (int rc = hmma ? launch_mid_mma(L, p, st) : launch_mid(L, p, fp4, st)) return rc;
     stage_mark(5, st);
     if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st))) return rc;
     stage_mark(6, st);
-    const int rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)
-                        : launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    int rc;
+    if (hmma) {
+        rc = launch_down_out_mma(L, p, st);
+        if (!rc) rc = launch_combine_sum(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    } else {
+        rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)
+                  : launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    }
     stage_mark(7, st);
     return rc;
 }
@@ -149,7 +160,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 3; }
+int chronos_b200_abi_version(void) { return 4; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256, 1) bank_gemm_kernel(const GemmArgs a) {
     // operand tiles need 1024-byte alignment for the swizzle pattern to line up with the descriptor
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int R = a.R, K = a.K, RB = R / 128, KS = K / kGemmKStep;
     const long n_tiles = (long)a.counters[3] * RB;
 

@@ -171,6 +171,13 @@ int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Pl
 int launch_combine_tiled(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                          int y_dtype, cudaStream_t st);
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st);
+// tensor-core healer path for batches with many pairs per expert (csrc/healer_mma.cu)
+bool healer_mma_fits(const chronos_layer_t& L);
+int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
+int launch_mid_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_combine_sum(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                       int y_dtype, cudaStream_t st);
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                    int y_dtype, cudaStream_t st);
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
@@ -331,6 +338,68 @@ __device__ __forceinline__ __half f32_to_f16_sat(float v) {
     return __ushort_as_half(r);
 }
 // ---- mbarrier / bulk-copy primitives (every wait is bounded) ----------------------------------------------------
+// Power-of-two scale near the root mean square of a vector (1 when the vector is all zero).
+__device__ __forceinline__ float pow2_scale(float sumsq, int n) {
+    const float rms = sqrtf(sumsq / (float)n);
+    return rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
+}
+
+// One 128-block of a gate_up input: gather + sign, Walsh-Hadamard, sign (identity for the shared expert).
+__device__ __forceinline__ void transform_gu_block(const chronos_layer_t& L, const void* __restrict__ x, int x_dtype,
+                                                   int t, int e, int blk, int lane, float (&v)[4]) {
+    const int H = L.hidden;
+    if (e >= L.n_experts) {  // shared expert: plain weights, identity keys
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = ld_act(x, x_dtype, (size_t)t * H + blk * 128 + lane * 4 + i);
+        return;
+    }
+    const uint2 ce = *reinterpret_cast<const uint2*>(L.gu_cin + (size_t)e * H + blk * 128 + lane * 4);
+    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float xv = ld_act(x, x_dtype, (size_t)t * H + (ent[i] & 0x7fffu));
+        v[i] = (ent[i] >> 15) ? -xv : xv;
+    }
+    fwht128_warp(v, lane);
+    const uint32_t sw = L.gu_cs2[(size_t)e * (H / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
+// One 128-block of a down input from the SwiGLU outputs `act` (fp32, natural order) of the pair.
+__device__ __forceinline__ void transform_dn_block(const chronos_layer_t& L, const float* __restrict__ act, int e, int blk,
+                                                   int lane, float (&v)[4]) {
+    const int I = L.inter;
+    if (e >= L.n_experts) {
+        const float4 a = *reinterpret_cast<const float4*>(act + blk * 128 + lane * 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        return;
+    }
+    const uint2 ce = *reinterpret_cast<const uint2*>(L.dn_cin + (size_t)e * I + blk * 128 + lane * 4);
+    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float a = act[ent[i] & 0x7fffu];
+        v[i] = (ent[i] >> 15) ? -a : a;
+    }
+    fwht128_warp(v, lane);
+    const uint32_t sw = L.dn_cs2[(size_t)e * (I / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
+__device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
+    __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
+    __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&h01);
+    o.y = *reinterpret_cast<uint32_t*>(&h23);
+    *reinterpret_cast<uint2*>(dst) = o;
+}
+
+
 constexpr uint32_t kWaitLimit = 1u << 22;  // polls of a ~1 us bounded try_wait before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }

@@ -1,0 +1,329 @@
+// Healer products and the transforms between the bank passes for batches with many pairs per expert: the rank-r
+// factors run on the tensor cores (mma.sync m16n8k16, fp16 operands converted exactly from e4m3, fp32 accumulate),
+// because a CUDA-core e4m3 decode per multiply costs more than the multiply.
+// Mathematics as in csrc/transform_kernels.cu (ChronosGlm5HolographicExpertGroup.forward_cold_fast,
+// chronos_1t/models/glm5_chronos_moe.py:149-195):
+//   hmid = V_gu x;  z_gu = beta r_s1 z1[r_inv] + U_gu hmid;  act = silu(z_gu[:I]) z_gu[I:];
+//   hd = V_down act;  y_pair = beta_d r_s1 y1[r_inv] + U_down hd.
+//
+// Contraction index trick shared by all kernels here: a k16 step of the MMA wants lane (g = lane / 4, q = lane % 4) to
+// hold A[row g][2q, 2q+1] and A[row g][2q+8, 2q+9]. Any permutation of the contraction index is legal if A and B
+// agree, so lane q owns a CONTIGUOUS run of the row (W 32-bit words of e4m3 = 4 W columns starting at 4 W q), and
+// step s takes word s of that run: columns 4Wq + 4s + {0,1} for the low pair, + {2,3} for the high pair. Loads are
+// then 4W-byte vectors per lane on the e4m3 side and 8-byte fp16 vectors on the activation side.
+#include "common.cuh"
+
+namespace chronos {
+
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v16) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((uint16_t)v16));
+    return r;
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+    const __half2 h = __halves2half2(f32_to_f16_sat(lo), f32_to_f16_sat(hi));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Healer input factor of a tensor-regime work item (one expert, up to 128 sorted pairs):
+//   out[pair, c] = (1 / g_pair) * sum_k V[e, c, k] * X[row(pair), k]      c < r, stored as fp16
+// V e4m3 [E, r, K]; X rows are activations (bf16 / fp32, row = token of the pair) or SwiGLU outputs (fp32, row = pair);
+// g_pair is the power-of-two scale the bank pass uses for the same pair (so the fp16 image stays in range); the
+// consumer multiplies it back. One CTA per work item; warp w owns rank rows 16 (w % MT) .. +15 and the pairs of
+// 8-pair tiles (w / MT), (w / MT) + 8 / MT, ...
+// ---------------------------------------------------------------------------------------------------------------
+struct HealInArgs {
+    const uint8_t* v;           // [E, r, K]
+    const void* x; int x_dtype; // rows of K
+    const int32_t* row_of_pair; // NULL: row = pair
+    const float* pscale;        // [P]
+    __half* out;                // [P, r]
+    const int32_t* gitem_start; const int32_t* gitem_cnt; const int32_t* pair_expert; const int32_t* counters;
+    int K, r, n_experts;
+};
+
+template <int MT>  // rank / 16
+__global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) {
+    constexpr int NG = 8 / MT;        // groups of warps along the pairs
+    constexpr int NTW = 16 / NG;      // 8-pair tiles per warp
+    const int item = blockIdx.x;
+    if (item >= a.counters[3]) return;
+    const int start = a.gitem_start[item], cnt = a.gitem_cnt[item];
+    const int e = a.pair_expert[start];
+    if (e >= a.n_experts) return;     // shared expert: no healer
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, q = lane & 3;
+    const int mt = warp % MT, ng = warp / MT;
+    const int K = a.K, r = a.r;
+    const int ntiles = (cnt + 7) >> 3;
+    float acc[NTW][4];
+    const uint8_t* xrow[NTW];
+    float inv[NTW];
+#pragma unroll
+    for (int i = 0; i < NTW; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        const int n = (ng + i * NG) * 8 + g;
+        const bool valid = n < cnt;
+        const int pair = start + (valid ? n : 0);
+        const size_t row = a.row_of_pair ? (size_t)a.row_of_pair[pair] : (size_t)pair;
+        xrow[i] = reinterpret_cast<const uint8_t*>(a.x) + row * K * (a.x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+        inv[i] = valid ? 1.0f / a.pscale[pair] : 0.0f;
+    }
+    const uint8_t* v0 = a.v + ((size_t)e * r + mt * 16 + g) * K + 16 * q;
+    const uint8_t* v1 = v0 + (size_t)8 * K;
+    for (int kc = 0; kc < K; kc += 64) {
+        const uint4 w0 = *reinterpret_cast<const uint4*>(v0 + kc);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(v1 + kc);
+        const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w}, r1[4] = {w1.x, w1.y, w1.z, w1.w};
+        uint32_t af[4][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            af[s][0] = e4m3x2_to_f16x2(r0[s] & 0xffffu);
+            af[s][1] = e4m3x2_to_f16x2(r1[s] & 0xffffu);
+            af[s][2] = e4m3x2_to_f16x2(r0[s] >> 16);
+            af[s][3] = e4m3x2_to_f16x2(r1[s] >> 16);
+        }
+#pragma unroll
+        for (int i = 0; i < NTW; ++i) {
+            if (ng + i * NG >= ntiles) continue;  // warp-uniform
+            uint32_t bf[8];                       // 16 columns kc + 16 q .. + 15 of this lane's pair, as fp16 pairs
+            if (a.x_dtype == CHRONOS_DTYPE_BF16) {
+                const uint4* src = reinterpret_cast<const uint4*>(xrow[i] + (size_t)(kc + 16 * q) * 2);
+                const uint4 u0 = src[0], u1 = src[1];
+                const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    bf[j] = pack_f16x2_sat(__uint_as_float(uu[j] << 16) * inv[i], __uint_as_float(uu[j] & 0xffff0000u) * inv[i]);
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(xrow[i] + (size_t)(kc + 16 * q) * 4);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 f = src[j];
+                    bf[2 * j] = pack_f16x2_sat(f.x * inv[i], f.y * inv[i]);
+                    bf[2 * j + 1] = pack_f16x2_sat(f.z * inv[i], f.w * inv[i]);
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < 4; ++s) mma_16816(acc[i], af[s][0], af[s][1], af[s][2], af[s][3], bf[2 * s], bf[2 * s + 1]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NTW; ++i) {
+        if (ng + i * NG >= ntiles) continue;
+        const int n0 = (ng + i * NG) * 8 + 2 * q;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + (j & 1), c = mt * 16 + g + (j >> 1) * 8;
+            if (n < cnt) a.out[(size_t)(start + n) * r + c] = f32_to_f16_sat(acc[i][j]);
+        }
+    }
+}
+
+int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st) {
+    HealInArgs a{};
+    a.v = stage == 0 ? L.v_gu : L.v_dn;
+    a.x = stage == 0 ? x : p.act;
+    a.x_dtype = stage == 0 ? x_dtype : CHRONOS_DTYPE_F32;
+    a.row_of_pair = stage == 0 ? p.pair_token : nullptr;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
+    a.out = reinterpret_cast<__half*>(stage == 0 ? p.hmid : p.hpart);
+    a.gitem_start = p.gitem_start;
+    a.gitem_cnt = p.gitem_cnt;
+    a.pair_expert = p.pair_expert;
+    a.counters = p.counters;
+    a.K = stage == 0 ? L.hidden : L.inter;
+    a.r = L.rank;
+    a.n_experts = L.n_experts;
+    const unsigned grid = (unsigned)p.max_gitems;
+    switch (L.rank / 16) {
+        case 1: healer_in_mma_kernel<1><<<grid, 256, 0, st>>>(a); break;
+        case 2: healer_in_mma_kernel<2><<<grid, 256, 0, st>>>(a); break;
+        case 4: healer_in_mma_kernel<4><<<grid, 256, 0, st>>>(a); break;
+        default: healer_in_mma_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    }
+    return check_launch("healer_in_mma");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Output side of a bank pass for 8 sorted pairs of one expert (a sub-range of a tensor-regime work item).
+// The pairs' bank-pass outputs (permuted row order, fp32) are staged in shared memory with coalesced loads, so the
+// inverse-permutation gather runs in shared memory. Then, 16 output rows at a time per warp,
+//   D[row, pair] = U[e, row, :] . h[pair, :]      (tensor cores; U rows converted e4m3 -> fp16 in registers)
+//   z[row, pair] = beta * sign * vec[pair][r_inv[row]] + g_pair * D[row, pair].
+// MODE 0 (gate_up): rows come in (gate, up) couples; act = silu(z_gate) * z_up is kept in shared memory, then per
+//   pair the power-of-two scale of the down pass, the natural-order copy for the down healer, and the down-input
+//   transform (gather + sign, FWHT128, sign) written as fp16 rows.
+// MODE 1 (down): z is the pair's layer-output term, stored in natural row order for the gate-weighted sum.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kOutThreads = 512;
+
+template <int MODE, int R16>
+__global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_layer_t L, Plan p) {
+    extern __shared__ __align__(16) float smem_f[];
+    const int item = blockIdx.x >> 4, sub = blockIdx.x & 15;
+    if (item >= p.counters[3]) return;
+    const int cnt8 = min(8, p.gitem_cnt[item] - sub * 8);
+    if (cnt8 <= 0) return;
+    const int p0 = p.gitem_start[item] + sub * 8;
+    const int e = p.pair_expert[p0];
+    const int H = L.hidden, I = L.inter;
+    constexpr int r = R16 * 16;
+    const int VL = MODE == 0 ? 2 * I : H;      // length of a staged vector
+    const int NR = MODE == 0 ? I : H;          // output rows (gate/up couples count once)
+    float* vec = smem_f;                       // [8][VL]
+    float* acts = smem_f + (size_t)8 * VL;     // MODE 0: [8][I]
+    const float* src = MODE == 0 ? p.z1 : p.y1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
+    constexpr int NW = kOutThreads / 32;
+
+    if (e >= L.n_experts) {  // shared expert: plain rows, no healer, identity keys
+        if constexpr (MODE == 1) {
+            for (int i = tid * 4; i < cnt8 * H; i += kOutThreads * 4)
+                *reinterpret_cast<float4*>(p.yt + (size_t)p0 * H + i) = *reinterpret_cast<const float4*>(src + (size_t)p0 * H + i);
+            return;
+        } else {
+            for (int n = 0; n < cnt8; ++n)
+                for (int i = tid; i < I; i += kOutThreads) {
+                    const float zg = src[(size_t)(p0 + n) * 2 * I + i], zu = src[(size_t)(p0 + n) * 2 * I + I + i];
+                    acts[n * I + i] = silu_f32(zg) * zu;
+                }
+        }
+    } else {
+        for (int i = tid * 4; i < 8 * VL; i += kOutThreads * 4) {
+            const int n = i / VL;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (n < cnt8) v = *reinterpret_cast<const float4*>(src + (size_t)p0 * VL + i);
+            *reinterpret_cast<float4*>(vec + i) = v;
+        }
+        // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per step
+        const __half* h16 = reinterpret_cast<const __half*>(MODE == 0 ? p.hmid : p.hpart);
+        uint32_t bf[R16][2];
+#pragma unroll
+        for (int s = 0; s < R16; ++s) {
+            uint2 v = make_uint2(0u, 0u);
+            if (g < cnt8) v = *reinterpret_cast<const uint2*>(h16 + (size_t)(p0 + g) * r + 4 * R16 * q + 4 * s);
+            bf[s][0] = v.x;
+            bf[s][1] = v.y;
+        }
+        const float* psc = MODE == 0 ? p.pscale_gu : p.pscale_dn;
+        const float gs0 = 2 * q < cnt8 ? psc[p0 + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt8 ? psc[p0 + 2 * q + 1] : 0.0f;
+        const float beta = (MODE == 0 ? L.gu_beta : L.dn_beta)[e];
+        const uint16_t* rout = (MODE == 0 ? L.gu_rout : L.dn_rout) + (size_t)e * VL;
+        const uint8_t* U = (MODE == 0 ? L.u_gu : L.u_dn) + (size_t)e * VL * r;
+        __syncthreads();
+        for (int jt = warp; jt < NR / 16; jt += NW) {
+            const int row_lo = jt * 16 + g, row_hi = row_lo + 8;
+            float zz[MODE == 0 ? 2 : 1][4];
+#pragma unroll
+            for (int half = 0; half < (MODE == 0 ? 2 : 1); ++half) {
+                const int base = half * I;
+                uint32_t w_lo[R16], w_hi[R16];
+                const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)(base + row_lo) * r + 4 * R16 * q);
+                const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)(base + row_hi) * r + 4 * R16 * q);
+                if constexpr (R16 % 4 == 0) {
+#pragma unroll
+                    for (int s = 0; s < R16; s += 4) {
+                        const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s), b4 = *reinterpret_cast<const uint4*>(u_hi + s);
+                        w_lo[s] = a4.x; w_lo[s + 1] = a4.y; w_lo[s + 2] = a4.z; w_lo[s + 3] = a4.w;
+                        w_hi[s] = b4.x; w_hi[s + 1] = b4.y; w_hi[s + 2] = b4.z; w_hi[s + 3] = b4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int s = 0; s < R16; ++s) { w_lo[s] = u_lo[s]; w_hi[s] = u_hi[s]; }
+                }
+                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int s = 0; s < R16; ++s)
+                    mma_16816(d, e4m3x2_to_f16x2(w_lo[s] & 0xffffu), e4m3x2_to_f16x2(w_hi[s] & 0xffffu),
+                              e4m3x2_to_f16x2(w_lo[s] >> 16), e4m3x2_to_f16x2(w_hi[s] >> 16), bf[s][0], bf[s][1]);
+                const uint32_t ro_lo = rout[base + row_lo], ro_hi = rout[base + row_hi];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {  // d[j]: row (j < 2 ? lo : hi), pair 2q + (j & 1)
+                    const uint32_t ro = j < 2 ? ro_lo : ro_hi;
+                    const float v = vec[(size_t)(2 * q + (j & 1)) * VL + (ro & 0x7fffu)];
+                    zz[half][j] = fmaf(beta, (ro >> 15) ? -v : v, ((j & 1) ? gs1 : gs0) * d[j]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = 2 * q + (j & 1), row = j < 2 ? row_lo : row_hi;
+                if (MODE == 0) acts[n * I + row] = silu_f32(zz[0][j]) * zz[MODE == 0 ? 1 : 0][j];
+                else if (n < cnt8) p.yt[(size_t)(p0 + n) * H + row] = zz[0][j];
+            }
+        }
+    }
+    if (MODE == 1) return;
+    __syncthreads();
+    // per pair: scale of the down pass, natural-order copy, down-input transform; warps 0..7 <-> pairs, two warps each
+    // when 16 warps run (the second takes the odd 128-blocks)
+    for (int n = warp % 8; n < cnt8; n += 8) {
+        const float* an = acts + (size_t)n * I;
+        float ss = 0.0f;
+        for (int i = lane * 4; i < I; i += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(an + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float gsc = pow2_scale(ss, I), gi = 1.0f / gsc;
+        const int pair = p0 + n, wsel = warp / 8;
+        if (wsel == 0 && lane == 0) p.pscale_dn[pair] = gsc;
+        for (int blk = wsel; blk < I / 128; blk += NW / 8) {
+            *reinterpret_cast<float4*>(p.act + (size_t)pair * I + blk * 128 + lane * 4) =
+                *reinterpret_cast<const float4*>(an + blk * 128 + lane * 4);
+            float v[4];
+            transform_dn_block(L, an, e, blk, lane, v);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] *= gi;
+            store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+        }
+    }
+}
+
+template <int MODE>
+static int launch_pairs8(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
+    const size_t smem = MODE == 0 ? (size_t)8 * (2 * L.inter + L.inter) * 4 : (size_t)8 * L.hidden * 4;
+    if (smem > 220 * 1024) {
+        set_error("pairs8_out: %zu bytes of shared memory needed for hidden %d / inter %d", smem, L.hidden, L.inter);
+        return CHRONOS_E_SHAPE;
+    }
+    const unsigned grid = (unsigned)p.max_gitems * 16u;
+    cudaError_t rc = cudaSuccess;
+#define CHRONOS_P8(R)                                                                                                   \
+    rc = cudaFuncSetAttribute(pairs8_out_kernel<MODE, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
+    if (rc == cudaSuccess) pairs8_out_kernel<MODE, R><<<grid, kOutThreads, smem, st>>>(L, p);
+    switch (L.rank / 16) {
+        case 1: CHRONOS_P8(1) break;
+        case 2: CHRONOS_P8(2) break;
+        case 4: CHRONOS_P8(4) break;
+        default: CHRONOS_P8(8) break;
+    }
+#undef CHRONOS_P8
+    if (rc != cudaSuccess) {
+        set_error("pairs8_out: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    return check_launch("pairs8_out");
+}
+
+bool healer_mma_fits(const chronos_layer_t& L) {
+    return L.v_dn != nullptr && (size_t)8 * 3 * L.inter * 4 <= 220 * 1024 && (size_t)8 * L.hidden * 4 <= 220 * 1024;
+}
+
+int launch_mid_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
+    if (int rc = launch_pairs8<0>(L, p, st)) return rc;
+    return launch_healer_in_mma(L, 1, nullptr, CHRONOS_DTYPE_F32, p, st);
+}
+
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pairs8<1>(L, p, st); }
+
+}  // namespace chronos

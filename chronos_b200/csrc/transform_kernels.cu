@@ -55,67 +55,6 @@ __device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int la
     }
 }
 
-// Power-of-two scale near the root mean square of a vector (1 when the vector is all zero).
-__device__ __forceinline__ float pow2_scale(float sumsq, int n) {
-    const float rms = sqrtf(sumsq / (float)n);
-    return rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
-}
-
-// One 128-block of a gate_up input: gather + sign, Walsh-Hadamard, sign (identity for the shared expert).
-__device__ __forceinline__ void transform_gu_block(const chronos_layer_t& L, const void* __restrict__ x, int x_dtype,
-                                                   int t, int e, int blk, int lane, float (&v)[4]) {
-    const int H = L.hidden;
-    if (e >= L.n_experts) {  // shared expert: plain weights, identity keys
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = ld_act(x, x_dtype, (size_t)t * H + blk * 128 + lane * 4 + i);
-        return;
-    }
-    const uint2 ce = *reinterpret_cast<const uint2*>(L.gu_cin + (size_t)e * H + blk * 128 + lane * 4);
-    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float xv = ld_act(x, x_dtype, (size_t)t * H + (ent[i] & 0x7fffu));
-        v[i] = (ent[i] >> 15) ? -xv : xv;
-    }
-    fwht128_warp(v, lane);
-    const uint32_t sw = L.gu_cs2[(size_t)e * (H / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        if ((sw >> i) & 1u) v[i] = -v[i];
-}
-
-// One 128-block of a down input from the SwiGLU outputs `act` (fp32, natural order) of the pair.
-__device__ __forceinline__ void transform_dn_block(const chronos_layer_t& L, const float* __restrict__ act, int e, int blk,
-                                                   int lane, float (&v)[4]) {
-    const int I = L.inter;
-    if (e >= L.n_experts) {
-        const float4 a = *reinterpret_cast<const float4*>(act + blk * 128 + lane * 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        return;
-    }
-    const uint2 ce = *reinterpret_cast<const uint2*>(L.dn_cin + (size_t)e * I + blk * 128 + lane * 4);
-    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float a = act[ent[i] & 0x7fffu];
-        v[i] = (ent[i] >> 15) ? -a : a;
-    }
-    fwht128_warp(v, lane);
-    const uint32_t sw = L.dn_cs2[(size_t)e * (I / 32) + blk * 4 + lane / 8] >> ((lane & 7) * 4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        if ((sw >> i) & 1u) v[i] = -v[i];
-}
-
-__device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
-    __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
-    __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t*>(&h01);
-    o.y = *reinterpret_cast<uint32_t*>(&h23);
-    *reinterpret_cast<uint2*>(dst) = o;
-}
-
 // ---------------------------------------------------------------------------------------------------------------
 // gate_up input. Transform warps: fp16 mode - one warp per (sorted pair, 128-column block) writes x_c;
 // FP4 mode - one warp per (work item, position in item, 128-column block) writes three e2m1 terms into the item's
@@ -277,7 +216,7 @@ int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Pl
     const long warps = xf + (many_pairs ? 0 : (long)p.max_pairs * L.rank);
     pre_gu_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L, x, x_dtype, p, fp4);
     if (int rc = check_launch("pre_gu")) return rc;
-    if (!many_pairs) return CHRONOS_OK;
+    if (many_pairs != 1) return CHRONOS_OK;  // 2: the caller runs the tensor-core healer kernel instead
     healer_in_tile_kernel<<<(unsigned)(((p.max_pairs + 7) / 8) * (L.rank / 8)), 256, 0, st>>>(L, x, x_dtype, p);
     return check_launch("healer_in_tile");
 }
@@ -629,6 +568,12 @@ int launch_combine_tiled(const chronos_layer_t& L, const Plan& p, const float* g
         default: down_term_kernel<8><<<grid, 256, 0, st>>>(L, p); break;
     }
     if (int rc = check_launch("down_term")) return rc;
+    return launch_combine_sum(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+}
+
+int launch_combine_sum(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                       int y_dtype, cudaStream_t st) {
+    if (n_tokens <= 0) return CHRONOS_OK;
     dim3 g2((unsigned)n_tokens, (unsigned)((L.hidden / 4 + 255) / 256));
     combine_sum_kernel<<<g2, 256, 0, st>>>(L, p, gates, with_shared && L.shared_inter > 0, y, y_dtype);
     return check_launch("combine_sum");

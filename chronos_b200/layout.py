@@ -145,6 +145,10 @@ class PackedLayer:
         s.routed_scaling = float(cfg.routed_scaling_factor)
         s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
         self._add_fp4_images()
+        if "v_dn" not in tensors and "v_dn_t" in tensors and self.device.type == "cuda":
+            # healer.v_down in its on-disk orientation [E, r, I] beside the transposed copy: the tensor-core healer
+            # kernels of the large-batch regime contract over I
+            tensors["v_dn"] = tensors["v_dn_t"].transpose(1, 2).contiguous()
         for name, _ in _lib.LayerStruct._fields_:
             if name in tensors:
                 setattr(s, name, tensors[name].data_ptr())

@@ -76,6 +76,8 @@ extern "C" {
  * of nibbles in K-major core-matrix order followed by four 512-byte scale blocks (see chronos_b200_fp4_mma_probe):
  *   gu_t u8 [n_slots, 2I/128, H/256, 18432], dn_t u8 [n_slots, H/128, I/256, 18432], sh_gu_t / sh_dn_t without the
  *   slot axis.  A pure permutation of the "s_gu.weight" + "s_gu.weight_scale" bytes; the file format is untouched.
+ * Optional: v_dn e4m3 [n_experts, r, I], "healer.v_down" exactly as on disk (kept beside its transposed copy); with it
+ *   large batches run their healer products on the tensor cores.
  */
 typedef struct chronos_layer {
     int32_t hidden, inter, n_experts, group_size, n_slots, rank, top_k;
@@ -94,6 +96,7 @@ typedef struct chronos_layer {
     const uint8_t* sh_gu_w; const uint8_t* sh_gu_s; const float* sh_gu_s2;
     const uint8_t* sh_dn_w; const uint8_t* sh_dn_s; const float* sh_dn_s2;
     const uint8_t* gu_t; const uint8_t* dn_t; const uint8_t* sh_gu_t; const uint8_t* sh_dn_t;
+    const uint8_t* v_dn;
 } chronos_layer_t;
 
 /* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated

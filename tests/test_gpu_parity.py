@@ -286,12 +286,16 @@ def test_tensor_regime_matches_oracle_and_stream_regime():
     assert _rel_l2(y_t.cpu().numpy(), y_s.cpu().numpy()) <= 2e-3
     y_t2 = layer.routed_forward(x, ids, w, regime="tensor", out_dtype=torch.float32)
     assert torch.equal(y_t, y_t2), "two runs on the same input must be bit-identical"
+    # fp32 activations at the boundary (same values): same result within the fp16 operand rounding
+    y_f = layer.routed_forward(x.float(), ids, w, regime="tensor", out_dtype=torch.float32)
+    assert _rel_l2(y_f.cpu().numpy(), ref) <= LAYER_TOL
 
 
-def test_tensor_regime_whole_layer_with_router_and_shared():
+@pytest.mark.parametrize("rank", [32, 64, 128])
+def test_tensor_regime_whole_layer_with_router_and_shared(rank):
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
-    cfg = FoldedLayerConfig(hidden=1024, inter=384, n_experts=16, group_size=4, rank=32, top_k=4)
+    cfg = FoldedLayerConfig(hidden=1024, inter=384, n_experts=16, group_size=4, rank=rank, top_k=4)
     layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, with_shared=True), register=False)
     gen = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(200, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
