@@ -109,19 +109,23 @@ static void stage_mark(int idx, cudaStream_t st) {
 
 // Regime choice when the caller leaves it open: the tensor-core pass pays off once a slot sees enough pairs to
 // fill MMA tiles; below that the bank bytes dominate and the streaming pass reads each of them exactly once.
-static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, bool fp4_laid_out) {
-    if (regime == CHRONOS_REGIME_STREAM_FP4 && !fp4_laid_out) regime = CHRONOS_REGIME_STREAM;  // no re-tiled banks / batch too large
+static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, const Plan& p) {
+    if (regime == CHRONOS_REGIME_STREAM_FP4 && !p.fp4_stream) regime = CHRONOS_REGIME_STREAM;  // no re-tiled banks / batch too large
+    if (regime == CHRONOS_REGIME_TENSOR_FP4 && !p.fp4_wide) regime = CHRONOS_REGIME_TENSOR;   // no re-tiled banks / batch too small
     if (regime != CHRONOS_REGIME_AUTO) return regime;
-    if ((long)n_tokens * L.top_k >= 16L * L.n_slots) return CHRONOS_REGIME_TENSOR;
-    return fp4_laid_out ? CHRONOS_REGIME_STREAM_FP4 : CHRONOS_REGIME_STREAM;
+    if ((long)n_tokens * L.top_k >= 16L * L.n_slots) return p.fp4_wide ? CHRONOS_REGIME_TENSOR_FP4 : CHRONOS_REGIME_TENSOR;
+    return p.fp4_stream ? CHRONOS_REGIME_STREAM_FP4 : CHRONOS_REGIME_STREAM;
 }
 
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
-                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& p, int regime,
+                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& plan, int regime,
                           bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
-    const int reg = pick_regime(L, n_tokens, regime, p.bq_gu != nullptr);
-    const bool tensor = reg == CHRONOS_REGIME_TENSOR;
-    const int fp4 = reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0;
+    const int reg = pick_regime(L, n_tokens, regime, plan);
+    const bool wide = reg == CHRONOS_REGIME_TENSOR_FP4;
+    const bool tensor = reg == CHRONOS_REGIME_TENSOR || wide;
+    const int fp4 = wide ? 2 : (reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0);
+    Plan p = plan;
+    p.gitem_pairs = wide ? kPairsPerWideItem : kPairsPerGemmItem;
     stage_mark(1, st);
     // token scales come from the router kernel when this call ran it; otherwise from a kernel of their own
     if (!have_tok_scale)
@@ -136,11 +140,13 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     if (hmma)
         if (int rc = launch_healer_in_mma(L, 0, x, x_dtype, p, st)) return rc;
     stage_mark(3, st);
-    if (int rc = tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st))) return rc;
+    if (int rc = wide ? launch_bank_fp4_wide(L, 0, p, st)
+                      : (tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st)))) return rc;
     stage_mark(4, st);
-    if (int rc = hmma ? launch_mid_mma(L, p, st) : launch_mid(L, p, fp4, st)) return rc;
+    if (int rc = hmma ? launch_mid_mma(L, p, wide ? 1 : 0, st) : launch_mid(L, p, fp4, st)) return rc;
     stage_mark(5, st);
-    if (int rc = tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st))) return rc;
+    if (int rc = wide ? launch_bank_fp4_wide(L, 1, p, st)
+                      : (tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st)))) return rc;
     stage_mark(6, st);
     int rc;
     if (hmma) {
@@ -208,7 +214,7 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
                         void* workspace, size_t workspace_bytes, int regime, void* stream) {
     if (int rc = validate_layer(layer, true)) return rc;
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
-    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_STREAM_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (n_tokens == 0) return CHRONOS_OK;
     const PlanLayout lay = plan_layout(*layer, n_tokens);
     if (!aligned16(workspace) || workspace_bytes < lay.total) {
@@ -239,7 +245,7 @@ int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, 
 
 int chronos_b200_folded_moe_prefill(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
                                     int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
-    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_TENSOR, stream);
+    return full_forward(layer, x, x_dtype, n_tokens, y, y_dtype, workspace, workspace_bytes, CHRONOS_REGIME_TENSOR_FP4, stream);
 }
 
 int chronos_b200_folded_moe_forward(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
@@ -251,7 +257,7 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
                                    const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
                                    int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
-    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_STREAM_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
+    if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
     if (n_tokens == 0) return CHRONOS_OK;
     if (!ids || !gates) { set_error("routed: ids or gates is NULL"); return CHRONOS_E_ALIGN; }
@@ -264,11 +270,12 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
     return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, false, TopkArgs{}, (cudaStream_t)stream);
 }
 
-int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out, int32_t* status,
-                               void* stream) {
+int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, int b_rows, float* d_out,
+                               int32_t* status, void* stream) {
     if (n_stages <= 0 || n_stages > 4096) { set_error("fp4_probe: n_stages (%d) out of range", n_stages); return CHRONOS_E_SHAPE; }
+    if (b_rows < 16 || b_rows > 256 || b_rows % 16) { set_error("fp4_probe: b_rows (%d) must be a multiple of 16 in 16..256", b_rows); return CHRONOS_E_SHAPE; }
     if (!aligned16(a_image) || !aligned16(b_image) || !d_out || !status) { set_error("fp4_probe: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
-    return launch_fp4_probe(a_image, b_image, n_stages, d_out, status, (cudaStream_t)stream);
+    return launch_fp4_probe(a_image, b_image, n_stages, b_rows, d_out, status, (cudaStream_t)stream);
 }
 
 int chronos_b200_set_stage_events(void** events, int n_events) {

@@ -62,6 +62,15 @@ __device__ __forceinline__ void tmem_ld32_f4(uint32_t taddr, uint32_t (&r)[32]) 
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16_f4(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Lean forms for the issuing thread (its instruction stream is the critical path of the streaming kernel): the
 // descriptors' high words are constants, the low words are a base plus a 16-byte-unit offset.
 __device__ __forceinline__ void tc_cp_sf_lo(uint32_t tmem_dst, uint32_t desc_lo) {
@@ -92,12 +101,13 @@ __device__ __forceinline__ uint32_t idesc_nvf4(int m, int n) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Operand-format probe: D[128, 32] = sum over n_stages * 256 columns of (A * scaleA) (B * scaleB)^T, one CTA.
-// a_img: n_stages x 18432 B, b_img: n_stages x 6144 B in the layouts above. Used by the parity tests to pin the
-// descriptor, scale-factor and nibble conventions against a plain dequantise-and-multiply on the CPU.
+// Operand-format probe: D[128, NB] = sum over n_stages * 256 columns of (A * scaleA) (B * scaleB)^T, one CTA.
+// a_img: n_stages x 18432 B; b_img: n_stages x (NB * 128 + 2048 * ceil(NB / 128)) B in the layouts above, NB = 32
+// (streaming regime) ... 256 rows in steps of 16. Used by the parity tests to pin the descriptor, scale-factor and
+// nibble conventions against a plain dequantise-and-multiply on the CPU.
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __restrict__ a_img,
-                                                               const uint8_t* __restrict__ b_img, int n_stages,
+                                                               const uint8_t* __restrict__ b_img, int n_stages, int nb,
                                                                float* __restrict__ d_out, int32_t* __restrict__ status) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2];  // stage landed, MMAs done
@@ -105,40 +115,43 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
     uint8_t* sa = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sb = sa + kF4AStage;  // 18432 is a multiple of 1024
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int nblk = (nb + 127) / 128;                 // 512-byte scale blocks per MMA on the B side
+    const uint32_t b_nib = (uint32_t)nb * 128u, b_stage = b_nib + 2048u * nblk;
     if (tid == 0) {
         mbar_init(smem_u32(&bars[0]), 1);
         mbar_init(smem_u32(&bars[1]), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)), "r"(64u) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)), "r"(512u) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
-    const uint32_t tmem_d = tmem, tmem_sfa = tmem + 32, tmem_sfb = tmem + 48;  // 32 + 16 + 16 columns
-    const uint32_t idesc = idesc_nvf4(kF4ARows, kF4BRows);
+    const uint32_t tmem_d = tmem, tmem_sfa = tmem + 256, tmem_sfb = tmem + 272;  // 256 + 16 + up to 32 columns
+    const uint32_t idesc = idesc_nvf4(kF4ARows, nb);
     int failed = 0;
     for (int st = 0; st < n_stages && !failed; ++st) {
         if (tid == 0) {
-            mbar_expect_tx(smem_u32(&bars[0]), kF4AStage + kF4BStage);
+            mbar_expect_tx(smem_u32(&bars[0]), kF4AStage + b_stage);
             bulk_g2s(smem_u32(sa), a_img + (size_t)st * kF4AStage, kF4AStage, smem_u32(&bars[0]));
-            bulk_g2s(smem_u32(sb), b_img + (size_t)st * kF4BStage, kF4BStage, smem_u32(&bars[0]));
+            bulk_g2s(smem_u32(sb), b_img + (size_t)st * b_stage, b_stage, smem_u32(&bars[0]));
             bool ok = mbar_wait(smem_u32(&bars[0]), st & 1);
             if (ok) {
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     tc_cp_sf(tmem_sfa + 4 * j, smem_u32(sa + kF4ANib + 512 * j));
-                    tc_cp_sf(tmem_sfb + 4 * j, smem_u32(sb + kF4BNib + 512 * j));
+                    for (int k = 0; k < nblk; ++k)
+                        tc_cp_sf(tmem_sfb + 4 * nblk * j + 4 * k, smem_u32(sb + b_nib + 512 * (nblk * j + k)));
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint64_t da = smem_desc_interleaved(smem_u32(sa + 2 * j * (kF4ARows * 16)), kF4ARows * 16);
-                    const uint64_t db = smem_desc_interleaved(smem_u32(sb + 2 * j * (kF4BRows * 16)), kF4BRows * 16);
-                    tc_mma_nvf4(tmem_d, da, db, idesc, tmem_sfa + 4 * j, tmem_sfb + 4 * j, (st > 0 || j > 0) ? 1u : 0u);
+                    const uint64_t db = smem_desc_interleaved(smem_u32(sb + 2 * j * (nb * 16)), nb * 16);
+                    tc_mma_nvf4(tmem_d, da, db, idesc, tmem_sfa + 4 * j, tmem_sfb + 4 * nblk * j, (st > 0 || j > 0) ? 1u : 0u);
                 }
                 tc_commit_f4(smem_u32(&bars[1]));
                 ok = mbar_wait(smem_u32(&bars[1]), st & 1);  // single-buffered: wait before the next stage overwrites
@@ -149,15 +162,17 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (!failed) {
-        uint32_t r[32];
-        tmem_ld32_f4(tmem_d + ((uint32_t)(warp * 32) << 16), r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        for (int c0 = 0; c0 < nb; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16_f4(tmem_d + (uint32_t)c0 + ((uint32_t)(warp * 32) << 16), r);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 32; ++i) d_out[(size_t)tid * 32 + i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 16; ++i) d_out[(size_t)tid * nb + c0 + i] = __uint_as_float(r[i]);
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64u) : "memory");
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -472,15 +487,243 @@ int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStre
     return check_launch("bank_fp4");
 }
 
-int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, float* d_out, int32_t* status,
+// ---------------------------------------------------------------------------------------------------------------
+// FP4 tensor regime (large batches): the same block-scaled MMA with both operands streamed.
+// Work item = up to 64 sorted pairs of ONE expert; its activation image per 256-column stage holds 192 rows
+// (row = term * 64 + position): 24576 B of nibbles, byte(r, c, b) at c * 3072 + r * 16 + b, then per MMA two 512-byte
+// scale blocks (rows 0-127, rows 128-191). Tile = (work item, 128 bank rows): D[128 x 192] in tensor memory, two
+// buffers, so the epilogue of a tile overlaps the MMAs of the next.
+// 10 warps: producer (per stage one 18432 B bank copy + one 28672 B activation copy into a 4-deep ring), MMA issuer
+// (per stage 12 scale-block copies to tensor memory + 4 MMAs of 128 x 192 x 64), 8 epilogue warps (TMEM lane quarter =
+// warp % 4; warps 2-5 take positions 0-31, warps 6-9 positions 32-63): sum the 3 terms, transpose through shared
+// memory, then per pair scale, r_s2 sign, FWHT128 over the bank rows, store.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kWStages = 4;
+constexpr int kWStage = kF4AStage + kWideStageBytes;  // 47104
+constexpr int kWThreads = 320;
+constexpr int kWZsFloats = 2 * 32 * 132;
+
+struct Fp4WideArgs {
+    const uint8_t* bank_t; const uint8_t* sh_bank_t;
+    const float* s2; const float* sh_s2; int sh_split;
+    const uint32_t* rs2;
+    const uint8_t* bq;         // [gitems, NS, 28672]
+    const float* pscale;
+    float* zout;               // [P, R]
+    const int32_t* item_start; const int32_t* item_cnt; const int32_t* item_slot; const int32_t* pair_expert;
+    int32_t* counters;
+    int R, K, n_slots;
+};
+
+
+__global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4WideArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t bars[2 * kWStages + 4];  // full[S], empty[S], acc_full[2], acc_empty[2]
+    __shared__ uint32_t tmem_base_s;
+    uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    float* zs = reinterpret_cast<float*>(stages + (size_t)kWStages * kWStage);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int R = a.R, RB = R / 128, NS = a.K / kF4StageK;
+    constexpr uint32_t S = kWStages;
+    const long n_tiles = (long)a.counters[3] * RB;
+    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kWStages;
+    uint64_t* acc_full = bars + 2 * kWStages;
+    uint64_t* acc_empty = bars + 2 * kWStages + 2;
+
+    if (tid == 0) {
+        for (int s = 0; s < kWStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&acc_full[b]), 1); mbar_init(smem_u32(&acc_empty[b]), 8); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)), "r"(512u) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_s;  // columns: D buffer 0 at 0, D buffer 1 at 192, scale slots from 384
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool live = true;
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
+                const int item = (int)(tile / RB), rb = (int)(tile % RB);
+                const int slot = a.item_slot[item];
+                const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
+                                      (size_t)rb * NS * kF4AStage;
+                const uint8_t* bsrc = a.bq + (size_t)item * NS * kWideStageBytes;
+                for (int st = 0; st < NS; ++st, ++it) {
+                    const uint32_t s = it % S;
+                    if (!mbar_wait(smem_u32(&empty[s]), ((it / S) & 1u) ^ 1u)) {
+                        atomicOr(a.counters + 2, kStatusFp4Timeout);
+                        live = false;
+                        break;
+                    }
+                    uint8_t* dst = stages + (size_t)s * kWStage;
+                    mbar_expect_tx(smem_u32(&full[s]), kWStage);
+                    bulk_g2s(smem_u32(dst), asrc + (size_t)st * kF4AStage, kF4AStage, smem_u32(&full[s]));
+                    bulk_g2s(smem_u32(dst + kF4AStage), bsrc + (size_t)st * kWideStageBytes, kWideStageBytes, smem_u32(&full[s]));
+                }
+            }
+            for (uint32_t back = 0; back < S && back < it; ++back) {  // copies in flight must land before the CTA exits
+                const uint32_t j = it - 1 - back;
+                if (!mbar_wait(smem_u32(&full[j % S]), (j / S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_nvf4(kF4ARows, kWideRows);
+            const uint32_t hi_word = 0x00004008u;
+            const uint32_t a_lo0 = ((smem_u32(stages) >> 4) & 0x3FFFu) | ((uint32_t)(kF4ARows * 16 >> 4) << 16);
+            const uint32_t b_lo0 = ((smem_u32(stages + kF4AStage) >> 4) & 0x3FFFu) | ((uint32_t)(kWideRows * 16 >> 4) << 16);
+            const uint32_t sfa_lo0 = (smem_u32(stages + kF4ANib) >> 4) & 0x3FFFu;
+            const uint32_t sfb_lo0 = (smem_u32(stages + kF4AStage + kWideRows * 128) >> 4) & 0x3FFFu;
+            uint32_t it = 0, tcount = 0;
+            bool live = true;
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
+                const uint32_t buf = tcount & 1u;
+                if (!mbar_wait(smem_u32(&acc_empty[buf]), ((tcount >> 1) & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t tmem_d = tmem + buf * kWideRows;
+                for (int st = 0; st < NS; ++st, ++it) {
+                    const uint32_t s = it % S;
+                    if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    // scale blocks of the stage: per MMA 4 columns for the bank rows, 8 for the 192 activation rows; two
+                    // sets of slots alternate between consecutive stages
+                    const uint32_t sf = tmem + 2 * kWideRows + (it & 1u) * 48u;
+                    const uint32_t so = s * (kWStage >> 4);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        tc_cp_sf_lo(sf + 12 * j, sfa_lo0 + so + j * 32);
+                        tc_cp_sf_lo(sf + 12 * j + 4, sfb_lo0 + so + j * 64);
+                        tc_cp_sf_lo(sf + 12 * j + 8, sfb_lo0 + so + j * 64 + 32);
+                    }
+                    const uint32_t a_lo = a_lo0 + so, b_lo = b_lo0 + so;
+                    if (st == 0) tc_mma_nvf4_lo<false>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sf, sf + 4);
+                    else tc_mma_nvf4_lo<true>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sf, sf + 4);
+#pragma unroll
+                    for (int j = 1; j < 4; ++j)
+                        tc_mma_nvf4_lo<true>(tmem_d, a_lo + j * (2 * kF4ARows * 16 >> 4), hi_word, b_lo + j * (2 * kWideRows * 16 >> 4), hi_word,
+                                             idesc, sf + 12 * j, sf + 12 * j + 4);
+                    tc_commit_f4(smem_u32(&empty[s]));
+                }
+                if (live) tc_commit_f4(smem_u32(&acc_full[buf]));
+            }
+        }
+    } else {
+        // ---------------- epilogue warps ----------------
+        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2, wq = ew & 3;
+        const int row = quarter * 32 + lane;
+        float* zsh = zs + (size_t)half * 32 * 132;
+        const int bar_id = 2 + half;
+        uint32_t tcount = 0;
+        for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
+            const int item = (int)(tile / RB), rb = (int)(tile % RB);
+            const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
+            const bool sh = slot >= a.n_slots;
+            const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
+            uint32_t sw = 0u;  // r_s2 sign bits of this lane's 4 rows (one expert per work item)
+            if (!sh) sw = a.rs2[(size_t)a.pair_expert[start] * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
+            const uint32_t buf = tcount & 1u;
+            uint32_t fail = mbar_wait(smem_u32(&acc_full[buf]), (tcount >> 1) & 1u) ? 0u : 1u;
+            asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbarrier.red.or.pred p, %2, 128, q;\nselp.u32 %0, 1, 0, p;\n}"
+                         : "=r"(fail) : "r"(fail), "r"(bar_id) : "memory");
+            if (fail) { if (lane == 0 && wq == 0) atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int n0 = half * 32;
+            if (n0 < cnt) {
+                const uint32_t tbase = tmem + buf * kWideRows + (uint32_t)n0 + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll
+                for (int ch = 0; ch < 2; ++ch) {
+                    uint32_t t0[16], t1[16], t2[16];
+                    tmem_ld16_f4(tbase + ch * 16, t0);
+                    tmem_ld16_f4(tbase + 64 + ch * 16, t1);
+                    tmem_ld16_f4(tbase + 128 + ch * 16, t2);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int n = 0; n < 16; ++n)
+                        zsh[(ch * 16 + n) * 132 + row] =
+                            __uint_as_float(t0[n]) + 0.03125f * __uint_as_float(t1[n]) + 0.0009765625f * __uint_as_float(t2[n]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));  // accumulator buffer may be overwritten
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+#pragma unroll 2
+            for (int i = 0; i < 8; ++i) {
+                const int n = n0 + wq * 8 + i;
+                if (n < cnt) {
+                    const float g = a.pscale[start + n] * s2;
+                    const float4 t4 = *reinterpret_cast<const float4*>(&zsh[(wq * 8 + i) * 132 + lane * 4]);
+                    float v[4] = {t4.x * g, t4.y * g, t4.z * g, t4.w * g};
+                    if (!sh) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            if ((sw >> q) & 1u) v[q] = -v[q];
+                        fwht128_warp(v, lane);
+                    }
+                    *reinterpret_cast<float4*>(a.zout + (size_t)(start + n) * R + rb * 128 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+                }
+            }
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
+}
+
+int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st) {
+    Fp4WideArgs a{};
+    a.K = stage == 0 ? L.hidden : L.inter;
+    a.R = stage == 0 ? 2 * L.inter : L.hidden;
+    a.bank_t = stage == 0 ? L.gu_t : L.dn_t;
+    a.sh_bank_t = stage == 0 ? L.sh_gu_t : L.sh_dn_t;
+    a.s2 = stage == 0 ? L.gu_s2 : L.dn_s2;
+    a.sh_s2 = stage == 0 ? L.sh_gu_s2 : L.sh_dn_s2;
+    a.sh_split = stage == 0 ? L.inter : 0x7fffffff;
+    a.rs2 = stage == 0 ? L.gu_rs2 : L.dn_rs2;
+    a.bq = stage == 0 ? p.bq_gu : p.bq_dn;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
+    a.zout = stage == 0 ? p.z1 : p.y1;
+    a.item_start = p.gitem_start;
+    a.item_cnt = p.gitem_cnt;
+    a.item_slot = p.gitem_slot;
+    a.pair_expert = p.pair_expert;
+    a.counters = p.counters;
+    a.n_slots = L.n_slots;
+    const size_t smem = (size_t)kWStages * kWStage + (size_t)kWZsFloats * 4 + 1024;
+    cudaError_t rc = cudaFuncSetAttribute(bank_fp4_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (rc != cudaSuccess) {
+        set_error("bank_fp4_wide: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long max_tiles = (long)p.max_gitems * (a.R / 128);
+    const int grid = (int)(max_tiles < sms ? max_tiles : sms);
+    bank_fp4_wide_kernel<<<grid, kWThreads, smem, st>>>(a);
+    return check_launch("bank_fp4_wide");
+}
+
+int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st) {
-    const size_t smem = kF4AStage + kF4BStage + 1024;
+    const size_t smem = kF4AStage + (size_t)b_rows * 128 + 2048 * ((b_rows + 127) / 128) + 1024;
     cudaError_t rc = cudaFuncSetAttribute(fp4_mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (rc != cudaSuccess) {
         set_error("fp4_probe: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
         return CHRONOS_E_LAUNCH;
     }
-    fp4_mma_probe_kernel<<<1, 128, smem, st>>>(a_img, b_img, n_stages, d_out, status);
+    fp4_mma_probe_kernel<<<1, 128, smem, st>>>(a_img, b_img, n_stages, b_rows, d_out, status);
     return check_launch("fp4_probe");
 }
 

@@ -11,7 +11,10 @@
 namespace chronos {
 
 constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
-constexpr int kPairsPerGemmItem = 128;  // pairs of ONE expert per tensor-core work item (= MMA M)
+constexpr int kPairsPerGemmItem = 128;  // pairs of ONE expert per tensor-core work item, fp16 regime (= MMA M)
+constexpr int kPairsPerWideItem = 64;   // the same in the FP4 tensor regime: 3 residual terms x 64 pairs = MMA N of 192
+constexpr int kWideRows = 3 * kPairsPerWideItem;           // rows of a wide activation stage image
+constexpr int kWideStageBytes = kWideRows * 128 + 4 * 1024;  // 24576 B of nibbles + 4 MMAs x 2 scale blocks = 28672
 constexpr int kMaxTopK = 32;
 constexpr int kMaxRank = 128;
 constexpr int kStageEvents = 8;   // stage boundaries of one forward call that can carry a profiling event
@@ -46,6 +49,9 @@ struct Plan {
     uint8_t* bq_gu;        // [max_items, H/256, 6144] FP4 activation images of the gate_up pass (NULL: not laid out)
     uint8_t* bq_dn;        // [max_items, I/256, 6144]
     float* yt;             // [P, H]   per-pair down outputs in natural row order (tensor regime only, else NULL)
+    int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
+    int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
+    int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
     int max_pairs;
     int max_items;
     int max_gitems;
@@ -55,7 +61,7 @@ struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
         off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, total;
-    int fp4, tiled;
+    int fp4, tiled, wide;
     int max_pairs, max_items, max_gitems;
 };
 
@@ -68,7 +74,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     const size_t P = T * k + (L.shared_inter > 0 ? T : 0);
     p.max_pairs = (int)P;
     p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
-    p.max_gitems = (int)(E + 1 + P / kPairsPerGemmItem + 1);
+    p.max_gitems = (int)(E + 1 + P / kPairsPerWideItem + 1);  // sized for the smaller (64-pair) work items
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
     p.off_logits = take(T * E * 4);
@@ -100,9 +106,14 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
              T * k < 16 * (size_t)L.n_slots &&
              (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
-    p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : 0);
-    p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : 0);
     p.tiled = (T * k >= 16 * (size_t)L.n_slots) ? 1 : 0;  // batch shapes the tensor regime serves
+    // the FP4 tensor regime: re-tiled banks, the tensor-core healer path (needs healer.v_down as on disk) and its
+    // shared-memory budget (8 staged vectors of 3 I or H floats)
+    const bool images = L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 &&
+                        (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr));
+    p.wide = (p.tiled && images && L.v_dn != nullptr && 8 * 3 * I * 4 <= 220 * 1024 && 8 * H * 4 <= 220 * 1024) ? 1 : 0;
+    p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (H / 256) * kWideStageBytes : 0));
+    p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (I / 256) * kWideStageBytes : 0));
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.total = o;
     return p;
@@ -136,8 +147,11 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.tok_scale = (float*)(b + l.off_tok_scale);
     p.pscale_gu = (float*)(b + l.off_pscale_gu);
     p.pscale_dn = (float*)(b + l.off_pscale_dn);
-    p.bq_gu = l.fp4 ? (uint8_t*)(b + l.off_bq_gu) : nullptr;
-    p.bq_dn = l.fp4 ? (uint8_t*)(b + l.off_bq_dn) : nullptr;
+    p.bq_gu = (l.fp4 || l.wide) ? (uint8_t*)(b + l.off_bq_gu) : nullptr;
+    p.bq_dn = (l.fp4 || l.wide) ? (uint8_t*)(b + l.off_bq_dn) : nullptr;
+    p.fp4_stream = l.fp4;
+    p.fp4_wide = l.wide;
+    p.gitem_pairs = kPairsPerGemmItem;
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
@@ -174,7 +188,8 @@ int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st
 // tensor-core healer path for batches with many pairs per expert (csrc/healer_mma.cu)
 bool healer_mma_fits(const chronos_layer_t& L);
 int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
-int launch_mid_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st);
+int launch_bank_fp4_wide(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
 int launch_combine_sum(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                        int y_dtype, cudaStream_t st);
@@ -183,7 +198,7 @@ int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, 
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_fp4(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
-int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, float* d_out, int32_t* status,
+int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st);
 int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, int dtype, int n_tokens, int hidden,
                             float eps, cudaStream_t st);
@@ -338,6 +353,57 @@ __device__ __forceinline__ __half f32_to_f16_sat(float v) {
     return __ushort_as_half(r);
 }
 // ---- mbarrier / bulk-copy primitives (every wait is bounded) ----------------------------------------------------
+// ---------------------------------------------------------------------------------------------------------------
+// FP4 quantiser: a 128-block of activations (lane l holds elements 4l..4l+3, already divided by the pair's scale) is
+// written as three residual e2m1 terms with ue4m3 scales per 16 elements into an activation stage image
+// (csrc/bank_fp4.cu describes the image): term t quantises the residual times 32^t, so the tensor-core column of
+// term t is worth 32^-t. Row of the image = t * TSTRIDE + p (p = the pair's position in its work item).
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+    uint16_t r;
+    asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\nmov.b16 %0, {t, 0};\n}" : "=h"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {
+    uint32_t h2;
+    asm("{\n.reg .b8 t, z;\nmov.b16 {t, z}, %1;\ncvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(h2) : "h"((uint16_t)byte));
+    return __half22float2(*reinterpret_cast<__half2*>(&h2));
+}
+
+template <int ROWS, int TSTRIDE>  // rows of the stage image (32 streaming, 192 tensor regime); row of term t = t * TSTRIDE + prow
+__device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int lane, uint8_t* __restrict__ stage_img,
+                                                     int half, int prow) {
+    constexpr int SFJ = 512 * ((ROWS + 127) / 128);  // scale bytes of one MMA (64 columns): a 512-byte block per 128 rows
+    float r[4] = {v[0], v[1], v[2], v[3]};
+    const int c = half * 4 + (lane >> 3), b = 2 * (lane & 7);
+    const int j = half * 2 + (lane >> 4), sidx = (lane & 15) >> 2;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        const float up = t == 0 ? 1.0f : (t == 1 ? 32.0f : 1024.0f);
+        float m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const uint32_t sc8 = f32x2_to_e4m3x2(m * up * (1.0f / 6.0f), 0.0f) & 0xffu;
+        const float sdec = e4m3_to_f32((uint8_t)sc8);
+        const float inv = sdec > 0.0f ? up / sdec : 0.0f;
+        const uint32_t b01 = f32x2_to_e2m1x2(r[0] * inv, r[1] * inv) & 0xffu;
+        const uint32_t b23 = f32x2_to_e2m1x2(r[2] * inv, r[3] * inv) & 0xffu;
+        const float2 q01 = e2m1x2_to_f32(b01), q23 = e2m1x2_to_f32(b23);
+        const float back = sdec / up;
+        r[0] = fmaf(-q01.x, back, r[0]); r[1] = fmaf(-q01.y, back, r[1]);
+        r[2] = fmaf(-q23.x, back, r[2]); r[3] = fmaf(-q23.y, back, r[3]);
+        const int n = t * TSTRIDE + prow;
+        *reinterpret_cast<uint16_t*>(stage_img + c * (ROWS * 16) + n * 16 + b) = (uint16_t)(b01 | (b23 << 8));
+        if ((lane & 3) == 0)
+            stage_img[ROWS * 128 + j * SFJ + (n >> 7) * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 + sidx] = (uint8_t)sc8;
+    }
+}
+
 // Power-of-two scale near the root mean square of a vector (1 when the vector is all zero).
 __device__ __forceinline__ float pow2_scale(float sumsq, int n) {
     const float rms = sqrtf(sumsq / (float)n);

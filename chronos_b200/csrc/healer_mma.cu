@@ -166,7 +166,7 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kOutThreads = 512;
 
-template <int MODE, int R16>
+template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
 __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
     const int item = blockIdx.x >> 4, sub = blockIdx.x & 15;
@@ -284,12 +284,17 @@ __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_laye
             transform_dn_block(L, an, e, blk, lane, v);
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[i] *= gi;
-            store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+            if (WIDE) {
+                uint8_t* img = p.bq_dn + ((size_t)item * (I / 256) + blk / 2) * kWideStageBytes;
+                quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, blk & 1, sub * 8 + n);
+            } else {
+                store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+            }
         }
     }
 }
 
-template <int MODE>
+template <int MODE, bool WIDE>
 static int launch_pairs8(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
     const size_t smem = MODE == 0 ? (size_t)8 * (2 * L.inter + L.inter) * 4 : (size_t)8 * L.hidden * 4;
     if (smem > 220 * 1024) {
@@ -299,8 +304,8 @@ static int launch_pairs8(const chronos_layer_t& L, const Plan& p, cudaStream_t s
     const unsigned grid = (unsigned)p.max_gitems * 16u;
     cudaError_t rc = cudaSuccess;
 #define CHRONOS_P8(R)                                                                                                   \
-    rc = cudaFuncSetAttribute(pairs8_out_kernel<MODE, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
-    if (rc == cudaSuccess) pairs8_out_kernel<MODE, R><<<grid, kOutThreads, smem, st>>>(L, p);
+    rc = cudaFuncSetAttribute(pairs8_out_kernel<MODE, R, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
+    if (rc == cudaSuccess) pairs8_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
     switch (L.rank / 16) {
         case 1: CHRONOS_P8(1) break;
         case 2: CHRONOS_P8(2) break;
@@ -319,11 +324,11 @@ bool healer_mma_fits(const chronos_layer_t& L) {
     return L.v_dn != nullptr && (size_t)8 * 3 * L.inter * 4 <= 220 * 1024 && (size_t)8 * L.hidden * 4 <= 220 * 1024;
 }
 
-int launch_mid_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
-    if (int rc = launch_pairs8<0>(L, p, st)) return rc;
+int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
+    if (int rc = wide ? launch_pairs8<0, true>(L, p, st) : launch_pairs8<0, false>(L, p, st)) return rc;
     return launch_healer_in_mma(L, 1, nullptr, CHRONOS_DTYPE_F32, p, st);
 }
 
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pairs8<1>(L, p, st); }
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pairs8<1, false>(L, p, st); }
 
 }  // namespace chronos

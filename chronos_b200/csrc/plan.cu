@@ -1,6 +1,6 @@
 // Batch coalescing on the device: sorts (token, expert) routing entries by expert, so that the entries of one slot
 // are contiguous, and cuts them into work items: up to 8 pairs that share one pass over the slot's bank (streaming
-// regimes) and up to 128 pairs of one expert (tensor regime).
+// regimes) and up to 128 (64 in the FP4 tensor regime) pairs of one expert.
 // Takes the role of `torch.unique` + per-expert gathers (chronos_1t/models/glm5_chronos_moe.py:508-522) and of
 // the argsort/unique_consecutive grouping (chronos_1t/models/glm53_chronos_moe.py:456-459) with no host round trip.
 // For decode-sized batches the top-k selection runs inside the same launch (one warp per token).
@@ -116,20 +116,21 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
     }
     const int n_items_total = carry;
     // tensor-core work items: expert e (bin n_experts = shared expert) owns sorted pairs [off[e], off[e+1]), cut into
-    // blocks of 128 so that one MMA tile never mixes experts
+    // blocks of gitem_pairs (128, or 64 in the FP4 tensor regime) so that one MMA tile never mixes experts
     carry = 0;
     for (int base = 0; base < n_bins; base += kPlanThreads) {
         const int e = base + tid;
         int lo = 0, hi = 0;
         if (e < n_bins) { lo = off[e]; hi = off[e + 1]; }
-        const int ni = (hi - lo + kPairsPerGemmItem - 1) / kPairsPerGemmItem;
+        const int gp = p.gitem_pairs;
+        const int ni = (hi - lo + gp - 1) / gp;
         int total;
         const int first = carry + block_exclusive_scan(ni, warp_tot, total);
         for (int q = 0; q < ni; ++q) {
             const int it = first + q;
             if (it < p.max_gitems) {
-                p.gitem_start[it] = lo + q * kPairsPerGemmItem;
-                p.gitem_cnt[it] = min(kPairsPerGemmItem, hi - lo - q * kPairsPerGemmItem);
+                p.gitem_start[it] = lo + q * gp;
+                p.gitem_cnt[it] = min(gp, hi - lo - q * gp);
                 p.gitem_slot[it] = e < n_experts ? e / group_size : n_slots;
             }
         }

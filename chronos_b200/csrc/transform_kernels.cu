@@ -7,53 +7,6 @@
 
 namespace chronos {
 
-// ---------------------------------------------------------------------------------------------------------------
-// FP4 quantiser: a 128-block of activations (lane l holds elements 4l..4l+3, already divided by the pair's scale) is
-// written as three residual e2m1 terms with ue4m3 scales per 16 elements into an activation stage image
-// (csrc/bank_fp4.cu describes the image): term t quantises the residual times 32^t, so the tensor-core column of
-// term t is worth 32^-t. Row of the image = t * 8 + p (p = the pair's position in its work item).
-// ---------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
-    uint16_t r;
-    asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\nmov.b16 %0, {t, 0};\n}" : "=h"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {
-    uint32_t h2;
-    asm("{\n.reg .b8 t, z;\nmov.b16 {t, z}, %1;\ncvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(h2) : "h"((uint16_t)byte));
-    return __half22float2(*reinterpret_cast<__half2*>(&h2));
-}
-
-__device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int lane, uint8_t* __restrict__ stage_img,
-                                                     int half, int prow) {
-    float r[4] = {v[0], v[1], v[2], v[3]};
-    const int c = half * 4 + (lane >> 3), b = 2 * (lane & 7);
-    const int j = half * 2 + (lane >> 4), sidx = (lane & 15) >> 2;
-#pragma unroll
-    for (int t = 0; t < 3; ++t) {
-        const float up = t == 0 ? 1.0f : (t == 1 ? 32.0f : 1024.0f);
-        float m = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        const uint32_t sc8 = f32x2_to_e4m3x2(m * up * (1.0f / 6.0f), 0.0f) & 0xffu;
-        const float sdec = e4m3_to_f32((uint8_t)sc8);
-        const float inv = sdec > 0.0f ? up / sdec : 0.0f;
-        const uint32_t b01 = f32x2_to_e2m1x2(r[0] * inv, r[1] * inv) & 0xffu;
-        const uint32_t b23 = f32x2_to_e2m1x2(r[2] * inv, r[3] * inv) & 0xffu;
-        const float2 q01 = e2m1x2_to_f32(b01), q23 = e2m1x2_to_f32(b23);
-        const float back = sdec / up;
-        r[0] = fmaf(-q01.x, back, r[0]); r[1] = fmaf(-q01.y, back, r[1]);
-        r[2] = fmaf(-q23.x, back, r[2]); r[3] = fmaf(-q23.y, back, r[3]);
-        const int n = t * 8 + prow;
-        *reinterpret_cast<uint16_t*>(stage_img + c * 512 + n * 16 + b) = (uint16_t)(b01 | (b23 << 8));
-        if ((lane & 3) == 0) stage_img[4096 + j * 512 + n * 16 + sidx] = (uint8_t)sc8;
-    }
-}
 
 // ---------------------------------------------------------------------------------------------------------------
 // gate_up input. Transform warps: fp16 mode - one warp per (sorted pair, 128-column block) writes x_c;
@@ -67,7 +20,8 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
     const int n_pairs = p.counters[1];
     const int H = L.hidden, E = L.n_experts, r = L.rank;
     const int nblk = H / 128;
-    const long xf_warps = fp4 ? (long)p.max_items * kPairsPerItem * nblk : (long)p.max_pairs * nblk;
+    const long xf_warps = fp4 == 2 ? (long)p.max_gitems * kPairsPerWideItem * nblk
+                                   : (fp4 ? (long)p.max_items * kPairsPerItem * nblk : (long)p.max_pairs * nblk);
     if (gw < xf_warps) {
         float v[4];
         if (!fp4) {
@@ -84,12 +38,14 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
             return;
         }
         const int blk = (int)(gw % nblk);
-        const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
+        const bool wide = fp4 == 2;  // FP4 tensor regime: work items of up to 64 pairs of one expert
+        const int per = wide ? kPairsPerWideItem : kPairsPerItem;
+        const int ip = (int)(gw / nblk), item = ip / per, pos = ip % per;
         // positions past the item's pair count are left unwritten: row n of the image only feeds accumulator column n,
         // and the bank pass never reads the columns of absent pairs
-        if (item >= p.counters[0] || pos >= p.item_cnt[item]) return;
+        if (item >= p.counters[wide ? 3 : 0] || pos >= (wide ? p.gitem_cnt : p.item_cnt)[item]) return;
         {
-            const int pair = p.item_start[item] + pos;
+            const int pair = (wide ? p.gitem_start : p.item_start)[item] + pos;
             const int t = p.pair_token[pair];
             const float g = p.tok_scale[t];
             transform_gu_block(L, x, x_dtype, t, p.pair_expert[pair], blk, lane, v);
@@ -98,8 +54,13 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
             for (int i = 0; i < 4; ++i) v[i] *= gi;
             if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
         }
-        uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * 6144;
-        quantize_block_fp4x3(v, lane, img, blk & 1, pos);
+        if (wide) {
+            uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * kWideStageBytes;
+            quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, blk & 1, pos);
+        } else {
+            uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * 6144;
+            quantize_block_fp4x3<32, 8>(v, lane, img, blk & 1, pos);
+        }
         return;
     }
     // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, rank row): the row's
@@ -210,7 +171,8 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
 
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
                   cudaStream_t st) {
-    const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
+    const long xf = fp4 == 2 ? (long)p.max_gitems * kPairsPerWideItem * (L.hidden / 128)
+                             : (fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128));
     // few pairs per expert: healer warps ride along in the same launch, one per (pair, rank row); many pairs per expert:
     // a second launch whose blocks share healer rows through L1
     const long warps = xf + (many_pairs ? 0 : (long)p.max_pairs * L.rank);
@@ -370,7 +332,7 @@ __global__ void __launch_bounds__(256) mid_xform_kernel(chronos_layer_t L, Plan 
         if (blk == 0 && lane == 0) p.pscale_dn[pair] = g;
     }
     uint8_t* img = p.bq_dn + ((size_t)item * (I / 256) + blk / 2) * 6144;
-    quantize_block_fp4x3(v, lane, img, blk & 1, pos);
+    quantize_block_fp4x3<32, 8>(v, lane, img, blk & 1, pos);
 }
 
 int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st) {

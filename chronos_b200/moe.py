@@ -34,7 +34,7 @@ class _DummyExperts(nn.Module):
 
 _DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
 _REGIMES = {"auto": _lib.REGIME_AUTO, "stream": _lib.REGIME_STREAM, "tensor": _lib.REGIME_TENSOR,
-            "stream_fp4": _lib.REGIME_STREAM_FP4}
+            "stream_fp4": _lib.REGIME_STREAM_FP4, "tensor_fp4": _lib.REGIME_TENSOR_FP4}
 
 # One scratch buffer per device, shared by every layer on it: layers of a model run one after another on the
 # worker's stream (the reference's blocks are used the same way), so they never need scratch at the same time.
@@ -168,20 +168,21 @@ class FoldedMoELayer(nn.Module):
         """Router + routed experts + shared expert (chronos_1t/models/glm53_chronos_moe.py:474-483). fp32 inputs stay
         fp32 end to end; anything else is computed from bf16 activations. `regime`: "auto" (by batch shape),
         "stream_fp4" (HBM-bound pass on the block-scaled FP4 tensor cores), "stream" (HBM-bound pass with CUDA-core
-        conversion) or "tensor" (tcgen05 grouped GEMM)."""
+        conversion), "tensor_fp4" (block-scaled FP4 grouped GEMM, both operands streamed) or "tensor" (fp16 tcgen05
+        grouped GEMM with the bank converted on the fly)."""
         orig_shape, orig_dtype = hidden_states.shape, hidden_states.dtype
         x = self._prep(hidden_states)
         n = x.shape[0]
-        if regime == "stream" and n:  # the CUDA-core streaming pass has no whole-layer entry point of its own
+        if regime in ("stream", "tensor") and n:  # regimes without a whole-layer entry point of their own
             ids, w = self.route(x)
-            y = self.routed_forward(x, ids, w, with_shared=True, out_dtype=x.dtype, regime="stream")
+            y = self.routed_forward(x, ids, w, with_shared=True, out_dtype=x.dtype, regime=regime)
             return y.to(orig_dtype).view(orig_shape)
         y = torch.empty_like(x)
         if n:
             ws = self._workspace(n)
             self._last_n = n
             fn = {"auto": _lib.lib().chronos_b200_folded_moe_forward, "stream_fp4": _lib.lib().chronos_b200_folded_moe_decode,
-                  "tensor": _lib.lib().chronos_b200_folded_moe_prefill}[regime]
+                  "tensor_fp4": _lib.lib().chronos_b200_folded_moe_prefill}[regime]
             _lib.check(fn(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, y.data_ptr(),
                           _DTYPES[x.dtype], ws.data_ptr(), ws.numel(), self._stream()))
         return y.to(orig_dtype).view(orig_shape)

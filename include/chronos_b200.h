@@ -36,6 +36,9 @@ extern "C" {
 #define CHRONOS_REGIME_TENSOR 2 /* dense: tcgen05 grouped GEMM, 128 pairs of one expert per tile */
 #define CHRONOS_REGIME_STREAM_FP4 3 /* HBM-bound, banks fed as stored (e2m1 + ue4m3) to tcgen05 block-scaled FP4 MMA;
                                        needs the re-tiled bank copies (gu_t, dn_t); falls back to STREAM without them */
+#define CHRONOS_REGIME_TENSOR_FP4 4 /* dense, block-scaled FP4 MMA with both operands streamed: 64 pairs of one expert x 3
+                                       residual FP4 terms per tile; needs the re-tiled banks and v_dn, else falls back to
+                                       CHRONOS_REGIME_TENSOR */
 
 #define CHRONOS_ROUTER_SOFTMAX_TOPK 0 /* chronos_1t/models/vllm_chronos_moe.py:310-314     */
 #define CHRONOS_ROUTER_SIGMOID_NOAUX 1 /* chronos_1t/models/glm53_chronos_moe.py:392-399    */
@@ -180,14 +183,16 @@ int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, v
                                   int hidden, float eps, void* stream);
 
 /* Operand-format probe of the block-scaled FP4 tensor-core path (tcgen05.mma kind::mxf4nvf4, e2m1 operands with a
- * ue4m3 scale per 16 elements): d_out f32 [128, 32] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns.
- * a_image: n_stages x 18432 bytes, b_image: n_stages x 6144 bytes; per stage the packed nibbles of a 128-row (resp.
- * 32-row) x 256-column tile in K-major core-matrix order - byte(r, c, b) at c * rows * 16 + r * 16 + b, c = 16-byte
- * chunk along K - followed by four 512-byte scale blocks (one per 64 columns; byte(r, s) at (r % 32) * 16 +
- * (r / 32) * 4 + s).  status: one int32 the kernel raises bits in if a bounded wait expires (clear it first).
+ * ue4m3 scale per 16 elements): d_out f32 [128, b_rows] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns;
+ * b_rows a multiple of 16 in 16..256 (32 = streaming regime, 192 = tensor regime).
+ * a_image: n_stages x 18432 bytes, b_image: n_stages x (b_rows * 128 + 2048 * ceil(b_rows / 128)) bytes; per stage the
+ * packed nibbles of a 128-row (resp. b_rows-row) x 256-column tile in K-major core-matrix order - byte(r, c, b) at
+ * c * rows * 16 + r * 16 + b, c = 16-byte chunk along K - followed, per 64 columns, by one 512-byte scale block per
+ * 128 rows (byte(r, s) of a block at (r % 32) * 16 + ((r % 128) / 32) * 4 + s).
+ * status: one int32 the kernel raises bits in if a bounded wait expires (clear it first).
  * The values are what unpack_nvfp4 (chronos_1t/converter/convert_glm53_flash_colab.py:81-89) gives with
  * weight_scale_2 = 1; the reference has no tensor-core path to compare with beyond that. */
-int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, float* d_out,
+int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, int b_rows, float* d_out,
                                int32_t* status, void* stream);
 
 /* Profiling aid for the calling thread: with n_events = 8 CUDA events (cudaEvent_t handles, timing enabled) the

@@ -289,6 +289,13 @@ def test_tensor_regime_matches_oracle_and_stream_regime():
     # fp32 activations at the boundary (same values): same result within the fp16 operand rounding
     y_f = layer.routed_forward(x.float(), ids, w, regime="tensor", out_dtype=torch.float32)
     assert _rel_l2(y_f.cpu().numpy(), ref) <= LAYER_TOL
+    # the block-scaled FP4 grouped GEMM (work items of 64 pairs x 3 residual terms) on the same batch
+    y_w = layer.routed_forward(x, ids, w, regime="tensor_fp4", out_dtype=torch.float32)
+    assert layer.device_status() == 0
+    assert _rel_l2(y_w.cpu().numpy(), ref) <= LAYER_TOL
+    assert _rel_l2(y_w.cpu().numpy(), y_t.cpu().numpy()) <= 3e-3
+    assert torch.equal(y_w, layer.routed_forward(x, ids, w, regime="tensor_fp4", out_dtype=torch.float32))
+    assert torch.equal(y_w, layer.routed_forward(x, ids, w, regime="auto", out_dtype=torch.float32))
 
 
 @pytest.mark.parametrize("rank", [32, 64, 128])
@@ -308,8 +315,27 @@ def test_tensor_regime_whole_layer_with_router_and_shared(rank):
     assert torch.equal(layer.forward_impl(x, regime="auto"), y)  # 800 pairs on 4 slots: auto picks the tensor regime
 
 
-@pytest.mark.parametrize("n_stages", [1, 3])
-def test_fp4_tensor_core_operand_format(n_stages):
+@pytest.mark.parametrize("scale", [1.0, 3e-3, 200.0])
+def test_tensor_fp4_regime_whole_layer(scale):
+    """Router + routed + shared expert through the FP4 grouped-GEMM regime, decode-like dimensions scaled down,
+    activations of very different magnitudes (the per-pair scaling keeps the e2m1 images in range)."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=1024, inter=512, n_experts=16, group_size=4, rank=64, top_k=4)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(13)
+    x = (torch.randn(330, cfg.hidden, generator=gen, device="cuda") * scale).to(torch.bfloat16)
+    y = layer.forward_impl(x, regime="tensor_fp4")
+    assert layer.device_status() == 0
+    ref, ref_ids, _ = _oracle_layer(layer, x.float().cpu().numpy())
+    assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL
+    assert torch.equal(layer.forward_impl(x, regime="auto"), y)  # 1320 pairs on 4 slots: auto = FP4 tensor regime
+    y16 = layer.forward_impl(x, regime="tensor")
+    assert _rel_l2(y16.float().cpu().numpy(), ref) <= LAYER_TOL
+
+
+@pytest.mark.parametrize("n_stages,b_rows", [(1, 32), (3, 32), (2, 192), (1, 256), (1, 64)])
+def test_fp4_tensor_core_operand_format(n_stages, b_rows):
     """tcgen05 block-scaled FP4 MMA on re-tiled operand images == dequantise-and-multiply of the same bytes."""
     from chronos_b200 import _lib
     from chronos_b200.fp4_layout import tile_matrix_fp4
@@ -317,16 +343,17 @@ def test_fp4_tensor_core_operand_format(n_stages):
     rng = np.random.default_rng(n_stages)
     k = 256 * n_stages
     a_p = rng.integers(0, 256, (128, k // 2), dtype=np.uint8)
-    b_p = rng.integers(0, 256, (32, k // 2), dtype=np.uint8)
+    b_p = rng.integers(0, 256, (b_rows, k // 2), dtype=np.uint8)
     a_s = rng.integers(0x28, 0x48, (128, k // 16), dtype=np.uint8)   # e4m3 2^-2 .. 2^1.9, non-negative
-    b_s = rng.integers(0x28, 0x48, (32, k // 16), dtype=np.uint8)
+    b_s = rng.integers(0x28, 0x48, (b_rows, k // 16), dtype=np.uint8)
     ref = O.unpack_nvfp4(a_p, a_s, 1.0).astype(np.float64) @ O.unpack_nvfp4(b_p, b_s, 1.0).astype(np.float64).T
     a_img = tile_matrix_fp4(torch.from_numpy(a_p).cuda(), torch.from_numpy(a_s).cuda(), 128)
-    b_img = tile_matrix_fp4(torch.from_numpy(b_p).cuda(), torch.from_numpy(b_s).cuda(), 32)
-    assert a_img.shape == (1, n_stages, 18432) and b_img.shape == (1, n_stages, 6144)
-    d = torch.zeros((128, 32), dtype=torch.float32, device="cuda")
+    b_img = tile_matrix_fp4(torch.from_numpy(b_p).cuda(), torch.from_numpy(b_s).cuda(), b_rows)
+    assert a_img.shape == (1, n_stages, 18432)
+    assert b_img.shape == (1, n_stages, b_rows * 128 + 2048 * ((b_rows + 127) // 128))
+    d = torch.zeros((128, b_rows), dtype=torch.float32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    _lib.check(_lib.lib().chronos_b200_fp4_mma_probe(a_img.data_ptr(), b_img.data_ptr(), n_stages, d.data_ptr(),
+    _lib.check(_lib.lib().chronos_b200_fp4_mma_probe(a_img.data_ptr(), b_img.data_ptr(), n_stages, b_rows, d.data_ptr(),
                                                     status.data_ptr(), torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
