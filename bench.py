@@ -290,6 +290,7 @@ def run_prefill(args) -> dict:
     cfg = FoldedLayerConfig(**DECODE)
     layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, device=dev, with_shared=True), register=False)
     n_tok = args.tokens
+    regime = args.regime or "tensor_fp4"
     gen = torch.Generator(device=dev).manual_seed(2)
     x = torch.randn(n_tok, cfg.hidden, generator=gen, device=dev).to(torch.bfloat16)
     # Zipf(1.1) popularity over a seeded permutation of experts: add c * log p_e to the logits by shifting the router
@@ -305,12 +306,12 @@ def run_prefill(args) -> dict:
     K, W = max(args.steps // 20, 3), 3
     st = torch.cuda.current_stream()
     for _ in range(W):
-        layer.forward_impl(x, regime="tensor")
+        layer.forward_impl(x, regime=regime)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for _ in range(K):
-        layer.forward_impl(x, regime="tensor")
+        layer.forward_impl(x, regime=regime)
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / K
@@ -324,7 +325,7 @@ def run_prefill(args) -> dict:
     torch.cuda.synchronize()
     arr = (ctypes.c_void_p * 8)(*[ev.cuda_event for ev in evs])
     _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, 8))
-    layer.forward_impl(x, regime="tensor")
+    layer.forward_impl(x, regime=regime)
     _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
     torch.cuda.synchronize()
     names = ("router", "plan", "gu_input", "gu_bank_pass", "swiglu_dn_input", "dn_bank_pass", "combine")
@@ -340,18 +341,30 @@ def run_prefill(args) -> dict:
     if pk.exists():
         peaks = json.loads(pk.read_text())
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
+    fp4 = regime == "tensor_fp4"
+    achieved = gemm_flops / gemm_s / 1e12
+    if fp4:
+        # the block-scaled pass multiplies every bank tile by 3 residual FP4 terms of the activations: the pipe does 3x the
+        # useful FLOPs; no FP4 figure is in MEASURED_PEAKS.json, so the denominator is the datasheet dense FP4 rate
+        roof = {"bound": "tensor", "kernel": "bank_fp4_wide_kernel (both passes)", "achieved": achieved, "peak": 9000.0,
+                "peak_kind": "nominal dense FP4 (datasheet; not in MEASURED_PEAKS.json)", "unit": "TFLOP/s", "frac": achieved / 9000.0,
+                "mma_issue_tflops": 3 * achieved, "mma_issue_frac": 3 * achieved / 9000.0,
+                "achieved_vs_measured_bf16": achieved / bf16_peak, "traffic": None}
+        dtype = "e2m1 x ue4m3 block-scaled operands (banks as stored, activations as 3 residual FP4 terms), fp32 accumulate in TMEM"
+    else:
+        roof = {"bound": "tensor", "kernel": "bank_gemm_kernel (both passes)", "achieved": achieved, "peak": bf16_peak,
+                "peak_kind": "of measured bf16 (operands are f16)", "unit": "TFLOP/s", "frac": achieved / bf16_peak, "traffic": None}
+        dtype = "f16 operands (NVFP4 banks converted exactly), fp32 accumulate in TMEM"
     return {
         "metric": "folded_moe_prefill_tokens_per_s", "value": n_tok / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f16 operands (NVFP4 banks converted exactly), fp32 accumulate in TMEM", "data": "synthetic",
-        "config": {"workload": "prefill_layer", "regime": "tensor", "tokens": n_tok, "hidden": cfg.hidden, "routed_experts": cfg.n_experts,
+        "dtype": dtype, "data": "synthetic",
+        "config": {"workload": "prefill_layer", "regime": regime, "tokens": n_tok, "hidden": cfg.hidden, "routed_experts": cfg.n_experts,
                    "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
                    "router_popularity": "Zipf(1.1)", "pairs_per_expert_max": int(counts.max()), "pairs_per_expert_median": float(np.median(counts)),
                    "pairs_per_expert_min": int(counts.min())},
         "useful_tflops_layer": useful / (ms * 1e-3) / 1e12,
-        "roofline": {"bound": "tensor", "kernel": "bank_gemm_kernel (both passes)", "achieved": gemm_flops / gemm_s / 1e12,
-                     "peak": bf16_peak, "peak_kind": "of measured bf16 (operands are f16; the FP4 pipe is not used in this regime)",
-                     "unit": "TFLOP/s", "frac": gemm_flops / gemm_s / 1e12 / bf16_peak, "traffic": None},
+        "roofline": roof,
         "stages_us": stage_us,
     }
 
@@ -461,6 +474,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--workload", default=None, choices=(None, "decode", "ep_stack", "prefill", "sweep"))
     ap.add_argument("--tokens", type=int, default=8192, help="tokens of the prefill workload")
+    ap.add_argument("--regime", default=None, choices=(None, "auto", "tensor", "tensor_fp4"), help="bank-pass regime of the prefill workload")
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=EP_LAYERS, help="depth of the ep_stack workload")

@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX = 0, 1
-ABI_VERSION = 4
+ABI_VERSION = 5
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4, REGIME_TENSOR_FP4 = 0, 1, 2, 3, 4
 
 
@@ -51,7 +51,7 @@ EXPORTS = {
     "chronos_b200_folded_moe_decode": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
     "chronos_b200_folded_moe_prefill": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
     "chronos_b200_folded_moe_forward": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
-    "chronos_b200_folded_moe_routed": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "chronos_b200_folded_moe_routed": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
     "chronos_b200_residual_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p]),
 }
 

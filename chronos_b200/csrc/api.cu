@@ -118,14 +118,17 @@ static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, const
 }
 
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
-                          const float* gates, int with_shared, void* y, int y_dtype, const Plan& plan, int regime,
-                          bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
+                          const float* gates, int shared_first, int shared_count, void* y, int y_dtype, const Plan& plan,
+                          int regime, bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
     const int reg = pick_regime(L, n_tokens, regime, plan);
     const bool wide = reg == CHRONOS_REGIME_TENSOR_FP4;
     const bool tensor = reg == CHRONOS_REGIME_TENSOR || wide;
     const int fp4 = wide ? 2 : (reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0);
     Plan p = plan;
     p.gitem_pairs = wide ? kPairsPerWideItem : kPairsPerGemmItem;
+    const int with_shared = (shared_count > 0 && L.shared_inter > 0) ? 1 : 0;
+    p.shared_lo = with_shared ? shared_first : 0;
+    p.shared_n = with_shared ? shared_count : 0;
     stage_mark(1, st);
     // token scales come from the router kernel when this call ran it; otherwise from a kernel of their own
     if (!have_tok_scale)
@@ -166,7 +169,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 4; }
+int chronos_b200_abi_version(void) { return 5; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -235,7 +238,7 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
     if (int rc = launch_router(*layer, x, x_dtype, n_tokens, fuse_topk ? nullptr : p.ids, p.gates, p.logits, p.tok_scale,
                                p.counters + 2, st))
         return rc;
-    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 1, y, y_dtype, p, regime, true, tk, st);
+    return routed_forward(*layer, x, x_dtype, n_tokens, p.ids, p.gates, 0, n_tokens, y, y_dtype, p, regime, true, tk, st);
 }
 
 int chronos_b200_folded_moe_decode(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, void* y,
@@ -254,20 +257,24 @@ int chronos_b200_folded_moe_forward(const chronos_layer_t* layer, const void* x,
 }
 
 int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
-                                   const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
-                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                                   const int32_t* ids, const float* gates, int shared_first, int shared_count, int regime,
+                                   void* y, int y_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
     if (regime < CHRONOS_REGIME_AUTO || regime > CHRONOS_REGIME_TENSOR_FP4) { set_error("regime %d is not a CHRONOS_REGIME_* value", regime); return CHRONOS_E_ARG; }
     if (int rc = validate_io(x, x_dtype, n_tokens, y, y_dtype)) return rc;
     if (n_tokens == 0) return CHRONOS_OK;
     if (!ids || !gates) { set_error("routed: ids or gates is NULL"); return CHRONOS_E_ALIGN; }
+    if (shared_count < 0 || shared_first < 0 || (long)shared_first + shared_count > n_tokens) {
+        set_error("routed: shared-expert token range [%d, %d + %d) does not lie inside the %d tokens", shared_first, shared_first, shared_count, n_tokens);
+        return CHRONOS_E_ARG;
+    }
     const PlanLayout lay = plan_layout(*layer, n_tokens);
     if (!aligned16(workspace) || workspace_bytes < lay.total) {
         set_error("workspace of %zu bytes is too small or misaligned (%zu needed)", workspace_bytes, lay.total);
         return CHRONOS_E_WORKSPACE;
     }
     const Plan p = plan_bind(lay, workspace);
-    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, with_shared, y, y_dtype, p, regime, false, TopkArgs{}, (cudaStream_t)stream);
+    return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, shared_first, shared_count, y, y_dtype, p, regime, false, TopkArgs{}, (cudaStream_t)stream);
 }
 
 int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, int n_stages, int b_rows, float* d_out,

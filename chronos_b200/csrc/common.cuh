@@ -52,6 +52,7 @@ struct Plan {
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
     int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
+    int shared_lo, shared_n;  // tokens shared_lo .. shared_lo + shared_n - 1 also go through the shared expert
     int max_pairs;
     int max_items;
     int max_gitems;

@@ -169,10 +169,14 @@ constexpr int kOutThreads = 512;
 template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
 __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
-    const int item = blockIdx.x >> 4, sub = blockIdx.x & 15;
-    if (item >= p.counters[3]) return;
+    // grid-stride over (8-pair sub-range, work item), work item fastest so that neighbouring CTAs get comparable work;
+    // the bound comes from the device-side item count, so a launch sized for the worst case costs nothing extra
+    const int n_items = p.counters[3];
+    for (int w = blockIdx.x; w < n_items * 16; w += gridDim.x) {
+    const int sub = w / n_items, item = w % n_items;
     const int cnt8 = min(8, p.gitem_cnt[item] - sub * 8);
-    if (cnt8 <= 0) return;
+    if (cnt8 <= 0) continue;
+    __syncthreads();  // shared memory of the previous iteration is no longer read
     const int p0 = p.gitem_start[item] + sub * 8;
     const int e = p.pair_expert[p0];
     const int H = L.hidden, I = L.inter;
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_laye
         if constexpr (MODE == 1) {
             for (int i = tid * 4; i < cnt8 * H; i += kOutThreads * 4)
                 *reinterpret_cast<float4*>(p.yt + (size_t)p0 * H + i) = *reinterpret_cast<const float4*>(src + (size_t)p0 * H + i);
-            return;
+            continue;
         } else {
             for (int n = 0; n < cnt8; ++n)
                 for (int i = tid; i < I; i += kOutThreads) {
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_laye
             }
         }
     }
-    if (MODE == 1) return;
+    if (MODE == 1) continue;
     __syncthreads();
     // per pair: scale of the down pass, natural-order copy, down-input transform; warps 0..7 <-> pairs, two warps each
     // when 16 warps run (the second takes the odd 128-blocks)
@@ -292,6 +296,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_laye
             }
         }
     }
+    }  // grid-stride loop
 }
 
 template <int MODE, bool WIDE>
@@ -301,7 +306,11 @@ static int launch_pairs8(const chronos_layer_t& L, const Plan& p, cudaStream_t s
         set_error("pairs8_out: %zu bytes of shared memory needed for hidden %d / inter %d", smem, L.hidden, L.inter);
         return CHRONOS_E_SHAPE;
     }
-    const unsigned grid = (unsigned)p.max_gitems * 16u;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned most = (unsigned)p.max_gitems * 16u;
+    const unsigned grid = most < (unsigned)sms ? most : (unsigned)sms;  // one CTA per SM fits (shared memory)
     cudaError_t rc = cudaSuccess;
 #define CHRONOS_P8(R)                                                                                                   \
     rc = cudaFuncSetAttribute(pairs8_out_kernel<MODE, R, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \

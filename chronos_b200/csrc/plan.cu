@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         const int e = ids[i];
         if (e >= 0 && e < n_experts) atomicAdd(&cnt[e], 1);
     }
-    if (tid == 0 && with_shared) cnt[n_experts] = n_tokens;
+    if (tid == 0 && with_shared) cnt[n_experts] = p.shared_n;  // tokens shared_lo .. shared_lo + shared_n - 1
     __syncthreads();
     // exclusive scan of cnt[0 .. n_bins) (n_bins <= 1025): chunks of 1024 with a carry
     int carry = 0;
@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __res
         p.pos_of[i] = pos;
     }
     if (with_shared)
-        for (int t = tid; t < n_tokens; t += kPlanThreads) {
-            p.pair_token[off[n_experts] + t] = t;
+        for (int t = tid; t < p.shared_n; t += kPlanThreads) {
+            p.pair_token[off[n_experts] + t] = p.shared_lo + t;
             p.pair_expert[off[n_experts] + t] = n_experts;
         }
     // streaming work items: slot s owns sorted pairs [off[s*K], off[(s+1)*K]); the shared expert is slot n_slots

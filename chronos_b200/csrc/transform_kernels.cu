@@ -20,8 +20,7 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
     const int n_pairs = p.counters[1];
     const int H = L.hidden, E = L.n_experts, r = L.rank;
     const int nblk = H / 128;
-    const long xf_warps = fp4 == 2 ? (long)p.max_gitems * kPairsPerWideItem * nblk
-                                   : (fp4 ? (long)p.max_items * kPairsPerItem * nblk : (long)p.max_pairs * nblk);
+    const long xf_warps = fp4 ? (long)p.max_items * kPairsPerItem * nblk : (long)p.max_pairs * nblk;
     if (gw < xf_warps) {
         float v[4];
         if (!fp4) {
@@ -38,14 +37,12 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
             return;
         }
         const int blk = (int)(gw % nblk);
-        const bool wide = fp4 == 2;  // FP4 tensor regime: work items of up to 64 pairs of one expert
-        const int per = wide ? kPairsPerWideItem : kPairsPerItem;
-        const int ip = (int)(gw / nblk), item = ip / per, pos = ip % per;
+        const int ip = (int)(gw / nblk), item = ip / kPairsPerItem, pos = ip % kPairsPerItem;
         // positions past the item's pair count are left unwritten: row n of the image only feeds accumulator column n,
         // and the bank pass never reads the columns of absent pairs
-        if (item >= p.counters[wide ? 3 : 0] || pos >= (wide ? p.gitem_cnt : p.item_cnt)[item]) return;
+        if (item >= p.counters[0] || pos >= p.item_cnt[item]) return;
         {
-            const int pair = (wide ? p.gitem_start : p.item_start)[item] + pos;
+            const int pair = p.item_start[item] + pos;
             const int t = p.pair_token[pair];
             const float g = p.tok_scale[t];
             transform_gu_block(L, x, x_dtype, t, p.pair_expert[pair], blk, lane, v);
@@ -54,13 +51,8 @@ __global__ void __launch_bounds__(256) pre_gu_kernel(chronos_layer_t L, const vo
             for (int i = 0; i < 4; ++i) v[i] *= gi;
             if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
         }
-        if (wide) {
-            uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * kWideStageBytes;
-            quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, blk & 1, pos);
-        } else {
-            uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * 6144;
-            quantize_block_fp4x3<32, 8>(v, lane, img, blk & 1, pos);
-        }
+        uint8_t* img = p.bq_gu + ((size_t)item * (H / 256) + blk / 2) * 6144;
+        quantize_block_fp4x3<32, 8>(v, lane, img, blk & 1, pos);
         return;
     }
     // healer input factor: hmid[pair, c] = sum_k V_gu[e, c, k] * x[t, k]; one warp per (pair, rank row): the row's
@@ -169,10 +161,51 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
     return check_launch("token_scale");
 }
 
+// FP4 tensor regime: one CTA per (work item of up to 64 pairs, 256-column stage) builds the stage's activation image
+// (192 rows: 3 residual terms x 64 positions) in shared memory - warp tasks = (position, 128-block) - and copies the rows
+// of present pairs out in 16-byte units, 512 consecutive bytes per warp. Grid-stride over the device-side item count.
+__global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p) {
+    __shared__ __align__(16) uint8_t img[kWideStageBytes];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int NS = L.hidden / 256, n_items = p.counters[3];
+    for (int w = blockIdx.x; w < n_items * NS; w += gridDim.x) {
+        const int item = w / NS, st = w % NS;
+        const int start = p.gitem_start[item], cnt = p.gitem_cnt[item];
+        const int e = p.pair_expert[start];
+        for (int task = warp; task < 2 * cnt; task += 16) {
+            const int pos = task >> 1, half = task & 1, blk = st * 2 + half;
+            const int pair = start + pos, t = p.pair_token[pair];
+            const float g = p.tok_scale[t];
+            float v[4];
+            transform_gu_block(L, x, x_dtype, t, e, blk, lane, v);
+            const float gi = 1.0f / g;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] *= gi;
+            if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
+            quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, half, pos);
+        }
+        __syncthreads();
+        uint4* dst = reinterpret_cast<uint4*>(p.bq_gu + (size_t)w * kWideStageBytes);
+        const uint4* src = reinterpret_cast<const uint4*>(img);
+        for (int u = tid; u < kWideRows * 8; u += 512)            // nibble rows: unit u = chunk * 192 + row
+            if (((u % kWideRows) & (kPairsPerWideItem - 1)) < cnt) dst[u] = src[u];
+        for (int u = kWideRows * 8 + tid; u < kWideStageBytes / 16; u += 512) dst[u] = src[u];  // scale blocks
+        __syncthreads();
+    }
+}
+
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
                   cudaStream_t st) {
-    const long xf = fp4 == 2 ? (long)p.max_gitems * kPairsPerWideItem * (L.hidden / 128)
-                             : (fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128));
+    if (fp4 == 2) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const long most = (long)p.max_gitems * (L.hidden / 256);
+        const unsigned grid = (unsigned)(most < 3L * sms ? most : 3L * sms);
+        pre_gu_wide_kernel<<<grid, 512, 0, st>>>(L, x, x_dtype, p);
+        return check_launch("pre_gu_wide");
+    }
+    const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
     // few pairs per expert: healer warps ride along in the same launch, one per (pair, rank row); many pairs per expert:
     // a second launch whose blocks share healer rows through L1
     const long warps = xf + (many_pairs ? 0 : (long)p.max_pairs * L.rank);
@@ -423,7 +456,8 @@ __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p,
         const int i = rb * 128 + threadIdx.x;
         float acc = 0.0f;
         for (int j = 0; j < k; ++j) acc += terms[j][threadIdx.x];
-        if (with_shared) acc += p.y1[(size_t)(p.offsets[E] + t) * H + i];
+        if (with_shared && t >= p.shared_lo && t < p.shared_lo + p.shared_n)
+            acc += p.y1[(size_t)(p.offsets[E] + t - p.shared_lo) * H + i];
         if (y_dtype == CHRONOS_DTYPE_BF16)
             reinterpret_cast<__nv_bfloat16*>(y)[(size_t)t * H + i] = __float2bfloat16(acc);
         else
@@ -504,8 +538,8 @@ __global__ void __launch_bounds__(256) combine_sum_kernel(chronos_layer_t L, Pla
         acc[0] = fmaf(g, v.x, acc[0]); acc[1] = fmaf(g, v.y, acc[1]);
         acc[2] = fmaf(g, v.z, acc[2]); acc[3] = fmaf(g, v.w, acc[3]);
     }
-    if (with_shared) {
-        const float4 v = *reinterpret_cast<const float4*>(p.yt + (size_t)(p.offsets[L.n_experts] + t) * H + i0);
+    if (with_shared && t >= p.shared_lo && t < p.shared_lo + p.shared_n) {
+        const float4 v = *reinterpret_cast<const float4*>(p.yt + (size_t)(p.offsets[L.n_experts] + t - p.shared_lo) * H + i0);
         acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
     }
     if (y_dtype == CHRONOS_DTYPE_BF16) {

@@ -9,7 +9,7 @@ Per layer, stream-ordered and free of host synchronisation:
             exchanged so that each rank sees all tokens (capacity-padded exchange: each peer gets a fixed-size
             block, so no split sizes ever travel through the host);
   compute   each rank evaluates only the routing entries whose expert it owns (the others are masked to -1 and
-            skipped on the device) plus the shared expert for its own tokens;
+            skipped on the device) plus, in the same pass, the shared expert for the tokens it is the home of;
   combine   the per-rank partial sums are reduce-scattered back to the tokens' home ranks in fp32.
 One process per GPU; `torch.distributed` (NCCL over NVLink, or gloo in CPU tests of the host logic).
 """
@@ -58,8 +58,22 @@ class ExpertParallelMoE:
         self.n_local = len(slots) * cfg_global.group_size
         self.layer = local_layer
         self.route_fn = route_fn or (lambda x: local_layer.route_global(x))
-        self.compute_routed = compute_routed or (lambda x, ids, w: local_layer.routed_forward(x, ids, w, with_shared=False, out_dtype=torch.float32))
+        # CUDA default: one pass over the gathered tokens evaluates the entries this rank owns AND the shared expert of
+        # the tokens it is the home of (their block inside the gathered order); tests substitute CPU callables and a
+        # separate shared-expert callable
+        self.fused_shared = compute_routed is None and compute_shared is None
+        self.compute_routed = compute_routed or self._routed_cuda
         self.compute_shared = compute_shared or self._shared_cuda
+        self.phase_events = None   # set to [] to record (name, start, end) CUDA events of the next forward
+
+    def _mark(self, name: str):
+        """Context manager recording a CUDA event pair around a phase when `phase_events` is a list."""
+        return _Phase(self.phase_events, name)
+
+    def _routed_cuda(self, x_all: torch.Tensor, local_ids: torch.Tensor, gates_all: torch.Tensor) -> torch.Tensor:
+        tl = x_all.shape[0] // self.world
+        rng = (self.rank * tl, tl) if self.layer.n_shared_experts else None
+        return self.layer.routed_forward(x_all, local_ids, gates_all, out_dtype=torch.float32, shared_range=rng)
 
     def _shared_cuda(self, x_local: torch.Tensor) -> Optional[torch.Tensor]:
         if self.layer.n_shared_experts == 0:
@@ -73,27 +87,51 @@ class ExpertParallelMoE:
         """x_local [Tl, H] (same Tl on every rank) -> y_local fp32 [Tl, H]."""
         tl, h = x_local.shape
         k = self.cfg.top_k
-        ids, gates = self.route_fn(x_local)
+        with self._mark("route"):
+            ids, gates = self.route_fn(x_local)
         # ---- dispatch: gather rows and routing lists of all ranks (fixed-size blocks, no host-side sizes) ----------
-        x_all = torch.empty((self.world * tl, h), dtype=x_local.dtype, device=x_local.device)
-        meta_local = torch.cat([ids.to(torch.float32), gates.to(torch.float32)], dim=1).contiguous()  # ids < 2^24: exact
-        meta_all = torch.empty((self.world * tl, 2 * k), dtype=torch.float32, device=x_local.device)
-        dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
-        dist.all_gather_into_tensor(meta_all, meta_local, group=self.group)
-        ids_all = meta_all[:, :k].to(torch.int64)
-        gates_all = meta_all[:, k:].contiguous()
-        local_ids = localize_routing(ids_all, self.first_expert, self.n_local)
+        with self._mark("dispatch"):
+            x_all = torch.empty((self.world * tl, h), dtype=x_local.dtype, device=x_local.device)
+            meta_local = torch.cat([ids.to(torch.float32), gates.to(torch.float32)], dim=1).contiguous()  # ids < 2^24: exact
+            meta_all = torch.empty((self.world * tl, 2 * k), dtype=torch.float32, device=x_local.device)
+            dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+            dist.all_gather_into_tensor(meta_all, meta_local, group=self.group)
+            ids_all = meta_all[:, :k].to(torch.int64)
+            gates_all = meta_all[:, k:].contiguous()
+            local_ids = localize_routing(ids_all, self.first_expert, self.n_local)
         # ---- compute: only entries this rank owns ---------------------------------------------------------------------
-        part = self.compute_routed(x_all, local_ids, gates_all)
+        with self._mark("routed_experts"):
+            part = self.compute_routed(x_all, local_ids, gates_all)
         # ---- combine: partial sums back to the home ranks -------------------------------------------------------------
-        y = torch.empty((tl, h), dtype=torch.float32, device=x_local.device)
-        dist.reduce_scatter_tensor(y, part.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
-        sh = self.compute_shared(x_local)
-        if sh is not None:
-            y += sh
+        with self._mark("combine"):
+            y = torch.empty((tl, h), dtype=torch.float32, device=x_local.device)
+            dist.reduce_scatter_tensor(y, part.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
+        if not self.fused_shared:
+            with self._mark("shared_expert"):
+                sh = self.compute_shared(x_local)
+                if sh is not None:
+                    y += sh
         return y
 
     __call__ = forward
+
+
+class _Phase:
+    def __init__(self, sink, name):
+        self.sink, self.name = sink, name
+
+    def __enter__(self):
+        if self.sink is not None and torch.cuda.is_available():
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e0.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.sink is not None and torch.cuda.is_available():
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self.sink.append((self.name, self.e0, e1))
+        return False
 
 
 def build_local_layer(cfg_global: FoldedLayerConfig, seed: int, world: int, rank: int, device, with_shared: bool,

@@ -64,16 +64,30 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         ms_e2e = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
         clocks = sampler.stop() if sampler else None
+        # per-layer phase split on this rank (one extra untimed step with event pairs around the phases)
+        for lay in layers:
+            lay.phase_events = []
+        h.copy_(h0)
+        stack(h)
+        torch.cuda.synchronize()
+        phase_us: dict[str, float] = {}
+        for lay in layers:
+            for name, a, b in lay.phase_events:
+                phase_us[name] = phase_us.get(name, 0.0) + 1e3 * a.elapsed_time(b) / n_layers
+            lay.phase_events = None
         step_s = float(ms.item()) * 1e-3 / K
         pairs = tokens * cfg.top_k
         bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
         healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
         useful = n_layers * (pairs * (bank_flops + healer_flops) + tokens * bank_flops)
-        launches_per_layer = 1 + 2 + 7 + 6  # rmsnorm, router (2), routed pass (plan..combine), shared pass (plan..combine)
+        # this library's kernels per layer: rmsnorm, router (2), then twice (routed entries of all tokens; shared expert of
+        # the local tokens) token_scale, plan, input transform, healer in, bank pass, SwiGLU/transform, healer in, bank
+        # pass, output term, gate-weighted sum
+        launches_per_layer = 1 + 2 + 2 * 11
         return {
             "metric": "folded_moe_ep_stack_tokens_per_s", "value": tokens / step_s, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": float(ms.item()) / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16 (NVFP4 weights exact in f16; fp32 accumulate)", "data": "synthetic",
+            "vs_baseline": None, "dtype": "e2m1 x ue4m3 block-scaled tensor-core operands (activations as 3 residual FP4 terms), fp32 accumulate", "data": "synthetic",
             "config": {"workload": "ep_stack", "layers": n_layers, "tokens_per_step": tokens, "hidden": cfg.hidden,
                        "routed_experts": cfg.n_experts, "experts_per_gpu": cfg.n_experts // world, "shared_experts": 1,
                        "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
@@ -84,6 +98,7 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
             "gpu_launches": launches_per_layer * n_layers * K,
             "clocks": clocks,
             "useful_tflops": useful / step_s / 1e12,
+            "phase_us_per_layer_rank0": {k_: round(v, 1) for k_, v in phase_us.items()},
             "device_status": status,
         }
     finally:

@@ -145,9 +145,11 @@ class FoldedMoELayer(nn.Module):
 
     @torch.no_grad()
     def routed_forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, with_shared: bool = False,
-                       out_dtype: torch.dtype | None = None, regime: str = "auto") -> torch.Tensor:
+                       out_dtype: torch.dtype | None = None, regime: str = "auto",
+                       shared_range: tuple[int, int] | None = None) -> torch.Tensor:
         """Routed experts for caller-supplied routing (chronos_1t/models/glm53_chronos_moe.py:441-472). Entries with
-        ids < 0 are skipped."""
+        ids < 0 are skipped. `with_shared` adds the shared expert for every token; `shared_range = (first, count)`
+        only for that block of tokens (an expert-parallel rank: the tokens it is the home of)."""
         x = self._prep(x)
         n = x.shape[0]
         out_dtype = out_dtype or x.dtype
@@ -158,8 +160,9 @@ class FoldedMoELayer(nn.Module):
         w = w.to(device=self.device, dtype=torch.float32).contiguous()
         ws = self._workspace(n)
         self._last_n = n
+        sh_first, sh_count = shared_range if shared_range is not None else ((0, n) if with_shared else (0, 0))
         _lib.check(_lib.lib().chronos_b200_folded_moe_routed(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, ids.data_ptr(),
-                                                           w.data_ptr(), int(with_shared), _REGIMES[regime], y.data_ptr(), _DTYPES[out_dtype],
+                                                           w.data_ptr(), int(sh_first), int(sh_count), _REGIMES[regime], y.data_ptr(), _DTYPES[out_dtype],
                                                            ws.data_ptr(), ws.numel(), self._stream()))
         return y
 

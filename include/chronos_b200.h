@@ -170,12 +170,13 @@ int chronos_b200_folded_moe_forward(const chronos_layer_t* layer, const void* x,
                                     int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Same, with routing supplied by the caller (ids < 0 are skipped; used by the expert-parallel host layer where
- * a rank only owns some slots).  ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k].  with_shared != 0 adds
- * the shared expert.  regime is a CHRONOS_REGIME_* value.
+ * a rank only owns some slots).  ids i32 [n_tokens, top_k], gates f32 [n_tokens, top_k].  Tokens shared_first ..
+ * shared_first + shared_count - 1 also get the shared expert's output added (0, n_tokens = all; count 0 = none; an
+ * expert-parallel rank passes the block of tokens it is the home of).  regime is a CHRONOS_REGIME_* value.
  * Replaces: ChronosGlm53SparseMoeBlock.routed_forward, chronos_1t/models/glm53_chronos_moe.py:441-472. */
 int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens,
-                                   const int32_t* ids, const float* gates, int with_shared, int regime, void* y,
-                                   int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+                                   const int32_t* ids, const float* gates, int shared_first, int shared_count, int regime,
+                                   void* y, int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* h[n_tokens, H] += y (when y != NULL); x_norm = h * rsqrt(mean(h^2) + eps) * (weight or 1), fp32 math.
  * Replaces: rms_norm + residual wiring, chronos_1t/models/glm53_engine.py:71-73 and :200-204. */
