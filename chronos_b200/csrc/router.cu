@@ -50,7 +50,9 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
     // the warp that owns expert tile 0 of a token tile also produces the tokens' power-of-two activation scales
     // (near rms(x[t])): it reads every x element anyway
     const bool do_scale = tok_scale != nullptr && et == 0;
-    constexpr int UN = EXP == 1 ? 8 : 4;  // 128-column steps whose loads are issued together (the FMA order per dot is unchanged)
+    // 128-column steps whose loads are issued together (the FMA order per dot is unchanged); the 8 x 8 tile already holds 64
+    // accumulators and 16 vector loads per step
+    constexpr int UN = EXP == 1 ? 8 : (TOK * EXP > 16 ? 1 : 4);
     int k = 0;
     for (; k + UN * 128 <= hidden; k += UN * 128) {
         float4 xv[UN][TOK], wv[UN][EXP];
@@ -220,6 +222,11 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
         const unsigned grid = (unsigned)((tiles + 7) / 8);
         if (bf16) router_logits_kernel<4, 1, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
         else router_logits_kernel<4, 1, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+    } else if (n_tokens >= 256) {  // large batches: 8 tokens x 8 experts per warp, 0.75 B of L1 traffic per FMA
+        const long tiles = (long)((L.n_experts + 7) / 8) * ((n_tokens + 7) / 8);
+        const unsigned grid = (unsigned)((tiles + 7) / 8);
+        if (bf16) router_logits_kernel<8, 8, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+        else router_logits_kernel<8, 8, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     } else {
         const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
         const unsigned grid = (unsigned)((tiles + 7) / 8);

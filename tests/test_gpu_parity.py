@@ -95,7 +95,7 @@ def test_router_matches_reference_and_oracle(golden):
         assert np.array_equal(layer.last_logits.cpu().numpy().view(np.uint32), fixed.view(np.uint32))
 
 
-@pytest.mark.parametrize("n_tok,dtype", [(1, "f32"), (37, "bf16"), (256, "bf16")])
+@pytest.mark.parametrize("n_tok,dtype", [(1, "f32"), (37, "bf16"), (100, "f32"), (256, "bf16"), (259, "f32")])
 def test_router_bit_exact_large(n_tok, dtype):
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
