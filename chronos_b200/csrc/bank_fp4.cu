@@ -526,7 +526,9 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
     const int R = a.R, RB = R / 128, NS = a.K / kF4StageK;
     constexpr uint32_t S = kWStages;
     const long n_tiles = (long)a.counters[3] * RB;
-    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    // tiles go round-robin over the CTAs: at any moment the CTAs work on neighbouring tiles, i.e. on the same few work items
+    // (whose activation image they share through L2) and on neighbouring row blocks of the same few banks
+    const long tile_lo = blockIdx.x, tile_hi = n_tiles, tile_step = gridDim.x;
     uint64_t* full = bars;
     uint64_t* empty = bars + kWStages;
     uint64_t* acc_full = bars + 2 * kWStages;
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
         if (lane == 0) {
             uint32_t it = 0;
             bool live = true;
-            for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
+            for (long tile = tile_lo; tile < tile_hi && live; tile += tile_step) {
                 const int item = (int)(tile / RB), rb = (int)(tile % RB);
                 const int slot = a.item_slot[item];
                 const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
             const uint32_t sfb_lo0 = (smem_u32(stages + kF4AStage + kWideRows * 128) >> 4) & 0x3FFFu;
             uint32_t it = 0, tcount = 0;
             bool live = true;
-            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
+            for (long tile = tile_lo; tile < tile_hi && live; tile += tile_step, ++tcount) {
                 const uint32_t buf = tcount & 1u;
                 if (!mbar_wait(smem_u32(&acc_empty[buf]), ((tcount >> 1) & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -624,7 +626,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
         float* zsh = zs + (size_t)half * 32 * 132;
         const int bar_id = 2 + half;
         uint32_t tcount = 0;
-        for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
+        for (long tile = tile_lo; tile < tile_hi; tile += tile_step, ++tcount) {
             const int item = (int)(tile / RB), rb = (int)(tile % RB);
             const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
             const bool sh = slot >= a.n_slots;
