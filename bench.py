@@ -36,9 +36,10 @@ N_BATCHES = 8             # distinct routed batches the timed loop rotates throu
 STREAM_CORR = 0.67        # shared share of variance of a stream's tokens -> ~30 % top-8 overlap at 288 experts
 EP_LAYERS, EP_TOKENS = 42, 4096
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up bank-pass launch at the decode workload (ncu capture
-# summarised in profiles/); None until a capture exists for the current kernel.
-GU_PASS_DRAM_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch of bank_fp4_kernel from the ncu capture summarised
+# under profiles/ (bank_fp4_kernel, decode layer): 314.98 MB + 4.02 MB for a forward over 44 banks (311.43 MB algorithmic).
+# Traffic grows in proportion to the banks a launch streams, so the line reports this ratio times the launch's bytes.
+GU_PASS_TRAFFIC_OVER_ALGORITHMIC = (314.98 + 4.02) / 311.43
 
 
 def _peaks() -> tuple[float, str]:
@@ -253,6 +254,7 @@ def run_decode(args) -> dict:
                    "streams": streams, "tokens_per_stream": TOKENS_PER_STREAM, "activations": "bf16", "router": cfg.router,
                    "l2_policy": f"each step streams {layer_bytes / 1e6:.0f} MB of banks (> 126 MB L2) and batches rotate over {N_BATCHES} routings",
                    "distinct_slots_per_step": statistics.mean(s["slots"] for s in stats),
+                   "distinct_slots_by_routing": [s["slots"] for s in stats],
                    "distinct_experts_per_step": statistics.mean(s["experts"] for s in stats),
                    "top8_overlap_within_stream": round(statistics.mean(s["overlap"] for s in stats), 3)},
         "e2e": {"value": n_tok / (ms_e2e * 1e-3 / K), "unit": "tokens/s", "h2d_bytes_per_step": n_tok * cfg.hidden * 2,
@@ -261,7 +263,7 @@ def run_decode(args) -> dict:
         "clocks": clocks,
         "roofline": {"bound": "hbm", "kernel": f"{bank_kernel} (gate_up pass)", "achieved": gu_gbs, "peak": peak,
                      "peak_kind": f"of {peak_kind}", "unit": "GB/s", "frac": gu_gbs / peak,
-                     "traffic": GU_PASS_DRAM_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": gu_bytes},
+                     "traffic": GU_PASS_TRAFFIC_OVER_ALGORITHMIC * gu_bytes, "algorithmic_bytes_per_launch": gu_bytes},
         "layer_hbm": {"algorithmic_bytes_per_step": layer_bytes, "achieved_gbs": layer_bytes / step_s / 1e9,
                       "frac_of_peak": layer_bytes / step_s / 1e9 / peak, "frac_of_8tbs": layer_bytes / step_s / 8e12},
         "stages_us": {k: round(v, 2) for k, v in stage_us.items()},
