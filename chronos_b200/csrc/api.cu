@@ -139,9 +139,11 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     // the layer carries healer.v_down in its on-disk orientation, else CUDA-core kernels that share healer rows through L1
     const int many = (tensor && p.yt != nullptr) ? 1 : 0;
     const bool hmma = many && healer_mma_fits(L);
+    if (hmma)  // the large-batch kernels read a token's row once per pair: give them x / token scale as fp16
+        if (int rc = launch_tokens_f16(x, x_dtype, n_tokens, L.hidden, p.tok_scale, p.x16, st)) return rc;
     if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, hmma ? 2 : many, st)) return rc;
     if (hmma)
-        if (int rc = launch_healer_in_mma(L, 0, x, x_dtype, p, st)) return rc;
+        if (int rc = launch_healer_in_mma(L, 0, p.x16, kDtypeF16Scaled, p, st)) return rc;
     stage_mark(3, st);
     if (int rc = wide ? launch_bank_fp4_wide(L, 0, p, st)
                       : (tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st)))) return rc;

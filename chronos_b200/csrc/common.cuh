@@ -12,6 +12,8 @@ namespace chronos {
 
 constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
 constexpr int kPairsPerGemmItem = 128;  // pairs of ONE expert per tensor-core work item, fp16 regime (= MMA M)
+constexpr int kGroupPairs = 8;          // pairs whose bank-pass outputs one CTA of the large-batch output kernel stages in shared memory
+constexpr int kDtypeF16Scaled = 2;      // internal activation source: fp16 rows already divided by the token / pair scale
 constexpr int kPairsPerWideItem = 64;   // the same in the FP4 tensor regime: 3 residual terms x 64 pairs = MMA N of 192
 constexpr int kWideRows = 3 * kPairsPerWideItem;           // rows of a wide activation stage image
 constexpr int kWideStageBytes = kWideRows * 128 + 4 * 1024;  // 24576 B of nibbles + 4 MMAs x 2 scale blocks = 28672
@@ -49,6 +51,7 @@ struct Plan {
     uint8_t* bq_gu;        // [max_items, H/256, 6144] FP4 activation images of the gate_up pass (NULL: not laid out)
     uint8_t* bq_dn;        // [max_items, I/256, 6144]
     float* yt;             // [P, H]   per-pair down outputs in natural row order (tensor regime only, else NULL)
+    __half* x16;           // [T, H]   x / token scale as fp16 (large batches only, else NULL)
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
     int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
@@ -61,7 +64,7 @@ struct Plan {
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
-        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, total;
+        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, total;
     int fp4, tiled, wide;
     int max_pairs, max_items, max_gitems;
 };
@@ -109,13 +112,14 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
              (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
     p.tiled = (T * k >= 16 * (size_t)L.n_slots) ? 1 : 0;  // batch shapes the tensor regime serves
     // the FP4 tensor regime: re-tiled banks, the tensor-core healer path (needs healer.v_down as on disk) and its
-    // shared-memory budget (8 staged vectors of 3 I or H floats)
+    // shared-memory budget (4 staged vectors of 3 I or H floats)
     const bool images = L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 &&
                         (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr));
-    p.wide = (p.tiled && images && L.v_dn != nullptr && 8 * 3 * I * 4 <= 220 * 1024 && 8 * H * 4 <= 220 * 1024) ? 1 : 0;
+    p.wide = (p.tiled && images && L.v_dn != nullptr && kGroupPairs * 3 * I * 4 <= 220 * 1024 && kGroupPairs * H * 4 <= 220 * 1024) ? 1 : 0;
     p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (H / 256) * kWideStageBytes : 0));
     p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (I / 256) * kWideStageBytes : 0));
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
+    p.off_x16 = take(p.tiled ? T * H * 2 : 0);
     p.total = o;
     return p;
 }
@@ -154,6 +158,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.fp4_wide = l.wide;
     p.gitem_pairs = kPairsPerGemmItem;
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
+    p.x16 = l.tiled ? (__half*)(b + l.off_x16) : nullptr;
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
     p.max_gitems = l.max_gitems;
@@ -181,6 +186,7 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
 int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, int reset_status,
                 const TopkArgs& tk, const Plan& p, cudaStream_t st);
 int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st);
+int launch_tokens_f16(const void* x, int x_dtype, int n_tokens, int hidden, const float* tok_scale, __half* x16, cudaStream_t st);
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
                   cudaStream_t st);
 int launch_combine_tiled(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
@@ -211,6 +217,7 @@ int check_launch(const char* what);
 // ---- device helpers ---------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ float ld_act(const void* x, int dtype, size_t i) {
+    if (dtype == kDtypeF16Scaled) return __half2float(((const __half*)x)[i]);
     return dtype == CHRONOS_DTYPE_BF16 ? __bfloat162float(((const __nv_bfloat16*)x)[i]) : ((const float*)x)[i];
 }
 

@@ -36,7 +36,8 @@ __device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
 // ---------------------------------------------------------------------------------------------------------------
 // Healer input factor of a tensor-regime work item (one expert, up to 128 sorted pairs):
 //   out[pair, c] = (1 / g_pair) * sum_k V[e, c, k] * X[row(pair), k]      c < r, stored as fp16
-// V e4m3 [E, r, K]; X rows are activations (bf16 / fp32, row = token of the pair) or SwiGLU outputs (fp32, row = pair);
+// V e4m3 [E, r, K]; X rows are activations (bf16 / fp32, or the fp16 image already divided by the token scale; row =
+// token of the pair) or SwiGLU outputs (fp32, or fp16 already divided by the pair scale; row = pair);
 // g_pair is the power-of-two scale the bank pass uses for the same pair (so the fp16 image stays in range); the
 // consumer multiplies it back. One CTA per work item; warp w owns rank rows 16 (w % MT) .. +15 and the pairs of
 // 8-pair tiles (w / MT), (w / MT) + 8 / MT, ...
@@ -75,11 +76,12 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
         const bool valid = n < cnt;
         const int pair = start + (valid ? n : 0);
         const size_t row = a.row_of_pair ? (size_t)a.row_of_pair[pair] : (size_t)pair;
-        xrow[i] = reinterpret_cast<const uint8_t*>(a.x) + row * K * (a.x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+        xrow[i] = reinterpret_cast<const uint8_t*>(a.x) + row * K * (a.x_dtype == CHRONOS_DTYPE_F32 ? 4 : 2);
         inv[i] = valid ? 1.0f / a.pscale[pair] : 0.0f;
     }
     const uint8_t* v0 = a.v + ((size_t)e * r + mt * 16 + g) * K + 16 * q;
     const uint8_t* v1 = v0 + (size_t)8 * K;
+#pragma unroll 2
     for (int kc = 0; kc < K; kc += 64) {
         const uint4 w0 = *reinterpret_cast<const uint4*>(v0 + kc);
         const uint4 w1 = *reinterpret_cast<const uint4*>(v1 + kc);
@@ -96,7 +98,12 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
         for (int i = 0; i < NTW; ++i) {
             if (ng + i * NG >= ntiles) continue;  // warp-uniform
             uint32_t bf[8];                       // 16 columns kc + 16 q .. + 15 of this lane's pair, as fp16 pairs
-            if (a.x_dtype == CHRONOS_DTYPE_BF16) {
+            if (a.x_dtype == kDtypeF16Scaled) {   // already fp16 and divided by the pair's scale: no conversion work
+                const uint4* src = reinterpret_cast<const uint4*>(xrow[i] + (size_t)(kc + 16 * q) * 2);
+                const uint4 u0 = src[0], u1 = src[1];
+                bf[0] = u0.x; bf[1] = u0.y; bf[2] = u0.z; bf[3] = u0.w;
+                bf[4] = u1.x; bf[5] = u1.y; bf[6] = u1.z; bf[7] = u1.w;
+            } else if (a.x_dtype == CHRONOS_DTYPE_BF16) {
                 const uint4* src = reinterpret_cast<const uint4*>(xrow[i] + (size_t)(kc + 16 * q) * 2);
                 const uint4 u0 = src[0], u1 = src[1];
                 const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -131,8 +138,8 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
 int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st) {
     HealInArgs a{};
     a.v = stage == 0 ? L.v_gu : L.v_dn;
-    a.x = stage == 0 ? x : p.act;
-    a.x_dtype = stage == 0 ? x_dtype : CHRONOS_DTYPE_F32;
+    a.x = x;             // stage 0: token rows; stage 1: SwiGLU outputs per pair (fp32 p.act, or fp16 rows in p.ac)
+    a.x_dtype = x_dtype;
     a.row_of_pair = stage == 0 ? p.pair_token : nullptr;
     a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
     a.out = reinterpret_cast<__half*>(stage == 0 ? p.hmid : p.hpart);
@@ -154,190 +161,231 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Output side of a bank pass for 8 sorted pairs of one expert (a sub-range of a tensor-regime work item).
-// The pairs' bank-pass outputs (permuted row order, fp32) are staged in shared memory with coalesced loads, so the
-// inverse-permutation gather runs in shared memory. Then, 16 output rows at a time per warp,
-//   D[row, pair] = U[e, row, :] . h[pair, :]      (tensor cores; U rows converted e4m3 -> fp16 in registers)
+// Output side of a bank pass for a group of kGroupPairs sorted pairs of one expert (a sub-range of a tensor-regime work
+// item). The pairs' bank-pass outputs (permuted row order, fp32) are staged in shared memory with asynchronous 16-byte
+// copies, so the inverse-permutation gather runs in shared memory. Then, 16 output rows at a time per warp,
+//   D[row, pair] = U[e, row, :] . h[pair, :]      (tensor cores; U rows converted e4m3 -> fp16 in registers; the MMA's
+//                                                  8 pair columns are half used - the healer FLOPs are negligible)
 //   z[row, pair] = beta * sign * vec[pair][r_inv[row]] + g_pair * D[row, pair].
 // MODE 0 (gate_up): rows come in (gate, up) couples; act = silu(z_gate) * z_up is kept in shared memory, then per
 //   pair the power-of-two scale of the down pass, the natural-order copy for the down healer, and the down-input
-//   transform (gather + sign, FWHT128, sign) written as fp16 rows.
+//   transform (gather + sign, FWHT128, sign) written as fp16 rows or as an FP4 image.
 // MODE 1 (down): z is the pair's layer-output term, stored in natural row order for the gate-weighted sum.
+// Small groups keep the shared-memory footprint at a third of an SM, so three CTAs overlap each other's latencies.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kOutThreads = 512;
+constexpr int kGroupsPerItem = 128 / kGroupPairs;
+
+__device__ __forceinline__ void cp_async16_g2s(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
 
 template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
-__global__ void __launch_bounds__(kOutThreads, 1) pairs8_out_kernel(chronos_layer_t L, Plan p) {
+__global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
-    // grid-stride over (8-pair sub-range, work item), work item fastest so that neighbouring CTAs get comparable work;
-    // the bound comes from the device-side item count, so a launch sized for the worst case costs nothing extra
-    const int n_items = p.counters[3];
-    for (int w = blockIdx.x; w < n_items * 16; w += gridDim.x) {
-    const int sub = w / n_items, item = w % n_items;
-    const int cnt8 = min(8, p.gitem_cnt[item] - sub * 8);
-    if (cnt8 <= 0) continue;
-    __syncthreads();  // shared memory of the previous iteration is no longer read
-    const int p0 = p.gitem_start[item] + sub * 8;
-    const int e = p.pair_expert[p0];
-    const int H = L.hidden, I = L.inter;
+    constexpr int PG = kGroupPairs, NW = kOutThreads / 32;
     constexpr int r = R16 * 16;
+    const int H = L.hidden, I = L.inter;
     const int VL = MODE == 0 ? 2 * I : H;      // length of a staged vector
     const int NR = MODE == 0 ? I : H;          // output rows (gate/up couples count once)
-    float* vec = smem_f;                       // [8][VL]
-    float* acts = smem_f + (size_t)8 * VL;     // MODE 0: [8][I]
+    float* vec = smem_f;                       // [PG][VL]
+    float* acts = smem_f + (size_t)PG * VL;    // MODE 0: [PG][I]
     const float* src = MODE == 0 ? p.z1 : p.y1;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
-    constexpr int NW = kOutThreads / 32;
-
-    if (e >= L.n_experts) {  // shared expert: plain rows, no healer, identity keys
-        if constexpr (MODE == 1) {
-            for (int i = tid * 4; i < cnt8 * H; i += kOutThreads * 4)
-                *reinterpret_cast<float4*>(p.yt + (size_t)p0 * H + i) = *reinterpret_cast<const float4*>(src + (size_t)p0 * H + i);
-            continue;
-        } else {
-            for (int n = 0; n < cnt8; ++n)
-                for (int i = tid; i < I; i += kOutThreads) {
-                    const float zg = src[(size_t)(p0 + n) * 2 * I + i], zu = src[(size_t)(p0 + n) * 2 * I + I + i];
-                    acts[n * I + i] = silu_f32(zg) * zu;
-                }
-        }
-    } else {
-        for (int i = tid * 4; i < 8 * VL; i += kOutThreads * 4) {
-            const int n = i / VL;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (n < cnt8) v = *reinterpret_cast<const float4*>(src + (size_t)p0 * VL + i);
-            *reinterpret_cast<float4*>(vec + i) = v;
-        }
-        // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per step
-        const __half* h16 = reinterpret_cast<const __half*>(MODE == 0 ? p.hmid : p.hpart);
-        uint32_t bf[R16][2];
-#pragma unroll
-        for (int s = 0; s < R16; ++s) {
-            uint2 v = make_uint2(0u, 0u);
-            if (g < cnt8) v = *reinterpret_cast<const uint2*>(h16 + (size_t)(p0 + g) * r + 4 * R16 * q + 4 * s);
-            bf[s][0] = v.x;
-            bf[s][1] = v.y;
-        }
-        const float* psc = MODE == 0 ? p.pscale_gu : p.pscale_dn;
-        const float gs0 = 2 * q < cnt8 ? psc[p0 + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt8 ? psc[p0 + 2 * q + 1] : 0.0f;
-        const float beta = (MODE == 0 ? L.gu_beta : L.dn_beta)[e];
-        const uint16_t* rout = (MODE == 0 ? L.gu_rout : L.dn_rout) + (size_t)e * VL;
-        const uint8_t* U = (MODE == 0 ? L.u_gu : L.u_dn) + (size_t)e * VL * r;
-        __syncthreads();
-        for (int jt = warp; jt < NR / 16; jt += NW) {
-            const int row_lo = jt * 16 + g, row_hi = row_lo + 8;
-            float zz[MODE == 0 ? 2 : 1][4];
-#pragma unroll
-            for (int half = 0; half < (MODE == 0 ? 2 : 1); ++half) {
-                const int base = half * I;
-                uint32_t w_lo[R16], w_hi[R16];
-                const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)(base + row_lo) * r + 4 * R16 * q);
-                const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)(base + row_hi) * r + 4 * R16 * q);
-                if constexpr (R16 % 4 == 0) {
-#pragma unroll
-                    for (int s = 0; s < R16; s += 4) {
-                        const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s), b4 = *reinterpret_cast<const uint4*>(u_hi + s);
-                        w_lo[s] = a4.x; w_lo[s + 1] = a4.y; w_lo[s + 2] = a4.z; w_lo[s + 3] = a4.w;
-                        w_hi[s] = b4.x; w_hi[s + 1] = b4.y; w_hi[s + 2] = b4.z; w_hi[s + 3] = b4.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int s = 0; s < R16; ++s) { w_lo[s] = u_lo[s]; w_hi[s] = u_hi[s]; }
-                }
-                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int s = 0; s < R16; ++s)
-                    mma_16816(d, e4m3x2_to_f16x2(w_lo[s] & 0xffffu), e4m3x2_to_f16x2(w_hi[s] & 0xffffu),
-                              e4m3x2_to_f16x2(w_lo[s] >> 16), e4m3x2_to_f16x2(w_hi[s] >> 16), bf[s][0], bf[s][1]);
-                const uint32_t ro_lo = rout[base + row_lo], ro_hi = rout[base + row_hi];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {  // d[j]: row (j < 2 ? lo : hi), pair 2q + (j & 1)
-                    const uint32_t ro = j < 2 ? ro_lo : ro_hi;
-                    const float v = vec[(size_t)(2 * q + (j & 1)) * VL + (ro & 0x7fffu)];
-                    zz[half][j] = fmaf(beta, (ro >> 15) ? -v : v, ((j & 1) ? gs1 : gs0) * d[j]);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int n = 2 * q + (j & 1), row = j < 2 ? row_lo : row_hi;
-                if (MODE == 0) acts[n * I + row] = silu_f32(zz[0][j]) * zz[MODE == 0 ? 1 : 0][j];
-                else if (n < cnt8) p.yt[(size_t)(p0 + n) * H + row] = zz[0][j];
-            }
-        }
-    }
-    if (MODE == 1) continue;
-    __syncthreads();
-    // per pair: scale of the down pass, natural-order copy, down-input transform; warps 0..7 <-> pairs, two warps each
-    // when 16 warps run (the second takes the odd 128-blocks)
-    for (int n = warp % 8; n < cnt8; n += 8) {
-        const float* an = acts + (size_t)n * I;
-        float ss = 0.0f;
-        for (int i = lane * 4; i < I; i += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(an + i);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        const float gsc = pow2_scale(ss, I), gi = 1.0f / gsc;
-        const int pair = p0 + n, wsel = warp / 8;
-        if (wsel == 0 && lane == 0) p.pscale_dn[pair] = gsc;
-        for (int blk = wsel; blk < I / 128; blk += NW / 8) {
-            *reinterpret_cast<float4*>(p.act + (size_t)pair * I + blk * 128 + lane * 4) =
-                *reinterpret_cast<const float4*>(an + blk * 128 + lane * 4);
-            float v[4];
-            transform_dn_block(L, an, e, blk, lane, v);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] *= gi;
-            if (WIDE) {
-                uint8_t* img = p.bq_dn + ((size_t)item * (I / 256) + blk / 2) * kWideStageBytes;
-                quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, blk & 1, sub * 8 + n);
+    // grid-stride over (group, work item), work item fastest so that neighbouring CTAs get comparable work; the bound
+    // comes from the device-side item count, so a launch sized for the worst case costs nothing extra
+    const int n_items = p.counters[3];
+    for (int w = blockIdx.x; w < n_items * kGroupsPerItem; w += gridDim.x) {
+        const int sub = w / n_items, item = w % n_items;
+        const int cnt = min(PG, p.gitem_cnt[item] - sub * PG);
+        if (cnt <= 0) continue;
+        __syncthreads();  // shared memory of the previous iteration is no longer read
+        const int p0 = p.gitem_start[item] + sub * PG;
+        const int e = p.pair_expert[p0];
+        if (e >= L.n_experts) {  // shared expert: plain rows, no healer, identity keys
+            if constexpr (MODE == 1) {
+                for (int i = tid * 4; i < cnt * H; i += kOutThreads * 4)
+                    *reinterpret_cast<float4*>(p.yt + (size_t)p0 * H + i) = *reinterpret_cast<const float4*>(src + (size_t)p0 * H + i);
+                continue;
             } else {
-                store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+                for (int n = 0; n < cnt; ++n)
+                    for (int i = tid; i < I; i += kOutThreads) {
+                        const float zg = src[(size_t)(p0 + n) * 2 * I + i], zu = src[(size_t)(p0 + n) * 2 * I + I + i];
+                        acts[n * I + i] = silu_f32(zg) * zu;
+                    }
+            }
+        } else {
+            for (int i = tid * 4; i < PG * VL; i += kOutThreads * 4) {
+                if (i / VL < cnt) cp_async16_g2s(vec + i, src + (size_t)p0 * VL + i);
+                else *reinterpret_cast<float4*>(vec + i) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per step (columns g >= cnt are zero)
+            const __half* h16 = reinterpret_cast<const __half*>(MODE == 0 ? p.hmid : p.hpart);
+            uint32_t bf[R16][2];
+#pragma unroll
+            for (int s = 0; s < R16; ++s) {
+                uint2 v = make_uint2(0u, 0u);
+                if (g < cnt) v = *reinterpret_cast<const uint2*>(h16 + (size_t)(p0 + g) * r + 4 * R16 * q + 4 * s);
+                bf[s][0] = v.x;
+                bf[s][1] = v.y;
+            }
+            const float* psc = MODE == 0 ? p.pscale_gu : p.pscale_dn;
+            const float gs0 = 2 * q < cnt ? psc[p0 + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt ? psc[p0 + 2 * q + 1] : 0.0f;
+            const float beta = (MODE == 0 ? L.gu_beta : L.dn_beta)[e];
+            const uint16_t* rout = (MODE == 0 ? L.gu_rout : L.dn_rout) + (size_t)e * VL;
+            const uint8_t* U = (MODE == 0 ? L.u_gu : L.u_dn) + (size_t)e * VL * r;
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            __syncthreads();
+            // software pipeline over the 16-row tiles of this warp: the healer rows and permutation entries of the next
+            // tile are requested before the current tile is multiplied (each request is a full L2 round trip)
+            constexpr int NH = MODE == 0 ? 2 : 1;
+            uint32_t w_lo[NH][R16], w_hi[NH][R16], ro_lo[NH], ro_hi[NH];
+            auto fetch = [&](int jt, uint32_t (&wl)[NH][R16], uint32_t (&wh)[NH][R16], uint32_t (&rl)[NH], uint32_t (&rh)[NH]) {
+#pragma unroll
+                for (int half = 0; half < NH; ++half) {
+                    const int row_lo = half * I + jt * 16 + g, row_hi = row_lo + 8;
+                    const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)row_lo * r + 4 * R16 * q);
+                    const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)row_hi * r + 4 * R16 * q);
+                    if constexpr (R16 % 4 == 0) {
+#pragma unroll
+                        for (int s = 0; s < R16; s += 4) {
+                            const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s), b4 = *reinterpret_cast<const uint4*>(u_hi + s);
+                            wl[half][s] = a4.x; wl[half][s + 1] = a4.y; wl[half][s + 2] = a4.z; wl[half][s + 3] = a4.w;
+                            wh[half][s] = b4.x; wh[half][s + 1] = b4.y; wh[half][s + 2] = b4.z; wh[half][s + 3] = b4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int s = 0; s < R16; ++s) { wl[half][s] = u_lo[s]; wh[half][s] = u_hi[s]; }
+                    }
+                    rl[half] = rout[row_lo];
+                    rh[half] = rout[row_hi];
+                }
+            };
+            if (warp < NR / 16) fetch(warp, w_lo, w_hi, ro_lo, ro_hi);
+            for (int jt = warp; jt < NR / 16; jt += NW) {
+                uint32_t n_lo[NH][R16], n_hi[NH][R16], nr_lo[NH], nr_hi[NH];
+                const bool more = jt + NW < NR / 16;
+                if (more) fetch(jt + NW, n_lo, n_hi, nr_lo, nr_hi);
+                const int row_lo = jt * 16 + g, row_hi = row_lo + 8;
+                float zz[NH][4];
+#pragma unroll
+                for (int half = 0; half < NH; ++half) {
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int s = 0; s < R16; ++s)
+                        mma_16816(d, e4m3x2_to_f16x2(w_lo[half][s] & 0xffffu), e4m3x2_to_f16x2(w_hi[half][s] & 0xffffu),
+                                  e4m3x2_to_f16x2(w_lo[half][s] >> 16), e4m3x2_to_f16x2(w_hi[half][s] >> 16), bf[s][0], bf[s][1]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // d[j]: row (j < 2 ? lo : hi), pair 2q + (j & 1)
+                        const uint32_t ro = j < 2 ? ro_lo[half] : ro_hi[half];
+                        const int n = 2 * q + (j & 1);
+                        float v = 0.0f;
+                        if (n < PG) v = vec[(size_t)n * VL + (ro & 0x7fffu)];
+                        zz[half][j] = fmaf(beta, (ro >> 15) ? -v : v, ((j & 1) ? gs1 : gs0) * d[j]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int n = 2 * q + (j & 1), row = j < 2 ? row_lo : row_hi;
+                    if (MODE == 0) {
+                        if (n < PG) acts[n * I + row] = silu_f32(zz[0][j]) * zz[NH - 1][j];
+                    } else if (n < cnt) {
+                        p.yt[(size_t)(p0 + n) * H + row] = zz[0][j];
+                    }
+                }
+                if (more) {
+#pragma unroll
+                    for (int half = 0; half < NH; ++half) {
+#pragma unroll
+                        for (int s = 0; s < R16; ++s) { w_lo[half][s] = n_lo[half][s]; w_hi[half][s] = n_hi[half][s]; }
+                        ro_lo[half] = nr_lo[half];
+                        ro_hi[half] = nr_hi[half];
+                    }
+                }
+            }
+        }
+        if (MODE == 1) continue;
+        __syncthreads();
+        // per pair: scale of the down pass, natural-order copy, down-input transform; warp w serves pair w % PG and the
+        // 128-blocks w / PG, w / PG + NW / PG, ...
+        for (int n = warp % PG; n < cnt; n += PG) {
+            const float* an = acts + (size_t)n * I;
+            float ss = 0.0f;
+            for (int i = lane * 4; i < I; i += 128) {
+                const float4 v = *reinterpret_cast<const float4*>(an + i);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float gsc = pow2_scale(ss, I), gi = 1.0f / gsc;
+            const int pair = p0 + n, wsel = warp / PG;
+            if (wsel == 0 && lane == 0) p.pscale_dn[pair] = gsc;
+            for (int blk = wsel; blk < I / 128; blk += NW / PG) {
+                {   // natural-order copy for the down healer: fp16 / pair scale (FP4 regime; p.ac is free there) or fp32
+                    const float4 a4 = *reinterpret_cast<const float4*>(an + blk * 128 + lane * 4);
+                    if (WIDE) {
+                        const float s4[4] = {a4.x * gi, a4.y * gi, a4.z * gi, a4.w * gi};
+                        store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, s4);
+                    } else {
+                        *reinterpret_cast<float4*>(p.act + (size_t)pair * I + blk * 128 + lane * 4) = a4;
+                    }
+                }
+                float v[4];
+                transform_dn_block(L, an, e, blk, lane, v);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= gi;
+                if (WIDE) {
+                    uint8_t* img = p.bq_dn + ((size_t)item * (I / 256) + blk / 2) * kWideStageBytes;
+                    quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, blk & 1, sub * PG + n);
+                } else {
+                    store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, v);
+                }
             }
         }
     }
-    }  // grid-stride loop
 }
 
 template <int MODE, bool WIDE>
-static int launch_pairs8(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
-    const size_t smem = MODE == 0 ? (size_t)8 * (2 * L.inter + L.inter) * 4 : (size_t)8 * L.hidden * 4;
+static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
+    const size_t smem = MODE == 0 ? (size_t)kGroupPairs * (2 * L.inter + L.inter) * 4 : (size_t)kGroupPairs * L.hidden * 4;
     if (smem > 220 * 1024) {
-        set_error("pairs8_out: %zu bytes of shared memory needed for hidden %d / inter %d", smem, L.hidden, L.inter);
+        set_error("pair_group_out: %zu bytes of shared memory needed for hidden %d / inter %d", smem, L.hidden, L.inter);
         return CHRONOS_E_SHAPE;
     }
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const unsigned most = (unsigned)p.max_gitems * 16u;
-    const unsigned grid = most < (unsigned)sms ? most : (unsigned)sms;  // one CTA per SM fits (shared memory)
+    const unsigned most = (unsigned)p.max_gitems * (unsigned)kGroupsPerItem;
+    const unsigned resident = (unsigned)sms * (smem * 3 <= 225 * 1024 ? 3u : (smem * 2 <= 225 * 1024 ? 2u : 1u));
+    const unsigned grid = most < resident ? most : resident;
     cudaError_t rc = cudaSuccess;
-#define CHRONOS_P8(R)                                                                                                   \
-    rc = cudaFuncSetAttribute(pairs8_out_kernel<MODE, R, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
-    if (rc == cudaSuccess) pairs8_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
+#define CHRONOS_PG(R)                                                                                                   \
+    rc = cudaFuncSetAttribute(pair_group_out_kernel<MODE, R, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (rc == cudaSuccess) pair_group_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
     switch (L.rank / 16) {
-        case 1: CHRONOS_P8(1) break;
-        case 2: CHRONOS_P8(2) break;
-        case 4: CHRONOS_P8(4) break;
-        default: CHRONOS_P8(8) break;
+        case 1: CHRONOS_PG(1) break;
+        case 2: CHRONOS_PG(2) break;
+        case 4: CHRONOS_PG(4) break;
+        default: CHRONOS_PG(8) break;
     }
-#undef CHRONOS_P8
+#undef CHRONOS_PG
     if (rc != cudaSuccess) {
-        set_error("pairs8_out: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
+        set_error("pair_group_out: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
         return CHRONOS_E_LAUNCH;
     }
-    return check_launch("pairs8_out");
+    return check_launch("pair_group_out");
 }
 
 bool healer_mma_fits(const chronos_layer_t& L) {
-    return L.v_dn != nullptr && (size_t)8 * 3 * L.inter * 4 <= 220 * 1024 && (size_t)8 * L.hidden * 4 <= 220 * 1024;
+    return L.v_dn != nullptr && (size_t)kGroupPairs * 3 * L.inter * 4 <= 220 * 1024 && (size_t)kGroupPairs * L.hidden * 4 <= 220 * 1024;
 }
 
 int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
-    if (int rc = wide ? launch_pairs8<0, true>(L, p, st) : launch_pairs8<0, false>(L, p, st)) return rc;
-    return launch_healer_in_mma(L, 1, nullptr, CHRONOS_DTYPE_F32, p, st);
+    if (int rc = wide ? launch_pair_groups<0, true>(L, p, st) : launch_pair_groups<0, false>(L, p, st)) return rc;
+    return wide ? launch_healer_in_mma(L, 1, p.ac, kDtypeF16Scaled, p, st) : launch_healer_in_mma(L, 1, p.act, CHRONOS_DTYPE_F32, p, st);
 }
 
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pairs8<1, false>(L, p, st); }
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pair_groups<1, false>(L, p, st); }
 
 }  // namespace chronos

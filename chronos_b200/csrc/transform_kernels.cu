@@ -155,6 +155,24 @@ __global__ void __launch_bounds__(256) token_scale_kernel(const void* __restrict
     if (lane == 0) tok_scale[t] = pow2_scale(ss, hidden);
 }
 
+// x / token scale as fp16 rows: the activation source of the large-batch kernels (read many times per token).
+__global__ void __launch_bounds__(256) tokens_f16_kernel(const void* __restrict__ x, int x_dtype, long n_elems, int hidden,
+                                                         const float* __restrict__ tok_scale, __half* __restrict__ x16) {
+    const long i = ((long)blockIdx.x * 256 + threadIdx.x) * 4;
+    if (i >= n_elems) return;
+    const float gi = 1.0f / tok_scale[i / hidden];
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = ld_act(x, x_dtype, (size_t)i + j) * gi;
+    store_half4(x16 + i, v);
+}
+
+int launch_tokens_f16(const void* x, int x_dtype, int n_tokens, int hidden, const float* tok_scale, __half* x16, cudaStream_t st) {
+    const long n = (long)n_tokens * hidden;
+    tokens_f16_kernel<<<(unsigned)((n / 4 + 255) / 256), 256, 0, st>>>(x, x_dtype, n, hidden, tok_scale, x16);
+    return check_launch("tokens_f16");
+}
+
 int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
     token_scale_kernel<<<(unsigned)((n_tokens + 7) / 8), 256, 0, st>>>(x, x_dtype, n_tokens, hidden, tok_scale);
@@ -164,7 +182,7 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
 // FP4 tensor regime: one CTA per (work item of up to 64 pairs, 256-column stage) builds the stage's activation image
 // (192 rows: 3 residual terms x 64 positions) in shared memory - warp tasks = (position, 128-block) - and copies the rows
 // of present pairs out in 16-byte units, 512 consecutive bytes per warp. Grid-stride over the device-side item count.
-__global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, const void* __restrict__ x, int x_dtype, Plan p) {
+__global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, Plan p) {
     __shared__ __align__(16) uint8_t img[kWideStageBytes];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int NS = L.hidden / 256, n_items = p.counters[3];
@@ -175,13 +193,9 @@ __global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, con
         for (int task = warp; task < 2 * cnt; task += 16) {
             const int pos = task >> 1, half = task & 1, blk = st * 2 + half;
             const int pair = start + pos, t = p.pair_token[pair];
-            const float g = p.tok_scale[t];
             float v[4];
-            transform_gu_block(L, x, x_dtype, t, e, blk, lane, v);
-            const float gi = 1.0f / g;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] *= gi;
-            if (blk == 0 && lane == 0) p.pscale_gu[pair] = g;
+            transform_gu_block(L, p.x16, kDtypeF16Scaled, t, e, blk, lane, v);  // rows already divided by the token scale
+            if (blk == 0 && lane == 0) p.pscale_gu[pair] = p.tok_scale[t];
             quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, half, pos);
         }
         __syncthreads();
@@ -202,7 +216,7 @@ int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Pl
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const long most = (long)p.max_gitems * (L.hidden / 256);
         const unsigned grid = (unsigned)(most < 3L * sms ? most : 3L * sms);
-        pre_gu_wide_kernel<<<grid, 512, 0, st>>>(L, x, x_dtype, p);
+        pre_gu_wide_kernel<<<grid, 512, 0, st>>>(L, p);
         return check_launch("pre_gu_wide");
     }
     const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);
