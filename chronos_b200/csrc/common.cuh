@@ -12,6 +12,7 @@ namespace chronos {
 
 constexpr int kPairsPerItem = 8;  // (token, expert) pairs that share one pass over a slot's bank (= MMA N)
 constexpr int kPairsPerGemmItem = 128;  // pairs of ONE expert per tensor-core work item, fp16 regime (= MMA M)
+constexpr int kHealSplit = 4;           // slices of the contraction the tensor-core healer-input kernel is split into (one CTA each)
 constexpr int kGroupPairs = 8;          // pairs whose bank-pass outputs one CTA of the large-batch output kernel stages in shared memory
 constexpr int kDtypeF16Scaled = 2;      // internal activation source: fp16 rows already divided by the token / pair scale
 constexpr int kPairsPerWideItem = 64;   // the same in the FP4 tensor regime: 3 residual terms x 64 pairs = MMA N of 192
@@ -52,6 +53,7 @@ struct Plan {
     uint8_t* bq_dn;        // [max_items, I/256, 6144]
     float* yt;             // [P, H]   per-pair down outputs in natural row order (tensor regime only, else NULL)
     __half* x16;           // [T, H]   x / token scale as fp16 (large batches only, else NULL)
+    float* hsplit;         // [2 stages][kHealSplit][P, r] healer input factors, one partial sum per slice of the contraction
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
     int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
@@ -64,7 +66,7 @@ struct Plan {
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
-        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, total;
+        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, total;
     int fp4, tiled, wide;
     int max_pairs, max_items, max_gitems;
 };
@@ -120,6 +122,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (I / 256) * kWideStageBytes : 0));
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.off_x16 = take(p.tiled ? T * H * 2 : 0);
+    p.off_hsplit = take(p.tiled ? 2 * kHealSplit * P * r * 4 : 0);
     p.total = o;
     return p;
 }
@@ -159,6 +162,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.gitem_pairs = kPairsPerGemmItem;
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.x16 = l.tiled ? (__half*)(b + l.off_x16) : nullptr;
+    p.hsplit = l.tiled ? (float*)(b + l.off_hsplit) : nullptr;
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
     p.max_gitems = l.max_gitems;
@@ -353,7 +357,8 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
     return d;
 }
 
-__device__ __forceinline__ float silu_f32(float z) { return z / (1.0f + expf(-z)); }
+// z * sigmoid(z) with the fast exponential and division (relative error ~1e-6, far inside the layer tolerance)
+__device__ __forceinline__ float silu_f32(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
 
 __device__ __forceinline__ __half f32_to_f16_sat(float v) {
     unsigned short r;
@@ -398,11 +403,12 @@ __device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int la
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
         const uint32_t sc8 = f32x2_to_e4m3x2(m * up * (1.0f / 6.0f), 0.0f) & 0xffu;
         const float sdec = e4m3_to_f32((uint8_t)sc8);
-        const float inv = sdec > 0.0f ? up / sdec : 0.0f;
+        // approximate reciprocal: inv only positions the values for rounding; the residual is taken from what was stored
+        const float inv = sdec > 0.0f ? __fdividef(up, sdec) : 0.0f;
         const uint32_t b01 = f32x2_to_e2m1x2(r[0] * inv, r[1] * inv) & 0xffu;
         const uint32_t b23 = f32x2_to_e2m1x2(r[2] * inv, r[3] * inv) & 0xffu;
         const float2 q01 = e2m1x2_to_f32(b01), q23 = e2m1x2_to_f32(b23);
-        const float back = sdec / up;
+        const float back = sdec * (1.0f / up);  // exact: up is a power of two
         r[0] = fmaf(-q01.x, back, r[0]); r[1] = fmaf(-q01.y, back, r[1]);
         r[2] = fmaf(-q23.x, back, r[2]); r[3] = fmaf(-q23.y, back, r[3]);
         const int n = t * TSTRIDE + prow;

@@ -35,11 +35,12 @@ __device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Healer input factor of a tensor-regime work item (one expert, up to 128 sorted pairs):
-//   out[pair, c] = (1 / g_pair) * sum_k V[e, c, k] * X[row(pair), k]      c < r, stored as fp16
+//   out[slice][pair, c] = (1 / g_pair) * sum_{k in slice} V[e, c, k] * X[row(pair), k]      c < r, fp32 partial sums
 // V e4m3 [E, r, K]; X rows are activations (bf16 / fp32, or the fp16 image already divided by the token scale; row =
 // token of the pair) or SwiGLU outputs (fp32, or fp16 already divided by the pair scale; row = pair);
 // g_pair is the power-of-two scale the bank pass uses for the same pair (so the fp16 image stays in range); the
-// consumer multiplies it back. One CTA per work item; warp w owns rank rows 16 (w % MT) .. +15 and the pairs of
+// consumer adds the slices in order and multiplies the scale back. One CTA per (work item, slice of K): the kernel is
+// a chain of dependent L2 round trips, so more CTAs in flight is what shortens it. Warp w owns rank rows 16 (w % MT) .. +15 and the pairs of
 // 8-pair tiles (w / MT), (w / MT) + 8 / MT, ...
 // ---------------------------------------------------------------------------------------------------------------
 struct HealInArgs {
@@ -47,7 +48,9 @@ struct HealInArgs {
     const void* x; int x_dtype; // rows of K
     const int32_t* row_of_pair; // NULL: row = pair
     const float* pscale;        // [P]
-    __half* out;                // [P, r]
+    float* out;                 // [kHealSplit][P, r] partial sums over the slices of K (slices past n_split stay unwritten)
+    size_t split_stride;        // P * r
+    int n_split;
     const int32_t* gitem_start; const int32_t* gitem_cnt; const int32_t* pair_expert; const int32_t* counters;
     int K, r, n_experts;
 };
@@ -81,8 +84,9 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
     }
     const uint8_t* v0 = a.v + ((size_t)e * r + mt * 16 + g) * K + 16 * q;
     const uint8_t* v1 = v0 + (size_t)8 * K;
+    const int k_lo = (int)blockIdx.y * (K / a.n_split), k_hi = k_lo + K / a.n_split;
 #pragma unroll 2
-    for (int kc = 0; kc < K; kc += 64) {
+    for (int kc = k_lo; kc < k_hi; kc += 64) {
         const uint4 w0 = *reinterpret_cast<const uint4*>(v0 + kc);
         const uint4 w1 = *reinterpret_cast<const uint4*>(v1 + kc);
         const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w}, r1[4] = {w1.x, w1.y, w1.z, w1.w};
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int n = n0 + (j & 1), c = mt * 16 + g + (j >> 1) * 8;
-            if (n < cnt) a.out[(size_t)(start + n) * r + c] = f32_to_f16_sat(acc[i][j]);
+            if (n < cnt) a.out[blockIdx.y * a.split_stride + (size_t)(start + n) * r + c] = acc[i][j];
         }
     }
 }
@@ -142,7 +146,10 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
     a.x_dtype = x_dtype;
     a.row_of_pair = stage == 0 ? p.pair_token : nullptr;
     a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
-    a.out = reinterpret_cast<__half*>(stage == 0 ? p.hmid : p.hpart);
+    a.split_stride = (size_t)p.max_pairs * L.rank;
+    a.out = p.hsplit + (size_t)stage * kHealSplit * a.split_stride;
+    const int kdim = stage == 0 ? L.hidden : L.inter;
+    a.n_split = kdim % (64 * kHealSplit) == 0 ? kHealSplit : (kdim % 128 == 0 ? 2 : 1);
     a.gitem_start = p.gitem_start;
     a.gitem_cnt = p.gitem_cnt;
     a.pair_expert = p.pair_expert;
@@ -150,7 +157,7 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
     a.K = stage == 0 ? L.hidden : L.inter;
     a.r = L.rank;
     a.n_experts = L.n_experts;
-    const unsigned grid = (unsigned)p.max_gitems;
+    const dim3 grid((unsigned)p.max_gitems, (unsigned)a.n_split);
     switch (L.rank / 16) {
         case 1: healer_in_mma_kernel<1><<<grid, 256, 0, st>>>(a); break;
         case 2: healer_in_mma_kernel<2><<<grid, 256, 0, st>>>(a); break;
@@ -183,6 +190,7 @@ __device__ __forceinline__ void cp_async16_g2s(void* smem_dst, const void* gsrc)
 template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
 __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
+    __shared__ __align__(16) __half hsm[kGroupPairs][kMaxRank];
     constexpr int PG = kGroupPairs, NW = kOutThreads / 32;
     constexpr int r = R16 * 16;
     const int H = L.hidden, I = L.inter;
@@ -220,15 +228,27 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                 else *reinterpret_cast<float4*>(vec + i) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
-            // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per step (columns g >= cnt are zero)
-            const __half* h16 = reinterpret_cast<const __half*>(MODE == 0 ? p.hmid : p.hpart);
-            uint32_t bf[R16][2];
+            // healer input factors of the group: the sum, in slice order, of the healer-input kernel's partial sums, as
+            // fp16 in shared memory (rows of absent pairs are zero)
+            const size_t sstride = (size_t)p.max_pairs * r;
+            const float* hs = p.hsplit + (size_t)MODE * kHealSplit * sstride;
+            const int kdim = MODE == 0 ? H : I;
+            const int n_split = kdim % (64 * kHealSplit) == 0 ? kHealSplit : (kdim % 128 == 0 ? 2 : 1);
+            if (tid < PG * (r / 4)) {
+                const int n = tid / (r / 4), c4 = (tid % (r / 4)) * 4;
+                float4 part[kHealSplit];
 #pragma unroll
-            for (int s = 0; s < R16; ++s) {
-                uint2 v = make_uint2(0u, 0u);
-                if (g < cnt) v = *reinterpret_cast<const uint2*>(h16 + (size_t)(p0 + g) * r + 4 * R16 * q + 4 * s);
-                bf[s][0] = v.x;
-                bf[s][1] = v.y;
+                for (int ks = 0; ks < kHealSplit; ++ks) {  // all slices requested before any is added
+                    part[ks] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (n < cnt && ks < n_split) part[ks] = *reinterpret_cast<const float4*>(hs + ks * sstride + (size_t)(p0 + n) * r + c4);
+                }
+                float4 acc4 = part[0];
+#pragma unroll
+                for (int ks = 1; ks < kHealSplit; ++ks) {
+                    acc4.x += part[ks].x; acc4.y += part[ks].y; acc4.z += part[ks].z; acc4.w += part[ks].w;
+                }
+                const float h4[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+                store_half4(&hsm[n][c4], h4);
             }
             const float* psc = MODE == 0 ? p.pscale_gu : p.pscale_dn;
             const float gs0 = 2 * q < cnt ? psc[p0 + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt ? psc[p0 + 2 * q + 1] : 0.0f;
@@ -237,6 +257,14 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
             const uint8_t* U = (MODE == 0 ? L.u_gu : L.u_dn) + (size_t)e * VL * r;
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
+            // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per step
+            uint32_t bf[R16][2];
+#pragma unroll
+            for (int s = 0; s < R16; ++s) {
+                const uint2 v = *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s]);
+                bf[s][0] = v.x;
+                bf[s][1] = v.y;
+            }
             // software pipeline over the 16-row tiles of this warp: the healer rows and permutation entries of the next
             // tile are requested before the current tile is multiplied (each request is a full L2 round trip)
             constexpr int NH = MODE == 0 ? 2 : 1;

@@ -115,6 +115,111 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
         }
 }
 
+// Large batches: the same dots from shared memory. A CTA of 16 warps computes 64 tokens x 16 experts; per 128-column
+// step it stages the 64 activation rows (in their own dtype) and the 16 router rows with 16-byte asynchronous copies
+// into an 8-deep ring, and warp (wt, we) multiplies tokens 8 wt .. + 7 by experts 8 we .. + 7 in the stated order
+// (lane l: k = 128 j + 4 l + i). Global traffic per logit drops from 3 KB (register tile straight from L2) to 24 B
+// per step, which is what bounded the register-tile kernel on large batches. Bits are identical to the other kernels.
+constexpr int kRtTok = 64, kRtExp = 16, kRtThreads = 512;
+constexpr int kRtStagesBf16 = 8, kRtStagesF32 = 5;  // steps in flight: enough to cover the L2 latency, bounded by shared memory
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRtThreads) router_logits_tiled_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                                         float* __restrict__ logits, int n_tokens, int n_experts,
+                                                                         int hidden, float* __restrict__ tok_scale) {
+    extern __shared__ __align__(16) uint8_t rts[];
+    constexpr int XB = BF16 ? 2 : 4;
+    constexpr int kRtStages = BF16 ? kRtStagesBf16 : kRtStagesF32;
+    constexpr int XS = kRtTok * 128 * XB, WS = kRtExp * 128 * 4, STAGE = XS + WS;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wt = warp >> 1, we = warp & 1;
+    const int e_tiles = (n_experts + kRtExp - 1) / kRtExp;
+    const int t0 = (int)(blockIdx.x / e_tiles) * kRtTok, e0 = (int)(blockIdx.x % e_tiles) * kRtExp;
+    const int n_steps = hidden / 128;
+    auto stage_in = [&](int step) {
+        uint8_t* dst = rts + (size_t)(step % kRtStages) * STAGE;
+        // activations: 64 rows x (128 * XB / 16) chunks; router rows: 16 rows x 32 chunks
+        constexpr int XC = 128 * XB / 16;
+        for (int c = tid; c < kRtTok * XC; c += kRtThreads) {
+            const int row = c / XC, ch = c % XC;
+            const int t = min(t0 + row, n_tokens - 1);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(x) + ((size_t)t * hidden + (size_t)step * 128) * XB + ch * 16;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + row * 128 * XB + ch * 16)), "l"(src) : "memory");
+        }
+        for (int c = tid; c < kRtExp * 32; c += kRtThreads) {
+            const int row = c / 32, ch = c % 32;
+            const int e = min(e0 + row, n_experts - 1);
+            const float* src = w + (size_t)e * hidden + (size_t)step * 128 + ch * 4;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + XS + row * 512 + ch * 16)), "l"(src) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float acc[8][8], ssq[8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        ssq[a] = 0.0f;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+    }
+    const bool do_scale = tok_scale != nullptr && e0 == 0 && we == 0;
+    for (int s = 0; s < kRtStages - 1; ++s) {
+        if (s < n_steps) stage_in(s);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int step = 0; step < n_steps; ++step) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2) : "memory");
+        __syncthreads();  // the step's bytes have landed for every thread; the slot refilled below was read a step ago
+        if (step + kRtStages - 1 < n_steps) stage_in(step + kRtStages - 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint8_t* cur = rts + (size_t)(step % kRtStages) * STAGE;
+        float4 wv[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) wv[b] = *reinterpret_cast<const float4*>(cur + XS + (we * 8 + b) * 512 + lane * 16);
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            float4 xq;
+            if (BF16) {
+                const uint2 u = *reinterpret_cast<const uint2*>(cur + (wt * 8 + a) * 256 + lane * 8);
+                xq = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                                 __uint_as_float(u.y & 0xffff0000u));
+            } else {
+                xq = *reinterpret_cast<const float4*>(cur + (wt * 8 + a) * 512 + lane * 16);
+            }
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                acc[a][b] = __fmaf_rn(xq.x, wv[b].x, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.y, wv[b].y, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.z, wv[b].z, acc[a][b]);
+                acc[a][b] = __fmaf_rn(xq.w, wv[b].w, acc[a][b]);
+            }
+            ssq[a] = fmaf(xq.x, xq.x, fmaf(xq.y, xq.y, fmaf(xq.z, xq.z, fmaf(xq.w, xq.w, ssq[a]))));
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    const int tw = t0 + wt * 8, ew = e0 + we * 8;
+    if (do_scale) {
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            float v = ssq[a];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0 && tw + a < n_tokens) {
+                const float rms = sqrtf(v / (float)hidden);
+                tok_scale[tw + a] = rms > 0.0f ? exp2f(rintf(log2f(rms))) : 1.0f;
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            float v = acc[a][b];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0 && tw + a < n_tokens && ew + b < n_experts) logits[(size_t)(tw + a) * n_experts + ew + b] = v;
+        }
+}
+
 // Decode-sized batches: the dots are few and every one is a long dependent walk over k, so the time is pure memory
 // latency. One CTA stages EPC router rows and up to 4 activation rows in shared memory with bulk async copies
 // (all bytes requested at once, one wait), then warp w computes expert e0 + w against the 4 tokens in the stated
@@ -222,11 +327,14 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
         const unsigned grid = (unsigned)((tiles + 7) / 8);
         if (bf16) router_logits_kernel<4, 1, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
         else router_logits_kernel<4, 1, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
-    } else if (n_tokens >= 256) {  // large batches: 8 tokens x 8 experts per warp, 0.75 B of L1 traffic per FMA
-        const long tiles = (long)((L.n_experts + 7) / 8) * ((n_tokens + 7) / 8);
-        const unsigned grid = (unsigned)((tiles + 7) / 8);
-        if (bf16) router_logits_kernel<8, 8, true><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
-        else router_logits_kernel<8, 8, false><<<grid, 256, 0, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+    } else if (n_tokens >= 256) {  // large batches: shared-memory tiles of 64 tokens x 16 experts
+        const unsigned grid = (unsigned)(((n_tokens + kRtTok - 1) / kRtTok) * ((L.n_experts + kRtExp - 1) / kRtExp));
+        const size_t smem = (size_t)(bf16 ? kRtStagesBf16 : kRtStagesF32) * (kRtTok * 128 * (bf16 ? 2 : 4) + kRtExp * 512);
+        cudaError_t rc = bf16 ? cudaFuncSetAttribute(router_logits_tiled_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                              : cudaFuncSetAttribute(router_logits_tiled_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (rc != cudaSuccess) { set_error("router: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc)); return CHRONOS_E_LAUNCH; }
+        if (bf16) router_logits_tiled_kernel<true><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+        else router_logits_tiled_kernel<false><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     } else {
         const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
         const unsigned grid = (unsigned)((tiles + 7) / 8);
