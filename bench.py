@@ -178,7 +178,8 @@ def run_decode(args) -> dict:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = FoldedLayerConfig(**DECODE)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=1, device=dev, with_shared=True), register=False)
+    tail = (args.tail, args.tail) if args.tail else (0, 0)  # optional tail lattice (next-row feature): same codes width for both products
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=1, device=dev, with_shared=True, tail_bits=tail), register=False)
     streams = args.streams
     batches = decode_batches(cfg, streams, dev)
     n_tok = batches[0].shape[0]
@@ -222,6 +223,10 @@ def run_decode(args) -> dict:
     gu_bytes = statistics.mean(stats[i % N_BATCHES]["gu_pass_bytes"] for i in range(K))
     dn_bytes = statistics.mean(stats[i % N_BATCHES]["dn_pass_bytes"] for i in range(K))
     layer_bytes = statistics.mean(stats[i % N_BATCHES]["layer_bytes"] for i in range(K))
+    if args.tail:  # per distinct expert: codes + e4m3 block scales of the gate_up and down tail matrices
+        blk = 32 if args.tail == 2 else 64
+        tail_per_expert = 3 * cfg.hidden * cfg.inter * args.tail // 8 + 3 * cfg.hidden * cfg.inter // blk
+        layer_bytes += statistics.mean(stats[i % N_BATCHES]["experts"] for i in range(K)) * tail_per_expert
 
     # ---- end to end: pinned host input -> device -> forward -> pinned host output, copies inside the timed region --
     host_in = [b.cpu().pin_memory() for b in batches]
@@ -253,6 +258,7 @@ def run_decode(args) -> dict:
                    "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
                    "streams": streams, "tokens_per_stream": TOKENS_PER_STREAM, "activations": "bf16", "router": cfg.router,
                    "l2_policy": f"each step streams {layer_bytes / 1e6:.0f} MB of banks (> 126 MB L2) and batches rotate over {N_BATCHES} routings",
+                   "tail_lattice_bits": args.tail,
                    "distinct_slots_per_step": statistics.mean(s["slots"] for s in stats),
                    "distinct_slots_by_routing": [s["slots"] for s in stats],
                    "distinct_experts_per_step": statistics.mean(s["experts"] for s in stats),
@@ -479,6 +485,7 @@ def main() -> None:
     ap.add_argument("--regime", default=None, choices=(None, "auto", "tensor", "tensor_fp4"), help="bank-pass regime of the prefill workload")
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tail", type=int, default=0, choices=(0, 1, 2), help="decode workload: add a tail lattice of this many bits per weight")
     ap.add_argument("--layers", type=int, default=EP_LAYERS, help="depth of the ep_stack workload")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX = 0, 1
-ABI_VERSION = 5
+ABI_VERSION = 6
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4, REGIME_TENSOR_FP4 = 0, 1, 2, 3, 4
 
 
@@ -26,14 +26,15 @@ class LayerStruct(C.Structure):
     _fields_ = (
         [(n, C.c_int32) for n in ("hidden", "inter", "n_experts", "group_size", "n_slots", "rank", "top_k",
                                   "router_kind", "renorm")]
-        + [("routed_scaling", C.c_float), ("shared_inter", C.c_int32), ("reserved_", C.c_int32)]
+        + [("routed_scaling", C.c_float), ("shared_inter", C.c_int32), ("tail_bits", C.c_int32)]
         + [(n, C.c_void_p) for n in (
             "router_w", "e_bias",
             "gu_w", "gu_s", "gu_s2", "gu_beta", "dn_w", "dn_s", "dn_s2", "dn_beta",
             "u_gu", "v_gu", "u_dn", "v_dn_t",
             "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2",
             "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
-            "gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn")]
+            "gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn",
+            "tail_gu_p", "tail_gu_s", "tail_dn_p", "tail_dn_s")]
     )
 
 

@@ -11,7 +11,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libchronos_b200.so"
-SOURCES = ("api.cu", "probe_kernels.cu", "router.cu", "plan.cu", "transform_kernels.cu", "bank_stream.cu", "bank_gemm.cu", "bank_fp4.cu", "healer_mma.cu")
+SOURCES = ("api.cu", "probe_kernels.cu", "router.cu", "plan.cu", "transform_kernels.cu", "bank_stream.cu", "bank_gemm.cu", "bank_fp4.cu", "healer_mma.cu", "tail.cu")
 
 
 def nvcc_path() -> str:

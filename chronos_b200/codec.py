@@ -1,7 +1,7 @@
 """Codec probes with the reference's function names and argument meaning, executed by the CUDA library.
 
 `unpack_nvfp4` mirrors chronos_1t/converter/convert_glm53_flash_colab.py:81-89 (fp32, bit-exact);
-`reconstruct_group_experts` mirrors chronos_1t/models/glm53_holo.py:336-368 with include_tail=False.
+`reconstruct_group_experts` mirrors chronos_1t/models/glm53_holo.py:336-368 (with or without the tail lattice).
 Inputs must live on a CUDA device; there is no CPU implementation behind these calls.
 """
 from __future__ import annotations
@@ -41,7 +41,8 @@ def unpack_nvfp4(packed: torch.Tensor, scale_fp8: torch.Tensor, scale_2: torch.T
 
 
 def reconstruct_experts(layer: PackedLayer, experts: list[int]) -> list[tuple[torch.Tensor, torch.Tensor]]:
-    """fp32 (gate_up [2I, H], down [H, I]) = beta * unbind(bank) + U.V for the given global expert ids."""
+    """fp32 (gate_up [2I, H], down [H, I]) = beta * unbind(bank) + U.V (+ tail when the layer carries it) for the
+    given global expert ids."""
     c = layer.cfg
     out = []
     scratch = torch.empty(max(2 * c.inter * c.hidden, c.hidden * c.inter), dtype=torch.float32, device=layer.device)
@@ -57,15 +58,13 @@ def reconstruct_experts(layer: PackedLayer, experts: list[int]) -> list[tuple[to
 def reconstruct_group_experts(g: Mapping[str, torch.Tensor], g_idx: int, members: list[int], hidden: int, inter: int,
                               include_tail: bool = False, dtype: torch.dtype = torch.float32,
                               device: torch.device | str = "cuda") -> list[tuple[torch.Tensor, torch.Tensor]]:
-    """Same call shape as the reference function; `g` holds one slot's tensors. The tail lattice is not part of
-    this path, so include_tail=True is refused rather than silently ignored."""
-    if include_tail:
-        raise NotImplementedError("the tail lattice is outside the folded fast path (include_tail must be False)")
+    """Same call shape as the reference function; `g` holds one slot's tensors. `include_tail=True` adds the tail
+    lattice term (chronos_1t/models/glm53_holo.py:362-366); the slot must then carry the `tail.*` tensors."""
     k = int(g["s_gu.beta"].shape[0])
     rank = int(g["healer.u_gu"].shape[-1])
     # a one-slot layer whose slot index is g_idx: place the slot at position g_idx of an otherwise empty table
     cfg = FoldedLayerConfig(hidden=hidden, inter=inter, n_experts=k * (g_idx + 1), group_size=k, rank=rank, top_k=1)
     groups = [g] * (g_idx + 1)
-    layer = PackedLayer.from_groups(cfg, groups, device=device)
+    layer = PackedLayer.from_groups(cfg, groups, device=device, include_tail=include_tail)
     rec = reconstruct_experts(layer, [g_idx * k + m for m in members])
     return [(a.to(dtype), b.to(dtype)) for a, b in rec]

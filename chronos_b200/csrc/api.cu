@@ -64,6 +64,16 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
             return CHRONOS_E_ALIGN;
         }
     }
+    if (L->tail_bits != 0) {
+        const int gb = L->tail_bits & 0xff, db = (L->tail_bits >> 8) & 0xff;
+        if ((gb != 1 && gb != 2) || (db != 1 && db != 2) || (L->tail_bits >> 16) != 0) {
+            set_error("tail_bits 0x%x: gate_up and down tail widths must each be 1 or 2", L->tail_bits);
+            return CHRONOS_E_ARG;
+        }
+        const void* tl[] = {L->tail_gu_p, L->tail_gu_s, L->tail_dn_p, L->tail_dn_s};
+        for (const void* q : tl)
+            if (!aligned16(q)) { set_error("a tail-lattice pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
+    }
     if (need_router && L->router_w == nullptr) { set_error("layer.router_w is NULL"); return CHRONOS_E_ALIGN; }
     if (L->shared_inter > 0) {
         const void* sh[] = {L->sh_gu_w, L->sh_gu_s, L->sh_dn_w, L->sh_dn_s};
@@ -139,16 +149,21 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     // the layer carries healer.v_down in its on-disk orientation, else CUDA-core kernels that share healer rows through L1
     const int many = (tensor && p.yt != nullptr) ? 1 : 0;
     const bool hmma = many && healer_mma_fits(L);
-    if (hmma)  // the large-batch kernels read a token's row once per pair: give them x / token scale as fp16
+    const bool tail = p.tail_gu != nullptr;
+    if (hmma || tail)  // the large-batch kernels and the tail pass read a token's row once per pair: give them x / token scale as fp16
         if (int rc = launch_tokens_f16(x, x_dtype, n_tokens, L.hidden, p.tok_scale, p.x16, st)) return rc;
     if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, hmma ? 2 : many, st)) return rc;
     if (hmma)
         if (int rc = launch_healer_in_mma(L, 0, p.x16, kDtypeF16Scaled, p, st)) return rc;
+    if (tail)
+        if (int rc = launch_tail_pass(L, 0, p.x16, kDtypeF16Scaled, p, st)) return rc;
     stage_mark(3, st);
     if (int rc = wide ? launch_bank_fp4_wide(L, 0, p, st)
                       : (tensor ? launch_bank_gemm(L, 0, p, st) : (fp4 ? launch_bank_fp4(L, 0, p, st) : launch_bank_stream(L, 0, p, st)))) return rc;
     stage_mark(4, st);
     if (int rc = hmma ? launch_mid_mma(L, p, wide ? 1 : 0, st) : launch_mid(L, p, fp4, st)) return rc;
+    if (tail)  // SwiGLU outputs in natural order: fp16 rows / pair scale in the FP4 tensor regime, fp32 rows otherwise
+        if (int rc = wide ? launch_tail_pass(L, 1, p.ac, kDtypeF16Scaled, p, st) : launch_tail_pass(L, 1, p.act, CHRONOS_DTYPE_F32, p, st)) return rc;
     stage_mark(5, st);
     if (int rc = wide ? launch_bank_fp4_wide(L, 1, p, st)
                       : (tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st)))) return rc;
@@ -171,7 +186,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 5; }
+int chronos_b200_abi_version(void) { return 6; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -187,14 +202,16 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
     if (int rc = validate_layer(layer, false)) return rc;
     if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
     if (!out || !scratch) { set_error("unfold: out or scratch is NULL"); return CHRONOS_E_ALIGN; }
-    return launch_unfold(*layer, expert, which, out, scratch, (cudaStream_t)stream);
+    if (int rc = launch_unfold(*layer, expert, which, out, scratch, (cudaStream_t)stream)) return rc;
+    return layer->tail_bits ? launch_tail_add(*layer, expert, which, out, (cudaStream_t)stream) : CHRONOS_OK;
 }
 
 int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int expert, int which, float* out, void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
     if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold_static: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
     if (!out) { set_error("unfold_static: out is NULL"); return CHRONOS_E_ALIGN; }
-    return launch_unfold_static(*layer, expert, which, out, (cudaStream_t)stream);
+    if (int rc = launch_unfold_static(*layer, expert, which, out, (cudaStream_t)stream)) return rc;
+    return layer->tail_bits ? launch_tail_add(*layer, expert, which, out, (cudaStream_t)stream) : CHRONOS_OK;
 }
 
 int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,

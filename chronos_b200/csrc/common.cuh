@@ -53,6 +53,8 @@ struct Plan {
     uint8_t* bq_dn;        // [max_items, I/256, 6144]
     float* yt;             // [P, H]   per-pair down outputs in natural row order (tensor regime only, else NULL)
     __half* x16;           // [T, H]   x / token scale as fp16 (large batches only, else NULL)
+    float* tail_gu;        // [P, 2I]  tail-lattice term of the gate_up product, natural row order (NULL: layer has no tail)
+    float* tail_dn;        // [P, H]   the same for the down product
     float* hsplit;         // [2 stages][kHealSplit][P, r] healer input factors, one partial sum per slice of the contraction
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
@@ -66,8 +68,8 @@ struct Plan {
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
-        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, total;
-    int fp4, tiled, wide;
+        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, off_tail_gu, off_tail_dn, off_x16t, total;
+    int fp4, tiled, wide, tail;
     int max_pairs, max_items, max_gitems;
 };
 
@@ -123,6 +125,10 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.off_x16 = take(p.tiled ? T * H * 2 : 0);
     p.off_hsplit = take(p.tiled ? 2 * kHealSplit * P * r * 4 : 0);
+    p.tail = L.tail_bits != 0 ? 1 : 0;
+    p.off_tail_gu = take(p.tail ? P * 2 * I * 4 : 0);
+    p.off_tail_dn = take(p.tail ? P * H * 4 : 0);
+    p.off_x16t = take((p.tail && !p.tiled) ? T * H * 2 : 0);  // the fp16 token image for the tail pass when no other regime lays it out
     p.total = o;
     return p;
 }
@@ -163,6 +169,9 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.x16 = l.tiled ? (__half*)(b + l.off_x16) : nullptr;
     p.hsplit = l.tiled ? (float*)(b + l.off_hsplit) : nullptr;
+    p.tail_gu = l.tail ? (float*)(b + l.off_tail_gu) : nullptr;
+    p.tail_dn = l.tail ? (float*)(b + l.off_tail_dn) : nullptr;
+    if (l.tail && !l.tiled) p.x16 = (__half*)(b + l.off_x16t);
     p.max_pairs = l.max_pairs;
     p.max_items = l.max_items;
     p.max_gitems = l.max_gitems;
@@ -200,6 +209,9 @@ int launch_mid(const chronos_layer_t& L, const Plan& p, int fp4, cudaStream_t st
 bool healer_mma_fits(const chronos_layer_t& L);
 int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
 int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st);
+// tail lattice (csrc/tail.cu)
+int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
+int launch_tail_add(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_bank_fp4_wide(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
 int launch_combine_sum(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,

@@ -311,6 +311,8 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                         float v = 0.0f;
                         if (n < PG) v = vec[(size_t)n * VL + (ro & 0x7fffu)];
                         zz[half][j] = fmaf(beta, (ro >> 15) ? -v : v, ((j & 1) ? gs1 : gs0) * d[j]);
+                        const float* tl = MODE == 0 ? p.tail_gu : p.tail_dn;  // tail-lattice term, natural row order
+                        if (tl != nullptr && n < cnt) zz[half][j] += tl[(size_t)(p0 + n) * VL + half * I + (j < 2 ? row_lo : row_hi)];
                     }
                 }
 #pragma unroll

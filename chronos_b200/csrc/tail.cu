@@ -1,0 +1,217 @@
+// Tail lattice: per expert a coarse matrix in natural weight space that the converter adds on top of the unfolded bank
+// and the healer (chronos_1t/models/glm53_holo.py:362-366). Codes are 2-bit Lloyd-Max levels with an e4m3 scale per 32
+// columns (unpack_2bit_lloyd_max, chronos_1t/models/chronos_moe_block.py:145-157) or 1-bit signs with a scale per 64
+// columns (unpack_1bit_rademacher, :212-224): value = level * float(scale).
+//
+// tail_pass_kernel streams an expert's tail rows once per group of 8 of its pairs and multiplies them by the pairs'
+// activations on the tensor cores (mma.sync m16n8k16, fp16): out[pair, row] = g_pair * sum_k T[e, row, k] * x16[pair, k],
+// x16 = activations / g_pair in fp16. The consumers (SwiGLU kernel, combine kernel) add the term where they add the healer.
+// A warp owns 16 rows; lane (g = lane / 4, q = lane % 4) owns rows g, g + 8 and, per 64-column step, the 16 contiguous
+// columns 16 q .. 16 q + 15 (4 bytes of 2-bit codes or 2 bytes of sign bits per row): any permutation of the
+// contraction index is legal as long as both operands use it, so MMA step s takes columns 16 q + 4 s .. + 3.
+#include "common.cuh"
+
+namespace chronos {
+
+__device__ __forceinline__ void mma_16816_t(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                            uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// fp16 bit patterns of the Lloyd-Max levels -1.510417, -0.452780, 0.452780, 1.510417 (round to nearest)
+constexpr uint32_t kLloydLo = 0xB73FBE0Bu;  // level 1 in the high half, level 0 in the low half
+constexpr uint32_t kLloydHi = 0x3E0B373Fu;  // level 3 high, level 2 low
+
+// two 2-bit codes (bits 0-1 and 2-3 of c4) -> fp16x2 (first code in the low half): one byte permute on the level table
+__device__ __forceinline__ uint32_t lloyd2_pair(uint32_t c4) {
+    const uint32_t u = (c4 & 3u) | ((c4 & 12u) << 6);  // code 0 at bits 0-1, code 1 at bits 8-9
+    return __byte_perm(kLloydLo, kLloydHi, u * 0x22u + 0x1010u);
+}
+// two sign bits (bit 0, bit 1 of b2; set = +1) -> fp16x2 of +-1
+__device__ __forceinline__ uint32_t sign_pair(uint32_t b2) {
+    return 0xBC00BC00u ^ (((b2 & 1u) << 15) | ((b2 & 2u) << 30));
+}
+__device__ __forceinline__ uint32_t e4m3_to_f16x2_dup(uint32_t byte) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((uint16_t)(byte | (byte << 8))));
+    return r;
+}
+
+struct TailArgs {
+    const uint8_t* codes; const uint8_t* scales;  // [E, R, K * bits / 8], [E, R, K / block]
+    const void* x; int x_dtype;                   // fp16 rows already divided by the pair's scale, or fp32 rows (divided here)
+    const int32_t* row_of_pair;                   // token of the pair (gate_up) or NULL: row = pair (down)
+    const float* pscale;                          // [P]
+    float* out;                                   // [P, R]
+    const int32_t* gitem_start; const int32_t* gitem_cnt; const int32_t* pair_expert; const int32_t* counters;
+    int R, K, n_experts;
+};
+
+template <int BITS>
+__global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
+    extern __shared__ __align__(16) uint8_t tsm[];  // 8 activation rows of K fp16 (+ 8 bytes of padding per row)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
+    const int R = a.R, K = a.K, RB = R / 128;
+    const int xstride = K * 2 + 8;
+    constexpr int BLK = BITS == 2 ? 32 : 64;
+    const long n_tiles = (long)a.counters[3] * RB;
+    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    int cur_item = -1, cur_chunk = -1;
+    for (long tile = tile_lo; tile < tile_hi; ++tile) {
+        const int item = (int)(tile / RB), rb = (int)(tile % RB);
+        const int start = a.gitem_start[item], cnt = a.gitem_cnt[item];
+        const int e = a.pair_expert[start];
+        if (e >= a.n_experts) continue;  // shared expert: no tail
+        const int row_lo = rb * 128 + warp * 16 + g, row_hi = row_lo + 8;
+        const uint8_t* c_lo = a.codes + ((size_t)e * R + row_lo) * (K * BITS / 8);
+        const uint8_t* c_hi = a.codes + ((size_t)e * R + row_hi) * (K * BITS / 8);
+        const uint8_t* s_lo = a.scales + ((size_t)e * R + row_lo) * (K / BLK);
+        const uint8_t* s_hi = a.scales + ((size_t)e * R + row_hi) * (K / BLK);
+        for (int chunk = 0; chunk * 8 < cnt; ++chunk) {
+            const int c0 = chunk * 8, cn = min(8, cnt - c0);
+            if (item != cur_item || chunk != cur_chunk) {  // stage the group's activation rows (block-uniform branch)
+                __syncthreads();
+                for (int i = tid * 8; i < 8 * K; i += 256 * 8) {
+                    const int n = i / K, k = i % K;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (n < cn) {
+                        const int pair = start + c0 + n;
+                        const size_t row = a.row_of_pair ? (size_t)a.row_of_pair[pair] : (size_t)pair;
+                        if (a.x_dtype == kDtypeF16Scaled) {
+                            v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.x) + row * K + k);
+                        } else {
+                            const float gi = 1.0f / a.pscale[pair];
+                            const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + row * K + k);
+                            const float4 f0 = src[0], f1 = src[1];
+                            const __half2 h0 = __halves2half2(f32_to_f16_sat(f0.x * gi), f32_to_f16_sat(f0.y * gi));
+                            const __half2 h1 = __halves2half2(f32_to_f16_sat(f0.z * gi), f32_to_f16_sat(f0.w * gi));
+                            const __half2 h2 = __halves2half2(f32_to_f16_sat(f1.x * gi), f32_to_f16_sat(f1.y * gi));
+                            const __half2 h3 = __halves2half2(f32_to_f16_sat(f1.z * gi), f32_to_f16_sat(f1.w * gi));
+                            v.x = *reinterpret_cast<const uint32_t*>(&h0); v.y = *reinterpret_cast<const uint32_t*>(&h1);
+                            v.z = *reinterpret_cast<const uint32_t*>(&h2); v.w = *reinterpret_cast<const uint32_t*>(&h3);
+                        }
+                    }
+                    // rows are 8 bytes out of phase so that the 8 pairs of a fragment load hit different banks
+                    uint2* dst = reinterpret_cast<uint2*>(tsm + (size_t)n * xstride + (size_t)k * 2);
+                    dst[0] = make_uint2(v.x, v.y);
+                    dst[1] = make_uint2(v.z, v.w);
+                }
+                __syncthreads();
+                cur_item = item;
+                cur_chunk = chunk;
+            }
+            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint8_t* xrow = tsm + (size_t)g * xstride + (size_t)(16 * q) * 2;
+#pragma unroll 4
+            for (int k0 = 0; k0 < K; k0 += 64) {
+                uint32_t w_lo, w_hi, sc_lo, sc_hi;
+                if (BITS == 2) {
+                    w_lo = *reinterpret_cast<const uint32_t*>(c_lo + k0 / 4 + 4 * q);
+                    w_hi = *reinterpret_cast<const uint32_t*>(c_hi + k0 / 4 + 4 * q);
+                    sc_lo = s_lo[k0 / 32 + (q >> 1)];
+                    sc_hi = s_hi[k0 / 32 + (q >> 1)];
+                } else {
+                    w_lo = *reinterpret_cast<const uint16_t*>(c_lo + k0 / 8 + 2 * q);
+                    w_hi = *reinterpret_cast<const uint16_t*>(c_hi + k0 / 8 + 2 * q);
+                    sc_lo = s_lo[k0 / 64];
+                    sc_hi = s_hi[k0 / 64];
+                }
+                const uint32_t f_lo = e4m3_to_f16x2_dup(sc_lo), f_hi = e4m3_to_f16x2_dup(sc_hi);
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    uint32_t a0, a1, a2, a3;
+                    if (BITS == 2) {
+                        const uint32_t b_lo = w_lo >> (8 * s), b_hi = w_hi >> (8 * s);
+                        a0 = lloyd2_pair(b_lo); a2 = lloyd2_pair(b_lo >> 4);
+                        a1 = lloyd2_pair(b_hi); a3 = lloyd2_pair(b_hi >> 4);
+                    } else {
+                        const uint32_t b_lo = w_lo >> (4 * s), b_hi = w_hi >> (4 * s);
+                        a0 = sign_pair(b_lo); a2 = sign_pair(b_lo >> 2);
+                        a1 = sign_pair(b_hi); a3 = sign_pair(b_hi >> 2);
+                    }
+                    a0 = hmul2_u32(a0, f_lo); a2 = hmul2_u32(a2, f_lo);
+                    a1 = hmul2_u32(a1, f_hi); a3 = hmul2_u32(a3, f_hi);
+                    const uint2 b = *reinterpret_cast<const uint2*>(xrow + (size_t)(k0 + 4 * s) * 2);
+                    mma_16816_t(d, a0, a1, a2, a3, b.x, b.y);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = 2 * q + (j & 1), row = j < 2 ? row_lo : row_hi;
+                if (n < cn) a.out[(size_t)(start + c0 + n) * R + row] = d[j] * a.pscale[start + c0 + n];
+            }
+        }
+    }
+}
+
+int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st) {
+    const int bits = stage == 0 ? (L.tail_bits & 0xff) : ((L.tail_bits >> 8) & 0xff);
+    TailArgs a{};
+    a.codes = stage == 0 ? L.tail_gu_p : L.tail_dn_p;
+    a.scales = stage == 0 ? L.tail_gu_s : L.tail_dn_s;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.row_of_pair = stage == 0 ? p.pair_token : nullptr;
+    a.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
+    a.out = stage == 0 ? p.tail_gu : p.tail_dn;
+    a.gitem_start = p.gitem_start;
+    a.gitem_cnt = p.gitem_cnt;
+    a.pair_expert = p.pair_expert;
+    a.counters = p.counters;
+    a.R = stage == 0 ? 2 * L.inter : L.hidden;
+    a.K = stage == 0 ? L.hidden : L.inter;
+    a.n_experts = L.n_experts;
+    const size_t smem = (size_t)8 * (a.K * 2 + 8);
+    if (smem > 200 * 1024) {
+        set_error("tail_pass: %d columns need %zu bytes of shared memory", a.K, smem);
+        return CHRONOS_E_SHAPE;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long max_tiles = (long)p.max_gitems * (a.R / 128);
+    const long resident = (long)sms * (smem * 3 <= 200 * 1024 ? 3 : (smem * 2 <= 200 * 1024 ? 2 : 1));
+    const unsigned grid = (unsigned)(max_tiles < resident ? max_tiles : resident);
+    cudaError_t rc = bits == 2 ? cudaFuncSetAttribute(tail_pass_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                               : cudaFuncSetAttribute(tail_pass_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (rc != cudaSuccess) {
+        set_error("tail_pass: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    if (bits == 2) tail_pass_kernel<2><<<grid, 256, smem, st>>>(a);
+    else tail_pass_kernel<1><<<grid, 256, smem, st>>>(a);
+    return check_launch("tail_pass");
+}
+
+// Weight-space probe: out[r, c] += level(code[e, r, c]) * float(scale[e, r, c / block])  (fp32, as the reference adds it)
+__global__ void __launch_bounds__(256) tail_add_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                                                       int bits, int rows, int cols, float* __restrict__ out) {
+    const long i = (long)blockIdx.x * 256 + threadIdx.x;
+    if (i >= (long)rows * cols) return;
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    float level, scale;
+    if (bits == 2) {
+        const uint32_t code = (codes[(size_t)r * (cols / 4) + c / 4] >> (2 * (c & 3))) & 3u;
+        level = code == 0 ? -1.510417f : (code == 1 ? -0.452780f : (code == 2 ? 0.452780f : 1.510417f));
+        scale = e4m3_to_f32(scales[(size_t)r * (cols / 32) + c / 32]);
+    } else {
+        level = ((codes[(size_t)r * (cols / 8) + c / 8] >> (c & 7)) & 1u) ? 1.0f : -1.0f;
+        scale = e4m3_to_f32(scales[(size_t)r * (cols / 64) + c / 64]);
+    }
+    out[i] += level * scale;
+}
+
+int launch_tail_add(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st) {
+    const int bits = which == 0 ? (L.tail_bits & 0xff) : ((L.tail_bits >> 8) & 0xff);
+    const int rows = which == 0 ? 2 * L.inter : L.hidden, cols = which == 0 ? L.hidden : L.inter;
+    const int blk = bits == 2 ? 32 : 64;
+    const uint8_t* codes = (which == 0 ? L.tail_gu_p : L.tail_dn_p) + (size_t)expert * rows * (cols * bits / 8);
+    const uint8_t* scales = (which == 0 ? L.tail_gu_s : L.tail_dn_s) + (size_t)expert * rows * (cols / blk);
+    const long n = (long)rows * cols;
+    tail_add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(codes, scales, bits, rows, cols, out);
+    return check_launch("tail_add");
+}
+
+}  // namespace chronos

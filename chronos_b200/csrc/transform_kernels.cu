@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(256) mid_act_kernel(chronos_layer_t L, Plan p)
                     }
                 }
                 zz[half][q] = fmaf(beta, zb[q], heal);
+                if (p.tail_gu) zz[half][q] += p.tail_gu[(size_t)pair * 2 * I + half * I + i0 + q];
             }
         }
 #pragma unroll
@@ -459,7 +460,9 @@ __global__ void __launch_bounds__(256) combine_kernel(chronos_layer_t L, Plan p,
                         heal = fmaf(hi.y, hp[3], heal);
                     }
                 }
-                out[q] = g * fmaf(beta, yb[q], heal);
+                float term = fmaf(beta, yb[q], heal);
+                if (p.tail_dn) term += p.tail_dn[(size_t)pos * H + row0 + q];
+                out[q] = g * term;
             }
             __syncwarp();
         }
@@ -533,6 +536,7 @@ __global__ void __launch_bounds__(256) down_term_kernel(chronos_layer_t L, Plan 
             }
         }
         out[q] = fmaf(beta, yb, heal);
+        if (p.tail_dn) out[q] += p.tail_dn[(size_t)pos * H + row0 + q];
     }
     *dst = make_float4(out[0], out[1], out[2], out[3]);
 }

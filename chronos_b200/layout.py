@@ -24,7 +24,7 @@ GROUP_TENSOR_SUFFIXES = (  # chronos_1t/models/glm53_holo.py:45-51
     "tail.gu_bits", "tail.gu_packed", "tail.gu_scale",
     "tail.down_bits", "tail.down_packed", "tail.down_scale",
 )
-_REQUIRED = GROUP_TENSOR_SUFFIXES[:12]  # the tail lattice is carried by the format but not read by this path
+_REQUIRED = GROUP_TENSOR_SUFFIXES[:12]  # the tail lattice tensors are optional (include_tail)
 
 
 @dataclass
@@ -130,9 +130,10 @@ class PackedLayer:
     """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
 
     def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device,
-                 fp4_images: bool = True):
+                 fp4_images: bool = True, tail_bits: tuple[int, int] = (0, 0)):
         cfg.validate()
         self.cfg = cfg
+        self.tail_bits = tuple(tail_bits) if "tail_gu_p" in tensors else (0, 0)
         self.fp4_images = fp4_images
         self.device = _norm_device(device)
         self.t = tensors
@@ -144,6 +145,7 @@ class PackedLayer:
         s.renorm = int(cfg.norm_topk_prob)
         s.routed_scaling = float(cfg.routed_scaling_factor)
         s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
+        s.tail_bits = self.tail_bits[0] | (self.tail_bits[1] << 8)
         self._add_fp4_images()
         if "v_dn" not in tensors and "v_dn_t" in tensors and self.device.type == "cuda":
             # healer.v_down in its on-disk orientation [E, r, I] beside the transposed copy: the tensor-core healer
@@ -220,9 +222,10 @@ class PackedLayer:
     @classmethod
     def from_groups(cls, cfg: FoldedLayerConfig, groups: Iterable[Mapping[str, Any]], router_w: Any = None,
                     e_bias: Any = None, shared: Mapping[str, Any] | None = None,
-                    device: torch.device | str = "cuda") -> "PackedLayer":
+                    device: torch.device | str = "cuda", include_tail: bool = False) -> "PackedLayer":
         """`groups[g]` maps the on-disk suffixes to tensors/arrays (fp8 either as float8_e4m3fn or raw uint8).
-        `shared` (optional) holds a plain-NVFP4 expert: `{gate,up,down}_proj.{weight,weight_scale,weight_scale_2}`."""
+        `shared` (optional) holds a plain-NVFP4 expert: `{gate,up,down}_proj.{weight,weight_scale,weight_scale_2}`.
+        `include_tail` also loads the tail lattice tensors and makes every call on the layer add the tail term."""
         device = _norm_device(device)
         groups = list(groups)
         if len(groups) != cfg.n_slots:
@@ -250,6 +253,21 @@ class PackedLayer:
             "u_dn": torch.cat([_u8(d["healer.u_down"]) for d in groups]),
             "v_dn_t": torch.cat([_u8(d["healer.v_down"]) for d in groups]).transpose(1, 2).contiguous(),
         }
+        if include_tail:
+            # the tail lattice (chronos_1t/models/glm53_holo.py:362-366): per expert a 2-bit Lloyd-Max (block 32) or 1-bit
+            # Rademacher (block 64) matrix with e4m3 block scales, added to the reconstruction in natural weight space
+            for d in groups:
+                for sfx in GROUP_TENSOR_SUFFIXES[12:]:
+                    if sfx not in d:
+                        raise ValueError(f"include_tail: a slot is missing tensor {sfx!r}")
+            bits = {(int(np.asarray(d["tail.gu_bits"]).reshape(-1)[0]), int(np.asarray(d["tail.down_bits"]).reshape(-1)[0])) for d in groups}
+            if len(bits) != 1 or not bits <= {(1, 1), (1, 2), (2, 1), (2, 2)}:
+                raise ValueError(f"include_tail: slots disagree on the tail bit widths or use unsupported ones: {sorted(bits)}")
+            t["tail_gu_p"] = torch.cat([_u8(d["tail.gu_packed"]) for d in groups])
+            t["tail_gu_s"] = torch.cat([_u8(d["tail.gu_scale"]) for d in groups])
+            t["tail_dn_p"] = torch.cat([_u8(d["tail.down_packed"]) for d in groups])
+            t["tail_dn_s"] = torch.cat([_u8(d["tail.down_scale"]) for d in groups])
+            tail_bits = next(iter(bits))
         if router_w is not None:
             t["router_w"] = _f32(router_w)
         if e_bias is not None:
@@ -262,7 +280,7 @@ class PackedLayer:
             t["sh_dn_s2"] = _f32(shared["down_proj.weight_scale_2"]).reshape(1)
         t = {n: v.to(device).contiguous() for n, v in t.items()}
         t.update(key_tables(cfg, device))
-        return cls(cfg, t, device)
+        return cls(cfg, t, device, tail_bits=tail_bits if include_tail else (0, 0))
 
     @classmethod
     def from_safetensors(cls, path: str | Path, cfg: FoldedLayerConfig, prefix: str, device: torch.device | str = "cuda",
@@ -291,7 +309,7 @@ class PackedLayer:
 
     @classmethod
     def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda",
-                  with_shared: bool = False) -> "PackedLayer":
+                  with_shared: bool = False, tail_bits: tuple[int, int] = (0, 0)) -> "PackedLayer":
         """Seeded random layer in the converter's byte format, generated on the device (for benchmarks: the real
         converter takes seconds per slot). Value ranges follow what the converter emits for N(0, 0.02) weights:
         uniform nibbles, e4m3 block-scale codes 0x58..0x77, scale_2 = amax / 2688, beta ~ 0.5, healer ~ N(0, 0.05)."""
@@ -303,8 +321,15 @@ class PackedLayer:
             t["e_bias"] = torch.zeros(cfg.router_experts, device=device)
         if with_shared:
             t.update(cls._random_shared_tensors(cfg, gen, device))
+        if tail_bits != (0, 0):  # random codes; block scales 0.004 .. 0.02, below the typical bank value
+            h, i, e = cfg.hidden, cfg.inter, cfg.n_experts
+            gb, db = tail_bits
+            t["tail_gu_p"] = torch.randint(0, 256, (e, 2 * i, h * gb // 8), generator=gen, device=device, dtype=torch.uint8)
+            t["tail_gu_s"] = torch.randint(0x02, 0x0C, (e, 2 * i, h // (32 if gb == 2 else 64)), generator=gen, device=device, dtype=torch.uint8)
+            t["tail_dn_p"] = torch.randint(0, 256, (e, h, i * db // 8), generator=gen, device=device, dtype=torch.uint8)
+            t["tail_dn_s"] = torch.randint(0x02, 0x0C, (e, h, i // (32 if db == 2 else 64)), generator=gen, device=device, dtype=torch.uint8)
         t.update(key_tables(cfg, device))
-        return cls(cfg, t, device)
+        return cls(cfg, t, device, tail_bits=tail_bits)
 
     @classmethod
     def synthetic_sharded(cls, cfg_global: FoldedLayerConfig, seed: int, slots: range, device: torch.device | str = "cuda",
@@ -382,6 +407,12 @@ class PackedLayer:
                 "healer.u_gu": t["u_gu"][sl], "healer.v_gu": t["v_gu"][sl], "healer.u_down": t["u_dn"][sl],
                 "healer.v_down": np.ascontiguousarray(t["v_dn_t"][sl].transpose(0, 2, 1)),
             })
+        if "tail_gu_p" in t:
+            for g in range(c.n_slots):
+                sl = slice(g * k, (g + 1) * k)
+                groups[g].update({"tail.gu_bits": np.uint8(self.tail_bits[0]), "tail.gu_packed": t["tail_gu_p"][sl],
+                                  "tail.gu_scale": t["tail_gu_s"][sl], "tail.down_bits": np.uint8(self.tail_bits[1]),
+                                  "tail.down_packed": t["tail_dn_p"][sl], "tail.down_scale": t["tail_dn_s"][sl]})
         # (the re-tiled FP4 images are derived data and are not exported)
         extras = {n: t[n] for n in ("router_w", "e_bias", "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2") if n in t}
         return groups, extras

@@ -79,6 +79,12 @@ extern "C" {
  * of nibbles in K-major core-matrix order followed by four 512-byte scale blocks (see chronos_b200_fp4_mma_probe):
  *   gu_t u8 [n_slots, 2I/128, H/256, 18432], dn_t u8 [n_slots, H/128, I/256, 18432], sh_gu_t / sh_dn_t without the
  *   slot axis.  A pure permutation of the "s_gu.weight" + "s_gu.weight_scale" bytes; the file format is untouched.
+ * Optional tail lattice (tail_bits != 0; chronos_1t/models/chronos_moe_block.py:122-229, applied at
+ *   chronos_1t/models/glm53_holo.py:362-366): per expert a matrix in natural weight space added to the reconstruction,
+ *   tail_gu_p u8 [n_experts, 2I, H*bits/8] "tail.gu_packed", tail_gu_s e4m3 [n_experts, 2I, H/32 (2-bit) | H/64 (1-bit)]
+ *   "tail.gu_scale", tail_dn_* the same with [H, I*bits/8] and [H, I/32 | I/64].  2-bit codes (4 per byte, column 4j in
+ *   bits 0-1) index the Lloyd-Max levels (-1.510417, -0.452780, 0.452780, 1.510417); 1-bit codes (8 per byte, column 8j
+ *   in bit 0) mean -1 / +1; the value is level * float(block scale).  With tail_bits set every entry point adds the term.
  * Optional: v_dn e4m3 [n_experts, r, I], "healer.v_down" exactly as on disk (kept beside its transposed copy); with it
  *   large batches run their healer products on the tensor cores.
  */
@@ -88,7 +94,7 @@ typedef struct chronos_layer {
     int32_t renorm;        /* sigmoid router: divide weights by their sum (norm_topk_prob) */
     float routed_scaling;  /* sigmoid router: routed_scaling_factor */
     int32_t shared_inter;
-    int32_t reserved_;
+    int32_t tail_bits;     /* 0 = no tail; else gate_up bits (1 or 2) | down bits << 8 */
     const float* router_w; /* [n_experts, H] */
     const float* e_bias;   /* [n_experts] or NULL (sigmoid router's e_score_correction_bias) */
     const uint8_t* gu_w; const uint8_t* gu_s; const float* gu_s2; const float* gu_beta;
@@ -100,6 +106,7 @@ typedef struct chronos_layer {
     const uint8_t* sh_dn_w; const uint8_t* sh_dn_s; const float* sh_dn_s2;
     const uint8_t* gu_t; const uint8_t* dn_t; const uint8_t* sh_gu_t; const uint8_t* sh_dn_t;
     const uint8_t* v_dn;
+    const uint8_t* tail_gu_p; const uint8_t* tail_gu_s; const uint8_t* tail_dn_p; const uint8_t* tail_dn_s;
 } chronos_layer_t;
 
 /* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated

@@ -83,6 +83,46 @@ def test_reconstruction_matches_reference(golden):
     assert seen == 2
 
 
+def test_reconstruction_with_tail_matches_reference(golden):
+    """Weight-space probe with the tail lattice term (2-bit Lloyd-Max and 1-bit Rademacher cases) against the
+    reference's reconstruct_group_experts(include_tail=True)."""
+    from chronos_b200 import codec
+
+    h, i, e, k = (int(v) for v in golden["meta"][:4])
+    groups = golden_groups(golden)
+    seen = 0
+    for key in golden:
+        if not key.startswith("ref.recon_tail.") or not key.endswith(".gu"):
+            continue
+        _, gs, ms, _ = key[len("ref.recon_"):].split(".")
+        g, m = int(gs[1:]), int(ms[1:])
+        gt = {s: torch.from_numpy(np.ascontiguousarray(v)) for s, v in groups[g].items()}
+        gu, dn = codec.reconstruct_group_experts(gt, g, [m], h, i, include_tail=True)[0]
+        for got, ref in ((gu, golden[key]), (dn, golden[key[:-3] + ".down"])):
+            err = np.abs(got.cpu().numpy() - ref).max()
+            assert err <= 4e-6 * max(1.0, np.abs(ref).max()), (key, err)
+        seen += 1
+    assert seen == 1
+
+
+@pytest.mark.parametrize("regime,n_tok,tails", [("auto", 5, (2, 2)), ("auto", 5, (1, 2)), ("stream", 7, (2, 1)), ("tensor", 90, (2, 2)),
+                                                ("tensor_fp4", 90, (1, 1)), ("tensor_fp4", 150, (2, 2))])
+def test_layer_with_tail_matches_oracle(regime, n_tok, tails):
+    """Whole layer with the tail lattice term in every regime against the fp32 oracle (include_tail=True)."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=32, top_k=2)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=21, with_shared=True, tail_bits=tails), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(n_tok)
+    x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    y = layer.forward_impl(x, regime=regime)
+    assert layer.device_status() == 0
+    ref, _, _ = _oracle_layer(layer, x.float().cpu().numpy(), include_tail=True)
+    ref0, _, _ = _oracle_layer(layer, x.float().cpu().numpy(), include_tail=False)
+    assert _rel_l2(ref0, ref) > 5e-2, "the synthetic tail must matter, or the test proves nothing"
+    assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL
+
+
 def test_router_matches_reference_and_oracle(golden):
     top_k = int(golden["meta"][5])
     x = torch.from_numpy(golden["x"]).cuda()
@@ -130,7 +170,7 @@ def test_layer_output_matches_reference(golden):
         assert _rel_l2(yb.float().cpu().numpy(), ref_b) <= LAYER_TOL, flavour
 
 
-def _oracle_layer(layer, x_np, with_shared=True):
+def _oracle_layer(layer, x_np, with_shared=True, include_tail=False):
     groups, extras = layer.packed.to_groups_numpy()
     c = layer.cfg
     shared = None
@@ -141,7 +181,7 @@ def _oracle_layer(layer, x_np, with_shared=True):
         shared = (np.concatenate([gate, up]), O.unpack_nvfp4(extras["sh_dn_w"], extras["sh_dn_s"], extras["sh_dn_s2"][0]))
     return O.moe_layer_forward(x_np, groups, extras["router_w"], c.top_k, c.hidden, c.inter, c.group_size, router=c.router,
                                e_bias=extras.get("e_bias"), routed_scaling=c.routed_scaling_factor, shared=shared,
-                               return_routing=True)
+                               include_tail=include_tail, return_routing=True)
 
 
 def test_config0_layer_with_folded_weights():
