@@ -6,9 +6,10 @@
 // tail_pass_kernel streams an expert's tail rows once per group of 8 of its pairs and multiplies them by the pairs'
 // activations on the tensor cores (mma.sync m16n8k16, fp16): out[pair, row] = g_pair * sum_k T[e, row, k] * x16[pair, k],
 // x16 = activations / g_pair in fp16. The consumers (SwiGLU kernel, combine kernel) add the term where they add the healer.
-// A warp owns 16 rows; lane (g = lane / 4, q = lane % 4) owns rows g, g + 8 and, per 64-column step, the 16 contiguous
-// columns 16 q .. 16 q + 15 (4 bytes of 2-bit codes or 2 bytes of sign bits per row): any permutation of the
-// contraction index is legal as long as both operands use it, so MMA step s takes columns 16 q + 4 s .. + 3.
+// A warp owns 16 rows; lane (g = lane / 4, q = lane % 4) owns rows g, g + 8 and, per 256-column step, the 64 contiguous
+// columns 64 q .. 64 q + 63 (16 bytes of 2-bit codes or 8 bytes of sign bits per row, one vector load): any permutation
+// of the contraction index is legal as long as both operands use it, so MMA step s of the 16 takes columns
+// 64 q + 4 s .. + 3. Widths that are not a multiple of 256 finish with 64-column steps (16 columns per lane).
 #include "common.cuh"
 
 namespace chronos {
@@ -49,13 +50,43 @@ struct TailArgs {
     int R, K, n_experts;
 };
 
+// Shared-memory image of the 8 activation rows: every 64-column segment (128 bytes) is followed by 8 bytes of padding
+// and rows are 32 bytes (mod 128) apart, so the fragment loads of a warp (8 rows x 4 segments, 8 bytes each) spread over
+// the banks as evenly as 256 bytes can.
+__host__ __device__ inline int tail_xrow_bytes(int K) {
+    const int len = (K / 64) * 136;
+    return len + ((32 - len % 128) + 128) % 128;
+}
+__device__ __forceinline__ int tail_xoff(int k) { return (k >> 6) * 136 + (k & 63) * 2; }
+
+template <int BITS>
+__device__ __forceinline__ void tail_step4(float (&d)[4], uint32_t w_lo, uint32_t w_hi, uint32_t f_lo, uint32_t f_hi,
+                                           const uint8_t* xrow, int k, int s) {
+    // w_*: the codes of 4 columns of rows g / g + 8 in the low bits; k: first of the 4 columns
+    uint32_t a0, a1, a2, a3;
+    if (BITS == 2) {
+        a0 = lloyd2_pair(w_lo); a2 = lloyd2_pair(w_lo >> 4);
+        a1 = lloyd2_pair(w_hi); a3 = lloyd2_pair(w_hi >> 4);
+    } else {
+        a0 = sign_pair(w_lo); a2 = sign_pair(w_lo >> 2);
+        a1 = sign_pair(w_hi); a3 = sign_pair(w_hi >> 2);
+    }
+    a0 = hmul2_u32(a0, f_lo); a2 = hmul2_u32(a2, f_lo);
+    a1 = hmul2_u32(a1, f_hi); a3 = hmul2_u32(a3, f_hi);
+    const uint2 b = *reinterpret_cast<const uint2*>(xrow + tail_xoff(k));
+    mma_16816_t(d, a0, a1, a2, a3, b.x, b.y);
+    (void)s;
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
-    extern __shared__ __align__(16) uint8_t tsm[];  // 8 activation rows of K fp16 (+ 8 bytes of padding per row)
+    extern __shared__ __align__(16) uint8_t tsm[];  // 8 activation rows of K fp16, padded (tail_xrow_bytes)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
     const int R = a.R, K = a.K, RB = R / 128;
-    const int xstride = K * 2 + 8;
+    const int xstride = tail_xrow_bytes(K);
     constexpr int BLK = BITS == 2 ? 32 : 64;
+    constexpr int CB = BITS == 2 ? 16 : 8;  // code bytes per lane per 256-column step
+    const int K256 = K & ~255;
     const long n_tiles = (long)a.counters[3] * RB;
     const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
     int cur_item = -1, cur_chunk = -1;
@@ -93,8 +124,7 @@ __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
                             v.z = *reinterpret_cast<const uint32_t*>(&h2); v.w = *reinterpret_cast<const uint32_t*>(&h3);
                         }
                     }
-                    // rows are 8 bytes out of phase so that the 8 pairs of a fragment load hit different banks
-                    uint2* dst = reinterpret_cast<uint2*>(tsm + (size_t)n * xstride + (size_t)k * 2);
+                    uint2* dst = reinterpret_cast<uint2*>(tsm + (size_t)n * xstride + tail_xoff(k));  // 8 columns stay inside a segment
                     dst[0] = make_uint2(v.x, v.y);
                     dst[1] = make_uint2(v.z, v.w);
                 }
@@ -103,38 +133,52 @@ __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
                 cur_chunk = chunk;
             }
             float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const uint8_t* xrow = tsm + (size_t)g * xstride + (size_t)(16 * q) * 2;
-#pragma unroll 4
-            for (int k0 = 0; k0 < K; k0 += 64) {
-                uint32_t w_lo, w_hi, sc_lo, sc_hi;
+            const uint8_t* xrow = tsm + (size_t)g * xstride;
+            // 256-column steps: one 16-byte (8-byte) vector of codes and the 2 (1) scale bytes per row and lane
+#pragma unroll 2
+            for (int k0 = 0; k0 < K256; k0 += 256) {
+                uint32_t wl[4], wh[4];
+                if (BITS == 2) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(c_lo + k0 / 4 + CB * q), v = *reinterpret_cast<const uint4*>(c_hi + k0 / 4 + CB * q);
+                    wl[0] = u.x; wl[1] = u.y; wl[2] = u.z; wl[3] = u.w;
+                    wh[0] = v.x; wh[1] = v.y; wh[2] = v.z; wh[3] = v.w;
+                } else {
+                    const uint2 u = *reinterpret_cast<const uint2*>(c_lo + k0 / 8 + CB * q), v = *reinterpret_cast<const uint2*>(c_hi + k0 / 8 + CB * q);
+                    wl[0] = u.x & 0xffffu; wl[1] = u.x >> 16; wl[2] = u.y & 0xffffu; wl[3] = u.y >> 16;
+                    wh[0] = v.x & 0xffffu; wh[1] = v.x >> 16; wh[2] = v.y & 0xffffu; wh[3] = v.y >> 16;
+                }
+                uint32_t fl[2], fh[2];
+                if (BITS == 2) {  // two blocks of 32 inside the lane's 64 columns
+                    const uint32_t sl = *reinterpret_cast<const uint16_t*>(s_lo + k0 / 32 + 2 * q), sh = *reinterpret_cast<const uint16_t*>(s_hi + k0 / 32 + 2 * q);
+                    fl[0] = e4m3_to_f16x2_dup(sl & 0xffu); fl[1] = e4m3_to_f16x2_dup(sl >> 8);
+                    fh[0] = e4m3_to_f16x2_dup(sh & 0xffu); fh[1] = e4m3_to_f16x2_dup(sh >> 8);
+                } else {
+                    fl[0] = fl[1] = e4m3_to_f16x2_dup(s_lo[k0 / 64 + q]);
+                    fh[0] = fh[1] = e4m3_to_f16x2_dup(s_hi[k0 / 64 + q]);
+                }
+#pragma unroll
+                for (int s = 0; s < 16; ++s) {  // word s / 4 holds the codes of columns 16 (s / 4) .. + 15 of the lane's run
+                    const int sh = (s & 3) * (BITS == 2 ? 8 : 4);
+                    tail_step4<BITS>(d, wl[s >> 2] >> sh, wh[s >> 2] >> sh, fl[s >> 3], fh[s >> 3], xrow, k0 + 64 * q + 4 * s, s);
+                }
+            }
+            for (int k0 = K256; k0 < K; k0 += 64) {  // remainder: 16 columns per lane
+                uint32_t w_lo, w_hi, f_lo, f_hi;
                 if (BITS == 2) {
                     w_lo = *reinterpret_cast<const uint32_t*>(c_lo + k0 / 4 + 4 * q);
                     w_hi = *reinterpret_cast<const uint32_t*>(c_hi + k0 / 4 + 4 * q);
-                    sc_lo = s_lo[k0 / 32 + (q >> 1)];
-                    sc_hi = s_hi[k0 / 32 + (q >> 1)];
+                    f_lo = e4m3_to_f16x2_dup(s_lo[k0 / 32 + (q >> 1)]);
+                    f_hi = e4m3_to_f16x2_dup(s_hi[k0 / 32 + (q >> 1)]);
                 } else {
                     w_lo = *reinterpret_cast<const uint16_t*>(c_lo + k0 / 8 + 2 * q);
                     w_hi = *reinterpret_cast<const uint16_t*>(c_hi + k0 / 8 + 2 * q);
-                    sc_lo = s_lo[k0 / 64];
-                    sc_hi = s_hi[k0 / 64];
+                    f_lo = e4m3_to_f16x2_dup(s_lo[k0 / 64]);
+                    f_hi = e4m3_to_f16x2_dup(s_hi[k0 / 64]);
                 }
-                const uint32_t f_lo = e4m3_to_f16x2_dup(sc_lo), f_hi = e4m3_to_f16x2_dup(sc_hi);
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    uint32_t a0, a1, a2, a3;
-                    if (BITS == 2) {
-                        const uint32_t b_lo = w_lo >> (8 * s), b_hi = w_hi >> (8 * s);
-                        a0 = lloyd2_pair(b_lo); a2 = lloyd2_pair(b_lo >> 4);
-                        a1 = lloyd2_pair(b_hi); a3 = lloyd2_pair(b_hi >> 4);
-                    } else {
-                        const uint32_t b_lo = w_lo >> (4 * s), b_hi = w_hi >> (4 * s);
-                        a0 = sign_pair(b_lo); a2 = sign_pair(b_lo >> 2);
-                        a1 = sign_pair(b_hi); a3 = sign_pair(b_hi >> 2);
-                    }
-                    a0 = hmul2_u32(a0, f_lo); a2 = hmul2_u32(a2, f_lo);
-                    a1 = hmul2_u32(a1, f_hi); a3 = hmul2_u32(a3, f_hi);
-                    const uint2 b = *reinterpret_cast<const uint2*>(xrow + (size_t)(k0 + 4 * s) * 2);
-                    mma_16816_t(d, a0, a1, a2, a3, b.x, b.y);
+                    const int sh = s * (BITS == 2 ? 8 : 4);
+                    tail_step4<BITS>(d, w_lo >> sh, w_hi >> sh, f_lo, f_hi, xrow, k0 + 16 * q + 4 * s, s);
                 }
             }
 #pragma unroll
@@ -163,7 +207,7 @@ int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_d
     a.R = stage == 0 ? 2 * L.inter : L.hidden;
     a.K = stage == 0 ? L.hidden : L.inter;
     a.n_experts = L.n_experts;
-    const size_t smem = (size_t)8 * (a.K * 2 + 8);
+    const size_t smem = (size_t)8 * tail_xrow_bytes(a.K);
     if (smem > 200 * 1024) {
         set_error("tail_pass: %d columns need %zu bytes of shared memory", a.K, smem);
         return CHRONOS_E_SHAPE;
@@ -172,7 +216,7 @@ int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_d
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long max_tiles = (long)p.max_gitems * (a.R / 128);
-    const long resident = (long)sms * (smem * 3 <= 200 * 1024 ? 3 : (smem * 2 <= 200 * 1024 ? 2 : 1));
+    const long resident = (long)sms * (smem * 3 <= 222 * 1024 ? 3 : (smem * 2 <= 222 * 1024 ? 2 : 1));
     const unsigned grid = (unsigned)(max_tiles < resident ? max_tiles : resident);
     cudaError_t rc = bits == 2 ? cudaFuncSetAttribute(tail_pass_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
                                : cudaFuncSetAttribute(tail_pass_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
