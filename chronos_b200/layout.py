@@ -284,7 +284,7 @@ class PackedLayer:
 
     @classmethod
     def from_safetensors(cls, path: str | Path, cfg: FoldedLayerConfig, prefix: str, device: torch.device | str = "cuda",
-                         shared_prefix: str | None = None) -> "PackedLayer":
+                         shared_prefix: str | None = None, include_tail: bool = False) -> "PackedLayer":
         """Reads `{prefix}.chronos_groups.{g}.{suffix}` (chronos_1t/models/glm53_chronos_spec.py:186-191) and
         `{prefix}.gate.weight` (+ `.gate.e_score_correction_bias`) from a converter shard."""
         from safetensors import safe_open
@@ -297,7 +297,8 @@ class PackedLayer:
                 missing = [s for s in _REQUIRED if gp + s not in names]
                 if missing:
                     raise ValueError(f"{path}: slot {g} is missing {missing}")
-                groups.append({s: fh.get_tensor(gp + s) for s in _REQUIRED})
+                want = GROUP_TENSOR_SUFFIXES if include_tail else _REQUIRED
+                groups.append({s: fh.get_tensor(gp + s) for s in want if gp + s in names})
             router_w = fh.get_tensor(f"{prefix}.gate.weight") if f"{prefix}.gate.weight" in names else None
             bias_key = f"{prefix}.gate.e_score_correction_bias"
             e_bias = fh.get_tensor(bias_key) if bias_key in names else None
@@ -305,7 +306,7 @@ class PackedLayer:
             if shared_prefix is not None and f"{shared_prefix}.gate_proj.weight" in names:
                 shared = {f"{p}.{s}": fh.get_tensor(f"{shared_prefix}.{p}.{s}")
                           for p in ("gate_proj", "up_proj", "down_proj") for s in ("weight", "weight_scale", "weight_scale_2")}
-        return cls.from_groups(cfg, groups, router_w, e_bias, shared, device)
+        return cls.from_groups(cfg, groups, router_w, e_bias, shared, device, include_tail=include_tail)
 
     @classmethod
     def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda",
