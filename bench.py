@@ -265,7 +265,7 @@ def run_decode(args) -> dict:
                    "top8_overlap_within_stream": round(statistics.mean(s["overlap"] for s in stats), 3)},
         "e2e": {"value": n_tok / (ms_e2e * 1e-3 / K), "unit": "tokens/s", "h2d_bytes_per_step": n_tok * cfg.hidden * 2,
                 "d2h_bytes_per_step": n_tok * cfg.hidden * 2},
-        "gpu_launches": 9 * K,
+        "gpu_launches": (8 + (2 if args.tail else 0) + (1 if args.tail else 0)) * K,  # router, plan(+top-k), input transform, 2 bank passes, SwiGLU, down transform, combine (+ fp16 image, 2 tail passes)
         "clocks": clocks,
         "roofline": {"bound": "hbm", "kernel": f"{bank_kernel} (gate_up pass)", "achieved": gu_gbs, "peak": peak,
                      "peak_kind": f"of {peak_kind}", "unit": "GB/s", "frac": gu_gbs / peak,
@@ -295,8 +295,11 @@ def run_prefill(args) -> dict:
     cuda_build.build()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cfg = FoldedLayerConfig(**DECODE)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, device=dev, with_shared=True), register=False)
+    ceiling = args.workload == "fp4_ceiling"
+    # fp4_ceiling: the same kernels on ONE slot (4 experts, every token routed to all 4): banks and activation images
+    # stay in L2, work items are all full - an empirical ceiling for this tile shape, not a workload of the reference
+    cfg = FoldedLayerConfig(**{**DECODE, **({"n_experts": 4, "top_k": 4} if ceiling else {})})
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, device=dev, with_shared=not ceiling), register=False)
     n_tok = args.tokens
     regime = args.regime or "tensor_fp4"
     gen = torch.Generator(device=dev).manual_seed(2)
@@ -307,8 +310,9 @@ def run_prefill(args) -> dict:
     perm = torch.randperm(cfg.n_experts, generator=torch.Generator().manual_seed(2))
     p_e = (torch.arange(1, cfg.n_experts + 1, dtype=torch.float64) ** -1.1)
     p_e = (p_e / p_e.sum())[torch.argsort(perm)]
-    layer.packed.t["router_w"][:, 0] = (1.0 * torch.log(p_e)).to(torch.float32).to(dev)
-    x[:, 0] = 1.0
+    if not ceiling:
+        layer.packed.t["router_w"][:, 0] = (1.0 * torch.log(p_e)).to(torch.float32).to(dev)
+        x[:, 0] = 1.0
     ids = layer.route(x)[0]
     counts = torch.bincount(ids.reshape(-1).long(), minlength=cfg.n_experts).cpu().numpy()
     K, W = max(args.steps // 20, 3), 3
@@ -341,8 +345,9 @@ def run_prefill(args) -> dict:
     pairs = n_tok * cfg.top_k
     bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
     healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
-    useful = pairs * (bank_flops + healer_flops) + n_tok * bank_flops
-    gemm_flops = (pairs + n_tok) * bank_flops
+    n_sh = 0 if ceiling else n_tok
+    useful = pairs * (bank_flops + healer_flops) + n_sh * bank_flops
+    gemm_flops = (pairs + n_sh) * bank_flops
     gemm_s = (stage_us["gu_bank_pass"] + stage_us["dn_bank_pass"]) * 1e-6
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -367,9 +372,9 @@ def run_prefill(args) -> dict:
         "metric": "folded_moe_prefill_tokens_per_s", "value": n_tok / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": dtype, "data": "synthetic",
-        "config": {"workload": "prefill_layer", "regime": regime, "tokens": n_tok, "hidden": cfg.hidden, "routed_experts": cfg.n_experts,
+        "config": {"workload": "fp4_ceiling_one_slot" if ceiling else "prefill_layer", "regime": regime, "tokens": n_tok, "hidden": cfg.hidden, "routed_experts": cfg.n_experts,
                    "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
-                   "router_popularity": "Zipf(1.1)", "pairs_per_expert_max": int(counts.max()), "pairs_per_expert_median": float(np.median(counts)),
+                   "router_popularity": "all tokens to all 4 experts" if ceiling else "Zipf(1.1)", "pairs_per_expert_max": int(counts.max()), "pairs_per_expert_median": float(np.median(counts)),
                    "pairs_per_expert_min": int(counts.min())},
         "useful_tflops_layer": useful / (ms * 1e-3) / 1e12,
         "roofline": roof,
@@ -480,7 +485,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--workload", default=None, choices=(None, "decode", "ep_stack", "prefill", "sweep"))
+    ap.add_argument("--workload", default=None, choices=(None, "decode", "ep_stack", "prefill", "sweep", "fp4_ceiling"))
     ap.add_argument("--tokens", type=int, default=8192, help="tokens of the prefill workload")
     ap.add_argument("--regime", default=None, choices=(None, "auto", "tensor", "tensor_fp4"), help="bank-pass regime of the prefill workload")
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
@@ -495,9 +500,9 @@ def main() -> None:
             print(json.dumps(run_reference(args)), flush=True)
         return
     workload = args.workload or ("decode" if args.gpus == 1 and world == 1 else "ep_stack")
-    if workload in ("decode", "prefill", "sweep"):
+    if workload in ("decode", "prefill", "sweep", "fp4_ceiling"):
         if rank == 0:
-            fn = {"decode": run_decode, "prefill": run_prefill, "sweep": run_sweep}[workload]
+            fn = {"decode": run_decode, "prefill": run_prefill, "sweep": run_sweep, "fp4_ceiling": run_prefill}[workload]
             print(json.dumps(fn(args)), flush=True)
         return
     from chronos_b200 import ep_bench

@@ -77,6 +77,25 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
             for name, a, b in lay.phase_events:
                 phase_us[name] = phase_us.get(name, 0.0) + 1e3 * a.elapsed_time(b) / n_layers
             lay.phase_events = None
+        # bank passes of one layer on this rank (stage events inside the C ABI call) -> roofline of the dominant kernel
+        import ctypes
+
+        from . import _lib
+        lay0 = layers[0]
+        ids0, _ = lay0.route_fn(h0)
+        ids_all = torch.empty((world * tl, cfg.top_k), dtype=ids0.dtype, device=dev)
+        dist.all_gather_into_tensor(ids_all, ids0.contiguous())
+        owned = int(((ids_all >= lay0.first_expert) & (ids_all < lay0.first_expert + lay0.n_local)).sum().item())
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        for ev in evs:
+            ev.record(st)
+        torch.cuda.synchronize()
+        arr = (ctypes.c_void_p * 8)(*[ev.cuda_event for ev in evs])
+        _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, 8))
+        lay0(h0)
+        _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
+        torch.cuda.synchronize()
+        gemm_ms = evs[3].elapsed_time(evs[4]) + evs[5].elapsed_time(evs[6])
         step_s = float(ms.item()) * 1e-3 / K
         pairs = tokens * cfg.top_k
         bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
@@ -100,6 +119,11 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
             "gpu_launches": launches_per_layer * n_layers * K,
             "clocks": clocks,
             "useful_tflops": useful / step_s / 1e12,
+            "roofline": {"bound": "tensor", "kernel": "bank_fp4_wide_kernel (both passes of one layer, rank 0)",
+                         "achieved": (owned + tl) * bank_flops / (gemm_ms * 1e-3) / 1e12, "peak": 9000.0,
+                         "peak_kind": "nominal dense FP4 (datasheet; not in MEASURED_PEAKS.json); the pipe issues 3x the useful FLOPs",
+                         "unit": "TFLOP/s", "frac": (owned + tl) * bank_flops / (gemm_ms * 1e-3) / 1e12 / 9000.0, "traffic": None,
+                         "pairs_on_rank0": owned + tl, "bank_pass_ms": gemm_ms},
             "phase_us_per_layer_rank0": {k_: round(v, 1) for k_, v in phase_us.items()},
             "device_status": status,
         }
