@@ -26,14 +26,14 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot /*[kPla
     if (lane == 31) warp_tot[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        const int w = warp_tot[lane];
+        const int w = lane < kPlanWarps ? warp_tot[lane] : 0;  // fewer than 32 warps: the other lanes scan zeros
         int winc = w;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
             const int o = __shfl_up_sync(0xffffffffu, winc, d);
             if (lane >= d) winc += o;
         }
-        warp_tot[lane] = winc - w;  // exclusive prefix of the warp totals
+        if (lane < kPlanWarps) warp_tot[lane] = winc - w;  // exclusive prefix of the warp totals
         if (lane == 31) warp_tot[kPlanWarps] = winc;
     }
     __syncthreads();
