@@ -374,6 +374,37 @@ def test_tensor_fp4_regime_whole_layer(scale):
     assert _rel_l2(y16.float().cpu().numpy(), ref) <= LAYER_TOL
 
 
+def test_large_batch_without_optional_copies_and_shared_expert_range():
+    """A layer description without the optional load-time copies (FP4 stage images, healer.v_down as on disk) takes the
+    fp16 tensor regime with the CUDA-core healer kernels; and the shared expert can be limited to a block of tokens
+    (what an expert-parallel rank does for the tokens it is the home of)."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=32, top_k=2)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=17, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(120, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    ids, w = layer.route(x)
+    y_all = layer.routed_forward(x, ids, w, with_shared=True, out_dtype=torch.float32)
+    y_none = layer.routed_forward(x, ids, w, with_shared=False, out_dtype=torch.float32)
+    y_rng = layer.routed_forward(x, ids, w, out_dtype=torch.float32, shared_range=(40, 50))
+    assert layer.device_status() == 0
+    assert torch.equal(y_rng[:40], y_none[:40]) and torch.equal(y_rng[90:], y_none[90:])
+    assert torch.equal(y_rng[40:90], y_all[40:90])
+    with pytest.raises(Exception):
+        layer.routed_forward(x, ids, w, shared_range=(100, 50))  # runs past the last token
+    ref, _, _ = _oracle_layer(layer, x.float().cpu().numpy())
+    assert _rel_l2(y_all.cpu().numpy(), ref) <= LAYER_TOL
+    # strip the optional copies from the struct: same answer from the fallback kernels
+    st = layer.packed.struct
+    for name in ("gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn"):
+        setattr(st, name, None)
+    y_fb = layer.routed_forward(x, ids, w, with_shared=True, out_dtype=torch.float32)
+    assert layer.device_status() == 0
+    assert _rel_l2(y_fb.cpu().numpy(), ref) <= LAYER_TOL
+    assert _rel_l2(y_fb.cpu().numpy(), y_all.cpu().numpy()) <= 3e-3
+
+
 @pytest.mark.parametrize("n_stages,b_rows", [(1, 32), (3, 32), (2, 192), (1, 256), (1, 64)])
 def test_fp4_tensor_core_operand_format(n_stages, b_rows):
     """tcgen05 block-scaled FP4 MMA on re-tiled operand images == dequantise-and-multiply of the same bytes."""

@@ -105,6 +105,64 @@ def test_packed_layer_validation_on_cpu(golden):
         PackedLayer.from_groups(cfg, bad, device="cpu")
 
 
+def test_tail_tensors_load_and_round_trip_on_cpu(tmp_path, golden):
+    """include_tail stacks the tail lattice tensors per expert, records the bit widths in the struct, and the loader
+    reads them from a converter shard; the oracle's view of the layer (to_groups_numpy) carries them back unchanged."""
+    from safetensors.torch import save_file
+
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    cfg = FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k)
+    groups = golden_groups(golden)
+    gb, db = int(np.asarray(groups[0]["tail.gu_bits"]).reshape(-1)[0]), int(np.asarray(groups[0]["tail.down_bits"]).reshape(-1)[0])
+    layer = PackedLayer.from_groups(cfg, groups, golden["router_w"], device="cpu", include_tail=True)
+    assert layer.tail_bits == (gb, db) and layer.struct.tail_bits == (gb | (db << 8))
+    assert tuple(layer.t["tail_gu_p"].shape) == (e, 2 * i, h * gb // 8)
+    assert tuple(layer.t["tail_dn_s"].shape) == (e, h, i // (32 if db == 2 else 64))
+    back, _ = layer.to_groups_numpy()
+    assert np.array_equal(back[1]["tail.gu_packed"], groups[1]["tail.gu_packed"])
+    assert np.array_equal(back[1]["tail.down_scale"], groups[1]["tail.down_scale"])
+    plain = PackedLayer.from_groups(cfg, groups, golden["router_w"], device="cpu")
+    assert plain.tail_bits == (0, 0) and plain.struct.tail_bits == 0 and "tail_gu_p" not in plain.t
+    bad = [dict(g) for g in groups]
+    del bad[0]["tail.down_packed"]
+    with pytest.raises(ValueError, match="include_tail"):
+        PackedLayer.from_groups(cfg, bad, device="cpu", include_tail=True)
+    prefix = "model.layers.0.mlp"
+    tensors = {}
+    for g, grp in enumerate(groups):
+        for sfx, arr in grp.items():
+            tensors[f"{prefix}.chronos_groups.{g}.{sfx}"] = torch.from_numpy(np.ascontiguousarray(arr)).reshape(np.asarray(arr).shape)
+    tensors[f"{prefix}.gate.weight"] = torch.from_numpy(golden["router_w"])
+    path = tmp_path / "chronos-glm53-layer-00000-of-00001.safetensors"
+    save_file(tensors, str(path))
+    loaded = PackedLayer.from_safetensors(path, cfg, prefix, device="cpu", include_tail=True)
+    for n in layer.t:
+        assert torch.equal(loaded.t[n], layer.t[n]), n
+
+
+def test_fp4_stage_image_tiler_layout():
+    """tile_matrix_fp4 is a pure byte permutation into the documented stage-image layout, for 32, 128 and 192 rows."""
+    from chronos_b200.fp4_layout import tile_matrix_fp4
+
+    g = torch.Generator().manual_seed(0)
+    for rows in (32, 128, 192):
+        p = torch.randint(0, 256, (rows, 256), dtype=torch.uint8, generator=g)   # K = 512: two stages
+        s = torch.randint(0, 256, (rows, 32), dtype=torch.uint8, generator=g)
+        img = tile_matrix_fp4(p, s, rows)
+        nblk = (rows + 127) // 128
+        assert tuple(img.shape) == (1, 2, rows * 128 + 2048 * nblk)
+        for st in (0, 1):
+            for r in (0, rows // 2 + 1, rows - 1):
+                for c in (0, 3, 7):
+                    for b in (0, 9, 15):
+                        assert img[0, st, c * rows * 16 + r * 16 + b] == p[r, st * 128 + c * 16 + b]
+                for j in range(4):
+                    for si in range(4):
+                        off = rows * 128 + j * 512 * nblk + (r // 128) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + si
+                        assert img[0, st, off] == s[r, st * 16 + j * 4 + si]
+        assert sorted(img[0, :, : rows * 128].reshape(-1).tolist()) == sorted(p.reshape(-1).tolist())
+
+
 def test_no_cpu_compute_path(golden):
     h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
     cfg = FoldedLayerConfig(hidden=h, inter=i, n_experts=e, group_size=k, rank=r, top_k=top_k)
