@@ -59,31 +59,44 @@ __host__ __device__ inline int tail_xrow_bytes(int K) {
 }
 __device__ __forceinline__ int tail_xoff(int k) { return (k >> 6) * 136 + (k & 63) * 2; }
 
+// Code -> fp16 table in shared memory: entry = the 4 values of one code byte (2-bit: 256 entries) or nibble (1-bit: 16
+// entries) as two fp16 pairs, 16 copies side by side (entry stride 128 bytes, copy = lane % 16) so that the 32 lookups
+// of a warp touch every bank exactly twice - the floor for 256 bytes. One lookup replaces ~12 integer instructions.
+template <int BITS>
+__device__ __forceinline__ void tail_table_fill(uint8_t* tab, int tid, int nthreads) {
+    constexpr int N = BITS == 2 ? 256 : 16;
+    for (int i = tid; i < N * 16; i += nthreads) {
+        const uint32_t code = (uint32_t)(i >> 4);
+        uint2 v;
+        if (BITS == 2) { v.x = lloyd2_pair(code); v.y = lloyd2_pair(code >> 4); }
+        else { v.x = sign_pair(code); v.y = sign_pair(code >> 2); }
+        *reinterpret_cast<uint2*>(tab + (size_t)code * 128 + (i & 15) * 8) = v;
+    }
+}
+
 template <int BITS>
 __device__ __forceinline__ void tail_step4(float (&d)[4], uint32_t w_lo, uint32_t w_hi, uint32_t f_lo, uint32_t f_hi,
-                                           const uint8_t* xrow, int k, int s) {
+                                           const uint8_t* xrow, const uint8_t* tab_lane, int k) {
     // w_*: the codes of 4 columns of rows g / g + 8 in the low bits; k: first of the 4 columns
-    uint32_t a0, a1, a2, a3;
-    if (BITS == 2) {
-        a0 = lloyd2_pair(w_lo); a2 = lloyd2_pair(w_lo >> 4);
-        a1 = lloyd2_pair(w_hi); a3 = lloyd2_pair(w_hi >> 4);
-    } else {
-        a0 = sign_pair(w_lo); a2 = sign_pair(w_lo >> 2);
-        a1 = sign_pair(w_hi); a3 = sign_pair(w_hi >> 2);
-    }
-    a0 = hmul2_u32(a0, f_lo); a2 = hmul2_u32(a2, f_lo);
-    a1 = hmul2_u32(a1, f_hi); a3 = hmul2_u32(a3, f_hi);
+    constexpr uint32_t M = BITS == 2 ? 0xffu : 0xfu;
+    const uint2 lo = *reinterpret_cast<const uint2*>(tab_lane + (size_t)(w_lo & M) * 128);
+    const uint2 hi = *reinterpret_cast<const uint2*>(tab_lane + (size_t)(w_hi & M) * 128);
+    const uint32_t a0 = hmul2_u32(lo.x, f_lo), a2 = hmul2_u32(lo.y, f_lo);
+    const uint32_t a1 = hmul2_u32(hi.x, f_hi), a3 = hmul2_u32(hi.y, f_hi);
     const uint2 b = *reinterpret_cast<const uint2*>(xrow + tail_xoff(k));
     mma_16816_t(d, a0, a1, a2, a3, b.x, b.y);
-    (void)s;
 }
 
 template <int BITS>
 __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
-    extern __shared__ __align__(16) uint8_t tsm[];  // 8 activation rows of K fp16, padded (tail_xrow_bytes)
+    extern __shared__ __align__(128) uint8_t tsm_all[];  // [code table][8 activation rows of K fp16, padded (tail_xrow_bytes)]
+    constexpr int TAB = (BITS == 2 ? 256 : 16) * 128;
+    uint8_t* tsm = tsm_all + TAB;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
     const int R = a.R, K = a.K, RB = R / 128;
     const int xstride = tail_xrow_bytes(K);
+    tail_table_fill<BITS>(tsm_all, tid, 256);  // visible after the first staging barrier below
+    const uint8_t* tab_lane = tsm_all + (lane & 15) * 8;
     constexpr int BLK = BITS == 2 ? 32 : 64;
     constexpr int CB = BITS == 2 ? 16 : 8;  // code bytes per lane per 256-column step
     const int K256 = K & ~255;
@@ -159,7 +172,7 @@ __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
 #pragma unroll
                 for (int s = 0; s < 16; ++s) {  // word s / 4 holds the codes of columns 16 (s / 4) .. + 15 of the lane's run
                     const int sh = (s & 3) * (BITS == 2 ? 8 : 4);
-                    tail_step4<BITS>(d, wl[s >> 2] >> sh, wh[s >> 2] >> sh, fl[s >> 3], fh[s >> 3], xrow, k0 + 64 * q + 4 * s, s);
+                    tail_step4<BITS>(d, wl[s >> 2] >> sh, wh[s >> 2] >> sh, fl[s >> 3], fh[s >> 3], xrow, tab_lane, k0 + 64 * q + 4 * s);
                 }
             }
             for (int k0 = K256; k0 < K; k0 += 64) {  // remainder: 16 columns per lane
@@ -178,7 +191,7 @@ __global__ void __launch_bounds__(256) tail_pass_kernel(const TailArgs a) {
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const int sh = s * (BITS == 2 ? 8 : 4);
-                    tail_step4<BITS>(d, w_lo >> sh, w_hi >> sh, f_lo, f_hi, xrow, k0 + 16 * q + 4 * s, s);
+                    tail_step4<BITS>(d, w_lo >> sh, w_hi >> sh, f_lo, f_hi, xrow, tab_lane, k0 + 16 * q + 4 * s);
                 }
             }
 #pragma unroll
@@ -207,7 +220,7 @@ int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_d
     a.R = stage == 0 ? 2 * L.inter : L.hidden;
     a.K = stage == 0 ? L.hidden : L.inter;
     a.n_experts = L.n_experts;
-    const size_t smem = (size_t)8 * tail_xrow_bytes(a.K);
+    const size_t smem = (size_t)8 * tail_xrow_bytes(a.K) + (bits == 2 ? 256 : 16) * 128;
     if (smem > 200 * 1024) {
         set_error("tail_pass: %d columns need %zu bytes of shared memory", a.K, smem);
         return CHRONOS_E_SHAPE;
