@@ -479,6 +479,23 @@ def run_reference(args) -> dict:
     }
 
 
+def ep_stack_single_gpu(args) -> dict:
+    """The N > 1 workload (42-layer stack, 4096 tokens per step) on one GPU, 3 timed steps."""
+    import argparse
+    import gc
+
+    import torch
+
+    from chronos_b200 import ep_bench
+
+    gc.collect()
+    torch.cuda.empty_cache()
+    small = argparse.Namespace(**{**vars(args), "steps": 3, "warmup": 3})
+    res = ep_bench.run(small, args.layers, EP_TOKENS, DECODE, None)
+    return {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "ms_per_step": res["ms_per_step"],
+            "steps": res["steps"], "config": {"workload": "ep_stack", "layers": args.layers, "tokens_per_step": EP_TOKENS}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -490,6 +507,7 @@ def main() -> None:
     ap.add_argument("--regime", default=None, choices=(None, "auto", "tensor", "tensor_fp4"), help="bank-pass regime of the prefill workload")
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep-base", action="store_true", help="skip the single-GPU run of the N > 1 workload appended to the default line")
     ap.add_argument("--tail", type=int, default=0, choices=(0, 1, 2), help="decode workload: add a tail lattice of this many bits per weight")
     ap.add_argument("--layers", type=int, default=EP_LAYERS, help="depth of the ep_stack workload")
     args = ap.parse_args()
@@ -503,7 +521,12 @@ def main() -> None:
     if workload in ("decode", "prefill", "sweep", "fp4_ceiling"):
         if rank == 0:
             fn = {"decode": run_decode, "prefill": run_prefill, "sweep": run_sweep, "fp4_ceiling": run_prefill}[workload]
-            print(json.dumps(fn(args)), flush=True)
+            out = fn(args)
+            if workload == "decode" and args.workload is None and not args.no_ep_base:
+                # the N > 1 lines run the expert-parallel stack (a different workload): give the N = 1 line the same
+                # stack on one GPU, so that strong-scaling ratios can be formed from like quantities
+                out["ep_stack_1gpu"] = ep_stack_single_gpu(args)
+            print(json.dumps(out), flush=True)
         return
     from chronos_b200 import ep_bench
 

@@ -20,8 +20,8 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
     os.environ.setdefault("MASTER_PORT", "29531")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-        os.environ["NCCL_DEBUG"] = "WARN"  # keep the version banner off stdout: the bench prints exactly one JSON line
+    # NCCL's banner and warnings go to stderr: the bench prints exactly one JSON line on stdout
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     try:
         cfg = FoldedLayerConfig(**layer_kw)
