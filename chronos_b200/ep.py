@@ -87,18 +87,23 @@ class ExpertParallelMoE:
         """x_local [Tl, H] (same Tl on every rank) -> y_local fp32 [Tl, H]."""
         tl, h = x_local.shape
         k = self.cfg.top_k
+        # ---- dispatch: gather rows and routing lists of all ranks (fixed-size blocks, no host-side sizes). The token rows
+        # do not depend on the routing, so their exchange is issued first and runs (on the collective's own stream) while
+        # the router kernels run on this one; the current stream waits for it only before the expert pass. -----------------
+        x_all = torch.empty((self.world * tl, h), dtype=x_local.dtype, device=x_local.device)
+        with self._mark("dispatch_rows_issue"):
+            rows = dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group, async_op=True)
         with self._mark("route"):
             ids, gates = self.route_fn(x_local)
-        # ---- dispatch: gather rows and routing lists of all ranks (fixed-size blocks, no host-side sizes) ----------
         with self._mark("dispatch"):
-            x_all = torch.empty((self.world * tl, h), dtype=x_local.dtype, device=x_local.device)
             meta_local = torch.cat([ids.to(torch.float32), gates.to(torch.float32)], dim=1).contiguous()  # ids < 2^24: exact
             meta_all = torch.empty((self.world * tl, 2 * k), dtype=torch.float32, device=x_local.device)
-            dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
             dist.all_gather_into_tensor(meta_all, meta_local, group=self.group)
             ids_all = meta_all[:, :k].to(torch.int64)
             gates_all = meta_all[:, k:].contiguous()
             local_ids = localize_routing(ids_all, self.first_expert, self.n_local)
+            if rows is not None:
+                rows.wait()  # stream-ordered: no host synchronisation
         # ---- compute: only entries this rank owns ---------------------------------------------------------------------
         with self._mark("routed_experts"):
             part = self.compute_routed(x_all, local_ids, gates_all)
