@@ -516,16 +516,24 @@ struct Fp4WideArgs {
 };
 
 
+// NT = bank row blocks multiplied against one activation stage: 1 (two accumulator buffers, the epilogue overlaps the next
+// tile) or 2 (more MMA work per staged byte: stage = 2 x 18432 + 28672 B, 3 stages, accumulators of the two row blocks side
+// by side in tensor memory, single-buffered).
+template <int NT>
 __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4WideArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2 * kWStages + 4];  // full[S], empty[S], acc_full[2], acc_empty[2]
     __shared__ uint32_t tmem_base_s;
     uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    float* zs = reinterpret_cast<float*>(stages + (size_t)kWStages * kWStage);
+    constexpr int STG = NT == 2 ? 3 : kWStages;
+    constexpr int STAGE = NT * kF4AStage + kWideStageBytes;
+    constexpr uint32_t SFW = NT == 2 ? 16u : 12u;  // scale columns per MMA step: 4 per bank row block + 8 for the 192 activation rows
+    float* zs = reinterpret_cast<float*>(stages + (size_t)STG * STAGE);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.R, RB = R / 128, NS = a.K / kF4StageK;
-    constexpr uint32_t S = kWStages;
-    const long n_tiles = (long)a.counters[3] * RB;
+    constexpr uint32_t S = STG;
+    const int RBT = RB / NT;  // tiles (groups of NT row blocks) per work item
+    const long n_tiles = (long)a.counters[3] * RBT;
     // tiles go round-robin over the CTAs: at any moment the CTAs work on neighbouring tiles, i.e. on the same few work items
     // (whose activation image they share through L2) and on neighbouring row blocks of the same few banks
     const long tile_lo = blockIdx.x, tile_hi = n_tiles, tile_step = gridDim.x;
@@ -535,7 +543,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
     uint64_t* acc_empty = bars + 2 * kWStages + 2;
 
     if (tid == 0) {
-        for (int s = 0; s < kWStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
+        for (int s = 0; s < STG; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&acc_full[b]), 1); mbar_init(smem_u32(&acc_empty[b]), 8); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -554,7 +562,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
             uint32_t it = 0;
             bool live = true;
             for (long tile = tile_lo; tile < tile_hi && live; tile += tile_step) {
-                const int item = (int)(tile / RB), rb = (int)(tile % RB);
+                const int item = (int)(tile / RBT), rb = (int)(tile % RBT) * NT;
                 const int slot = a.item_slot[item];
                 const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
                                       (size_t)rb * NS * kF4AStage;
@@ -566,10 +574,12 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
                         live = false;
                         break;
                     }
-                    uint8_t* dst = stages + (size_t)s * kWStage;
-                    mbar_expect_tx(smem_u32(&full[s]), kWStage);
-                    bulk_g2s(smem_u32(dst), asrc + (size_t)st * kF4AStage, kF4AStage, smem_u32(&full[s]));
-                    bulk_g2s(smem_u32(dst + kF4AStage), bsrc + (size_t)st * kWideStageBytes, kWideStageBytes, smem_u32(&full[s]));
+                    uint8_t* dst = stages + (size_t)s * STAGE;
+                    mbar_expect_tx(smem_u32(&full[s]), STAGE);
+#pragma unroll
+                    for (int d = 0; d < NT; ++d)  // row block rb + d of the same slot: NS stages further on in the bank image
+                        bulk_g2s(smem_u32(dst + d * kF4AStage), asrc + ((size_t)d * NS + st) * kF4AStage, kF4AStage, smem_u32(&full[s]));
+                    bulk_g2s(smem_u32(dst + NT * kF4AStage), bsrc + (size_t)st * kWideStageBytes, kWideStageBytes, smem_u32(&full[s]));
                 }
             }
             for (uint32_t back = 0; back < S && back < it; ++back) {  // copies in flight must land before the CTA exits
@@ -583,14 +593,15 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
             const uint32_t idesc = idesc_nvf4(kF4ARows, kWideRows);
             const uint32_t hi_word = 0x00004008u;
             const uint32_t a_lo0 = ((smem_u32(stages) >> 4) & 0x3FFFu) | ((uint32_t)(kF4ARows * 16 >> 4) << 16);
-            const uint32_t b_lo0 = ((smem_u32(stages + kF4AStage) >> 4) & 0x3FFFu) | ((uint32_t)(kWideRows * 16 >> 4) << 16);
+            const uint32_t b_lo0 = ((smem_u32(stages + NT * kF4AStage) >> 4) & 0x3FFFu) | ((uint32_t)(kWideRows * 16 >> 4) << 16);
             const uint32_t sfa_lo0 = (smem_u32(stages + kF4ANib) >> 4) & 0x3FFFu;
-            const uint32_t sfb_lo0 = (smem_u32(stages + kF4AStage + kWideRows * 128) >> 4) & 0x3FFFu;
+            const uint32_t sfb_lo0 = (smem_u32(stages + NT * kF4AStage + kWideRows * 128) >> 4) & 0x3FFFu;
             uint32_t it = 0, tcount = 0;
             bool live = true;
             for (long tile = tile_lo; tile < tile_hi && live; tile += tile_step, ++tcount) {
-                const uint32_t buf = tcount & 1u;
-                if (!mbar_wait(smem_u32(&acc_empty[buf]), ((tcount >> 1) & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                const uint32_t buf = NT == 2 ? 0u : (tcount & 1u);
+                const uint32_t eph = NT == 2 ? (tcount & 1u) : ((tcount >> 1) & 1u);
+                if (!mbar_wait(smem_u32(&acc_empty[buf]), eph ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t tmem_d = tmem + buf * kWideRows;
                 for (int st = 0; st < NS; ++st, ++it) {
@@ -599,21 +610,26 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     // scale blocks of the stage: per MMA 4 columns for the bank rows, 8 for the 192 activation rows; two
                     // sets of slots alternate between consecutive stages
-                    const uint32_t sf = tmem + 2 * kWideRows + (it & 1u) * 48u;
-                    const uint32_t so = s * (kWStage >> 4);
+                    const uint32_t sf = tmem + 2 * kWideRows + (it & 1u) * (4u * SFW);
+                    const uint32_t so = s * (STAGE >> 4);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        tc_cp_sf_lo(sf + 12 * j, sfa_lo0 + so + j * 32);
-                        tc_cp_sf_lo(sf + 12 * j + 4, sfb_lo0 + so + j * 64);
-                        tc_cp_sf_lo(sf + 12 * j + 8, sfb_lo0 + so + j * 64 + 32);
+#pragma unroll
+                        for (int d = 0; d < NT; ++d) tc_cp_sf_lo(sf + SFW * j + 4 * d, sfa_lo0 + so + d * (kF4AStage >> 4) + j * 32);
+                        tc_cp_sf_lo(sf + SFW * j + 4 * NT, sfb_lo0 + so + j * 64);
+                        tc_cp_sf_lo(sf + SFW * j + 4 * NT + 4, sfb_lo0 + so + j * 64 + 32);
                     }
                     const uint32_t a_lo = a_lo0 + so, b_lo = b_lo0 + so;
-                    if (st == 0) tc_mma_nvf4_lo<false>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sf, sf + 4);
-                    else tc_mma_nvf4_lo<true>(tmem_d, a_lo, hi_word, b_lo, hi_word, idesc, sf, sf + 4);
 #pragma unroll
-                    for (int j = 1; j < 4; ++j)
-                        tc_mma_nvf4_lo<true>(tmem_d, a_lo + j * (2 * kF4ARows * 16 >> 4), hi_word, b_lo + j * (2 * kWideRows * 16 >> 4), hi_word,
-                                             idesc, sf + 12 * j, sf + 12 * j + 4);
+                    for (int d = 0; d < NT; ++d) {  // row block d: its own bank tile, scales and accumulator, the same activations
+                        const uint32_t ad = a_lo + d * (kF4AStage >> 4), dd = tmem_d + d * kWideRows;
+                        if (st == 0) tc_mma_nvf4_lo<false>(dd, ad, hi_word, b_lo, hi_word, idesc, sf + 4 * d, sf + 4 * NT);
+                        else tc_mma_nvf4_lo<true>(dd, ad, hi_word, b_lo, hi_word, idesc, sf + 4 * d, sf + 4 * NT);
+#pragma unroll
+                        for (int j = 1; j < 4; ++j)
+                            tc_mma_nvf4_lo<true>(dd, ad + j * (2 * kF4ARows * 16 >> 4), hi_word, b_lo + j * (2 * kWideRows * 16 >> 4), hi_word,
+                                                 idesc, sf + SFW * j + 4 * d, sf + SFW * j + 4 * NT);
+                    }
                     tc_commit_f4(smem_u32(&empty[s]));
                 }
                 if (live) tc_commit_f4(smem_u32(&acc_full[buf]));
@@ -627,55 +643,62 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
         const int bar_id = 2 + half;
         uint32_t tcount = 0;
         for (long tile = tile_lo; tile < tile_hi; tile += tile_step, ++tcount) {
-            const int item = (int)(tile / RB), rb = (int)(tile % RB);
+            const int item = (int)(tile / RBT), rb0 = (int)(tile % RBT) * NT;
             const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
             const bool sh = slot >= a.n_slots;
-            const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
-            uint32_t sw = 0u;  // r_s2 sign bits of this lane's 4 rows (one expert per work item)
-            if (!sh) sw = a.rs2[(size_t)a.pair_expert[start] * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
-            const uint32_t buf = tcount & 1u;
-            uint32_t fail = mbar_wait(smem_u32(&acc_full[buf]), (tcount >> 1) & 1u) ? 0u : 1u;
+            const uint32_t buf = NT == 2 ? 0u : (tcount & 1u);
+            const uint32_t fph = NT == 2 ? (tcount & 1u) : ((tcount >> 1) & 1u);
+            uint32_t fail = mbar_wait(smem_u32(&acc_full[buf]), fph) ? 0u : 1u;
             asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbarrier.red.or.pred p, %2, 128, q;\nselp.u32 %0, 1, 0, p;\n}"
                          : "=r"(fail) : "r"(fail), "r"(bar_id) : "memory");
             if (fail) { if (lane == 0 && wq == 0) atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int n0 = half * 32;
-            if (n0 < cnt) {
-                const uint32_t tbase = tmem + buf * kWideRows + (uint32_t)n0 + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
-                for (int ch = 0; ch < 2; ++ch) {
-                    uint32_t t0[16], t1[16], t2[16];
-                    tmem_ld16_f4(tbase + ch * 16, t0);
-                    tmem_ld16_f4(tbase + 64 + ch * 16, t1);
-                    tmem_ld16_f4(tbase + 128 + ch * 16, t2);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int d = 0; d < NT; ++d) {
+                const int rb = rb0 + d;
+                const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
+                uint32_t sw = 0u;  // r_s2 sign bits of this lane's 4 rows (one expert per work item)
+                if (!sh) sw = a.rs2[(size_t)a.pair_expert[start] * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
+                if (n0 < cnt) {
+                    const uint32_t tbase = tmem + (buf + d) * kWideRows + (uint32_t)n0 + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
-                    for (int n = 0; n < 16; ++n)
-                        zsh[(ch * 16 + n) * 132 + row] =
-                            __uint_as_float(t0[n]) + 0.03125f * __uint_as_float(t1[n]) + 0.0009765625f * __uint_as_float(t2[n]);
-                }
-            }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));  // accumulator buffer may be overwritten
-            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-#pragma unroll 2
-            for (int i = 0; i < 8; ++i) {
-                const int n = n0 + wq * 8 + i;
-                if (n < cnt) {
-                    const float g = a.pscale[start + n] * s2;
-                    const float4 t4 = *reinterpret_cast<const float4*>(&zsh[(wq * 8 + i) * 132 + lane * 4]);
-                    float v[4] = {t4.x * g, t4.y * g, t4.z * g, t4.w * g};
-                    if (!sh) {
+                    for (int ch = 0; ch < 2; ++ch) {
+                        uint32_t t0[16], t1[16], t2[16];
+                        tmem_ld16_f4(tbase + ch * 16, t0);
+                        tmem_ld16_f4(tbase + 64 + ch * 16, t1);
+                        tmem_ld16_f4(tbase + 128 + ch * 16, t2);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            if ((sw >> q) & 1u) v[q] = -v[q];
-                        fwht128_warp(v, lane);
+                        for (int n = 0; n < 16; ++n)
+                            zsh[(ch * 16 + n) * 132 + row] =
+                                __uint_as_float(t0[n]) + 0.03125f * __uint_as_float(t1[n]) + 0.0009765625f * __uint_as_float(t2[n]);
                     }
-                    *reinterpret_cast<float4*>(a.zout + (size_t)(start + n) * R + rb * 128 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
                 }
+                if (d == NT - 1) {  // every accumulator of the tile has been read: the issuer may overwrite them
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+                }
+                asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+#pragma unroll 2
+                for (int i = 0; i < 8; ++i) {
+                    const int n = n0 + wq * 8 + i;
+                    if (n < cnt) {
+                        const float g = a.pscale[start + n] * s2;
+                        const float4 t4 = *reinterpret_cast<const float4*>(&zsh[(wq * 8 + i) * 132 + lane * 4]);
+                        float v[4] = {t4.x * g, t4.y * g, t4.z * g, t4.w * g};
+                        if (!sh) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if ((sw >> q) & 1u) v[q] = -v[q];
+                            fwht128_warp(v, lane);
+                        }
+                        *reinterpret_cast<float4*>(a.zout + (size_t)(start + n) * R + rb * 128 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                }
+                asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
             }
-            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -702,8 +725,12 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
     a.pair_expert = p.pair_expert;
     a.counters = p.counters;
     a.n_slots = L.n_slots;
-    const size_t smem = (size_t)kWStages * kWStage + (size_t)kWZsFloats * 4 + 1024;
-    cudaError_t rc = cudaFuncSetAttribute(bank_fp4_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // the gate_up pass (16 stages per tile) multiplies two row blocks per activation stage; the down pass (6 stages per
+    // tile) keeps one row block and the overlapped epilogue
+    const bool two = stage == 0 && (a.R / 128) % 2 == 0;
+    const size_t smem = (two ? (size_t)3 * (2 * kF4AStage + kWideStageBytes) : (size_t)kWStages * kWStage) + (size_t)kWZsFloats * 4 + 1024;
+    cudaError_t rc = two ? cudaFuncSetAttribute(bank_fp4_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                         : cudaFuncSetAttribute(bank_fp4_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (rc != cudaSuccess) {
         set_error("bank_fp4_wide: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
         return CHRONOS_E_LAUNCH;
@@ -713,7 +740,8 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long max_tiles = (long)p.max_gitems * (a.R / 128);
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-    bank_fp4_wide_kernel<<<grid, kWThreads, smem, st>>>(a);
+    if (two) bank_fp4_wide_kernel<2><<<grid, kWThreads, smem, st>>>(a);
+    else bank_fp4_wide_kernel<1><<<grid, kWThreads, smem, st>>>(a);
     return check_launch("bank_fp4_wide");
 }
 
