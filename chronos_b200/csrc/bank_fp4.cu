@@ -727,10 +727,17 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
     a.n_slots = L.n_slots;
     // the gate_up pass (16 stages per tile) multiplies two row blocks per activation stage; the down pass (6 stages per
     // tile) keeps one row block and the overlapped epilogue
-    const bool two = stage == 0 && (a.R / 128) % 2 == 0;
-    const size_t smem = (two ? (size_t)3 * (2 * kF4AStage + kWideStageBytes) : (size_t)kWStages * kWStage) + (size_t)kWZsFloats * 4 + 1024;
-    cudaError_t rc = two ? cudaFuncSetAttribute(bank_fp4_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                         : cudaFuncSetAttribute(bank_fp4_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    bool two = stage == 0 && (a.R / 128) % 2 == 0;
+    size_t smem = (size_t)3 * (2 * kF4AStage + kWideStageBytes) + (size_t)kWZsFloats * 4 + 1024;
+    cudaError_t rc = cudaSuccess;
+    if (two && cudaFuncSetAttribute(bank_fp4_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();  // the two-row-block form needs every byte of shared memory an SM has: fall back to one row block
+        two = false;
+    }
+    if (!two) {
+        smem = (size_t)kWStages * kWStage + (size_t)kWZsFloats * 4 + 1024;
+        rc = cudaFuncSetAttribute(bank_fp4_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
     if (rc != cudaSuccess) {
         set_error("bank_fp4_wide: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
         return CHRONOS_E_LAUNCH;
