@@ -374,6 +374,34 @@ def test_tensor_fp4_regime_whole_layer(scale):
     assert _rel_l2(y16.float().cpu().numpy(), ref) <= LAYER_TOL
 
 
+@pytest.mark.parametrize("n_tok,regime", [(6, "auto"), (200, "auto")])
+def test_forward_is_cuda_graph_capturable(n_tok, regime):
+    """The whole-layer call makes no host synchronisation and no allocation of its own: it can be captured into a CUDA graph
+    (what a serving engine does with the decode step) and replayed on new inputs with the same result as an eager call."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=32, top_k=4)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=23, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(n_tok)
+    x_static = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    x_new = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up: the workspace reaches its final size before capture
+        layer.forward_impl(x_static, regime=regime)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y_static = layer.forward_impl(x_static, regime=regime)
+    x_static.copy_(x_new)
+    graph.replay()
+    torch.cuda.synchronize()
+    y_eager = layer.forward_impl(x_new, regime=regime)
+    assert layer.device_status() == 0
+    assert torch.equal(y_static, y_eager)
+
+
 def test_large_batch_without_optional_copies_and_shared_expert_range():
     """A layer description without the optional load-time copies (FP4 stage images, healer.v_down as on disk) takes the
     fp16 tensor regime with the CUDA-core healer kernels; and the shared expert can be limited to a block of tokens
