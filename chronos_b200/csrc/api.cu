@@ -2,6 +2,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -21,6 +22,55 @@ int check_launch(const char* what) {
     if (rc == cudaSuccess) return CHRONOS_OK;
     set_error("%s: %s", what, cudaGetErrorString(rc));
     return CHRONOS_E_LAUNCH;
+}
+
+// ---- per-device launch facts, looked up once -----------------------------------------------------------------
+// The SM count and the dynamic shared-memory opt-in of a kernel do not change while the process lives; asking the
+// runtime for them on every launch costs several driver calls per layer on the host side of a ~100 us step.
+constexpr int kMaxDevices = 64;
+static std::mutex g_cache_mu;
+static int g_sm_count[kMaxDevices];
+
+static int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    return dev;
+}
+
+int device_sm_count() {
+    const int dev = current_device();
+    if (dev < 0) return 148;
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    if (g_sm_count[dev] == 0) {
+        int sms = 148;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) { cudaGetLastError(); sms = 148; }
+        g_sm_count[dev] = sms;
+    }
+    return g_sm_count[dev];
+}
+
+struct SmemOptIn { const void* func; int dev; size_t bytes; };
+static SmemOptIn g_optin[256];
+static int g_n_optin = 0;
+
+// Makes sure `func` may be launched with `bytes` of dynamic shared memory on the current device; the runtime is asked
+// only when a (kernel, device) pair needs more than it was granted before.
+int ensure_dynamic_smem(const void* func, size_t bytes, const char* what) {
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    SmemOptIn* slot = nullptr;
+    for (int i = 0; i < g_n_optin; ++i)
+        if (g_optin[i].func == func && g_optin[i].dev == dev) { slot = &g_optin[i]; break; }
+    if (slot != nullptr && slot->bytes >= bytes) return CHRONOS_OK;
+    const cudaError_t rc = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (rc != cudaSuccess) {
+        cudaGetLastError();
+        set_error("%s: cannot opt in to %zu bytes of shared memory: %s", what, bytes, cudaGetErrorString(rc));
+        return CHRONOS_E_LAUNCH;
+    }
+    if (slot == nullptr && g_n_optin < 256 && dev >= 0) slot = &g_optin[g_n_optin++];
+    if (slot != nullptr) *slot = SmemOptIn{func, dev, bytes};
+    return CHRONOS_OK;
 }
 
 static bool aligned16(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -47,7 +97,7 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
         set_error("shared_inter (%d) must be 0 or equal to inter (%d)", L->shared_inter, L->inter);
         return CHRONOS_E_SHAPE;
     }
-    if (L->router_kind != CHRONOS_ROUTER_SOFTMAX_TOPK && L->router_kind != CHRONOS_ROUTER_SIGMOID_NOAUX) {
+    if (L->router_kind < CHRONOS_ROUTER_SOFTMAX_TOPK || L->router_kind > CHRONOS_ROUTER_SQRT_SOFTPLUS) {
         set_error("router_kind %d is not a CHRONOS_ROUTER_* value", L->router_kind);
         return CHRONOS_E_ARG;
     }
@@ -74,7 +124,7 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
         for (const void* q : tl)
             if (!aligned16(q)) { set_error("a tail-lattice pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
     }
-    if (need_router && L->router_w == nullptr) { set_error("layer.router_w is NULL"); return CHRONOS_E_ALIGN; }
+    if (need_router && !aligned16(L->router_w)) { set_error("layer.router_w is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
     if (L->shared_inter > 0) {
         const void* sh[] = {L->sh_gu_w, L->sh_gu_s, L->sh_dn_w, L->sh_dn_s};
         for (const void* q : sh)
@@ -93,8 +143,9 @@ static int validate_router(const chronos_layer_t* L) {
         set_error("router: n_experts (%d) in [1, 1024] and top_k (%d) in [1, min(%d, n_experts)] required", L->n_experts, L->top_k, kMaxTopK);
         return CHRONOS_E_SHAPE;
     }
-    if (L->router_kind != CHRONOS_ROUTER_SOFTMAX_TOPK && L->router_kind != CHRONOS_ROUTER_SIGMOID_NOAUX) { set_error("router_kind %d is not a CHRONOS_ROUTER_* value", L->router_kind); return CHRONOS_E_ARG; }
-    if (!L->router_w) { set_error("layer.router_w is NULL"); return CHRONOS_E_ALIGN; }
+    if (L->router_kind < CHRONOS_ROUTER_SOFTMAX_TOPK || L->router_kind > CHRONOS_ROUTER_SQRT_SOFTPLUS) { set_error("router_kind %d is not a CHRONOS_ROUTER_* value", L->router_kind); return CHRONOS_E_ARG; }
+    // the router kernels fetch rows with 16-byte bulk copies and vector loads
+    if (!aligned16(L->router_w)) { set_error("layer.router_w is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
     return CHRONOS_OK;
 }
 
@@ -186,7 +237,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 6; }
+int chronos_b200_abi_version(void) { return 7; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -302,6 +353,12 @@ int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, i
     if (b_rows < 16 || b_rows > 256 || b_rows % 16) { set_error("fp4_probe: b_rows (%d) must be a multiple of 16 in 16..256", b_rows); return CHRONOS_E_SHAPE; }
     if (!aligned16(a_image) || !aligned16(b_image) || !d_out || !status) { set_error("fp4_probe: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
     return launch_fp4_probe(a_image, b_image, n_stages, b_rows, d_out, status, (cudaStream_t)stream);
+}
+
+int chronos_b200_wait_probe(int32_t* status, unsigned poll_limit, void* stream) {
+    if (!status) { set_error("wait_probe: status is NULL"); return CHRONOS_E_ALIGN; }
+    if (poll_limit == 0 || poll_limit > 4096) { set_error("wait_probe: poll_limit (%u) must be in 1..4096", poll_limit); return CHRONOS_E_ARG; }
+    return launch_wait_probe(status, poll_limit, (cudaStream_t)stream);
 }
 
 int chronos_b200_set_stage_events(void** events, int n_events) {

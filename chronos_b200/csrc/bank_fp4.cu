@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
                 tc_commit_f4(smem_u32(&bars[1]));
                 ok = mbar_wait(smem_u32(&bars[1]), st & 1);  // single-buffered: wait before the next stage overwrites
             }
-            if (!ok) atomicOr(status, 0x40);
+            if (!ok) atomicOr(status, kStatusFp4ProbeTimeout);
         }
         failed = __syncthreads_or(tid == 0 ? (*(volatile int32_t*)status != 0) : 0);
     }
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kF4MaxStages = 8;
 constexpr int kF4Threads = 224;  // producer, MMA issuer A, 4 epilogue warps, MMA issuer B
-constexpr int kStatusFp4Timeout = 0x80;
+constexpr int kStatusFp4Timeout = kStatusBankFp4Timeout;
 constexpr uint32_t kF4TmemCols = 512;  // 2 buffers x 2 accumulators x 32 columns, then bank scales (16 per ring stage), then activation scales
 
 struct Fp4Args {
@@ -473,14 +473,8 @@ int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStre
     int stages = (int)((budget - 1024 - bimg) / kF4AStage);
     a.n_stages = stages > kF4MaxStages ? kF4MaxStages : stages;
     const size_t smem = bimg + (size_t)a.n_stages * kF4AStage + 1024;
-    cudaError_t rc = cudaFuncSetAttribute(bank_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (rc != cudaSuccess) {
-        set_error("bank_fp4: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(bank_fp4_kernel), smem, "bank_fp4")) return rc;
+    const int sms = device_sm_count();
     const long max_tiles = (long)p.max_items * (a.R / 128);
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
     bank_fp4_kernel<<<grid, kF4Threads, smem, st>>>(a);
@@ -729,22 +723,13 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
     // tile) keeps one row block and the overlapped epilogue
     bool two = stage == 0 && (a.R / 128) % 2 == 0;
     size_t smem = (size_t)3 * (2 * kF4AStage + kWideStageBytes) + (size_t)kWZsFloats * 4 + 1024;
-    cudaError_t rc = cudaSuccess;
-    if (two && cudaFuncSetAttribute(bank_fp4_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-        cudaGetLastError();  // the two-row-block form needs every byte of shared memory an SM has: fall back to one row block
-        two = false;
-    }
+    // the two-row-block form needs every byte of shared memory an SM has: fall back to one row block when it is refused
+    if (two && ensure_dynamic_smem(reinterpret_cast<const void*>(bank_fp4_wide_kernel<2>), smem, "bank_fp4_wide") != CHRONOS_OK) two = false;
     if (!two) {
         smem = (size_t)kWStages * kWStage + (size_t)kWZsFloats * 4 + 1024;
-        rc = cudaFuncSetAttribute(bank_fp4_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(bank_fp4_wide_kernel<1>), smem, "bank_fp4_wide")) return rc;
     }
-    if (rc != cudaSuccess) {
-        set_error("bank_fp4_wide: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sm_count();
     const long max_tiles = (long)p.max_gitems * (a.R / 128);
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
     if (two) bank_fp4_wide_kernel<2><<<grid, kWThreads, smem, st>>>(a);
@@ -755,11 +740,7 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st) {
     const size_t smem = kF4AStage + (size_t)b_rows * 128 + 2048 * ((b_rows + 127) / 128) + 1024;
-    cudaError_t rc = cudaFuncSetAttribute(fp4_mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (rc != cudaSuccess) {
-        set_error("fp4_probe: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
+    if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(fp4_mma_probe_kernel), smem, "fp4_probe")) return rc;
     fp4_mma_probe_kernel<<<1, 128, smem, st>>>(a_img, b_img, n_stages, b_rows, d_out, status);
     return check_launch("fp4_probe");
 }

@@ -21,7 +21,7 @@ namespace chronos {
 constexpr int kGemmStages = 4;
 constexpr int kGemmKStep = 64;                       // columns per stage (= one 128-byte swizzle row of fp16)
 constexpr int kTileBytes = 128 * kGemmKStep * 2;     // one operand tile: 128 rows x 128 bytes
-constexpr int kStatusGemmTimeout = 0x20;
+constexpr int kStatusGemmTimeout = kStatusBankGemmTimeout;
 constexpr uint32_t kTmemCols = 128;
 
 struct GemmArgs {
@@ -239,14 +239,8 @@ int launch_bank_gemm(const chronos_layer_t& L, int stage, const Plan& p, cudaStr
         return CHRONOS_E_SHAPE;
     }
     const size_t smem = (size_t)kGemmStages * 2 * kTileBytes + 1024;
-    cudaError_t rc = cudaFuncSetAttribute(bank_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (rc != cudaSuccess) {
-        set_error("bank_gemm: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(bank_gemm_kernel), smem, "bank_gemm")) return rc;
+    const int sms = device_sm_count();
     const long max_tiles = (long)p.max_gitems * (a.R / 128);
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
     bank_gemm_kernel<<<grid, 256, smem, st>>>(a);

@@ -21,7 +21,7 @@ namespace chronos {
 constexpr int kRowsPerStage = 16;
 constexpr int kStagesPerTile = 128 / kRowsPerStage;
 constexpr int kRedStride = 132;           // floats per (warp, pair) row of the reduction buffer (bank-conflict pad)
-constexpr int kStatusBankTimeout = 0x10;
+constexpr int kStatusBankTimeout = kStatusBankStreamTimeout;
 
 struct BankArgs {
     const uint8_t* w;       // [n_slots, R, K/2]
@@ -314,19 +314,13 @@ int launch_bank_stream(const chronos_layer_t& L, int stage, const Plan& p, cudaS
     a.n_stages = stages;
     const size_t smem = 256 + (size_t)stages * a.stage_bytes + red_bytes;
 
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sm_count();
     const long max_tiles = (long)p.max_items * (a.R / 128);
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
     const int threads = (a.n_warps + 1) * 32;
 
     auto go = [&](auto kern) -> int {
-        cudaError_t rc = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (rc != cudaSuccess) {
-            set_error("bank_stream: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-            return CHRONOS_E_LAUNCH;
-        }
+        if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem, "bank_stream")) return rc;
         kern<<<grid, threads, smem, st>>>(a);
         return check_launch("bank_stream");
     };

@@ -221,6 +221,7 @@ int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, 
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_fp4(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+int launch_wait_probe(int32_t* status, uint32_t poll_limit, cudaStream_t st);
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st);
 int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, int dtype, int n_tokens, int hidden,
@@ -228,6 +229,8 @@ int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, in
 
 void set_error(const char* fmt, ...);
 int check_launch(const char* what);
+int device_sm_count();  // SMs of the current device (cached per device)
+int ensure_dynamic_smem(const void* func, size_t bytes, const char* what);  // shared-memory opt-in, cached per (kernel, device)
 
 #ifdef __CUDACC__
 // ---- device helpers ---------------------------------------------------------------------------------------------
@@ -299,7 +302,28 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     for (int i = 0; i < 4; ++i) v[i] *= 0.08838834764831845f;
 }
 
+// softplus as torch evaluates it (F.softplus, beta 1, threshold 20): x above the threshold passes through.
+__device__ __forceinline__ float softplus_f32(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// Router flavours. choice = the score the top-k ranks by; weight source = the unbiased score the gate is made from.
+//   softmax top-k     (chronos_1t/models/vllm_chronos_moe.py:310-314): both are the logit; gate = softmax over the k chosen
+//   sigmoid noaux_tc  (chronos_1t/models/glm53_chronos_moe.py:392-399): sigmoid(logit) (+ bias for the choice)
+//   sqrt-softplus     (chronos_1t/models/dsv41_chronos_moe.py:3402-3410): sqrt(softplus(logit)) (+ bias for the choice)
+__device__ __forceinline__ float router_weight_source(const TopkArgs& a, float lg) {
+    if (a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX) return 1.0f / (1.0f + expf(-lg));
+    if (a.kind == CHRONOS_ROUTER_SQRT_SOFTPLUS) return sqrtf(softplus_f32(lg));
+    return lg;
+}
+__device__ __forceinline__ float router_choice(const TopkArgs& a, float lg, int e) {
+    const float s = router_weight_source(a, lg);
+    return a.kind == CHRONOS_ROUTER_SOFTMAX_TOPK ? s : s + (a.e_bias ? a.e_bias[e] : 0.0f);
+}
+
 // k rounds of warp arg-max for token t (ties -> lower index) and the gate weights; executed by one full warp.
+// A candidate whose choice score is NaN (a NaN activation row makes every logit NaN) or -inf (a -inf bias entry) can
+// never win a round. When no candidate is left the round emits id -1 with gate 0 - an entry every consumer skips -
+// so no index outside [0, n_experts) is ever formed or used as an address.
+constexpr int kNoExpert = 0x7fffffff;
 template <int PL>
 __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int lane) {
     float choice[PL];
@@ -309,7 +333,8 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
         float c = -INFINITY;
         if (e < a.n_experts) {
             const float lg = a.logits[(size_t)t * a.n_experts + e];
-            c = a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? (1.0f / (1.0f + expf(-lg))) + (a.e_bias ? a.e_bias[e] : 0.0f) : lg;
+            c = router_choice(a, lg, e);
+            if (!(c == c)) c = -INFINITY;  // NaN never wins
         }
         choice[i] = c;
     }
@@ -317,7 +342,7 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
     int my_id = -1;
     for (int j = 0; j < a.top_k; ++j) {
         float best = -INFINITY;
-        int best_e = 0x7fffffff;
+        int best_e = kNoExpert;
 #pragma unroll
         for (int i = 0; i < PL; ++i) {
             const int e = i * 32 + lane;
@@ -329,32 +354,33 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
             const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
             if (ov > best || (ov == best && oe < best_e)) { best = ov; best_e = oe; }
         }
+        const bool found = best_e != kNoExpert;  // warp-uniform
 #pragma unroll
         for (int i = 0; i < PL; ++i)
-            if (i * 32 + lane == best_e) choice[i] = -INFINITY;  // remove the winner from its owner lane
-        if (lane == j) {
+            if (found && i * 32 + lane == best_e) choice[i] = -INFINITY;  // remove the winner from its owner lane
+        if (lane == j && found) {
             my_id = best_e;
-            const float lg = a.logits[(size_t)t * a.n_experts + best_e];
-            my_val = a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX ? 1.0f / (1.0f + expf(-lg)) : lg;
+            my_val = router_weight_source(a, a.logits[(size_t)t * a.n_experts + best_e]);
         }
     }
+    const bool have = lane < a.top_k && my_id >= 0;
     float gate;
-    if (a.kind == CHRONOS_ROUTER_SIGMOID_NOAUX) {
-        const float s = lane < a.top_k ? my_val : 0.0f;
+    if (a.kind != CHRONOS_ROUTER_SOFTMAX_TOPK) {
+        const float s = have ? my_val : 0.0f;
         float tot = 0.0f;  // sequential sum in index order, the way a row reduction over k values reads
         for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, s, j);
         gate = a.renorm ? my_val / (tot + 1e-20f) : my_val;
         gate *= a.scaling;
     } else {
         const float mx = __shfl_sync(0xffffffffu, my_val, 0);  // chosen values are in descending order
-        const float ex = lane < a.top_k ? expf(my_val - mx) : 0.0f;
+        const float ex = have ? expf(my_val - mx) : 0.0f;
         float tot = 0.0f;
         for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, ex, j);
         gate = ex / tot;
     }
     if (lane < a.top_k) {
         a.ids[(size_t)t * a.top_k + lane] = my_id;
-        a.gates[(size_t)t * a.top_k + lane] = gate;
+        a.gates[(size_t)t * a.top_k + lane] = have ? gate : 0.0f;
     }
 }
 __device__ __forceinline__ void topk_one_token(const TopkArgs& a, int t, int lane) {
@@ -492,7 +518,16 @@ __device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
 }
 
 
-constexpr uint32_t kWaitLimit = 1u << 22;  // polls of a ~1 us bounded try_wait before giving up
+constexpr uint32_t kWaitLimit = 1u << 20;  // polls of a ~1 us bounded try_wait before giving up: about a second
+
+// Bits of the device status word (counters[2] of the workspace; the probes take a status pointer of their own).
+constexpr int kStatusBankStreamTimeout = 0x10;   // bank_stream_kernel: a ring wait expired
+constexpr int kStatusBankGemmTimeout = 0x20;     // bank_gemm_kernel
+constexpr int kStatusFp4ProbeTimeout = 0x40;     // fp4_mma_probe_kernel
+constexpr int kStatusBankFp4Timeout = 0x80;      // bank_fp4_kernel / bank_fp4_wide_kernel
+constexpr int kStatusRouterTimeout = 0x100;      // router_logits_small_kernel: staged rows never arrived
+constexpr int kStatusWaitProbeTimeout = 0x200;   // wait_probe_kernel: the wait it is built to lose
+constexpr int kStatusGridSyncTimeout = 0x400;    // a fused decode kernel gave up waiting for the other CTAs of its grid
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -506,8 +541,8 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 // Bounded wait: returns false when the phase did not complete within the poll limit.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = kWaitLimit) {
+    for (uint32_t it = 0; it < limit; ++it) {
         uint32_t ok;
         asm volatile(
             "{\n.reg .pred p;\n"

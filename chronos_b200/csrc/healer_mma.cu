@@ -383,16 +383,14 @@ static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStrea
         set_error("pair_group_out: %zu bytes of shared memory needed for hidden %d / inter %d", smem, L.hidden, L.inter);
         return CHRONOS_E_SHAPE;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sm_count();
     const unsigned most = (unsigned)p.max_gitems * (unsigned)kGroupsPerItem;
     const unsigned resident = (unsigned)sms * (smem * 3 <= 225 * 1024 ? 3u : (smem * 2 <= 225 * 1024 ? 2u : 1u));
     const unsigned grid = most < resident ? most : resident;
-    cudaError_t rc = cudaSuccess;
+    int rc = CHRONOS_OK;
 #define CHRONOS_PG(R)                                                                                                   \
-    rc = cudaFuncSetAttribute(pair_group_out_kernel<MODE, R, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    if (rc == cudaSuccess) pair_group_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
+    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pair_group_out_kernel<MODE, R, WIDE>), smem, "pair_group_out"); \
+    if (rc == CHRONOS_OK) pair_group_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
     switch (L.rank / 16) {
         case 1: CHRONOS_PG(1) break;
         case 2: CHRONOS_PG(2) break;
@@ -400,10 +398,7 @@ static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStrea
         default: CHRONOS_PG(8) break;
     }
 #undef CHRONOS_PG
-    if (rc != cudaSuccess) {
-        set_error("pair_group_out: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
+    if (rc != CHRONOS_OK) return rc;
     return check_launch("pair_group_out");
 }
 

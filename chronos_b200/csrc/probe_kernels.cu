@@ -33,9 +33,10 @@ int launch_dequant(const uint8_t* packed, const uint8_t* scale, const float* s2,
 
 // Row-axis half of the unbind: scratch[rb*128 + :, j] = H_128( r_s2 * S[rb*128 + :, j] ).
 // One warp per (128-row block, column): lane l holds rows 4l..4l+3.
-__global__ void unfold_rows_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ s, float s2,
+__global__ void unfold_rows_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ s, const float* __restrict__ s2p,
                                    const uint32_t* __restrict__ rs2, float* __restrict__ scratch, int rows, int cols) {
     const int lane = threadIdx.x & 31;
+    const float s2 = *s2p;
     const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
     const size_t total = (size_t)(rows / 128) * cols;
     if (warp >= total) return;
@@ -59,13 +60,14 @@ __global__ void unfold_rows_kernel(const uint8_t* __restrict__ w, const uint8_t*
 // Column-axis half + healer: out[i, c_perm[j']] = c_s1 * H_128( c_s2 * r_s1[i] * scratch[r_inv[i], :] )[j'] * beta
 //                                               + sum_c U[i, c] V[c, .].  One warp per (output row, 128-column block).
 __global__ void unfold_cols_kernel(const float* __restrict__ scratch, const uint16_t* __restrict__ rout,
-                                   const uint16_t* __restrict__ cin, const uint32_t* __restrict__ cs2, float beta,
+                                   const uint16_t* __restrict__ cin, const uint32_t* __restrict__ cs2, const float* __restrict__ betap,
                                    const uint8_t* __restrict__ u, const uint8_t* __restrict__ vmat, int v_is_transposed,
                                    int rank, float* __restrict__ out, int rows, int cols) {
     const int lane = threadIdx.x & 31;
     const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
     const size_t total = (size_t)rows * (cols / 128);
     if (warp >= total) return;
+    const float beta = *betap;
     const int i = (int)(warp / (cols / 128)), cb = (int)(warp % (cols / 128));
     const uint16_t ro = rout[i];
     const int src = ro & 0x7fff;
@@ -103,12 +105,8 @@ int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, f
     const uint8_t* s = (which == 0 ? L.gu_s : L.dn_s) + (size_t)slot * rows * (cols / 16);
     const float* s2p = (which == 0 ? L.gu_s2 : L.dn_s2) + slot;
     const float* betap = (which == 0 ? L.gu_beta : L.dn_beta) + expert;
-    float hs[2];
-    // two scalars; the probe is not on the serving path, so a synchronous read is acceptable here
-    if (cudaMemcpyAsync(&hs[0], s2p, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaMemcpyAsync(&hs[1], betap, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
-        return check_launch("unfold scalars");
+    // the two per-slot / per-expert scalars are read by the kernels through their device pointers: the probe is
+    // stream-ordered like every other entry point (no copy to the host, no synchronisation)
     const uint32_t* rs2 = (which == 0 ? L.gu_rs2 : L.dn_rs2) + (size_t)expert * (rows / 32);
     const uint16_t* rout = (which == 0 ? L.gu_rout : L.dn_rout) + (size_t)expert * rows;
     const uint16_t* cin = (which == 0 ? L.gu_cin : L.dn_cin) + (size_t)expert * cols;
@@ -116,12 +114,33 @@ int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, f
     const uint8_t* u = (which == 0 ? L.u_gu : L.u_dn) + (size_t)expert * rows * L.rank;
     const uint8_t* v = (which == 0 ? L.v_gu : L.v_dn_t) + (size_t)expert * cols * L.rank;
     size_t warps = (size_t)(rows / 128) * cols;
-    unfold_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(w, s, hs[0], rs2, scratch, rows, cols);
+    unfold_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(w, s, s2p, rs2, scratch, rows, cols);
     if (int rc = check_launch("unfold_rows")) return rc;
     warps = (size_t)rows * (cols / 128);
-    unfold_cols_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(scratch, rout, cin, cs2, hs[1], u, v, which == 1,
+    unfold_cols_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(scratch, rout, cin, cs2, betap, u, v, which == 1,
                                                                    L.rank, out, rows, cols);
     return check_launch("unfold_cols");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Wait probe: exercises the give-up path every kernel of the library shares. One thread arms a shared-memory barrier
+// for bytes that nobody ever sends, polls it through the same bounded wait the bank kernels use - with the caller's
+// small poll limit - and, when the limit is reached, raises the status bit and returns normally. Nothing traps,
+// nothing hangs, the context stays usable.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void wait_probe_kernel(int32_t* __restrict__ status, uint32_t poll_limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(smem_u32(&bar), 16);  // 16 bytes that no copy will deliver
+        if (!mbar_wait(smem_u32(&bar), 0, poll_limit)) atomicOr(status, kStatusWaitProbeTimeout);
+    }
+}
+
+int launch_wait_probe(int32_t* status, uint32_t poll_limit, cudaStream_t st) {
+    wait_probe_kernel<<<1, 32, 0, st>>>(status, poll_limit);
+    return check_launch("wait_probe");
 }
 
 // ---------------------------------------------------------------------------------------------------------------

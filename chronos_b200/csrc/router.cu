@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(256) router_logits_small_kernel(const void* __
     __syncthreads();
     const bool ok = mbar_wait(smem_u32(&bar), 0);
     if (__syncthreads_or(!ok)) {
-        if (threadIdx.x == 0) atomicOr(status, 0x100);
+        if (threadIdx.x == 0) atomicOr(status, kStatusRouterTimeout);
         return;
     }
     for (int ew = warp; ew < ne; ew += 8) {
@@ -313,13 +313,15 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
     if (n_tokens <= 0) return CHRONOS_OK;
     const bool bf16 = x_dtype == CHRONOS_DTYPE_BF16;
     const size_t xrow = (size_t)L.hidden * (bf16 ? 2 : 4), wrow = (size_t)L.hidden * 4;
-    const int epc = (int)std::min<size_t>(8, (200 * 1024 - 4 * xrow) / wrow);
+    // router rows per CTA of the shared-memory kernel: what is left of 200 KiB after 4 activation rows; 0 (rows too
+    // long to stage, e.g. hidden 16384 in fp32) selects the register-tile kernel below
+    const size_t stage_budget = 200 * 1024;
+    const int epc = 4 * xrow + wrow <= stage_budget ? (int)std::min<size_t>(8, (stage_budget - 4 * xrow) / wrow) : 0;
     if (n_tokens <= 64 && epc >= 1 && status != nullptr) {
         const size_t smem = (size_t)epc * wrow + 4 * xrow;
         const unsigned grid = (unsigned)(((L.n_experts + epc - 1) / epc) * ((n_tokens + 3) / 4));
-        cudaError_t rc = bf16 ? cudaFuncSetAttribute(router_logits_small_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                              : cudaFuncSetAttribute(router_logits_small_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (rc != cudaSuccess) { set_error("router: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc)); return CHRONOS_E_LAUNCH; }
+        if (int rc = ensure_dynamic_smem(bf16 ? reinterpret_cast<const void*>(router_logits_small_kernel<true>)
+                                              : reinterpret_cast<const void*>(router_logits_small_kernel<false>), smem, "router")) return rc;
         if (bf16) router_logits_small_kernel<true><<<grid, 256, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, epc, tok_scale, status);
         else router_logits_small_kernel<false><<<grid, 256, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, epc, tok_scale, status);
     } else if (n_tokens <= 64) {
@@ -330,9 +332,8 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
     } else if (n_tokens >= 256) {  // large batches: shared-memory tiles of 64 tokens x 16 experts
         const unsigned grid = (unsigned)(((n_tokens + kRtTok - 1) / kRtTok) * ((L.n_experts + kRtExp - 1) / kRtExp));
         const size_t smem = (size_t)(bf16 ? kRtStagesBf16 : kRtStagesF32) * (kRtTok * 128 * (bf16 ? 2 : 4) + kRtExp * 512);
-        cudaError_t rc = bf16 ? cudaFuncSetAttribute(router_logits_tiled_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                              : cudaFuncSetAttribute(router_logits_tiled_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (rc != cudaSuccess) { set_error("router: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc)); return CHRONOS_E_LAUNCH; }
+        if (int rc = ensure_dynamic_smem(bf16 ? reinterpret_cast<const void*>(router_logits_tiled_kernel<true>)
+                                              : reinterpret_cast<const void*>(router_logits_tiled_kernel<false>), smem, "router")) return rc;
         if (bf16) router_logits_tiled_kernel<true><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
         else router_logits_tiled_kernel<false><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
     } else {

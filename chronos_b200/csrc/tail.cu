@@ -225,18 +225,12 @@ int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_d
         set_error("tail_pass: %d columns need %zu bytes of shared memory", a.K, smem);
         return CHRONOS_E_SHAPE;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sm_count();
     const long max_tiles = (long)p.max_gitems * (a.R / 128);
     const long resident = (long)sms * (smem * 3 <= 222 * 1024 ? 3 : (smem * 2 <= 222 * 1024 ? 2 : 1));
     const unsigned grid = (unsigned)(max_tiles < resident ? max_tiles : resident);
-    cudaError_t rc = bits == 2 ? cudaFuncSetAttribute(tail_pass_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                               : cudaFuncSetAttribute(tail_pass_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (rc != cudaSuccess) {
-        set_error("tail_pass: cannot opt in to %zu bytes of shared memory: %s", smem, cudaGetErrorString(rc));
-        return CHRONOS_E_LAUNCH;
-    }
+    if (int rc = ensure_dynamic_smem(bits == 2 ? reinterpret_cast<const void*>(tail_pass_kernel<2>) : reinterpret_cast<const void*>(tail_pass_kernel<1>),
+                                     smem, "tail_pass")) return rc;
     if (bits == 2) tail_pass_kernel<2><<<grid, 256, smem, st>>>(a);
     else tail_pass_kernel<1><<<grid, 256, smem, st>>>(a);
     return check_launch("tail_pass");

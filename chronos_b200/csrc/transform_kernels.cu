@@ -211,9 +211,7 @@ __global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, Pla
 int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int fp4, int many_pairs,
                   cudaStream_t st) {
     if (fp4 == 2) {
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int sms = device_sm_count();
         const long most = (long)p.max_gitems * (L.hidden / 256);
         const unsigned grid = (unsigned)(most < 3L * sms ? most : 3L * sms);
         pre_gu_wide_kernel<<<grid, 512, 0, st>>>(L, p);

@@ -24,6 +24,7 @@ GROUP_TENSOR_SUFFIXES = (  # chronos_1t/models/glm53_holo.py:45-51
     "tail.gu_bits", "tail.gu_packed", "tail.gu_scale",
     "tail.down_bits", "tail.down_packed", "tail.down_scale",
 )
+ROUTER_KINDS = {"softmax": _lib.ROUTER_SOFTMAX_TOPK, "sigmoid": _lib.ROUTER_SIGMOID_NOAUX, "sqrt_softplus": _lib.ROUTER_SQRT_SOFTPLUS}
 _REQUIRED = GROUP_TENSOR_SUFFIXES[:12]  # the tail lattice tensors are optional (include_tail)
 
 
@@ -38,7 +39,7 @@ class FoldedLayerConfig:
     group_size: int
     rank: int
     top_k: int
-    router: str = "softmax"        # "softmax" (top-k then softmax) or "sigmoid" (noaux_tc)
+    router: str = "softmax"        # "softmax" (top-k then softmax), "sigmoid" (noaux_tc) or "sqrt_softplus" (noaux_tc on sqrt(softplus))
     norm_topk_prob: bool = True
     routed_scaling_factor: float = 2.5
     seed_stride: int = keys.SEED_GROUP_STRIDE
@@ -59,7 +60,7 @@ class FoldedLayerConfig:
             raise ValueError("hidden and inter must be multiples of 128 (chronos_1t/models/glm53_chronos_spec.py:149-151)")
         if self.n_experts % self.group_size:
             raise ValueError("n_experts must be a multiple of group_size")
-        if self.router not in ("softmax", "sigmoid"):
+        if self.router not in ROUTER_KINDS:
             raise ValueError(f"unknown router flavour {self.router!r}")
         if self.key_generator != "torch_cpu_v1":
             raise ValueError("only key_generator = 'torch_cpu_v1' checkpoints can be read")
@@ -141,7 +142,7 @@ class PackedLayer:
         s = self.struct
         s.hidden, s.inter, s.n_experts, s.group_size, s.n_slots = cfg.hidden, cfg.inter, cfg.n_experts, cfg.group_size, cfg.n_slots
         s.rank, s.top_k = cfg.rank, cfg.top_k
-        s.router_kind = _lib.ROUTER_SOFTMAX_TOPK if cfg.router == "softmax" else _lib.ROUTER_SIGMOID_NOAUX
+        s.router_kind = ROUTER_KINDS[cfg.router]
         s.renorm = int(cfg.norm_topk_prob)
         s.routed_scaling = float(cfg.routed_scaling_factor)
         s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
@@ -318,7 +319,7 @@ class PackedLayer:
         gen = torch.Generator(device=device).manual_seed(seed)
         t = cls._random_slot_tensors(cfg, gen, device)
         t["router_w"] = torch.randn(cfg.router_experts, cfg.hidden, generator=gen, device=device) * 0.02
-        if cfg.router == "sigmoid":
+        if cfg.router != "softmax":
             t["e_bias"] = torch.zeros(cfg.router_experts, device=device)
         if with_shared:
             t.update(cls._random_shared_tensors(cfg, gen, device))
@@ -353,7 +354,7 @@ class PackedLayer:
         t = {n: torch.cat(v) for n, v in parts.items()}
         gen = torch.Generator(device=device).manual_seed(seed * 100003 + 99991)
         t["router_w"] = torch.randn(cfg_global.n_experts, cfg.hidden, generator=gen, device=device) * 0.02
-        if cfg.router == "sigmoid":
+        if cfg.router != "softmax":
             t["e_bias"] = torch.zeros(cfg_global.n_experts, device=device)
         if with_shared:
             t.update(cls._random_shared_tensors(cfg, gen, device))

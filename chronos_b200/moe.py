@@ -8,6 +8,7 @@ input raises - nothing here computes on the CPU.
 """
 from __future__ import annotations
 
+import os
 from pathlib import Path
 from typing import Any, Iterable
 
@@ -40,13 +41,19 @@ _REGIMES = {"auto": _lib.REGIME_AUTO, "stream": _lib.REGIME_STREAM, "tensor": _l
 # worker's stream (the reference's blocks are used the same way), so they never need scratch at the same time.
 # Two forwards that overlap on the SAME device from different streams would race on it.
 _WORKSPACE_POOL: dict[torch.device, torch.Tensor] = {}
+# Buffers the pool outgrew stay allocated: a CUDA graph captured while one of them was current replays with that
+# pointer baked in, and it is still large enough for the batch the graph was captured for.
+_WORKSPACE_RETIRED: list[torch.Tensor] = []
 
 
 class FoldedMoELayer(nn.Module):
     def __init__(self, layer_idx: int = 3, shard_path: str | Path | None = None, config: FoldedLayerConfig | None = None,
                  device: torch.device | str | None = None, packed: PackedLayer | None = None, vllm_config: Any = None,
-                 prefix: str = "", register: bool = True, **_: Any) -> None:
+                 prefix: str = "", register: bool = True, check_status: bool | None = None, **_: Any) -> None:
         super().__init__()
+        # opt-in: read the device status word after every forward (a synchronisation per call) and raise when a kernel
+        # reported an expired wait; off by default because it breaks stream-ordered / graph-captured use
+        self.check_status = bool(int(os.environ.get("CHRONOS_B200_CHECK_STATUS", "0"))) if check_status is None else check_status
         if vllm_config is not None:
             idx = layer_index_from_prefix(prefix)
             if idx is not None:
@@ -84,8 +91,9 @@ class FoldedMoELayer(nn.Module):
 
     # -- plumbing ---------------------------------------------------------------------------------------------------
     def _workspace(self, n_tokens: int) -> torch.Tensor:
-        """Scratch from the per-device pool; it only ever grows, so a captured graph keeps seeing a valid pointer as
-        long as the largest batch has been run once before capture."""
+        """Scratch from the per-device pool. The pool only grows, and a buffer it outgrows is kept alive, so a graph
+        captured earlier keeps replaying on valid memory. Growing inside a stream capture is refused (an allocation there
+        would belong to the graph's private pool): run the largest batch once, or call `reserve_workspace`, before capture."""
         need = self._ws_need.get(n_tokens)
         if need is None:
             need = _lib.lib().chronos_b200_workspace_bytes(self.packed.ptr, n_tokens)
@@ -94,10 +102,19 @@ class FoldedMoELayer(nn.Module):
             self._ws_need[n_tokens] = need
         buf = _WORKSPACE_POOL.get(self.device)
         if buf is None or buf.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise _lib.ChronosError(f"the workspace would have to grow to {need} bytes inside a stream capture: run this "
+                                        "batch size once (or call reserve_workspace) before capturing")
+            if buf is not None:
+                _WORKSPACE_RETIRED.append(buf)
             buf = torch.empty(need, dtype=torch.uint8, device=self.device)
             _WORKSPACE_POOL[self.device] = buf
         self._ws = buf
         return buf
+
+    def reserve_workspace(self, max_tokens: int) -> None:
+        """Sizes the device's scratch pool for batches of up to `max_tokens` tokens ahead of time."""
+        self._workspace(max_tokens)
 
     def _prep(self, hidden_states: torch.Tensor) -> torch.Tensor:
         if not hidden_states.is_cuda:
@@ -119,6 +136,13 @@ class FoldedMoELayer(nn.Module):
         if off < 0:
             raise _lib.ChronosError("workspace_status_offset rejected the layer description")
         return int(self._ws[off:off + 4].view(torch.int32).item())
+
+    def _after_call(self) -> None:
+        if self.check_status:
+            st = self.device_status()
+            if st != 0:
+                raise _lib.ChronosError(f"device status word 0x{st:x} after the forward: a kernel gave up a bounded wait "
+                                        "(bits are listed in include/chronos_b200.h); the output of this call is invalid")
 
     def load_weights(self, weights: Iterable[tuple[str, torch.Tensor]]) -> set[str]:
         """Drains and ignores vLLM's weight stream (chronos_1t/models/glm53_chronos_moe.py:386-389)."""
@@ -164,6 +188,7 @@ class FoldedMoELayer(nn.Module):
         _lib.check(_lib.lib().chronos_b200_folded_moe_routed(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, ids.data_ptr(),
                                                            w.data_ptr(), int(sh_first), int(sh_count), _REGIMES[regime], y.data_ptr(), _DTYPES[out_dtype],
                                                            ws.data_ptr(), ws.numel(), self._stream()))
+        self._after_call()
         return y
 
     @torch.no_grad()
@@ -188,6 +213,7 @@ class FoldedMoELayer(nn.Module):
                   "tensor_fp4": _lib.lib().chronos_b200_folded_moe_prefill}[regime]
             _lib.check(fn(self.packed.ptr, x.data_ptr(), _DTYPES[x.dtype], n, y.data_ptr(),
                           _DTYPES[x.dtype], ws.data_ptr(), ws.numel(), self._stream()))
+            self._after_call()
         return y.to(orig_dtype).view(orig_shape)
 
     def forward(self, hidden_states: torch.Tensor, *args: Any, **kwargs: Any) -> torch.Tensor:

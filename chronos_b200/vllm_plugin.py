@@ -63,7 +63,8 @@ def config_from_checkpoint(model_dir: Path) -> FoldedLayerConfig | None:
             hidden=int(text["hidden_size"]), inter=int(text["moe_intermediate_size"]),
             n_experts=int(text["n_routed_experts"]), group_size=int(holo.get("group_size", 8)),
             rank=int(holo.get("svd_rank", 64)), top_k=int(text["num_experts_per_tok"]),
-            router="sigmoid" if text.get("scoring_func", "sigmoid") == "sigmoid" else "softmax",
+            router={"sigmoid": "sigmoid", "sqrtsoftplus": "sqrt_softplus", "sqrt_softplus": "sqrt_softplus"}.get(
+                str(text.get("scoring_func", "sigmoid")), "softmax"),
             norm_topk_prob=bool(text.get("norm_topk_prob", True)),
             routed_scaling_factor=float(text.get("routed_scaling_factor", 2.5)),
             key_generator=str(holo.get("key_generator", "torch_cpu_v1")),

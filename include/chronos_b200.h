@@ -42,6 +42,8 @@ extern "C" {
 
 #define CHRONOS_ROUTER_SOFTMAX_TOPK 0 /* chronos_1t/models/vllm_chronos_moe.py:310-314     */
 #define CHRONOS_ROUTER_SIGMOID_NOAUX 1 /* chronos_1t/models/glm53_chronos_moe.py:392-399    */
+#define CHRONOS_ROUTER_SQRT_SOFTPLUS 2 /* chronos_1t/models/dsv41_chronos_moe.py:3402-3410: choose by
+                                          sqrt(softplus(logit)) + bias, weigh by the unbiased scores, renorm, scaling */
 
 /* One folded MoE layer resident in HBM.
  *
@@ -116,9 +118,10 @@ typedef struct chronos_layer {
 int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, const float* scale_2, float* out,
                                int rows, int cols, void* stream);
 
-/* Weight-space reconstruction probe of ONE expert: out f32 = beta * unbind(bank) + U.V  (no tail).
- * which = 0: gate_up [2I, H]; which = 1: down [H, I].  `scratch` holds rows*cols floats.
- * Replaces: reconstruct_group_experts(include_tail=False), chronos_1t/models/glm53_holo.py:336-368. */
+/* Weight-space reconstruction probe of ONE expert: out f32 = beta * unbind(bank) + U.V, plus the tail-lattice term
+ * when the layer carries one (tail_bits != 0).  which = 0: gate_up [2I, H]; which = 1: down [H, I].  `scratch` holds
+ * rows*cols floats.  Stream-ordered like every other entry point: no copy to the host, no synchronisation.
+ * Replaces: reconstruct_group_experts(include_tail = tail_bits != 0), chronos_1t/models/glm53_holo.py:336-368. */
 int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, int which, float* out, float* scratch,
                                     void* stream);
 
@@ -130,7 +133,7 @@ int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, in
  * rows * cols <= 4,194,304 are accepted (e.g. 1536 x 2048); larger ones are refused with CHRONOS_E_SHAPE and a
  * message naming the limit - use the entry point above for those.  The entry point calls no cudaMalloc / cudaFree
  * and no allocating library routine.  The first call on a device looks up the array's device address (the device
- * must be current; make that first call outside any stream capture).  All calls on a device share the one array:
+ * must be current; that look-up is a runtime query, so make the first call on a device before any stream capture).  All calls on a device share the one array:
  * its previous contents are simply overwritten (nothing needs clearing), and two calls that overlap on the GPU -
  * different streams, or a second call issued before the first finished on another stream - race on it.
  * This entry point has no counterpart in the reference. */
@@ -213,10 +216,30 @@ int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, i
 int chronos_b200_set_stage_events(void** events, int n_events);
 
 /* Byte offset, inside a workspace laid out for n_tokens, of the int32 device status word that the forward entry
- * points clear at the start of a call and kernels raise on a device-side anomaly (bit 0x10: a bounded wait in the
- * streaming bank kernel expired).  Read it after synchronising the stream.  Returns -1 on bad arguments.
+ * points clear at the start of a call and kernels raise on a device-side anomaly.  Every wait inside a kernel (on a
+ * shared-memory barrier, or on the other CTAs of its grid) is bounded to about a second; a kernel whose wait runs
+ * out raises its bit, stops feeding its pipeline, lets its copies in flight land, frees its tensor memory and
+ * returns - the output of that call is then garbage, the context stays usable.  Bits:
+ *   CHRONOS_STATUS_BANK_STREAM 0x10   streaming bank pass (CUDA-core conversion)     CHRONOS_STATUS_BANK_GEMM 0x20  fp16 grouped GEMM
+ *   CHRONOS_STATUS_FP4_PROBE   0x40   chronos_b200_fp4_mma_probe                     CHRONOS_STATUS_BANK_FP4  0x80  FP4 bank passes
+ *   CHRONOS_STATUS_ROUTER      0x100  router row staging                             CHRONOS_STATUS_WAIT_PROBE 0x200 chronos_b200_wait_probe
+ *   CHRONOS_STATUS_GRID_SYNC   0x400  a fused decode kernel waiting for the other CTAs of its grid
+ * Read it after synchronising the stream.  Returns -1 on bad arguments.
  * No counterpart in the reference (its kernels have no device-side waits). */
+#define CHRONOS_STATUS_BANK_STREAM 0x10
+#define CHRONOS_STATUS_BANK_GEMM 0x20
+#define CHRONOS_STATUS_FP4_PROBE 0x40
+#define CHRONOS_STATUS_BANK_FP4 0x80
+#define CHRONOS_STATUS_ROUTER 0x100
+#define CHRONOS_STATUS_WAIT_PROBE 0x200
+#define CHRONOS_STATUS_GRID_SYNC 0x400
 long chronos_b200_workspace_status_offset(const chronos_layer_t* layer, int n_tokens);
+
+/* Exercises the give-up path of the library's bounded waits without any fault: a one-warp kernel waits, through the
+ * same bounded wait the bank kernels use, on a shared-memory barrier that nothing will ever complete; after
+ * poll_limit polls (1..4096, about a microsecond each) it raises CHRONOS_STATUS_WAIT_PROBE in *status (device int32,
+ * clear it first) and returns.  No counterpart in the reference. */
+int chronos_b200_wait_probe(int32_t* status, unsigned poll_limit, void* stream);
 
 /* Message for the last non-zero status returned to the calling thread ("" if none). */
 const char* chronos_b200_last_error(void);

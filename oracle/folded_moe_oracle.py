@@ -228,21 +228,8 @@ def reconstruct_expert(g: dict, g_idx: int, m: int, hidden: int, inter: int, inc
 def expert_forward_activation_space(x: np.ndarray, g: dict, g_idx: int, m: int, hidden: int, inter: int) -> np.ndarray:
     """chronos_1t/models/glm5_chronos_moe.py:149-195 with the hard-coded 4096/2048 dims made generic, fp32.
     The bank is used as stored; only activations are transformed. x [n, H] -> y [n, H]."""
-    seed_gu, seed_dn = group_seed_bases(g_idx)
-    s_gu = unpack_nvfp4(g["s_gu.weight"], g["s_gu.weight_scale"], g["s_gu.weight_scale_2"])
-    s_dn = unpack_nvfp4(g["s_down.weight"], g["s_down.weight_scale"], g["s_down.weight_scale_2"])
-    r_s1, _, r_inv, r_s2, c_s1, c_perm, _, c_s2 = expert_keys(2 * inter, hidden, m, seed_gu)
     x = np.asarray(x, dtype=np.float32)
-    x_c = _had_blocks((x * c_s1[None, :])[:, c_perm]) * c_s2[None, :]
-    z = _had_blocks((x_c @ s_gu.T) * r_s2[None, :])[:, r_inv] * r_s1[None, :]
-    u, v = e4m3_to_f32(g["healer.u_gu"][m]), e4m3_to_f32(g["healer.v_gu"][m])
-    z = np.float32(g["s_gu.beta"][m]) * z + (x @ v.T) @ u.T
-    act = silu(z[:, :inter]) * z[:, inter:]
-    r_s1, _, r_inv, r_s2, c_s1, c_perm, _, c_s2 = expert_keys(hidden, inter, m, seed_dn)
-    a_c = _had_blocks((act * c_s1[None, :])[:, c_perm]) * c_s2[None, :]
-    y = _had_blocks((a_c @ s_dn.T) * r_s2[None, :])[:, r_inv] * r_s1[None, :]
-    u, v = e4m3_to_f32(g["healer.u_down"][m]), e4m3_to_f32(g["healer.v_down"][m])
-    return (np.float32(g["s_down.beta"][m]) * y + (act @ v.T) @ u.T).astype(np.float32)
+    return _expert_rows_activation_space(x, g, g_idx, m, hidden, inter, unpack_banks(g))
 
 
 def silu(z: np.ndarray) -> np.ndarray:
@@ -290,27 +277,62 @@ def router_logits_fixed(x: np.ndarray, wr: np.ndarray) -> np.ndarray:
 
 
 def topk_desc(vals: np.ndarray, k: int) -> np.ndarray:
-    """Indices of the k largest per row, descending; equal values -> lower index first."""
-    order = np.lexsort((np.broadcast_to(np.arange(vals.shape[1]), vals.shape), -vals.astype(np.float64)), axis=1)
-    return order[:, :k].astype(np.int64)
+    """Indices of the k largest per row, descending; equal values -> lower index first. A candidate that is NaN or
+    -inf can never be chosen: once only such candidates are left the remaining positions hold -1 (an entry every
+    consumer skips). The reference's `torch.topk` has no defined answer for NaN rows; this is the stated rule of the
+    device kernels."""
+    v = np.asarray(vals, dtype=np.float64)
+    v = np.where(np.isnan(v), -np.inf, v)
+    order = np.lexsort((np.broadcast_to(np.arange(v.shape[1]), v.shape), -v), axis=1)
+    ids = order[:, :k].astype(np.int64)
+    chosen = np.take_along_axis(v, ids, axis=1)
+    return np.where(np.isneginf(chosen), -1, ids)
+
+
+def _gather_valid(src: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    """src[t, ids[t, j]] with 0 where ids is -1."""
+    return np.where(ids >= 0, np.take_along_axis(src, np.maximum(ids, 0), axis=1), np.float32(0.0)).astype(np.float32)
 
 
 def router_softmax_topk(logits: np.ndarray, k: int):
     """chronos_1t/models/vllm_chronos_moe.py:310-314: topk(logits) then softmax over the k values (fp32)."""
     ids = topk_desc(logits, k)
-    tv = np.take_along_axis(logits, ids, axis=1).astype(np.float32)
-    ex = np.exp((tv - tv.max(axis=1, keepdims=True)).astype(np.float32)).astype(np.float32)
-    return ids, (ex / ex.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    tv = _gather_valid(logits, ids)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        ex = np.where(ids >= 0, np.exp((tv - tv[:, :1]).astype(np.float32)), np.float32(0.0)).astype(np.float32)
+        w = (ex / ex.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    return ids, np.where(ids >= 0, w, np.float32(0.0)).astype(np.float32)
+
+
+def _noaux_topk(scores: np.ndarray, e_bias, k: int, routed_scaling: float, renorm: bool):
+    """`noaux_tc` selection shared by the sigmoid and sqrt-softplus routers: choose by score + bias, weigh by the
+    unbiased scores, optional renormalisation, times the routed scaling factor."""
+    bias = np.zeros(scores.shape[1], dtype=np.float32) if e_bias is None else np.asarray(e_bias, dtype=np.float32)
+    ids = topk_desc(scores + bias[None, :], k)
+    w = _gather_valid(scores, ids)
+    if renorm:
+        w = w / (w.sum(axis=1, keepdims=True, dtype=np.float32) + np.float32(1e-20))
+    return ids, np.where(ids >= 0, w * np.float32(routed_scaling), np.float32(0.0)).astype(np.float32)
 
 
 def router_sigmoid_topk(logits: np.ndarray, e_bias: np.ndarray, k: int, routed_scaling: float = 2.5, renorm: bool = True):
     """chronos_1t/models/glm53_chronos_moe.py:392-399 (`noaux_tc`): choose by sigmoid+bias, weigh by unbiased scores."""
     scores = (1.0 / (1.0 + np.exp(-logits.astype(np.float32)))).astype(np.float32)
-    ids = topk_desc(scores + np.asarray(e_bias, dtype=np.float32)[None, :], k)
-    w = np.take_along_axis(scores, ids, axis=1)
-    if renorm:
-        w = w / (w.sum(axis=1, keepdims=True, dtype=np.float32) + np.float32(1e-20))
-    return ids, (w * np.float32(routed_scaling)).astype(np.float32)
+    return _noaux_topk(scores, e_bias, k, routed_scaling, renorm)
+
+
+def softplus(x: np.ndarray) -> np.ndarray:
+    """torch.nn.functional.softplus with beta 1, threshold 20 (fp32): x above the threshold passes through."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        return np.where(x > np.float32(20.0), x, np.log1p(np.exp(x)).astype(np.float32)).astype(np.float32)
+
+
+def router_sqrt_softplus_topk(logits: np.ndarray, e_bias, k: int, routed_scaling: float = 1.5, renorm: bool = True):
+    """chronos_1t/models/dsv41_chronos_moe.py:3402-3410: scores = sqrt(softplus(logits)); topk(scores + bias); weights =
+    unbiased scores, divided by their sum (+1e-20), times routed_scaling_factor."""
+    scores = np.sqrt(softplus(logits)).astype(np.float32)
+    return _noaux_topk(scores, e_bias, k, routed_scaling, renorm)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -329,6 +351,8 @@ def moe_layer_forward(x, groups, router_w, top_k, hidden, inter, group_size, rou
         logits = router_logits_fixed(x, router_w)
     if router == "softmax":
         ids, w = router_softmax_topk(logits, top_k)
+    elif router == "sqrt_softplus":
+        ids, w = router_sqrt_softplus_topk(logits, e_bias, top_k, routed_scaling)
     else:
         ids, w = router_sigmoid_topk(logits, e_bias, top_k, routed_scaling)
     y = np.zeros((n_tok, hidden), dtype=np.float32)
@@ -336,7 +360,7 @@ def moe_layer_forward(x, groups, router_w, top_k, hidden, inter, group_size, rou
     flat_w = w.reshape(-1)
     tok_of = np.repeat(np.arange(n_tok), top_k)
     bank_cache: tuple = (-1, None)  # each distinct slot is dequantised once (chronos_1t/models/glm5_chronos_moe.py:530-539)
-    for eid in np.unique(flat_ids):
+    for eid in np.unique(flat_ids[flat_ids >= 0]):  # -1 = no expert chosen (see topk_desc)
         sel = np.nonzero(flat_ids == eid)[0]
         g_idx, m = int(eid) // group_size, int(eid) % group_size
         if bank_cache[0] != g_idx:
@@ -354,6 +378,53 @@ def moe_layer_forward(x, groups, router_w, top_k, hidden, inter, group_size, rou
     if return_routing:
         return y.astype(np.float32), ids, w
     return y.astype(np.float32)
+
+
+def routed_tokens_activation_space(x, ids, gates, groups, hidden, inter, group_size, shared=None, first_slot=0):
+    """Layer output rows for explicit routing, evaluated in activation space: every (token, expert) pair goes through
+    `expert_forward_activation_space` (chronos_1t/models/glm5_chronos_moe.py:149-195), pairs grouped by expert and the
+    slot's banks dequantised once per slot (chronos_1t/models/glm5_chronos_moe.py:530-539). Algebraically the same as
+    multiplying by the fp32 reconstruction (the two are pinned against each other by the golden tests) but without
+    forming any [rows, cols] expert matrix, so a sample of tokens of a full-size layer takes seconds.
+    x [n, H] fp32, ids [n, k] (global expert ids, < 0 skipped), gates [n, k]; `groups[g - first_slot]` is slot g.
+    `shared` = optional (gu [2I, H], down [H, I]) fp32 always-on expert."""
+    x = np.asarray(x, dtype=np.float32)
+    ids = np.asarray(ids)
+    gates = np.asarray(gates, dtype=np.float32)
+    y = np.zeros((x.shape[0], hidden), dtype=np.float32)
+    order = sorted({int(e) for e in ids.reshape(-1) if e >= 0})
+    cache: tuple = (-1, None)
+    for eid in order:
+        g_idx, m = eid // group_size, eid % group_size
+        g = groups[g_idx - first_slot]
+        if cache[0] != g_idx:
+            cache = (g_idx, unpack_banks(g))
+        t_idx, j_idx = np.nonzero(ids == eid)
+        out = _expert_rows_activation_space(x[t_idx], g, g_idx, m, hidden, inter, cache[1])
+        np.add.at(y, t_idx, out * gates[t_idx, j_idx][:, None])
+    if shared is not None:
+        sgu, sdn = shared
+        si = sdn.shape[1]
+        z = x @ sgu.T
+        y = y + (silu(z[:, :si]) * z[:, si:]) @ sdn.T
+    return y.astype(np.float32)
+
+
+def _expert_rows_activation_space(x, g, g_idx, m, hidden, inter, banks):
+    """`expert_forward_activation_space` with the slot's dequantised banks supplied by the caller."""
+    seed_gu, seed_dn = group_seed_bases(g_idx)
+    s_gu, s_dn = banks
+    r_s1, _, r_inv, r_s2, c_s1, c_perm, _, c_s2 = expert_keys(2 * inter, hidden, m, seed_gu)
+    x_c = _had_blocks((x * c_s1[None, :])[:, c_perm]) * c_s2[None, :]
+    z = _had_blocks((x_c @ s_gu.T) * r_s2[None, :])[:, r_inv] * r_s1[None, :]
+    u, v = e4m3_to_f32(g["healer.u_gu"][m]), e4m3_to_f32(g["healer.v_gu"][m])
+    z = np.float32(g["s_gu.beta"][m]) * z + (x @ v.T) @ u.T
+    act = silu(z[:, :inter]) * z[:, inter:]
+    r_s1, _, r_inv, r_s2, c_s1, c_perm, _, c_s2 = expert_keys(hidden, inter, m, seed_dn)
+    a_c = _had_blocks((act * c_s1[None, :])[:, c_perm]) * c_s2[None, :]
+    yv = _had_blocks((a_c @ s_dn.T) * r_s2[None, :])[:, r_inv] * r_s1[None, :]
+    u, v = e4m3_to_f32(g["healer.u_down"][m]), e4m3_to_f32(g["healer.v_down"][m])
+    return (np.float32(g["s_down.beta"][m]) * yv + (act @ v.T) @ u.T).astype(np.float32)
 
 
 def rms_norm(x: np.ndarray, eps: float = 1e-6, weight=None) -> np.ndarray:

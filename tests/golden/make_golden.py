@@ -14,6 +14,8 @@ functions return on those bytes:
   * `pack_nvfp4` of a seeded matrix incl. an all-tiny block       (byte-exact target)
   * softmax-top-k and sigmoid-noaux_tc routers (torch CPU)        (ids exact, gates fp32)
   * the routed layer output, grouped dense loop in fp32 torch     (layer tolerance target)
+plus one router-only case at the benchmark's shape (288 experts x hidden 4096 x 512 tokens): logits, ids and gates of
+the softmax, sigmoid `noaux_tc` and sqrt-softplus `noaux_tc` routers as the reference computes them.
 The fixtures are small `.npz` files; fp8 tensors are stored as uint8 bit patterns.
 """
 from __future__ import annotations
@@ -126,8 +128,49 @@ def make_case(name: str, c: dict) -> None:
     print(name, "->", (HERE / f"{name}.npz").stat().st_size, "bytes")
 
 
+ROUTER_CASE = dict(name="router_e288_h4096", experts=288, hidden=4096, tokens=512, top_k=8, seed=11)
+
+
+def router_case_inputs(c: dict = ROUTER_CASE):
+    """Seeded inputs of the router-only case (torch CPU generator): bf16-rounded activations, router table, bias.
+    The tests regenerate them from the seed, so the fixture only stores what the reference computed from them."""
+    gen = torch.Generator().manual_seed(c["seed"])
+    x = torch.randn(c["tokens"], c["hidden"], generator=gen).to(torch.bfloat16).float()
+    router_w = torch.randn(c["experts"], c["hidden"], generator=gen) * 0.02
+    e_bias = torch.randn(c["experts"], generator=gen) * 0.05
+    return x, router_w, e_bias
+
+
+def make_router_case(c: dict = ROUTER_CASE) -> None:
+    """Router at the benchmark's own shape (288 experts, hidden 4096), the three flavours exactly as the reference
+    writes them: chronos_1t/models/vllm_chronos_moe.py:310-314, chronos_1t/models/glm53_chronos_moe.py:392-399,
+    chronos_1t/models/dsv41_chronos_moe.py:3402-3410. Stores logits, ids and gates only."""
+    x, router_w, e_bias = router_case_inputs(c)
+    k = c["top_k"]
+    out: dict[str, np.ndarray] = {"meta": np.array([c["experts"], c["hidden"], c["tokens"], k, c["seed"]], dtype=np.int64)}
+    logits = F.linear(x.float(), router_w.float())
+    tv, ti = torch.topk(logits, k=k, dim=-1)
+    out["logits"] = _np(logits)
+    out["softmax_ids"], out["softmax_gates"] = _np(ti).astype(np.int16), _np(F.softmax(tv, dim=-1))
+    scores = torch.sigmoid(x.float() @ router_w.T)
+    _, si = torch.topk(scores + e_bias, k, dim=-1)
+    sw = scores.gather(1, si)
+    sw = sw / (sw.sum(-1, keepdim=True) + 1e-20)
+    out["sigmoid_ids"], out["sigmoid_gates"] = _np(si).astype(np.int16), _np(sw * 2.5)
+    raw = F.linear(x, router_w).float()
+    sc = F.softplus(raw).sqrt()
+    _, qi = torch.topk(sc + e_bias.unsqueeze(0), k=k, dim=-1)
+    qw = sc.gather(1, qi)
+    out["sqrt_softplus_ids"] = _np(qi).astype(np.int16)
+    out["sqrt_softplus_gates"] = _np((qw / (qw.sum(dim=-1, keepdim=True) + 1e-20)) * 1.5)
+    np.savez_compressed(HERE / f"{c['name']}.npz", **out)
+    print(c["name"], "->", (HERE / f"{c['name']}.npz").stat().st_size, "bytes")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     for nm, cfg in CASES.items():
         if len(sys.argv) < 2 or nm in sys.argv[1:]:
             make_case(nm, cfg)
+    if len(sys.argv) < 2 or ROUTER_CASE["name"] in sys.argv[1:]:
+        make_router_case()

@@ -153,6 +153,60 @@ def test_router_bit_exact_large(n_tok, dtype):
     assert np.allclose(w.cpu().numpy(), ref_w, rtol=2e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("flavour", ["softmax", "sigmoid", "sqrt_softplus"])
+def test_router_at_benchmark_shape_vs_reference(flavour):
+    """288 experts x hidden 4096 x 512 bf16 tokens: device ids against the reference's own torch router (golden file).
+    Logits are bit-equal to the oracle's stated order; tokens whose k / k+1 choice scores are closer than the fp32
+    summation error are counted apart from true mismatches, of which there must be none."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+    from conftest import compare_router_ids, router_case, router_choice_scores
+
+    gold, x, router_w, e_bias, k = router_case()
+    e, h = router_w.shape
+    cfg = FoldedLayerConfig(hidden=h, inter=128, n_experts=e, group_size=4, rank=16, top_k=k, router=flavour,
+                            routed_scaling_factor=1.5 if flavour == "sqrt_softplus" else 2.5)
+    packed = PackedLayer.synthetic(cfg, seed=5)
+    packed.t["router_w"].copy_(torch.from_numpy(router_w))
+    if flavour != "softmax":
+        packed.t["e_bias"].copy_(torch.from_numpy(e_bias))
+    layer = FoldedMoELayer(packed=packed, register=False)
+    ids, w = layer.route(torch.from_numpy(x).cuda().to(torch.bfloat16))
+    fixed = O.router_logits_fixed(x, router_w)
+    assert np.array_equal(layer.last_logits.cpu().numpy().view(np.uint32), fixed.view(np.uint32))
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    rep = compare_router_ids(ids, gold[f"{flavour}_ids"], router_choice_scores(gold["logits"], flavour, e_bias), k)
+    print(flavour, rep)
+    assert rep["true_mismatch_tokens"] == 0 and rep["near_tie_tokens"] <= rep["tokens"] // 50, rep
+    same = (ids == gold[f"{flavour}_ids"]).all(axis=1)
+    assert np.allclose(w[same], gold[f"{flavour}_gates"][same], rtol=3e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("flavour", ["softmax", "sigmoid"])
+def test_nan_activation_row_selects_no_expert(flavour):
+    """A token whose hidden row is NaN has NaN logits: no candidate can win, the token gets ids -1 / gates 0 and its
+    routed output is skipped; the other tokens of the batch are unaffected and no address is formed from a bad id."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=4, router=flavour)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=31), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    for n_tok in (5, 70):  # top-k fused into the plan launch / the router's own top-k kernel
+        x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda")
+        clean = layer(x).clone()
+        xb = x.clone()
+        xb[2] = float("nan")
+        ids, w = layer.route(xb)
+        assert ids[2].tolist() == [-1] * 4 and w[2].tolist() == [0.0] * 4
+        ref_ids, ref_w = (O.router_softmax_topk if flavour == "softmax" else
+                          (lambda lg, k: O.router_sigmoid_topk(lg, layer.packed.t["e_bias"].cpu().numpy(), k)))(layer.last_logits.cpu().numpy(), 4)
+        assert np.array_equal(ids.cpu().numpy(), ref_ids)
+        y = layer(xb)
+        assert layer.device_status() == 0
+        keep = [t for t in range(n_tok) if t != 2]
+        assert torch.equal(y[keep], clean[keep])
+        assert torch.count_nonzero(y[2]) == 0  # no shared expert in this layer: nothing was added for the token
+
+
 def test_layer_output_matches_reference(golden):
     for flavour in ("softmax", "sigmoid"):
         layer = _golden_layer(golden, flavour)
@@ -460,6 +514,41 @@ def test_fp4_tensor_core_operand_format(n_stages, b_rows):
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max(), np.abs(got - ref).max() / np.abs(ref).max()
 
 
+def test_bounded_wait_gives_up_and_reports():
+    """A wait that can never complete runs out after its poll limit, raises its status bit and lets the kernel return:
+    no fault, no hang, and the context keeps working (the next launch below runs normally)."""
+    from chronos_b200 import _lib
+
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().chronos_b200_wait_probe(status.data_ptr(), 64, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0x200
+    assert _lib.lib().chronos_b200_wait_probe(status.data_ptr(), 0, None) == -5
+    assert float(torch.ones(8, device="cuda").sum().item()) == 8.0
+
+
+def test_router_with_long_rows_matches_oracle():
+    """hidden 16384 in fp32: the rows do not fit the shared-memory staging of the small-batch router kernel, the
+    register-tile kernel takes over with the same bits."""
+    from chronos_b200 import FoldedLayerConfig, _lib
+    from chronos_b200.layout import ROUTER_KINDS
+
+    h, e, k, n = 16384, 16, 4, 5
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(n, h, generator=gen, device="cuda")
+    wr = torch.randn(e, h, generator=gen, device="cuda") * 0.02
+    s = _lib.LayerStruct()
+    s.hidden, s.n_experts, s.top_k, s.router_kind, s.router_w = h, e, k, ROUTER_KINDS["softmax"], wr.data_ptr()
+    ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
+    gates = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    logits = torch.empty((n, e), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().chronos_b200_router_topk(s, x.data_ptr(), 0, n, ids.data_ptr(), gates.data_ptr(), logits.data_ptr(),
+                                                  torch.cuda.current_stream().cuda_stream))
+    fixed = O.router_logits_fixed(x.cpu().numpy(), wr.cpu().numpy())
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), fixed.view(np.uint32))
+    assert np.array_equal(ids.cpu().numpy(), O.router_softmax_topk(fixed, k)[0])
+
+
 def test_residual_rmsnorm_matches_oracle():
     from chronos_b200 import residual_rmsnorm
 
@@ -493,3 +582,62 @@ def test_bad_arguments_raise(golden):
     rc = _lib.lib().chronos_b200_folded_moe_decode(layer.packed.ptr, x.data_ptr(), 0, x.shape[0], y.data_ptr(), 0,
                                                    ws.data_ptr(), ws.numel(), None)
     assert rc == -3 and b"workspace" in _lib.lib().chronos_b200_last_error()
+
+
+@pytest.fixture(scope="module")
+def decode_shaped_layer():
+    """The benchmark's layer (hidden 4096, 288 + 1 experts, top-8, inter 1536, fold 4, rank 64) with seeded synthetic bytes."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+    from chronos_b200.workloads import DECODE
+
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(FoldedLayerConfig(**DECODE), seed=2, with_shared=True), register=False)
+    yield layer
+    del layer
+    torch.cuda.empty_cache()
+
+
+def _sampled_parity(layer, x, y, ids, w, sample):
+    """rel-L2 of sampled output rows against the activation-space oracle (explicit routing + shared expert)."""
+    c = layer.cfg
+    groups, ex = layer.packed.to_groups_numpy()
+    i = c.inter
+    shared = (np.concatenate([O.unpack_nvfp4(ex["sh_gu_w"][:i], ex["sh_gu_s"][:i], ex["sh_gu_s2"][0]),
+                              O.unpack_nvfp4(ex["sh_gu_w"][i:], ex["sh_gu_s"][i:], ex["sh_gu_s2"][1])]),
+              O.unpack_nvfp4(ex["sh_dn_w"], ex["sh_dn_s"], ex["sh_dn_s2"][0]))
+    sel = torch.as_tensor(sample, device=x.device)
+    ref = O.routed_tokens_activation_space(x[sel].float().cpu().numpy(), ids[sel].cpu().numpy(), w[sel].cpu().numpy(), groups,
+                                           c.hidden, c.inter, c.group_size, shared=shared)
+    return _rel_l2(y[sel].float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("n_tokens", [8192, 4096])
+def test_prefill_shaped_layer_at_benchmark_size(decode_shaped_layer, n_tokens):
+    """The prefill configuration at its own shape: 8192 (and 4096, the per-step batch of the 42-layer stack) bf16 tokens,
+    router popularity Zipf(1.1) (one expert with thousands of pairs next to experts with one or none), through the
+    auto regime and the forced FP4 tensor regime. A token's output depends only on its own routing, so a sample of
+    tokens - including tokens of the most popular expert and of the least popular ones - is compared with the oracle."""
+    from chronos_b200.workloads import zipf_prefill_batch
+
+    layer = decode_shaped_layer
+    cfg = layer.cfg
+    x = zipf_prefill_batch(layer, n_tokens)
+    ids, w = layer.route(x)
+    ref_ids, _ = O.router_softmax_topk(O.router_logits_fixed(x[:64].float().cpu().numpy(), layer.packed.t["router_w"].cpu().numpy()), cfg.top_k)
+    assert np.array_equal(ids[:64].cpu().numpy(), ref_ids)
+    counts = torch.bincount(ids.reshape(-1).long(), minlength=cfg.n_experts)
+    assert int(counts.max()) > n_tokens // 2 and int((counts <= 2).sum()) > 0, "the batch must be skewed, or the test proves nothing"
+    hot, cold = int(counts.argmax()), [int(e) for e in torch.nonzero((counts > 0) & (counts <= 2)).flatten()[:6]]
+    sample = torch.nonzero((ids == hot).any(dim=1)).flatten()[:10].tolist()
+    for e in cold:
+        sample += torch.nonzero((ids == e).any(dim=1)).flatten()[:1].tolist()
+    gen = torch.Generator().manual_seed(n_tokens)
+    sample += torch.randint(0, n_tokens, (32 - len(sample),), generator=gen).tolist()
+    sample = sorted(set(sample))
+    y_auto = layer.forward_impl(x, regime="auto")
+    assert layer.device_status() == 0
+    y_fp4 = layer.forward_impl(x, regime="tensor_fp4")
+    assert layer.device_status() == 0
+    assert torch.equal(y_auto, y_fp4), "the auto regime must pick the FP4 tensor regime for this batch"
+    err = _sampled_parity(layer, x, y_fp4, ids, w, sample)
+    print(f"prefill-shaped layer, {n_tokens} tokens: rel-L2 over {len(sample)} sampled tokens = {err:.3e}, hottest expert {int(counts.max())} pairs")
+    assert err <= LAYER_TOL

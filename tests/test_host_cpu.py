@@ -59,6 +59,40 @@ def test_host_rejects_bad_layer_without_a_gpu():
         _lib.check(rc)
 
 
+def _router_struct(hidden, n_experts, top_k, router_w_addr):
+    s = _lib.LayerStruct()
+    s.hidden, s.n_experts, s.top_k, s.router_kind, s.router_w = hidden, n_experts, top_k, 0, router_w_addr
+    return s
+
+
+def test_router_rejects_misaligned_table_on_the_host():
+    """The router kernels fetch rows with 16-byte bulk copies and vector loads: a table that is not 16-byte aligned
+    is refused with CHRONOS_E_ALIGN before any launch (no pointer is dereferenced on the host)."""
+    lib = _lib.lib()
+    s = _router_struct(256, 8, 2, 0x7F0000000008)  # 8-byte aligned only
+    rc = lib.chronos_b200_router_topk(s, 0x7F0000001000, 0, 4, 0x7F0000002000, 0x7F0000003000, 0x7F0000004000, None)
+    assert rc == -2 and b"router_w" in lib.chronos_b200_last_error()
+    full = _lib.LayerStruct()
+    full.hidden, full.inter, full.n_experts, full.group_size, full.n_slots, full.rank, full.top_k = 256, 128, 8, 4, 2, 16, 2
+    for name, _ in _lib.LayerStruct._fields_[12:34]:
+        setattr(full, name, 0x7F0000010000)
+    full.router_w = 0x7F0000000004
+    rc = lib.chronos_b200_folded_moe_forward(full, 0x7F0000001000, 0, 4, 0x7F0000002000, 0, 0x7F0000100000, 1 << 30, None)
+    assert rc == -2 and b"router_w" in lib.chronos_b200_last_error()
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="relies on launches being refused for lack of a device")
+def test_router_with_rows_too_long_to_stage_takes_the_register_kernel():
+    """hidden 16384 in fp32: four activation rows alone exceed the staging budget of the shared-memory router kernel, so
+    the launcher must pick the register-tile kernel instead of asking for an impossible amount of shared memory.
+    Without a device every launch is refused; which launch was attempted shows in the message."""
+    lib = _lib.lib()
+    s = _router_struct(16384, 8, 2, 0x7F0000000000)
+    rc = lib.chronos_b200_router_topk(s, 0x7F0000100000, 0, 4, 0x7F0000200000, 0x7F0000300000, 0x7F0000400000, None)
+    msg = lib.chronos_b200_last_error()
+    assert rc == -4 and b"opt in" not in msg and b"router_logits" in msg, msg
+
+
 def test_compact_key_tables_match_reference_keys(golden):
     h, i, e, k = (int(v) for v in golden["meta"][:4])
     g, m = e // k - 1, k - 1
