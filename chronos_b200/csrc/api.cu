@@ -178,6 +178,35 @@ static int pick_regime(const chronos_layer_t& L, int n_tokens, int regime, const
     return p.fp4_stream ? CHRONOS_REGIME_STREAM_FP4 : CHRONOS_REGIME_STREAM;
 }
 
+// Decode-sized batch in the FP4 streaming regime: five launches (csrc/decode_fused.cu). `ids_in` NULL: the front kernel
+// routes by itself; otherwise the caller's routing is used and the token scales come from a kernel of their own.
+static int fused_decode_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids_in,
+                                const float* gates_in, int shared_first, int shared_count, void* y, int y_dtype, const Plan& plan,
+                                cudaStream_t st) {
+    Plan p = plan;
+    p.gitem_pairs = 8;
+    const int with_shared = (shared_count > 0 && L.shared_inter > 0) ? 1 : 0;
+    p.shared_lo = with_shared ? shared_first : 0;
+    p.shared_n = with_shared ? shared_count : 0;
+    // counters, status word and the grid hand-off counter start at zero (a memset node, no allocation)
+    if (cudaMemsetAsync(p.counters, 0, 64, st) != cudaSuccess) return check_launch("clear counters");
+    if (ids_in != nullptr)
+        if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, p.tok_scale, st)) return rc;
+    if (int rc = launch_decode_front(L, x, x_dtype, n_tokens, ids_in, with_shared, p, st)) return rc;
+    stage_mark(1, st);
+    stage_mark(2, st);
+    stage_mark(3, st);
+    if (int rc = launch_bank_fp4_fused(L, 0, p, x, x_dtype, st)) return rc;
+    stage_mark(4, st);
+    if (int rc = launch_decode_mid(L, p, st)) return rc;
+    stage_mark(5, st);
+    if (int rc = launch_bank_fp4_fused(L, 1, p, x, x_dtype, st)) return rc;
+    stage_mark(6, st);
+    const int rc = launch_decode_combine(L, p, ids_in != nullptr ? gates_in : p.gates, n_tokens, with_shared, y, y_dtype, st);
+    stage_mark(7, st);
+    return rc;
+}
+
 static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids,
                           const float* gates, int shared_first, int shared_count, void* y, int y_dtype, const Plan& plan,
                           int regime, bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
@@ -297,6 +326,8 @@ static int full_forward(const chronos_layer_t* layer, const void* x, int x_dtype
     const Plan p = plan_bind(lay, workspace);
     cudaStream_t st = (cudaStream_t)stream;
     stage_mark(0, st);
+    if (pick_regime(*layer, n_tokens, regime, p) == CHRONOS_REGIME_STREAM_FP4 && decode_fused_fits(*layer, x_dtype, n_tokens, p))
+        return fused_decode_forward(*layer, x, x_dtype, n_tokens, nullptr, nullptr, 0, n_tokens, y, y_dtype, p, st);
     // the router may raise the status word, so it is cleared here (a memset node, no allocation) and not by the plan kernel
     if (cudaMemsetAsync(p.counters, 0, 64, st) != cudaSuccess) return check_launch("clear counters");
     // decode-sized batches: the top-k runs inside the plan launch (one launch less on the critical path)
@@ -344,6 +375,10 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
         return CHRONOS_E_WORKSPACE;
     }
     const Plan p = plan_bind(lay, workspace);
+    if (pick_regime(*layer, n_tokens, regime, p) == CHRONOS_REGIME_STREAM_FP4 && decode_fused_fits(*layer, x_dtype, n_tokens, p)) {
+        stage_mark(1, (cudaStream_t)stream);
+        return fused_decode_forward(*layer, x, x_dtype, n_tokens, ids, gates, shared_first, shared_count, y, y_dtype, p, (cudaStream_t)stream);
+    }
     return routed_forward(*layer, x, x_dtype, n_tokens, ids, gates, shared_first, shared_count, y, y_dtype, p, regime, false, TopkArgs{}, (cudaStream_t)stream);
 }
 

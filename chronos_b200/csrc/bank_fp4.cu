@@ -190,10 +190,28 @@ __global__ void __launch_bounds__(128, 1) fp4_mma_probe_kernel(const uint8_t* __
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kF4MaxStages = 8;
 constexpr int kF4Threads = 224;  // producer, MMA issuer A, 4 epilogue warps, MMA issuer B
+constexpr int kF4SideThreads = 128;  // fused decode path: 4 more warps for the healer product of the pass
 constexpr int kStatusFp4Timeout = kStatusBankFp4Timeout;
 constexpr uint32_t kF4TmemCols = 512;  // 2 buffers x 2 accumulators x 32 columns, then bank scales (16 per ring stage), then activation scales
 
+// Healer product the side warps of the fused decode path compute while the bank streams (kind 0: none).
+//   kind 1 (gate_up pass): heal[pair, row] = g_pair * U_gu[e, row, :] . (V_gu[e] . x[token(pair), :] / g),  g = token scale
+//   kind 2 (down pass):    heal[pair, row] = g_pair * U_down[e, row, :] . (V_down[e] . ac[pair, :]),  ac = act / g
+// per chunk of up to 8 sorted pairs of one expert, on mma.sync m16n8k16 (e4m3 factors converted to fp16 exactly).
+struct Fp4Side {
+    int kind;
+    const uint8_t* u;          // [E, R, r]
+    const uint8_t* v;          // input factor [E, r, kc]: healer.v_gu (kind 1) / healer.v_down as on disk (kind 2)
+    const void* x; int x_dtype; const int32_t* pair_token;  // kind 1: activation rows [T, kc] (bf16 / fp32)
+    const __half* ac;          // kind 2: [P, kc]
+    const float* pscale;       // [P]
+    float* heal;               // [P, R]
+    const int32_t* chunk_start; const int32_t* chunk_cnt;
+    int rank, n_experts, kc;   // kc: contraction length of the input product (H for kind 1, I for kind 2)
+};
+
 struct Fp4Args {
+    Fp4Side side;
     const uint8_t* bank_t;     // [n_slots, RB, NS, 18432]
     const uint8_t* sh_bank_t;  // [RB, NS, 18432] shared expert (slot == n_slots)
     const float* s2; const float* sh_s2; int sh_split;
@@ -206,14 +224,162 @@ struct Fp4Args {
     int R, K, n_slots, n_stages;
 };
 
+// The side warps' work (4 warps = one team per CTA; chunks are dealt round-robin over the CTAs, and there are fewer chunks
+// than CTAs in a decode step). Every step requests the healer rows of several 16-row tiles before multiplying any: the
+// work is a handful of dependent round trips to L2 / HBM, and the number of requests in flight is what bounds it. Every
+// healer byte is read exactly once per step.
+template <int R16>
+__device__ __forceinline__ void side_healer(const Fp4Args& a, __half (*hsm)[kMaxRank], int sw, int lane) {
+    const Fp4Side& sd = a.side;
+    constexpr int r = R16 * 16;
+    constexpr int G = R16 >= 8 ? 4 : 8;  // 16-row tiles whose rows are requested together (64 registers of healer bytes)
+    const int g = lane >> 2, q = lane & 3;
+    const int R = a.R, n_chunks = a.counters[3];
+    if (n_chunks <= 0) return;
+    const int n_tiles16 = R / 16;
+    for (int ch = blockIdx.x; ch < n_chunks; ch += gridDim.x) {
+        const int start = sd.chunk_start[ch], cnt = sd.chunk_cnt[ch];
+        const int e = a.pair_expert[start];
+        if (e >= sd.n_experts) continue;  // shared expert: no healer (uniform over the team)
+        asm volatile("bar.sync 3, 128;" ::: "memory");  // the previous chunk's factors are no longer read
+        {
+            // h[n, c] = sum_k V[e, c, k] * a[pair n, k] with a = x[token] / g (kind 1) or ac[pair] (kind 2): warp sw takes the
+            // 16-row tiles sw, sw + 4, ...; four 64-column steps of both operands are requested before they are multiplied.
+            // Lane (g, q) owns a contiguous run of 16 columns per step on both operands (any permutation of the contraction
+            // index is legal when both operands use it).
+            const bool valid = g < cnt;
+            const int prow = start + (valid ? g : 0);
+            const uint8_t* arow;
+            float inv = 0.0f;
+            int abytes = 2;
+            if (sd.kind == 1) {
+                abytes = sd.x_dtype == CHRONOS_DTYPE_F32 ? 4 : 2;
+                arow = reinterpret_cast<const uint8_t*>(sd.x) + ((size_t)sd.pair_token[prow] * sd.kc + 16 * q) * abytes;
+                inv = valid ? 1.0f / sd.pscale[prow] : 0.0f;
+            } else {
+                arow = reinterpret_cast<const uint8_t*>(sd.ac + (size_t)prow * sd.kc + 16 * q);
+            }
+            for (int mt = sw; mt < R16; mt += 4) {
+                const uint8_t* v0 = sd.v + ((size_t)e * r + mt * 16 + g) * sd.kc + 16 * q;
+                const uint8_t* v1 = v0 + (size_t)8 * sd.kc;
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int kc0 = 0; kc0 < sd.kc; kc0 += 256) {
+                    uint4 w0[4], w1[4];
+                    uint32_t bf[4][8];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int kc = kc0 + 64 * c;
+                        w0[c] = w1[c] = make_uint4(0u, 0u, 0u, 0u);
+                        if (kc < sd.kc) {
+                            w0[c] = *reinterpret_cast<const uint4*>(v0 + kc);
+                            w1[c] = *reinterpret_cast<const uint4*>(v1 + kc);
+                        }
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int kc = min(kc0 + 64 * c, sd.kc - 64);  // steps past the end multiply zero healer bytes
+                        if (sd.kind == 2) {
+                            uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
+                            if (valid) {
+                                u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
+                                u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
+                            }
+                            bf[c][0] = u0.x; bf[c][1] = u0.y; bf[c][2] = u0.z; bf[c][3] = u0.w;
+                            bf[c][4] = u1.x; bf[c][5] = u1.y; bf[c][6] = u1.z; bf[c][7] = u1.w;
+                        } else if (abytes == 2) {
+                            const uint4 u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
+                            const uint4 u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
+                            const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                bf[c][j] = pack_f16x2_sat(__uint_as_float(uu[j] << 16) * inv, __uint_as_float(uu[j] & 0xffff0000u) * inv);
+                        } else {
+                            const float4* src = reinterpret_cast<const float4*>(arow + (size_t)kc * 4);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float4 f = src[j];
+                                bf[c][2 * j] = pack_f16x2_sat(f.x * inv, f.y * inv);
+                                bf[c][2 * j + 1] = pack_f16x2_sat(f.z * inv, f.w * inv);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint32_t r0[4] = {w0[c].x, w0[c].y, w0[c].z, w0[c].w}, r1[4] = {w1[c].x, w1[c].y, w1[c].z, w1[c].w};
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4)
+                            mma_16816(acc, e4m3x2_to_f16x2(r0[s4] & 0xffffu), e4m3x2_to_f16x2(r1[s4] & 0xffffu), e4m3x2_to_f16x2(r0[s4] >> 16),
+                                      e4m3x2_to_f16x2(r1[s4] >> 16), bf[c][2 * s4], bf[c][2 * s4 + 1]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)  // acc[j]: rank row mt*16 + g (+ 8), pair 2q + (j & 1)
+                    hsm[2 * q + (j & 1)][mt * 16 + g + (j >> 1) * 8] = f32_to_f16_sat(acc[j]);
+            }
+        }
+        asm volatile("bar.sync 3, 128;" ::: "memory");
+        // B fragments: h[pair g][4 R16 q + 4 s .. + 3] as two fp16 pairs per k16 step
+        uint32_t bf[R16][2];
+#pragma unroll
+        for (int s4 = 0; s4 < R16; ++s4) {
+            const uint2 hv = *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s4]);
+            bf[s4][0] = hv.x;
+            bf[s4][1] = hv.y;
+        }
+        const float gs0 = 2 * q < cnt ? sd.pscale[start + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt ? sd.pscale[start + 2 * q + 1] : 0.0f;
+        const uint8_t* U = sd.u + (size_t)e * R * r;
+        const int t_hi = n_tiles16;
+        for (int jt0 = sw * G; jt0 < t_hi; jt0 += 4 * G) {
+            uint32_t wl[G][R16], wh[G][R16];
+#pragma unroll
+            for (int t = 0; t < G; ++t) {
+                const int jt = jt0 + t;
+                if (jt < t_hi) {
+                    const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)(jt * 16 + g) * r + 4 * R16 * q);
+                    const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)(jt * 16 + g + 8) * r + 4 * R16 * q);
+                    if constexpr (R16 % 4 == 0) {
+#pragma unroll
+                        for (int s4 = 0; s4 < R16; s4 += 4) {
+                            const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s4), b4 = *reinterpret_cast<const uint4*>(u_hi + s4);
+                            wl[t][s4] = a4.x; wl[t][s4 + 1] = a4.y; wl[t][s4 + 2] = a4.z; wl[t][s4 + 3] = a4.w;
+                            wh[t][s4] = b4.x; wh[t][s4 + 1] = b4.y; wh[t][s4 + 2] = b4.z; wh[t][s4 + 3] = b4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int s4 = 0; s4 < R16; ++s4) { wl[t][s4] = u_lo[s4]; wh[t][s4] = u_hi[s4]; }
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < G; ++t) {
+                const int jt = jt0 + t;
+                if (jt < t_hi) {
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int s4 = 0; s4 < R16; ++s4)
+                        mma_16816(d, e4m3x2_to_f16x2(wl[t][s4] & 0xffffu), e4m3x2_to_f16x2(wh[t][s4] & 0xffffu), e4m3x2_to_f16x2(wl[t][s4] >> 16),
+                                  e4m3x2_to_f16x2(wh[t][s4] >> 16), bf[s4][0], bf[s4][1]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // d[j]: row jt*16 + g (+ 8 for j >= 2), pair 2q + (j & 1)
+                        const int n = 2 * q + (j & 1), row = jt * 16 + g + (j >> 1) * 8;
+                        if (n < cnt) sd.heal[(size_t)(start + n) * R + row] = ((j & 1) ? gs1 : gs0) * d[j];
+                    }
+                }
+            }
+        }
+    }
+}
+
 // Shared memory: [activation image of the current work item: NS x 6144 B][ring of n_stages bank stages x 18432 B].
 // The activation image is fetched once per work item and stays while the CTA walks the item's row blocks
 // (a CTA owns a contiguous run of tiles, so it changes item only once or twice per launch).
-__global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a) {
+template <bool SIDE>
+__global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) bank_fp4_kernel(const Fp4Args a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2 * kF4MaxStages + 6];  // full[S], empty[S], acc_full[2], acc_empty[2], b_full, b_empty
     __shared__ uint32_t tmem_base_s;
-    __shared__ __align__(16) float zs[8][132];
+    __shared__ __align__(16) float zs[2][8][128];    // epilogue exchange between the four lane quarters, double-buffered
+    __shared__ __align__(16) __half hsm[SIDE ? 8 : 1][kMaxRank];  // side warps: healer input factors of the current chunk
     uint8_t* bimg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.R, RB = R / 128, NS = a.K / kF4StageK, S = a.n_stages;
@@ -373,28 +539,32 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
                 }
             }
         }
-    } else {
+    } else if (warp < 6) {
         // ---------------- epilogue warps (TMEM lane quarter = warp % 4) ----------------
-        const int quarter = warp & 3, ew = warp - 2, et = tid - 64;  // warps 2..5: ew 0..3, et 0..127
+        // Thread = bank row (quarter * 32 + lane) for all pairs of the item. The 128-point Walsh-Hadamard transform over
+        // the rows runs where the rows are: five butterfly stages across the lanes (shuffles), the two stages across the
+        // lane quarters through one shared-memory exchange - one barrier per tile, all four warps busy however few
+        // pairs the item holds.
+        const int quarter = warp & 3, et = tid - 64;
         const int row = quarter * 32 + lane;
-        uint32_t tcount = 0;
+        const bool q0 = (quarter & 1) != 0, q1 = (quarter & 2) != 0;
+        uint32_t tcount = 0, zpar = 0;
         for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
             const int item = (int)(tile / RB), rb = (int)(tile % RB);
             const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
             const bool sh = slot >= a.n_slots;
             // operands of the epilogue, fetched while the tile streams
             const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
-            uint32_t sw[2];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int n = ew * 2 + q;
-                sw[q] = 0u;
-                if (n < cnt && !sh)
-                    sw[q] = a.rs2[(size_t)a.pair_expert[start + n] * (R / 32) + rb * 4 + lane / 8] >> ((lane & 7) * 4);
-            }
             float g8[8];
+            uint32_t sbits = 0u;  // bit n: r_s2 sign of this thread's row for pair n
 #pragma unroll
-            for (int n = 0; n < 8; ++n) g8[n] = n < cnt ? a.pscale[start + n] * s2 : 0.0f;
+            for (int n = 0; n < 8; ++n) {
+                g8[n] = 0.0f;
+                if (n < cnt) {
+                    g8[n] = a.pscale[start + n] * s2;
+                    if (!sh) sbits |= ((a.rs2[(size_t)a.pair_expert[start + n] * (R / 32) + rb * 4 + quarter] >> lane) & 1u) << n;
+                }
+            }
             const uint32_t buf = tcount & 1u;
             // the 128 epilogue threads must take the same branch: a named barrier ORs their verdicts
             uint32_t fail = mbar_wait(smem_u32(&acc_full[buf]), (tcount >> 1) & 1u) ? 0u : 1u;
@@ -415,28 +585,53 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));  // accumulator buffer may be overwritten
+            float v8[8];
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
-                const float v = __uint_as_float(d[n]) + 0.03125f * __uint_as_float(d[8 + n]) + 0.0009765625f * __uint_as_float(d[16 + n]);
-                zs[n][row] = v * g8[n];
+                float v = (__uint_as_float(d[n]) + 0.03125f * __uint_as_float(d[8 + n]) + 0.0009765625f * __uint_as_float(d[16 + n])) * g8[n];
+                v8[n] = ((sbits >> n) & 1u) ? -v : v;
             }
-            asm volatile("bar.sync 2, 128;" ::: "memory");
+            float* zrow = a.zout + (size_t)start * R + rb * 128 + row;
+            if (sh) {  // plain weights: no sign, no transform
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int n = ew * 2 + q;
-                if (n < cnt) {
-                    const float4 t4 = *reinterpret_cast<const float4*>(&zs[n][lane * 4]);
-                    float v[4] = {t4.x, t4.y, t4.z, t4.w};
-                    if (!sh) {
+                for (int n = 0; n < 8; ++n)
+                    if (n < cnt) zrow[(size_t)n * R] = v8[n];
+                continue;
+            }
+            float(*z)[128] = zs[zpar & 1u];
+            ++zpar;
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            if ((sw[q] >> i) & 1u) v[i] = -v[i];
-                        fwht128_warp(v, lane);
+            for (int n = 0; n < 8; ++n) {
+                if (n < cnt) {  // cnt is uniform over the warp
+                    float v = v8[n];
+#pragma unroll
+                    for (int m = 1; m < 32; m <<= 1) {
+                        const float o = __shfl_xor_sync(0xffffffffu, v, m);
+                        v = (lane & m) ? (o - v) : (v + o);
                     }
-                    *reinterpret_cast<float4*>(a.zout + (size_t)(start + n) * R + rb * 128 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+                    z[n][row] = v;
                 }
             }
             asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                if (n < cnt) {
+                    const float a0 = z[n][lane], a1 = z[n][32 + lane], a2 = z[n][64 + lane], a3 = z[n][96 + lane];
+                    const float lo = a0 + (q0 ? -a1 : a1), hi = a2 + (q0 ? -a3 : a3);
+                    zrow[(size_t)n * R] = (lo + (q1 ? -hi : hi)) * 0.08838834764831845f;
+                }
+            }
+            // no second barrier: the next tile writes the other buffer, and nobody reaches the tile after it before every
+            // thread has passed the next tile's barrier
+        }
+    } else if (SIDE) {
+        // ---------------- side warps: the healer product of this pass, chunk by chunk ----------------
+        const int sw = warp - 7;
+        switch (a.side.rank / 16) {
+            case 1: side_healer<1>(a, hsm, sw, lane); break;
+            case 2: side_healer<2>(a, hsm, sw, lane); break;
+            case 4: side_healer<4>(a, hsm, sw, lane); break;
+            default: side_healer<8>(a, hsm, sw, lane); break;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -444,7 +639,7 @@ __global__ void __launch_bounds__(kF4Threads, 1) bank_fp4_kernel(const Fp4Args a
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kF4TmemCols) : "memory");
 }
 
-int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st) {
+static int launch_bank_fp4_impl(const chronos_layer_t& L, int stage, const Plan& p, bool side, const void* x, int x_dtype, cudaStream_t st) {
     Fp4Args a{};
     a.K = stage == 0 ? L.hidden : L.inter;
     a.R = stage == 0 ? 2 * L.inter : L.hidden;
@@ -463,9 +658,26 @@ int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStre
     a.pair_expert = p.pair_expert;
     a.counters = p.counters;
     a.n_slots = L.n_slots;
+    if (side) {
+        Fp4Side& sd = a.side;
+        sd.kind = stage == 0 ? 1 : 2;
+        sd.u = stage == 0 ? L.u_gu : L.u_dn;
+        sd.v = stage == 0 ? L.v_gu : L.v_dn;
+        sd.x = x;
+        sd.x_dtype = x_dtype;
+        sd.pair_token = p.pair_token;
+        sd.ac = p.ac;
+        sd.pscale = stage == 0 ? p.pscale_gu : p.pscale_dn;
+        sd.heal = stage == 0 ? p.heal_gu : p.heal_dn;
+        sd.chunk_start = p.gitem_start;
+        sd.chunk_cnt = p.gitem_cnt;
+        sd.rank = L.rank;
+        sd.n_experts = L.n_experts;
+        sd.kc = stage == 0 ? L.hidden : L.inter;
+    }
     const int ns = a.K / kF4StageK;
     const size_t bimg = (size_t)ns * kF4BStage;
-    const size_t budget = 218 * 1024;
+    const size_t budget = 214 * 1024;  // dynamic part; the kernel's static shared memory (barriers, exchange buffers) takes the rest
     if (bimg + 2 * (size_t)kF4AStage + 1024 > budget) {
         set_error("bank_fp4: K = %d columns need a %zu-byte activation image, too large for shared memory", a.K, bimg);
         return CHRONOS_E_SHAPE;
@@ -473,12 +685,17 @@ int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStre
     int stages = (int)((budget - 1024 - bimg) / kF4AStage);
     a.n_stages = stages > kF4MaxStages ? kF4MaxStages : stages;
     const size_t smem = bimg + (size_t)a.n_stages * kF4AStage + 1024;
-    if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(bank_fp4_kernel), smem, "bank_fp4")) return rc;
-    const int sms = device_sm_count();
-    const long max_tiles = (long)p.max_items * (a.R / 128);
-    const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-    bank_fp4_kernel<<<grid, kF4Threads, smem, st>>>(a);
+    const void* fn = side ? reinterpret_cast<const void*>(bank_fp4_kernel<true>) : reinterpret_cast<const void*>(bank_fp4_kernel<false>);
+    if (int rc = ensure_dynamic_smem(fn, smem, "bank_fp4")) return rc;
+    const int grid = bank_fp4_grid(L, stage, p);
+    if (side) bank_fp4_kernel<true><<<grid, kF4Threads + kF4SideThreads, smem, st>>>(a);
+    else bank_fp4_kernel<false><<<grid, kF4Threads, smem, st>>>(a);
     return check_launch("bank_fp4");
+}
+
+int launch_bank_fp4(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st) { return launch_bank_fp4_impl(L, stage, p, false, nullptr, 0, st); }
+int launch_bank_fp4_fused(const chronos_layer_t& L, int stage, const Plan& p, const void* x, int x_dtype, cudaStream_t st) {
+    return launch_bank_fp4_impl(L, stage, p, true, x, x_dtype, st);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

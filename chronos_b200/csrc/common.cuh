@@ -37,7 +37,8 @@ struct Plan {
     int32_t* gitem_start;  // [max_gitems] tensor-core work items: up to 128 sorted pairs of one expert
     int32_t* gitem_cnt;
     int32_t* gitem_slot;
-    int32_t* counters;     // [0] = number of items, [1] = number of pairs, [2] = device status word, [3] = number of gemm items
+    int32_t* counters;     // [0] = number of items, [1] = number of pairs, [2] = device status word, [3] = number of gemm items,
+                           // [8] = arrivals at the grid-wide hand-off of the fused decode front kernel (16 words, cleared per call)
     __half* xc;            // [P, H]   transformed gate_up inputs
     float* hmid;           // [P, r]   V_gu . x
     float* z1;             // [P, 2I]  H_r(r_s2 * (S_gu . x_c)) * scale_2
@@ -56,6 +57,10 @@ struct Plan {
     float* tail_gu;        // [P, 2I]  tail-lattice term of the gate_up product, natural row order (NULL: layer has no tail)
     float* tail_dn;        // [P, H]   the same for the down product
     float* hsplit;         // [2 stages][kHealSplit][P, r] healer input factors, one partial sum per slice of the contraction
+    float* heal_gu;        // [P, 2I]  healer term U_gu (V_gu x) in natural row order (fused decode path only, else NULL)
+    float* heal_dn;        // [P, H]   healer term U_down (V_down act) in natural row order (fused decode path only)
+    int32_t* pair_item;    // [P]      streaming work item of sorted pair p (fused decode path only)
+    int32_t* pair_pos;     // [P]      position 0..7 of sorted pair p inside its work item
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
     int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
@@ -68,7 +73,8 @@ struct Plan {
 struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
-        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, off_tail_gu, off_tail_dn, off_x16t, total;
+        off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, off_tail_gu, off_tail_dn, off_x16t, off_heal_gu,
+        off_heal_dn, off_pair_item, off_pair_pos, total;
     int fp4, tiled, wide, tail;
     int max_pairs, max_items, max_gitems;
 };
@@ -82,7 +88,13 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     const size_t P = T * k + (L.shared_inter > 0 ? T : 0);
     p.max_pairs = (int)P;
     p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
-    p.max_gitems = (int)(E + 1 + P / kPairsPerWideItem + 1);  // sized for the smaller (64-pair) work items
+    // FP4 activation images exist only for batch shapes the streaming regime serves and layers that carry re-tiled banks
+    p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
+             T * k < 16 * (size_t)L.n_slots &&
+             (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
+    // per-expert work items: 64 pairs in the FP4 tensor regime (128 in the fp16 one); the fused decode path cuts the
+    // same lists into chunks of 8 pairs for its healer products
+    p.max_gitems = (int)(E + 1 + P / (p.fp4 ? 8 : kPairsPerWideItem) + 1);
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
     p.off_logits = take(T * E * 4);
@@ -110,10 +122,6 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_tok_scale = take(T * 4);
     p.off_pscale_gu = take(P * 4);
     p.off_pscale_dn = take(P * 4);
-    // FP4 activation images exist only for batch shapes the streaming regime serves and layers that carry re-tiled banks
-    p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
-             T * k < 16 * (size_t)L.n_slots &&
-             (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
     p.tiled = (T * k >= 16 * (size_t)L.n_slots) ? 1 : 0;  // batch shapes the tensor regime serves
     // the FP4 tensor regime: re-tiled banks, the tensor-core healer path (needs healer.v_down as on disk) and its
     // shared-memory budget (4 staged vectors of 3 I or H floats)
@@ -125,6 +133,10 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.off_x16 = take(p.tiled ? T * H * 2 : 0);
     p.off_hsplit = take(p.tiled ? 2 * kHealSplit * P * r * 4 : 0);
+    p.off_heal_gu = take(p.fp4 ? P * 2 * I * 4 : 0);
+    p.off_heal_dn = take(p.fp4 ? P * H * 4 : 0);
+    p.off_pair_item = take(p.fp4 ? P * 4 : 0);
+    p.off_pair_pos = take(p.fp4 ? P * 4 : 0);
     p.tail = L.tail_bits != 0 ? 1 : 0;
     p.off_tail_gu = take(p.tail ? P * 2 * I * 4 : 0);
     p.off_tail_dn = take(p.tail ? P * H * 4 : 0);
@@ -169,6 +181,10 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.x16 = l.tiled ? (__half*)(b + l.off_x16) : nullptr;
     p.hsplit = l.tiled ? (float*)(b + l.off_hsplit) : nullptr;
+    p.heal_gu = l.fp4 ? (float*)(b + l.off_heal_gu) : nullptr;
+    p.heal_dn = l.fp4 ? (float*)(b + l.off_heal_dn) : nullptr;
+    p.pair_item = l.fp4 ? (int32_t*)(b + l.off_pair_item) : nullptr;
+    p.pair_pos = l.fp4 ? (int32_t*)(b + l.off_pair_pos) : nullptr;
     p.tail_gu = l.tail ? (float*)(b + l.off_tail_gu) : nullptr;
     p.tail_dn = l.tail ? (float*)(b + l.off_tail_dn) : nullptr;
     if (l.tail && !l.tiled) p.x16 = (__half*)(b + l.off_x16t);
@@ -221,6 +237,15 @@ int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, 
 int launch_bank_stream(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_fp4(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
 int launch_bank_gemm(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
+// fused decode path (csrc/decode_fused.cu): front kernel (router, top-k, coalescing, gate_up input), the kernels between and
+// after the bank passes; the healer products ride along inside the bank passes (side warps of bank_fp4_kernel)
+bool decode_fused_fits(const chronos_layer_t& L, int x_dtype, int n_tokens, const Plan& p);
+int launch_decode_front(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids_in,
+                        int with_shared, const Plan& p, cudaStream_t st);
+int launch_decode_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                          int y_dtype, cudaStream_t st);
+int launch_bank_fp4_fused(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, const void* x, int x_dtype, cudaStream_t st);
 int launch_wait_probe(int32_t* status, uint32_t poll_limit, cudaStream_t st);
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st);
@@ -230,6 +255,12 @@ int launch_residual_rmsnorm(void* h, const void* y, const float* w, void* xn, in
 void set_error(const char* fmt, ...);
 int check_launch(const char* what);
 int device_sm_count();  // SMs of the current device (cached per device)
+// CTAs a streaming FP4 bank pass is launched with (stage 0: gate_up, 1: down)
+inline int bank_fp4_grid(const chronos_layer_t& L, int stage, const Plan& p) {
+    const long max_tiles = (long)p.max_items * ((stage == 0 ? 2 * L.inter : L.hidden) / 128);
+    const int sms = device_sm_count();
+    return (int)(max_tiles < sms ? max_tiles : sms);
+}
 int ensure_dynamic_smem(const void* func, size_t bytes, const char* what);  // shared-memory opt-in, cached per (kernel, device)
 
 #ifdef __CUDACC__
@@ -358,12 +389,12 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
 #pragma unroll
         for (int i = 0; i < PL; ++i)
             if (found && i * 32 + lane == best_e) choice[i] = -INFINITY;  // remove the winner from its owner lane
-        if (lane == j && found) {
-            my_id = best_e;
-            my_val = router_weight_source(a, a.logits[(size_t)t * a.n_experts + best_e]);
-        }
+        if (lane == j && found) my_id = best_e;
     }
+    // lane j fetches the logit of its winner once, after the rounds: a load inside the loop would make every round wait
+    // for the previous round's load (they would all target the same register)
     const bool have = lane < a.top_k && my_id >= 0;
+    if (have) my_val = router_weight_source(a, a.logits[(size_t)t * a.n_experts + my_id]);
     float gate;
     if (a.kind != CHRONOS_ROUTER_SOFTMAX_TOPK) {
         const float s = have ? my_val : 0.0f;
@@ -403,7 +434,23 @@ __device__ __forceinline__ __half f32_to_f16_sat(float v) {
     asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(r) : "f"(v));
     return __ushort_as_half(r);
 }
-// ---- mbarrier / bulk-copy primitives (every wait is bounded) ----------------------------------------------------
+// ---- warp-level tensor-core helpers of the healer products (mma.sync m16n8k16, fp16 operands, fp32 accumulate) ------
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v16) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((uint16_t)v16));
+    return r;
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+    const __half2 h = __halves2half2(f32_to_f16_sat(lo), f32_to_f16_sat(hi));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // FP4 quantiser: a 128-block of activations (lane l holds elements 4l..4l+3, already divided by the pair's scale) is
 // written as three residual e2m1 terms with ue4m3 scales per 16 elements into an activation stage image

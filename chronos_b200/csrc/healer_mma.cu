@@ -15,24 +15,6 @@
 
 namespace chronos {
 
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v16) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((uint16_t)v16));
-    return r;
-}
-
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                          uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
-    const __half2 h = __halves2half2(f32_to_f16_sat(lo), f32_to_f16_sat(hi));
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 // ---------------------------------------------------------------------------------------------------------------
 // Healer input factor of a tensor-regime work item (one expert, up to 128 sorted pairs):
 //   out[slice][pair, c] = (1 / g_pair) * sum_{k in slice} V[e, c, k] * X[row(pair), k]      c < r, fp32 partial sums

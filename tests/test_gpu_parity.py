@@ -307,6 +307,30 @@ def test_fp4_streaming_regime_matches_oracle_and_cuda_core_regime():
         assert torch.equal(layer.forward_impl(x, regime="auto"), y4)  # 28 pairs on 8 slots: auto = FP4 streaming
 
 
+@pytest.mark.parametrize("n_tok,top_k,rank", [(32, 8, 32), (40, 8, 32), (9, 6, 128), (2, 3, 16)])
+def test_streaming_fp4_paths_at_their_batch_limits(n_tok, top_k, rank):
+    """The FP4 streaming regime on both of its code paths: up to 32 tokens take the fused decode path (front kernel with
+    the grid-wide hand-off, healer products inside the bank passes), larger batches the separate-kernel path; many
+    slots, few pairs per slot, shared expert, every healer rank the side warps are instantiated for."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=288, group_size=4, rank=rank, top_k=top_k)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=41, with_shared=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(n_tok)
+    x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+    y = layer.forward_impl(x, regime="stream_fp4")
+    assert layer.device_status() == 0
+    assert torch.equal(y, layer.forward_impl(x, regime="auto"))
+    ref, ref_ids, _ = _oracle_layer(layer, x.float().cpu().numpy())
+    ids, w = layer.route(x)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL
+    # the same batch with the routing handed in by the caller, fp32 activations at the boundary
+    y_r = layer.routed_forward(x.float(), ids, w, with_shared=True, regime="stream_fp4")
+    assert layer.device_status() == 0
+    assert _rel_l2(y_r.cpu().numpy(), ref) <= LAYER_TOL
+
+
 def test_many_tokens_on_one_slot_and_skipped_entries():
     """More than 8 pairs on a slot (several work items per slot), entries with id -1, routing supplied by the caller."""
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
