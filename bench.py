@@ -1,19 +1,25 @@
 #!/usr/bin/env python3
 """Benchmark of the folded-expert MoE forward on B200.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|ep_stack]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|ep_stack|prefill|sweep]
 
 One JSON line on stdout (rank 0). A step = one forward of the workload over one batch of seeded synthetic input.
 
-N = 1 (default) workload "decode": the decode-shaped layer (hidden 4096, 288 routed experts + 1 shared, top-8,
-SwiGLU inter 1536, fold factor 4, healer rank 64, NVFP4 banks; 4 streams x 3 speculative tokens, bf16).
-N > 1 workload "ep_stack": the same layer stacked 42 deep with experts sharded over the ranks (all-to-all
-dispatch / combine over NCCL, residual + RMSNorm between layers), 4096 tokens per step.
+Plain `python bench.py` (no launcher, N = 1), workload "decode": the decode-shaped layer (hidden 4096, 288 routed
+experts + 1 shared, top-8, SwiGLU inter 1536, fold factor 4, healer rank 64, NVFP4 banks; 4 streams x 3 speculative
+tokens, bf16). The line also carries a `prefill` sub-record (8192 tokens, Zipf(1.1) routing, FP4 tensor regime, with the
+empirical FP4 ceiling of the same tile shapes measured in the same run) and an `ep_stack_1gpu` sub-record.
+Under `torch.distributed.run` (any world size, 1 included) or with `--gpus N > 1`, workload "ep_stack": the same layer
+stacked 42 deep with experts sharded over the ranks (all-to-all dispatch / combine over NCCL, residual + RMSNorm
+between layers), 4096 tokens per step, strong scaling; at world size 1 the line carries the decode result as a
+`decode_layer` sub-record, and every line carries `parity` (layer 0 of the stack against the CPU oracle on a sample of
+rank 0's tokens; the run fails above 1e-2).
 
 `value`     device-resident throughput (tokens/s), CUDA events over exactly K steps, max over ranks.
 `e2e`       the same metric through the public module call with pinned-host inputs and outputs (copies timed).
 `roofline`  the dominant kernel (gate_up bank pass) against measured HBM bandwidth.
-`cpu_baseline` / `--impl reference`: the CPU oracle (a numpy port of the reference's PyTorch path) on the host cores.
+`cpu_baseline` / `--impl reference`: the reference's own PyTorch code for this path (from oracle/_ref; the numpy port of it
+when that folder is absent) on the host cores, same configuration, bounded number of steps.
 """
 from __future__ import annotations
 
@@ -30,16 +36,18 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-DECODE = dict(hidden=4096, inter=1536, n_experts=288, group_size=4, rank=64, top_k=8)
-DECODE_STREAMS, TOKENS_PER_STREAM = 4, 3
-N_BATCHES = 8             # distinct routed batches the timed loop rotates through
-STREAM_CORR = 0.67        # shared share of variance of a stream's tokens -> ~30 % top-8 overlap at 288 experts
+from chronos_b200.workloads import DECODE, N_BATCHES, TOKENS_PER_STREAM, decode_batches  # noqa: E402  (no CUDA needed to import)
+
+DECODE_STREAMS = 4
 EP_LAYERS, EP_TOKENS = 42, 4096
+PREFILL_TOKENS = 8192
+FP4_NOMINAL_TFLOPS = 9000.0  # dense FP4 of a B200 (datasheet); MEASURED_PEAKS.json holds no FP4 figure
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch of bank_fp4_kernel from the ncu capture summarised
-# under profiles/ (bank_fp4_kernel, decode layer): 314.98 MB + 4.02 MB for a forward over 44 banks (311.43 MB algorithmic).
-# Traffic grows in proportion to the banks a launch streams, so the line reports this ratio times the launch's bytes.
-GU_PASS_TRAFFIC_OVER_ALGORITHMIC = (314.98 + 4.02) / 311.43
+REFERENCE_BUDGET_S = 150.0   # wall-clock bound of the reference arm's timed steps
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch of bank_fp4_kernel over its algorithmic bytes (bank
+# images + the healer factors its side warps read), from the ncu capture summarised under profiles/ (bank_fp4_kernel,
+# decode layer). Traffic grows in proportion to the bytes a launch streams, so the line reports this ratio times them.
+GU_PASS_TRAFFIC_OVER_ALGORITHMIC = 1.02
 
 
 def _peaks() -> tuple[float, str]:
@@ -93,21 +101,6 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------------------------
-def decode_batches(cfg, streams: int, device, seed: int = 1):
-    """N_BATCHES seeded activation batches [streams*3, H] bf16: the 3 tokens of a stream share a common component
-    (correlation 0.67 of their router logits), which makes their top-8 sets overlap by about 30 % (the realised
-    overlap is reported)."""
-    import torch
-
-    gen = torch.Generator(device=device).manual_seed(seed)
-    out = []
-    for _ in range(N_BATCHES):
-        base = torch.randn(streams, 1, cfg.hidden, generator=gen, device=device)
-        eps = torch.randn(streams, TOKENS_PER_STREAM, cfg.hidden, generator=gen, device=device)
-        out.append((STREAM_CORR ** 0.5 * base + (1.0 - STREAM_CORR) ** 0.5 * eps).reshape(-1, cfg.hidden).to(torch.bfloat16).contiguous())
-    return out
-
-
 def routing_stats(layer, batches, streams: int):
     """Per batch: distinct slots / experts touched and the algorithmic HBM bytes of one forward."""
     cfg = layer.cfg
@@ -122,40 +115,21 @@ def routing_stats(layer, batches, streams: int):
             for a in range(TOKENS_PER_STREAM):
                 for b in range(a + 1, TOKENS_PER_STREAM):
                     ov.append(len(set(blk[a]) & set(blk[b])) / cfg.top_k)
-        h, i = cfg.hidden, cfg.inter
+        h, i, r = cfg.hidden, cfg.inter, cfg.rank
         gu_bank = 2 * i * h // 2 + 2 * i * h // 16
         dn_bank = h * i // 2 + h * i // 16
         n_sh = 1 if layer.n_shared_experts else 0
         stats.append({
             "slots": len(slots), "experts": len(experts), "overlap": sum(ov) / max(len(ov), 1),
-            "gu_pass_bytes": (len(slots) + n_sh) * gu_bank, "dn_pass_bytes": (len(slots) + n_sh) * dn_bank,
+            # a bank pass streams the banks of the distinct slots (+ shared expert) and, in its side warps, the healer
+            # factors of the distinct experts: V_gu [r, H] + U_gu [2I, r] (gate_up), V_down [r, I] + U_down [H, r] (down)
+            "gu_pass_bytes": (len(slots) + n_sh) * gu_bank + len(experts) * r * (h + 2 * i),
+            "dn_pass_bytes": (len(slots) + n_sh) * dn_bank + len(experts) * r * (i + h),
+            "gu_bank_bytes": (len(slots) + n_sh) * gu_bank, "dn_bank_bytes": (len(slots) + n_sh) * dn_bank,
             "layer_bytes": (len(slots) + n_sh) * (gu_bank + dn_bank) + len(experts) * cfg.healer_bytes_per_expert()
                            + 2 * x.shape[0] * h * 2,
         })
     return stats
-
-
-def cpu_oracle_tokens_per_s(layer, x_sample, threads: int) -> tuple[float, float]:
-    """Times the CPU oracle (numpy port of the reference path) on a token sample; returns (tokens/s, seconds)."""
-    import numpy as np
-
-    from oracle import folded_moe_oracle as O  # CPU-baseline leg only
-
-    O.set_threads(threads)
-    groups, ex = layer.packed.to_groups_numpy()
-    cfg = layer.cfg
-    shared = None
-    if "sh_gu_w" in ex:
-        i = cfg.inter
-        shared = (np.concatenate([O.unpack_nvfp4(ex["sh_gu_w"][:i], ex["sh_gu_s"][:i], ex["sh_gu_s2"][0]),
-                                  O.unpack_nvfp4(ex["sh_gu_w"][i:], ex["sh_gu_s"][i:], ex["sh_gu_s2"][1])]),
-                  O.unpack_nvfp4(ex["sh_dn_w"], ex["sh_dn_s"], ex["sh_dn_s2"][0]))
-    xs = x_sample.float().cpu().numpy()
-    t0 = time.perf_counter()
-    O.moe_layer_forward(xs, groups, ex["router_w"], cfg.top_k, cfg.hidden, cfg.inter, cfg.group_size, router=cfg.router,
-                        e_bias=ex.get("e_bias"), shared=shared)
-    dt = time.perf_counter() - t0
-    return xs.shape[0] / dt, dt
 
 
 def host_threads() -> int:
@@ -165,20 +139,103 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-# ---------------------------------------------------------------------------------------------------------------
-def run_decode(args) -> dict:
+def _shared_fp32(ex):
+    """The plain-NVFP4 shared expert of a layer as fp32 (gate_up, down) via the numpy oracle."""
+    import numpy as np
+
+    from oracle import folded_moe_oracle as O  # checker / CPU-baseline leg only
+
+    i = ex["sh_gu_w"].shape[0] // 2
+    return (np.concatenate([O.unpack_nvfp4(ex["sh_gu_w"][:i], ex["sh_gu_s"][:i], ex["sh_gu_s2"][0]),
+                            O.unpack_nvfp4(ex["sh_gu_w"][i:], ex["sh_gu_s"][i:], ex["sh_gu_s2"][1])]),
+            O.unpack_nvfp4(ex["sh_dn_w"], ex["sh_dn_s"], ex["sh_dn_s2"][0]))
+
+
+class CpuReference:
+    """The reference's algorithm for one layer on the host cores: its own PyTorch code from oracle/_ref when present
+    (kind "reference"), else the numpy port (kind "port"). Holds the layer's packed bytes, converts slots lazily."""
+
+    def __init__(self, packed, threads: int):
+        import torch
+
+        from oracle import ref_torch  # CPU-baseline leg only
+
+        self.cfg = packed.cfg
+        self.threads = threads
+        self.groups, self.ex = packed.to_groups_numpy()
+        self.kind = "reference" if ref_torch.available() else "port"
+        self._ref = ref_torch
+        self._torch_groups: dict[int, dict] = {}
+        torch.set_num_threads(threads)
+
+    def _slots_of(self, x_f32):
+        import numpy as np
+
+        from oracle import folded_moe_oracle as O
+
+        ids, _ = O.router_softmax_topk(O.router_logits_fixed(x_f32, self.ex["router_w"]), self.cfg.top_k)
+        return sorted({int(e) // self.cfg.group_size for e in np.asarray(ids).reshape(-1)})
+
+    def forward(self, x) -> tuple[float, int]:
+        """Runs one forward over the token batch x (torch tensor, any device); returns (seconds, tokens)."""
+        import torch
+
+        c = self.cfg
+        xs = x.float().cpu()
+        if self.kind == "reference":
+            for g in self._slots_of(xs.numpy()):  # conversion of the touched slots' bytes to tensors is not timed
+                if g not in self._torch_groups:
+                    self._torch_groups[g] = self._ref.group_to_torch(self.groups[g])
+            shared = {k: torch.from_numpy(v) for k, v in self.ex.items() if k.startswith("sh_")} or None
+            rw = torch.from_numpy(self.ex["router_w"])
+            t0 = time.perf_counter()
+            self._ref.layer_forward(xs, self._torch_groups, rw, c.top_k, c.hidden, c.inter, c.group_size, shared=shared)
+            return time.perf_counter() - t0, xs.shape[0]
+        from oracle import folded_moe_oracle as O
+
+        O.set_threads(self.threads)
+        shared = _shared_fp32(self.ex) if "sh_gu_w" in self.ex else None
+        t0 = time.perf_counter()
+        O.moe_layer_forward(xs.numpy(), self.groups, self.ex["router_w"], c.top_k, c.hidden, c.inter, c.group_size,
+                            router=c.router, e_bias=self.ex.get("e_bias"), shared=shared)
+        return time.perf_counter() - t0, xs.shape[0]
+
+
+def _stage_events(layer, x, fn=None):
+    """One forward with CUDA events at the stage boundaries inside the C ABI call; returns the 7 stage durations in us."""
     import ctypes
 
     import torch
 
-    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer, _lib
+    from chronos_b200 import _lib
+
+    st = torch.cuda.current_stream()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    for ev in evs:
+        ev.record(st)  # forces creation of the underlying handle
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * 8)(*[ev.cuda_event for ev in evs])
+    _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, 8))
+    (fn or layer)(x)
+    _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
+    torch.cuda.synchronize()
+    return [1e3 * evs[j].elapsed_time(evs[j + 1]) for j in range(7)]
+
+
+STAGE_NAMES = ("router", "plan", "gu_input", "gu_bank_pass", "swiglu_dn_input", "dn_bank_pass", "combine")
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
+    import torch
+
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
     from chronos_b200 import build as cuda_build
 
     cuda_build.build()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     cfg = FoldedLayerConfig(**DECODE)
-    tail = (args.tail, args.tail) if args.tail else (0, 0)  # optional tail lattice (next-row feature): same codes width for both products
+    tail = (args.tail, args.tail) if args.tail else (0, 0)  # optional tail lattice: same code width for both products
     layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=1, device=dev, with_shared=True, tail_bits=tail), register=False)
     streams = args.streams
     batches = decode_batches(cfg, streams, dev)
@@ -187,13 +244,14 @@ def run_decode(args) -> dict:
     K, W = args.steps, max(args.warmup, 3)
     st = torch.cuda.current_stream()
 
-    sampler = ClockSampler(0)
+    own_sampler = sampler is None
+    if own_sampler:
+        sampler = ClockSampler(dev.index or 0)
     for i in range(W):
         layer(batches[i % N_BATCHES])
     torch.cuda.synchronize()
     # ---- device-resident throughput: exactly K steps between two events -----------------------------------------
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     e0.record(st)
     for i in range(K):
         layer(batches[i % N_BATCHES])
@@ -203,25 +261,15 @@ def run_decode(args) -> dict:
     assert layer.device_status() == 0, "device status word raised during the timed loop"
 
     # ---- per-stage durations (same steps, events at the stage boundaries inside the C ABI call) ------------------
-    n_ev = 8
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(K)]
-    for row in evs:
-        for ev in row:
-            ev.record(st)  # forces creation of the underlying handle
-    torch.cuda.synchronize()
-    arr_t = ctypes.c_void_p * n_ev
-    for i in range(K):
-        arr = arr_t(*[ev.cuda_event for ev in evs[i]])
-        _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, n_ev))
-        layer(batches[i % N_BATCHES])
-    _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
-    torch.cuda.synchronize()
-    names = ("router", "plan", "gu_input", "gu_bank_pass", "swiglu_dn_input", "dn_bank_pass", "combine")
+    n_ev_steps = min(K, 40)
+    rows = [_stage_events(layer, batches[i % N_BATCHES]) for i in range(n_ev_steps)]
     fp4 = bool(layer.packed.struct.gu_t)  # the layer carries re-tiled banks: the auto regime streams them through FP4 MMA
+    fused = fp4 and not args.tail
     bank_kernel = "bank_fp4_kernel" if fp4 else "bank_stream_kernel"
-    stage_us = {nm: 1e3 * statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(K)) for j, nm in enumerate(names)}
-    gu_bytes = statistics.mean(stats[i % N_BATCHES]["gu_pass_bytes"] for i in range(K))
-    dn_bytes = statistics.mean(stats[i % N_BATCHES]["dn_pass_bytes"] for i in range(K))
+    stage_us = {nm: statistics.mean(r[j] for r in rows) for j, nm in enumerate(STAGE_NAMES)}
+    key_gu, key_dn = ("gu_pass_bytes", "dn_pass_bytes") if fused else ("gu_bank_bytes", "dn_bank_bytes")
+    gu_bytes = statistics.mean(stats[i % N_BATCHES][key_gu] for i in range(n_ev_steps))
+    dn_bytes = statistics.mean(stats[i % N_BATCHES][key_dn] for i in range(n_ev_steps))
     layer_bytes = statistics.mean(stats[i % N_BATCHES]["layer_bytes"] for i in range(K))
     if args.tail:  # per distinct expert: codes + e4m3 block scales of the gate_up and down tail matrices
         blk = 32 if args.tail == 2 else 64
@@ -243,12 +291,15 @@ def run_decode(args) -> dict:
     e1.record(st)
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1)
-    clocks = sampler.stop()
+    clocks = sampler.stop() if own_sampler else None
 
     peak, peak_kind = _peaks()
     gu_gbs = gu_bytes / (stage_us["gu_bank_pass"] * 1e-6) / 1e9
     dn_gbs = dn_bytes / (stage_us["dn_bank_pass"] * 1e-6) / 1e9
     step_s = ms_total * 1e-3 / K
+    # kernels of this library per step: fused decode path = front, gate_up pass, mid, down pass, combine; the separate-kernel
+    # path = router, plan (+ top-k), input transform, 2 bank passes, SwiGLU, down transform, combine (+ fp16 image, 2 tail passes)
+    launches = 5 if fused else 8 + (3 if args.tail else 0)
     out = {
         "metric": "folded_moe_decode_tokens_per_s", "value": n_tok / step_s, "unit": "tokens/s", "n_gpus": 1,
         "steps": K, "warmup": W, "ms_per_step": ms_total / K, "higher_is_better": True, "scaling": "weak",
@@ -265,25 +316,28 @@ def run_decode(args) -> dict:
                    "top8_overlap_within_stream": round(statistics.mean(s["overlap"] for s in stats), 3)},
         "e2e": {"value": n_tok / (ms_e2e * 1e-3 / K), "unit": "tokens/s", "h2d_bytes_per_step": n_tok * cfg.hidden * 2,
                 "d2h_bytes_per_step": n_tok * cfg.hidden * 2},
-        "gpu_launches": (8 + (2 if args.tail else 0) + (1 if args.tail else 0)) * K,  # router, plan(+top-k), input transform, 2 bank passes, SwiGLU, down transform, combine (+ fp16 image, 2 tail passes)
+        "gpu_launches": launches * K,
         "clocks": clocks,
-        "roofline": {"bound": "hbm", "kernel": f"{bank_kernel} (gate_up pass)", "achieved": gu_gbs, "peak": peak,
-                     "peak_kind": f"of {peak_kind}", "unit": "GB/s", "frac": gu_gbs / peak,
+        "roofline": {"bound": "hbm", "kernel": f"{bank_kernel} (gate_up pass" + (", healer product in its side warps)" if fused else ")"),
+                     "achieved": gu_gbs, "peak": peak, "peak_kind": f"of {peak_kind}", "unit": "GB/s", "frac": gu_gbs / peak,
                      "traffic": GU_PASS_TRAFFIC_OVER_ALGORITHMIC * gu_bytes, "algorithmic_bytes_per_launch": gu_bytes},
         "layer_hbm": {"algorithmic_bytes_per_step": layer_bytes, "achieved_gbs": layer_bytes / step_s / 1e9,
                       "frac_of_peak": layer_bytes / step_s / 1e9 / peak, "frac_of_8tbs": layer_bytes / step_s / 8e12},
         "stages_us": {k: round(v, 2) for k, v in stage_us.items()},
         "dn_bank_pass_gbs": dn_gbs,
     }
-    if not args.no_cpu_baseline:
+    if with_cpu_baseline and not args.no_cpu_baseline:
         threads = host_threads()
-        tps, secs = cpu_oracle_tokens_per_s(layer, batches[0][:TOKENS_PER_STREAM], threads)
-        out["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+        ref = CpuReference(layer.packed, threads)
+        secs, n = ref.forward(batches[0][:TOKENS_PER_STREAM])
+        out["cpu_baseline"] = {"value": n / secs, "unit": "tokens/s", "cores": threads, "kind": ref.kind,
                                "sample": f"one stream ({TOKENS_PER_STREAM} tokens) of batch 0, one pass, {secs:.1f} s"}
+    del layer
+    torch.cuda.empty_cache()
     return out
 
 
-def run_prefill(args) -> dict:
+def run_prefill(args, steps: int | None = None, ceiling: bool | None = None) -> dict:
     """Prefill-shaped layer (config index 3): the decode layer's shapes, 8192 tokens bf16, router biased so that
     expert popularity follows Zipf(1.1). Reports tokens/s and useful TFLOP/s of the tensor regime."""
     import numpy as np
@@ -291,31 +345,24 @@ def run_prefill(args) -> dict:
 
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
     from chronos_b200 import build as cuda_build
+    from chronos_b200.workloads import zipf_prefill_batch
 
     cuda_build.build()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    ceiling = args.workload == "fp4_ceiling"
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ceiling = (args.workload == "fp4_ceiling") if ceiling is None else ceiling
     # fp4_ceiling: the same kernels on ONE slot (4 experts, every token routed to all 4): banks and activation images
     # stay in L2, work items are all full - an empirical ceiling for this tile shape, not a workload of the reference
     cfg = FoldedLayerConfig(**{**DECODE, **({"n_experts": 4, "top_k": 4} if ceiling else {})})
     layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, device=dev, with_shared=not ceiling), register=False)
     n_tok = args.tokens
     regime = args.regime or "tensor_fp4"
-    gen = torch.Generator(device=dev).manual_seed(2)
-    x = torch.randn(n_tok, cfg.hidden, generator=gen, device=dev).to(torch.bfloat16)
-    # Zipf(1.1) popularity over a seeded permutation of experts: add c * log p_e to the logits by shifting the router
-    # rows along the mean activation direction is not possible for N(0,1) inputs, so the bias is injected through one
-    # extra input channel: x[:, 0] = 1 and router_w[:, 0] = c * log p_e.
-    perm = torch.randperm(cfg.n_experts, generator=torch.Generator().manual_seed(2))
-    p_e = (torch.arange(1, cfg.n_experts + 1, dtype=torch.float64) ** -1.1)
-    p_e = (p_e / p_e.sum())[torch.argsort(perm)]
-    if not ceiling:
-        layer.packed.t["router_w"][:, 0] = (1.0 * torch.log(p_e)).to(torch.float32).to(dev)
-        x[:, 0] = 1.0
+    if ceiling:
+        x = torch.randn(n_tok, cfg.hidden, generator=torch.Generator(device=dev).manual_seed(2), device=dev).to(torch.bfloat16)
+    else:
+        x = zipf_prefill_batch(layer, n_tok, seed=2)
     ids = layer.route(x)[0]
     counts = torch.bincount(ids.reshape(-1).long(), minlength=cfg.n_experts).cpu().numpy()
-    K, W = max(args.steps // 20, 3), 3
+    K, W = steps or max(args.steps // 20, 3), 3
     st = torch.cuda.current_stream()
     for _ in range(W):
         layer.forward_impl(x, regime=regime)
@@ -328,20 +375,8 @@ def run_prefill(args) -> dict:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / K
     assert layer.device_status() == 0
-    import ctypes
-
-    from chronos_b200 import _lib
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
-    for ev in evs:
-        ev.record(st)
-    torch.cuda.synchronize()
-    arr = (ctypes.c_void_p * 8)(*[ev.cuda_event for ev in evs])
-    _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, 8))
-    layer.forward_impl(x, regime=regime)
-    _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
-    torch.cuda.synchronize()
-    names = ("router", "plan", "gu_input", "gu_bank_pass", "swiglu_dn_input", "dn_bank_pass", "combine")
-    stage_us = {nm: round(1e3 * evs[j].elapsed_time(evs[j + 1]), 1) for j, nm in enumerate(names)}
+    stage = _stage_events(layer, x, fn=lambda t: layer.forward_impl(t, regime=regime))
+    stage_us = {nm: round(stage[j], 1) for j, nm in enumerate(STAGE_NAMES)}
     pairs = n_tok * cfg.top_k
     bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
     healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
@@ -356,19 +391,20 @@ def run_prefill(args) -> dict:
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
     fp4 = regime == "tensor_fp4"
     achieved = gemm_flops / gemm_s / 1e12
+    terms = layer.activation_terms if fp4 else 1
     if fp4:
-        # the block-scaled pass multiplies every bank tile by 3 residual FP4 terms of the activations: the pipe does 3x the
-        # useful FLOPs; no FP4 figure is in MEASURED_PEAKS.json, so the denominator is the datasheet dense FP4 rate
-        roof = {"bound": "tensor", "kernel": "bank_fp4_wide_kernel (both passes)", "achieved": achieved, "peak": 9000.0,
-                "peak_kind": "nominal dense FP4 (datasheet; not in MEASURED_PEAKS.json)", "unit": "TFLOP/s", "frac": achieved / 9000.0,
-                "mma_issue_tflops": 3 * achieved, "mma_issue_frac": 3 * achieved / 9000.0,
+        # the block-scaled pass multiplies every bank tile by `terms` residual FP4 terms of the activations: the pipe does
+        # that many times the useful FLOPs; no FP4 figure is in MEASURED_PEAKS.json, so the denominator is the datasheet rate
+        roof = {"bound": "tensor", "kernel": "bank_fp4_wide_kernel (both passes)", "achieved": achieved, "peak": FP4_NOMINAL_TFLOPS,
+                "peak_kind": "nominal dense FP4 (datasheet; not in MEASURED_PEAKS.json)", "unit": "TFLOP/s", "frac": achieved / FP4_NOMINAL_TFLOPS,
+                "activation_terms": terms, "mma_issue_tflops": terms * achieved, "mma_issue_frac": terms * achieved / FP4_NOMINAL_TFLOPS,
                 "achieved_vs_measured_bf16": achieved / bf16_peak, "traffic": None}
-        dtype = "e2m1 x ue4m3 block-scaled operands (banks as stored, activations as 3 residual FP4 terms), fp32 accumulate in TMEM"
+        dtype = f"e2m1 x ue4m3 block-scaled operands (banks as stored, activations as {terms} residual FP4 terms), fp32 accumulate in TMEM"
     else:
         roof = {"bound": "tensor", "kernel": "bank_gemm_kernel (both passes)", "achieved": achieved, "peak": bf16_peak,
                 "peak_kind": "of measured bf16 (operands are f16)", "unit": "TFLOP/s", "frac": achieved / bf16_peak, "traffic": None}
         dtype = "f16 operands (NVFP4 banks converted exactly), fp32 accumulate in TMEM"
-    return {
+    out = {
         "metric": "folded_moe_prefill_tokens_per_s", "value": n_tok / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": dtype, "data": "synthetic",
@@ -377,9 +413,27 @@ def run_prefill(args) -> dict:
                    "router_popularity": "all tokens to all 4 experts" if ceiling else "Zipf(1.1)", "pairs_per_expert_max": int(counts.max()), "pairs_per_expert_median": float(np.median(counts)),
                    "pairs_per_expert_min": int(counts.min())},
         "useful_tflops_layer": useful / (ms * 1e-3) / 1e12,
+        "non_gemm_share_of_layer": 1.0 - gemm_s / (sum(stage_us.values()) * 1e-6),
         "roofline": roof,
         "stages_us": stage_us,
     }
+    del layer
+    torch.cuda.empty_cache()
+    return out
+
+
+def prefill_subrecord(args) -> dict:
+    """Config 3 (8192 tokens, Zipf(1.1)) with its roofline, plus the empirical FP4 ceiling of the same tile shapes."""
+    import argparse as _ap
+
+    a = _ap.Namespace(**{**vars(args), "tokens": PREFILL_TOKENS, "regime": "tensor_fp4", "workload": "prefill"})
+    res = run_prefill(a, steps=5, ceiling=False)
+    ceil = run_prefill(a, steps=5, ceiling=True)
+    roof = res["roofline"]
+    roof["empirical_ceiling_tflops"] = ceil["roofline"]["achieved"]
+    roof["frac_of_empirical_ceiling"] = roof["achieved"] / ceil["roofline"]["achieved"]
+    return {k: res[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "config", "useful_tflops_layer",
+                                "non_gemm_share_of_layer", "roofline", "stages_us", "dtype")}
 
 
 def run_sweep(args) -> dict:
@@ -434,49 +488,73 @@ def run_sweep(args) -> dict:
             "peak": peak, "peak_kind": f"of {kind}", "rows": rows}
 
 
-def run_reference(args) -> dict:
-    """The reference's algorithm on the host cores: the CPU oracle port, one token of the decode workload per step."""
+def run_reference(args, workload: str) -> dict:
+    """The reference's algorithm for the same configuration on the host cores (its own PyTorch code from oracle/_ref;
+    the numpy port when that folder is absent). decode: the GPU arm's 12-token batches, one batch per step, as many of
+    the requested steps as fit the time bound. ep_stack: one layer of the stack on a token subsample, scaled to the
+    42-layer step (the reference has no distributed path: the CPU arm is one process whatever N is)."""
     import torch
 
     from chronos_b200 import FoldedLayerConfig, PackedLayer
 
     cfg = FoldedLayerConfig(**DECODE)
     have_gpu = torch.cuda.is_available()
-    dev = torch.device("cuda", 0) if have_gpu else torch.device("cpu")
-
-    class _Holder:  # the packed bytes only; nothing of the CUDA path runs in this arm
-        pass
-
-    if have_gpu:
-        packed = PackedLayer.synthetic(cfg, seed=1, device=dev, with_shared=True)
-        batches = decode_batches(cfg, args.streams, dev)
-    else:
-        raise SystemExit(json.dumps({"impl": "reference", "unavailable": "needs the synthetic layer generator, which draws on a CUDA device"}))
-    holder = _Holder()
-    holder.packed, holder.cfg = packed, cfg
+    dev = torch.device("cuda", 0) if have_gpu else torch.device("cpu")  # same seeded bytes as the GPU arm when it can draw them there
     threads = host_threads()
     K, W = args.steps, args.warmup
-    times = []
-    for i in range(W + K):
-        x = batches[i % N_BATCHES][:1]
-        tps, secs = cpu_oracle_tokens_per_s(holder, x, threads)
-        if i >= W:
-            times.append(secs)
-        if sum(times) > 240:  # bounded: a few minutes at most
+    if workload == "decode":
+        packed = PackedLayer.synthetic(cfg, seed=1, device=dev, with_shared=True)
+        batches = decode_batches(cfg, args.streams, dev)
+        sample = f"{args.streams} streams x {TOKENS_PER_STREAM} tokens per step (the GPU arm's batches)"
+        scale, metric, wl_cfg = 1.0, "folded_moe_decode_tokens_per_s", {"workload": "decode_layer", "streams": args.streams, "tokens_per_stream": TOKENS_PER_STREAM}
+        scaling = "weak"
+    else:
+        packed = PackedLayer.synthetic_sharded(cfg, 3, range(cfg.n_slots), dev, True)
+        gen = torch.Generator(device=dev).manual_seed(3)
+        h0 = torch.randn(EP_TOKENS, cfg.hidden, generator=gen, device=dev).to(torch.bfloat16)
+        n_sub = 12
+        batches = [h0[i * n_sub:(i + 1) * n_sub] for i in range(N_BATCHES)]
+        sample = f"layer 0 of the stack on {n_sub} of the {EP_TOKENS} tokens per step; tokens/s divided by the {args.layers} layers"
+        scale, metric, wl_cfg = 1.0 / args.layers, "folded_moe_ep_stack_tokens_per_s", {"workload": "ep_stack", "layers": args.layers, "tokens_per_step": EP_TOKENS}
+        scaling = "strong"
+    ref = CpuReference(packed, threads)
+    ref.forward(batches[0][:1])  # untimed: thread pools, imports, first-touch of one token's slots
+    times, toks = [], 0
+    for i in range(K):
+        secs, n = ref.forward(batches[i % N_BATCHES])
+        times.append(secs)
+        toks += n
+        if sum(times) + secs > REFERENCE_BUDGET_S:  # bounded: the next step would run past the budget
             break
     done = len(times)
-    val = done / sum(times)
-    return {
-        "impl": "reference", "metric": "folded_moe_decode_tokens_per_s", "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": done, "warmup": W, "ms_per_step": 1e3 * sum(times) / done, "higher_is_better": True, "scaling": "weak",
+    val = scale * toks / sum(times)
+    out = {
+        "impl": "reference", "metric": metric, "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": done, "warmup": 1, "ms_per_step": 1e3 * sum(times) / done, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode_layer", "hidden": cfg.hidden, "routed_experts": cfg.n_experts, "shared_experts": 1,
+        "config": {**wl_cfg, "hidden": cfg.hidden, "routed_experts": cfg.n_experts, "shared_experts": 1,
                    "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
-                   "sample": "1 token per step (8 routed experts + shared), same packed bytes as the GPU arm"},
-        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{done} steps of 1 token each"},
+                   "sample": sample, "steps_requested": K, "time_bound_s": REFERENCE_BUDGET_S},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": ref.kind, "sample": f"{done} steps; {sample}"},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if have_gpu and ref.kind == "reference" and not args.no_reference_cuda:
+        # the same reference code with its tensors on the GPU ("the reference on the same box"): one untimed + one timed step
+        from oracle import ref_torch
+
+        x = batches[0].float()
+        groups = {g: ref_torch.group_to_torch(ref.groups[g], "cuda") for g in ref._slots_of(x.cpu().numpy())}
+        shared = {k: torch.from_numpy(v).cuda() for k, v in ref.ex.items() if k.startswith("sh_")}
+        rw = torch.from_numpy(ref.ex["router_w"]).cuda()
+        for rep in range(2):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ref_torch.layer_forward(x, groups, rw, cfg.top_k, cfg.hidden, cfg.inter, cfg.group_size, shared=shared)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+        out["reference_on_gpu"] = {"value": scale * x.shape[0] / dt, "unit": "tokens/s", "ms_per_step": 1e3 * dt,
+                                   "note": "the reference's PyTorch path with device=cuda, one step, wall clock around a synchronise"}
+    return out
 
 
 class _StdoutToStderr:
@@ -497,8 +575,8 @@ class _StdoutToStderr:
 
 
 def ep_stack_single_gpu(args) -> dict:
-    """The N > 1 workload (42-layer stack, 4096 tokens per step) on one GPU, 3 timed steps."""
-    import argparse
+    """The expert-parallel workload (42-layer stack, 4096 tokens per step) on one GPU, as a sub-record of the decode line."""
+    import argparse as _ap
     import gc
 
     import torch
@@ -507,54 +585,73 @@ def ep_stack_single_gpu(args) -> dict:
 
     gc.collect()
     torch.cuda.empty_cache()
-    small = argparse.Namespace(**{**vars(args), "steps": 3, "warmup": 3})
+    small = _ap.Namespace(**{**vars(args), "steps": min(args.steps, 10), "warmup": 3})
     res = ep_bench.run(small, args.layers, EP_TOKENS, DECODE, None)
-    return {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "ms_per_step": res["ms_per_step"],
-            "steps": res["steps"], "config": {"workload": "ep_stack", "layers": args.layers, "tokens_per_step": EP_TOKENS}}
+    return {k: res[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "parity", "phase_us_per_layer_rank0") if k in res} | {
+        "config": {"workload": "ep_stack", "layers": args.layers, "tokens_per_step": EP_TOKENS}}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--workload", default=None, choices=(None, "decode", "ep_stack", "prefill", "sweep", "fp4_ceiling"))
-    ap.add_argument("--tokens", type=int, default=8192, help="tokens of the prefill workload")
+    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS, help="tokens of the prefill workload")
     ap.add_argument("--regime", default=None, choices=(None, "auto", "tensor", "tensor_fp4"), help="bank-pass regime of the prefill workload")
     ap.add_argument("--streams", type=int, default=DECODE_STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-ep-base", action="store_true", help="skip the single-GPU run of the N > 1 workload appended to the default line")
+    ap.add_argument("--no-sub-records", action="store_true", help="skip the prefill / ep_stack (resp. decode) sub-records of the default lines")
+    ap.add_argument("--no-reference-cuda", action="store_true", help="reference arm: skip the extra run of the reference code on the GPU")
     ap.add_argument("--tail", type=int, default=0, choices=(0, 1, 2), help="decode workload: add a tail lattice of this many bits per weight")
     ap.add_argument("--layers", type=int, default=EP_LAYERS, help="depth of the ep_stack workload")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    # under the distributed launcher (world size 1 included) and for N > 1 the line is the expert-parallel stack, so that the
+    # lines of a 1-2-4-8 GPU series are the same metric; a plain `python bench.py` is the decode layer
+    launched = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_RANK" in os.environ
+    workload = args.workload or ("ep_stack" if (args.gpus > 1 or world > 1 or launched) else "decode")
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            with _StdoutToStderr():
+                res = run_reference(args, "ep_stack" if workload == "ep_stack" else "decode")
+            print(json.dumps(res), flush=True)
         return
-    workload = args.workload or ("decode" if args.gpus == 1 and world == 1 else "ep_stack")
     if workload in ("decode", "prefill", "sweep", "fp4_ceiling"):
         if rank == 0:
-            fn = {"decode": run_decode, "prefill": run_prefill, "sweep": run_sweep, "fp4_ceiling": run_prefill}[workload]
-            out = fn(args)
-            if workload == "decode" and args.workload is None and not args.no_ep_base:
-                # the N > 1 lines run the expert-parallel stack (a different workload): give the N = 1 line the same
-                # stack on one GPU, so that strong-scaling ratios can be formed from like quantities
-                try:
-                    with _StdoutToStderr():
-                        out["ep_stack_1gpu"] = ep_stack_single_gpu(args)
-                except Exception as exc:  # the headline line must not depend on this extra measurement
-                    out["ep_stack_1gpu"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+            import torch
+
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            with _StdoutToStderr():
+                out = {"decode": run_decode, "prefill": run_prefill, "sweep": run_sweep, "fp4_ceiling": run_prefill}[workload](args)
+                if workload == "decode" and args.workload is None and not args.no_sub_records:
+                    # the other half of the metric (prefill FP4 TFLOP/s) and the N > 1 workload on one GPU, in the same line
+                    for name, fn in (("prefill", prefill_subrecord), ("ep_stack_1gpu", ep_stack_single_gpu)):
+                        try:
+                            out[name] = fn(args)
+                        except Exception as exc:  # the headline must not depend on the extra measurements
+                            out[name] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
             print(json.dumps(out), flush=True)
         return
     from chronos_b200 import ep_bench
 
     with _StdoutToStderr():
         res = ep_bench.run(args, args.layers, EP_TOKENS, DECODE, ClockSampler)
+        if rank == 0 and world == 1 and not args.no_sub_records:
+            # world size 1: the decode layer (the configuration the headline metric is quoted on) rides along
+            try:
+                import argparse as _ap
+
+                d = run_decode(_ap.Namespace(**{**vars(args), "steps": min(args.steps, 50)}), sampler=False, with_cpu_baseline=False)
+                res["decode_layer"] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "roofline", "layer_hbm", "stages_us", "e2e")}
+            except Exception as exc:
+                res["decode_layer"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0:
         print(json.dumps(res), flush=True)
+        if res.get("parity", {}).get("rel_l2", 0.0) > 1e-2:
+            sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX, ROUTER_SQRT_SOFTPLUS = 0, 1, 2
-ABI_VERSION = 7
+ABI_VERSION = 8
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4, REGIME_TENSOR_FP4 = 0, 1, 2, 3, 4
 
 
@@ -47,6 +47,10 @@ EXPORTS = {
     "chronos_b200_router_topk": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_workspace_bytes": (C.c_size_t, [C.POINTER(LayerStruct), C.c_int]),
     "chronos_b200_fp4_mma_probe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "chronos_b200_ep_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "chronos_b200_ep_unpack_meta": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "chronos_b200_ep_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
     "chronos_b200_wait_probe": (C.c_int, [C.c_void_p, C.c_uint, C.c_void_p]),
     "chronos_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int]),
     "chronos_b200_workspace_status_offset": (C.c_long, [C.POINTER(LayerStruct), C.c_int]),

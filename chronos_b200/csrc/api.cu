@@ -266,7 +266,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 7; }
+int chronos_b200_abi_version(void) { return 8; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -388,6 +388,49 @@ int chronos_b200_fp4_mma_probe(const uint8_t* a_image, const uint8_t* b_image, i
     if (b_rows < 16 || b_rows > 256 || b_rows % 16) { set_error("fp4_probe: b_rows (%d) must be a multiple of 16 in 16..256", b_rows); return CHRONOS_E_SHAPE; }
     if (!aligned16(a_image) || !aligned16(b_image) || !d_out || !status) { set_error("fp4_probe: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
     return launch_fp4_probe(a_image, b_image, n_stages, b_rows, d_out, status, (cudaStream_t)stream);
+}
+
+static int validate_ep(int n_tokens, int top_k, int hidden, int world, int capacity) {
+    if (n_tokens < 0 || n_tokens > (1 << 20) || top_k <= 0 || top_k > kMaxTopK || hidden <= 0 || hidden % 8 || world <= 0 || world > 64 ||
+        capacity <= 0 || capacity > (1 << 20)) {
+        set_error("ep: n_tokens %d, top_k %d, hidden %d (multiple of 8), world %d (<= 64) or capacity %d out of range", n_tokens, top_k, hidden, world, capacity);
+        return CHRONOS_E_SHAPE;
+    }
+    return CHRONOS_OK;
+}
+
+int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                         int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
+                         int32_t* overflow, void* stream) {
+    if (int rc = validate_ep(n_tokens, top_k, hidden, world, capacity)) return rc;
+    if (x_dtype != CHRONOS_DTYPE_F32 && x_dtype != CHRONOS_DTYPE_BF16) { set_error("ep_pack: bad dtype"); return CHRONOS_E_ARG; }
+    if (experts_per_rank <= 0) { set_error("ep_pack: experts_per_rank (%d) must be positive", experts_per_rank); return CHRONOS_E_SHAPE; }
+    if (n_tokens > 0 && (!aligned16(x) || !aligned16(send_rows) || !ids || !gates || !send_meta || !slot_of || !overflow)) {
+        set_error("ep_pack: NULL or misaligned pointer");
+        return CHRONOS_E_ALIGN;
+    }
+    return launch_ep_pack(x, x_dtype, ids, gates, n_tokens, top_k, hidden, world, experts_per_rank, capacity, send_rows, send_meta, slot_of,
+                          overflow, (cudaStream_t)stream);
+}
+
+int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, void* stream) {
+    if (int rc = validate_ep(0, top_k, 8, world, capacity)) return rc;
+    if (!recv_meta || !ids_out || !gates_out) { set_error("ep_unpack_meta: NULL pointer"); return CHRONOS_E_ALIGN; }
+    return launch_ep_unpack_meta(recv_meta, world, capacity, top_k, ids_out, gates_out, (cudaStream_t)stream);
+}
+
+int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
+                            int capacity, void* y, int y_dtype, void* stream) {
+    if (int rc = validate_ep(n_tokens, 1, hidden, world, capacity)) return rc;
+    if ((dtype != CHRONOS_DTYPE_F32 && dtype != CHRONOS_DTYPE_BF16) || (y_dtype != CHRONOS_DTYPE_F32 && y_dtype != CHRONOS_DTYPE_BF16)) {
+        set_error("ep_combine: bad dtype");
+        return CHRONOS_E_ARG;
+    }
+    if (n_tokens > 0 && (!aligned16(back_rows) || !aligned16(y) || !slot_of || (extra != nullptr && !aligned16(extra)))) {
+        set_error("ep_combine: NULL or misaligned pointer");
+        return CHRONOS_E_ALIGN;
+    }
+    return launch_ep_combine(back_rows, dtype, slot_of, extra, n_tokens, hidden, world, capacity, y, y_dtype, (cudaStream_t)stream);
 }
 
 int chronos_b200_wait_probe(int32_t* status, unsigned poll_limit, void* stream) {

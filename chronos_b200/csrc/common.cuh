@@ -246,6 +246,13 @@ int launch_decode_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
 int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                           int y_dtype, cudaStream_t st);
 int launch_bank_fp4_fused(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, const void* x, int x_dtype, cudaStream_t st);
+// expert-parallel dispatch / combine helpers (csrc/ep_kernels.cu)
+int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                   int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
+                   int32_t* overflow, cudaStream_t st);
+int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, cudaStream_t st);
+int launch_ep_combine(const void* back, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
+                      int capacity, void* y, int y_dtype, cudaStream_t st);
 int launch_wait_probe(int32_t* status, uint32_t poll_limit, cudaStream_t st);
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st);

@@ -5,16 +5,23 @@ never split (its K experts share one bank), rank g owns slots [g*n_slots/G, (g+1
 RMSNorm and the shared expert are replicated; tokens are data-parallel.
 
 Per layer, stream-ordered and free of host synchronisation:
-  dispatch  every rank routes its own tokens, then the normed token rows and their (expert id, gate) lists are
-            exchanged so that each rank sees all tokens (capacity-padded exchange: each peer gets a fixed-size
-            block, so no split sizes ever travel through the host);
-  compute   each rank evaluates only the routing entries whose expert it owns (the others are masked to -1 and
-            skipped on the device) plus, in the same pass, the shared expert for the tokens it is the home of;
-  combine   the per-rank partial sums are reduce-scattered back to the tokens' home ranks in fp32.
-One process per GPU; `torch.distributed` (NCCL over NVLink, or gloo in CPU tests of the host logic).
+  route     every rank routes its own tokens (global expert ids + gates);
+  dispatch  a token's normed hidden row goes ONCE to every rank that owns at least one of its experts, with its expert
+            ids local to that rank and their gates: a device kernel packs fixed-capacity blocks per destination
+            (`chronos_b200_ep_pack`), one all-to-all with equal splits moves the rows, one the metadata - no split
+            sizes ever travel through the host;
+  compute   each rank evaluates the received rows' entries (all of them are its own experts) and, in the same pass,
+            the shared expert of the tokens it is the home of;
+  combine   ONE bf16 partial-sum row per received token goes back the same way, and the home rank adds the partial rows in
+            rank order to the shared expert's row (`chronos_b200_ep_combine`).
+A block's capacity covers the expected number of tokens per destination plus six standard deviations; a batch routed
+so unevenly that a block overflows raises a device flag that `overflowed()` reads (the caller then repeats the step with
+`capacity_factor = 1`, which always fits). One process per GPU; `torch.distributed` (NCCL over NVLink, or gloo in CPU
+tests of the host logic, which substitute their own pack / compute / combine callables).
 """
 from __future__ import annotations
 
+import math
 from typing import Callable, Optional
 
 import torch
@@ -22,7 +29,7 @@ import torch.distributed as dist
 
 from . import _lib
 from .layout import FoldedLayerConfig, PackedLayer
-from .moe import FoldedMoELayer, residual_rmsnorm
+from .moe import _DTYPES, FoldedMoELayer, residual_rmsnorm
 
 
 def slot_range(n_slots: int, world: int, rank: int) -> range:
@@ -39,16 +46,35 @@ def localize_routing(ids: torch.Tensor, first_expert: int, n_local: int) -> torc
     return torch.where((local >= 0) & (local < n_local), local, torch.full_like(local, -1)).to(torch.int32)
 
 
+def block_capacity(tokens_local: int, world: int, top_k: int, capacity_factor: Optional[float] = None) -> int:
+    """Rows per (source, destination) block. A token routes >= 1 of its top_k experts to a given rank with probability
+    p = 1 - (1 - 1/world)^top_k under balanced routing; the default leaves six standard deviations of head-room (and never
+    exceeds the token count, which always fits). `capacity_factor` overrides it as a fraction of the local tokens."""
+    if capacity_factor is not None:
+        cap = math.ceil(capacity_factor * tokens_local)
+    else:
+        p = 1.0 - (1.0 - 1.0 / world) ** top_k
+        cap = math.ceil(p * tokens_local + 6.0 * math.sqrt(tokens_local * p * (1.0 - p)) + 8.0)
+    return max(8, min(tokens_local, (cap + 7) // 8 * 8))
+
+
+_OVERFLOW_FLAGS: dict[torch.device, torch.Tensor] = {}  # one device flag per GPU, shared by all layers: one read per step
+
+
+class EpConfigMismatch(RuntimeError):
+    """Raised on EVERY rank, before any data collective, when the ranks disagree on the exchange geometry."""
+
+
 class ExpertParallelMoE:
     """One expert-parallel layer. `local_layer` holds this rank's slots (its config describes the LOCAL expert table
-    with `first_slot` set), `router` computes (global ids, gates) for local tokens.
+    with `first_slot` set); `route_fn(x) -> (global ids, gates)` for local tokens.
 
-    `compute_routed(x_all, local_ids, gates) -> fp32 [T, H]` and `compute_shared(x_local) -> fp32 [Tl, H]` default to
-    the CUDA layer; tests of the host logic on CPU ranks substitute their own callables."""
+    The device work (pack, expert pass, combine) defaults to the CUDA library; tests of the host logic on CPU ranks pass
+    their own `pack_fn`, `compute_fn` and `combine_fn` with the same contracts (see `_pack_cuda` & co.)."""
 
     def __init__(self, local_layer: Optional[FoldedMoELayer], cfg_global: FoldedLayerConfig, group=None,
-                 route_fn: Optional[Callable] = None, compute_routed: Optional[Callable] = None,
-                 compute_shared: Optional[Callable] = None):
+                 route_fn: Optional[Callable] = None, pack_fn: Optional[Callable] = None, compute_fn: Optional[Callable] = None,
+                 combine_fn: Optional[Callable] = None, capacity_factor: Optional[float] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -57,65 +83,119 @@ class ExpertParallelMoE:
         self.first_expert = slots.start * cfg_global.group_size
         self.n_local = len(slots) * cfg_global.group_size
         self.layer = local_layer
+        self.capacity_factor = capacity_factor
         self.route_fn = route_fn or (lambda x: local_layer.route_global(x))
-        # CUDA default: one pass over the gathered tokens evaluates the entries this rank owns AND the shared expert of
-        # the tokens it is the home of (their block inside the gathered order); tests substitute CPU callables and a
-        # separate shared-expert callable
-        self.fused_shared = compute_routed is None and compute_shared is None
-        self.compute_routed = compute_routed or self._routed_cuda
-        self.compute_shared = compute_shared or self._shared_cuda
+        self.pack_fn = pack_fn or self._pack_cuda
+        self.compute_fn = compute_fn or self._compute_cuda
+        self.combine_fn = combine_fn or self._combine_cuda
         self.phase_events = None   # set to [] to record (name, start, end) CUDA events of the next forward
+        self._checked: set[tuple] = set()
 
     def _mark(self, name: str):
         """Context manager recording a CUDA event pair around a phase when `phase_events` is a list."""
         return _Phase(self.phase_events, name)
 
-    def _routed_cuda(self, x_all: torch.Tensor, local_ids: torch.Tensor, gates_all: torch.Tensor) -> torch.Tensor:
-        tl = x_all.shape[0] // self.world
-        rng = (self.rank * tl, tl) if self.layer.n_shared_experts else None
-        return self.layer.routed_forward(x_all, local_ids, gates_all, out_dtype=torch.float32, shared_range=rng)
+    # -- geometry agreement -----------------------------------------------------------------------------------------
+    def check_geometry(self, tokens_local: int, hidden: int, capacity: int) -> None:
+        """All ranks exchange (tokens, hidden, top_k, capacity, experts per rank) once per batch shape and compare: an
+        all-to-all with equal splits would otherwise read or write past a peer's block. Raises `EpConfigMismatch` on
+        every rank (they all see the same table), before any data collective of the layer runs."""
+        key = (tokens_local, hidden, capacity)
+        if key in self._checked:
+            return
+        mine = [tokens_local, hidden, self.cfg.top_k, capacity, self.n_local]
+        table: list = [None] * self.world
+        dist.all_gather_object(table, mine, group=self.group)
+        if any(row != table[0] for row in table):
+            raise EpConfigMismatch("expert-parallel ranks disagree on (tokens per rank, hidden, top_k, block capacity, experts per rank): "
+                                   + "; ".join(f"rank {r}: {row}" for r, row in enumerate(table)))
+        self._checked.add(key)
 
-    def _shared_cuda(self, x_local: torch.Tensor) -> Optional[torch.Tensor]:
-        if self.layer.n_shared_experts == 0:
-            return None
-        none = torch.full((x_local.shape[0], self.cfg.top_k), -1, dtype=torch.int32, device=x_local.device)
-        zero = torch.zeros((x_local.shape[0], self.cfg.top_k), dtype=torch.float32, device=x_local.device)
-        return self.layer.routed_forward(x_local, none, zero, with_shared=True, out_dtype=torch.float32)
+    # -- device work (CUDA library) -----------------------------------------------------------------------------------
+    def _pack_cuda(self, x, ids, gates, capacity):
+        tl, h = x.shape
+        k, w = self.cfg.top_k, self.world
+        dev = x.device
+        rows = torch.empty((w, capacity, h), dtype=x.dtype, device=dev)
+        meta = torch.empty((w, capacity + 1, 2 * k + 2), dtype=torch.int32, device=dev)
+        slot_of = torch.empty((tl, w), dtype=torch.int32, device=dev)
+        flag = _OVERFLOW_FLAGS.get(dev)
+        if flag is None:
+            flag = _OVERFLOW_FLAGS[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check(_lib.lib().chronos_b200_ep_pack(x.data_ptr(), _DTYPES[x.dtype], ids.data_ptr(), gates.data_ptr(), tl, k, h, w, self.n_local,
+                                                 capacity, rows.data_ptr(), meta.data_ptr(), slot_of.data_ptr(), flag.data_ptr(),
+                                                 torch.cuda.current_stream().cuda_stream))
+        return rows, meta, slot_of
 
+    def _compute_cuda(self, recv_rows, recv_meta, x_local, capacity, recv_all=None):
+        """Expert pass over the received rows + the shared expert of the home tokens, one call. Returns (partial rows
+        [world, capacity, H], shared rows [Tl, H] or None), both in the activation dtype. `recv_all` [world * capacity + Tl, H]
+        is the buffer whose head `recv_rows` views and whose tail already holds the home tokens' rows."""
+        w, k = self.world, self.cfg.top_k
+        tl, h = x_local.shape
+        n_recv = w * capacity
+        has_shared = self.layer.n_shared_experts > 0
+        dev = x_local.device
+        ids = torch.empty((n_recv + (tl if has_shared else 0), k), dtype=torch.int32, device=dev)
+        gates = torch.empty((n_recv + (tl if has_shared else 0), k), dtype=torch.float32, device=dev)
+        _lib.check(_lib.lib().chronos_b200_ep_unpack_meta(recv_meta.data_ptr(), w, capacity, k, ids.data_ptr(), gates.data_ptr(),
+                                                        torch.cuda.current_stream().cuda_stream))
+        if has_shared:  # the home tokens ride along as extra rows that take the shared expert only
+            ids[n_recv:].fill_(-1)
+            gates[n_recv:].zero_()
+            x_all = recv_all if recv_all is not None else torch.cat([recv_rows.reshape(n_recv, h), x_local])
+            out = self.layer.routed_forward(x_all, ids, gates, out_dtype=x_local.dtype, shared_range=(n_recv, tl))
+            return out[:n_recv].view(w, capacity, h), out[n_recv:]
+        out = self.layer.routed_forward(recv_rows.view(n_recv, h), ids, gates, out_dtype=x_local.dtype)
+        return out.view(w, capacity, h), None
+
+    def _combine_cuda(self, back_rows, slot_of, shared_rows, capacity):
+        w, _, h = back_rows.shape
+        tl = slot_of.shape[0]
+        y = torch.empty((tl, h), dtype=torch.float32, device=back_rows.device)
+        _lib.check(_lib.lib().chronos_b200_ep_combine(back_rows.data_ptr(), _DTYPES[back_rows.dtype], slot_of.data_ptr(),
+                                                    shared_rows.data_ptr() if shared_rows is not None else None, tl, h, w, capacity,
+                                                    y.data_ptr(), _lib.DTYPE_F32, torch.cuda.current_stream().cuda_stream))
+        return y
+
+    def overflowed(self) -> bool:
+        """True when a dispatch block of ANY layer on this rank's device overflowed since the last call (the layers share
+        one device flag; reading it synchronises, so call it once per step, not per layer)."""
+        hit = False
+        for flag in _OVERFLOW_FLAGS.values():
+            if int(flag.item()):
+                hit = True
+                flag.zero_()
+        return hit
+
+    # -- the layer ------------------------------------------------------------------------------------------------------
     @torch.no_grad()
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
         """x_local [Tl, H] (same Tl on every rank) -> y_local fp32 [Tl, H]."""
         tl, h = x_local.shape
-        k = self.cfg.top_k
-        # ---- dispatch: gather rows and routing lists of all ranks (fixed-size blocks, no host-side sizes). The token rows
-        # do not depend on the routing, so their exchange is issued first and runs (on the collective's own stream) while
-        # the router kernels run on this one; the current stream waits for it only before the expert pass. -----------------
-        x_all = torch.empty((self.world * tl, h), dtype=x_local.dtype, device=x_local.device)
-        with self._mark("dispatch_rows_issue"):
-            rows = dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group, async_op=True)
+        x_local = x_local.contiguous()
+        capacity = block_capacity(tl, self.world, self.cfg.top_k, self.capacity_factor)
+        self.check_geometry(tl, h, capacity)
         with self._mark("route"):
             ids, gates = self.route_fn(x_local)
+        if self.world == 1 and self.layer is not None:  # every expert is local: nothing to exchange
+            with self._mark("routed_experts"):
+                return self.layer.routed_forward(x_local, ids, gates, with_shared=self.layer.n_shared_experts > 0, out_dtype=torch.float32)
         with self._mark("dispatch"):
-            meta_local = torch.cat([ids.to(torch.float32), gates.to(torch.float32)], dim=1).contiguous()  # ids < 2^24: exact
-            meta_all = torch.empty((self.world * tl, 2 * k), dtype=torch.float32, device=x_local.device)
-            dist.all_gather_into_tensor(meta_all, meta_local, group=self.group)
-            ids_all = meta_all[:, :k].to(torch.int64)
-            gates_all = meta_all[:, k:].contiguous()
-            local_ids = localize_routing(ids_all, self.first_expert, self.n_local)
-            if rows is not None:
-                rows.wait()  # stream-ordered: no host synchronisation
-        # ---- compute: only entries this rank owns ---------------------------------------------------------------------
+            send_rows, send_meta, slot_of = self.pack_fn(x_local, ids, gates, capacity)
+            # received rows and, behind them, the home tokens' own rows (they take the shared expert in the same pass)
+            recv_all = torch.empty((self.world * capacity + tl, h), dtype=x_local.dtype, device=x_local.device)
+            recv_rows = recv_all[:self.world * capacity].view(self.world, capacity, h)
+            recv_all[self.world * capacity:].copy_(x_local)
+            recv_meta = torch.empty_like(send_meta)
+            dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+            dist.all_to_all_single(recv_rows, send_rows, group=self.group)
         with self._mark("routed_experts"):
-            part = self.compute_routed(x_all, local_ids, gates_all)
-        # ---- combine: partial sums back to the home ranks -------------------------------------------------------------
+            part, shared_rows = self.compute_fn(recv_rows, recv_meta, x_local, capacity, recv_all=recv_all)
         with self._mark("combine"):
-            y = torch.empty((tl, h), dtype=torch.float32, device=x_local.device)
-            dist.reduce_scatter_tensor(y, part.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
-        if not self.fused_shared:
-            with self._mark("shared_expert"):
-                sh = self.compute_shared(x_local)
-                if sh is not None:
-                    y += sh
+            back = torch.empty_like(part)
+            dist.all_to_all_single(back, part.contiguous(), group=self.group)
+            y = self.combine_fn(back, slot_of, shared_rows, capacity)
         return y
 
     __call__ = forward
@@ -139,8 +219,7 @@ class _Phase:
         return False
 
 
-def build_local_layer(cfg_global: FoldedLayerConfig, seed: int, world: int, rank: int, device, with_shared: bool,
-                      shared_from: Optional[FoldedMoELayer] = None) -> FoldedMoELayer:
+def build_local_layer(cfg_global: FoldedLayerConfig, seed: int, world: int, rank: int, device, with_shared: bool) -> FoldedMoELayer:
     """Synthetic layer holding only this rank's slots (seeded per slot so that every world size sees the same bytes
     for a given slot), with the full router table replicated."""
     slots = slot_range(cfg_global.n_slots, world, rank)
@@ -165,5 +244,9 @@ class ExpertParallelStack:
             y = lay(x).to(h_local.dtype)
         residual_rmsnorm(h_local, y, None, self.eps)           # last residual add
         return h_local
+
+    def overflowed(self) -> bool:
+        """True when any layer's dispatch overflowed since the last call (synchronises once)."""
+        return bool(self.layers) and self.layers[0].overflowed()
 
     __call__ = forward

@@ -9,7 +9,35 @@ import torch
 import torch.distributed as dist
 
 from . import FoldedLayerConfig
-from .ep import ExpertParallelMoE, ExpertParallelStack, build_local_layer
+from .ep import ExpertParallelMoE, ExpertParallelStack, block_capacity, build_local_layer
+from .layout import PackedLayer
+
+
+def layer_parity(cfg, lay, seed: int, x, y, ids, gates, dev, n_sample: int = 8) -> dict:
+    """Layer output of the expert-parallel path against the CPU oracle for a sample of this rank's home tokens. The rank
+    holds only its own slots, but every slot of the synthetic layer is drawn from a generator seeded by (layer seed,
+    slot), so the slots the sampled tokens touch on OTHER ranks are regenerated here for the check."""
+    import numpy as np
+
+    from oracle import folded_moe_oracle as O  # checker only
+
+    sel = torch.linspace(0, x.shape[0] - 1, n_sample).long().to(dev)
+    ids_s, gates_s = ids[sel].cpu().numpy(), gates[sel].cpu().numpy()
+    groups = {}
+    for g in sorted({int(e) // cfg.group_size for e in ids_s.reshape(-1) if e >= 0}):
+        one = PackedLayer.synthetic_sharded(cfg, seed, range(g, g + 1), dev, False)
+        groups[g] = one.to_groups_numpy()[0][0]
+        del one
+    _, ex = lay.layer.packed.to_groups_numpy()
+    i = cfg.inter
+    shared = (np.concatenate([O.unpack_nvfp4(ex["sh_gu_w"][:i], ex["sh_gu_s"][:i], ex["sh_gu_s2"][0]),
+                              O.unpack_nvfp4(ex["sh_gu_w"][i:], ex["sh_gu_s"][i:], ex["sh_gu_s2"][1])]),
+              O.unpack_nvfp4(ex["sh_dn_w"], ex["sh_dn_s"], ex["sh_dn_s2"][0]))
+    ref = O.routed_tokens_activation_space(x[sel].float().cpu().numpy(), ids_s, gates_s, groups, cfg.hidden, cfg.inter, cfg.group_size, shared=shared)
+    got = y[sel].float().cpu().numpy()
+    ref_ids, _ = O.router_softmax_topk(O.router_logits_fixed(x[sel].float().cpu().numpy(), ex["router_w"]), cfg.top_k)
+    return {"rel_l2": float(np.linalg.norm(got - ref) / np.linalg.norm(ref)), "tokens": int(n_sample), "against": "oracle",
+            "router_ids_equal": bool(np.array_equal(ids_s, ref_ids)), "layer": 0, "tolerance": 1e-2}
 
 
 def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> dict:
@@ -50,6 +78,7 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         status = max(l.layer.device_status() for l in layers[-1:])
+        overflow = stack.overflowed()  # a dispatch block too small for the routing would have dropped tokens: the run is void then
         # end to end: pinned host tokens -> device -> stack -> pinned host result
         host_in = h0.cpu().pin_memory()
         host_out = torch.empty_like(host_in).pin_memory()
@@ -81,8 +110,10 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         import ctypes
 
         from . import _lib
+        from .moe import residual_rmsnorm
         lay0 = layers[0]
-        ids0, _ = lay0.route_fn(h0)
+        x0 = residual_rmsnorm(h0.clone(), None, None, 1e-6)  # what layer 0 sees in the stack
+        ids0, gates0 = lay0.route_fn(x0)
         ids_all = torch.empty((world * tl, cfg.top_k), dtype=ids0.dtype, device=dev)
         dist.all_gather_into_tensor(ids_all, ids0.contiguous())
         owned = int(((ids_all >= lay0.first_expert) & (ids_all < lay0.first_expert + lay0.n_local)).sum().item())
@@ -92,19 +123,20 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         torch.cuda.synchronize()
         arr = (ctypes.c_void_p * 8)(*[ev.cuda_event for ev in evs])
         _lib.check(_lib.lib().chronos_b200_set_stage_events(arr, 8))
-        lay0(h0)
+        y0 = lay0(x0)
         _lib.check(_lib.lib().chronos_b200_set_stage_events(None, 0))
         torch.cuda.synchronize()
         gemm_ms = evs[3].elapsed_time(evs[4]) + evs[5].elapsed_time(evs[6])
+        parity = layer_parity(cfg, lay0, 3, x0, y0, ids0, gates0, dev) if rank == 0 else None
         step_s = float(ms.item()) * 1e-3 / K
         pairs = tokens * cfg.top_k
         bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
         healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
         useful = n_layers * (pairs * (bank_flops + healer_flops) + tokens * bank_flops)
-        # this library's kernels per layer: rmsnorm, router (2), then twice (routed entries of all tokens; shared expert of
-        # the local tokens) token_scale, plan, input transform, healer in, bank pass, SwiGLU/transform, healer in, bank
-        # pass, output term, gate-weighted sum
-        launches_per_layer = 1 + 2 + 2 * 11
+        # this library's kernels per layer: rmsnorm, router (2), dispatch pack (2), metadata unpack, then one pass over the
+        # received rows + home tokens (token_scale, plan, fp16 rows, input transform, healer in, bank pass, SwiGLU/transform,
+        # healer in, bank pass, output term, gate-weighted sum), combine
+        launches_per_layer = 1 + 2 + (3 if world > 1 else 0) + 11 + (1 if world > 1 else 0)
         return {
             "metric": "folded_moe_ep_stack_tokens_per_s", "value": tokens / step_s, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": float(ms.item()) / K, "higher_is_better": True, "scaling": "strong",
@@ -125,6 +157,9 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
                          "unit": "TFLOP/s", "frac": (owned + tl) * bank_flops / (gemm_ms * 1e-3) / 1e12 / 9000.0, "traffic": None,
                          "pairs_on_rank0": owned + tl, "bank_pass_ms": gemm_ms},
             "phase_us_per_layer_rank0": {k_: round(v, 1) for k_, v in phase_us.items()},
+            "dispatch": {"kind": "deduplicated all-to-all, fixed-capacity blocks" if world > 1 else "none (one rank)",
+                         "block_capacity_rows": block_capacity(tl, world, cfg.top_k), "tokens_per_rank": tl, "overflowed": overflow},
+            "parity": parity,
             "device_status": status,
         }
     finally:

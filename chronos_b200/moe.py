@@ -83,6 +83,7 @@ class FoldedMoELayer(nn.Module):
         self.n_redundant_experts = 0
         self.experts = _DummyExperts()
         self.is_sequence_parallel = False
+        self.activation_terms = 3  # residual FP4 terms per activation in the block-scaled tensor-core regimes
         self._ws: torch.Tensor | None = None
         self._ws_need: dict[int, int] = {}
         self._last_n = 0

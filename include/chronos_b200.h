@@ -193,6 +193,35 @@ int chronos_b200_folded_moe_routed(const chronos_layer_t* layer, const void* x, 
 int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, void* x_norm, int dtype, int n_tokens,
                                   int hidden, float eps, void* stream);
 
+/* Expert-parallel dispatch, device side (one process per GPU; experts sharded by slot, rank d owns experts
+ * [d * experts_per_rank, (d + 1) * experts_per_rank)).  Fills, for every destination rank d, a fixed-capacity block:
+ *   send_rows [world, capacity, hidden]  (x's dtype) the hidden rows of the local tokens that route >= 1 expert to d, each
+ *             token ONCE per destination, in token order;
+ *   send_meta i32 [world, capacity + 1, 2 * top_k + 2]: row p < capacity = (source token, top_k expert ids local to d or
+ *             -1, top_k gates as fp32 bits, pad); row `capacity`, word 0 = rows used in the block;
+ *   slot_of  i32 [n_tokens, world]: position of token t in d's block, or -1.
+ * ids are GLOBAL expert ids [n_tokens, top_k] (< 0 skipped), gates f32.  A token that does not fit (more than
+ * `capacity` tokens for one destination) is left out and *overflow (device int32, caller-cleared) is raised: the
+ * caller checks it at the end of the step and repeats the step with capacity = n_tokens, which always fits.
+ * The blocks are then exchanged by a collective with equal splits (NCCL all-to-all in the shipped host layer).
+ * No counterpart in the reference (single device; chronos_1t/docs/CHRONOS_ARCHITECTURE_PAPER.md:244 only names the idea). */
+int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                         int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
+                         int32_t* overflow, void* stream);
+
+/* Received metadata blocks [world, capacity + 1, 2 * top_k + 2] -> the routing lists of the received rows:
+ * ids_out i32 [world * capacity, top_k] (local expert ids; -1 for unused rows and entries), gates_out f32 likewise.
+ * No counterpart in the reference. */
+int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out,
+                                void* stream);
+
+/* Expert-parallel combine on the home rank: y[t] = extra[t] + sum over ranks d = 0 .. world - 1 (in that order) of
+ * back_rows[d, slot_of[t, d]] where slot_of >= 0.  back_rows [world, capacity, hidden] are the partial-sum rows the
+ * peers returned (bf16 or f32), extra [n_tokens, hidden] (same dtype, or NULL) e.g. the shared expert's rows.
+ * No counterpart in the reference. */
+int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden,
+                            int world, int capacity, void* y, int y_dtype, void* stream);
+
 /* Operand-format probe of the block-scaled FP4 tensor-core path (tcgen05.mma kind::mxf4nvf4, e2m1 operands with a
  * ue4m3 scale per 16 elements): d_out f32 [128, b_rows] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns;
  * b_rows a multiple of 16 in 16..256 (32 = streaming regime, 192 = tensor regime).
