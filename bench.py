@@ -293,6 +293,26 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
     ms_e2e = e0.elapsed_time(e1)
     clocks = sampler.stop() if own_sampler else None
 
+    # ---- the same batches with the batch-coalesced routing policy (drafts prefer experts their stream's anchor selected) ----
+    coalesced = None
+    if not args.tail:
+        pool, keep = 12, 4
+        routed = [layer.route_coalesced(b, tokens_per_stream=TOKENS_PER_STREAM, pool=pool, keep=keep) for b in batches]
+        c_slots = [len({int(e) // cfg.group_size for e in ids.reshape(-1).tolist()}) for ids, _ in routed]
+        for i in range(W):
+            layer.routed_forward(batches[i % N_BATCHES], *layer.route_coalesced(batches[i % N_BATCHES], TOKENS_PER_STREAM, pool, keep), with_shared=True)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for i in range(K):
+            b = batches[i % N_BATCHES]
+            layer.routed_forward(b, *layer.route_coalesced(b, TOKENS_PER_STREAM, pool, keep), with_shared=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+        coalesced = {"pool": pool, "keep": keep, "distinct_slots_per_step": statistics.mean(c_slots),
+                     "distinct_slots_natural": statistics.mean(s["slots"] for s in stats),
+                     "ms_per_step": e0.elapsed_time(e1) / K, "tokens_per_s": n_tok / (e0.elapsed_time(e1) * 1e-3 / K),
+                     "note": "router + coalescing selection as separate launches, then the routed entry point"}
+
     peak, peak_kind = _peaks()
     gu_gbs = gu_bytes / (stage_us["gu_bank_pass"] * 1e-6) / 1e9
     dn_gbs = dn_bytes / (stage_us["dn_bank_pass"] * 1e-6) / 1e9
@@ -325,6 +345,7 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
                       "frac_of_peak": layer_bytes / step_s / 1e9 / peak, "frac_of_8tbs": layer_bytes / step_s / 8e12},
         "stages_us": {k: round(v, 2) for k, v in stage_us.items()},
         "dn_bank_pass_gbs": dn_gbs,
+        "coalesced_routing": coalesced,
     }
     if with_cpu_baseline and not args.no_cpu_baseline:
         threads = host_threads()

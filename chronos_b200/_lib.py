@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX, ROUTER_SQRT_SOFTPLUS = 0, 1, 2
-ABI_VERSION = 8
+ABI_VERSION = 10
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4, REGIME_TENSOR_FP4 = 0, 1, 2, 3, 4
 
 
@@ -34,7 +34,8 @@ class LayerStruct(C.Structure):
             "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout", "dn_rs2",
             "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
             "gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn",
-            "tail_gu_p", "tail_gu_s", "tail_dn_p", "tail_dn_s")]
+            "tail_gu_p", "tail_gu_s", "tail_dn_p", "tail_dn_s",
+            "sh8_gu_w", "sh8_gu_s", "sh8_dn_w", "sh8_dn_s")]
     )
 
 
@@ -42,9 +43,12 @@ EXPORTS = {
     "chronos_b200_abi_version": (C.c_int, []),
     "chronos_b200_last_error": (C.c_char_p, []),
     "chronos_b200_dequant_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "chronos_b200_dequant_fp8_block": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "chronos_b200_unfold_expert_fp32": (C.c_int, [C.POINTER(LayerStruct), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_unfold_expert_fp32_static": (C.c_int, [C.POINTER(LayerStruct), C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "chronos_b200_router_topk": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "chronos_b200_router_topk_coalesced": (C.c_int, [C.POINTER(LayerStruct), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_workspace_bytes": (C.c_size_t, [C.POINTER(LayerStruct), C.c_int]),
     "chronos_b200_fp4_mma_probe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_ep_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

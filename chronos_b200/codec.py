@@ -65,6 +65,6 @@ def reconstruct_group_experts(g: Mapping[str, torch.Tensor], g_idx: int, members
     # a one-slot layer whose slot index is g_idx: place the slot at position g_idx of an otherwise empty table
     cfg = FoldedLayerConfig(hidden=hidden, inter=inter, n_experts=k * (g_idx + 1), group_size=k, rank=rank, top_k=1)
     groups = [g] * (g_idx + 1)
-    layer = PackedLayer.from_groups(cfg, groups, device=device, include_tail=include_tail)
+    layer = PackedLayer.from_groups(cfg, groups, device=device, include_tail=include_tail, keep_disk_order=True)
     rec = reconstruct_experts(layer, [g_idx * k + m for m in members])
     return [(a.to(dtype), b.to(dtype)) for a, b in rec]

@@ -107,8 +107,12 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
     const char* names[] = {"gu_w", "gu_s", "gu_s2", "gu_beta", "dn_w", "dn_s", "dn_s2", "dn_beta", "u_gu", "v_gu",
                            "u_dn", "v_dn_t", "gu_cin", "gu_cs2", "gu_rout", "gu_rs2", "dn_cin", "dn_cs2", "dn_rout",
                            "dn_rs2"};
+    // a layer may hold its banks as re-tiled stage images only (gu_t / dn_t): the on-disk-order copies are then optional
+    const bool images_only = L->gu_t != nullptr && L->dn_t != nullptr && aligned16(L->gu_t) && aligned16(L->dn_t);
     for (size_t i = 0; i < sizeof(need) / sizeof(need[0]); ++i) {
         const bool scalar_table = (i == 2 || i == 3 || i == 6 || i == 7);
+        const bool bank_bytes = (i == 0 || i == 1 || i == 4 || i == 5);
+        if (bank_bytes && need[i] == nullptr && images_only) continue;
         if (need[i] == nullptr || (!scalar_table && !aligned16(need[i]))) {
             set_error("layer.%s is NULL or not 16-byte aligned", names[i]);
             return CHRONOS_E_ALIGN;
@@ -125,10 +129,16 @@ static int validate_layer(const chronos_layer_t* L, bool need_router) {
             if (!aligned16(q)) { set_error("a tail-lattice pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
     }
     if (need_router && !aligned16(L->router_w)) { set_error("layer.router_w is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
-    if (L->shared_inter > 0) {
+    if (shared_is_fp8(*L)) {
+        if (!aligned16(L->sh8_gu_w) || !aligned16(L->sh8_dn_w) || !L->sh8_gu_s || !L->sh8_dn_s) {
+            set_error("a block-FP8 shared-expert pointer is NULL or not 16-byte aligned");
+            return CHRONOS_E_ALIGN;
+        }
+    } else if (L->shared_inter > 0) {
         const void* sh[] = {L->sh_gu_w, L->sh_gu_s, L->sh_dn_w, L->sh_dn_s};
+        const bool sh_images_only = aligned16(L->sh_gu_t) && aligned16(L->sh_dn_t);
         for (const void* q : sh)
-            if (!aligned16(q)) { set_error("a shared-expert bank pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
+            if (!aligned16(q) && !(q == nullptr && sh_images_only)) { set_error("a shared-expert bank pointer is NULL or not 16-byte aligned"); return CHRONOS_E_ALIGN; }
         if (!L->sh_gu_s2 || !L->sh_dn_s2) { set_error("a shared-expert scale_2 pointer is NULL"); return CHRONOS_E_ALIGN; }
     }
     return CHRONOS_OK;
@@ -185,7 +195,7 @@ static int fused_decode_forward(const chronos_layer_t& L, const void* x, int x_d
                                 cudaStream_t st) {
     Plan p = plan;
     p.gitem_pairs = 8;
-    const int with_shared = (shared_count > 0 && L.shared_inter > 0) ? 1 : 0;
+    const int with_shared = (shared_count > 0 && shared_is_nvfp4(L)) ? 1 : 0;
     p.shared_lo = with_shared ? shared_first : 0;
     p.shared_n = with_shared ? shared_count : 0;
     // counters, status word and the grid hand-off counter start at zero (a memset node, no allocation)
@@ -202,7 +212,8 @@ static int fused_decode_forward(const chronos_layer_t& L, const void* x, int x_d
     stage_mark(5, st);
     if (int rc = launch_bank_fp4_fused(L, 1, p, x, x_dtype, st)) return rc;
     stage_mark(6, st);
-    const int rc = launch_decode_combine(L, p, ids_in != nullptr ? gates_in : p.gates, n_tokens, with_shared, y, y_dtype, st);
+    int rc = launch_decode_combine(L, p, ids_in != nullptr ? gates_in : p.gates, n_tokens, with_shared, y, y_dtype, st);
+    if (!rc && shared_is_fp8(L)) rc = launch_shared_fp8(L, x, x_dtype, p, shared_first, shared_count, y, y_dtype, st);
     stage_mark(7, st);
     return rc;
 }
@@ -211,12 +222,18 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
                           const float* gates, int shared_first, int shared_count, void* y, int y_dtype, const Plan& plan,
                           int regime, bool have_tok_scale, const TopkArgs& tk, cudaStream_t st) {
     const int reg = pick_regime(L, n_tokens, regime, plan);
+    if ((reg == CHRONOS_REGIME_STREAM || reg == CHRONOS_REGIME_TENSOR) &&
+        (L.gu_w == nullptr || L.dn_w == nullptr || (shared_is_nvfp4(L) && L.sh_gu_w == nullptr))) {
+        set_error("regime %d reads the banks in their on-disk order, but this layer holds them as FP4 stage images only "
+                  "(load it with the on-disk-order copy kept, or use an FP4 regime)", reg);
+        return CHRONOS_E_ARG;
+    }
     const bool wide = reg == CHRONOS_REGIME_TENSOR_FP4;
     const bool tensor = reg == CHRONOS_REGIME_TENSOR || wide;
     const int fp4 = wide ? 2 : (reg == CHRONOS_REGIME_STREAM_FP4 ? 1 : 0);
     Plan p = plan;
     p.gitem_pairs = wide ? kPairsPerWideItem : kPairsPerGemmItem;
-    const int with_shared = (shared_count > 0 && L.shared_inter > 0) ? 1 : 0;
+    const int with_shared = (shared_count > 0 && shared_is_nvfp4(L)) ? 1 : 0;
     p.shared_lo = with_shared ? shared_first : 0;
     p.shared_n = with_shared ? shared_count : 0;
     stage_mark(1, st);
@@ -256,6 +273,7 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
         rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)
                   : launch_combine(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     }
+    if (!rc && shared_is_fp8(L)) rc = launch_shared_fp8(L, x, x_dtype, p, shared_first, shared_count, y, y_dtype, st);
     stage_mark(7, st);
     return rc;
 }
@@ -266,7 +284,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 8; }
+int chronos_b200_abi_version(void) { return 10; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 
@@ -277,11 +295,18 @@ int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, cons
     return launch_dequant(packed, scale, scale_2, out, rows, cols, (cudaStream_t)stream);
 }
 
+int chronos_b200_dequant_fp8_block(const uint8_t* w, const float* scale_inv, float* out, int rows, int cols, void* stream) {
+    if (rows <= 0 || cols <= 0) { set_error("dequant_fp8_block: rows (%d) and cols (%d) must be positive", rows, cols); return CHRONOS_E_SHAPE; }
+    if (!w || !scale_inv || !out) { set_error("dequant_fp8_block: NULL pointer"); return CHRONOS_E_ALIGN; }
+    return launch_dequant_fp8_block(w, scale_inv, out, rows, cols, (cudaStream_t)stream);
+}
+
 int chronos_b200_unfold_expert_fp32(const chronos_layer_t* layer, int expert, int which, float* out, float* scratch,
                                     void* stream) {
     if (int rc = validate_layer(layer, false)) return rc;
     if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
     if (!out || !scratch) { set_error("unfold: out or scratch is NULL"); return CHRONOS_E_ALIGN; }
+    if (!layer->gu_w || !layer->dn_w) { set_error("unfold: the layer holds no on-disk-order banks (FP4 stage images only)"); return CHRONOS_E_ARG; }
     if (int rc = launch_unfold(*layer, expert, which, out, scratch, (cudaStream_t)stream)) return rc;
     return layer->tail_bits ? launch_tail_add(*layer, expert, which, out, (cudaStream_t)stream) : CHRONOS_OK;
 }
@@ -290,6 +315,7 @@ int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int exp
     if (int rc = validate_layer(layer, false)) return rc;
     if (expert < 0 || expert >= layer->n_experts || (which != 0 && which != 1)) { set_error("unfold_static: expert %d / which %d out of range", expert, which); return CHRONOS_E_ARG; }
     if (!out) { set_error("unfold_static: out is NULL"); return CHRONOS_E_ALIGN; }
+    if (!layer->gu_w || !layer->dn_w) { set_error("unfold_static: the layer holds no on-disk-order banks (FP4 stage images only)"); return CHRONOS_E_ARG; }
     if (int rc = launch_unfold_static(*layer, expert, which, out, (cudaStream_t)stream)) return rc;
     return layer->tail_bits ? launch_tail_add(*layer, expert, which, out, (cudaStream_t)stream) : CHRONOS_OK;
 }
@@ -300,6 +326,22 @@ int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_
     if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
     if (!ids || !gates || !logits) { set_error("router: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
     return launch_router(*layer, x, x_dtype, n_tokens, ids, gates, logits, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+int chronos_b200_router_topk_coalesced(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int tokens_per_stream,
+                                       int pool, int keep, float bonus, int32_t* ids, float* gates, float* logits, void* stream) {
+    if (int rc = validate_router(layer)) return rc;
+    if (int rc = validate_io(x, x_dtype, n_tokens, x, CHRONOS_DTYPE_F32)) return rc;
+    if (!ids || !gates || !logits) { set_error("router_coalesced: ids, gates or logits is NULL"); return CHRONOS_E_ALIGN; }
+    if (tokens_per_stream < 1 || pool < layer->top_k || pool > 32 || pool > layer->n_experts || keep < 0 || keep > layer->top_k || !(bonus >= 0.0f)) {
+        set_error("router_coalesced: tokens_per_stream (%d) >= 1, top_k <= pool (%d) <= min(32, n_experts), 0 <= keep (%d) <= top_k and bonus >= 0 required",
+                  tokens_per_stream, pool, keep);
+        return CHRONOS_E_ARG;
+    }
+    if (n_tokens == 0) return CHRONOS_OK;
+    // logits exactly as the plain router computes them (ids == NULL: no top-k there), then the coalescing selection
+    if (int rc = launch_router(*layer, x, x_dtype, n_tokens, nullptr, gates, logits, nullptr, nullptr, (cudaStream_t)stream)) return rc;
+    return launch_coalesced_topk(*layer, logits, n_tokens, tokens_per_stream, pool, keep, bonus, ids, gates, (cudaStream_t)stream);
 }
 
 size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens) {

@@ -61,6 +61,9 @@ struct Plan {
     float* heal_dn;        // [P, H]   healer term U_down (V_down act) in natural row order (fused decode path only)
     int32_t* pair_item;    // [P]      streaming work item of sorted pair p (fused decode path only)
     int32_t* pair_pos;     // [P]      position 0..7 of sorted pair p inside its work item
+    float* sh8_z;          // [T, 2I]  block-FP8 shared expert: gate_up outputs (NULL: the layer has no such expert)
+    __half* sh8_act;       // [T, I]   its SwiGLU outputs
+    float* sh8_y;          // [T, H]   its down outputs
     int fp4_stream;        // bq_* are laid out for the FP4 streaming regime ([max_items, K/256, 6144])
     int fp4_wide;          // bq_* are laid out for the FP4 tensor regime ([max_gitems, K/256, 28672])
     int gitem_pairs;       // pairs per tensor-core work item in this call (128 or 64)
@@ -74,24 +77,29 @@ struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
         off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, off_tail_gu, off_tail_dn, off_x16t, off_heal_gu,
-        off_heal_dn, off_pair_item, off_pair_pos, total;
-    int fp4, tiled, wide, tail;
+        off_heal_dn, off_pair_item, off_pair_pos, off_sh8_z, off_sh8_act, off_sh8_y, total;
+    int fp4, tiled, wide, tail, sh8;
     int max_pairs, max_items, max_gitems;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// The always-on expert comes in one of two formats: plain NVFP4 (handled as an extra slot by the bank passes) or the
+// stock block-FP8 format (csrc/shared_fp8.cu, a pass of its own).
+inline bool shared_is_fp8(const chronos_layer_t& L) { return L.shared_inter > 0 && L.sh8_gu_w != nullptr; }
+inline bool shared_is_nvfp4(const chronos_layer_t& L) { return L.shared_inter > 0 && L.sh8_gu_w == nullptr; }
+
 inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     PlanLayout p{};
     const size_t T = (size_t)n_tokens, E = (size_t)L.n_experts, k = (size_t)L.top_k, H = (size_t)L.hidden,
                  I = (size_t)L.inter, r = (size_t)L.rank;
-    const size_t P = T * k + (L.shared_inter > 0 ? T : 0);
+    const size_t P = T * k + (shared_is_nvfp4(L) ? T : 0);
     p.max_pairs = (int)P;
     p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
     // FP4 activation images exist only for batch shapes the streaming regime serves and layers that carry re-tiled banks
     p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
              T * k < 16 * (size_t)L.n_slots &&
-             (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
+             (!shared_is_nvfp4(L) || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr))) ? 1 : 0;
     // per-expert work items: 64 pairs in the FP4 tensor regime (128 in the fp16 one); the fused decode path cuts the
     // same lists into chunks of 8 pairs for its healer products
     p.max_gitems = (int)(E + 1 + P / (p.fp4 ? 8 : kPairsPerWideItem) + 1);
@@ -126,7 +134,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     // the FP4 tensor regime: re-tiled banks, the tensor-core healer path (needs healer.v_down as on disk) and its
     // shared-memory budget (4 staged vectors of 3 I or H floats)
     const bool images = L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 &&
-                        (L.shared_inter == 0 || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr));
+                        (!shared_is_nvfp4(L) || (L.sh_gu_t != nullptr && L.sh_dn_t != nullptr));
     p.wide = (p.tiled && images && L.v_dn != nullptr && kGroupPairs * 3 * I * 4 <= 220 * 1024 && kGroupPairs * H * 4 <= 220 * 1024) ? 1 : 0;
     p.off_bq_gu = take(p.fp4 ? (size_t)p.max_items * (H / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (H / 256) * kWideStageBytes : 0));
     p.off_bq_dn = take(p.fp4 ? (size_t)p.max_items * (I / 256) * 6144 : (p.wide ? (size_t)p.max_gitems * (I / 256) * kWideStageBytes : 0));
@@ -137,6 +145,10 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_heal_dn = take(p.fp4 ? P * H * 4 : 0);
     p.off_pair_item = take(p.fp4 ? P * 4 : 0);
     p.off_pair_pos = take(p.fp4 ? P * 4 : 0);
+    p.sh8 = shared_is_fp8(L) ? 1 : 0;
+    p.off_sh8_z = take(p.sh8 ? T * 2 * I * 4 : 0);
+    p.off_sh8_act = take(p.sh8 ? T * I * 2 : 0);
+    p.off_sh8_y = take(p.sh8 ? T * H * 4 : 0);
     p.tail = L.tail_bits != 0 ? 1 : 0;
     p.off_tail_gu = take(p.tail ? P * 2 * I * 4 : 0);
     p.off_tail_dn = take(p.tail ? P * H * 4 : 0);
@@ -185,6 +197,9 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.heal_dn = l.fp4 ? (float*)(b + l.off_heal_dn) : nullptr;
     p.pair_item = l.fp4 ? (int32_t*)(b + l.off_pair_item) : nullptr;
     p.pair_pos = l.fp4 ? (int32_t*)(b + l.off_pair_pos) : nullptr;
+    p.sh8_z = l.sh8 ? (float*)(b + l.off_sh8_z) : nullptr;
+    p.sh8_act = l.sh8 ? (__half*)(b + l.off_sh8_act) : nullptr;
+    p.sh8_y = l.sh8 ? (float*)(b + l.off_sh8_y) : nullptr;
     p.tail_gu = l.tail ? (float*)(b + l.off_tail_gu) : nullptr;
     p.tail_dn = l.tail ? (float*)(b + l.off_tail_dn) : nullptr;
     if (l.tail && !l.tiled) p.x16 = (__half*)(b + l.off_x16t);
@@ -212,6 +227,8 @@ int launch_unfold(const chronos_layer_t& L, int expert, int which, float* out, f
 int launch_unfold_static(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
                   float* logits, float* tok_scale, int32_t* status, cudaStream_t st);
+int launch_coalesced_topk(const chronos_layer_t& L, const float* logits, int n_tokens, int tps, int pool, int keep, float bonus,
+                          int32_t* ids, float* gates, cudaStream_t st);
 int launch_plan(const chronos_layer_t& L, const int32_t* ids, int n_tokens, int with_shared, int reset_status,
                 const TopkArgs& tk, const Plan& p, cudaStream_t st);
 int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, float* tok_scale, cudaStream_t st);
@@ -253,6 +270,9 @@ int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* 
 int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, cudaStream_t st);
 int launch_ep_combine(const void* back, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
                       int capacity, void* y, int y_dtype, cudaStream_t st);
+int launch_dequant_fp8_block(const uint8_t* w, const float* s, float* out, int rows, int cols, cudaStream_t st);
+int launch_shared_fp8(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int first, int count, void* y, int y_dtype,
+                      cudaStream_t st);
 int launch_wait_probe(int32_t* status, uint32_t poll_limit, cudaStream_t st);
 int launch_fp4_probe(const uint8_t* a_img, const uint8_t* b_img, int n_stages, int b_rows, float* d_out, int32_t* status,
                      cudaStream_t st);

@@ -308,6 +308,133 @@ __global__ void __launch_bounds__(256) router_topk_kernel(TopkArgs tk) {
     topk_one_token(tk, t, threadIdx.x & 31);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Batch-coalesced routing policy for speculative verify batches (streams of `tps` tokens: one anchor + drafts).
+// Only a prose description of the policy exists in the reference (README.md:56, :208, :372 and
+// docs/CHRONOS_ARCHITECTURE_PAPER.md:270-277; its kernel lives in another repository), so this is a clean-room design
+// that keeps the stated invariants:
+//   * the anchor (token 0 of a stream) gets its natural top-k, untouched;
+//   * a draft token only ever picks from its own natural top-`pool` candidates (pool >= k);
+//   * its `keep` best natural experts are always kept, in natural order;
+//   * the remaining k - keep picks go to the candidates ranked by (choice score + bonus if the anchor selected the
+//     expert too), ties to the better natural rank - so experts whose bank the anchor already streams are preferred;
+//   * pool == k (or bonus == 0) gives natural routing; gate weights come from the unbiased scores of what was picked.
+// One CTA per stream: warp 0 routes the anchor, then one warp per draft.
+// ---------------------------------------------------------------------------------------------------------------
+template <int PL>
+__device__ __forceinline__ void natural_ranking(const TopkArgs& a, int t, int lane, int n_rounds, int& my_id, float& my_choice) {
+    float choice[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = i * 32 + lane;
+        float c = -INFINITY;
+        if (e < a.n_experts) {
+            c = router_choice(a, a.logits[(size_t)t * a.n_experts + e], e);
+            if (!(c == c)) c = -INFINITY;
+        }
+        choice[i] = c;
+    }
+    my_id = -1;
+    my_choice = -INFINITY;
+    for (int j = 0; j < n_rounds; ++j) {  // lane j keeps the j-th best candidate
+        float best = -INFINITY;
+        int best_e = kNoExpert;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+            const int e = i * 32 + lane;
+            if (e < a.n_experts && choice[i] > best) { best = choice[i]; best_e = e; }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+            const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
+            if (ov > best || (ov == best && oe < best_e)) { best = ov; best_e = oe; }
+        }
+        const bool found = best_e != kNoExpert;
+#pragma unroll
+        for (int i = 0; i < PL; ++i)
+            if (found && i * 32 + lane == best_e) choice[i] = -INFINITY;
+        if (lane == j && found) { my_id = best_e; my_choice = best; }
+    }
+}
+
+__device__ __forceinline__ void write_gates(const TopkArgs& a, int t, int lane, int my_id) {
+    // lane j < top_k holds the j-th selected expert (or -1); gate weights per flavour from the unbiased scores
+    const bool have = lane < a.top_k && my_id >= 0;
+    float my_val = 0.0f;
+    if (have) my_val = router_weight_source(a, a.logits[(size_t)t * a.n_experts + my_id]);
+    float gate;
+    if (a.kind != CHRONOS_ROUTER_SOFTMAX_TOPK) {
+        const float sv = have ? my_val : 0.0f;
+        float tot = 0.0f;
+        for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, sv, j);
+        gate = (a.renorm ? my_val / (tot + 1e-20f) : my_val) * a.scaling;
+    } else {
+        float mx = have ? my_val : -INFINITY;  // the picks of a draft are not sorted by logit: take the maximum explicitly
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const float ex = have ? expf(my_val - mx) : 0.0f;
+        float tot = 0.0f;
+        for (int j = 0; j < a.top_k; ++j) tot += __shfl_sync(0xffffffffu, ex, j);
+        gate = ex / tot;
+    }
+    if (lane < a.top_k) {
+        a.ids[(size_t)t * a.top_k + lane] = my_id;
+        a.gates[(size_t)t * a.top_k + lane] = have ? gate : 0.0f;
+    }
+}
+
+template <int PL>
+__global__ void __launch_bounds__(256) coalesced_topk_kernel(TopkArgs a, int tps, int pool, int keep, float bonus) {
+    __shared__ int anchor_ids[kMaxTopK];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5;
+    const int t0 = blockIdx.x * tps;
+    if (warp == 0) {
+        int id;
+        float c;
+        natural_ranking<PL>(a, t0, lane, a.top_k, id, c);
+        if (lane < a.top_k) anchor_ids[lane] = id;
+        write_gates(a, t0, lane, id);
+    }
+    __syncthreads();
+    for (int m = 1 + warp; m < tps; m += n_warps) {
+        const int t = t0 + m;
+        if (t >= a.n_tokens) break;
+        int id;
+        float c;
+        natural_ranking<PL>(a, t, lane, pool, id, c);  // lane j: j-th natural candidate
+        bool shared_with_anchor = false;
+        for (int j = 0; j < a.top_k; ++j) shared_with_anchor |= (id >= 0 && anchor_ids[j] == id);
+        const bool cand = lane >= keep && lane < pool && id >= 0;
+        const float sc = cand ? c + (shared_with_anchor ? bonus : 0.0f) : -INFINITY;
+        int rank = 0;  // candidates that come before this lane's
+        for (int j = 0; j < 32; ++j) {
+            const float oj = __shfl_sync(0xffffffffu, sc, j);
+            rank += (oj > sc) || (oj == sc && j < lane);
+        }
+        // output position: kept candidates stay where they are, the others go by rank behind them
+        const int out_pos = lane < keep ? lane : (cand ? keep + rank : 32);
+        int sel_id = -1;
+        for (int j = 0; j < 32; ++j) {  // lane p takes the id of the lane whose output position is p
+            const int pj = __shfl_sync(0xffffffffu, out_pos, j);
+            const int ij = __shfl_sync(0xffffffffu, id, j);
+            if (pj == lane) sel_id = ij;
+        }
+        write_gates(a, t, lane, lane < a.top_k ? sel_id : -1);
+    }
+}
+
+int launch_coalesced_topk(const chronos_layer_t& L, const float* logits, int n_tokens, int tps, int pool, int keep, float bonus,
+                          int32_t* ids, float* gates, cudaStream_t st) {
+    TopkArgs tk{logits, L.e_bias, L.router_kind, L.renorm, L.routed_scaling, n_tokens, L.n_experts, L.top_k, ids, gates};
+    const unsigned grid = (unsigned)((n_tokens + tps - 1) / tps);
+    const int threads = 32 * (tps < 8 ? tps : 8);
+    if (L.n_experts <= 256) coalesced_topk_kernel<8><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
+    else if (L.n_experts <= 512) coalesced_topk_kernel<16><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
+    else coalesced_topk_kernel<32><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
+    return check_launch("coalesced_topk");
+}
+
 int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, int32_t* ids, float* gates,
                   float* logits, float* tok_scale, int32_t* status, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;

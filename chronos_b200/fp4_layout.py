@@ -35,3 +35,20 @@ def tile_matrix_fp4(packed: torch.Tensor, scales: torch.Tensor, tile_rows: int) 
     sf = sf.permute(*range(nd), nd, nd + 4, nd + 5, nd + 1, nd + 3, nd + 2, nd + 6)  # [.., rb, st, j, blk, r0, r1, s]
     sf = sf.reshape(*lead, rb, ns, 2048 * nblk)
     return torch.cat([nib, sf], dim=-1).contiguous()
+
+
+def untile_matrix_fp4(image: torch.Tensor, tile_rows: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of `tile_matrix_fp4` for tile_rows a multiple of 128: u8 [..., rows/tile_rows, K/256, tile_rows*128 + 2048*nblk]
+    -> (packed u8 [..., rows, K/2], scales u8 [..., rows, K/16]), the on-disk row-major bytes."""
+    *lead, rb, ns, stage = image.shape
+    nblk = tile_rows // 128
+    if tile_rows % 128 or stage != tile_rows * 128 + 2048 * nblk:
+        raise ValueError("not a stage image of tile_rows rows")
+    nd = len(lead)
+    nib = image[..., : tile_rows * 128].reshape(*lead, rb, ns, 8, tile_rows, 16)          # [.., rb, st, c, r, b]
+    nib = nib.permute(*range(nd), nd, nd + 3, nd + 1, nd + 2, nd + 4)                      # [.., rb, r, st, c, b]
+    packed = nib.reshape(*lead, rb * tile_rows, ns * 128).contiguous()
+    sf = image[..., tile_rows * 128:].reshape(*lead, rb, ns, 4, nblk, 32, 4, 4)           # [.., rb, st, j, blk, r0, r1, s]
+    sf = sf.permute(*range(nd), nd, nd + 3, nd + 5, nd + 4, nd + 1, nd + 2, nd + 6)        # [.., rb, blk, r1, r0, st, j, s]
+    scales = sf.reshape(*lead, rb * tile_rows, ns * 16).contiguous()
+    return packed, scales

@@ -131,9 +131,13 @@ class PackedLayer:
     """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
 
     def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device,
-                 fp4_images: bool = True, tail_bits: tuple[int, int] = (0, 0)):
+                 fp4_images: bool = True, tail_bits: tuple[int, int] = (0, 0), keep_disk_order: bool = False):
+        """`keep_disk_order`: keep the banks in their on-disk row-major order beside the re-tiled stage images. The FP4
+        regimes read only the images, so by default the on-disk-order copy is released once the images exist (a layer is
+        then resident once, not twice); the reconstruction probes and the forced "stream" / "tensor" regimes need it."""
         cfg.validate()
         self.cfg = cfg
+        self.keep_disk_order = keep_disk_order
         self.tail_bits = tuple(tail_bits) if "tail_gu_p" in tensors else (0, 0)
         self.fp4_images = fp4_images
         self.device = _norm_device(device)
@@ -145,7 +149,7 @@ class PackedLayer:
         s.router_kind = ROUTER_KINDS[cfg.router]
         s.renorm = int(cfg.norm_topk_prob)
         s.routed_scaling = float(cfg.routed_scaling_factor)
-        s.shared_inter = cfg.inter if "sh_gu_w" in tensors else 0
+        s.shared_inter = cfg.inter if ("sh_gu_w" in tensors or "sh_gu_t" in tensors or "sh8_gu_w" in tensors) else 0
         s.tail_bits = self.tail_bits[0] | (self.tail_bits[1] << 8)
         self._add_fp4_images()
         if "v_dn" not in tensors and "v_dn_t" in tensors and self.device.type == "cuda":
@@ -173,11 +177,22 @@ class PackedLayer:
         c, t = self.cfg, self.t
         if c.hidden % 256 or c.inter % 256 or self.device.type != "cuda" or not self.fp4_images or "gu_t" in t:
             return
-        t["gu_t"] = tile_matrix_fp4(t["gu_w"], t["gu_s"], 128)
-        t["dn_t"] = tile_matrix_fp4(t["dn_w"], t["dn_s"], 128)
+        # slot by slot, so that the transient of the byte permutation stays one slot large
+        t["gu_t"] = torch.stack([tile_matrix_fp4(t["gu_w"][g], t["gu_s"][g], 128) for g in range(c.n_slots)])
+        t["dn_t"] = torch.stack([tile_matrix_fp4(t["dn_w"][g], t["dn_s"][g], 128) for g in range(c.n_slots)])
         if "sh_gu_w" in t:
             t["sh_gu_t"] = tile_matrix_fp4(t["sh_gu_w"], t["sh_gu_s"], 128)
             t["sh_dn_t"] = tile_matrix_fp4(t["sh_dn_w"], t["sh_dn_s"], 128)
+        if not self.keep_disk_order and self.fp4_only_ok():
+            for name in ("gu_w", "gu_s", "dn_w", "dn_s", "sh_gu_w", "sh_gu_s", "sh_dn_w", "sh_dn_s"):
+                t.pop(name, None)
+
+    def fp4_only_ok(self) -> bool:
+        """True when every batch shape of this layer is served by an FP4 regime (the limits csrc/common.cuh states for
+        them), so that nothing on the forward path ever reads the on-disk-order banks."""
+        c = self.cfg
+        return (c.hidden % 256 == 0 and c.inter % 256 == 0 and c.hidden <= 7168 and c.inter <= 7168
+                and 8 * 3 * c.inter * 4 <= 220 * 1024 and 8 * c.hidden * 4 <= 220 * 1024 and self.tail_bits == (0, 0))
 
     @property
     def router_ptr(self):
@@ -188,12 +203,15 @@ class PackedLayer:
         c, t = self.cfg, self.t
         h, i, e, ns, r = c.hidden, c.inter, c.n_experts, c.n_slots, c.rank
         want = {
-            "gu_w": (ns, 2 * i, h // 2), "gu_s": (ns, 2 * i, h // 16), "gu_s2": (ns,), "gu_beta": (e,),
-            "dn_w": (ns, h, i // 2), "dn_s": (ns, h, i // 16), "dn_s2": (ns,), "dn_beta": (e,),
+            "gu_s2": (ns,), "gu_beta": (e,), "dn_s2": (ns,), "dn_beta": (e,),
             "u_gu": (e, 2 * i, r), "v_gu": (e, r, h), "u_dn": (e, h, r), "v_dn_t": (e, i, r),
             "gu_cin": (e, h), "gu_cs2": (e, h // 32), "gu_rout": (e, 2 * i), "gu_rs2": (e, 2 * i // 32),
             "dn_cin": (e, i), "dn_cs2": (e, i // 32), "dn_rout": (e, h), "dn_rs2": (e, h // 32),
         }
+        if "gu_t" in t and "gu_w" not in t:  # resident as stage images only
+            want.update({"gu_t": (ns, 2 * i // 128, h // 256, 18432), "dn_t": (ns, h // 128, i // 256, 18432)})
+        else:
+            want.update({"gu_w": (ns, 2 * i, h // 2), "gu_s": (ns, 2 * i, h // 16), "dn_w": (ns, h, i // 2), "dn_s": (ns, h, i // 16)})
         if "router_w" in t:
             want["router_w"] = (c.router_experts, h)
         if "e_bias" in t:
@@ -201,6 +219,10 @@ class PackedLayer:
         if "sh_gu_w" in t:
             want.update({"sh_gu_w": (2 * i, h // 2), "sh_gu_s": (2 * i, h // 16), "sh_gu_s2": (2,),
                          "sh_dn_w": (h, i // 2), "sh_dn_s": (h, i // 16), "sh_dn_s2": (1,)})
+        if "sh8_gu_w" in t:
+            want.update({"sh8_gu_w": (2 * i, h), "sh8_gu_s": (2 * i // 128, h // 128), "sh8_dn_w": (h, i), "sh8_dn_s": (h // 128, i // 128)})
+        elif "sh_gu_t" in t and "sh_gu_w" not in t:
+            want.update({"sh_gu_t": (2 * i // 128, h // 256, 18432), "sh_dn_t": (h // 128, i // 256, 18432), "sh_gu_s2": (2,), "sh_dn_s2": (1,)})
         for name, shape in want.items():
             if name not in t:
                 raise ValueError(f"packed layer is missing tensor {name!r}")
@@ -223,7 +245,7 @@ class PackedLayer:
     @classmethod
     def from_groups(cls, cfg: FoldedLayerConfig, groups: Iterable[Mapping[str, Any]], router_w: Any = None,
                     e_bias: Any = None, shared: Mapping[str, Any] | None = None,
-                    device: torch.device | str = "cuda", include_tail: bool = False) -> "PackedLayer":
+                    device: torch.device | str = "cuda", include_tail: bool = False, keep_disk_order: bool = False) -> "PackedLayer":
         """`groups[g]` maps the on-disk suffixes to tensors/arrays (fp8 either as float8_e4m3fn or raw uint8).
         `shared` (optional) holds a plain-NVFP4 expert: `{gate,up,down}_proj.{weight,weight_scale,weight_scale_2}`.
         `include_tail` also loads the tail lattice tensors and makes every call on the layer add the tail term."""
@@ -273,7 +295,13 @@ class PackedLayer:
             t["router_w"] = _f32(router_w)
         if e_bias is not None:
             t["e_bias"] = _f32(e_bias)
-        if shared is not None:
+        if shared is not None and "gate_proj.weight_scale_inv" in shared:
+            # the stock block-FP8 format of the reference's shared expert (chronos_1t/models/glm53_chronos_moe.py:170-181):
+            # e4m3 weights + one fp32 weight_scale_inv per 128 x 128 block; gate and up fused along the rows
+            t["sh8_gu_w"] = torch.cat([_u8(shared["gate_proj.weight"]), _u8(shared["up_proj.weight"])])
+            t["sh8_gu_s"] = torch.cat([_f32(shared["gate_proj.weight_scale_inv"]), _f32(shared["up_proj.weight_scale_inv"])])
+            t["sh8_dn_w"], t["sh8_dn_s"] = _u8(shared["down_proj.weight"]), _f32(shared["down_proj.weight_scale_inv"])
+        elif shared is not None:
             t["sh_gu_w"] = torch.cat([_u8(shared["gate_proj.weight"]), _u8(shared["up_proj.weight"])])
             t["sh_gu_s"] = torch.cat([_u8(shared["gate_proj.weight_scale"]), _u8(shared["up_proj.weight_scale"])])
             t["sh_gu_s2"] = torch.stack([_f32(shared["gate_proj.weight_scale_2"]).reshape(()), _f32(shared["up_proj.weight_scale_2"]).reshape(())])
@@ -281,15 +309,28 @@ class PackedLayer:
             t["sh_dn_s2"] = _f32(shared["down_proj.weight_scale_2"]).reshape(1)
         t = {n: v.to(device).contiguous() for n, v in t.items()}
         t.update(key_tables(cfg, device))
-        return cls(cfg, t, device, tail_bits=tail_bits if include_tail else (0, 0))
+        return cls(cfg, t, device, tail_bits=tail_bits if include_tail else (0, 0), keep_disk_order=keep_disk_order)
 
     @classmethod
     def from_safetensors(cls, path: str | Path, cfg: FoldedLayerConfig, prefix: str, device: torch.device | str = "cuda",
-                         shared_prefix: str | None = None, include_tail: bool = False) -> "PackedLayer":
+                         shared_prefix: str | None = None, include_tail: bool = False, keep_disk_order: bool = False,
+                         evict_page_cache: bool = True) -> "PackedLayer":
         """Reads `{prefix}.chronos_groups.{g}.{suffix}` (chronos_1t/models/glm53_chronos_spec.py:186-191) and
-        `{prefix}.gate.weight` (+ `.gate.e_score_correction_bias`) from a converter shard."""
+        `{prefix}.gate.weight` (+ `.gate.e_score_correction_bias`) from a converter shard.
+
+        On a CUDA device the shard is streamed tensor by tensor from the memory-mapped file straight into the stacked
+        device tensors (no CPU copy of the layer is ever assembled), the FP4 stage images are built on the device slot by
+        slot, and the shard's pages are dropped from the page cache afterwards, as the reference's loader does
+        (chronos_1t/models/glm53_chronos_moe.py:56-63) - a model of dozens of such shards would otherwise fill the host's
+        page cache with bytes that are never read again."""
         from safetensors import safe_open
 
+        device = _norm_device(device)
+        if device.type == "cuda":
+            layer = cls._from_safetensors_direct(path, cfg, prefix, device, shared_prefix, include_tail, keep_disk_order)
+            if evict_page_cache:
+                evict_from_page_cache(path)
+            return layer
         with safe_open(str(path), framework="pt", device="cpu") as fh:
             names = set(fh.keys())
             groups = []
@@ -305,13 +346,79 @@ class PackedLayer:
             e_bias = fh.get_tensor(bias_key) if bias_key in names else None
             shared = None
             if shared_prefix is not None and f"{shared_prefix}.gate_proj.weight" in names:
-                shared = {f"{p}.{s}": fh.get_tensor(f"{shared_prefix}.{p}.{s}")
-                          for p in ("gate_proj", "up_proj", "down_proj") for s in ("weight", "weight_scale", "weight_scale_2")}
-        return cls.from_groups(cfg, groups, router_w, e_bias, shared, device, include_tail=include_tail)
+                shared = _read_shared(fh, names, shared_prefix)
+        return cls.from_groups(cfg, groups, router_w, e_bias, shared, device, include_tail=include_tail, keep_disk_order=keep_disk_order)
+
+    @classmethod
+    def _from_safetensors_direct(cls, path, cfg: FoldedLayerConfig, prefix: str, device: torch.device, shared_prefix, include_tail: bool,
+                                 keep_disk_order: bool) -> "PackedLayer":
+        from safetensors import safe_open
+
+        h, i, ns, k, r, e = cfg.hidden, cfg.inter, cfg.n_slots, cfg.group_size, cfg.rank, cfg.n_experts
+        u8 = dict(dtype=torch.uint8, device=device)
+        t: dict[str, torch.Tensor] = {
+            "gu_w": torch.empty((ns, 2 * i, h // 2), **u8), "gu_s": torch.empty((ns, 2 * i, h // 16), **u8),
+            "dn_w": torch.empty((ns, h, i // 2), **u8), "dn_s": torch.empty((ns, h, i // 16), **u8),
+            "gu_s2": torch.empty(ns, dtype=torch.float32, device=device), "dn_s2": torch.empty(ns, dtype=torch.float32, device=device),
+            "gu_beta": torch.empty(e, dtype=torch.float32, device=device), "dn_beta": torch.empty(e, dtype=torch.float32, device=device),
+            "u_gu": torch.empty((e, 2 * i, r), **u8), "v_gu": torch.empty((e, r, h), **u8),
+            "u_dn": torch.empty((e, h, r), **u8), "v_dn": torch.empty((e, r, i), **u8),
+        }
+        dest = {"s_gu.weight": "gu_w", "s_gu.weight_scale": "gu_s", "s_down.weight": "dn_w", "s_down.weight_scale": "dn_s",
+                "healer.u_gu": "u_gu", "healer.v_gu": "v_gu", "healer.u_down": "u_dn", "healer.v_down": "v_dn"}
+        tail_bits = (0, 0)
+        with safe_open(str(path), framework="pt", device="cpu") as fh:  # memory-mapped: a tensor's pages are touched when it is copied
+            names = set(fh.keys())
+            for g in range(ns):
+                gp = f"{prefix}.chronos_groups.{g}."
+                missing = [s for s in _REQUIRED if gp + s not in names]
+                if missing:
+                    raise ValueError(f"{path}: slot {g} is missing {missing}")
+                beta = fh.get_tensor(gp + "s_gu.beta")
+                if int(beta.shape[0]) != k:
+                    raise ValueError(f"slot {g} folds {int(beta.shape[0])} experts, config says {k}")
+                for sfx, name in dest.items():
+                    src = _u8(fh.get_tensor(gp + sfx))
+                    dst = t[name][g] if name in ("gu_w", "gu_s", "dn_w", "dn_s") else t[name][g * k:(g + 1) * k]
+                    if tuple(src.shape) != tuple(dst.shape):
+                        raise ValueError(f"{path}: {gp + sfx} has shape {tuple(src.shape)}, expected {tuple(dst.shape)}")
+                    dst.copy_(src, non_blocking=True)
+                t["gu_s2"][g].copy_(_f32(fh.get_tensor(gp + "s_gu.weight_scale_2")).reshape(()))
+                t["dn_s2"][g].copy_(_f32(fh.get_tensor(gp + "s_down.weight_scale_2")).reshape(()))
+                t["gu_beta"][g * k:(g + 1) * k].copy_(_f32(beta))
+                t["dn_beta"][g * k:(g + 1) * k].copy_(_f32(fh.get_tensor(gp + "s_down.beta")))
+            if include_tail:
+                groups = [{s: fh.get_tensor(f"{prefix}.chronos_groups.{g}.{s}") for s in GROUP_TENSOR_SUFFIXES[12:]} for g in range(ns)]
+                bits = {(int(d["tail.gu_bits"].reshape(-1)[0]), int(d["tail.down_bits"].reshape(-1)[0])) for d in groups}
+                if len(bits) != 1 or not bits <= {(1, 1), (1, 2), (2, 1), (2, 2)}:
+                    raise ValueError(f"include_tail: slots disagree on the tail bit widths or use unsupported ones: {sorted(bits)}")
+                tail_bits = next(iter(bits))
+                for name, sfx in (("tail_gu_p", "tail.gu_packed"), ("tail_gu_s", "tail.gu_scale"), ("tail_dn_p", "tail.down_packed"), ("tail_dn_s", "tail.down_scale")):
+                    t[name] = torch.cat([_u8(d[sfx]).to(device) for d in groups])
+            if f"{prefix}.gate.weight" in names:
+                t["router_w"] = _f32(fh.get_tensor(f"{prefix}.gate.weight")).to(device)
+            if f"{prefix}.gate.e_score_correction_bias" in names:
+                t["e_bias"] = _f32(fh.get_tensor(f"{prefix}.gate.e_score_correction_bias")).to(device)
+            sh = _read_shared(fh, names, shared_prefix) if (shared_prefix is not None and f"{shared_prefix}.gate_proj.weight" in names) else None
+            if sh is not None and "gate_proj.weight_scale_inv" in sh:
+                t["sh8_gu_w"] = torch.cat([_u8(sh["gate_proj.weight"]), _u8(sh["up_proj.weight"])]).to(device)
+                t["sh8_gu_s"] = torch.cat([_f32(sh["gate_proj.weight_scale_inv"]), _f32(sh["up_proj.weight_scale_inv"])]).to(device)
+                t["sh8_dn_w"], t["sh8_dn_s"] = _u8(sh["down_proj.weight"]).to(device), _f32(sh["down_proj.weight_scale_inv"]).to(device)
+            elif sh is not None:
+                t["sh_gu_w"] = torch.cat([_u8(sh["gate_proj.weight"]), _u8(sh["up_proj.weight"])]).to(device)
+                t["sh_gu_s"] = torch.cat([_u8(sh["gate_proj.weight_scale"]), _u8(sh["up_proj.weight_scale"])]).to(device)
+                t["sh_gu_s2"] = torch.stack([_f32(sh["gate_proj.weight_scale_2"]).reshape(()), _f32(sh["up_proj.weight_scale_2"]).reshape(())]).to(device)
+                t["sh_dn_w"], t["sh_dn_s"] = _u8(sh["down_proj.weight"]).to(device), _u8(sh["down_proj.weight_scale"]).to(device)
+                t["sh_dn_s2"] = _f32(sh["down_proj.weight_scale_2"]).reshape(1).to(device)
+            torch.cuda.synchronize(device)  # the copies read the mapping: finish them before it is closed
+        t["v_dn_t"] = t["v_dn"].transpose(1, 2).contiguous()
+        t.update(key_tables(cfg, device))
+        return cls(cfg, t, device, tail_bits=tail_bits, keep_disk_order=keep_disk_order)
 
     @classmethod
     def synthetic(cls, cfg: FoldedLayerConfig, seed: int, device: torch.device | str = "cuda",
-                  with_shared: bool = False, tail_bits: tuple[int, int] = (0, 0)) -> "PackedLayer":
+                  with_shared: bool = False, tail_bits: tuple[int, int] = (0, 0), keep_disk_order: bool = False,
+                  shared_format: str = "nvfp4") -> "PackedLayer":
         """Seeded random layer in the converter's byte format, generated on the device (for benchmarks: the real
         converter takes seconds per slot). Value ranges follow what the converter emits for N(0, 0.02) weights:
         uniform nibbles, e4m3 block-scale codes 0x58..0x77, scale_2 = amax / 2688, beta ~ 0.5, healer ~ N(0, 0.05)."""
@@ -321,7 +428,9 @@ class PackedLayer:
         t["router_w"] = torch.randn(cfg.router_experts, cfg.hidden, generator=gen, device=device) * 0.02
         if cfg.router != "softmax":
             t["e_bias"] = torch.zeros(cfg.router_experts, device=device)
-        if with_shared:
+        if with_shared and shared_format == "fp8":
+            t.update(cls._random_shared_fp8_tensors(cfg, gen, device))
+        elif with_shared:
             t.update(cls._random_shared_tensors(cfg, gen, device))
         if tail_bits != (0, 0):  # random codes; block scales 0.004 .. 0.02, below the typical bank value
             h, i, e = cfg.hidden, cfg.inter, cfg.n_experts
@@ -331,7 +440,7 @@ class PackedLayer:
             t["tail_dn_p"] = torch.randint(0, 256, (e, h, i * db // 8), generator=gen, device=device, dtype=torch.uint8)
             t["tail_dn_s"] = torch.randint(0x02, 0x0C, (e, h, i // (32 if db == 2 else 64)), generator=gen, device=device, dtype=torch.uint8)
         t.update(key_tables(cfg, device))
-        return cls(cfg, t, device, tail_bits=tail_bits)
+        return cls(cfg, t, device, tail_bits=tail_bits, keep_disk_order=keep_disk_order)
 
     @classmethod
     def synthetic_sharded(cls, cfg_global: FoldedLayerConfig, seed: int, slots: range, device: torch.device | str = "cuda",
@@ -395,9 +504,33 @@ class PackedLayer:
             "sh_dn_s2": torch.full((1,), 0.08 / 2688.0, device=device),
         }
 
+    @staticmethod
+    def _random_shared_fp8_tensors(cfg: FoldedLayerConfig, gen: torch.Generator, device: torch.device) -> dict[str, torch.Tensor]:
+        """An N(0, 0.02) SwiGLU expert quantised to the stock 128 x 128 block-FP8 format (scale_inv = block max / 448)."""
+        h, i = cfg.hidden, cfg.inter
+        out = {}
+        for name, rows, cols in (("sh8_gu", 2 * i, h), ("sh8_dn", h, i)):
+            w = torch.randn((rows, cols), generator=gen, device=device) * 0.02
+            blocks = w.view(rows // 128, 128, cols // 128, 128)
+            s = blocks.abs().amax(dim=(1, 3)).clamp_min(1e-12) / 448.0
+            q = (blocks / s[:, None, :, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+            out[f"{name}_w"] = q.view(torch.uint8).reshape(rows, cols).contiguous()
+            out[f"{name}_s"] = s.float().contiguous()
+        return out
+
     def to_groups_numpy(self) -> tuple[list[dict[str, np.ndarray]], dict[str, np.ndarray]]:
         """Back to per-slot dicts of on-disk suffixes (numpy, fp8 as uint8) + extras: what a checker needs."""
-        c, t = self.cfg, {n: v.cpu().numpy() for n, v in self.t.items()}
+        c = self.cfg
+        tt = dict(self.t)
+        if "gu_w" not in tt and "gu_t" in tt:  # resident as stage images only: undo the byte permutation
+            from .fp4_layout import untile_matrix_fp4
+
+            tt["gu_w"], tt["gu_s"] = untile_matrix_fp4(tt["gu_t"])
+            tt["dn_w"], tt["dn_s"] = untile_matrix_fp4(tt["dn_t"])
+            if "sh_gu_t" in tt:
+                tt["sh_gu_w"], tt["sh_gu_s"] = untile_matrix_fp4(tt["sh_gu_t"])
+                tt["sh_dn_w"], tt["sh_dn_s"] = untile_matrix_fp4(tt["sh_dn_t"])
+        t = {n: v.cpu().numpy() for n, v in tt.items() if not n.endswith("_t") or n == "v_dn_t"}
         k = c.group_size
         groups = []
         for g in range(c.n_slots):
@@ -416,8 +549,33 @@ class PackedLayer:
                                   "tail.gu_scale": t["tail_gu_s"][sl], "tail.down_bits": np.uint8(self.tail_bits[1]),
                                   "tail.down_packed": t["tail_dn_p"][sl], "tail.down_scale": t["tail_dn_s"][sl]})
         # (the re-tiled FP4 images are derived data and are not exported)
-        extras = {n: t[n] for n in ("router_w", "e_bias", "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2") if n in t}
+        extras = {n: t[n] for n in ("router_w", "e_bias", "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
+                                    "sh8_gu_w", "sh8_gu_s", "sh8_dn_w", "sh8_dn_s") if n in t}
         return groups, extras
+
+
+def _read_shared(fh, names: set, shared_prefix: str) -> dict:
+    """The always-on expert's tensors under `shared_prefix`: plain NVFP4 (`weight`, `weight_scale`, `weight_scale_2`, the hub
+    expert format of chronos_1t/models/vllm_chronos_moe.py:131-141) or stock block-FP8 (`weight`, `weight_scale_inv`,
+    chronos_1t/models/glm53_chronos_moe.py:170-181), told apart by the scale tensor's name."""
+    fp8 = f"{shared_prefix}.gate_proj.weight_scale_inv" in names
+    sfx = ("weight", "weight_scale_inv") if fp8 else ("weight", "weight_scale", "weight_scale_2")
+    return {f"{p}.{s}": fh.get_tensor(f"{shared_prefix}.{p}.{s}") for p in ("gate_proj", "up_proj", "down_proj") for s in sfx}
+
+
+def evict_from_page_cache(path: str | Path) -> None:
+    """Tells the kernel that the file's cached pages will not be needed again (chronos_1t/models/glm53_chronos_moe.py:56-63)."""
+    import os
+
+    if hasattr(os, "posix_fadvise") and hasattr(os, "POSIX_FADV_DONTNEED"):
+        try:
+            fd = os.open(os.path.realpath(str(path)), os.O_RDONLY)
+            try:
+                os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+            finally:
+                os.close(fd)
+        except OSError:
+            pass
 
 
 def layer_index_from_prefix(prefix: str) -> int | None:

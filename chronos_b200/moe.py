@@ -166,6 +166,25 @@ class FoldedMoELayer(nn.Module):
         self.last_logits = logits
         return ids, w
 
+    @torch.no_grad()
+    def route_coalesced(self, x: torch.Tensor, tokens_per_stream: int = 3, pool: int = 12, keep: int = 4,
+                        bonus: float = 1.0e4) -> tuple[torch.Tensor, torch.Tensor]:
+        """Batch-coalesced routing for speculative verify batches (streams of `tokens_per_stream` tokens, token 0 of each
+        the anchor): the anchor keeps its natural top-k; a draft keeps its `keep` best natural experts and fills the rest from
+        its own natural top-`pool`, preferring experts the anchor selected. Fewer distinct banks per step, no token ever
+        routed outside its natural top-`pool`. A clean-room stand-in for the policy the reference describes in prose only
+        (README.md:56, :208, :372). Returns (ids, weights) for `routed_forward`."""
+        x = self._prep(x)
+        n = x.shape[0]
+        ids = torch.empty((n, self.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((n, self.top_k), dtype=torch.float32, device=self.device)
+        logits = torch.empty((n, self.cfg.router_experts), dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().chronos_b200_router_topk_coalesced(self.packed.router_ptr, x.data_ptr(), _DTYPES[x.dtype], n, int(tokens_per_stream),
+                                                               int(pool), int(keep), float(bonus), ids.data_ptr(), w.data_ptr(),
+                                                               logits.data_ptr(), self._stream()))
+        self.last_logits = logits
+        return ids, w
+
     route_global = route  # expert-parallel shards: ids index the full (replicated) router table
 
     @torch.no_grad()

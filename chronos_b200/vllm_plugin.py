@@ -19,6 +19,7 @@ from .layout import FoldedLayerConfig, layer_index_from_prefix
 from .moe import LIVE_BLOCKS, FoldedMoELayer
 
 OP_NAME = "chronos_b200::moe_forward"
+REFERENCE_OP_NAME = "chronos_glm53::moe_forward"  # the name the reference registers (chronos_1t/models/patch_glm53_vllm.py:79-93)
 _OP_REGISTERED = False
 MODEL_SITES = (
     "vllm.models.deepseek_v32.nvidia.model",
@@ -27,19 +28,31 @@ MODEL_SITES = (
 )
 
 
+def _reference_op_taken() -> bool:
+    """True when `torch.ops.chronos_glm53.moe_forward` already exists (the reference package registered it first)."""
+    try:
+        return hasattr(torch.ops.chronos_glm53, "moe_forward")
+    except (AttributeError, RuntimeError):
+        return False
+
+
 def register_custom_op() -> None:
-    """Registers `torch.ops.chronos_b200.moe_forward` once; traceable by torch.compile through its fake impl."""
+    """Registers `torch.ops.chronos_b200.moe_forward(hidden_states, layer_idx) -> Tensor` once, traceable by torch.compile
+    through its `empty_like` fake impl, and the same operator under the reference's own name
+    `torch.ops.chronos_glm53.moe_forward` (chronos_1t/models/patch_glm53_vllm.py:79-93) so that an unchanged caller of
+    the reference resolves it - unless the reference package already registered that name in this process."""
     global _OP_REGISTERED
     if _OP_REGISTERED:
         return
+    names = [OP_NAME] + ([] if _reference_op_taken() else [REFERENCE_OP_NAME])
+    for name in names:
+        @torch.library.custom_op(name, mutates_args=())
+        def _moe_forward(hidden_states: torch.Tensor, layer_idx: int) -> torch.Tensor:
+            return LIVE_BLOCKS[layer_idx].forward_impl(hidden_states)
 
-    @torch.library.custom_op(OP_NAME, mutates_args=())
-    def _moe_forward(hidden_states: torch.Tensor, layer_idx: int) -> torch.Tensor:
-        return LIVE_BLOCKS[layer_idx].forward_impl(hidden_states)
-
-    @_moe_forward.register_fake
-    def _(hidden_states: torch.Tensor, layer_idx: int) -> torch.Tensor:
-        return torch.empty_like(hidden_states)
+        @_moe_forward.register_fake
+        def _(hidden_states: torch.Tensor, layer_idx: int) -> torch.Tensor:
+            return torch.empty_like(hidden_states)
 
     _OP_REGISTERED = True
 

@@ -81,6 +81,11 @@ extern "C" {
  * of nibbles in K-major core-matrix order followed by four 512-byte scale blocks (see chronos_b200_fp4_mma_probe):
  *   gu_t u8 [n_slots, 2I/128, H/256, 18432], dn_t u8 [n_slots, H/128, I/256, 18432], sh_gu_t / sh_dn_t without the
  *   slot axis.  A pure permutation of the "s_gu.weight" + "s_gu.weight_scale" bytes; the file format is untouched.
+ * Optional: the shared expert in the STOCK 128 x 128 block-FP8 checkpoint format instead (the format the reference keeps it in,
+ *   chronos_1t/models/glm53_chronos_moe.py:170-181): sh8_gu_w e4m3 [2*shared_inter, H] (gate rows, then up rows),
+ *   sh8_gu_s f32 [2*shared_inter/128, H/128] "weight_scale_inv", sh8_dn_w e4m3 [H, shared_inter], sh8_dn_s f32
+ *   [H/128, shared_inter/128]; value = float(e4m3) * scale_inv[row/128, col/128] (chronos_1t/models/glm53_tiers.py:74-95).
+ *   With sh8_gu_w set the NVFP4 shared-expert pointers (sh_*) are ignored.
  * Optional tail lattice (tail_bits != 0; chronos_1t/models/chronos_moe_block.py:122-229, applied at
  *   chronos_1t/models/glm53_holo.py:362-366): per expert a matrix in natural weight space added to the reconstruction,
  *   tail_gu_p u8 [n_experts, 2I, H*bits/8] "tail.gu_packed", tail_gu_s e4m3 [n_experts, 2I, H/32 (2-bit) | H/64 (1-bit)]
@@ -109,6 +114,7 @@ typedef struct chronos_layer {
     const uint8_t* gu_t; const uint8_t* dn_t; const uint8_t* sh_gu_t; const uint8_t* sh_dn_t;
     const uint8_t* v_dn;
     const uint8_t* tail_gu_p; const uint8_t* tail_gu_s; const uint8_t* tail_dn_p; const uint8_t* tail_dn_s;
+    const uint8_t* sh8_gu_w; const float* sh8_gu_s; const uint8_t* sh8_dn_w; const float* sh8_dn_s;
 } chronos_layer_t;
 
 /* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated
@@ -117,6 +123,11 @@ typedef struct chronos_layer {
  *           (= chronos_1t/models/chronos_moe_block.py:109-119 with dtype=float32). */
 int chronos_b200_dequant_nvfp4(const uint8_t* packed, const uint8_t* scale, const float* scale_2, float* out,
                                int rows, int cols, void* stream);
+
+/* Block-FP8 dequantisation probe: out[rows, cols] f32 = float(e4m3 w[r, c]) * scale_inv[r / 128, c / 128] in fp32 (bit-exact
+ * target); scale_inv f32 [ceil(rows/128), ceil(cols/128)].
+ * Replaces: dequant_fp8_block(dtype=float32), chronos_1t/models/glm53_tiers.py:74-95. */
+int chronos_b200_dequant_fp8_block(const uint8_t* w, const float* scale_inv, float* out, int rows, int cols, void* stream);
 
 /* Weight-space reconstruction probe of ONE expert: out f32 = beta * unbind(bank) + U.V, plus the tail-lattice term
  * when the layer carries one (tail_bits != 0).  which = 0: gate_up [2I, H]; which = 1: down [H, I].  `scratch` holds
@@ -149,6 +160,19 @@ int chronos_b200_unfold_expert_fp32_static(const chronos_layer_t* layer, int exp
  *           chronos_1t/models/glm53_chronos_moe.py:392-399. */
 int chronos_b200_router_topk(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int32_t* ids,
                              float* gates, float* logits, void* stream);
+
+/* Router with the batch-coalesced selection policy for speculative verify batches: tokens come in streams of
+ * tokens_per_stream (token 0 = the verified anchor, the rest drafts).  The anchor gets its natural top-k.  A draft keeps
+ * its `keep` best natural experts, and fills the other top_k - keep places from its own natural top-`pool` candidates
+ * ranked by choice score + `bonus` for experts the anchor selected too (ties to the better natural rank), so that fewer
+ * distinct banks are streamed per step; it is never routed outside its natural top-`pool`.  pool == top_k or bonus == 0
+ * reproduces chronos_b200_router_topk.  Gate weights follow router_kind on the unbiased scores of the picked experts.
+ * Feed ids / gates to chronos_b200_folded_moe_routed.
+ * Stands in for `_chronos_fused_topk_sigmoid_kernel`, which the reference only describes (README.md:56, :208, :372;
+ * docs/CHRONOS_ARCHITECTURE_PAPER.md:270-277): its source is not part of the reference, so this is a clean-room policy
+ * built to the stated invariants, not a transcription. */
+int chronos_b200_router_topk_coalesced(const chronos_layer_t* layer, const void* x, int x_dtype, int n_tokens, int tokens_per_stream,
+                                       int pool, int keep, float bonus, int32_t* ids, float* gates, float* logits, void* stream);
 
 /* Bytes of caller-owned scratch the forward entry points need for n_tokens tokens (0 on bad arguments). */
 size_t chronos_b200_workspace_bytes(const chronos_layer_t* layer, int n_tokens);

@@ -111,6 +111,21 @@ def pack_nvfp4(w: np.ndarray):
     return packed, scale_u8, scale_2
 
 
+def dequant_fp8_block(w_u8: np.ndarray, scale_inv: np.ndarray, block: int = 128) -> np.ndarray:
+    """chronos_1t/models/glm53_tiers.py:74-95 with dtype=float32: value = float(e4m3) * scale_inv[row // 128, col // 128]."""
+    w = e4m3_to_f32(w_u8)
+    n, k = w.shape
+    s = np.asarray(scale_inv, dtype=np.float32)
+    s_full = np.repeat(np.repeat(s, block, axis=0)[:n], block, axis=1)[:, :k]
+    return (w * s_full).astype(np.float32)
+
+
+def shared_fp8_weights(ex: dict):
+    """fp32 (gate_up [2I, H], down [H, I]) of a block-FP8 shared expert given as sh8_gu_w / sh8_gu_s / sh8_dn_w / sh8_dn_s
+    (gate rows, then up rows: chronos_1t/models/glm53_chronos_moe.py:176-181)."""
+    return dequant_fp8_block(ex["sh8_gu_w"], ex["sh8_gu_s"]), dequant_fp8_block(ex["sh8_dn_w"], ex["sh8_dn_s"])
+
+
 # ---------------------------------------------------------------------------------------------
 # Tail lattices (carried by the on-disk format; excluded from the timed path)
 # ---------------------------------------------------------------------------------------------
@@ -333,6 +348,48 @@ def router_sqrt_softplus_topk(logits: np.ndarray, e_bias, k: int, routed_scaling
     unbiased scores, divided by their sum (+1e-20), times routed_scaling_factor."""
     scores = np.sqrt(softplus(logits)).astype(np.float32)
     return _noaux_topk(scores, e_bias, k, routed_scaling, renorm)
+
+
+def router_coalesced(logits: np.ndarray, k: int, tokens_per_stream: int = 3, pool: int = 12, keep: int = 4, bonus: float = 1.0e4,
+                     router: str = "softmax", e_bias=None, routed_scaling: float = 2.5, renorm: bool = True):
+    """Batch-coalesced selection for speculative verify batches. PARITY UNPINNED: the reference only describes the policy
+    (README.md:56, :208, :372; docs/CHRONOS_ARCHITECTURE_PAPER.md:270-277 - the kernel's source is not part of it), so
+    this restates the clean-room rule of the device kernel, and the tests check the invariants the reference states:
+    the anchor (token 0 of a stream) is untouched; a draft never leaves its natural top-`pool`; its `keep` best natural
+    experts stay; the rest prefers experts the anchor selected (score + bonus), ties to the better natural rank."""
+    lg = np.asarray(logits, dtype=np.float32)
+    bias = np.zeros(lg.shape[1], dtype=np.float32) if e_bias is None else np.asarray(e_bias, dtype=np.float32)
+    if router == "softmax":
+        score = lg
+        choice = lg
+    else:
+        score = (1.0 / (1.0 + np.exp(-lg))).astype(np.float32) if router == "sigmoid" else np.sqrt(softplus(lg)).astype(np.float32)
+        choice = (score + bias[None, :]).astype(np.float32)
+    n = lg.shape[0]
+    nat = topk_desc(choice, pool)
+    ids = np.full((n, k), -1, dtype=np.int64)
+    for t in range(n):
+        if t % tokens_per_stream == 0:
+            ids[t] = nat[t, :k]
+            continue
+        anchor = set(int(e) for e in ids[t - t % tokens_per_stream] if e >= 0)
+        cand = [(j, int(e)) for j, e in enumerate(nat[t]) if e >= 0]
+        kept = [e for j, e in cand if j < keep]
+        rest = [(j, e) for j, e in cand if j >= keep]
+        key = lambda je: (-(np.float32(choice[t, je[1]]) + (np.float32(bonus) if je[1] in anchor else np.float32(0.0))), je[0])
+        picked = kept + [e for _, e in sorted(rest, key=key)][: k - len(kept)]
+        ids[t, : len(picked)] = picked
+    w = _gather_valid(score, ids)
+    if router == "softmax":
+        with np.errstate(invalid="ignore", divide="ignore"):
+            mx = np.where(ids >= 0, w, -np.inf).max(axis=1, keepdims=True)
+            ex = np.where(ids >= 0, np.exp((w - mx).astype(np.float32)), np.float32(0.0)).astype(np.float32)
+            w = (ex / ex.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    else:
+        if renorm:
+            w = w / (w.sum(axis=1, keepdims=True, dtype=np.float32) + np.float32(1e-20))
+        w = (w * np.float32(routed_scaling)).astype(np.float32)
+    return ids, np.where(ids >= 0, w, np.float32(0.0)).astype(np.float32)
 
 
 # ---------------------------------------------------------------------------------------------

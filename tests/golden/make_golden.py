@@ -167,6 +167,34 @@ def make_router_case(c: dict = ROUTER_CASE) -> None:
     print(c["name"], "->", (HERE / f"{c['name']}.npz").stat().st_size, "bytes")
 
 
+def make_fp8_block_case() -> None:
+    """Stock 128x128 block-FP8 weights (the format the reference keeps the shared expert in,
+    chronos_1t/models/glm53_chronos_moe.py:170-181): `dequant_fp8_block` (chronos_1t/models/glm53_tiers.py:74-95) of seeded
+    bytes, and the shared expert's output the way `shared_forward` (:401-404) computes it for a batch above its GEMV
+    threshold (dequantise, then F.linear), in fp32."""
+    from chronos_1t.models.glm53_tiers import dequant_fp8_block
+
+    gen = torch.Generator().manual_seed(21)
+    h, i, n_tok = 256, 128, 6
+    out: dict[str, np.ndarray] = {"meta": np.array([h, i, n_tok], dtype=np.int64)}
+    tens = {}
+    for name, (rows, cols) in (("gate_proj", (i, h)), ("up_proj", (i, h)), ("down_proj", (h, i))):
+        w = torch.randint(0, 256, (rows, cols), generator=gen, dtype=torch.uint8)
+        w[(w & 0x7F) == 0x7F] = 0x3A  # no NaN codes
+        s = torch.rand((rows // 128, cols // 128), generator=gen) * 0.02 + 0.001
+        tens[name] = (w, s)
+        out[f"{name}.weight"], out[f"{name}.weight_scale_inv"] = _np(w), _np(s)
+        out[f"ref.dequant.{name}"] = _np(dequant_fp8_block(w, s, dtype=torch.float32))
+    x = torch.randn(n_tok, h, generator=gen)
+    out["x"] = _np(x)
+    gu_w = torch.cat([dequant_fp8_block(*tens["gate_proj"], dtype=torch.float32), dequant_fp8_block(*tens["up_proj"], dtype=torch.float32)], 0)
+    gu = F.linear(x, gu_w)
+    act = F.silu(gu[:, :i]) * gu[:, i:]
+    out["ref.shared_y"] = _np(F.linear(act, dequant_fp8_block(*tens["down_proj"], dtype=torch.float32)))
+    np.savez_compressed(HERE / "fp8_block_shared.npz", **out)
+    print("fp8_block_shared ->", (HERE / "fp8_block_shared.npz").stat().st_size, "bytes")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     for nm, cfg in CASES.items():
@@ -174,3 +202,5 @@ if __name__ == "__main__":
             make_case(nm, cfg)
     if len(sys.argv) < 2 or ROUTER_CASE["name"] in sys.argv[1:]:
         make_router_case()
+    if len(sys.argv) < 2 or "fp8_block_shared" in sys.argv[1:]:
+        make_fp8_block_case()

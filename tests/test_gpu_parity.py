@@ -112,7 +112,7 @@ def test_layer_with_tail_matches_oracle(regime, n_tok, tails):
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=32, top_k=2)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=21, with_shared=True, tail_bits=tails), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=21, with_shared=True, tail_bits=tails, keep_disk_order=True), register=False)
     gen = torch.Generator(device="cuda").manual_seed(n_tok)
     x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
     y = layer.forward_impl(x, regime=regime)
@@ -228,7 +228,9 @@ def _oracle_layer(layer, x_np, with_shared=True, include_tail=False):
     groups, extras = layer.packed.to_groups_numpy()
     c = layer.cfg
     shared = None
-    if with_shared and "sh_gu_w" in extras:
+    if with_shared and "sh8_gu_w" in extras:
+        shared = O.shared_fp8_weights(extras)
+    elif with_shared and "sh_gu_w" in extras:
         i = c.inter
         gate = O.unpack_nvfp4(extras["sh_gu_w"][:i], extras["sh_gu_s"][:i], extras["sh_gu_s2"][0])
         up = O.unpack_nvfp4(extras["sh_gu_w"][i:], extras["sh_gu_s"][i:], extras["sh_gu_s2"][1])
@@ -291,7 +293,7 @@ def test_fp4_streaming_regime_matches_oracle_and_cuda_core_regime():
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=1024, inter=512, n_experts=32, group_size=4, rank=32, top_k=4)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True, keep_disk_order=True), register=False)
     assert layer.packed.struct.gu_t and layer.packed.struct.dn_t
     gen = torch.Generator(device="cuda").manual_seed(8)
     for scale in (1.0, 37.0, 0.004):  # the per-pair power-of-two scale must absorb the activation magnitude
@@ -336,7 +338,7 @@ def test_many_tokens_on_one_slot_and_skipped_entries():
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=2)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=7), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=7, keep_disk_order=True), register=False)
     n = 21
     gen = torch.Generator(device="cuda").manual_seed(3)
     x = torch.randn(n, cfg.hidden, generator=gen, device="cuda")
@@ -386,7 +388,7 @@ def test_tensor_regime_matches_oracle_and_stream_regime():
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=16, top_k=2)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=11, with_shared=True), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=11, with_shared=True, keep_disk_order=True), register=False)
     n = 300  # > 128 pairs on several experts: full tiles, ragged tiles and (expert 7 unused) empty ones
     gen = torch.Generator(device="cuda").manual_seed(5)
     x = torch.randn(n, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
@@ -421,7 +423,7 @@ def test_tensor_regime_whole_layer_with_router_and_shared(rank):
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=1024, inter=384, n_experts=16, group_size=4, rank=rank, top_k=4)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, with_shared=True), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=2, with_shared=True, keep_disk_order=True), register=False)
     gen = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(200, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
     y = layer.forward_impl(x, regime="tensor")
@@ -440,7 +442,7 @@ def test_tensor_fp4_regime_whole_layer(scale):
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=1024, inter=512, n_experts=16, group_size=4, rank=64, top_k=4)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=4, with_shared=True, keep_disk_order=True), register=False)
     gen = torch.Generator(device="cuda").manual_seed(13)
     x = (torch.randn(330, cfg.hidden, generator=gen, device="cuda") * scale).to(torch.bfloat16)
     y = layer.forward_impl(x, regime="tensor_fp4")
@@ -487,7 +489,7 @@ def test_large_batch_without_optional_copies_and_shared_expert_range():
     from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
 
     cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=32, top_k=2)
-    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=17, with_shared=True), register=False)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=17, with_shared=True, keep_disk_order=True), register=False)
     gen = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(120, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
     ids, w = layer.route(x)
@@ -536,6 +538,125 @@ def test_fp4_tensor_core_operand_format(n_stages, b_rows):
     assert int(status.item()) == 0
     got = d.cpu().numpy().astype(np.float64)
     assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max(), np.abs(got - ref).max() / np.abs(ref).max()
+
+
+def test_layer_resident_as_stage_images_only_and_direct_loader(golden, tmp_path):
+    """By default a layer whose shapes the FP4 regimes serve keeps ONE copy of its banks (the stage images): half the
+    resident bytes, same outputs; the regimes and probes that read the on-disk order refuse it with a clear message.
+    And a converter-format shard written from reference-converted slots loads straight onto the device (tensor by tensor
+    from the mapped file) and reproduces the reference's layer output."""
+    from safetensors.torch import save_file
+
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer, _lib
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=4)
+    both = PackedLayer.synthetic(cfg, seed=9, with_shared=True, keep_disk_order=True)
+    lean = PackedLayer.synthetic(cfg, seed=9, with_shared=True)
+    assert "gu_w" in both.t and "gu_w" not in lean.t and not lean.struct.gu_w and lean.struct.gu_t
+    assert lean.resident_bytes() < 0.62 * both.resident_bytes()
+    ga, gb = both.to_groups_numpy(), lean.to_groups_numpy()  # the images invert to the very bytes that were dropped
+    for da, db in zip(ga[0], gb[0]):
+        assert all(np.array_equal(da[n], db[n]) for n in da)
+    assert all(np.array_equal(ga[1][n], gb[1][n]) for n in ga[1])
+    la, lb = FoldedMoELayer(packed=both, register=False), FoldedMoELayer(packed=lean, register=False)
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    for n_tok in (5, 200):
+        x = torch.randn(n_tok, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+        assert torch.equal(la(x), lb(x))
+    with pytest.raises(_lib.ChronosError, match="on-disk order"):
+        lb.forward_impl(x, regime="stream")
+    # direct loader: golden slots (reference converter output) -> shard -> device
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    gcfg = _cfg(golden["meta"], "sigmoid")
+    prefix = "model.layers.3.mlp"
+    tensors = {}
+    for g, grp in enumerate(golden_groups(golden)):
+        for sfx, arr in grp.items():
+            t = torch.from_numpy(np.ascontiguousarray(arr))
+            tensors[f"{prefix}.chronos_groups.{g}.{sfx}"] = t.view(torch.float8_e4m3fn) if (sfx.endswith("_scale") or sfx.startswith("healer.")) else t
+    tensors[f"{prefix}.gate.weight"] = torch.from_numpy(golden["router_w"])
+    tensors[f"{prefix}.gate.e_score_correction_bias"] = torch.from_numpy(golden["e_bias"])
+    path = tmp_path / "chronos-glm53-layer-00003-of-00005.safetensors"
+    save_file(tensors, str(path))
+    direct = PackedLayer.from_safetensors(path, gcfg, prefix, device="cuda")
+    staged = PackedLayer.from_groups(gcfg, golden_groups(golden), golden["router_w"], golden["e_bias"], device="cuda")
+    for n in staged.t:
+        assert torch.equal(direct.t[n], staged.t[n]), n
+    y = FoldedMoELayer(packed=direct, register=False)(torch.from_numpy(golden["x"]).cuda())
+    assert _rel_l2(y.cpu().numpy(), golden["ref.layer_y.sigmoid"]) <= LAYER_TOL
+    with_tail = PackedLayer.from_safetensors(path, gcfg, prefix, device="cuda", include_tail=True)
+    assert with_tail.tail_bits != (0, 0) and "tail_gu_p" in with_tail.t
+
+
+@pytest.mark.parametrize("flavour", ["softmax", "sigmoid"])
+def test_coalesced_routing_matches_its_oracle_and_runs_the_layer(flavour):
+    """The batch-coalesced router on the device: ids identical to the oracle's restatement of the policy, gates equal,
+    fewer distinct slots per step than natural routing, and the layer evaluated with that routing matches the oracle."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer
+    from chronos_b200.workloads import decode_batches
+
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=288, group_size=4, rank=16, top_k=8, router=flavour)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=61, with_shared=True), register=False)
+    if flavour != "softmax":
+        layer.packed.t["e_bias"].copy_(torch.randn(cfg.n_experts, generator=torch.Generator().manual_seed(1)) * 0.05)
+    x = decode_batches(cfg, 4, "cuda", seed=5, n_batches=1)[0]
+    nat_ids, _ = layer.route(x)
+    ids, w = layer.route_coalesced(x, tokens_per_stream=3, pool=12, keep=4)
+    logits = layer.last_logits.cpu().numpy()
+    bias = layer.packed.t["e_bias"].cpu().numpy() if flavour != "softmax" else None
+    ref_ids, ref_w = O.router_coalesced(logits, cfg.top_k, 3, 12, 4, 1.0e4, router=flavour, e_bias=bias)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    assert np.allclose(w.cpu().numpy(), ref_w, rtol=3e-5, atol=1e-7)
+    assert torch.equal(ids[0::3], nat_ids[0::3]), "anchors must be routed naturally"
+    experts = lambda a: len(set(a.reshape(-1).tolist()))
+    slots = lambda a: len({int(e) // cfg.group_size for e in a.reshape(-1).tolist()})
+    assert experts(ids) < experts(nat_ids) and slots(ids) <= slots(nat_ids)
+    same, _ = layer.route_coalesced(x, tokens_per_stream=3, pool=8, keep=4)
+    assert torch.equal(torch.sort(same, dim=1).values, torch.sort(nat_ids, dim=1).values)
+    y = layer.routed_forward(x, ids, w, with_shared=True)
+    assert layer.device_status() == 0
+    groups, ex = layer.packed.to_groups_numpy()
+    shared = (np.concatenate([O.unpack_nvfp4(ex["sh_gu_w"][:cfg.inter], ex["sh_gu_s"][:cfg.inter], ex["sh_gu_s2"][0]),
+                              O.unpack_nvfp4(ex["sh_gu_w"][cfg.inter:], ex["sh_gu_s"][cfg.inter:], ex["sh_gu_s2"][1])]),
+              O.unpack_nvfp4(ex["sh_dn_w"], ex["sh_dn_s"], ex["sh_dn_s2"][0]))
+    ref = O.routed_tokens_activation_space(x.float().cpu().numpy(), ref_ids, ref_w, groups, cfg.hidden, cfg.inter, cfg.group_size, shared=shared)
+    assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL
+
+
+def test_block_fp8_shared_expert(golden):
+    """The always-on expert in the stock 128 x 128 block-FP8 format: the dequantisation probe is bit-exact against the
+    reference's `dequant_fp8_block`, the shared expert alone reproduces the reference's output on the golden bytes, and
+    layers that carry it match the oracle in every regime."""
+    from chronos_b200 import FoldedLayerConfig, FoldedMoELayer, PackedLayer, _lib
+    from conftest import load_golden
+
+    g8 = load_golden("fp8_block_shared")
+    h, i, n_tok = (int(v) for v in g8["meta"])
+    for name in ("gate_proj", "down_proj"):
+        w, s_inv = torch.from_numpy(g8[f"{name}.weight"]).cuda(), torch.from_numpy(g8[f"{name}.weight_scale_inv"]).cuda()
+        out = torch.empty(w.shape, dtype=torch.float32, device="cuda")
+        _lib.check(_lib.lib().chronos_b200_dequant_fp8_block(w.data_ptr(), s_inv.data_ptr(), out.data_ptr(), w.shape[0], w.shape[1],
+                                                            torch.cuda.current_stream().cuda_stream))
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), g8[f"ref.dequant.{name}"].view(np.uint32))
+    if (int(golden["meta"][0]), int(golden["meta"][1])) == (h, i):  # the golden layer of the same dimensions hosts the shared expert
+        shared = {f"{p}.{sfx}": g8[f"{p}.{sfx}"] for p in ("gate_proj", "up_proj", "down_proj") for sfx in ("weight", "weight_scale_inv")}
+        packed = PackedLayer.from_groups(_cfg(golden["meta"]), golden_groups(golden), golden["router_w"], shared=shared, device="cuda")
+        layer = FoldedMoELayer(packed=packed, register=False)
+        x = torch.from_numpy(g8["x"]).cuda()
+        none = torch.full((n_tok, layer.top_k), -1, dtype=torch.int32, device="cuda")
+        y = layer.routed_forward(x, none, torch.zeros_like(none, dtype=torch.float32), with_shared=True)
+        assert _rel_l2(y.cpu().numpy(), g8["ref.shared_y"]) <= 2e-3
+    cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=16, group_size=4, rank=16, top_k=4)
+    layer = FoldedMoELayer(packed=PackedLayer.synthetic(cfg, seed=51, with_shared=True, shared_format="fp8", keep_disk_order=True), register=False)
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    for n, regime in ((5, "auto"), (40, "stream"), (300, "auto"), (300, "tensor")):
+        x = torch.randn(n, cfg.hidden, generator=gen, device="cuda").to(torch.bfloat16)
+        y = layer.forward_impl(x, regime=regime)
+        assert layer.device_status() == 0
+        ref, _, _ = _oracle_layer(layer, x.float().cpu().numpy())
+        ref0, _, _ = _oracle_layer(layer, x.float().cpu().numpy(), with_shared=False)
+        assert _rel_l2(ref0, ref) > 5e-2, "the shared expert must matter"
+        assert _rel_l2(y.float().cpu().numpy(), ref) <= LAYER_TOL, (n, regime)
 
 
 def test_bounded_wait_gives_up_and_reports():
@@ -592,6 +713,71 @@ def test_custom_op_equals_direct_call(golden):
     VP.register_custom_op()
     x = torch.from_numpy(golden["x"]).cuda()
     assert torch.equal(torch.ops.chronos_b200.moe_forward(x, 0), layer.forward_impl(x))
+
+
+def test_hooked_vllm_class_with_a_shard_on_disk(golden, tmp_path, monkeypatch):
+    """Stub `vllm` import site + a checkpoint folder holding config.json and one converter-format layer shard: the hooked
+    class builds the folded layer from the shard, `forward` goes through the operator (both names), equals the direct
+    call and the reference's layer output, and compiles with fullgraph=True."""
+    import json
+    import sys
+    import types
+
+    from safetensors.torch import save_file
+
+    from chronos_b200 import vllm_plugin as VP
+
+    h, i, e, k, r, top_k, _ = (int(v) for v in golden["meta"])
+    l_idx = 4
+    prefix = f"model.layers.{l_idx}.mlp"
+    tensors = {}
+    for g, grp in enumerate(golden_groups(golden)):
+        for sfx, arr in grp.items():
+            t = torch.from_numpy(np.ascontiguousarray(arr))
+            if sfx.endswith("_scale") or sfx.startswith("healer."):
+                t = t.view(torch.float8_e4m3fn)
+            tensors[f"{prefix}.chronos_groups.{g}.{sfx}"] = t
+    tensors[f"{prefix}.gate.weight"] = torch.from_numpy(golden["router_w"])
+    tensors[f"{prefix}.gate.e_score_correction_bias"] = torch.from_numpy(golden["e_bias"])
+    save_file(tensors, str(tmp_path / f"chronos-glm53-layer-{l_idx:05d}-of-00008.safetensors"))
+    (tmp_path / "config.json").write_text(json.dumps({
+        "hidden_size": h, "moe_intermediate_size": i, "n_routed_experts": e, "num_experts_per_tok": top_k, "scoring_func": "sigmoid",
+        "routed_scaling_factor": 2.5, "norm_topk_prob": True,
+        "chronos_holographic_moe": {"group_size": k, "svd_rank": r, "key_generator": "torch_cpu_v1"}}))
+
+    class StockMoE(torch.nn.Module):
+        def __init__(self, *a, **kw):
+            super().__init__()
+
+    dsv2 = types.ModuleType("vllm.model_executor.models.deepseek_v2")
+    dsv2.DeepseekV2MoE = StockMoE
+    for name, mod in (("vllm", types.ModuleType("vllm")), ("vllm.model_executor", types.ModuleType("vllm.model_executor")),
+                      ("vllm.model_executor.models", types.ModuleType("vllm.model_executor.models")),
+                      ("vllm.model_executor.models.deepseek_v2", dsv2)):
+        monkeypatch.setitem(sys.modules, name, mod)
+    monkeypatch.setenv("CHRONOS_B200_CKPT", str(tmp_path))
+    assert VP.enable_chronos_b200_vllm_hook() is True
+    cls = dsv2.DeepseekV2MoE
+    moe = cls(config=None, parallel_config=None, quant_config=None, reduce_results=False, prefix=prefix, apply_routed_scale_to_output=False)
+    stock = cls(config=None, prefix="model.layers.0.mlp")  # no shard for layer 0: the stock class comes back
+    assert isinstance(moe, cls) and type(stock) is StockMoE
+    assert moe.load_weights(iter([("x", torch.zeros(1))])) == set()
+    x = torch.from_numpy(golden["x"]).cuda()
+    y_direct = moe.forward_impl(x)
+    assert torch.equal(moe(x), y_direct)
+    assert torch.equal(torch.ops.chronos_glm53.moe_forward(x, l_idx), y_direct)
+    assert _rel_l2(y_direct.cpu().numpy(), golden["ref.layer_y.sigmoid"]) <= LAYER_TOL
+
+    class Wrap(torch.nn.Module):
+        def __init__(self, m):
+            super().__init__()
+            self.m = m
+
+        def forward(self, hs):
+            return self.m(hs) * 2.0
+
+    yc = torch.compile(Wrap(moe), fullgraph=True, backend="eager")(x)
+    assert torch.allclose(yc, 2 * y_direct)
 
 
 def test_bad_arguments_raise(golden):

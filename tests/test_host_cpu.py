@@ -38,10 +38,10 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_layer_struct_matches_header_layout():
-    # 12 four-byte scalars then 32 pointers, no padding surprises
+    # 12 four-byte scalars then 41 pointers, no padding surprises
     import ctypes
 
-    assert ctypes.sizeof(_lib.LayerStruct) == 12 * 4 + 37 * 8
+    assert ctypes.sizeof(_lib.LayerStruct) == 12 * 4 + 41 * 8
     header = (ROOT / "include" / "chronos_b200.h").read_text()
     body = header[header.index("typedef struct chronos_layer {"):header.index("} chronos_layer_t;")]
     names = re.findall(r"(\w+)\s*[;,]", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
@@ -267,6 +267,47 @@ def test_vllm_hook_with_stub_modules(tmp_path, monkeypatch):
     # the operator exists and traces through its fake implementation
     assert hasattr(torch.ops.chronos_b200, "moe_forward")
     VP.register()  # never raises
+
+
+def test_operator_traces_under_fullgraph_compile_and_answers_to_the_reference_name():
+    """The operator is registered as `chronos_b200::moe_forward` and under the reference's own name
+    `chronos_glm53::moe_forward` (chronos_1t/models/patch_glm53_vllm.py:79-93); a module that calls it compiles with
+    `fullgraph=True` through the fake implementation (the check of benchmarks/glm53_vllm_hook_selftest.py:101-116).
+    The live block is a stand-in here: this test is about the operator boundary, not the kernels."""
+    from chronos_b200 import vllm_plugin as VP
+    from chronos_b200.moe import LIVE_BLOCKS
+
+    VP.register_custom_op()
+
+    class Stand:
+        def forward_impl(self, x):
+            return x * 3.0
+
+    LIVE_BLOCKS[901] = Stand()
+    try:
+        x = torch.randn(3, 16)
+        for op in (torch.ops.chronos_b200.moe_forward, torch.ops.chronos_glm53.moe_forward):
+            assert torch.equal(op(x, 901), x * 3.0)
+
+        class Wrap(torch.nn.Module):
+            def forward(self, h):
+                return torch.ops.chronos_glm53.moe_forward(h, 901) * 2.0
+
+        yc = torch.compile(Wrap(), fullgraph=True, backend="eager")(x)
+        assert torch.allclose(yc, x * 6.0)
+    finally:
+        del LIVE_BLOCKS[901]
+
+
+def test_packaging_declares_the_vllm_plugin_entry_point():
+    import importlib
+    import tomllib
+
+    meta = tomllib.loads((ROOT / "pyproject.toml").read_text())
+    eps = meta["project"]["entry-points"]["vllm.general_plugins"]
+    assert eps == {"chronos_b200": "chronos_b200.vllm_plugin:register"}
+    mod, fn = eps["chronos_b200"].split(":")
+    assert callable(getattr(importlib.import_module(mod), fn))
 
 
 def test_config_from_checkpoint(tmp_path):

@@ -1,5 +1,6 @@
 """Pins the CPU oracle against outputs of the reference's own code (fixtures made by golden/make_golden.py)."""
 import numpy as np
+import pytest
 
 from conftest import golden_groups
 from oracle import folded_moe_oracle as O
@@ -181,6 +182,57 @@ def test_sampled_activation_space_oracle_equals_layer_oracle(golden):
     sub = [3, 1]
     got = O.routed_tokens_activation_space(golden["x"][sub], ids[sub], w[sub], groups, h, i, k)
     assert np.linalg.norm(got - ref[sub]) <= 1e-5 * np.linalg.norm(ref[sub])
+
+
+@pytest.mark.parametrize("flavour", ["softmax", "sigmoid"])
+def test_coalesced_routing_keeps_the_stated_invariants(flavour):
+    """The batch-coalesced policy (clean-room: the reference describes it in prose only, so there is nothing to compare
+    bytes with): the anchor of every stream is routed naturally, a draft never leaves its natural top-`pool` and keeps its
+    `keep` best natural experts, pool == k or bonus == 0 give natural routing, and the step touches fewer distinct experts."""
+    rng = np.random.default_rng(7)
+    e, k, tps, n_streams = 288, 8, 3, 40
+    base = rng.standard_normal((n_streams, 1, e)).astype(np.float32)
+    logits = (0.8 * base + 0.6 * rng.standard_normal((n_streams, tps, e)).astype(np.float32)).reshape(-1, e)
+    bias = (rng.standard_normal(e) * 0.05).astype(np.float32)
+    nat_fn = (lambda lg, kk: O.router_softmax_topk(lg, kk)) if flavour == "softmax" else (lambda lg, kk: O.router_sigmoid_topk(lg, bias, kk))
+    nat_ids, nat_w = nat_fn(logits, k)
+    kw = dict(router=flavour, e_bias=bias if flavour != "softmax" else None)
+    pool, keep = 12, 4
+    ids, w = O.router_coalesced(logits, k, tps, pool, keep, 1.0e4, **kw)
+    nat_pool, _ = nat_fn(logits, pool)
+    for t in range(logits.shape[0]):
+        assert len(set(ids[t])) == k
+        if t % tps == 0:
+            assert np.array_equal(ids[t], nat_ids[t]) and np.allclose(w[t], nat_w[t], rtol=1e-6)
+        else:
+            assert set(ids[t]) <= set(nat_pool[t]), "a draft left its natural candidate pool"
+            assert np.array_equal(ids[t, :keep], nat_ids[t, :keep]), "a draft lost one of its best natural experts"
+    for args in ((k, keep, 1.0e4), (pool, keep, 0.0)):  # no pool beyond k, or no bonus: natural routing
+        i2, w2 = O.router_coalesced(logits, k, tps, args[0], args[1], args[2], **kw)
+        assert np.array_equal(np.sort(i2, axis=1), np.sort(nat_ids, axis=1))
+    per_stream = lambda a: np.mean([len(set(a[s * tps:(s + 1) * tps].reshape(-1))) for s in range(n_streams)])
+    assert per_stream(ids) < per_stream(nat_ids) - 0.5, (per_stream(ids), per_stream(nat_ids))
+    tot = w.sum(axis=1)
+    assert np.allclose(tot, 1.0 if flavour == "softmax" else 2.5, rtol=1e-5)
+
+
+def test_block_fp8_dequant_and_shared_expert_match_reference():
+    """Stock 128 x 128 block-FP8 (the reference's shared-expert format): dequantisation bit-exact against
+    `dequant_fp8_block`, the SwiGLU expert built from it against the reference's fp32 evaluation."""
+    from conftest import load_golden
+
+    gold = load_golden("fp8_block_shared")
+    h, i, n_tok = (int(v) for v in gold["meta"])
+    for name in ("gate_proj", "up_proj", "down_proj"):
+        got = O.dequant_fp8_block(gold[f"{name}.weight"], gold[f"{name}.weight_scale_inv"])
+        assert np.array_equal(got.view(np.uint32), gold[f"ref.dequant.{name}"].view(np.uint32)), name
+    ex = {"sh8_gu_w": np.concatenate([gold["gate_proj.weight"], gold["up_proj.weight"]]),
+          "sh8_gu_s": np.concatenate([gold["gate_proj.weight_scale_inv"], gold["up_proj.weight_scale_inv"]]),
+          "sh8_dn_w": gold["down_proj.weight"], "sh8_dn_s": gold["down_proj.weight_scale_inv"]}
+    gu, dn = O.shared_fp8_weights(ex)
+    z = gold["x"] @ gu.T
+    y = (O.silu(z[:, :i]) * z[:, i:]) @ dn.T
+    assert np.linalg.norm(y - gold["ref.shared_y"]) <= 1e-5 * np.linalg.norm(gold["ref.shared_y"])
 
 
 def test_synthetic_fold_is_valid_format():

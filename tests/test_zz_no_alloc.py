@@ -17,7 +17,7 @@ def test_static_scratch_entry_matches_caller_scratch_entry():
 
     lib = _lib.lib()
     cfg = FoldedLayerConfig(hidden=512, inter=256, n_experts=8, group_size=4, rank=16, top_k=2)
-    layer = PackedLayer.synthetic(cfg, seed=21)
+    layer = PackedLayer.synthetic(cfg, seed=21, keep_disk_order=True)  # the probe reads the banks in their on-disk order
     stream = torch.cuda.current_stream().cuda_stream
     for which, (rows, cols) in enumerate(((2 * cfg.inter, cfg.hidden), (cfg.hidden, cfg.inter))):
         scratch = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
@@ -36,7 +36,7 @@ def test_static_scratch_entry_rejects_oversized_matrices():
 
     lib = _lib.lib()
     cfg = FoldedLayerConfig(hidden=4096, inter=1536, n_experts=4, group_size=4, rank=16, top_k=2)  # 3072 x 4096 > limit
-    layer = PackedLayer.synthetic(cfg, seed=22)
+    layer = PackedLayer.synthetic(cfg, seed=22, keep_disk_order=True)
     out = torch.empty((2 * cfg.inter, cfg.hidden), dtype=torch.float32, device="cuda")
     rc = lib.chronos_b200_unfold_expert_fp32_static(layer.ptr, 0, 0, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == -1
