@@ -222,12 +222,12 @@ struct Fp4Args {
     const int32_t* item_start; const int32_t* item_cnt; const int32_t* item_slot; const int32_t* pair_expert;
     int32_t* counters;
     int R, K, n_slots, n_stages;
+    int split_tiles;           // the output rows start at zero (fused decode path): tiles may be split between two CTAs
 };
 
-// The side warps' work (4 warps = one team per CTA; chunks are dealt round-robin over the CTAs, and there are fewer chunks
-// than CTAs in a decode step). Every step requests the healer rows of several 16-row tiles before multiplying any: the
-// work is a handful of dependent round trips to L2 / HBM, and the number of requests in flight is what bounds it. Every
-// healer byte is read exactly once per step.
+// The side warps' work (4 warps = one team per CTA; tasks are dealt round-robin over the CTAs). Every step requests the
+// healer bytes of several tiles before multiplying any: the work is a handful of dependent round trips to L2 / HBM, and
+// the number of requests in flight is what bounds it.
 template <int R16>
 __device__ __forceinline__ void side_healer(const Fp4Args& a, __half (*hsm)[kMaxRank], int sw, int lane) {
     const Fp4Side& sd = a.side;
@@ -237,7 +237,13 @@ __device__ __forceinline__ void side_healer(const Fp4Args& a, __half (*hsm)[kMax
     const int R = a.R, n_chunks = a.counters[3];
     if (n_chunks <= 0) return;
     const int n_tiles16 = R / 16;
-    for (int ch = blockIdx.x; ch < n_chunks; ch += gridDim.x) {
+    // chunks are few (one per distinct expert, about): when there are CTAs to spare a chunk's output rows are cut into
+    // slices handled by different CTAs (each recomputes the chunk's small input product)
+    int n_slices = (int)gridDim.x / n_chunks;
+    n_slices = n_slices < 1 ? 1 : (n_slices > 8 ? 8 : n_slices);
+    const int tiles_per_slice = (n_tiles16 + n_slices - 1) / n_slices;
+    for (int task = blockIdx.x; task < n_chunks * n_slices; task += gridDim.x) {
+        const int ch = task / n_slices, slice = task % n_slices;
         const int start = sd.chunk_start[ch], cnt = sd.chunk_cnt[ch];
         const int e = a.pair_expert[start];
         if (e >= sd.n_experts) continue;  // shared expert: no healer (uniform over the team)
@@ -263,53 +269,57 @@ __device__ __forceinline__ void side_healer(const Fp4Args& a, __half (*hsm)[kMax
                 const uint8_t* v0 = sd.v + ((size_t)e * r + mt * 16 + g) * sd.kc + 16 * q;
                 const uint8_t* v1 = v0 + (size_t)8 * sd.kc;
                 float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                for (int kc0 = 0; kc0 < sd.kc; kc0 += 256) {
-                    uint4 w0[4], w1[4];
-                    uint32_t bf[4][8];
+                // eight 64-column steps of the healer factor are requested at once (the bytes come from HBM); the activations
+                // of a step are fetched one step ahead (a few rows shared by the team's warps: they stay in L1)
+                auto load_act = [&](int kc, uint32_t (&bf)[8]) {
+                    kc = min(kc, sd.kc - 64);
+                    if (sd.kind == 2) {
+                        uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
+                        if (valid) {
+                            u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
+                            u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
+                        }
+                        bf[0] = u0.x; bf[1] = u0.y; bf[2] = u0.z; bf[3] = u0.w; bf[4] = u1.x; bf[5] = u1.y; bf[6] = u1.z; bf[7] = u1.w;
+                    } else if (abytes == 2) {
+                        const uint4 u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
+                        const uint4 u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
+                        const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                        for (int j = 0; j < 8; ++j)
+                            bf[j] = pack_f16x2_sat(__uint_as_float(uu[j] << 16) * inv, __uint_as_float(uu[j] & 0xffff0000u) * inv);
+                    } else {
+                        const float4* src = reinterpret_cast<const float4*>(arow + (size_t)kc * 4);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 f = src[j];
+                            bf[2 * j] = pack_f16x2_sat(f.x * inv, f.y * inv);
+                            bf[2 * j + 1] = pack_f16x2_sat(f.z * inv, f.w * inv);
+                        }
+                    }
+                };
+                for (int kc0 = 0; kc0 < sd.kc; kc0 += 512) {
+                    uint4 w0[8], w1[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
                         const int kc = kc0 + 64 * c;
-                        w0[c] = w1[c] = make_uint4(0u, 0u, 0u, 0u);
+                        w0[c] = w1[c] = make_uint4(0u, 0u, 0u, 0u);  // steps past the end multiply zero healer bytes
                         if (kc < sd.kc) {
                             w0[c] = *reinterpret_cast<const uint4*>(v0 + kc);
                             w1[c] = *reinterpret_cast<const uint4*>(v1 + kc);
                         }
                     }
+                    uint32_t bf[8], bn[8];
+                    load_act(kc0, bf);
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int kc = min(kc0 + 64 * c, sd.kc - 64);  // steps past the end multiply zero healer bytes
-                        if (sd.kind == 2) {
-                            uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
-                            if (valid) {
-                                u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
-                                u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
-                            }
-                            bf[c][0] = u0.x; bf[c][1] = u0.y; bf[c][2] = u0.z; bf[c][3] = u0.w;
-                            bf[c][4] = u1.x; bf[c][5] = u1.y; bf[c][6] = u1.z; bf[c][7] = u1.w;
-                        } else if (abytes == 2) {
-                            const uint4 u0 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2);
-                            const uint4 u1 = *reinterpret_cast<const uint4*>(arow + (size_t)kc * 2 + 16);
-                            const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                bf[c][j] = pack_f16x2_sat(__uint_as_float(uu[j] << 16) * inv, __uint_as_float(uu[j] & 0xffff0000u) * inv);
-                        } else {
-                            const float4* src = reinterpret_cast<const float4*>(arow + (size_t)kc * 4);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float4 f = src[j];
-                                bf[c][2 * j] = pack_f16x2_sat(f.x * inv, f.y * inv);
-                                bf[c][2 * j + 1] = pack_f16x2_sat(f.z * inv, f.w * inv);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < 8; ++c) {
+                        if (c + 1 < 8) load_act(kc0 + 64 * (c + 1), bn);
                         const uint32_t r0[4] = {w0[c].x, w0[c].y, w0[c].z, w0[c].w}, r1[4] = {w1[c].x, w1[c].y, w1[c].z, w1[c].w};
 #pragma unroll
                         for (int s4 = 0; s4 < 4; ++s4)
                             mma_16816(acc, e4m3x2_to_f16x2(r0[s4] & 0xffffu), e4m3x2_to_f16x2(r1[s4] & 0xffffu), e4m3x2_to_f16x2(r0[s4] >> 16),
-                                      e4m3x2_to_f16x2(r1[s4] >> 16), bf[c][2 * s4], bf[c][2 * s4 + 1]);
+                                      e4m3x2_to_f16x2(r1[s4] >> 16), bf[2 * s4], bf[2 * s4 + 1]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) bf[j] = bn[j];
                     }
                 }
 #pragma unroll
@@ -328,8 +338,8 @@ __device__ __forceinline__ void side_healer(const Fp4Args& a, __half (*hsm)[kMax
         }
         const float gs0 = 2 * q < cnt ? sd.pscale[start + 2 * q] : 0.0f, gs1 = 2 * q + 1 < cnt ? sd.pscale[start + 2 * q + 1] : 0.0f;
         const uint8_t* U = sd.u + (size_t)e * R * r;
-        const int t_hi = n_tiles16;
-        for (int jt0 = sw * G; jt0 < t_hi; jt0 += 4 * G) {
+        const int t_lo = slice * tiles_per_slice, t_hi = min(n_tiles16, t_lo + tiles_per_slice);
+        for (int jt0 = t_lo + sw * G; jt0 < t_hi; jt0 += 4 * G) {
             uint32_t wl[G][R16], wh[G][R16];
 #pragma unroll
             for (int t = 0; t < G; ++t) {
@@ -384,18 +394,34 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.R, RB = R / 128, NS = a.K / kF4StageK, S = a.n_stages;
     uint8_t* stages = bimg + (size_t)NS * kF4BStage;  // 6144 * NS is a multiple of 1024 when NS is even; descriptors need 16 B only
+    // Work split. A tile = (work item, 128-row block) = NS stages. Whole tiles per CTA leave the CTAs that get one tile more
+    // than the others running alone at the end (9 or 10 tiles each is a 10 % tail). With `split_tiles` the launch's stage
+    // sequence is cut into equal runs instead: a CTA's first and last tile may be partial (a slice of the contraction), and
+    // the two CTAs that share a tile add their halves into the zero-initialised output (two addends: the sum does not
+    // depend on their order).
     const long n_tiles = (long)a.counters[0] * RB;
-    const long tile_lo = n_tiles * blockIdx.x / gridDim.x, tile_hi = n_tiles * (blockIdx.x + 1) / gridDim.x;
+    const long total_st = n_tiles * NS;
+    long s_lo, s_hi;
+    if (a.split_tiles && total_st / (long)gridDim.x >= NS) {
+        s_lo = total_st * blockIdx.x / gridDim.x;
+        s_hi = total_st * (blockIdx.x + 1) / gridDim.x;
+    } else {
+        s_lo = (n_tiles * blockIdx.x / gridDim.x) * NS;
+        s_hi = (n_tiles * (blockIdx.x + 1) / gridDim.x) * NS;
+    }
+    const long tile_lo = s_lo / NS, tile_hi = s_hi > s_lo ? (s_hi - 1) / NS + 1 : tile_lo;  // tiles [tile_lo, tile_hi)
+    auto st_begin = [&](long tile) { return tile == tile_lo ? (int)(s_lo % NS) : 0; };
+    auto st_end = [&](long tile) { return tile == tile_hi - 1 ? (int)((s_hi - 1) % NS) + 1 : NS; };
     uint64_t* full = bars;
     uint64_t* empty = bars + kF4MaxStages;
     uint64_t* acc_full = bars + 2 * kF4MaxStages;
     uint64_t* acc_empty = bars + 2 * kF4MaxStages + 2;
     uint64_t* b_full = bars + 2 * kF4MaxStages + 4;
     uint64_t* b_empty = bars + 2 * kF4MaxStages + 5;
-    // two issuing threads take alternate stages into separate accumulators (the issuing thread's instruction stream is
-    // the critical path); an odd stage count per tile, or activation scales too large to stay in TMEM, keep one issuer
+    // two issuing threads take the even / odd stages of every tile into separate accumulators (the issuing thread's
+    // instruction stream is the critical path); activation scales too large to stay in TMEM keep one issuer
     const bool sfb_resident = 128 + S * 16 + NS * 16 <= (int)kF4TmemCols;  // activation scales of a whole item fit in TMEM
-    const uint32_t n_issuers = (NS % 2 == 0 && sfb_resident) ? 2u : 1u;   // even NS: a stage keeps its issuer in every tile
+    const uint32_t n_issuers = sfb_resident ? 2u : 1u;
 
     if (tid == 0) {
         for (int s = 0; s < kF4MaxStages; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
@@ -433,7 +459,8 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
                 const int slot = a.item_slot[item];
                 const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
                                       (size_t)rb * NS * kF4AStage;
-                for (int st = 0; st < NS; ++st, ++it) {
+                const int sb = st_begin(tile), se = st_end(tile);
+                for (int st = sb; st < se; ++st, ++it) {
                     const int s = (int)(it % (uint32_t)S);
                     if (!mbar_wait(smem_u32(&empty[s]), ((it / (uint32_t)S) & 1u) ^ 1u)) {
                         atomicOr(a.counters + 2, kStatusFp4Timeout);
@@ -453,14 +480,13 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
         }
     } else if (warp == 1 || warp == 6) {
         // ---------------- MMA issuers ----------------
-        // Issuer A (warp 1) takes the even stages of the CTA's stage sequence, issuer B (warp 6) the odd ones; each owns an
+        // Issuer A (warp 1) takes the even stages of every tile, issuer B (warp 6) the odd ones; each owns an
         // accumulator per buffer and the epilogue adds the two. Scale blocks travel to tensor memory with tcgen05.cp:
         // the bank scales of an issuer's next stage are copied before the MMAs of its current stage are issued (when
         // that stage has already landed), the activation scales of a work item once per item (each issuer its stages).
         const uint32_t me = warp == 1 ? 0u : 1u;
         if (lane == 0 && me < n_issuers) {
             const uint32_t idesc = idesc_nvf4(kF4ARows, kF4BRows);
-            const uint32_t total = (uint32_t)((tile_hi - tile_lo) * NS);
             const uint32_t tmem_sfb_item = tmem_sf0 + S * 16;  // NS x 16 columns when resident
             // descriptor words: smem address >> 4 in the low 14 bits; LBO >> 4 at bit 16; SBO = 128 B, version 1 in the high word
             const uint32_t hi_word = 0x00004008u;
@@ -473,14 +499,15 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
             int cur_item = -1;
             bool live = true;
             uint32_t it0 = 0;       // index of the tile's first stage in the CTA's stage sequence
-            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount, it0 += (uint32_t)NS) {
+            for (long tile = tile_lo; tile < tile_hi && live; ++tile, ++tcount) {
                 const int item = (int)(tile / RB);
+                const int sb = st_begin(tile), se = st_end(tile);
                 if (item != cur_item) {
                     if (!mbar_wait(smem_u32(b_full), n_items_seen & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     if (sfb_resident)
                         for (int st = 0; st < NS; ++st)
-                            if (((it0 + (uint32_t)st) & (n_issuers - 1u)) == me)  // the stages this issuer will multiply
+                            if (((uint32_t)st & (n_issuers - 1u)) == me)  // the stages this issuer will multiply
 #pragma unroll
                                 for (int j = 0; j < 4; ++j)
                                     tc_cp_sf_lo(tmem_sfb_item + 16 * st + 4 * j, sfb_lo0 + (uint32_t)((st * kF4BStage + 512 * j) >> 4));
@@ -493,9 +520,9 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t tmem_d = tmem + buf * 64 + me * 32;
                 bool first = true;
-                for (int st = 0; st < NS; ++st) {
-                    const uint32_t it = it0 + (uint32_t)st;
-                    if ((it & (n_issuers - 1u)) != me) continue;
+                for (int st = sb; st < se; ++st) {
+                    const uint32_t it = it0 + (uint32_t)(st - sb);
+                    if (((uint32_t)st & (n_issuers - 1u)) != me) continue;
                     const uint32_t s = it % (uint32_t)S, ph = (it / (uint32_t)S) & 1u;
                     if (sfa_done <= it) {  // not copied ahead: wait for the stage and copy now
                         if (!mbar_wait(smem_u32(&full[s]), ph)) { atomicOr(a.counters + 2, kStatusFp4Timeout); live = false; break; }
@@ -505,8 +532,8 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
                         for (int j = 0; j < 4; ++j) tc_cp_sf_lo(tmem_sf0 + s * 16 + 4 * j, lo + j * 32);
                         sfa_done = it + 1;
                     }
-                    const uint32_t nx = it + n_issuers;  // this issuer's next stage
-                    if (nx < total && sfa_done <= nx) {
+                    const uint32_t nx = it + n_issuers;  // this issuer's next stage, when it lies in the same tile
+                    if (st + (int)n_issuers < se && sfa_done <= nx) {
                         const uint32_t sn = nx % (uint32_t)S, phn = (nx / (uint32_t)S) & 1u;
                         if (mbar_test(smem_u32(&full[sn]), phn)) {
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -537,6 +564,7 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
                     tc_commit_f4(smem_u32(&acc_full[buf]));
                     if (last_of_item) tc_commit_f4(smem_u32(b_empty));  // every MMA of this issuer that reads the activation image is done
                 }
+                it0 += (uint32_t)(se - sb);
             }
         }
     } else if (warp < 6) {
@@ -553,6 +581,10 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
             const int item = (int)(tile / RB), rb = (int)(tile % RB);
             const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
             const bool sh = slot >= a.n_slots;
+            // a partial tile (a slice of the contraction): which issuers multiplied anything, and the result is added
+            const int sb = st_begin(tile), se = st_end(tile);
+            const bool partial = sb > 0 || se < NS;
+            const bool has_a = n_issuers == 1 || sb + (sb & 1) < se, has_b = n_issuers == 2 && sb + ((sb & 1) ^ 1) < se;
             // operands of the epilogue, fetched while the tile streams
             const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
             float g8[8];
@@ -573,9 +605,14 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
             if (fail) { if (et == 0) atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             uint32_t d[32];
-            tmem_ld32_f4(tmem + buf * 64 + ((uint32_t)(quarter * 32) << 16), d);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (n_issuers == 2) {  // add issuer B's accumulator
+            if (has_a) {
+                tmem_ld32_f4(tmem + buf * 64 + ((uint32_t)(quarter * 32) << 16), d);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            } else {
+#pragma unroll
+                for (int n = 0; n < 32; ++n) d[n] = 0u;
+            }
+            if (has_b) {  // add issuer B's accumulator
                 uint32_t d2[32];
                 tmem_ld32_f4(tmem + buf * 64 + 32 + ((uint32_t)(quarter * 32) << 16), d2);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -595,7 +632,10 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
             if (sh) {  // plain weights: no sign, no transform
 #pragma unroll
                 for (int n = 0; n < 8; ++n)
-                    if (n < cnt) zrow[(size_t)n * R] = v8[n];
+                    if (n < cnt) {
+                        if (partial) atomicAdd(&zrow[(size_t)n * R], v8[n]);
+                        else zrow[(size_t)n * R] = v8[n];
+                    }
                 continue;
             }
             float(*z)[128] = zs[zpar & 1u];
@@ -618,7 +658,9 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
                 if (n < cnt) {
                     const float a0 = z[n][lane], a1 = z[n][32 + lane], a2 = z[n][64 + lane], a3 = z[n][96 + lane];
                     const float lo = a0 + (q0 ? -a1 : a1), hi = a2 + (q0 ? -a3 : a3);
-                    zrow[(size_t)n * R] = (lo + (q1 ? -hi : hi)) * 0.08838834764831845f;
+                    const float out = (lo + (q1 ? -hi : hi)) * 0.08838834764831845f;
+                    if (partial) atomicAdd(&zrow[(size_t)n * R], out);  // the transform is linear: the two slices of a tile just add
+                    else zrow[(size_t)n * R] = out;
                 }
             }
             // no second barrier: the next tile writes the other buffer, and nobody reaches the tile after it before every
@@ -658,6 +700,7 @@ static int launch_bank_fp4_impl(const chronos_layer_t& L, int stage, const Plan&
     a.pair_expert = p.pair_expert;
     a.counters = p.counters;
     a.n_slots = L.n_slots;
+    a.split_tiles = side ? 1 : 0;  // the fused decode path zero-initialises z1 / y1 (front and mid kernels)
     if (side) {
         Fp4Side& sd = a.side;
         sd.kind = stage == 0 ? 1 : 2;

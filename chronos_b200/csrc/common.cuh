@@ -382,6 +382,24 @@ __device__ __forceinline__ float router_choice(const TopkArgs& a, float lg, int 
 // never win a round. When no candidate is left the round emits id -1 with gate 0 - an entry every consumer skips -
 // so no index outside [0, n_experts) is ever formed or used as an address.
 constexpr int kNoExpert = 0x7fffffff;
+
+// Largest of a lane's PL candidates (candidate i = expert i * 32 + lane; absent or spent ones hold -inf) and its expert id,
+// ties to the lower id, kNoExpert when all are -inf. A pairwise tree: the dependent chain is log2(PL) selects long.
+template <int PL>
+__device__ __forceinline__ void lane_argmax(const float (&choice)[PL], int lane, float& best, int& best_e) {
+    float v[PL];
+    int id[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) { v[i] = choice[i]; id[i] = i; }
+#pragma unroll
+    for (int stride = 1; stride < PL; stride *= 2)
+#pragma unroll
+        for (int i = 0; i + stride < PL; i += 2 * stride)
+            if (v[i + stride] > v[i]) { v[i] = v[i + stride]; id[i] = id[i + stride]; }  // equal: the lower index stays
+    best = v[0];
+    best_e = v[0] > -INFINITY ? id[0] * 32 + lane : kNoExpert;
+}
+
 template <int PL>
 __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int lane) {
     float choice[PL];
@@ -399,13 +417,9 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
     float my_val = 0.0f;  // lane j keeps the j-th chosen weight source
     int my_id = -1;
     for (int j = 0; j < a.top_k; ++j) {
-        float best = -INFINITY;
-        int best_e = kNoExpert;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = i * 32 + lane;
-            if (e < a.n_experts && (choice[i] > best)) { best = choice[i]; best_e = e; }
-        }
+        float best;
+        int best_e;
+        lane_argmax<PL>(choice, lane, best, best_e);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best, off);
@@ -443,6 +457,7 @@ __device__ __forceinline__ void topk_one_token_pl(const TopkArgs& a, int t, int 
 }
 __device__ __forceinline__ void topk_one_token(const TopkArgs& a, int t, int lane) {
     if (a.n_experts <= 256) topk_one_token_pl<8>(a, t, lane);
+    else if (a.n_experts <= 320) topk_one_token_pl<10>(a, t, lane);
     else if (a.n_experts <= 512) topk_one_token_pl<16>(a, t, lane);
     else topk_one_token_pl<32>(a, t, lane);
 }

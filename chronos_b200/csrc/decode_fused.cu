@@ -12,8 +12,6 @@
 //
 // Mathematics as in csrc/transform_kernels.cu (ChronosGlm5HolographicExpertGroup.forward_cold_fast,
 // chronos_1t/models/glm5_chronos_moe.py:149-195); routing as chronos_1t/models/glm53_chronos_moe.py:392-399, :456-459.
-#include <cstdlib>
-
 #include "common.cuh"
 
 namespace chronos {
@@ -319,6 +317,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(const Fr
     // ---- phase 2: gate_up input transform of every (pair, 128-column block) into the FP4 activation images ----
     const int H = a.L.hidden, nblk = H / 128;
     const int gw = blockIdx.x * kFrontWarps + warp, n_warps = gridDim.x * kFrontWarps;
+    {   // the gate_up pass adds the slices of tiles it splits between two CTAs: its output rows start at zero
+        float4* z4 = reinterpret_cast<float4*>(a.p.z1);
+        const long n4 = (long)s.n_pairs * 2 * a.L.inter / 4;
+        for (long i = (long)blockIdx.x * kFrontThreads + tid; i < n4; i += (long)gridDim.x * kFrontThreads) z4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     for (int w = gw; w < s.n_pairs * nblk; w += n_warps) {
         const int pair = w / nblk, blk = w % nblk;
         const int t = s.pair_token[pair];
@@ -350,6 +353,10 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(const chronos_l
     if (pair >= p.counters[1]) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int I = L.inter, E = L.n_experts;
+    {   // the down pass adds the slices of tiles it splits between two CTAs: this pair's output row starts at zero
+        float4* y4 = reinterpret_cast<float4*>(p.y1 + (size_t)pair * L.hidden);
+        for (int i = tid; i < L.hidden / 4; i += kMidThreads) y4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     const int e = p.pair_expert[pair];
     const float* z1 = p.z1 + (size_t)pair * 2 * I;
     float ss = 0.0f;
@@ -468,8 +475,6 @@ static int front_token_group(const chronos_layer_t& L, int x_dtype, int n_tokens
 // The fused path serves decode-sized batches of the FP4 streaming regime on layers that carry what its kernels read:
 // re-tiled banks (p.fp4_stream), healer.v_down as on disk, no tail lattice.
 bool decode_fused_fits(const chronos_layer_t& L, int x_dtype, int n_tokens, const Plan& p) {
-    static const bool off = getenv("CHRONOS_B200_UNFUSED_DECODE") != nullptr;  // measurement aid: take the separate-kernel path
-    if (off) return false;
     return p.fp4_stream && p.heal_gu != nullptr && n_tokens >= 1 && n_tokens <= kFrontMaxTokens && L.tail_bits == 0 &&
            L.v_dn != nullptr && L.n_experts <= 1024 && L.inter <= 8192 && front_token_group(L, x_dtype, n_tokens) >= 1;
 }

@@ -337,13 +337,9 @@ __device__ __forceinline__ void natural_ranking(const TopkArgs& a, int t, int la
     my_id = -1;
     my_choice = -INFINITY;
     for (int j = 0; j < n_rounds; ++j) {  // lane j keeps the j-th best candidate
-        float best = -INFINITY;
-        int best_e = kNoExpert;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = i * 32 + lane;
-            if (e < a.n_experts && choice[i] > best) { best = choice[i]; best_e = e; }
-        }
+        float best;
+        int best_e;
+        lane_argmax<PL>(choice, lane, best, best_e);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best, off);
@@ -430,6 +426,7 @@ int launch_coalesced_topk(const chronos_layer_t& L, const float* logits, int n_t
     const unsigned grid = (unsigned)((n_tokens + tps - 1) / tps);
     const int threads = 32 * (tps < 8 ? tps : 8);
     if (L.n_experts <= 256) coalesced_topk_kernel<8><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
+    else if (L.n_experts <= 320) coalesced_topk_kernel<10><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
     else if (L.n_experts <= 512) coalesced_topk_kernel<16><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
     else coalesced_topk_kernel<32><<<grid, threads, 0, st>>>(tk, tps, pool, keep, bonus);
     return check_launch("coalesced_topk");
