@@ -46,8 +46,8 @@ FALLBACK_HBM_GBS = 6650.0
 REFERENCE_BUDGET_S = 150.0   # wall-clock bound of the reference arm's timed steps
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch of bank_fp4_kernel over its algorithmic bytes (bank
 # images + the healer factors its side warps read), from the ncu capture summarised under profiles/ (bank_fp4_kernel,
-# decode layer). Traffic grows in proportion to the bytes a launch streams, so the line reports this ratio times them.
-GU_PASS_TRAFFIC_OVER_ALGORITHMIC = 1.02
+# decode layer: 370.75 MB read + 5.23 MB written for 363.4 MB algorithmic). Traffic grows in proportion to the bytes a launch streams, so the line reports this ratio times them.
+GU_PASS_TRAFFIC_OVER_ALGORITHMIC = 1.035
 
 
 def _peaks() -> tuple[float, str]:
