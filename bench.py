@@ -9,7 +9,8 @@ Plain `python bench.py` (no launcher, N = 1), workload "decode": the decode-shap
 experts + 1 shared, top-8, SwiGLU inter 1536, fold factor 4, healer rank 64, NVFP4 banks; 4 streams x 3 speculative
 tokens, bf16). The line also carries a `prefill` sub-record (8192 tokens, Zipf(1.1) routing, FP4 tensor regime, with the
 empirical FP4 ceiling of the same tile shapes measured in the same run) and an `ep_stack_1gpu` sub-record.
-Under `torch.distributed.run` (any world size, 1 included) or with `--gpus N > 1`, workload "ep_stack": the same layer
+Under `torch.distributed.run` (any world size, 1 included), with `--gpus N > 1`, or with `--gpus 1` on a node that shows more
+than one GPU (the first point of a 1-2-4-8 series; `--workload decode` overrides), workload "ep_stack": the same layer
 stacked 42 deep with experts sharded over the ranks (all-to-all dispatch / combine over NCCL, residual + RMSNorm
 between layers), 4096 tokens per step, strong scaling; at world size 1 the line carries the decode result as a
 `decode_layer` sub-record, and every line carries `parity` (layer 0 of the stack against the CPU oracle on a sample of
@@ -633,7 +634,17 @@ def main() -> None:
     # under the distributed launcher (world size 1 included) and for N > 1 the line is the expert-parallel stack, so that the
     # lines of a 1-2-4-8 GPU series are the same metric; a plain `python bench.py` is the decode layer
     launched = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_RANK" in os.environ
-    workload = args.workload or ("ep_stack" if (args.gpus > 1 or world > 1 or launched) else "decode")
+    # `--gpus 1` on a node that shows several GPUs is the first point of a 1-2-4-8 series: it runs the stack too, so that the
+    # series is one metric (the decode layer rides along as a sub-record); on a one-GPU node it is the decode layer
+    series_point = False
+    if args.workload is None and args.gpus == 1 and not launched:
+        try:
+            import torch
+
+            series_point = torch.cuda.device_count() > 1
+        except Exception:
+            series_point = False
+    workload = args.workload or ("ep_stack" if (args.gpus > 1 or world > 1 or launched or series_point) else "decode")
     if args.impl == "reference":
         if rank == 0:
             with _StdoutToStderr():
