@@ -680,6 +680,15 @@ def main() -> None:
                 res["decode_layer"] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "roofline", "layer_hbm", "stages_us", "e2e")}
             except Exception as exc:
                 res["decode_layer"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            # the reference's CPU path on a bounded sample of the same workload (one layer, 12 tokens, scaled by the depth)
+            try:
+                import argparse as _ap
+
+                ref = run_reference(_ap.Namespace(**{**vars(args), "steps": 1, "no_reference_cuda": True}), "ep_stack")
+                res["cpu_baseline"] = ref["cpu_baseline"]
+            except Exception as exc:
+                res["cpu_baseline"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0:
         print(json.dumps(res), flush=True)
         if res.get("parity", {}).get("rel_l2", 0.0) > 1e-2:

@@ -12,7 +12,7 @@ LIB_PATH = _PKG / "libchronos_b200.so"
 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ROUTER_SOFTMAX_TOPK, ROUTER_SIGMOID_NOAUX, ROUTER_SQRT_SOFTPLUS = 0, 1, 2
-ABI_VERSION = 10
+ABI_VERSION = 11
 REGIME_AUTO, REGIME_STREAM, REGIME_TENSOR, REGIME_STREAM_FP4, REGIME_TENSOR_FP4 = 0, 1, 2, 3, 4
 
 
@@ -35,7 +35,7 @@ class LayerStruct(C.Structure):
             "sh_gu_w", "sh_gu_s", "sh_gu_s2", "sh_dn_w", "sh_dn_s", "sh_dn_s2",
             "gu_t", "dn_t", "sh_gu_t", "sh_dn_t", "v_dn",
             "tail_gu_p", "tail_gu_s", "tail_dn_p", "tail_dn_s",
-            "sh8_gu_w", "sh8_gu_s", "sh8_dn_w", "sh8_dn_s")]
+            "sh8_gu_w", "sh8_gu_s", "sh8_dn_w", "sh8_dn_s", "ut_gu", "ut_dn", "ut_scale")]
     )
 
 

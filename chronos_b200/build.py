@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 OBJ = CSRC / "obj"
 LIB = PKG / "libchronos_b200.so"
 SOURCES = ("api.cu", "probe_kernels.cu", "router.cu", "plan.cu", "transform_kernels.cu", "bank_stream.cu", "bank_gemm.cu",
-           "bank_fp4.cu", "healer_mma.cu", "tail.cu", "decode_fused.cu", "ep_kernels.cu", "shared_fp8.cu")
+           "bank_fp4.cu", "healer_mma.cu", "tail.cu", "decode_fused.cu", "ep_kernels.cu", "shared_fp8.cu", "fused_healer.cu")
 HEADERS = (CSRC / "common.cuh", CSRC / "fp4_mma.cuh", ROOT / "include" / "chronos_b200.h")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 

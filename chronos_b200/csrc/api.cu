@@ -252,6 +252,8 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
     if (int rc = launch_pre_gu(L, x, x_dtype, p, fp4, hmma ? 2 : many, st)) return rc;
     if (hmma)
         if (int rc = launch_healer_in_mma(L, 0, p.x16, kDtypeF16Scaled, p, st)) return rc;
+    if (hmma && wide && healer_fused(L, p))  // the healer factors as an operand tile: the bank pass adds the correction itself
+        if (int rc = launch_heal_image(L, 0, p, st)) return rc;
     if (tail)
         if (int rc = launch_tail_pass(L, 0, p.x16, kDtypeF16Scaled, p, st)) return rc;
     stage_mark(3, st);
@@ -266,8 +268,11 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
                       : (tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st)))) return rc;
     stage_mark(6, st);
     int rc;
-    if (hmma) {
-        rc = launch_down_out_mma(L, p, st);
+    if (hmma && wide && healer_fused(L, p) && combine_gather_fits(L)) {
+        // the down pass already added the healer term: one kernel gathers the token's rows and sums them
+        rc = launch_combine_gather(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
+    } else if (hmma) {
+        rc = launch_down_out_mma(L, p, wide ? 1 : 0, st);
         if (!rc) rc = launch_combine_sum(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     } else {
         rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)
@@ -284,7 +289,7 @@ using namespace chronos;
 
 extern "C" {
 
-int chronos_b200_abi_version(void) { return 10; }
+int chronos_b200_abi_version(void) { return 11; }
 
 const char* chronos_b200_last_error(void) { return g_err; }
 

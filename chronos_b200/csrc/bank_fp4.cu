@@ -767,7 +767,25 @@ struct Fp4WideArgs {
     const int32_t* item_start; const int32_t* item_cnt; const int32_t* item_slot; const int32_t* pair_expert;
     int32_t* counters;
     int R, K, n_slots;
+    // fused healer (NULL / 0 without it): per (expert, 128-row block) a K-major fp16 tile [rank/8][128][8] of the healer's
+    // output factor in the basis of the accumulators, per work item a tile [rank/8][64][8] of its input factors
+    const __half* ut; const __half* himg; int rank;
 };
+
+// kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A = B = fp16 (format 0), K-major, N at [17,23), M at [24,29)
+__device__ __forceinline__ uint32_t idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+// D[128 x N] += A[128 x 16] B[N x 16]^T, fp16 operands from shared memory, accumulating into the same tensor-memory
+// columns the block-scaled MMAs of the tile wrote
+__device__ __forceinline__ void tc_mma_f16_acc(uint32_t tmem_d, uint32_t da_lo, uint32_t da_hi, uint32_t db_lo, uint32_t db_hi,
+                                               uint32_t idesc) {
+    asm volatile(
+        "{\n.reg .b64 a, b;\n.reg .pred p;\nmov.b64 a, {%1, %2};\nmov.b64 b, {%3, %4};\nsetp.eq.u32 p, 0, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, p;\n}" ::"r"(tmem_d),
+        "r"(da_lo), "r"(da_hi), "r"(db_lo), "r"(db_hi), "r"(idesc)
+        : "memory");
+}
 
 
 // NT = bank row blocks multiplied against one activation stage: 1 (two accumulator buffers, the epilogue overlaps the next
@@ -791,6 +809,9 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
     // tiles go round-robin over the CTAs: at any moment the CTAs work on neighbouring tiles, i.e. on the same few work items
     // (whose activation image they share through L2) and on neighbouring row blocks of the same few banks
     const long tile_lo = blockIdx.x, tile_hi = n_tiles, tile_step = gridDim.x;
+    // fused healer: work items before counters[4] belong to routed experts (the shared expert's items come last and have none)
+    const int first_plain = a.ut != nullptr ? a.counters[4] : 0;
+    const uint32_t ut_bytes = 128u * (uint32_t)a.rank * 2u, h_bytes = (uint32_t)kPairsPerWideItem * (uint32_t)a.rank * 2u;
     uint64_t* full = bars;
     uint64_t* empty = bars + kWStages;
     uint64_t* acc_full = bars + 2 * kWStages;
@@ -835,6 +856,21 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
                         bulk_g2s(smem_u32(dst + d * kF4AStage), asrc + ((size_t)d * NS + st) * kF4AStage, kF4AStage, smem_u32(&full[s]));
                     bulk_g2s(smem_u32(dst + NT * kF4AStage), bsrc + (size_t)st * kWideStageBytes, kWideStageBytes, smem_u32(&full[s]));
                 }
+                if (live && item < first_plain) {  // one more ring slot: the healer tiles of the row blocks and the item's factors
+                    const uint32_t s = it % S;
+                    if (!mbar_wait(smem_u32(&empty[s]), ((it / S) & 1u) ^ 1u)) {
+                        atomicOr(a.counters + 2, kStatusFp4Timeout);
+                        break;
+                    }
+                    uint8_t* dst = stages + (size_t)s * STAGE;
+                    const int e = a.pair_expert[a.item_start[item]];
+                    mbar_expect_tx(smem_u32(&full[s]), NT * ut_bytes + h_bytes);
+#pragma unroll
+                    for (int d = 0; d < NT; ++d)
+                        bulk_g2s(smem_u32(dst + d * ut_bytes), a.ut + ((size_t)e * RB + rb + d) * (ut_bytes / 2), ut_bytes, smem_u32(&full[s]));
+                    bulk_g2s(smem_u32(dst + NT * ut_bytes), a.himg + (size_t)item * (h_bytes / 2), h_bytes, smem_u32(&full[s]));
+                    ++it;
+                }
             }
             for (uint32_t back = 0; back < S && back < it; ++back) {  // copies in flight must land before the CTA exits
                 const uint32_t j = it - 1 - back;
@@ -845,6 +881,7 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_nvf4(kF4ARows, kWideRows);
+            const uint32_t idesc_heal = idesc_f16(kF4ARows, kPairsPerWideItem);
             const uint32_t hi_word = 0x00004008u;
             const uint32_t a_lo0 = ((smem_u32(stages) >> 4) & 0x3FFFu) | ((uint32_t)(kF4ARows * 16 >> 4) << 16);
             const uint32_t b_lo0 = ((smem_u32(stages + NT * kF4AStage) >> 4) & 0x3FFFu) | ((uint32_t)(kWideRows * 16 >> 4) << 16);
@@ -885,6 +922,21 @@ __global__ void __launch_bounds__(kWThreads, 1) bank_fp4_wide_kernel(const Fp4Wi
                                                  idesc, sf + SFW * j + 4 * d, sf + SFW * j + 4 * NT);
                     }
                     tc_commit_f4(smem_u32(&empty[s]));
+                }
+                if (live && (int)(tile / RBT) < first_plain) {  // the healer step: rank / 16 MMAs of K = 16 per row block, N = 64
+                    const uint32_t s = it % S;
+                    if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t so = s * (STAGE >> 4);
+                    const uint32_t u_lo = a_lo0 + so;  // same leading-dimension offset as the bank tile: 128 rows x 16 bytes
+                    const uint32_t h_lo = (((smem_u32(stages) + NT * ut_bytes) >> 4) & 0x3FFFu) + so + ((uint32_t)(kPairsPerWideItem * 16 >> 4) << 16);
+#pragma unroll
+                    for (int d = 0; d < NT; ++d)
+                        for (int kk = 0; kk < a.rank / 16; ++kk)
+                            tc_mma_f16_acc(tmem_d + d * kWideRows, u_lo + d * (ut_bytes >> 4) + kk * (2 * kF4ARows * 16 >> 4), hi_word,
+                                           h_lo + kk * (2 * kPairsPerWideItem * 16 >> 4), hi_word, idesc_heal);
+                    tc_commit_f4(smem_u32(&empty[s]));
+                    ++it;
                 }
                 if (live) tc_commit_f4(smem_u32(&acc_full[buf]));
             }
@@ -979,6 +1031,11 @@ int launch_bank_fp4_wide(const chronos_layer_t& L, int stage, const Plan& p, cud
     a.pair_expert = p.pair_expert;
     a.counters = p.counters;
     a.n_slots = L.n_slots;
+    if (healer_fused(L, p)) {
+        a.ut = reinterpret_cast<const __half*>(stage == 0 ? L.ut_gu : L.ut_dn);
+        a.himg = p.himg;
+        a.rank = L.rank;
+    }
     // the gate_up pass (16 stages per tile) multiplies two row blocks per activation stage; the down pass (6 stages per
     // tile) keeps one row block and the overlapped epilogue
     bool two = stage == 0 && (a.R / 128) % 2 == 0;

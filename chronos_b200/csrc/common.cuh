@@ -28,6 +28,7 @@ struct Plan {
     int32_t* ids;          // [T, top_k]
     float* gates;          // [T, top_k]
     int32_t* offsets;      // [E + 2]  first sorted pair of expert e; entry E = shared expert; entry E+1 = total
+    int32_t* cursor;       // [E + 2]  pairs of expert e already placed by the multi-CTA scatter of a large batch
     int32_t* pair_token;   // [P]      token of sorted pair p
     int32_t* pair_expert;  // [P]      expert of sorted pair p (E = shared expert)
     int32_t* pos_of;       // [T * top_k] sorted position of routing entry (t, j); -1 when skipped
@@ -57,6 +58,7 @@ struct Plan {
     float* tail_gu;        // [P, 2I]  tail-lattice term of the gate_up product, natural row order (NULL: layer has no tail)
     float* tail_dn;        // [P, H]   the same for the down product
     float* hsplit;         // [2 stages][kHealSplit][P, r] healer input factors, one partial sum per slice of the contraction
+    __half* himg;          // [gitems][r/8][64][8] the same factors of a work item as a K-major fp16 operand tile (fused healer)
     float* heal_gu;        // [P, 2I]  healer term U_gu (V_gu x) in natural row order (fused decode path only, else NULL)
     float* heal_dn;        // [P, H]   healer term U_down (V_down act) in natural row order (fused decode path only)
     int32_t* pair_item;    // [P]      streaming work item of sorted pair p (fused decode path only)
@@ -77,9 +79,9 @@ struct PlanLayout {
     size_t off_logits, off_ids, off_gates, off_offsets, off_pair_token, off_pair_expert, off_pos_of, off_item_start,
         off_item_cnt, off_item_slot, off_gitem_start, off_gitem_cnt, off_gitem_slot, off_counters, off_xc, off_hmid, off_z1, off_ac, off_hpart, off_y1, off_act, off_act_ss, off_tok_scale, off_pscale_gu,
         off_pscale_dn, off_bq_gu, off_bq_dn, off_yt, off_x16, off_hsplit, off_tail_gu, off_tail_dn, off_x16t, off_heal_gu,
-        off_heal_dn, off_pair_item, off_pair_pos, off_sh8_z, off_sh8_act, off_sh8_y, total;
+        off_heal_dn, off_pair_item, off_pair_pos, off_sh8_z, off_sh8_act, off_sh8_y, off_himg, total;
     int fp4, tiled, wide, tail, sh8;
-    int max_pairs, max_items, max_gitems;
+    int max_pairs, max_items, max_gitems, n_bins_padded;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -95,6 +97,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
                  I = (size_t)L.inter, r = (size_t)L.rank;
     const size_t P = T * k + (shared_is_nvfp4(L) ? T : 0);
     p.max_pairs = (int)P;
+    p.n_bins_padded = (int)(E + 2);
     p.max_items = (int)((size_t)L.n_slots + 1 + P / kPairsPerItem + 1);
     // FP4 activation images exist only for batch shapes the streaming regime serves and layers that carry re-tiled banks
     p.fp4 = (L.gu_t != nullptr && L.dn_t != nullptr && H % 256 == 0 && I % 256 == 0 && H <= 7168 && I <= 7168 &&
@@ -108,7 +111,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_logits = take(T * E * 4);
     p.off_ids = take(T * k * 4);
     p.off_gates = take(T * k * 4);
-    p.off_offsets = take((E + 2) * 4);
+    p.off_offsets = take(2 * (E + 2) * 4);  // prefix sums, then the scatter cursors of the multi-CTA plan
     p.off_pair_token = take(P * 4);
     p.off_pair_expert = take(P * 4);
     p.off_pos_of = take(T * k * 4);
@@ -141,6 +144,7 @@ inline PlanLayout plan_layout(const chronos_layer_t& L, int n_tokens) {
     p.off_yt = take(p.tiled ? P * H * 4 : 0);
     p.off_x16 = take(p.tiled ? T * H * 2 : 0);
     p.off_hsplit = take(p.tiled ? 2 * kHealSplit * P * r * 4 : 0);
+    p.off_himg = take((p.wide && L.ut_gu != nullptr) ? (size_t)p.max_gitems * kPairsPerWideItem * r * 2 : 0);
     p.off_heal_gu = take(p.fp4 ? P * 2 * I * 4 : 0);
     p.off_heal_dn = take(p.fp4 ? P * H * 4 : 0);
     p.off_pair_item = take(p.fp4 ? P * 4 : 0);
@@ -164,6 +168,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.ids = (int32_t*)(b + l.off_ids);
     p.gates = (float*)(b + l.off_gates);
     p.offsets = (int32_t*)(b + l.off_offsets);
+    p.cursor = p.offsets + l.n_bins_padded;
     p.pair_token = (int32_t*)(b + l.off_pair_token);
     p.pair_expert = (int32_t*)(b + l.off_pair_expert);
     p.pos_of = (int32_t*)(b + l.off_pos_of);
@@ -193,6 +198,7 @@ inline Plan plan_bind(const PlanLayout& l, void* ws) {
     p.yt = l.tiled ? (float*)(b + l.off_yt) : nullptr;
     p.x16 = l.tiled ? (__half*)(b + l.off_x16) : nullptr;
     p.hsplit = l.tiled ? (float*)(b + l.off_hsplit) : nullptr;
+    p.himg = l.wide ? (__half*)(b + l.off_himg) : nullptr;
     p.heal_gu = l.fp4 ? (float*)(b + l.off_heal_gu) : nullptr;
     p.heal_dn = l.fp4 ? (float*)(b + l.off_heal_dn) : nullptr;
     p.pair_item = l.fp4 ? (int32_t*)(b + l.off_pair_item) : nullptr;
@@ -246,7 +252,13 @@ int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream
 int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
 int launch_tail_add(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_bank_fp4_wide(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st);
+int launch_heal_image(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st);
+bool healer_fused(const chronos_layer_t& L, const Plan& p);
+int launch_mid_fused(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
+bool combine_gather_fits(const chronos_layer_t& L);
+int launch_combine_gather(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
+                          int y_dtype, cudaStream_t st);
 int launch_combine_sum(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
                        int y_dtype, cudaStream_t st);
 int launch_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
@@ -349,11 +361,11 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     v[0] = a + c; v[1] = b + d; v[2] = a - c; v[3] = b - d;
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const bool hi = (lane & m) != 0;
+        const float sg = (lane & m) ? -1.0f : 1.0f;  // partner - own in the upper half, own + partner in the lower: one FMA
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-            v[i] = hi ? (o - v[i]) : (v[i] + o);
+            v[i] = __fmaf_rn(v[i], sg, o);
         }
     }
 #pragma unroll

@@ -15,6 +15,11 @@
 
 namespace chronos {
 
+__device__ __forceinline__ void cp_async16_g2s(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+
 // ---------------------------------------------------------------------------------------------------------------
 // Healer input factor of a tensor-regime work item (one expert, up to 128 sorted pairs):
 //   out[slice][pair, c] = (1 / g_pair) * sum_{k in slice} V[e, c, k] * X[row(pair), k]      c < r, fp32 partial sums
@@ -121,6 +126,165 @@ __global__ void __launch_bounds__(256) healer_in_mma_kernel(const HealInArgs a) 
     }
 }
 
+// The same product for fp16 rows that are already divided by the pair's scale (the FP4 tensor regime hands both stages
+// over in that form), with the operands staged through shared memory by a ring of asynchronous 16-byte copies:
+// kRingStages - 1 steps of 64 columns are in flight while one is multiplied, so the kernel no longer waits a full
+// L2 round trip per step, every activation row is fetched once per CTA instead of once per rank-row warp, and the loads
+// in flight do not cost registers. Fragment ownership as above; a step's tile is X [ROWS pairs][64 fp16] with rows
+// padded to 144 bytes and V [r][64 e4m3] unpadded (both conflict-free for the 16-byte fragment reads).
+constexpr int kRingStages = 4;
+constexpr int kRingXStride = 144;
+
+template <int MT, int ROWS>  // rank / 16; pairs of a work item at most (64 or 128)
+__global__ void __launch_bounds__(256) healer_in_ring_kernel(const HealInArgs a) {
+    extern __shared__ __align__(16) uint8_t ring[];
+    constexpr int r = MT * 16;
+    constexpr int NG = 8 / MT, NTW = (ROWS / 8) / NG;
+    constexpr int kXBytes = ROWS * kRingXStride, kStage = kXBytes + r * 64;
+    constexpr int XJ = ROWS * 8 / 256;                 // 16-byte activation chunks per thread and step
+    constexpr int VJ = (r * 4 + 255) / 256;            // healer chunks per thread and step
+    const int item = blockIdx.x;
+    if (item >= a.counters[3]) return;
+    const int start = a.gitem_start[item], cnt = a.gitem_cnt[item];
+    const int e = a.pair_expert[start];
+    if (e >= a.n_experts) return;     // shared expert: no healer
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q = lane & 3;
+    const int mt = warp % MT, ng = warp / MT;
+    const int K = a.K;
+    const int ntiles = (cnt + 7) >> 3;
+    const int k_lo = (int)blockIdx.y * (K / a.n_split), n_steps = (K / a.n_split) / 64;
+    const uint8_t* xsrc[XJ];
+    bool xok[XJ];
+#pragma unroll
+    for (int j = 0; j < XJ; ++j) {
+        const int c = tid + 256 * j, row = c >> 3;
+        xok[j] = row < cnt;
+        const int pair = start + (xok[j] ? row : 0);
+        const size_t src_row = a.row_of_pair ? (size_t)a.row_of_pair[pair] : (size_t)pair;
+        xsrc[j] = reinterpret_cast<const uint8_t*>(a.x) + (src_row * K + k_lo + (c & 7) * 8) * 2;
+    }
+    const uint8_t* vsrc = a.v + (size_t)e * r * K + k_lo;
+    auto issue = [&](int step) {
+        uint8_t* slot = ring + (step % kRingStages) * kStage;
+#pragma unroll
+        for (int j = 0; j < XJ; ++j) {
+            const int c = tid + 256 * j;
+            if (xok[j]) cp_async16_g2s(slot + (c >> 3) * kRingXStride + (c & 7) * 16, xsrc[j] + (size_t)step * 128);
+        }
+#pragma unroll
+        for (int j = 0; j < VJ; ++j) {
+            const int c = tid + 256 * j;
+            if (c < r * 4) cp_async16_g2s(slot + kXBytes + c * 16, vsrc + (size_t)(c >> 2) * K + step * 64 + (c & 3) * 16);
+        }
+    };
+    // rows of absent pairs are never copied: clear them once so that the unused MMA columns stay finite
+    for (int i = tid; i < kRingStages * ROWS * (kRingXStride / 16); i += 256) {
+        const int stg = i / (ROWS * (kRingXStride / 16)), rem = i % (ROWS * (kRingXStride / 16));
+        if (rem / (kRingXStride / 16) >= cnt)
+            *reinterpret_cast<uint4*>(ring + stg * kStage + rem * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    float acc[NTW][4];
+#pragma unroll
+    for (int i = 0; i < NTW; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+#pragma unroll
+    for (int s0 = 0; s0 < kRingStages - 1; ++s0) {
+        if (s0 < n_steps) issue(s0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int step = 0; step < n_steps; ++step) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kRingStages - 2) : "memory");
+        __syncthreads();  // the step's tile has landed for every thread; the slot refilled next was read one step ago
+        if (step + kRingStages - 1 < n_steps) issue(step + kRingStages - 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint8_t* slot = ring + (step % kRingStages) * kStage;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(slot + kXBytes + (mt * 16 + g) * 64 + 16 * q);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(slot + kXBytes + (mt * 16 + g + 8) * 64 + 16 * q);
+        const uint32_t r0[4] = {w0.x, w0.y, w0.z, w0.w}, r1[4] = {w1.x, w1.y, w1.z, w1.w};
+        uint32_t af[4][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            af[s][0] = e4m3x2_to_f16x2(r0[s] & 0xffffu);
+            af[s][1] = e4m3x2_to_f16x2(r1[s] & 0xffffu);
+            af[s][2] = e4m3x2_to_f16x2(r0[s] >> 16);
+            af[s][3] = e4m3x2_to_f16x2(r1[s] >> 16);
+        }
+#pragma unroll
+        for (int i = 0; i < NTW; ++i) {
+            if (ng + i * NG >= ntiles) continue;  // warp-uniform
+            const uint4* src = reinterpret_cast<const uint4*>(slot + ((ng + i * NG) * 8 + g) * kRingXStride + 32 * q);
+            const uint4 u0 = src[0], u1 = src[1];
+            const uint32_t bf[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int s = 0; s < 4; ++s) mma_16816(acc[i], af[s][0], af[s][1], af[s][2], af[s][3], bf[2 * s], bf[2 * s + 1]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NTW; ++i) {
+        if (ng + i * NG >= ntiles) continue;
+        const int n0 = (ng + i * NG) * 8 + 2 * q;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + (j & 1), c = mt * 16 + g + (j >> 1) * 8;
+            if (n < cnt) a.out[blockIdx.y * a.split_stride + (size_t)(start + n) * r + c] = acc[i][j];
+        }
+    }
+}
+
+template <int MT, int ROWS>
+static int launch_healer_ring(const HealInArgs& a, dim3 grid, cudaStream_t st) {
+    const size_t smem = (size_t)kRingStages * (ROWS * kRingXStride + MT * 16 * 64);
+    if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(healer_in_ring_kernel<MT, ROWS>), smem, "healer_in_ring")) return rc;
+    healer_in_ring_kernel<MT, ROWS><<<grid, 256, smem, st>>>(a);
+    return check_launch("healer_in_ring");
+}
+
+// Fused healer of the FP4 tensor regime: the healer input factors of a work item (the sum, in slice order, of the
+// partial sums above; still divided by the pair scale) times the layer's power-of-two tile scale, as the K-major fp16
+// operand tile the bank pass multiplies with the healer tiles: half (c, pos) at (c / 8) * 512 + pos * 8 + c % 8.
+// Positions past the item's count are zero. One CTA per work item; the shared expert has no healer.
+__global__ void __launch_bounds__(256) heal_image_kernel(const float* __restrict__ hsplit, size_t split_stride, int n_split, int r,
+                                                         const float* __restrict__ tile_scale, const int32_t* __restrict__ gitem_start,
+                                                         const int32_t* __restrict__ gitem_cnt, const int32_t* __restrict__ pair_expert,
+                                                         const int32_t* __restrict__ counters, int n_experts, __half* __restrict__ himg) {
+    const int item = blockIdx.x;
+    if (item >= counters[3]) return;
+    const int start = gitem_start[item], cnt = gitem_cnt[item];
+    if (pair_expert[start] >= n_experts) return;
+    const float k = *tile_scale;
+    __half* img = himg + (size_t)item * kPairsPerWideItem * r;
+    for (int idx = threadIdx.x * 4; idx < kPairsPerWideItem * r; idx += 256 * 4) {
+        const int pos = idx / r, c = idx % r;  // 4 consecutive rank columns of one position
+        float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (pos < cnt) {
+            float4 part[kHealSplit];
+#pragma unroll
+            for (int ks = 0; ks < kHealSplit; ++ks) {
+                part[ks] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (ks < n_split) part[ks] = *reinterpret_cast<const float4*>(hsplit + ks * split_stride + (size_t)(start + pos) * r + c);
+            }
+            acc4 = part[0];
+#pragma unroll
+            for (int ks = 1; ks < kHealSplit; ++ks) {
+                acc4.x += part[ks].x; acc4.y += part[ks].y; acc4.z += part[ks].z; acc4.w += part[ks].w;
+            }
+        }
+        const float h4[4] = {acc4.x * k, acc4.y * k, acc4.z * k, acc4.w * k};
+        store_half4(img + (c >> 3) * (kPairsPerWideItem * 8) + pos * 8 + (c & 7), h4);
+    }
+}
+
+int launch_heal_image(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st) {
+    const size_t sstride = (size_t)p.max_pairs * L.rank;
+    const int kdim = stage == 0 ? L.hidden : L.inter;
+    const int n_split = kdim % (64 * kHealSplit) == 0 ? kHealSplit : (kdim % 128 == 0 ? 2 : 1);
+    heal_image_kernel<<<(unsigned)p.max_gitems, 256, 0, st>>>(p.hsplit + (size_t)stage * kHealSplit * sstride, sstride, n_split, L.rank,
+                                                              L.ut_scale + stage, p.gitem_start, p.gitem_cnt, p.pair_expert, p.counters,
+                                                              L.n_experts, p.himg);
+    return check_launch("heal_image");
+}
+
 int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st) {
     HealInArgs a{};
     a.v = stage == 0 ? L.v_gu : L.v_dn;
@@ -140,6 +304,15 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
     a.r = L.rank;
     a.n_experts = L.n_experts;
     const dim3 grid((unsigned)p.max_gitems, (unsigned)a.n_split);
+    if (x_dtype == kDtypeF16Scaled && (a.K / a.n_split) % 64 == 0) {
+        const bool small = p.gitem_pairs <= 64;
+        switch (L.rank / 16) {
+            case 1: return small ? launch_healer_ring<1, 64>(a, grid, st) : launch_healer_ring<1, 128>(a, grid, st);
+            case 2: return small ? launch_healer_ring<2, 64>(a, grid, st) : launch_healer_ring<2, 128>(a, grid, st);
+            case 4: return small ? launch_healer_ring<4, 64>(a, grid, st) : launch_healer_ring<4, 128>(a, grid, st);
+            default: return small ? launch_healer_ring<8, 64>(a, grid, st) : launch_healer_ring<8, 128>(a, grid, st);
+        }
+    }
     switch (L.rank / 16) {
         case 1: healer_in_mma_kernel<1><<<grid, 256, 0, st>>>(a); break;
         case 2: healer_in_mma_kernel<2><<<grid, 256, 0, st>>>(a); break;
@@ -165,11 +338,8 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
 constexpr int kOutThreads = 512;
 constexpr int kGroupsPerItem = 128 / kGroupPairs;
 
-__device__ __forceinline__ void cp_async16_g2s(void* smem_dst, const void* gsrc) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-
-template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
+// FUSED: the bank pass already added the healer term to its output (healer tiles in the layer): no products here.
+template <int MODE, int R16, bool WIDE, bool FUSED>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
 __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
     __shared__ __align__(16) __half hsm[kGroupPairs][kMaxRank];
@@ -216,7 +386,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
             const float* hs = p.hsplit + (size_t)MODE * kHealSplit * sstride;
             const int kdim = MODE == 0 ? H : I;
             const int n_split = kdim % (64 * kHealSplit) == 0 ? kHealSplit : (kdim % 128 == 0 ? 2 : 1);
-            if (tid < PG * (r / 4)) {
+            if (!FUSED && tid < PG * (r / 4)) {
                 const int n = tid / (r / 4), c4 = (tid % (r / 4)) * 4;
                 float4 part[kHealSplit];
 #pragma unroll
@@ -243,21 +413,21 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
             uint32_t bf[R16][2];
 #pragma unroll
             for (int s = 0; s < R16; ++s) {
-                const uint2 v = *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s]);
+                const uint2 v = FUSED ? make_uint2(0u, 0u) : *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s]);
                 bf[s][0] = v.x;
                 bf[s][1] = v.y;
             }
             // software pipeline over the 16-row tiles of this warp: the healer rows and permutation entries of the next
             // tile are requested before the current tile is multiplied (each request is a full L2 round trip)
             constexpr int NH = MODE == 0 ? 2 : 1;
-            uint32_t w_lo[NH][R16], w_hi[NH][R16], ro_lo[NH], ro_hi[NH];
             auto fetch = [&](int jt, uint32_t (&wl)[NH][R16], uint32_t (&wh)[NH][R16], uint32_t (&rl)[NH], uint32_t (&rh)[NH]) {
 #pragma unroll
                 for (int half = 0; half < NH; ++half) {
                     const int row_lo = half * I + jt * 16 + g, row_hi = row_lo + 8;
                     const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)row_lo * r + 4 * R16 * q);
                     const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)row_hi * r + 4 * R16 * q);
-                    if constexpr (R16 % 4 == 0) {
+                    if constexpr (FUSED) {
+                    } else if constexpr (R16 % 4 == 0) {
 #pragma unroll
                         for (int s = 0; s < R16; s += 4) {
                             const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s), b4 = *reinterpret_cast<const uint4*>(u_hi + s);
@@ -272,23 +442,22 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                     rh[half] = rout[row_hi];
                 }
             };
-            if (warp < NR / 16) fetch(warp, w_lo, w_hi, ro_lo, ro_hi);
-            for (int jt = warp; jt < NR / 16; jt += NW) {
-                uint32_t n_lo[NH][R16], n_hi[NH][R16], nr_lo[NH], nr_hi[NH];
-                const bool more = jt + NW < NR / 16;
-                if (more) fetch(jt + NW, n_lo, n_hi, nr_lo, nr_hi);
+            // DEPTH tiles are in flight per warp (register buffers, rotated by unrolling): with one tile in flight an
+            // iteration lasted a full L2 round trip whatever it computed
+            auto compute = [&](int jt, const uint32_t (&wl)[NH][R16], const uint32_t (&wh)[NH][R16], const uint32_t (&rl)[NH],
+                               const uint32_t (&rh)[NH]) {
                 const int row_lo = jt * 16 + g, row_hi = row_lo + 8;
                 float zz[NH][4];
 #pragma unroll
                 for (int half = 0; half < NH; ++half) {
                     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                    for (int s = 0; s < R16; ++s)
-                        mma_16816(d, e4m3x2_to_f16x2(w_lo[half][s] & 0xffffu), e4m3x2_to_f16x2(w_hi[half][s] & 0xffffu),
-                                  e4m3x2_to_f16x2(w_lo[half][s] >> 16), e4m3x2_to_f16x2(w_hi[half][s] >> 16), bf[s][0], bf[s][1]);
+                    for (int s = 0; s < (FUSED ? 0 : R16); ++s)
+                        mma_16816(d, e4m3x2_to_f16x2(wl[half][s] & 0xffffu), e4m3x2_to_f16x2(wh[half][s] & 0xffffu),
+                                  e4m3x2_to_f16x2(wl[half][s] >> 16), e4m3x2_to_f16x2(wh[half][s] >> 16), bf[s][0], bf[s][1]);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {  // d[j]: row (j < 2 ? lo : hi), pair 2q + (j & 1)
-                        const uint32_t ro = j < 2 ? ro_lo[half] : ro_hi[half];
+                        const uint32_t ro = j < 2 ? rl[half] : rh[half];
                         const int n = 2 * q + (j & 1);
                         float v = 0.0f;
                         if (n < PG) v = vec[(size_t)n * VL + (ro & 0x7fffu)];
@@ -306,13 +475,20 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                         p.yt[(size_t)(p0 + n) * H + row] = zz[0][j];
                     }
                 }
-                if (more) {
+            };
+            constexpr int DEPTH = MODE == 0 ? 2 : 3;
+            const int NT = NR / 16;
+            uint32_t w_lo[DEPTH][NH][R16], w_hi[DEPTH][NH][R16], ro_lo[DEPTH][NH], ro_hi[DEPTH][NH];
 #pragma unroll
-                    for (int half = 0; half < NH; ++half) {
+            for (int dd = 0; dd < DEPTH; ++dd)
+                if (warp + dd * NW < NT) fetch(warp + dd * NW, w_lo[dd], w_hi[dd], ro_lo[dd], ro_hi[dd]);
+            for (int jt0 = warp; jt0 < NT; jt0 += DEPTH * NW) {
 #pragma unroll
-                        for (int s = 0; s < R16; ++s) { w_lo[half][s] = n_lo[half][s]; w_hi[half][s] = n_hi[half][s]; }
-                        ro_lo[half] = nr_lo[half];
-                        ro_hi[half] = nr_hi[half];
+                for (int dd = 0; dd < DEPTH; ++dd) {
+                    const int jt = jt0 + dd * NW;
+                    if (jt < NT) {  // warp-uniform
+                        compute(jt, w_lo[dd], w_hi[dd], ro_lo[dd], ro_hi[dd]);
+                        if (jt + DEPTH * NW < NT) fetch(jt + DEPTH * NW, w_lo[dd], w_hi[dd], ro_lo[dd], ro_hi[dd]);
                     }
                 }
             }
@@ -358,7 +534,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
     }
 }
 
-template <int MODE, bool WIDE>
+template <int MODE, bool WIDE, bool FUSED>
 static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
     const size_t smem = MODE == 0 ? (size_t)kGroupPairs * (2 * L.inter + L.inter) * 4 : (size_t)kGroupPairs * L.hidden * 4;
     if (smem > 220 * 1024) {
@@ -371,8 +547,8 @@ static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStrea
     const unsigned grid = most < resident ? most : resident;
     int rc = CHRONOS_OK;
 #define CHRONOS_PG(R)                                                                                                   \
-    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pair_group_out_kernel<MODE, R, WIDE>), smem, "pair_group_out"); \
-    if (rc == CHRONOS_OK) pair_group_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
+    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pair_group_out_kernel<MODE, R, WIDE, FUSED>), smem, "pair_group_out"); \
+    if (rc == CHRONOS_OK) pair_group_out_kernel<MODE, R, WIDE, FUSED><<<grid, kOutThreads, smem, st>>>(L, p);
     switch (L.rank / 16) {
         case 1: CHRONOS_PG(1) break;
         case 2: CHRONOS_PG(2) break;
@@ -388,11 +564,21 @@ bool healer_mma_fits(const chronos_layer_t& L) {
     return L.v_dn != nullptr && (size_t)kGroupPairs * 3 * L.inter * 4 <= 220 * 1024 && (size_t)kGroupPairs * L.hidden * 4 <= 220 * 1024;
 }
 
-int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
-    if (int rc = wide ? launch_pair_groups<0, true>(L, p, st) : launch_pair_groups<0, false>(L, p, st)) return rc;
-    return wide ? launch_healer_in_mma(L, 1, p.ac, kDtypeF16Scaled, p, st) : launch_healer_in_mma(L, 1, p.act, CHRONOS_DTYPE_F32, p, st);
+// The fused healer needs the FP4 tensor regime, the layer's healer tiles and a rank that fits a ring slot of the bank pass.
+bool healer_fused(const chronos_layer_t& L, const Plan& p) {
+    return p.fp4_wide && p.himg != nullptr && L.ut_gu != nullptr && L.ut_dn != nullptr && L.ut_scale != nullptr && L.rank <= 64;
 }
 
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pair_groups<1, false>(L, p, st); }
+int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
+    const bool fused = wide && healer_fused(L, p);
+    if (int rc = fused ? launch_mid_fused(L, p, st)
+                       : (wide ? launch_pair_groups<0, true, false>(L, p, st) : launch_pair_groups<0, false, false>(L, p, st))) return rc;
+    if (int rc = wide ? launch_healer_in_mma(L, 1, p.ac, kDtypeF16Scaled, p, st) : launch_healer_in_mma(L, 1, p.act, CHRONOS_DTYPE_F32, p, st)) return rc;
+    return fused ? launch_heal_image(L, 1, p, st) : CHRONOS_OK;
+}
+
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
+    return (wide && healer_fused(L, p)) ? launch_pair_groups<1, false, true>(L, p, st) : launch_pair_groups<1, false, false>(L, p, st);
+}
 
 }  // namespace chronos

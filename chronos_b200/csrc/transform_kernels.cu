@@ -179,32 +179,73 @@ int launch_token_scale(const void* x, int x_dtype, int n_tokens, int hidden, flo
     return check_launch("token_scale");
 }
 
-// FP4 tensor regime: one CTA per (work item of up to 64 pairs, 256-column stage) builds the stage's activation image
-// (192 rows: 3 residual terms x 64 positions) in shared memory - warp tasks = (position, 128-block) - and copies the rows
-// of present pairs out in 16-byte units, 512 consecutive bytes per warp. Grid-stride over the device-side item count.
-__global__ void __launch_bounds__(512) pre_gu_wide_kernel(chronos_layer_t L, Plan p) {
-    __shared__ __align__(16) uint8_t img[kWideStageBytes];
+// FP4 tensor regime: the activation images of a work item (up to 64 pairs of one expert; per 256-column stage 192 rows =
+// 3 residual terms x 64 positions). One CTA per (work item, group of kPreGuGroup positions): the group's token rows
+// (fp16, already divided by the token scale) are staged in shared memory by asynchronous copies, so that the gather of
+// the key permutation - which reaches anywhere in the row - costs shared-memory reads instead of one L1 sector per
+// element; warp tasks = (position, 128-block): gather + sign, FWHT, sign, three FP4 terms written straight into the
+// image (2 bytes per lane; the positions of a group fill each 16-byte row unit's neighbours, so the sectors merge in L2).
+// Rows of absent positions are not written: their MMA columns are never read back.
+constexpr int kPreGuGroup = 4;
+constexpr int kPreGuThreads = 512;
+
+__global__ void __launch_bounds__(kPreGuThreads) pre_gu_wide_kernel(chronos_layer_t L, Plan p) {
+    extern __shared__ __align__(16) __half rows_s[];  // [kPreGuGroup][hidden]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int NS = L.hidden / 256, n_items = p.counters[3];
-    for (int w = blockIdx.x; w < n_items * NS; w += gridDim.x) {
-        const int item = w / NS, st = w % NS;
-        const int start = p.gitem_start[item], cnt = p.gitem_cnt[item];
+    const int H = L.hidden, NB = H / 128, n_items = p.counters[3];
+    constexpr int kGroups = kPairsPerWideItem / kPreGuGroup;
+    for (int w = blockIdx.x; w < n_items * kGroups; w += gridDim.x) {
+        const int grp = w / n_items, item = w % n_items;  // item fastest: neighbouring CTAs get comparable work
+        const int start = p.gitem_start[item];
+        const int cnt = min(kPreGuGroup, p.gitem_cnt[item] - grp * kPreGuGroup);
+        if (cnt <= 0) continue;
         const int e = p.pair_expert[start];
-        for (int task = warp; task < 2 * cnt; task += 16) {
-            const int pos = task >> 1, half = task & 1, blk = st * 2 + half;
-            const int pair = start + pos, t = p.pair_token[pair];
-            float v[4];
-            transform_gu_block(L, p.x16, kDtypeF16Scaled, t, e, blk, lane, v);  // rows already divided by the token scale
-            if (blk == 0 && lane == 0) p.pscale_gu[pair] = p.tok_scale[t];
-            quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img, half, pos);
+        __syncthreads();  // the rows of the previous group are no longer read
+        const int units = H / 8;  // 16-byte units of a row
+        for (int u = tid; u < cnt * units; u += kPreGuThreads) {
+            const int n = u / units, c = u % units;
+            const int t = p.pair_token[start + grp * kPreGuGroup + n];
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(rows_s + (size_t)n * H + c * 8)),
+                         "l"(p.x16 + (size_t)t * H + c * 8) : "memory");
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
-        uint4* dst = reinterpret_cast<uint4*>(p.bq_gu + (size_t)w * kWideStageBytes);
-        const uint4* src = reinterpret_cast<const uint4*>(img);
-        for (int u = tid; u < kWideRows * 8; u += 512)            // nibble rows: unit u = chunk * 192 + row
-            if (((u % kWideRows) & (kPairsPerWideItem - 1)) < cnt) dst[u] = src[u];
-        for (int u = kWideRows * 8 + tid; u < kWideStageBytes / 16; u += 512) dst[u] = src[u];  // scale blocks
-        __syncthreads();
+        // warp -> (position n, 128-blocks blk0, blk0 + W, ...): everything that depends on the position alone is set up once
+        constexpr int W = kPreGuThreads / 32 / kPreGuGroup;
+        const int n = warp % kPreGuGroup;
+        if (n < cnt) {
+            const int pos = grp * kPreGuGroup + n, pair = start + pos;
+            const __half* row = rows_s + n * H;
+            const bool plain = e >= L.n_experts;  // shared expert: plain weights, identity keys
+            const uint16_t* cin = L.gu_cin + (size_t)(plain ? 0 : e) * H + lane * 4;
+            const uint32_t* cs2 = L.gu_cs2 + (size_t)(plain ? 0 : e) * (H / 32) + lane / 8;
+            uint8_t* img0 = p.bq_gu + (size_t)item * (H / 256) * kWideStageBytes;
+            if (warp < kPreGuGroup && lane == 0) p.pscale_gu[pair] = p.tok_scale[p.pair_token[pair]];
+            for (int blk = warp / kPreGuGroup; blk < NB; blk += W) {
+                float v[4];
+                if (plain) {
+                    const uint2 raw = *reinterpret_cast<const uint2*>(row + blk * 128 + lane * 4);
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                    v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+                } else {
+                    const uint2 ce = *reinterpret_cast<const uint2*>(cin + blk * 128);
+                    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float xv = __half2float(row[ent[i] & 0x7fffu]);
+                        v[i] = (ent[i] >> 15) ? -xv : xv;
+                    }
+                    fwht128_warp(v, lane);
+                    const uint32_t sw = cs2[blk * 4] >> ((lane & 7) * 4);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if ((sw >> i) & 1u) v[i] = -v[i];
+                }
+                quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img0 + (size_t)(blk >> 1) * kWideStageBytes, blk & 1, pos);
+            }
+        }
     }
 }
 
@@ -212,9 +253,11 @@ int launch_pre_gu(const chronos_layer_t& L, const void* x, int x_dtype, const Pl
                   cudaStream_t st) {
     if (fp4 == 2) {
         const int sms = device_sm_count();
-        const long most = (long)p.max_gitems * (L.hidden / 256);
-        const unsigned grid = (unsigned)(most < 3L * sms ? most : 3L * sms);
-        pre_gu_wide_kernel<<<grid, 512, 0, st>>>(L, p);
+        const size_t smem = (size_t)kPreGuGroup * L.hidden * 2;
+        if (int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pre_gu_wide_kernel), smem, "pre_gu_wide")) return rc;
+        const long most = (long)p.max_gitems * (kPairsPerWideItem / kPreGuGroup);
+        const long resident = (long)sms * (smem * 4 <= 200 * 1024 ? 4 : (smem * 2 <= 200 * 1024 ? 2 : 1));
+        pre_gu_wide_kernel<<<(unsigned)(most < resident ? most : resident), kPreGuThreads, smem, st>>>(L, p);
         return check_launch("pre_gu_wide");
     }
     const long xf = fp4 ? (long)p.max_items * kPairsPerItem * (L.hidden / 128) : (long)p.max_pairs * (L.hidden / 128);

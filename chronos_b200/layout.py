@@ -7,6 +7,7 @@ over slots / experts; nothing is re-quantised. Two load-time rearrangements that
 from __future__ import annotations
 
 import ctypes as C
+import math
 import re
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -130,6 +131,10 @@ def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.
 class PackedLayer:
     """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
 
+    # Build the healer operand tiles of the FP4 tensor regime (`ut_gu` / `ut_dn`, + 2 * rank bytes per bank row) at load.
+    # Instances read the class attribute at construction; set it to False for layers that only ever see decode-sized batches.
+    fused_healer_default = True
+
     def __init__(self, cfg: FoldedLayerConfig, tensors: dict[str, torch.Tensor], device: torch.device,
                  fp4_images: bool = True, tail_bits: tuple[int, int] = (0, 0), keep_disk_order: bool = False):
         """`keep_disk_order`: keep the banks in their on-disk row-major order beside the re-tiled stage images. The FP4
@@ -152,6 +157,8 @@ class PackedLayer:
         s.shared_inter = cfg.inter if ("sh_gu_w" in tensors or "sh_gu_t" in tensors or "sh8_gu_w" in tensors) else 0
         s.tail_bits = self.tail_bits[0] | (self.tail_bits[1] << 8)
         self._add_fp4_images()
+        if self.fused_healer_default:
+            self._add_healer_tiles()
         if "v_dn" not in tensors and "v_dn_t" in tensors and self.device.type == "cuda":
             # healer.v_down in its on-disk orientation [E, r, I] beside the transposed copy: the tensor-core healer
             # kernels of the large-batch regime contract over I
@@ -186,6 +193,51 @@ class PackedLayer:
         if not self.keep_disk_order and self.fp4_only_ok():
             for name in ("gu_w", "gu_s", "dn_w", "dn_s", "sh_gu_w", "sh_gu_s", "sh_dn_w", "sh_dn_s"):
                 t.pop(name, None)
+
+    def _add_healer_tiles(self) -> None:
+        """healer.u_gu / healer.u_down as fp16 operand tiles in the basis of the bank-pass accumulators (see `ut_gu` in
+        include/chronos_b200.h). With z1 the bank-pass output after its epilogue (r_s2 sign, 128-row Walsh-Hadamard), the
+        reference's z[i] = beta * r_s1[i] * z1[r_inv[i]] + (U h)[i] (chronos_1t/models/glm5_chronos_moe.py:149-195) equals
+        beta * r_s1[i] * z1'[r_inv[i]] with z1' = z1 + W h, W[r_inv[i]] = (r_s1[i] / beta) U[i]; moving W h in front of
+        the epilogue's orthonormal transform gives the tile rows r_s2 * WHT128(W)."""
+        c, t = self.cfg, self.t
+        if (self.device.type != "cuda" or "gu_t" not in t or "u_gu" not in t or "ut_gu" in t or c.rank % 16 or c.rank > 64
+                or "gu_rout" not in t):
+            return
+        if any(bool((t[n].abs() < 1e-30).any()) for n in ("gu_beta", "dn_beta", "gu_s2", "dn_s2")):
+            return  # a zero beta or scale_2 cannot be divided out: such a layer keeps the separate healer pass
+        had = torch.ones(1, 1, device=self.device)
+        for _ in range(7):  # Sylvester construction, the matrix of build_hadamard_128 (convert_glm53_flash_colab.py:41-45)
+            had = torch.cat([torch.cat([had, had], 1), torch.cat([had, -had], 1)], 0)
+        had = had / math.sqrt(128.0)
+
+        def tiles(u: torch.Tensor, beta: torch.Tensor, rout: torch.Tensor, rs2: torch.Tensor, s2: torch.Tensor) -> tuple[torch.Tensor, float]:
+            n_e, rows, r = u.shape
+            k = c.group_size
+            raw = torch.empty(n_e, rows // 128, r // 8, 128, 8, dtype=torch.float32, device=self.device)
+            shifts = torch.arange(32, device=self.device, dtype=torch.int64)
+            for e0 in range(0, n_e, 16):  # a few experts at a time: the fp32 transient stays small
+                e1 = min(n_e, e0 + 16)
+                n = e1 - e0
+                uf = u[e0:e1].view(torch.float8_e4m3fn).to(torch.float32)
+                ro = rout[e0:e1].to(torch.int32) & 0xffff
+                r_inv = (ro & 0x7fff).to(torch.int64)
+                s1 = 1.0 - 2.0 * ((ro >> 15) & 1).to(torch.float32)
+                slot_s2 = s2[torch.arange(e0, e1, device=self.device) // k]
+                src = uf * (s1 / (beta[e0:e1, None] * slot_s2[:, None]))[..., None]
+                w = torch.empty_like(src)
+                w.scatter_(1, r_inv[..., None].expand(-1, -1, r), src)           # w[r_inv[i]] = src[i]
+                w = torch.matmul(had, w.view(n, rows // 128, 128, r))            # 128-row blocks, orthonormal
+                bits = ((rs2[e0:e1].to(torch.int64) & 0xffffffff)[..., None] >> shifts) & 1
+                w = w * (1.0 - 2.0 * bits.to(torch.float32)).view(n, rows // 128, 128, 1)
+                raw[e0:e1] = w.view(n, rows // 128, 128, r // 8, 8).permute(0, 1, 3, 2, 4)
+            top = float(raw.abs().max())
+            scale = 2.0 ** math.ceil(math.log2(top / 4096.0)) if top > 0.0 else 1.0  # largest entry lands in (2048, 4096]
+            return (raw / scale).to(torch.float16), scale
+
+        t["ut_gu"], k_gu = tiles(t["u_gu"], t["gu_beta"], t["gu_rout"], t["gu_rs2"], t["gu_s2"])
+        t["ut_dn"], k_dn = tiles(t["u_dn"], t["dn_beta"], t["dn_rout"], t["dn_rs2"], t["dn_s2"])
+        t["ut_scale"] = torch.tensor([k_gu, k_dn], dtype=torch.float32, device=self.device)
 
     def fp4_only_ok(self) -> bool:
         """True when every batch shape of this layer is served by an FP4 regime (the limits csrc/common.cuh states for

@@ -94,6 +94,13 @@ extern "C" {
  *   in bit 0) mean -1 / +1; the value is level * float(block scale).  With tail_bits set every entry point adds the term.
  * Optional: v_dn e4m3 [n_experts, r, I], "healer.v_down" exactly as on disk (kept beside its transposed copy); with it
  *   large batches run their healer products on the tensor cores.
+ * Optional (rank 16 ... 64, with gu_t / dn_t): ut_gu f16 [n_experts, 2I/128, r/8, 128, 8] and ut_dn f16 [n_experts, H/128,
+ *   r/8, 128, 8] - healer.u_gu / healer.u_down carried once at load into the row order and basis of the bank-pass
+ *   accumulators (rows gathered by r_inv with the r_s1 sign and 1/beta, 128-row Walsh-Hadamard blocks, r_s2 sign), stored as
+ *   K-major fp16 operand tiles of 128 rows, divided by the slot's scale_2 and by a power of two ut_scale f32 [2] = (gate_up,
+ *   down) that keeps them in fp16 range (the kernel multiplies the other operand by it). With them the FP4 tensor regime adds the low-rank correction inside the bank
+ *   pass (one more tensor-core step per tile into the same accumulators) instead of in a pass of its own that re-reads
+ *   healer.u_* once per 8 pairs.
  */
 typedef struct chronos_layer {
     int32_t hidden, inter, n_experts, group_size, n_slots, rank, top_k;
@@ -115,6 +122,7 @@ typedef struct chronos_layer {
     const uint8_t* v_dn;
     const uint8_t* tail_gu_p; const uint8_t* tail_gu_s; const uint8_t* tail_dn_p; const uint8_t* tail_dn_s;
     const uint8_t* sh8_gu_w; const float* sh8_gu_s; const uint8_t* sh8_dn_w; const float* sh8_dn_s;
+    const void* ut_gu; const void* ut_dn; const float* ut_scale;
 } chronos_layer_t;
 
 /* NVFP4 dequantisation probe: out[rows, cols] f32 = lut[nibble] * (float(e4m3 scale) * scale_2), evaluated

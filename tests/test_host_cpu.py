@@ -41,7 +41,7 @@ def test_layer_struct_matches_header_layout():
     # 12 four-byte scalars then 41 pointers, no padding surprises
     import ctypes
 
-    assert ctypes.sizeof(_lib.LayerStruct) == 12 * 4 + 41 * 8
+    assert ctypes.sizeof(_lib.LayerStruct) == 12 * 4 + 44 * 8
     header = (ROOT / "include" / "chronos_b200.h").read_text()
     body = header[header.index("typedef struct chronos_layer {"):header.index("} chronos_layer_t;")]
     names = re.findall(r"(\w+)\s*[;,]", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
