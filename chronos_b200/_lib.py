@@ -52,9 +52,11 @@ EXPORTS = {
     "chronos_b200_workspace_bytes": (C.c_size_t, [C.POINTER(LayerStruct), C.c_int]),
     "chronos_b200_fp4_mma_probe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "chronos_b200_ep_pack": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
-                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
-    "chronos_b200_ep_unpack_meta": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
-    "chronos_b200_ep_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
+                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_long, C.c_void_p]),
+    "chronos_b200_ep_unpack_meta": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_long, C.c_int,
+                                             C.c_void_p]),
+    "chronos_b200_ep_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                         C.c_int, C.c_void_p]),
     "chronos_b200_wait_probe": (C.c_int, [C.c_void_p, C.c_uint, C.c_void_p]),
     "chronos_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int]),
     "chronos_b200_workspace_status_offset": (C.c_long, [C.POINTER(LayerStruct), C.c_int]),

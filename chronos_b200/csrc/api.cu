@@ -448,7 +448,7 @@ static int validate_ep(int n_tokens, int top_k, int hidden, int world, int capac
 
 int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
                          int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
-                         int32_t* overflow, void* stream) {
+                         int32_t* overflow, int block_rows, long meta_block_ints, void* stream) {
     if (int rc = validate_ep(n_tokens, top_k, hidden, world, capacity)) return rc;
     if (x_dtype != CHRONOS_DTYPE_F32 && x_dtype != CHRONOS_DTYPE_BF16) { set_error("ep_pack: bad dtype"); return CHRONOS_E_ARG; }
     if (experts_per_rank <= 0) { set_error("ep_pack: experts_per_rank (%d) must be positive", experts_per_rank); return CHRONOS_E_SHAPE; }
@@ -456,18 +456,28 @@ int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const f
         set_error("ep_pack: NULL or misaligned pointer");
         return CHRONOS_E_ALIGN;
     }
+    if ((block_rows != 0 && block_rows < capacity) || (meta_block_ints != 0 && meta_block_ints < (long)(capacity + 1) * (2 * top_k + 2))) {
+        set_error("ep_pack: block strides (%d rows, %ld words) smaller than a block", block_rows, meta_block_ints);
+        return CHRONOS_E_SHAPE;
+    }
     return launch_ep_pack(x, x_dtype, ids, gates, n_tokens, top_k, hidden, world, experts_per_rank, capacity, send_rows, send_meta, slot_of,
-                          overflow, (cudaStream_t)stream);
+                          overflow, block_rows, meta_block_ints, (cudaStream_t)stream);
 }
 
-int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, void* stream) {
+int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out,
+                                int block_rows, long meta_block_ints, int tail_rows, void* stream) {
     if (int rc = validate_ep(0, top_k, 8, world, capacity)) return rc;
     if (!recv_meta || !ids_out || !gates_out) { set_error("ep_unpack_meta: NULL pointer"); return CHRONOS_E_ALIGN; }
-    return launch_ep_unpack_meta(recv_meta, world, capacity, top_k, ids_out, gates_out, (cudaStream_t)stream);
+    if ((block_rows != 0 && block_rows < capacity) || tail_rows < 0 ||
+        (meta_block_ints != 0 && meta_block_ints < (long)(capacity + 1) * (2 * top_k + 2))) {
+        set_error("ep_unpack_meta: block strides (%d rows, %ld words) smaller than a block, or negative tail", block_rows, meta_block_ints);
+        return CHRONOS_E_SHAPE;
+    }
+    return launch_ep_unpack_meta(recv_meta, world, capacity, top_k, ids_out, gates_out, block_rows, meta_block_ints, tail_rows, (cudaStream_t)stream);
 }
 
 int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
-                            int capacity, void* y, int y_dtype, void* stream) {
+                            int capacity, void* y, int y_dtype, int block_rows, void* stream) {
     if (int rc = validate_ep(n_tokens, 1, hidden, world, capacity)) return rc;
     if ((dtype != CHRONOS_DTYPE_F32 && dtype != CHRONOS_DTYPE_BF16) || (y_dtype != CHRONOS_DTYPE_F32 && y_dtype != CHRONOS_DTYPE_BF16)) {
         set_error("ep_combine: bad dtype");
@@ -477,7 +487,8 @@ int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slo
         set_error("ep_combine: NULL or misaligned pointer");
         return CHRONOS_E_ALIGN;
     }
-    return launch_ep_combine(back_rows, dtype, slot_of, extra, n_tokens, hidden, world, capacity, y, y_dtype, (cudaStream_t)stream);
+    if (block_rows != 0 && block_rows < capacity) { set_error("ep_combine: block stride (%d rows) smaller than a block", block_rows); return CHRONOS_E_SHAPE; }
+    return launch_ep_combine(back_rows, dtype, slot_of, extra, n_tokens, hidden, world, capacity, y, y_dtype, block_rows, (cudaStream_t)stream);
 }
 
 int chronos_b200_wait_probe(int32_t* status, unsigned poll_limit, void* stream) {

@@ -278,10 +278,11 @@ int launch_bank_fp4_fused(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, 
 // expert-parallel dispatch / combine helpers (csrc/ep_kernels.cu)
 int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
                    int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
-                   int32_t* overflow, cudaStream_t st);
-int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, cudaStream_t st);
+                   int32_t* overflow, int block_rows, long meta_block_ints, cudaStream_t st);
+int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, int block_rows,
+                          long meta_block_ints, int tail_rows, cudaStream_t st);
 int launch_ep_combine(const void* back, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
-                      int capacity, void* y, int y_dtype, cudaStream_t st);
+                      int capacity, void* y, int y_dtype, int block_rows, cudaStream_t st);
 int launch_dequant_fp8_block(const uint8_t* w, const float* s, float* out, int rows, int cols, cudaStream_t st);
 int launch_shared_fp8(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int first, int count, void* y, int y_dtype,
                       cudaStream_t st);

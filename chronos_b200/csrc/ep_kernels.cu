@@ -21,7 +21,8 @@ constexpr int kEpPlanThreads = 1024;
 // the destination (-1: not owned there), [k + 1 .. 2k] gate bits; row `capacity`: [0] = rows used in the block.
 __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t* __restrict__ ids, int n_tokens, int top_k,
                                                                  int experts_per_rank, int capacity, int32_t* __restrict__ meta,
-                                                                 int32_t* __restrict__ slot_of, int world, int32_t* __restrict__ overflow) {
+                                                                 long meta_block_ints, int32_t* __restrict__ slot_of, int world,
+                                                                 int32_t* __restrict__ overflow) {
     __shared__ int warp_tot[kEpPlanThreads / 32 + 1];
     const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int lo = d * experts_per_rank, hi = lo + experts_per_rank;
@@ -60,21 +61,21 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t* 
         if (flag && pos >= capacity) atomicOr(overflow, 1);  // the block is full: the caller learns of it and repeats the step
         carry += warp_tot[32];
     }
-    if (tid == 0) meta[((size_t)d * (capacity + 1) + capacity) * (2 * top_k + 2)] = min(carry, capacity);
+    if (tid == 0) meta[(size_t)d * meta_block_ints + (size_t)capacity * (2 * top_k + 2)] = min(carry, capacity);
 }
 
 __global__ void __launch_bounds__(128) ep_pack_rows_kernel(const uint4* __restrict__ x, int row_vec16, const int32_t* __restrict__ ids,
                                                            const float* __restrict__ gates, int top_k, int experts_per_rank, int capacity,
                                                            const int32_t* __restrict__ slot_of, int world, uint4* __restrict__ send_rows,
-                                                           int32_t* __restrict__ meta) {
+                                                           int block_rows, int32_t* __restrict__ meta, long meta_block_ints) {
     const int t = blockIdx.x, d = blockIdx.y;
     const int p = slot_of[(size_t)t * world + d];
     if (p < 0) return;
     const uint4* src = x + (size_t)t * row_vec16;
-    uint4* dst = send_rows + ((size_t)d * capacity + p) * row_vec16;
+    uint4* dst = send_rows + ((size_t)d * block_rows + p) * row_vec16;
     for (int i = threadIdx.x; i < row_vec16; i += 128) dst[i] = src[i];
     const int m = 2 * top_k + 2;
-    int32_t* mrow = meta + ((size_t)d * (capacity + 1) + p) * m;
+    int32_t* mrow = meta + (size_t)d * meta_block_ints + (size_t)p * m;
     if (threadIdx.x == 0) mrow[0] = t;
     if (threadIdx.x < top_k) {
         const int e = ids[(size_t)t * top_k + threadIdx.x] - d * experts_per_rank;
@@ -84,17 +85,23 @@ __global__ void __launch_bounds__(128) ep_pack_rows_kernel(const uint4* __restri
     }
 }
 
-__global__ void __launch_bounds__(256) ep_unpack_meta_kernel(const int32_t* __restrict__ meta, int world, int capacity, int top_k,
-                                                             int32_t* __restrict__ ids_out, float* __restrict__ gates_out) {
-    const long i = (long)blockIdx.x * 256 + threadIdx.x;  // over world * capacity * top_k
-    if (i >= (long)world * capacity * top_k) return;
+// Rows of the routing lists: world blocks of block_rows rows (rows at and past `capacity` of a block, where a merged
+// exchange buffer carries the metadata itself, get no expert), then tail_rows rows without experts (the home tokens).
+__global__ void __launch_bounds__(256) ep_unpack_meta_kernel(const int32_t* __restrict__ meta, long meta_block_ints, int world, int capacity,
+                                                             int block_rows, int tail_rows, int top_k, int32_t* __restrict__ ids_out,
+                                                             float* __restrict__ gates_out) {
+    const long i = (long)blockIdx.x * 256 + threadIdx.x;  // over (world * block_rows + tail_rows) * top_k
+    if (i >= ((long)world * block_rows + tail_rows) * top_k) return;
     const int j = (int)(i % top_k);
     const long row = i / top_k;
-    const int s = (int)(row / capacity), p = (int)(row % capacity);
+    const int s = (int)(row / block_rows), p = (int)(row % block_rows);
     const int m = 2 * top_k + 2;
-    const int32_t* blk = meta + (size_t)s * (capacity + 1) * m;
-    const int cnt = blk[(size_t)capacity * m];
-    const bool valid = p < cnt;
+    bool valid = false;
+    const int32_t* blk = meta;
+    if (s < world && p < capacity) {
+        blk = meta + (size_t)s * meta_block_ints;
+        valid = p < blk[(size_t)capacity * m];
+    }
     ids_out[i] = valid ? blk[(size_t)p * m + 1 + j] : -1;
     gates_out[i] = valid ? __int_as_float(blk[(size_t)p * m + 1 + top_k + j]) : 0.0f;
 }
@@ -111,7 +118,7 @@ __device__ __forceinline__ float4 ld4<__nv_bfloat16>(const __nv_bfloat16* p) {
 
 template <typename TIN>
 __global__ void __launch_bounds__(256) ep_combine_kernel(const TIN* __restrict__ back, const int32_t* __restrict__ slot_of,
-                                                         const TIN* __restrict__ extra, int hidden, int world, int capacity,
+                                                         const TIN* __restrict__ extra, int hidden, int world, int block_rows,
                                                          void* __restrict__ y, int y_dtype) {
     const int t = blockIdx.x, i0 = (blockIdx.y * 256 + threadIdx.x) * 4;
     if (i0 >= hidden) return;
@@ -120,7 +127,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const TIN* __restrict__
     for (int d = 0; d < world; ++d) {  // rank order: the same sum whatever the arrival order was
         const int p = slot_of[(size_t)t * world + d];
         if (p < 0) continue;
-        const float4 v = ld4<TIN>(back + ((size_t)d * capacity + p) * hidden + i0);
+        const float4 v = ld4<TIN>(back + ((size_t)d * block_rows + p) * hidden + i0);
         acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     if (y_dtype == CHRONOS_DTYPE_BF16) {
@@ -136,34 +143,43 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const TIN* __restrict__
 
 int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
                    int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
-                   int32_t* overflow, cudaStream_t st) {
+                   int32_t* overflow, int block_rows, long meta_block_ints, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
-    ep_plan_kernel<<<(unsigned)world, kEpPlanThreads, 0, st>>>(ids, n_tokens, top_k, experts_per_rank, capacity, send_meta, slot_of, world, overflow);
+    if (block_rows <= 0) block_rows = capacity;
+    if (meta_block_ints <= 0) meta_block_ints = (long)(capacity + 1) * (2 * top_k + 2);
+    ep_plan_kernel<<<(unsigned)world, kEpPlanThreads, 0, st>>>(ids, n_tokens, top_k, experts_per_rank, capacity, send_meta, meta_block_ints,
+                                                              slot_of, world, overflow);
     if (int rc = check_launch("ep_plan")) return rc;
     const int row_vec16 = hidden * (x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4) / 16;
     ep_pack_rows_kernel<<<dim3((unsigned)n_tokens, (unsigned)world), 128, 0, st>>>(reinterpret_cast<const uint4*>(x), row_vec16, ids, gates, top_k,
                                                                                   experts_per_rank, capacity, slot_of, world,
-                                                                                  reinterpret_cast<uint4*>(send_rows), send_meta);
+                                                                                  reinterpret_cast<uint4*>(send_rows), block_rows, send_meta,
+                                                                                  meta_block_ints);
     return check_launch("ep_pack_rows");
 }
 
-int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, cudaStream_t st) {
-    const long n = (long)world * capacity * top_k;
+int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out, int block_rows,
+                          long meta_block_ints, int tail_rows, cudaStream_t st) {
+    if (block_rows <= 0) block_rows = capacity;
+    if (meta_block_ints <= 0) meta_block_ints = (long)(capacity + 1) * (2 * top_k + 2);
+    const long n = ((long)world * block_rows + tail_rows) * top_k;
     if (n <= 0) return CHRONOS_OK;
-    ep_unpack_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(meta, world, capacity, top_k, ids_out, gates_out);
+    ep_unpack_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(meta, meta_block_ints, world, capacity, block_rows, tail_rows, top_k,
+                                                                      ids_out, gates_out);
     return check_launch("ep_unpack_meta");
 }
 
 int launch_ep_combine(const void* back, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
-                      int capacity, void* y, int y_dtype, cudaStream_t st) {
+                      int capacity, void* y, int y_dtype, int block_rows, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
+    if (block_rows <= 0) block_rows = capacity;
     const dim3 grid((unsigned)n_tokens, (unsigned)((hidden / 4 + 255) / 256));
     if (dtype == CHRONOS_DTYPE_BF16)
         ep_combine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(back), slot_of,
-                                                              reinterpret_cast<const __nv_bfloat16*>(extra), hidden, world, capacity, y, y_dtype);
+                                                              reinterpret_cast<const __nv_bfloat16*>(extra), hidden, world, block_rows, y, y_dtype);
     else
         ep_combine_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(back), slot_of, reinterpret_cast<const float*>(extra),
-                                                      hidden, world, capacity, y, y_dtype);
+                                                      hidden, world, block_rows, y, y_dtype);
     return check_launch("ep_combine");
 }
 

@@ -8,8 +8,8 @@ Per layer, stream-ordered and free of host synchronisation:
   route     every rank routes its own tokens (global expert ids + gates);
   dispatch  a token's normed hidden row goes ONCE to every rank that owns at least one of its experts, with its expert
             ids local to that rank and their gates: a device kernel packs fixed-capacity blocks per destination
-            (`chronos_b200_ep_pack`), one all-to-all with equal splits moves the rows, one the metadata - no split
-            sizes ever travel through the host;
+            (`chronos_b200_ep_pack`), ONE all-to-all with equal splits moves rows and metadata (the metadata of a block
+            sits behind its rows) - no split sizes ever travel through the host;
   compute   each rank evaluates the received rows' entries (all of them are its own experts) and, in the same pass,
             the shared expert of the tokens it is the home of;
   combine   ONE bf16 partial-sum row per received token goes back the same way, and the home rank adds the partial rows in
@@ -112,50 +112,62 @@ class ExpertParallelMoE:
         self._checked.add(key)
 
     # -- device work (CUDA library) -----------------------------------------------------------------------------------
+    def _meta_rows(self, capacity: int, h: int, elem: int) -> int:
+        """Rows of hidden-size elements that hold one block's metadata ((capacity + 1) x (2 k + 2) int32) behind its rows."""
+        return -(-(capacity + 1) * (2 * self.cfg.top_k + 2) * 4 // (h * elem))
+
     def _pack_cuda(self, x, ids, gates, capacity):
+        """One buffer [world, capacity + m, H]: per destination its rows, then m rows of bytes that hold the block's metadata,
+        so that ONE collective moves both. Returns (buffer, None, slot_of)."""
         tl, h = x.shape
         k, w = self.cfg.top_k, self.world
         dev = x.device
-        rows = torch.empty((w, capacity, h), dtype=x.dtype, device=dev)
-        meta = torch.empty((w, capacity + 1, 2 * k + 2), dtype=torch.int32, device=dev)
+        m = self._meta_rows(capacity, h, x.element_size())
+        buf = torch.empty((w, capacity + m, h), dtype=x.dtype, device=dev)
         slot_of = torch.empty((tl, w), dtype=torch.int32, device=dev)
         flag = _OVERFLOW_FLAGS.get(dev)
         if flag is None:
             flag = _OVERFLOW_FLAGS[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+        row_bytes = h * x.element_size()
         _lib.check(_lib.lib().chronos_b200_ep_pack(x.data_ptr(), _DTYPES[x.dtype], ids.data_ptr(), gates.data_ptr(), tl, k, h, w, self.n_local,
-                                                 capacity, rows.data_ptr(), meta.data_ptr(), slot_of.data_ptr(), flag.data_ptr(),
+                                                 capacity, buf.data_ptr(), buf.data_ptr() + capacity * row_bytes, slot_of.data_ptr(),
+                                                 flag.data_ptr(), capacity + m, (capacity + m) * row_bytes // 4,
                                                  torch.cuda.current_stream().cuda_stream))
-        return rows, meta, slot_of
+        return buf, None, slot_of
 
     def _compute_cuda(self, recv_rows, recv_meta, x_local, capacity, recv_all=None):
-        """Expert pass over the received rows + the shared expert of the home tokens, one call. Returns (partial rows
-        [world, capacity, H], shared rows [Tl, H] or None), both in the activation dtype. `recv_all` [world * capacity + Tl, H]
-        is the buffer whose head `recv_rows` views and whose tail already holds the home tokens' rows."""
+        """Expert pass over the received blocks + the shared expert of the home tokens, one call. `recv_rows`
+        [world, capacity + m, H] are the merged blocks (rows, then metadata bytes; `recv_meta` is None), `recv_all`
+        [world * (capacity + m) + Tl, H] the buffer whose head they view and whose tail already holds the home tokens' rows.
+        The metadata rows ride through the pass as rows without experts. Returns (partial rows in the same block shape,
+        shared rows [Tl, H] or None), both in the activation dtype."""
         w, k = self.world, self.cfg.top_k
         tl, h = x_local.shape
-        n_recv = w * capacity
+        block_rows = recv_rows.shape[1]
+        n_recv = w * block_rows
         has_shared = self.layer.n_shared_experts > 0
         dev = x_local.device
-        ids = torch.empty((n_recv + (tl if has_shared else 0), k), dtype=torch.int32, device=dev)
-        gates = torch.empty((n_recv + (tl if has_shared else 0), k), dtype=torch.float32, device=dev)
-        _lib.check(_lib.lib().chronos_b200_ep_unpack_meta(recv_meta.data_ptr(), w, capacity, k, ids.data_ptr(), gates.data_ptr(),
+        tail = tl if has_shared else 0
+        ids = torch.empty((n_recv + tail, k), dtype=torch.int32, device=dev)
+        gates = torch.empty((n_recv + tail, k), dtype=torch.float32, device=dev)
+        row_bytes = h * x_local.element_size()
+        _lib.check(_lib.lib().chronos_b200_ep_unpack_meta(recv_rows.data_ptr() + capacity * row_bytes, w, capacity, k, ids.data_ptr(),
+                                                        gates.data_ptr(), block_rows, block_rows * row_bytes // 4, tail,
                                                         torch.cuda.current_stream().cuda_stream))
         if has_shared:  # the home tokens ride along as extra rows that take the shared expert only
-            ids[n_recv:].fill_(-1)
-            gates[n_recv:].zero_()
             x_all = recv_all if recv_all is not None else torch.cat([recv_rows.reshape(n_recv, h), x_local])
             out = self.layer.routed_forward(x_all, ids, gates, out_dtype=x_local.dtype, shared_range=(n_recv, tl))
-            return out[:n_recv].view(w, capacity, h), out[n_recv:]
+            return out[:n_recv].view(w, block_rows, h), out[n_recv:]
         out = self.layer.routed_forward(recv_rows.view(n_recv, h), ids, gates, out_dtype=x_local.dtype)
-        return out.view(w, capacity, h), None
+        return out.view(w, block_rows, h), None
 
     def _combine_cuda(self, back_rows, slot_of, shared_rows, capacity):
-        w, _, h = back_rows.shape
+        w, block_rows, h = back_rows.shape
         tl = slot_of.shape[0]
         y = torch.empty((tl, h), dtype=torch.float32, device=back_rows.device)
         _lib.check(_lib.lib().chronos_b200_ep_combine(back_rows.data_ptr(), _DTYPES[back_rows.dtype], slot_of.data_ptr(),
                                                     shared_rows.data_ptr() if shared_rows is not None else None, tl, h, w, capacity,
-                                                    y.data_ptr(), _lib.DTYPE_F32, torch.cuda.current_stream().cuda_stream))
+                                                    y.data_ptr(), _lib.DTYPE_F32, block_rows, torch.cuda.current_stream().cuda_stream))
         return y
 
     def overflowed(self) -> bool:
@@ -183,12 +195,15 @@ class ExpertParallelMoE:
                 return self.layer.routed_forward(x_local, ids, gates, with_shared=self.layer.n_shared_experts > 0, out_dtype=torch.float32)
         with self._mark("dispatch"):
             send_rows, send_meta, slot_of = self.pack_fn(x_local, ids, gates, capacity)
-            # received rows and, behind them, the home tokens' own rows (they take the shared expert in the same pass)
-            recv_all = torch.empty((self.world * capacity + tl, h), dtype=x_local.dtype, device=x_local.device)
-            recv_rows = recv_all[:self.world * capacity].view(self.world, capacity, h)
-            recv_all[self.world * capacity:].copy_(x_local)
-            recv_meta = torch.empty_like(send_meta)
-            dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+            # received blocks and, behind them, the home tokens' own rows (they take the shared expert in the same pass)
+            block_rows = send_rows.shape[1]  # capacity, plus the metadata rows when the pack function merged them in
+            recv_all = torch.empty((self.world * block_rows + tl, h), dtype=x_local.dtype, device=x_local.device)
+            recv_rows = recv_all[:self.world * block_rows].view(self.world, block_rows, h)
+            recv_all[self.world * block_rows:].copy_(x_local)
+            recv_meta = None
+            if send_meta is not None:  # a pack function that keeps the metadata apart: a collective of its own
+                recv_meta = torch.empty_like(send_meta)
+                dist.all_to_all_single(recv_meta, send_meta, group=self.group)
             dist.all_to_all_single(recv_rows, send_rows, group=self.group)
         with self._mark("routed_experts"):
             part, shared_rows = self.compute_fn(recv_rows, recv_meta, x_local, capacity, recv_all=recv_all)

@@ -236,23 +236,27 @@ int chronos_b200_residual_rmsnorm(void* h, const void* y, const float* weight, v
  * `capacity` tokens for one destination) is left out and *overflow (device int32, caller-cleared) is raised: the
  * caller checks it at the end of the step and repeats the step with capacity = n_tokens, which always fits.
  * The blocks are then exchanged by a collective with equal splits (NCCL all-to-all in the shipped host layer).
+ * block_rows / meta_block_ints: distance between the blocks of consecutive destinations in send_rows (in rows) and in
+ * send_meta (in 32-bit words); 0 = dense (capacity rows, (capacity + 1) * (2 top_k + 2) words).  With larger strides both can
+ * live in ONE buffer - block d = capacity rows followed by the block's metadata - so one collective moves them.
  * No counterpart in the reference (single device; chronos_1t/docs/CHRONOS_ARCHITECTURE_PAPER.md:244 only names the idea). */
 int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
                          int world, int experts_per_rank, int capacity, void* send_rows, int32_t* send_meta, int32_t* slot_of,
-                         int32_t* overflow, void* stream);
+                         int32_t* overflow, int block_rows, long meta_block_ints, void* stream);
 
-/* Received metadata blocks [world, capacity + 1, 2 * top_k + 2] -> the routing lists of the received rows:
- * ids_out i32 [world * capacity, top_k] (local expert ids; -1 for unused rows and entries), gates_out f32 likewise.
- * No counterpart in the reference. */
+/* Received metadata blocks [world, capacity + 1, 2 * top_k + 2] (meta_block_ints words apart; 0 = dense) -> the routing
+ * lists of the received rows: ids_out i32 [world * block_rows + tail_rows, top_k] (local expert ids; -1 for unused rows and
+ * entries, for the rows capacity .. block_rows - 1 of every block and for the tail_rows rows at the end), gates_out f32
+ * likewise; block_rows 0 = capacity.  No counterpart in the reference. */
 int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out,
-                                void* stream);
+                                int block_rows, long meta_block_ints, int tail_rows, void* stream);
 
 /* Expert-parallel combine on the home rank: y[t] = extra[t] + sum over ranks d = 0 .. world - 1 (in that order) of
- * back_rows[d, slot_of[t, d]] where slot_of >= 0.  back_rows [world, capacity, hidden] are the partial-sum rows the
- * peers returned (bf16 or f32), extra [n_tokens, hidden] (same dtype, or NULL) e.g. the shared expert's rows.
+ * back_rows[d, slot_of[t, d]] where slot_of >= 0.  back_rows [world, block_rows, hidden] (block_rows 0 = capacity) are the
+ * partial-sum rows the peers returned (bf16 or f32), extra [n_tokens, hidden] (same dtype, or NULL) e.g. the shared expert's rows.
  * No counterpart in the reference. */
 int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden,
-                            int world, int capacity, void* y, int y_dtype, void* stream);
+                            int world, int capacity, void* y, int y_dtype, int block_rows, void* stream);
 
 /* Operand-format probe of the block-scaled FP4 tensor-core path (tcgen05.mma kind::mxf4nvf4, e2m1 operands with a
  * ue4m3 scale per 16 elements): d_out f32 [128, b_rows] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns;
