@@ -447,16 +447,20 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
             int cur_item = -1;
             bool live = true;
             const uint64_t pol = l2_policy_evict_first();
+            // the slot of a work item is read once per item, and the next item's one tile ahead: a global load in front of
+            // every tile's first copy is a bubble the ring (a few microseconds of stages) does not always hide
+            int slot = tile_lo < tile_hi ? a.item_slot[(int)(tile_lo / RB)] : 0, next_slot = slot;
             for (long tile = tile_lo; tile < tile_hi && live; ++tile) {
                 const int item = (int)(tile / RB), rb = (int)(tile % RB);
                 if (item != cur_item) {  // new work item: its activation image replaces the previous one
+                    if (cur_item >= 0) slot = next_slot;
                     if (!mbar_wait(smem_u32(b_empty), (n_items_seen & 1u) ^ 1u)) { atomicOr(a.counters + 2, kStatusFp4Timeout); break; }
                     mbar_expect_tx(smem_u32(b_full), (uint32_t)NS * kF4BStage);
                     bulk_g2s(smem_u32(bimg), a.bq + (size_t)item * NS * kF4BStage, (uint32_t)NS * kF4BStage, smem_u32(b_full));
                     cur_item = item;
                     ++n_items_seen;
+                    if ((long)(item + 1) * RB < tile_hi) next_slot = a.item_slot[item + 1];  // in flight while this item streams
                 }
-                const int slot = a.item_slot[item];
                 const uint8_t* asrc = (slot >= a.n_slots ? a.sh_bank_t : a.bank_t + (size_t)slot * RB * NS * kF4AStage) +
                                       (size_t)rb * NS * kF4AStage;
                 const int sb = st_begin(tile), se = st_end(tile);
@@ -577,25 +581,41 @@ __global__ void __launch_bounds__(kF4Threads + (SIDE ? kF4SideThreads : 0), 1) b
         const int row = quarter * 32 + lane;
         const bool q0 = (quarter & 1) != 0, q1 = (quarter & 2) != 0;
         uint32_t tcount = 0, zpar = 0;
+        // per work item (the tiles of an item follow one another): its pairs, their scales and experts. Fetched when the
+        // item changes, not per tile - the chain item -> pairs -> experts -> sign words is several memory round trips,
+        // longer than a short tile streams
+        int cur_item = -1, start = 0, cnt = 0;
+        bool sh = false;
+        float s2_lo = 0.0f, s2_hi = 0.0f, ps8[8];
+        int ex8[8];
         for (long tile = tile_lo; tile < tile_hi; ++tile, ++tcount) {
             const int item = (int)(tile / RB), rb = (int)(tile % RB);
-            const int start = a.item_start[item], cnt = a.item_cnt[item], slot = a.item_slot[item];
-            const bool sh = slot >= a.n_slots;
+            if (item != cur_item) {
+                cur_item = item;
+                start = a.item_start[item];
+                cnt = a.item_cnt[item];
+                const int slot = a.item_slot[item];
+                sh = slot >= a.n_slots;
+                s2_lo = sh ? a.sh_s2[0] : a.s2[slot];
+                s2_hi = sh ? a.sh_s2[a.sh_split < R ? 1 : 0] : s2_lo;
+#pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                    ps8[n] = n < cnt ? a.pscale[start + n] : 0.0f;
+                    ex8[n] = (n < cnt && !sh) ? a.pair_expert[start + n] : 0;
+                }
+            }
             // a partial tile (a slice of the contraction): which issuers multiplied anything, and the result is added
             const int sb = st_begin(tile), se = st_end(tile);
             const bool partial = sb > 0 || se < NS;
             const bool has_a = n_issuers == 1 || sb + (sb & 1) < se, has_b = n_issuers == 2 && sb + ((sb & 1) ^ 1) < se;
-            // operands of the epilogue, fetched while the tile streams
-            const float s2 = sh ? a.sh_s2[rb * 128 >= a.sh_split ? 1 : 0] : a.s2[slot];
+            // operands of the epilogue that depend on the row block, fetched while the tile streams
+            const float s2 = rb * 128 >= a.sh_split ? s2_hi : s2_lo;
             float g8[8];
             uint32_t sbits = 0u;  // bit n: r_s2 sign of this thread's row for pair n
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
-                g8[n] = 0.0f;
-                if (n < cnt) {
-                    g8[n] = a.pscale[start + n] * s2;
-                    if (!sh) sbits |= ((a.rs2[(size_t)a.pair_expert[start + n] * (R / 32) + rb * 4 + quarter] >> lane) & 1u) << n;
-                }
+                g8[n] = ps8[n] * s2;
+                if (n < cnt && !sh) sbits |= ((a.rs2[(size_t)ex8[n] * (R / 32) + rb * 4 + quarter] >> lane) & 1u) << n;
             }
             const uint32_t buf = tcount & 1u;
             // the 128 epilogue threads must take the same branch: a named barrier ORs their verdicts
