@@ -268,11 +268,11 @@ static int routed_forward(const chronos_layer_t& L, const void* x, int x_dtype, 
                       : (tensor ? launch_bank_gemm(L, 1, p, st) : (fp4 ? launch_bank_fp4(L, 1, p, st) : launch_bank_stream(L, 1, p, st)))) return rc;
     stage_mark(6, st);
     int rc;
-    if (hmma && wide && healer_fused(L, p) && combine_gather_fits(L)) {
+    if (hmma && wide && healer_fused(L, p)) {
         // the down pass already added the healer term: one kernel gathers the token's rows and sums them
         rc = launch_combine_gather(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     } else if (hmma) {
-        rc = launch_down_out_mma(L, p, wide ? 1 : 0, st);
+        rc = launch_down_out_mma(L, p, st);
         if (!rc) rc = launch_combine_sum(L, p, gates, n_tokens, with_shared, y, y_dtype, st);
     } else {
         rc = many ? launch_combine_tiled(L, p, gates, n_tokens, with_shared, y, y_dtype, st)

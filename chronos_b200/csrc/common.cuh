@@ -252,7 +252,7 @@ int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream
 int launch_tail_pass(const chronos_layer_t& L, int stage, const void* x, int x_dtype, const Plan& p, cudaStream_t st);
 int launch_tail_add(const chronos_layer_t& L, int expert, int which, float* out, cudaStream_t st);
 int launch_bank_fp4_wide(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, cudaStream_t st);
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st);
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
 int launch_heal_image(const chronos_layer_t& L, int stage, const Plan& p, cudaStream_t st);
 bool healer_fused(const chronos_layer_t& L, const Plan& p);
 int launch_mid_fused(const chronos_layer_t& L, const Plan& p, cudaStream_t st);

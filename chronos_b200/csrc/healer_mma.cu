@@ -338,8 +338,7 @@ int launch_healer_in_mma(const chronos_layer_t& L, int stage, const void* x, int
 constexpr int kOutThreads = 512;
 constexpr int kGroupsPerItem = 128 / kGroupPairs;
 
-// FUSED: the bank pass already added the healer term to its output (healer tiles in the layer): no products here.
-template <int MODE, int R16, bool WIDE, bool FUSED>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
+template <int MODE, int R16, bool WIDE>  // WIDE: the down input goes out as an FP4 tensor-regime image, not as fp16 rows
 __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) float smem_f[];
     __shared__ __align__(16) __half hsm[kGroupPairs][kMaxRank];
@@ -386,7 +385,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
             const float* hs = p.hsplit + (size_t)MODE * kHealSplit * sstride;
             const int kdim = MODE == 0 ? H : I;
             const int n_split = kdim % (64 * kHealSplit) == 0 ? kHealSplit : (kdim % 128 == 0 ? 2 : 1);
-            if (!FUSED && tid < PG * (r / 4)) {
+            if (tid < PG * (r / 4)) {
                 const int n = tid / (r / 4), c4 = (tid % (r / 4)) * 4;
                 float4 part[kHealSplit];
 #pragma unroll
@@ -413,7 +412,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
             uint32_t bf[R16][2];
 #pragma unroll
             for (int s = 0; s < R16; ++s) {
-                const uint2 v = FUSED ? make_uint2(0u, 0u) : *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s]);
+                const uint2 v = *reinterpret_cast<const uint2*>(&hsm[g][4 * R16 * q + 4 * s]);
                 bf[s][0] = v.x;
                 bf[s][1] = v.y;
             }
@@ -426,8 +425,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                     const int row_lo = half * I + jt * 16 + g, row_hi = row_lo + 8;
                     const uint32_t* u_lo = reinterpret_cast<const uint32_t*>(U + (size_t)row_lo * r + 4 * R16 * q);
                     const uint32_t* u_hi = reinterpret_cast<const uint32_t*>(U + (size_t)row_hi * r + 4 * R16 * q);
-                    if constexpr (FUSED) {
-                    } else if constexpr (R16 % 4 == 0) {
+                    if constexpr (R16 % 4 == 0) {
 #pragma unroll
                         for (int s = 0; s < R16; s += 4) {
                             const uint4 a4 = *reinterpret_cast<const uint4*>(u_lo + s), b4 = *reinterpret_cast<const uint4*>(u_hi + s);
@@ -452,7 +450,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
                 for (int half = 0; half < NH; ++half) {
                     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                    for (int s = 0; s < (FUSED ? 0 : R16); ++s)
+                    for (int s = 0; s < R16; ++s)
                         mma_16816(d, e4m3x2_to_f16x2(wl[half][s] & 0xffffu), e4m3x2_to_f16x2(wh[half][s] & 0xffffu),
                                   e4m3x2_to_f16x2(wl[half][s] >> 16), e4m3x2_to_f16x2(wh[half][s] >> 16), bf[s][0], bf[s][1]);
 #pragma unroll
@@ -534,7 +532,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) pair_group_out_kernel(chronos_
     }
 }
 
-template <int MODE, bool WIDE, bool FUSED>
+template <int MODE, bool WIDE>
 static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStream_t st) {
     const size_t smem = MODE == 0 ? (size_t)kGroupPairs * (2 * L.inter + L.inter) * 4 : (size_t)kGroupPairs * L.hidden * 4;
     if (smem > 220 * 1024) {
@@ -547,8 +545,8 @@ static int launch_pair_groups(const chronos_layer_t& L, const Plan& p, cudaStrea
     const unsigned grid = most < resident ? most : resident;
     int rc = CHRONOS_OK;
 #define CHRONOS_PG(R)                                                                                                   \
-    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pair_group_out_kernel<MODE, R, WIDE, FUSED>), smem, "pair_group_out"); \
-    if (rc == CHRONOS_OK) pair_group_out_kernel<MODE, R, WIDE, FUSED><<<grid, kOutThreads, smem, st>>>(L, p);
+    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(pair_group_out_kernel<MODE, R, WIDE>), smem, "pair_group_out"); \
+    if (rc == CHRONOS_OK) pair_group_out_kernel<MODE, R, WIDE><<<grid, kOutThreads, smem, st>>>(L, p);
     switch (L.rank / 16) {
         case 1: CHRONOS_PG(1) break;
         case 2: CHRONOS_PG(2) break;
@@ -564,21 +562,21 @@ bool healer_mma_fits(const chronos_layer_t& L) {
     return L.v_dn != nullptr && (size_t)kGroupPairs * 3 * L.inter * 4 <= 220 * 1024 && (size_t)kGroupPairs * L.hidden * 4 <= 220 * 1024;
 }
 
-// The fused healer needs the FP4 tensor regime, the layer's healer tiles and a rank that fits a ring slot of the bank pass.
+// The fused healer needs the FP4 tensor regime, the layer's healer tiles, a rank that fits a ring slot of the bank pass and
+// shapes the gather kernels behind it serve (the regime's own limits imply them).
 bool healer_fused(const chronos_layer_t& L, const Plan& p) {
-    return p.fp4_wide && p.himg != nullptr && L.ut_gu != nullptr && L.ut_dn != nullptr && L.ut_scale != nullptr && L.rank <= 64;
+    return p.fp4_wide && p.himg != nullptr && L.ut_gu != nullptr && L.ut_dn != nullptr && L.ut_scale != nullptr && L.rank <= 64 &&
+           combine_gather_fits(L);
 }
 
 int launch_mid_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
     const bool fused = wide && healer_fused(L, p);
     if (int rc = fused ? launch_mid_fused(L, p, st)
-                       : (wide ? launch_pair_groups<0, true, false>(L, p, st) : launch_pair_groups<0, false, false>(L, p, st))) return rc;
+                       : (wide ? launch_pair_groups<0, true>(L, p, st) : launch_pair_groups<0, false>(L, p, st))) return rc;
     if (int rc = wide ? launch_healer_in_mma(L, 1, p.ac, kDtypeF16Scaled, p, st) : launch_healer_in_mma(L, 1, p.act, CHRONOS_DTYPE_F32, p, st)) return rc;
     return fused ? launch_heal_image(L, 1, p, st) : CHRONOS_OK;
 }
 
-int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, int wide, cudaStream_t st) {
-    return (wide && healer_fused(L, p)) ? launch_pair_groups<1, false, true>(L, p, st) : launch_pair_groups<1, false, false>(L, p, st);
-}
+int launch_down_out_mma(const chronos_layer_t& L, const Plan& p, cudaStream_t st) { return launch_pair_groups<1, false>(L, p, st); }
 
 }  // namespace chronos
