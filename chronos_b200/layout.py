@@ -128,6 +128,42 @@ def key_tables(cfg: FoldedLayerConfig, device: torch.device) -> dict[str, torch.
     return out
 
 
+def healer_tiles(u: torch.Tensor, beta: torch.Tensor, rout: torch.Tensor, rs2: torch.Tensor, s2: torch.Tensor,
+                 group_size: int) -> tuple[torch.Tensor, float]:
+    """The healer's output factor of every expert in the row order and basis of the bank-pass accumulators.
+
+    u e4m3 bytes [E, rows, r], beta f32 [E], rout i16 [E, rows] (bits 0-14 r_inv, bit 15 r_s1 < 0), rs2 i32 [E, rows/32] sign
+    bits, s2 f32 [n_slots]. Returns (tiles f16 [E, rows/128, r/8, 128, 8], scale): row j of block b of expert e holds
+    r_s2[j] * WHT128(W)[j] / (scale_2 * scale) with W[r_inv[i]] = (r_s1[i] / beta) * U[i], laid out as K-major operand tiles
+    (8 consecutive rank columns per 16-byte unit); `scale` is the power of two that puts the largest entry into (2048, 4096]."""
+    dev = u.device
+    n_e, rows, r = u.shape
+    had = torch.ones(1, 1, device=dev)
+    for _ in range(7):  # Sylvester construction, the matrix of build_hadamard_128 (convert_glm53_flash_colab.py:41-45)
+        had = torch.cat([torch.cat([had, had], 1), torch.cat([had, -had], 1)], 0)
+    had = had / math.sqrt(128.0)
+    raw = torch.empty(n_e, rows // 128, r // 8, 128, 8, dtype=torch.float32, device=dev)
+    shifts = torch.arange(32, device=dev, dtype=torch.int64)
+    for e0 in range(0, n_e, 16):  # a few experts at a time: the fp32 transient stays small
+        e1 = min(n_e, e0 + 16)
+        n = e1 - e0
+        uf = u[e0:e1].view(torch.float8_e4m3fn).to(torch.float32)
+        ro = rout[e0:e1].to(torch.int32) & 0xffff
+        r_inv = (ro & 0x7fff).to(torch.int64)
+        s1 = 1.0 - 2.0 * ((ro >> 15) & 1).to(torch.float32)
+        slot_s2 = s2[torch.arange(e0, e1, device=dev) // group_size]
+        src = uf * (s1 / (beta[e0:e1, None] * slot_s2[:, None]))[..., None]
+        w = torch.empty_like(src)
+        w.scatter_(1, r_inv[..., None].expand(-1, -1, r), src)           # w[r_inv[i]] = src[i]
+        w = torch.matmul(had, w.view(n, rows // 128, 128, r))            # 128-row blocks, orthonormal
+        bits = ((rs2[e0:e1].to(torch.int64) & 0xffffffff)[..., None] >> shifts) & 1
+        w = w * (1.0 - 2.0 * bits.to(torch.float32)).view(n, rows // 128, 128, 1)
+        raw[e0:e1] = w.view(n, rows // 128, 128, r // 8, 8).permute(0, 1, 3, 2, 4)
+    top = float(raw.abs().max())
+    scale = 2.0 ** math.ceil(math.log2(top / 4096.0)) if top > 0.0 else 1.0
+    return (raw / scale).to(torch.float16), scale
+
+
 class PackedLayer:
     """Owns the device tensors of one layer and exposes them as a `chronos_layer_t`."""
 
@@ -206,37 +242,8 @@ class PackedLayer:
             return
         if any(bool((t[n].abs() < 1e-30).any()) for n in ("gu_beta", "dn_beta", "gu_s2", "dn_s2")):
             return  # a zero beta or scale_2 cannot be divided out: such a layer keeps the separate healer pass
-        had = torch.ones(1, 1, device=self.device)
-        for _ in range(7):  # Sylvester construction, the matrix of build_hadamard_128 (convert_glm53_flash_colab.py:41-45)
-            had = torch.cat([torch.cat([had, had], 1), torch.cat([had, -had], 1)], 0)
-        had = had / math.sqrt(128.0)
-
-        def tiles(u: torch.Tensor, beta: torch.Tensor, rout: torch.Tensor, rs2: torch.Tensor, s2: torch.Tensor) -> tuple[torch.Tensor, float]:
-            n_e, rows, r = u.shape
-            k = c.group_size
-            raw = torch.empty(n_e, rows // 128, r // 8, 128, 8, dtype=torch.float32, device=self.device)
-            shifts = torch.arange(32, device=self.device, dtype=torch.int64)
-            for e0 in range(0, n_e, 16):  # a few experts at a time: the fp32 transient stays small
-                e1 = min(n_e, e0 + 16)
-                n = e1 - e0
-                uf = u[e0:e1].view(torch.float8_e4m3fn).to(torch.float32)
-                ro = rout[e0:e1].to(torch.int32) & 0xffff
-                r_inv = (ro & 0x7fff).to(torch.int64)
-                s1 = 1.0 - 2.0 * ((ro >> 15) & 1).to(torch.float32)
-                slot_s2 = s2[torch.arange(e0, e1, device=self.device) // k]
-                src = uf * (s1 / (beta[e0:e1, None] * slot_s2[:, None]))[..., None]
-                w = torch.empty_like(src)
-                w.scatter_(1, r_inv[..., None].expand(-1, -1, r), src)           # w[r_inv[i]] = src[i]
-                w = torch.matmul(had, w.view(n, rows // 128, 128, r))            # 128-row blocks, orthonormal
-                bits = ((rs2[e0:e1].to(torch.int64) & 0xffffffff)[..., None] >> shifts) & 1
-                w = w * (1.0 - 2.0 * bits.to(torch.float32)).view(n, rows // 128, 128, 1)
-                raw[e0:e1] = w.view(n, rows // 128, 128, r // 8, 8).permute(0, 1, 3, 2, 4)
-            top = float(raw.abs().max())
-            scale = 2.0 ** math.ceil(math.log2(top / 4096.0)) if top > 0.0 else 1.0  # largest entry lands in (2048, 4096]
-            return (raw / scale).to(torch.float16), scale
-
-        t["ut_gu"], k_gu = tiles(t["u_gu"], t["gu_beta"], t["gu_rout"], t["gu_rs2"], t["gu_s2"])
-        t["ut_dn"], k_dn = tiles(t["u_dn"], t["dn_beta"], t["dn_rout"], t["dn_rs2"], t["dn_s2"])
+        t["ut_gu"], k_gu = healer_tiles(t["u_gu"], t["gu_beta"], t["gu_rout"], t["gu_rs2"], t["gu_s2"], c.group_size)
+        t["ut_dn"], k_dn = healer_tiles(t["u_dn"], t["dn_beta"], t["dn_rout"], t["dn_rs2"], t["dn_s2"], c.group_size)
         t["ut_scale"] = torch.tensor([k_gu, k_dn], dtype=torch.float32, device=self.device)
 
     def fp4_only_ok(self) -> bool:

@@ -326,3 +326,48 @@ def test_config_from_checkpoint(tmp_path):
     assert VP.find_layer_shard(tmp_path, 3) is None
     (tmp_path / "chronos-glm53-layer-00003-of-00046.safetensors").write_bytes(b"")
     assert VP.find_layer_shard(tmp_path, 3).name.endswith("00003-of-00046.safetensors")
+
+
+def test_healer_tiles_carry_the_correction_into_the_accumulator_basis():
+    """Load-time algebra of the fused healer: adding tiles . (h * scale) to the bank-pass accumulators BEFORE the epilogue
+    (x pair scale x scale_2, r_s2 sign, 128-row Walsh-Hadamard) and gathering with r_inv / r_s1 / beta afterwards gives
+    beta * r_s1 * z1[r_inv] + g * U h, the reference's healer term (chronos_1t/models/glm5_chronos_moe.py:149-195)."""
+    import math
+
+    import numpy as np
+    import torch
+
+    from chronos_b200 import keys
+    from chronos_b200.layout import healer_tiles
+
+    torch.manual_seed(0)
+    rows, cols, r, n_e, fold = 256, 128, 16, 4, 4
+    tabs = [keys.compact_tables(rows, cols, m, 101) for m in range(n_e)]
+    rout = torch.from_numpy(np.stack([t["rout"] for t in tabs]).view(np.int16).copy())
+    rs2 = torch.from_numpy(np.stack([t["rs2"] for t in tabs]).view(np.int32).copy())
+    u8 = torch.randint(0, 256, (n_e, rows, r), dtype=torch.uint8)
+    u8[(u8 & 0x7F) == 0x7F] = 0x30  # no NaN codes
+    beta, s2 = torch.rand(n_e) + 0.5, torch.tensor([3e-5])
+    tiles, scale = healer_tiles(u8, beta, rout, rs2, s2, fold)
+    assert tiles.dtype == torch.float16 and tiles.shape == (n_e, rows // 128, r // 8, 128, 8)
+    assert 2048.0 < float(tiles.abs().max()) <= 4096.0 and math.log2(scale) == round(math.log2(scale))
+    had = torch.ones(1, 1)
+    for _ in range(7):
+        had = torch.cat([torch.cat([had, had], 1), torch.cat([had, -had], 1)], 0)
+    had = had / math.sqrt(128.0)
+    g = 2.0  # pair scale
+    for e in range(n_e):
+        bits = ((rs2[e].long() & 0xFFFFFFFF)[:, None] >> torch.arange(32)) & 1
+        sign2 = (1.0 - 2.0 * bits.float()).view(rows)
+
+        def epilogue(acc):
+            return (had @ (acc * g * s2[0] * sign2).view(rows // 128, 128, 1)).view(rows)
+
+        ro = rout[e].int() & 0xFFFF
+        r_inv, s1 = (ro & 0x7FFF).long(), 1.0 - 2.0 * ((ro >> 15) & 1).float()
+        u = u8[e].view(torch.float8_e4m3fn).float()
+        h, acc = torch.randn(r), torch.randn(rows) * 1e4
+        want = beta[e] * s1 * epilogue(acc)[r_inv] + g * (u @ h)
+        tile_rows = tiles[e].float().permute(0, 2, 1, 3).reshape(rows, r)  # [block, unit, row, 8] -> [row, rank column]
+        got = beta[e] * s1 * epilogue(acc + tile_rows @ (h * scale))[r_inv]
+        assert float((got - want).norm() / want.norm()) < 2e-3
