@@ -373,6 +373,33 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     for (int i = 0; i < 4; ++i) v[i] *= 0.08838834764831845f;
 }
 
+// The same transform with a 128-block per HALF-warp: lane jl = lane & 15 holds elements 8 jl .. 8 jl + 7 of the block of
+// its half-warp (a warp then covers a 256-column stage). The butterfly stages run in the same order (element bits 0 .. 6)
+// with the same operands, so the results are bit-identical to fwht128_warp; three stages are in-lane and four cross
+// lanes, and everything per lane (scales, addresses, stores) is amortised over eight values instead of four.
+__device__ __forceinline__ void fwht128_half(float (&v)[8], int lane) {
+#pragma unroll
+    for (int s = 1; s < 8; s <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!(i & s)) {
+                const float a = v[i], b = v[i | s];
+                v[i] = a + b;
+                v[i | s] = a - b;
+            }
+#pragma unroll
+    for (int m = 1; m < 16; m <<= 1) {
+        const float sg = (lane & m) ? -1.0f : 1.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = __fmaf_rn(v[i], sg, o);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= 0.08838834764831845f;
+}
+
 // softplus as torch evaluates it (F.softplus, beta 1, threshold 20): x above the threshold passes through.
 __device__ __forceinline__ float softplus_f32(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
@@ -554,6 +581,44 @@ __device__ __forceinline__ void quantize_block_fp4x3(const float (&v)[4], int la
         const int n = t * TSTRIDE + prow;
         *reinterpret_cast<uint16_t*>(stage_img + c * (ROWS * 16) + n * 16 + b) = (uint16_t)(b01 | (b23 << 8));
         if ((lane & 3) == 0)
+            stage_img[ROWS * 128 + j * SFJ + (n >> 7) * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 + sidx] = (uint8_t)sc8;
+    }
+}
+
+// The same quantiser for a whole 256-column stage per warp: lane (half = lane >> 4, jl = lane & 15) holds elements
+// 8 jl .. 8 jl + 7 of 128-block `half` of the stage (the layout fwht128_half leaves). Same arithmetic per 16-element scale
+// block (two lanes instead of four), same bytes; 4-byte nibble stores.
+template <int ROWS, int TSTRIDE>
+__device__ __forceinline__ void quantize_stage_fp4x3(const float (&v)[8], int lane, uint8_t* __restrict__ stage_img, int prow) {
+    constexpr int SFJ = 512 * ((ROWS + 127) / 128);
+    float r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = v[i];
+    const int half = lane >> 4, jl = lane & 15;
+    const int c = half * 4 + (jl >> 2), b = 4 * (jl & 3);
+    const int j = half * 2 + (jl >> 3), sidx = (jl & 7) >> 1;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+        const float up = t == 0 ? 1.0f : (t == 1 ? 32.0f : 1024.0f);
+        float m = fmaxf(fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3]))),
+                        fmaxf(fmaxf(fabsf(r[4]), fabsf(r[5])), fmaxf(fabsf(r[6]), fabsf(r[7]))));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        const uint32_t sc8 = f32x2_to_e4m3x2(m * up * (1.0f / 6.0f), 0.0f) & 0xffu;
+        const float sdec = e4m3_to_f32((uint8_t)sc8);
+        const float inv = sdec > 0.0f ? __fdividef(up, sdec) : 0.0f;
+        const float back = sdec * (1.0f / up);  // exact: up is a power of two
+        uint32_t word = 0u;
+#pragma unroll
+        for (int h2 = 0; h2 < 4; ++h2) {
+            const uint32_t byte = f32x2_to_e2m1x2(r[2 * h2] * inv, r[2 * h2 + 1] * inv) & 0xffu;
+            const float2 q = e2m1x2_to_f32(byte);
+            r[2 * h2] = fmaf(-q.x, back, r[2 * h2]);
+            r[2 * h2 + 1] = fmaf(-q.y, back, r[2 * h2 + 1]);
+            word |= byte << (8 * h2);
+        }
+        const int n = t * TSTRIDE + prow;
+        *reinterpret_cast<uint32_t*>(stage_img + c * (ROWS * 16) + n * 16 + b) = word;
+        if ((jl & 1) == 0)
             stage_img[ROWS * 128 + j * SFJ + (n >> 7) * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 + sidx] = (uint8_t)sc8;
     }
 }

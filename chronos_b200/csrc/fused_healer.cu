@@ -94,33 +94,42 @@ __global__ void __launch_bounds__(kMidThreads) mid_fused_kernel(chronos_layer_t 
             const int pos = grp * kMidGroup + n, pair = p0 + n;
             const float* an = acts + (size_t)n * I;
             if (wsel == 0 && lane == 0) p.pscale_dn[pair] = gsc;
-            const uint16_t* cin = L.dn_cin + (size_t)(plain ? 0 : e) * I + lane * 4;
-            const uint32_t* cs2 = L.dn_cs2 + (size_t)(plain ? 0 : e) * (I / 32) + lane / 8;
+            // a warp takes a whole 256-column stage: its two half-warps each transform one 128-block, eight values per lane
+            const int half = lane >> 4, jl = lane & 15;
+            const uint16_t* cin = L.dn_cin + (size_t)(plain ? 0 : e) * I + half * 128 + jl * 8;
+            const uint32_t* cs2 = L.dn_cs2 + (size_t)(plain ? 0 : e) * (I / 32) + half * 4 + (jl >> 2);
             uint8_t* img0 = p.bq_dn + (size_t)item * (I / 256) * kWideStageBytes;
-            for (int blk = wsel; blk < I / 128; blk += W) {
-                const float4 a4 = *reinterpret_cast<const float4*>(an + blk * 128 + lane * 4);
-                const float s4[4] = {a4.x * gi, a4.y * gi, a4.z * gi, a4.w * gi};
-                store_half4(p.ac + (size_t)pair * I + blk * 128 + lane * 4, s4);  // natural order, for V_down . act
-                float v[4];
+            for (int st = wsel; st < I / 256; st += W) {
+                const int k0 = st * 256 + half * 128 + jl * 8;
+                const float4 a0 = *reinterpret_cast<const float4*>(an + k0), a1 = *reinterpret_cast<const float4*>(an + k0 + 4);
+                const float s8[8] = {a0.x * gi, a0.y * gi, a0.z * gi, a0.w * gi, a1.x * gi, a1.y * gi, a1.z * gi, a1.w * gi};
+                {   // natural order, for V_down . act
+                    const float lo4[4] = {s8[0], s8[1], s8[2], s8[3]}, hi4[4] = {s8[4], s8[5], s8[6], s8[7]};
+                    store_half4(p.ac + (size_t)pair * I + k0, lo4);
+                    store_half4(p.ac + (size_t)pair * I + k0 + 4, hi4);
+                }
+                float v[8];
                 if (plain) {
-                    v[0] = s4[0]; v[1] = s4[1]; v[2] = s4[2]; v[3] = s4[3];
-                } else {
-                    const uint2 ce = *reinterpret_cast<const uint2*>(cin + blk * 128);
-                    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int q = 0; q < 8; ++q) v[q] = s8[q];
+                } else {
+                    const uint4 ce = *reinterpret_cast<const uint4*>(cin + st * 256);
+                    const uint32_t ent[8] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16,
+                                             ce.z & 0xffffu, ce.z >> 16, ce.w & 0xffffu, ce.w >> 16};
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
                         const float av = an[ent[q] & 0x7fffu];
                         v[q] = (ent[q] >> 15) ? -av : av;
                     }
-                    fwht128_warp(v, lane);
-                    const uint32_t sw = cs2[blk * 4] >> ((lane & 7) * 4);
+                    fwht128_half(v, lane);
+                    const uint32_t sw = cs2[st * 8] >> ((jl & 3) * 8);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int q = 0; q < 8; ++q) {
                         if ((sw >> q) & 1u) v[q] = -v[q];
                         v[q] *= gi;
                     }
                 }
-                quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img0 + (size_t)(blk >> 1) * kWideStageBytes, blk & 1, pos);
+                quantize_stage_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img0 + (size_t)st * kWideStageBytes, pos);
             }
         }
     }
@@ -178,10 +187,12 @@ __global__ void __launch_bounds__(kCgThreads) combine_gather_kernel(chronos_laye
         for (int base = 0; base < n_ent; base += kCgRows) {
             if (base > 0) __syncthreads();  // the previous staging has been summed
             const int rows_here = min(kCgRows, n_ent - base);
-            for (int u = tid; u < rows_here * (H / 4); u += kCgThreads) {
-                const int jj = u / (H / 4), c = u % (H / 4);
+            for (int jj = 0; jj < rows_here; ++jj) {  // row by row: no division in the copy loop
                 const int pos = e_pos[base + jj];
-                if (pos >= 0) cp_async16(cg_rows + (size_t)jj * H + c * 4, p.y1 + (size_t)pos * H + c * 4);
+                if (pos < 0) continue;
+                const float* src = p.y1 + (size_t)pos * H;
+                float* dst = cg_rows + (size_t)jj * H;
+                for (int c = tid * 4; c < H; c += kCgThreads * 4) cp_async16(dst + c, src + c);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
             asm volatile("cp.async.wait_all;" ::: "memory");
@@ -193,6 +204,8 @@ __global__ void __launch_bounds__(kCgThreads) combine_gather_kernel(chronos_laye
                 const float g = e_gate[base + jj], beta = e_beta[base + jj];
                 const float* row = cg_rows + (size_t)jj * H;
                 const bool plain = e >= L.n_experts;
+                const bool tail = p.tail_dn != nullptr && !plain;
+                const float gb = g * beta;  // without a tail term the two factors of a routed entry are applied as one
                 const uint16_t* rout = L.dn_rout + (size_t)(plain ? 0 : e) * H;
 #pragma unroll
                 for (int gI = 0; gI < kCgMaxGroups; ++gI) {
@@ -208,19 +221,20 @@ __global__ void __launch_bounds__(kCgThreads) combine_gather_kernel(chronos_laye
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const float yv = row[ent[q] & 0x7fffu];
-                            v[q] = beta * ((ent[q] >> 15) ? -yv : yv);
+                            v[q] = (ent[q] >> 15) ? -yv : yv;
                         }
-                    }
-                    if (p.tail_dn != nullptr && !plain) {
-                        const float4 t4 = *reinterpret_cast<const float4*>(p.tail_dn + (size_t)pos * H + i0);
-                        v[0] += t4.x; v[1] += t4.y; v[2] += t4.z; v[3] += t4.w;
                     }
                     if (plain) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) acc[gI][q] += v[q];
+                    } else if (tail) {
+                        const float4 t4 = *reinterpret_cast<const float4*>(p.tail_dn + (size_t)pos * H + i0);
+                        const float tl[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[gI][q] = fmaf(g, fmaf(beta, v[q], tl[q]), acc[gI][q]);
                     } else {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) acc[gI][q] = fmaf(g, v[q], acc[gI][q]);
+                        for (int q = 0; q < 4; ++q) acc[gI][q] = fmaf(gb, v[q], acc[gI][q]);
                     }
                 }
             }

@@ -192,7 +192,7 @@ constexpr int kPreGuThreads = 512;
 __global__ void __launch_bounds__(kPreGuThreads) pre_gu_wide_kernel(chronos_layer_t L, Plan p) {
     extern __shared__ __align__(16) __half rows_s[];  // [kPreGuGroup][hidden]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = L.hidden, NB = H / 128, n_items = p.counters[3];
+    const int H = L.hidden, n_items = p.counters[3];
     constexpr int kGroups = kPairsPerWideItem / kPreGuGroup;
     for (int w = blockIdx.x; w < n_items * kGroups; w += gridDim.x) {
         const int grp = w / n_items, item = w % n_items;  // item fastest: neighbouring CTAs get comparable work
@@ -201,49 +201,55 @@ __global__ void __launch_bounds__(kPreGuThreads) pre_gu_wide_kernel(chronos_laye
         if (cnt <= 0) continue;
         const int e = p.pair_expert[start];
         __syncthreads();  // the rows of the previous group are no longer read
-        const int units = H / 8;  // 16-byte units of a row
-        for (int u = tid; u < cnt * units; u += kPreGuThreads) {
-            const int n = u / units, c = u % units;
-            const int t = p.pair_token[start + grp * kPreGuGroup + n];
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(rows_s + (size_t)n * H + c * 8)),
-                         "l"(p.x16 + (size_t)t * H + c * 8) : "memory");
+        for (int n = 0; n < cnt; ++n) {  // row by row: no division in the copy loop
+            const __half* src = p.x16 + (size_t)p.pair_token[start + grp * kPreGuGroup + n] * H;
+            for (int c = tid * 8; c < H; c += kPreGuThreads * 8)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(rows_s + n * H + c)), "l"(src + c) : "memory");
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
-        // warp -> (position n, 128-blocks blk0, blk0 + W, ...): everything that depends on the position alone is set up once
+        // warp -> (position n, stages st0, st0 + W, ...): everything that depends on the position alone is set up once.
+        // A warp takes a whole 256-column stage: its two half-warps each transform one 128-block, eight values per lane
         constexpr int W = kPreGuThreads / 32 / kPreGuGroup;
         const int n = warp % kPreGuGroup;
         if (n < cnt) {
             const int pos = grp * kPreGuGroup + n, pair = start + pos;
-            const __half* row = rows_s + n * H;
+            const int half = lane >> 4, jl = lane & 15;
+            const __half* row = rows_s + n * H + half * 128 + jl * 8;
             const bool plain = e >= L.n_experts;  // shared expert: plain weights, identity keys
-            const uint16_t* cin = L.gu_cin + (size_t)(plain ? 0 : e) * H + lane * 4;
-            const uint32_t* cs2 = L.gu_cs2 + (size_t)(plain ? 0 : e) * (H / 32) + lane / 8;
+            const uint16_t* cin = L.gu_cin + (size_t)(plain ? 0 : e) * H + half * 128 + jl * 8;
+            const uint32_t* cs2 = L.gu_cs2 + (size_t)(plain ? 0 : e) * (H / 32) + half * 4 + (jl >> 2);
             uint8_t* img0 = p.bq_gu + (size_t)item * (H / 256) * kWideStageBytes;
             if (warp < kPreGuGroup && lane == 0) p.pscale_gu[pair] = p.tok_scale[p.pair_token[pair]];
-            for (int blk = warp / kPreGuGroup; blk < NB; blk += W) {
-                float v[4];
+            for (int st = warp / kPreGuGroup; st < H / 256; st += W) {
+                float v[8];
                 if (plain) {
-                    const uint2 raw = *reinterpret_cast<const uint2*>(row + blk * 128 + lane * 4);
-                    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                    v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
-                } else {
-                    const uint2 ce = *reinterpret_cast<const uint2*>(cin + blk * 128);
-                    const uint32_t ent[4] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16};
+                    const uint4 raw = *reinterpret_cast<const uint4*>(row + st * 256);
+                    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float xv = __half2float(row[ent[i] & 0x7fffu]);
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+                        v[2 * i] = f.x;
+                        v[2 * i + 1] = f.y;
+                    }
+                } else {
+                    const uint4 ce = *reinterpret_cast<const uint4*>(cin + st * 256);
+                    const uint32_t ent[8] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16,
+                                             ce.z & 0xffffu, ce.z >> 16, ce.w & 0xffffu, ce.w >> 16};
+                    const __half* base = rows_s + n * H;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float xv = __half2float(base[ent[i] & 0x7fffu]);
                         v[i] = (ent[i] >> 15) ? -xv : xv;
                     }
-                    fwht128_warp(v, lane);
-                    const uint32_t sw = cs2[blk * 4] >> ((lane & 7) * 4);
+                    fwht128_half(v, lane);
+                    const uint32_t sw = cs2[st * 8] >> ((jl & 3) * 8);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
+                    for (int i = 0; i < 8; ++i)
                         if ((sw >> i) & 1u) v[i] = -v[i];
                 }
-                quantize_block_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img0 + (size_t)(blk >> 1) * kWideStageBytes, blk & 1, pos);
+                quantize_stage_fp4x3<kWideRows, kPairsPerWideItem>(v, lane, img0 + (size_t)st * kWideStageBytes, pos);
             }
         }
     }
