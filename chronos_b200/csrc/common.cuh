@@ -675,6 +675,54 @@ __device__ __forceinline__ void transform_dn_block(const chronos_layer_t& L, con
         if ((sw >> i) & 1u) v[i] = -v[i];
 }
 
+// A whole 256-column stage per warp (half-warp = 128-block, lane jl holds elements 8 jl .. 8 jl + 7): the same values as
+// two calls of the block forms above, with the per-lane work amortised over eight elements.
+__device__ __forceinline__ void transform_gu_stage(const chronos_layer_t& L, const void* __restrict__ x, int x_dtype, int t, int e,
+                                                   int st, int lane, float (&v)[8]) {
+    const int H = L.hidden, half = lane >> 4, jl = lane & 15;
+    const int k0 = st * 256 + half * 128 + jl * 8;
+    if (e >= L.n_experts) {  // shared expert: plain weights, identity keys
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = ld_act(x, x_dtype, (size_t)t * H + k0 + i);
+        return;
+    }
+    const uint4 ce = *reinterpret_cast<const uint4*>(L.gu_cin + (size_t)e * H + k0);
+    const uint32_t ent[8] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16, ce.z & 0xffffu, ce.z >> 16, ce.w & 0xffffu, ce.w >> 16};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float xv = ld_act(x, x_dtype, (size_t)t * H + (ent[i] & 0x7fffu));
+        v[i] = (ent[i] >> 15) ? -xv : xv;
+    }
+    fwht128_half(v, lane);
+    const uint32_t sw = L.gu_cs2[(size_t)e * (H / 32) + st * 8 + half * 4 + (jl >> 2)] >> ((jl & 3) * 8);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
+__device__ __forceinline__ void transform_dn_stage(const chronos_layer_t& L, const float* __restrict__ act, int e, int st, int lane,
+                                                   float (&v)[8]) {
+    const int I = L.inter, half = lane >> 4, jl = lane & 15;
+    const int k0 = st * 256 + half * 128 + jl * 8;
+    if (e >= L.n_experts) {
+        const float4 a0 = *reinterpret_cast<const float4*>(act + k0), a1 = *reinterpret_cast<const float4*>(act + k0 + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        return;
+    }
+    const uint4 ce = *reinterpret_cast<const uint4*>(L.dn_cin + (size_t)e * I + k0);
+    const uint32_t ent[8] = {ce.x & 0xffffu, ce.x >> 16, ce.y & 0xffffu, ce.y >> 16, ce.z & 0xffffu, ce.z >> 16, ce.w & 0xffffu, ce.w >> 16};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float a = act[ent[i] & 0x7fffu];
+        v[i] = (ent[i] >> 15) ? -a : a;
+    }
+    fwht128_half(v, lane);
+    const uint32_t sw = L.dn_cs2[(size_t)e * (I / 32) + st * 8 + half * 4 + (jl >> 2)] >> ((jl & 3) * 8);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if ((sw >> i) & 1u) v[i] = -v[i];
+}
+
 __device__ __forceinline__ void store_half4(__half* dst, const float (&v)[4]) {
     __half2 h01 = __halves2half2(f32_to_f16_sat(v[0]), f32_to_f16_sat(v[1]));
     __half2 h23 = __halves2half2(f32_to_f16_sat(v[2]), f32_to_f16_sat(v[3]));

@@ -315,23 +315,24 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(const Fr
     front_plan(a, s);
     stamp(3);
     // ---- phase 2: gate_up input transform of every (pair, 128-column block) into the FP4 activation images ----
-    const int H = a.L.hidden, nblk = H / 128;
+    const int H = a.L.hidden;
     const int gw = blockIdx.x * kFrontWarps + warp, n_warps = gridDim.x * kFrontWarps;
     {   // the gate_up pass adds the slices of tiles it splits between two CTAs: its output rows start at zero
         float4* z4 = reinterpret_cast<float4*>(a.p.z1);
         const long n4 = (long)s.n_pairs * 2 * a.L.inter / 4;
         for (long i = (long)blockIdx.x * kFrontThreads + tid; i < n4; i += (long)gridDim.x * kFrontThreads) z4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    for (int w = gw; w < s.n_pairs * nblk; w += n_warps) {
-        const int pair = w / nblk, blk = w % nblk;
+    const int nst = H / 256;  // warp task = (pair, 256-column stage): a 128-block per half-warp, eight values per lane
+    for (int w = gw; w < s.n_pairs * nst; w += n_warps) {
+        const int pair = w / nst, st = w % nst;
         const int t = s.pair_token[pair];
-        float v[4];
-        transform_gu_block(a.L, a.x, a.x_dtype, t, s.pair_expert[pair], blk, lane, v);
+        float v[8];
+        transform_gu_stage(a.L, a.x, a.x_dtype, t, s.pair_expert[pair], st, lane, v);
         const float gi = 1.0f / a.p.tok_scale[t];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] *= gi;
-        uint8_t* img = a.p.bq_gu + ((size_t)s.pair_item[pair] * (H / 256) + blk / 2) * 6144;
-        quantize_block_fp4x3<32, 8>(v, lane, img, blk & 1, s.pair_pos[pair]);
+        for (int i = 0; i < 8; ++i) v[i] *= gi;
+        uint8_t* img = a.p.bq_gu + ((size_t)s.pair_item[pair] * nst + st) * 6144;
+        quantize_stage_fp4x3<32, 8>(v, lane, img, s.pair_pos[pair]);
     }
     __syncthreads();
     stamp(4);
@@ -414,12 +415,12 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(const chronos_l
     }
     uint8_t* img0 = p.bq_dn + (size_t)p.pair_item[pair] * (I / 256) * 6144;
     const int pos = p.pair_pos[pair];
-    for (int blk = warp; blk < I / 128; blk += kMidThreads / 32) {
-        float v[4];
-        transform_dn_block(L, act_s, e, blk, lane, v);
+    for (int st = warp; st < I / 256; st += kMidThreads / 32) {  // a warp per 256-column stage
+        float v[8];
+        transform_dn_stage(L, act_s, e, st, lane, v);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] *= gi;
-        quantize_block_fp4x3<32, 8>(v, lane, img0 + (size_t)(blk / 2) * 6144, blk & 1, pos);
+        for (int i = 0; i < 8; ++i) v[i] *= gi;
+        quantize_stage_fp4x3<32, 8>(v, lane, img0 + (size_t)st * 6144, pos);
     }
 }
 
