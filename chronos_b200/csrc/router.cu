@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
 constexpr int kRtTok = 64, kRtExp = 16, kRtThreads = 512;
 constexpr int kRtStagesBf16 = 8, kRtStagesF32 = 5;  // steps in flight: enough to cover the L2 latency, bounded by shared memory
 
-template <bool BF16>
+template <bool BF16, bool SCALE>  // SCALE: the CTAs of the first expert tile also produce the token scales
 __global__ void __launch_bounds__(kRtThreads) router_logits_tiled_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                                          float* __restrict__ logits, int n_tokens, int n_experts,
                                                                          int hidden, float* __restrict__ tok_scale) {
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_tiled_kernel(const v
 #pragma unroll
         for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
     }
-    const bool do_scale = tok_scale != nullptr && e0 == 0 && we == 0;
+    const bool do_scale = SCALE && tok_scale != nullptr && e0 == 0 && we == 0;
     for (int s = 0; s < kRtStages - 1; ++s) {
         if (s < n_steps) stage_in(s);
         else asm volatile("cp.async.commit_group;" ::: "memory");
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kRtThreads) router_logits_tiled_kernel(const v
                 acc[a][b] = __fmaf_rn(xq.z, wv[b].z, acc[a][b]);
                 acc[a][b] = __fmaf_rn(xq.w, wv[b].w, acc[a][b]);
             }
-            ssq[a] = fmaf(xq.x, xq.x, fmaf(xq.y, xq.y, fmaf(xq.z, xq.z, fmaf(xq.w, xq.w, ssq[a]))));
+            if (SCALE && do_scale) ssq[a] = fmaf(xq.x, xq.x, fmaf(xq.y, xq.y, fmaf(xq.z, xq.z, fmaf(xq.w, xq.w, ssq[a]))));  // warp-uniform
         }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -456,10 +456,14 @@ int launch_router(const chronos_layer_t& L, const void* x, int x_dtype, int n_to
     } else if (n_tokens >= 256) {  // large batches: shared-memory tiles of 64 tokens x 16 experts
         const unsigned grid = (unsigned)(((n_tokens + kRtTok - 1) / kRtTok) * ((L.n_experts + kRtExp - 1) / kRtExp));
         const size_t smem = (size_t)(bf16 ? kRtStagesBf16 : kRtStagesF32) * (kRtTok * 128 * (bf16 ? 2 : 4) + kRtExp * 512);
-        if (int rc = ensure_dynamic_smem(bf16 ? reinterpret_cast<const void*>(router_logits_tiled_kernel<true>)
-                                              : reinterpret_cast<const void*>(router_logits_tiled_kernel<false>), smem, "router")) return rc;
-        if (bf16) router_logits_tiled_kernel<true><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
-        else router_logits_tiled_kernel<false><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, tok_scale);
+        // the token scales come from a kernel of their own here: carrying eight more sums per lane through the tile loop
+        // spilled registers in every CTA for the sake of one expert tile in eighteen
+        if (int rc = ensure_dynamic_smem(bf16 ? reinterpret_cast<const void*>(router_logits_tiled_kernel<true, false>)
+                                              : reinterpret_cast<const void*>(router_logits_tiled_kernel<false, false>), smem, "router")) return rc;
+        if (bf16) router_logits_tiled_kernel<true, false><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, nullptr);
+        else router_logits_tiled_kernel<false, false><<<grid, kRtThreads, smem, st>>>(x, L.router_w, logits, n_tokens, L.n_experts, L.hidden, nullptr);
+        if (tok_scale != nullptr)
+            if (int rc = launch_token_scale(x, x_dtype, n_tokens, L.hidden, tok_scale, st)) return rc;
     } else {
         const long tiles = (long)((L.n_experts + 3) / 4) * ((n_tokens + 3) / 4);
         const unsigned grid = (unsigned)((tiles + 7) / 8);

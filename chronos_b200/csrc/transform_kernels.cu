@@ -146,9 +146,18 @@ __global__ void __launch_bounds__(256) token_scale_kernel(const void* __restrict
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (t >= n_tokens) return;
     float ss = 0.0f;
-    for (int k = lane; k < hidden; k += 32) {
-        const float v = ld_act(x, x_dtype, (size_t)t * hidden + k);
-        ss = fmaf(v, v, ss);
+    if (hidden % 512 == 0) {  // 16 consecutive elements per lane and step (vector loads); the order is fixed all the same
+        for (int k = lane * 16; k < hidden; k += 512) {
+            float v[16];
+            ld_act16(x, x_dtype, (size_t)t * hidden + k, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
+        }
+    } else {
+        for (int k = lane; k < hidden; k += 32) {
+            const float v = ld_act(x, x_dtype, (size_t)t * hidden + k);
+            ss = fmaf(v, v, ss);
+        }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
