@@ -704,7 +704,7 @@ def main() -> None:
             try:
                 import argparse as _ap
 
-                d = run_decode(_ap.Namespace(**{**vars(args), "steps": min(args.steps, 50)}), sampler=False, with_cpu_baseline=False)
+                d = run_decode(_ap.Namespace(**{**vars(args), "steps": 100, "warmup": 10}), sampler=False, with_cpu_baseline=False)  # 175 us per step: cheap
                 res["decode_layer"] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "roofline", "layer_hbm", "stages_us", "e2e")}
             except Exception as exc:
                 res["decode_layer"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
