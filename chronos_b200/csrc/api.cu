@@ -464,6 +464,42 @@ int chronos_b200_ep_pack(const void* x, int x_dtype, const int32_t* ids, const f
                           overflow, block_rows, meta_block_ints, (cudaStream_t)stream);
 }
 
+int chronos_b200_ep_pack_peer(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                              int world, int experts_per_rank, int capacity, void* const* peer_bases, int my_rank, int block_rows,
+                              int32_t* slot_of, int32_t* overflow, void* stream) {
+    if (int rc = validate_ep(n_tokens, top_k, hidden, world, capacity)) return rc;
+    if (x_dtype != CHRONOS_DTYPE_F32 && x_dtype != CHRONOS_DTYPE_BF16) { set_error("ep_pack_peer: bad dtype"); return CHRONOS_E_ARG; }
+    if (experts_per_rank <= 0 || my_rank < 0 || my_rank >= world) { set_error("ep_pack_peer: bad rank / experts_per_rank"); return CHRONOS_E_SHAPE; }
+    const long meta_bytes = (long)(capacity + 1) * (2 * top_k + 2) * 4, row_bytes = (long)hidden * (x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+    if ((long)(block_rows - capacity) * row_bytes < meta_bytes) {
+        set_error("ep_pack_peer: block_rows (%d) leaves no room for %ld bytes of metadata behind %d rows", block_rows, meta_bytes, capacity);
+        return CHRONOS_E_SHAPE;
+    }
+    if (n_tokens > 0 && (!aligned16(x) || !peer_bases || !ids || !gates || !slot_of || !overflow)) {
+        set_error("ep_pack_peer: NULL or misaligned pointer");
+        return CHRONOS_E_ALIGN;
+    }
+    return launch_ep_pack_peer(x, x_dtype, ids, gates, n_tokens, top_k, hidden, world, experts_per_rank, capacity, peer_bases, my_rank,
+                               block_rows, slot_of, overflow, (cudaStream_t)stream);
+}
+
+int chronos_b200_ep_send_back_peer(const void* part_rows, int dtype, int hidden, int world, int block_rows, int capacity, int top_k,
+                                   const void* recv_base, void* const* peer_back, int my_rank, void* stream) {
+    if (int rc = validate_ep(0, top_k, hidden, world, capacity)) return rc;
+    if (dtype != CHRONOS_DTYPE_F32 && dtype != CHRONOS_DTYPE_BF16) { set_error("ep_send_back_peer: bad dtype"); return CHRONOS_E_ARG; }
+    if (block_rows < capacity || my_rank < 0 || my_rank >= world) { set_error("ep_send_back_peer: bad block_rows / rank"); return CHRONOS_E_SHAPE; }
+    if (!aligned16(part_rows) || !aligned16(recv_base) || !peer_back) { set_error("ep_send_back_peer: NULL or misaligned pointer"); return CHRONOS_E_ALIGN; }
+    return launch_ep_send_back_peer(part_rows, dtype, hidden, world, block_rows, capacity, top_k, recv_base, peer_back, my_rank, (cudaStream_t)stream);
+}
+
+int chronos_b200_ep_barrier(void* const* pads, int my_rank, int world, uint32_t epoch, int32_t* status, void* stream) {
+    if (!pads || !status || world < 1 || world > 1024 || my_rank < 0 || my_rank >= world) {
+        set_error("ep_barrier: bad arguments (world %d, rank %d)", world, my_rank);
+        return CHRONOS_E_ARG;
+    }
+    return launch_ep_barrier(pads, my_rank, world, epoch, status, (cudaStream_t)stream);
+}
+
 int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacity, int top_k, int32_t* ids_out, float* gates_out,
                                 int block_rows, long meta_block_ints, int tail_rows, void* stream) {
     if (int rc = validate_ep(0, top_k, 8, world, capacity)) return rc;

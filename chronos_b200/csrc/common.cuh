@@ -283,6 +283,12 @@ int launch_ep_unpack_meta(const int32_t* meta, int world, int capacity, int top_
                           long meta_block_ints, int tail_rows, cudaStream_t st);
 int launch_ep_combine(const void* back, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden, int world,
                       int capacity, void* y, int y_dtype, int block_rows, cudaStream_t st);
+int launch_ep_pack_peer(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                        int world, int experts_per_rank, int capacity, void* const* peer_bases, int my_rank, int block_rows,
+                        int32_t* slot_of, int32_t* overflow, cudaStream_t st);
+int launch_ep_send_back_peer(const void* part, int dtype, int hidden, int world, int block_rows, int capacity, int top_k, const void* recv_base,
+                             void* const* peer_back, int my_rank, cudaStream_t st);
+int launch_ep_barrier(void* const* pads, int my_rank, int world, uint32_t epoch, int32_t* status, cudaStream_t st);
 int launch_dequant_fp8_block(const uint8_t* w, const float* s, float* out, int rows, int cols, cudaStream_t st);
 int launch_shared_fp8(const chronos_layer_t& L, const void* x, int x_dtype, const Plan& p, int first, int count, void* y, int y_dtype,
                       cudaStream_t st);
@@ -739,6 +745,7 @@ constexpr uint32_t kWaitLimit = 1u << 20;  // polls of a ~1 us bounded try_wait 
 constexpr int kStatusBankStreamTimeout = 0x10;   // bank_stream_kernel: a ring wait expired
 constexpr int kStatusBankGemmTimeout = 0x20;     // bank_gemm_kernel
 constexpr int kStatusFp4ProbeTimeout = 0x40;     // fp4_mma_probe_kernel
+constexpr int kStatusEpBarrierTimeout = 0x800;     // ep_barrier_kernel: a peer's word did not arrive
 constexpr int kStatusBankFp4Timeout = 0x80;      // bank_fp4_kernel / bank_fp4_wide_kernel
 constexpr int kStatusRouterTimeout = 0x100;      // router_logits_small_kernel: staged rows never arrived
 constexpr int kStatusWaitProbeTimeout = 0x200;   // wait_probe_kernel: the wait it is built to lose

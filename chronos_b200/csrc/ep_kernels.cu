@@ -11,6 +11,8 @@
 //   ep_unpack_meta_kernel received metadata -> routing lists (ids local to this rank, gates) of the received rows
 //   ep_combine_kernel    y[t] = extra[t] + sum over ranks d (in order) of the partial row d returned for token t
 // The reference has no distributed path (single device); the partitioning is by slot, never inside a slot.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace chronos {
@@ -139,6 +141,150 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const TIN* __restrict__
     } else {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + (size_t)t * hidden + i0) = acc;
     }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The same exchange without a collective: every rank holds a receive buffer that its peers can write (symmetric memory
+// over NVLink), laid out as world blocks of block_rows rows (block s = what rank s sent: its rows, then the metadata).
+// The pack kernels store straight into the peers' buffers (block index = this rank), a barrier kernel then tells every
+// peer "my stores of this epoch are done" and waits for the same word from each of them.
+//   peer_bases[d]  base of rank d's receive buffer as mapped into this process (d = this rank: the local buffer)
+//   pads[d]        a few 32-bit words in rank d's memory that peers may write: word s = last epoch rank s finished
+// Plain peer stores and loads only. The wait is bounded; on expiry the status word gets kStatusEpBarrierTimeout.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr uint32_t kEpBarrierPolls = 1u << 22;  // ~0.25 us each: about a second
+
+__global__ void __launch_bounds__(kEpPlanThreads) ep_plan_peer_kernel(const int32_t* __restrict__ ids, int n_tokens, int top_k,
+                                                                      int experts_per_rank, int capacity, uint8_t* const* __restrict__ peer_bases,
+                                                                      int my_rank, size_t block_bytes, size_t meta_off, int32_t* __restrict__ slot_of,
+                                                                      int world, int32_t* __restrict__ overflow) {
+    __shared__ int warp_tot[kEpPlanThreads / 32 + 1];
+    const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lo = d * experts_per_rank, hi = lo + experts_per_rank;
+    int carry = 0;
+    for (int base = 0; base < n_tokens; base += kEpPlanThreads) {
+        const int t = base + tid;
+        int flag = 0;
+        if (t < n_tokens)
+            for (int j = 0; j < top_k; ++j) {
+                const int e = ids[(size_t)t * top_k + j];
+                flag |= (e >= lo && e < hi);
+            }
+        int inc = flag;
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, inc, s);
+            if (lane >= s) inc += o;
+        }
+        __syncthreads();  // warp_tot of the previous chunk has been read
+        if (lane == 31) warp_tot[warp] = inc;
+        __syncthreads();
+        if (warp == 0) {
+            const int w = warp_tot[lane];
+            int winc = w;
+#pragma unroll
+            for (int s = 1; s < 32; s <<= 1) {
+                const int o = __shfl_up_sync(0xffffffffu, winc, s);
+                if (lane >= s) winc += o;
+            }
+            warp_tot[lane] = winc - w;
+            if (lane == 31) warp_tot[32] = winc;
+        }
+        __syncthreads();
+        const int pos = carry + warp_tot[warp] + inc - flag;
+        if (t < n_tokens) slot_of[(size_t)t * world + d] = (flag && pos < capacity) ? pos : -1;
+        if (flag && pos >= capacity) atomicOr(overflow, 1);
+        carry += warp_tot[32];
+    }
+    if (tid == 0) {
+        int32_t* meta = reinterpret_cast<int32_t*>(peer_bases[d] + (size_t)my_rank * block_bytes + meta_off);
+        meta[(size_t)capacity * (2 * top_k + 2)] = min(carry, capacity);
+    }
+}
+
+__global__ void __launch_bounds__(128) ep_pack_rows_peer_kernel(const uint4* __restrict__ x, int row_vec16, const int32_t* __restrict__ ids,
+                                                                const float* __restrict__ gates, int top_k, int experts_per_rank,
+                                                                const int32_t* __restrict__ slot_of, int world,
+                                                                uint8_t* const* __restrict__ peer_bases, int my_rank, size_t block_bytes,
+                                                                size_t meta_off) {
+    const int t = blockIdx.x, d = blockIdx.y;
+    const int p = slot_of[(size_t)t * world + d];
+    if (p < 0) return;
+    uint8_t* block = peer_bases[d] + (size_t)my_rank * block_bytes;
+    const uint4* src = x + (size_t)t * row_vec16;
+    uint4* dst = reinterpret_cast<uint4*>(block) + (size_t)p * row_vec16;
+    for (int i = threadIdx.x; i < row_vec16; i += 128) dst[i] = src[i];
+    const int m = 2 * top_k + 2;
+    int32_t* mrow = reinterpret_cast<int32_t*>(block + meta_off) + (size_t)p * m;
+    if (threadIdx.x == 0) mrow[0] = t;
+    if (threadIdx.x < top_k) {
+        const int e = ids[(size_t)t * top_k + threadIdx.x] - d * experts_per_rank;
+        const bool mine = e >= 0 && e < experts_per_rank;
+        mrow[1 + threadIdx.x] = mine ? e : -1;
+        mrow[1 + top_k + threadIdx.x] = mine ? __float_as_int(gates[(size_t)t * top_k + threadIdx.x]) : 0;
+    }
+}
+
+// The way back: block s of the local partial-sum rows (rows of the tokens rank s sent; their number is the count word of
+// the metadata rank s sent along) goes into block `my_rank` of rank s's return buffer.
+__global__ void __launch_bounds__(256) ep_send_back_peer_kernel(const uint4* __restrict__ part, int row_vec16, int block_rows,
+                                                                const uint8_t* __restrict__ recv_base, size_t block_bytes, size_t meta_off,
+                                                                int capacity, int top_k, uint8_t* const* __restrict__ peer_back, int my_rank) {
+    const int s = blockIdx.y;
+    const int cnt = reinterpret_cast<const int32_t*>(recv_base + (size_t)s * block_bytes + meta_off)[(size_t)capacity * (2 * top_k + 2)];
+    const uint4* src = part + (size_t)s * block_rows * row_vec16;
+    uint4* dst = reinterpret_cast<uint4*>(peer_back[s] + (size_t)my_rank * block_bytes);
+    const long n = (long)min(cnt, capacity) * row_vec16;
+    for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long)gridDim.x * 256) dst[i] = src[i];
+}
+
+__global__ void __launch_bounds__(1024) ep_barrier_kernel(uint32_t* const* __restrict__ pads, int my_rank, int world, uint32_t epoch,
+                                                          int32_t* __restrict__ status) {
+    const int d = threadIdx.x;
+    if (d >= world) return;
+    __threadfence_system();  // the stores of the kernels before this one are visible to the peers before the word below
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(pads[d] + my_rank), "r"(epoch) : "memory");
+    const uint32_t* mine = pads[my_rank] + d;
+    bool ok = false;
+    for (uint32_t poll = 0; poll < kEpBarrierPolls; ++poll) {
+        uint32_t seen;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(seen) : "l"(mine) : "memory");
+        if ((int32_t)(seen - epoch) >= 0) { ok = true; break; }
+        __nanosleep(200);
+    }
+    if (!ok) atomicOr(status, kStatusEpBarrierTimeout);
+}
+
+int launch_ep_pack_peer(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                        int world, int experts_per_rank, int capacity, void* const* peer_bases, int my_rank, int block_rows,
+                        int32_t* slot_of, int32_t* overflow, cudaStream_t st) {
+    if (n_tokens <= 0) return CHRONOS_OK;
+    const size_t row_bytes = (size_t)hidden * (x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+    const size_t block_bytes = (size_t)block_rows * row_bytes, meta_off = (size_t)capacity * row_bytes;
+    uint8_t* const* bases = reinterpret_cast<uint8_t* const*>(peer_bases);
+    ep_plan_peer_kernel<<<(unsigned)world, kEpPlanThreads, 0, st>>>(ids, n_tokens, top_k, experts_per_rank, capacity, bases, my_rank, block_bytes,
+                                                                   meta_off, slot_of, world, overflow);
+    if (int rc = check_launch("ep_plan_peer")) return rc;
+    ep_pack_rows_peer_kernel<<<dim3((unsigned)n_tokens, (unsigned)world), 128, 0, st>>>(reinterpret_cast<const uint4*>(x), (int)(row_bytes / 16), ids,
+                                                                                       gates, top_k, experts_per_rank, slot_of, world, bases, my_rank,
+                                                                                       block_bytes, meta_off);
+    return check_launch("ep_pack_rows_peer");
+}
+
+int launch_ep_send_back_peer(const void* part, int dtype, int hidden, int world, int block_rows, int capacity, int top_k, const void* recv_base,
+                             void* const* peer_back, int my_rank, cudaStream_t st) {
+    const size_t row_bytes = (size_t)hidden * (dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+    const size_t block_bytes = (size_t)block_rows * row_bytes, meta_off = (size_t)capacity * row_bytes;
+    const int per_peer = std::max(1, 4 * device_sm_count() / world);
+    ep_send_back_peer_kernel<<<dim3((unsigned)per_peer, (unsigned)world), 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(part), (int)(row_bytes / 16), block_rows, reinterpret_cast<const uint8_t*>(recv_base), block_bytes, meta_off,
+        capacity, top_k, reinterpret_cast<uint8_t* const*>(peer_back), my_rank);
+    return check_launch("ep_send_back_peer");
+}
+
+int launch_ep_barrier(void* const* pads, int my_rank, int world, uint32_t epoch, int32_t* status, cudaStream_t st) {
+    ep_barrier_kernel<<<1, 1024, 0, st>>>(reinterpret_cast<uint32_t* const*>(pads), my_rank, world, epoch, status);
+    return check_launch("ep_barrier");
 }
 
 int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,

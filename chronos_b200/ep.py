@@ -22,6 +22,7 @@ tests of the host logic, which substitute their own pack / compute / combine cal
 from __future__ import annotations
 
 import math
+import os
 from typing import Callable, Optional
 
 import torch
@@ -61,6 +62,38 @@ def block_capacity(tokens_local: int, world: int, top_k: int, capacity_factor: O
 _OVERFLOW_FLAGS: dict[torch.device, torch.Tensor] = {}  # one device flag per GPU, shared by all layers: one read per step
 
 
+class _PeerExchange:
+    """Receive and return buffers of one exchange shape in symmetric memory (every rank's buffers are mapped into every
+    other rank's address space), shared by all layers of the process: a layer's two barriers order its use of them against
+    the layers before and after. `recv` [world * block_rows + tokens, H]: block s = what rank s sent (rows, then metadata),
+    the tail = this rank's own tokens; `back` [world, block_rows, H]: block s = the partial sums rank s returned."""
+
+    def __init__(self, group, world: int, rank: int, tokens: int, block_rows: int, hidden: int, dtype: torch.dtype, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        name = group.group_name if group is not None else dist.group.WORLD.group_name
+        self.recv = symm_mem.empty((world * block_rows + tokens, hidden), dtype=dtype, device=device)
+        self.back = symm_mem.empty((world, block_rows, hidden), dtype=dtype, device=device)
+        self.recv.zero_()
+        self.back.zero_()
+        self._h_recv = symm_mem.rendezvous(self.recv, name)
+        self._h_back = symm_mem.rendezvous(self.back, name)
+        self.recv_bases = self._h_recv.buffer_ptrs_dev       # device array of world base pointers
+        self.back_bases = self._h_back.buffer_ptrs_dev
+        self.pads = self._h_recv.signal_pad_ptrs_dev         # device array of world pointers to peer-writable words
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = 0
+        self.world, self.rank = world, rank
+
+    def barrier(self) -> None:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        _lib.check(_lib.lib().chronos_b200_ep_barrier(self.pads, self.rank, self.world, self.epoch, self.status.data_ptr(),
+                                                    torch.cuda.current_stream().cuda_stream))
+
+
+_PEER_EXCHANGES: dict[tuple, Optional[_PeerExchange]] = {}
+
+
 class EpConfigMismatch(RuntimeError):
     """Raised on EVERY rank, before any data collective, when the ranks disagree on the exchange geometry."""
 
@@ -90,6 +123,9 @@ class ExpertParallelMoE:
         self.combine_fn = combine_fn or self._combine_cuda
         self.phase_events = None   # set to [] to record (name, start, end) CUDA events of the next forward
         self._checked: set[tuple] = set()
+        # peer stores over NVLink instead of the all-to-all (CUDA ranks of one box with symmetric memory; every rank must
+        # succeed in setting it up, else all of them stay with the collective); CHRONOS_B200_EP_PEER=0 switches it off
+        self.use_peer = pack_fn is None and compute_fn is None and combine_fn is None and os.environ.get("CHRONOS_B200_EP_PEER", "1") != "0"
 
     def _mark(self, name: str):
         """Context manager recording a CUDA event pair around a phase when `phase_events` is a list."""
@@ -170,6 +206,67 @@ class ExpertParallelMoE:
                                                     y.data_ptr(), _lib.DTYPE_F32, block_rows, torch.cuda.current_stream().cuda_stream))
         return y
 
+    def _peer_exchange(self, x: torch.Tensor, capacity: int) -> Optional[_PeerExchange]:
+        """The symmetric buffers of this exchange shape, or None when any rank could not set them up (decided together,
+        once per shape and process; the layers of a stack share the result)."""
+        if not self.use_peer or x.device.type != "cuda":
+            return None
+        tl, h = x.shape
+        block_rows = capacity + self._meta_rows(capacity, h, x.element_size())
+        key = (id(self.group), self.world, tl, block_rows, h, x.dtype, x.device)
+        if key not in _PEER_EXCHANGES:
+            ex, why = None, ""
+            try:
+                ex = _PeerExchange(self.group, self.world, self.rank, tl, block_rows, h, x.dtype, x.device)
+            except Exception as exc:  # no symmetric memory on this system / for this group: the collective path serves
+                why = f"{type(exc).__name__}: {exc}"[:200]
+            table: list = [None] * self.world
+            dist.all_gather_object(table, ex is not None, group=self.group)
+            if not all(table):
+                ex = None
+                if self.rank == 0 and why:
+                    print(f"chronos_b200: expert-parallel exchange stays on the all-to-all ({why})", flush=True)
+            _PEER_EXCHANGES[key] = ex
+        return _PEER_EXCHANGES[key]
+
+    def _forward_peer(self, ex: _PeerExchange, x_local: torch.Tensor, ids, gates, capacity: int) -> torch.Tensor:
+        """dispatch / compute / combine with peer stores: the pack kernel writes block `rank` of every peer's receive buffer,
+        a barrier, the expert pass over the receive buffer, the partial rows go into block `rank` of every peer's return
+        buffer, a barrier, the sum."""
+        tl, h = x_local.shape
+        k, w = self.cfg.top_k, self.world
+        dev = x_local.device
+        block_rows = ex.back.shape[1]
+        stream = torch.cuda.current_stream().cuda_stream
+        with self._mark("dispatch"):
+            slot_of = torch.empty((tl, w), dtype=torch.int32, device=dev)
+            flag = _OVERFLOW_FLAGS.get(dev)
+            if flag is None:
+                flag = _OVERFLOW_FLAGS[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+            _lib.check(_lib.lib().chronos_b200_ep_pack_peer(x_local.data_ptr(), _DTYPES[x_local.dtype], ids.data_ptr(), gates.data_ptr(), tl, k, h,
+                                                          w, self.n_local, capacity, ex.recv_bases, self.rank, block_rows,
+                                                          slot_of.data_ptr(), flag.data_ptr(), stream))
+            ex.recv[w * block_rows:].copy_(x_local)
+            ex.barrier()
+        with self._mark("routed_experts"):
+            recv_rows = ex.recv[:w * block_rows].view(w, block_rows, h)
+            part, shared_rows = self._compute_cuda(recv_rows, None, x_local, capacity, recv_all=ex.recv)
+        with self._mark("combine"):
+            _lib.check(_lib.lib().chronos_b200_ep_send_back_peer(part.data_ptr(), _DTYPES[part.dtype], h, w, block_rows, capacity, k,
+                                                               ex.recv.data_ptr(), ex.back_bases, self.rank, stream))
+            ex.barrier()
+            y = self._combine_cuda(ex.back, slot_of, shared_rows, capacity)
+        return y
+
+    def peer_status(self) -> int:
+        """Status words of the peer-exchange barriers of this process OR-ed together (0 = every barrier completed);
+        reading them synchronises, so call it once per step."""
+        word = 0
+        for ex in _PEER_EXCHANGES.values():
+            if ex is not None:
+                word |= int(ex.status.item())
+        return word
+
     def overflowed(self) -> bool:
         """True when a dispatch block of ANY layer on this rank's device overflowed since the last call (the layers share
         one device flag; reading it synchronises, so call it once per step, not per layer)."""
@@ -193,6 +290,9 @@ class ExpertParallelMoE:
         if self.world == 1 and self.layer is not None:  # every expert is local: nothing to exchange
             with self._mark("routed_experts"):
                 return self.layer.routed_forward(x_local, ids, gates, with_shared=self.layer.n_shared_experts > 0, out_dtype=torch.float32)
+        ex = self._peer_exchange(x_local, capacity)
+        if ex is not None:
+            return self._forward_peer(ex, x_local, ids, gates, capacity)
         with self._mark("dispatch"):
             send_rows, send_meta, slot_of = self.pack_fn(x_local, ids, gates, capacity)
             # received blocks and, behind them, the home tokens' own rows (they take the shared expert in the same pass)

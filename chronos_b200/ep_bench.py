@@ -77,8 +77,11 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         dist.barrier()
         ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        status = max(l.layer.device_status() for l in layers[-1:])
+        status = max(l.layer.device_status() for l in layers[-1:]) | layers[0].peer_status()  # incl. the exchange barriers' word
         overflow = stack.overflowed()  # a dispatch block too small for the routing would have dropped tokens: the run is void then
+        from .ep import _PEER_EXCHANGES
+
+        peer = any(ex is not None for ex in _PEER_EXCHANGES.values())
         # end to end: pinned host tokens -> device -> stack -> pinned host result
         host_in = h0.cpu().pin_memory()
         host_out = torch.empty_like(host_in).pin_memory()
@@ -157,7 +160,9 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
                          "unit": "TFLOP/s", "frac": (owned + tl) * bank_flops / (gemm_ms * 1e-3) / 1e12 / 9000.0, "traffic": None,
                          "pairs_on_rank0": owned + tl, "bank_pass_ms": gemm_ms},
             "phase_us_per_layer_rank0": {k_: round(v, 1) for k_, v in phase_us.items()},
-            "dispatch": {"kind": "deduplicated all-to-all, fixed-capacity blocks" if world > 1 else "none (one rank)",
+            "dispatch": {"kind": ("none (one rank)" if world == 1 else
+                                  ("deduplicated exchange by peer stores over NVLink, fixed-capacity blocks, two bounded barriers per layer"
+                                   if peer else "deduplicated all-to-all, fixed-capacity blocks")),
                          "block_capacity_rows": block_capacity(tl, world, cfg.top_k), "tokens_per_rank": tl, "overflowed": overflow},
             "parity": parity,
             "device_status": status,

@@ -258,6 +258,28 @@ int chronos_b200_ep_unpack_meta(const int32_t* recv_meta, int world, int capacit
 int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slot_of, const void* extra, int n_tokens, int hidden,
                             int world, int capacity, void* y, int y_dtype, int block_rows, void* stream);
 
+/* The same exchange by peer stores instead of a collective (ranks of one NVLink box whose receive buffers are mapped into
+ * each other's address space, e.g. torch symmetric memory).  A receive buffer is world blocks of block_rows rows of hidden
+ * elements; block s holds what rank s sent: capacity rows, then the block's metadata ((capacity + 1) x (2 top_k + 2) int32 as
+ * in chronos_b200_ep_pack) starting at row `capacity`.
+ *   chronos_b200_ep_pack_peer       fills block `my_rank` of EVERY rank's buffer: peer_bases = device array of world base
+ *                                   pointers (entry d = rank d's buffer as mapped here; entry my_rank = the local buffer).
+ *   chronos_b200_ep_send_back_peer  copies block s of part_rows [world, block_rows, hidden] (as many rows as the count word of
+ *                                   the metadata received from rank s, read at recv_base) into block `my_rank` of peer_back[s].
+ *   chronos_b200_ep_barrier         pads = device array of world pointers to a few peer-writable 32-bit words per rank (word s
+ *                                   of rank d's pad = last epoch rank s finished).  Tells every peer that this rank's stores
+ *                                   issued before it on the stream are done and waits for the same from every peer; epoch must
+ *                                   grow by one per call on every rank (wrap-around is fine).  The wait is bounded (about a
+ *                                   second); on expiry CHRONOS_STATUS_EP_BARRIER is raised in *status (device int32) and the
+ *                                   kernel returns - the caller must read it before it trusts the step.
+ * Plain peer loads and stores only.  No counterpart in the reference. */
+int chronos_b200_ep_pack_peer(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,
+                              int world, int experts_per_rank, int capacity, void* const* peer_bases, int my_rank, int block_rows,
+                              int32_t* slot_of, int32_t* overflow, void* stream);
+int chronos_b200_ep_send_back_peer(const void* part_rows, int dtype, int hidden, int world, int block_rows, int capacity, int top_k,
+                                   const void* recv_base, void* const* peer_back, int my_rank, void* stream);
+int chronos_b200_ep_barrier(void* const* pads, int my_rank, int world, uint32_t epoch, int32_t* status, void* stream);
+
 /* Operand-format probe of the block-scaled FP4 tensor-core path (tcgen05.mma kind::mxf4nvf4, e2m1 operands with a
  * ue4m3 scale per 16 elements): d_out f32 [128, b_rows] = (A * scaleA) (B * scaleB)^T over n_stages * 256 columns;
  * b_rows a multiple of 16 in 16..256 (32 = streaming regime, 192 = tensor regime).
@@ -289,6 +311,7 @@ int chronos_b200_set_stage_events(void** events, int n_events);
  *   CHRONOS_STATUS_FP4_PROBE   0x40   chronos_b200_fp4_mma_probe                     CHRONOS_STATUS_BANK_FP4  0x80  FP4 bank passes
  *   CHRONOS_STATUS_ROUTER      0x100  router row staging                             CHRONOS_STATUS_WAIT_PROBE 0x200 chronos_b200_wait_probe
  *   CHRONOS_STATUS_GRID_SYNC   0x400  a fused decode kernel waiting for the other CTAs of its grid
+ *   CHRONOS_STATUS_EP_BARRIER  0x800  chronos_b200_ep_barrier: a peer's word did not arrive
  * Read it after synchronising the stream.  Returns -1 on bad arguments.
  * No counterpart in the reference (its kernels have no device-side waits). */
 #define CHRONOS_STATUS_BANK_STREAM 0x10
@@ -298,6 +321,7 @@ int chronos_b200_set_stage_events(void** events, int n_events);
 #define CHRONOS_STATUS_ROUTER 0x100
 #define CHRONOS_STATUS_WAIT_PROBE 0x200
 #define CHRONOS_STATUS_GRID_SYNC 0x400
+#define CHRONOS_STATUS_EP_BARRIER 0x800
 long chronos_b200_workspace_status_offset(const chronos_layer_t* layer, int n_tokens);
 
 /* Exercises the give-up path of the library's bounded waits without any fault: a one-warp kernel waits, through the

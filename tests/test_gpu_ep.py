@@ -1,5 +1,6 @@
-"""Expert-parallel path on real GPUs (needs >= 2): 2 ranks over NCCL (deduplicated all-to-all dispatch / combine) must
-reproduce the CPU oracle on layer 0 and a single-GPU evaluation of the same 2-layer stack (residual + RMSNorm wiring)."""
+"""Expert-parallel path on real GPUs (needs >= 2): 2 ranks (deduplicated dispatch / combine, once by peer stores into
+symmetric memory with the library's bounded barrier, once by the NCCL all-to-all) must reproduce the CPU oracle on layer 0
+and a single-GPU evaluation of the same 2-layer stack (residual + RMSNorm wiring)."""
 import os
 import socket
 import sys
@@ -18,9 +19,9 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, ret):
+def _worker(rank: int, world: int, port: int, ret, peer: bool):
     sys.path.insert(0, str(ROOT))
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", CHRONOS_B200_EP_PEER="1" if peer else "0")
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
@@ -56,25 +57,31 @@ def _worker(rank: int, world: int, port: int, ret):
         ids0, gates0 = layers[0].route_fn(x0)
         y0 = layers[0](x0)
         par = layer_parity(cfg, layers[0], 3, x0, y0, ids0, gates0, dev, n_sample=6)
-        ret[rank] = (err, par["rel_l2"], par["router_ids_equal"], layers[0].overflowed())
+        from chronos_b200.ep import _PEER_EXCHANGES
+
+        used_peer = any(ex is not None for ex in _PEER_EXCHANGES.values())
+        ret[rank] = (err, par["rel_l2"], par["router_ids_equal"], layers[0].overflowed(), used_peer, layers[0].peer_status())
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_expert_parallel_stack_matches_single_gpu():
+@pytest.mark.parametrize("peer", [True, False])
+def test_expert_parallel_stack_matches_single_gpu(peer):
     import torch.multiprocessing as mp
 
     world = 2
     ctx = mp.get_context("spawn")
     ret = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, ret)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, ret, peer)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=600)
         assert p.exitcode == 0
     for r in range(world):
-        err, oracle_err, ids_ok, overflow = ret[r]
-        assert err < 1e-2 and oracle_err < 1e-2 and ids_ok and not overflow, (r, ret[r])
+        err, oracle_err, ids_ok, overflow, used_peer, peer_status = ret[r]
+        assert err < 1e-2 and oracle_err < 1e-2 and ids_ok and not overflow and peer_status == 0, (r, ret[r])
+        assert not used_peer if not peer else True  # the switch must hold; with it on, a system without symmetric memory falls back
+    print("exchange:", "peer stores" if ret[0][4] else "all-to-all", [tuple(ret[r])[:2] for r in range(world)])
