@@ -7,13 +7,16 @@ RMSNorm and the shared expert are replicated; tokens are data-parallel.
 Per layer, stream-ordered and free of host synchronisation:
   route     every rank routes its own tokens (global expert ids + gates);
   dispatch  a token's normed hidden row goes ONCE to every rank that owns at least one of its experts, with its expert
-            ids local to that rank and their gates: a device kernel packs fixed-capacity blocks per destination
-            (`chronos_b200_ep_pack`), ONE all-to-all with equal splits moves rows and metadata (the metadata of a block
-            sits behind its rows) - no split sizes ever travel through the host;
+            ids local to that rank and their gates: device kernels fill fixed-capacity blocks per destination (rows, then
+            the block's metadata). On CUDA ranks of one box the kernels store the blocks straight into the peers' receive
+            buffers (symmetric memory over NVLink; `chronos_b200_ep_pack_peer`) and a barrier kernel with bounded waits
+            (`chronos_b200_ep_barrier`) closes the phase; otherwise ONE all-to-all with equal splits moves them
+            (`chronos_b200_ep_pack`) - no split sizes ever travel through the host;
   compute   each rank evaluates the received rows' entries (all of them are its own experts) and, in the same pass,
             the shared expert of the tokens it is the home of;
-  combine   ONE bf16 partial-sum row per received token goes back the same way, and the home rank adds the partial rows in
-            rank order to the shared expert's row (`chronos_b200_ep_combine`).
+  combine   ONE bf16 partial-sum row per received token goes back the same way (`chronos_b200_ep_send_back_peer` + barrier,
+            or the all-to-all), and the home rank adds the partial rows in rank order to the shared expert's row
+            (`chronos_b200_ep_combine`).
 A block's capacity covers the expected number of tokens per destination plus six standard deviations; a batch routed
 so unevenly that a block overflows raises a device flag that `overflowed()` reads (the caller then repeats the step with
 `capacity_factor = 1`, which always fits). One process per GPU; `torch.distributed` (NCCL over NVLink, or gloo in CPU
