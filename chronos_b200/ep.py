@@ -72,6 +72,9 @@ class _PeerExchange:
     the tail = this rank's own tokens; `back` [world, block_rows, H]: block s = the partial sums rank s returned."""
 
     def __init__(self, group, world: int, rank: int, tokens: int, block_rows: int, hidden: int, dtype: torch.dtype, device: torch.device):
+        # plain peer loads and stores only: the buffers are not bound to an NVLink multicast object (a rank that dies while
+        # its memory is bound to one can raise link faults on its peers)
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
 
         name = group.group_name if group is not None else dist.group.WORLD.group_name
