@@ -208,10 +208,15 @@ __global__ void __launch_bounds__(128) ep_pack_rows_peer_kernel(const uint4* __r
                                                                 uint8_t* const* __restrict__ peer_bases, int my_rank, size_t block_bytes,
                                                                 size_t meta_off) {
     const int t = blockIdx.x, d = blockIdx.y;
+    const uint4* src = x + (size_t)t * row_vec16;
+    if (d == world) {  // the token's own copy behind the blocks of the local buffer (it takes the shared expert at home)
+        uint4* home = reinterpret_cast<uint4*>(peer_bases[my_rank] + (size_t)world * block_bytes) + (size_t)t * row_vec16;
+        for (int i = threadIdx.x; i < row_vec16; i += 128) home[i] = src[i];
+        return;
+    }
     const int p = slot_of[(size_t)t * world + d];
     if (p < 0) return;
     uint8_t* block = peer_bases[d] + (size_t)my_rank * block_bytes;
-    const uint4* src = x + (size_t)t * row_vec16;
     uint4* dst = reinterpret_cast<uint4*>(block) + (size_t)p * row_vec16;
     for (int i = threadIdx.x; i < row_vec16; i += 128) dst[i] = src[i];
     const int m = 2 * top_k + 2;
@@ -265,7 +270,7 @@ int launch_ep_pack_peer(const void* x, int x_dtype, const int32_t* ids, const fl
     ep_plan_peer_kernel<<<(unsigned)world, kEpPlanThreads, 0, st>>>(ids, n_tokens, top_k, experts_per_rank, capacity, bases, my_rank, block_bytes,
                                                                    meta_off, slot_of, world, overflow);
     if (int rc = check_launch("ep_plan_peer")) return rc;
-    ep_pack_rows_peer_kernel<<<dim3((unsigned)n_tokens, (unsigned)world), 128, 0, st>>>(reinterpret_cast<const uint4*>(x), (int)(row_bytes / 16), ids,
+    ep_pack_rows_peer_kernel<<<dim3((unsigned)n_tokens, (unsigned)world + 1), 128, 0, st>>>(reinterpret_cast<const uint4*>(x), (int)(row_bytes / 16), ids,
                                                                                        gates, top_k, experts_per_rank, slot_of, world, bases, my_rank,
                                                                                        block_bytes, meta_off);
     return check_launch("ep_pack_rows_peer");

@@ -252,8 +252,7 @@ class ExpertParallelMoE:
             _lib.check(_lib.lib().chronos_b200_ep_pack_peer(x_local.data_ptr(), _DTYPES[x_local.dtype], ids.data_ptr(), gates.data_ptr(), tl, k, h,
                                                           w, self.n_local, capacity, ex.recv_bases, self.rank, block_rows,
                                                           slot_of.data_ptr(), flag.data_ptr(), stream))
-            ex.recv[w * block_rows:].copy_(x_local)
-            ex.barrier()
+            ex.barrier()  # (the pack kernels also put x_local behind the blocks of the local buffer)
         with self._mark("routed_experts"):
             recv_rows = ex.recv[:w * block_rows].view(w, block_rows, h)
             part, shared_rows = self._compute_cuda(recv_rows, None, x_local, capacity, recv_all=ex.recv)

@@ -263,7 +263,8 @@ int chronos_b200_ep_combine(const void* back_rows, int dtype, const int32_t* slo
  * elements; block s holds what rank s sent: capacity rows, then the block's metadata ((capacity + 1) x (2 top_k + 2) int32 as
  * in chronos_b200_ep_pack) starting at row `capacity`.
  *   chronos_b200_ep_pack_peer       fills block `my_rank` of EVERY rank's buffer: peer_bases = device array of world base
- *                                   pointers (entry d = rank d's buffer as mapped here; entry my_rank = the local buffer).
+ *                                   pointers (entry d = rank d's buffer as mapped here; entry my_rank = the local buffer);
+ *                                   also copies x behind the world blocks of the local buffer (n_tokens more rows).
  *   chronos_b200_ep_send_back_peer  copies block s of part_rows [world, block_rows, hidden] (as many rows as the count word of
  *                                   the metadata received from rank s, read at recv_base) into block `my_rank` of peer_back[s].
  *   chronos_b200_ep_barrier         pads = device array of world pointers to a few peer-writable 32-bit words per rank (word s
