@@ -136,10 +136,12 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         bank_flops = 2 * (2 * cfg.inter) * cfg.hidden + 2 * cfg.hidden * cfg.inter
         healer_flops = 2 * cfg.rank * (cfg.hidden + 2 * cfg.inter) + 2 * cfg.rank * (cfg.inter + cfg.hidden)
         useful = n_layers * (pairs * (bank_flops + healer_flops) + tokens * bank_flops)
-        # this library's kernels per layer: rmsnorm, router (2), dispatch pack (2), metadata unpack, then one pass over the
-        # received rows + home tokens (token_scale, plan, fp16 rows, input transform, healer in, bank pass, SwiGLU/transform,
-        # healer in, bank pass, output term, gate-weighted sum), combine
-        launches_per_layer = 1 + 2 + (3 if world > 1 else 0) + 11 + (1 if world > 1 else 0)
+        # this library's kernels per layer: rmsnorm; router (logits, token scales, top-k); dispatch (plan + rows, and the
+        # barrier with peer stores), metadata unpack; one pass over the received rows + home tokens (token scales, plan +
+        # scatter, fp16 rows, input transform, healer in + operand tile, bank pass, SwiGLU / transform, healer in + operand
+        # tile, bank pass, gather-sum: 14); combine (send back + barrier with peer stores, sum)
+        exchange = 0 if world == 1 else ((3 + 1 + 3) if peer else (2 + 1 + 1))
+        launches_per_layer = 1 + 3 + exchange + 14
         return {
             "metric": "folded_moe_ep_stack_tokens_per_s", "value": tokens / step_s, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": float(ms.item()) / K, "higher_is_better": True, "scaling": "strong",
