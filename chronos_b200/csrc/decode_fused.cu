@@ -316,23 +316,34 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(const Fr
     stamp(3);
     // ---- phase 2: gate_up input transform of every (pair, 128-column block) into the FP4 activation images ----
     const int H = a.L.hidden;
-    const int gw = blockIdx.x * kFrontWarps + warp, n_warps = gridDim.x * kFrontWarps;
     {   // the gate_up pass adds the slices of tiles it splits between two CTAs: its output rows start at zero
         float4* z4 = reinterpret_cast<float4*>(a.p.z1);
         const long n4 = (long)s.n_pairs * 2 * a.L.inter / 4;
         for (long i = (long)blockIdx.x * kFrontThreads + tid; i < n4; i += (long)gridDim.x * kFrontThreads) z4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    const int nst = H / 256;  // warp task = (pair, 256-column stage): a 128-block per half-warp, eight values per lane
-    for (int w = gw; w < s.n_pairs * nst; w += n_warps) {
-        const int pair = w / nst, st = w % nst;
+    // CTA task = a pair: its token's row is staged in shared memory behind the plan (one coalesced read), then warp task =
+    // 256-column stage (a 128-block per half-warp, eight values per lane) with the key gathers served from shared memory
+    const int nst = H / 256;
+    const size_t xb = a.x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4;
+    uint8_t* xrow = fsm + ((sizeof(FrontPlan) + 127) & ~(size_t)127);
+    for (int pair = blockIdx.x; pair < s.n_pairs; pair += gridDim.x) {
         const int t = s.pair_token[pair];
-        float v[8];
-        transform_gu_stage(a.L, a.x, a.x_dtype, t, s.pair_expert[pair], st, lane, v);
+        __syncthreads();  // the previous pair's row is no longer read
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.x) + (size_t)t * H * xb);
+            uint4* dst = reinterpret_cast<uint4*>(xrow);
+            for (int i = tid; i < (int)(H * xb / 16); i += kFrontThreads) dst[i] = src[i];
+        }
         const float gi = 1.0f / a.p.tok_scale[t];
+        __syncthreads();
+        for (int st = warp; st < nst; st += kFrontWarps) {
+            float v[8];
+            transform_gu_stage(a.L, xrow, a.x_dtype, 0, s.pair_expert[pair], st, lane, v);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] *= gi;
-        uint8_t* img = a.p.bq_gu + ((size_t)s.pair_item[pair] * nst + st) * 6144;
-        quantize_stage_fp4x3<32, 8>(v, lane, img, s.pair_pos[pair]);
+            for (int i = 0; i < 8; ++i) v[i] *= gi;
+            uint8_t* img = a.p.bq_gu + ((size_t)s.pair_item[pair] * nst + st) * 6144;
+            quantize_stage_fp4x3<32, 8>(v, lane, img, s.pair_pos[pair]);
+        }
     }
     __syncthreads();
     stamp(4);
@@ -462,8 +473,10 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const chronos_layer
 
 // ---------------------------------------------------------------------------------------------------------------
 static size_t front_smem_bytes(const chronos_layer_t& L, int x_dtype, int tg) {
-    const size_t stage = (size_t)kFrontEpc * L.hidden * 4 + (size_t)tg * L.hidden * (x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
-    return stage > sizeof(FrontPlan) ? stage : sizeof(FrontPlan);
+    const size_t xrow = (size_t)L.hidden * (x_dtype == CHRONOS_DTYPE_BF16 ? 2 : 4);
+    const size_t stage = (size_t)kFrontEpc * L.hidden * 4 + (size_t)tg * xrow;
+    const size_t plan = ((sizeof(FrontPlan) + 127) & ~(size_t)127) + xrow;  // the plan, then one token row for the input transform
+    return stage > plan ? stage : plan;
 }
 
 static int front_token_group(const chronos_layer_t& L, int x_dtype, int n_tokens) {
