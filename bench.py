@@ -252,13 +252,30 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
         layer(batches[i % N_BATCHES])
     torch.cuda.synchronize()
     # ---- device-resident throughput: exactly K steps between two events -----------------------------------------
+    # The steps are replayed from CUDA graphs of N_BATCHES forward calls (the way a serving engine runs its decode steps), so
+    # that the figure is the device's, not this host's launch rate; a shorter graph supplies the K % N_BATCHES steps left over.
+    def capture_forwards(n_steps: int):
+        g, keep = torch.cuda.CUDAGraph(), []
+        with torch.cuda.graph(g):
+            for i in range(n_steps):
+                keep.append(layer(batches[i]))
+        return g, keep
+
+    g_full, keep_full = capture_forwards(N_BATCHES)
+    g_tail, keep_tail = capture_forwards(K % N_BATCHES) if K % N_BATCHES else (None, None)
+    g_full.replay()
+    torch.cuda.synchronize()
+    assert all(torch.equal(keep_full[i], layer(batches[i])) for i in range(N_BATCHES)), "graph replay differs from the eager forward"
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for i in range(K):
-        layer(batches[i % N_BATCHES])
+    for _ in range(K // N_BATCHES):
+        g_full.replay()
+    if g_tail is not None:
+        g_tail.replay()
     e1.record(st)
     torch.cuda.synchronize()
     ms_total = e0.elapsed_time(e1)
+    del g_full, g_tail, keep_full, keep_tail
     assert layer.device_status() == 0, "device status word raised during the timed loop"
 
     # ---- per-stage durations (same steps, events at the stage boundaries inside the C ABI call) ------------------
@@ -278,45 +295,66 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
         layer_bytes += statistics.mean(stats[i % N_BATCHES]["experts"] for i in range(K)) * tail_per_expert
 
     # ---- end to end: pinned host input -> device -> forward -> pinned host output, copies inside the timed region --
-    # The copies run on streams of their own, double-buffered, the way a serving loop feeds a layer: step i + 1's input lands
-    # while step i computes, step i's output leaves while step i + 1 computes. Every step's copies are inside the timed region.
+    # A CUDA graph holds a run of steps - per step the copy of its batch from pinned host memory, the public forward call, the
+    # copy of the result to pinned host memory - with the copies on side streams of the capture, double-buffered: step i + 1's
+    # input lands while step i computes, step i's output leaves while step i + 1 computes (the way a serving loop feeds a
+    # layer). Graphs, so that the measurement does not depend on how fast this host's Python issues three operations per
+    # 170 us step. Every step's copies are inside the timed region; exactly K steps are replayed.
     host_in = [b.cpu().pin_memory() for b in batches]
-    host_out = [torch.empty_like(host_in[0]).pin_memory() for _ in range(2)]
+    host_out = [torch.empty_like(host_in[0]).pin_memory() for _ in range(N_BATCHES)]
     dev_in = [torch.empty_like(batches[0]) for _ in range(2)]
+    for i in range(max(W, 3)):  # eager once: workspace and allocator pools exist before any capture
+        dev_in[0].copy_(host_in[i % N_BATCHES], non_blocking=True)
+        host_out[0].copy_(layer(dev_in[0]), non_blocking=True)
+    torch.cuda.synchronize()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
-    def e2e_loop(n_steps: int) -> None:
-        landed = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]
-        s_in.wait_stream(st)
-        s_out.wait_stream(st)
-        with torch.cuda.stream(s_in):
-            dev_in[0].copy_(host_in[0], non_blocking=True)
-            landed[0].record(s_in)
-        for i in range(n_steps):
-            b = i & 1
-            if i + 1 < n_steps:
-                with torch.cuda.stream(s_in):
+    def capture(n_steps: int):
+        g, keep = torch.cuda.CUDAGraph(), []
+        with torch.cuda.graph(g):
+            cur = torch.cuda.current_stream()
+            s_in.wait_stream(cur)
+            s_out.wait_stream(cur)
+            landed, done = [None, None], [None] * n_steps
+            with torch.cuda.stream(s_in):
+                dev_in[0].copy_(host_in[0], non_blocking=True)
+                landed[0] = torch.cuda.Event()
+                landed[0].record(s_in)
+            for i in range(n_steps):
+                b = i & 1
+                cur.wait_event(landed[b])
+                y = layer(dev_in[b])
+                keep.append(y)  # no block of the capture's pool is reused while a side stream may still read it
+                done[i] = torch.cuda.Event()
+                done[i].record(cur)
+                s_out.wait_event(done[i])
+                with torch.cuda.stream(s_out):
+                    host_out[i].copy_(y, non_blocking=True)
+                if i + 1 < n_steps:
                     if i >= 1:
-                        s_in.wait_event(consumed[b ^ 1])  # the forward of the previous step has read this buffer
-                    dev_in[b ^ 1].copy_(host_in[(i + 1) % N_BATCHES], non_blocking=True)
-                    landed[b ^ 1].record(s_in)
-            st.wait_event(landed[b])
-            y = layer(dev_in[b])
-            consumed[b].record(st)
-            s_out.wait_event(consumed[b])
-            with torch.cuda.stream(s_out):
-                host_out[b].copy_(y, non_blocking=True)
-            y.record_stream(s_out)
-        st.wait_stream(s_out)
-        st.wait_stream(s_in)
+                        s_in.wait_event(done[i - 1])  # the forward that read this input buffer has finished
+                    with torch.cuda.stream(s_in):
+                        dev_in[b ^ 1].copy_(host_in[i + 1], non_blocking=True)
+                        landed[b ^ 1] = torch.cuda.Event()
+                        landed[b ^ 1].record(s_in)
+            cur.wait_stream(s_in)
+            cur.wait_stream(s_out)
+        return g, keep
 
-    e2e_loop(max(W, 2))
+    g_full, keep_full = capture(N_BATCHES)
+    g_tail, keep_tail = capture(K % N_BATCHES) if K % N_BATCHES else (None, None)
+    g_full.replay()
     torch.cuda.synchronize()
+    for i in range(N_BATCHES):  # the replay left every step's result in its pinned host buffer
+        assert torch.equal(host_out[i], layer(batches[i]).cpu()), "graph replay differs from the eager forward"
     e0.record(st)
-    e2e_loop(K)
+    for _ in range(K // N_BATCHES):
+        g_full.replay()
+    if g_tail is not None:
+        g_tail.replay()
     e1.record(st)
     torch.cuda.synchronize()
+    del g_full, g_tail, keep_full, keep_tail
     ms_e2e = e0.elapsed_time(e1)
     clocks = sampler.stop() if own_sampler else None
 
@@ -356,6 +394,7 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
                    "top_k": cfg.top_k, "inter": cfg.inter, "fold_factor": cfg.group_size, "healer_rank": cfg.rank,
                    "streams": streams, "tokens_per_stream": TOKENS_PER_STREAM, "activations": "bf16", "router": cfg.router,
                    "l2_policy": f"each step streams {layer_bytes / 1e6:.0f} MB of banks (> 126 MB L2) and batches rotate over {N_BATCHES} routings",
+                   "launch": f"timed steps replayed from CUDA graphs of {N_BATCHES} forward calls (stage durations: eager calls with events)",
                    "tail_lattice_bits": args.tail,
                    "distinct_slots_per_step": statistics.mean(s["slots"] for s in stats),
                    "distinct_slots_by_routing": [s["slots"] for s in stats],
@@ -363,7 +402,7 @@ def run_decode(args, sampler=None, with_cpu_baseline=True) -> dict:
                    "top8_overlap_within_stream": round(statistics.mean(s["overlap"] for s in stats), 3)},
         "e2e": {"value": n_tok / (ms_e2e * 1e-3 / K), "unit": "tokens/s", "h2d_bytes_per_step": n_tok * cfg.hidden * 2,
                 "d2h_bytes_per_step": n_tok * cfg.hidden * 2,
-                "copies": "every step's input and output copy inside the timed region, on copy streams, double-buffered"},
+                "copies": "every step's input and output copy inside the timed region; CUDA graphs of 8 steps, copies on side streams, double-buffered"},
         "gpu_launches": launches * K,
         "clocks": clocks,
         "roofline": {"bound": "hbm", "kernel": f"{bank_kernel} (gate_up pass" + (", healer product in its side warps)" if fused else ")"),
