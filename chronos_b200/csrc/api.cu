@@ -212,7 +212,7 @@ static int fused_decode_forward(const chronos_layer_t& L, const void* x, int x_d
     stage_mark(5, st);
     if (int rc = launch_bank_fp4_fused(L, 1, p, x, x_dtype, st)) return rc;
     stage_mark(6, st);
-    int rc = launch_decode_combine(L, p, ids_in != nullptr ? gates_in : p.gates, n_tokens, with_shared, y, y_dtype, st);
+    int rc = launch_decode_combine(L, p, ids_in != nullptr ? ids_in : p.ids, ids_in != nullptr ? gates_in : p.gates, n_tokens, with_shared, y, y_dtype, st);
     if (!rc && shared_is_fp8(L)) rc = launch_shared_fp8(L, x, x_dtype, p, shared_first, shared_count, y, y_dtype, st);
     stage_mark(7, st);
     return rc;

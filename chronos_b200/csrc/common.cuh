@@ -272,8 +272,8 @@ bool decode_fused_fits(const chronos_layer_t& L, int x_dtype, int n_tokens, cons
 int launch_decode_front(const chronos_layer_t& L, const void* x, int x_dtype, int n_tokens, const int32_t* ids_in,
                         int with_shared, const Plan& p, cudaStream_t st);
 int launch_decode_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st);
-int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
-                          int y_dtype, cudaStream_t st);
+int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const int32_t* ids, const float* gates, int n_tokens, int with_shared,
+                          void* y, int y_dtype, cudaStream_t st);
 int launch_bank_fp4_fused(const chronos_layer_t& L, int stage /*0 gu, 1 down*/, const Plan& p, const void* x, int x_dtype, cudaStream_t st);
 // expert-parallel dispatch / combine helpers (csrc/ep_kernels.cu)
 int launch_ep_pack(const void* x, int x_dtype, const int32_t* ids, const float* gates, int n_tokens, int top_k, int hidden,

@@ -439,8 +439,8 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(const chronos_l
 // Combine: y[t, i] = sum_j gate[t, j] * (beta_d * r_s1[i] * y1[p_j, r_inv[i]] + heal_dn[p_j, i]) (+ shared expert row),
 // j = 0 .. top_k - 1 in that order. One block per (token, 128 output rows), thread = row.
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) decode_combine_kernel(const chronos_layer_t L, const Plan p, const float* __restrict__ gates,
-                                                             int with_shared, void* __restrict__ y, int y_dtype) {
+__global__ void __launch_bounds__(128) decode_combine_kernel(const chronos_layer_t L, const Plan p, const int32_t* __restrict__ ids,
+                                                             const float* __restrict__ gates, int with_shared, void* __restrict__ y, int y_dtype) {
     const int t = blockIdx.x, i = blockIdx.y * 128 + threadIdx.x;
     const int H = L.hidden, k = L.top_k;
     float acc = 0.0f;
@@ -453,8 +453,8 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const chronos_layer
             gt[jj] = 0.0f;
             if (j >= k) continue;
             const int pos = p.pos_of[t * k + j];
+            const int e = ids[t * k + j];  // the entry's expert straight from the routing list: not a second hop after pos
             if (pos < 0) continue;
-            const int e = p.pair_expert[pos];
             const uint32_t ro = L.dn_rout[(size_t)e * H + i];
             const float v = p.y1[(size_t)pos * H + (ro & 0x7fffu)];
             term[jj] = fmaf(L.dn_beta[e], (ro >> 15) ? -v : v, p.heal_dn[(size_t)pos * H + i]);
@@ -537,10 +537,11 @@ int launch_decode_mid(const chronos_layer_t& L, const Plan& p, cudaStream_t st) 
     return check_launch("decode_mid");
 }
 
-int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const float* gates, int n_tokens, int with_shared, void* y,
-                          int y_dtype, cudaStream_t st) {
+int launch_decode_combine(const chronos_layer_t& L, const Plan& p, const int32_t* ids, const float* gates, int n_tokens, int with_shared,
+                          void* y, int y_dtype, cudaStream_t st) {
     if (n_tokens <= 0) return CHRONOS_OK;
-    decode_combine_kernel<<<dim3((unsigned)n_tokens, (unsigned)(L.hidden / 128)), 128, 0, st>>>(L, p, gates, with_shared && L.shared_inter > 0, y, y_dtype);
+    decode_combine_kernel<<<dim3((unsigned)n_tokens, (unsigned)(L.hidden / 128)), 128, 0, st>>>(L, p, ids, gates, with_shared && L.shared_inter > 0, y,
+                                                                                                y_dtype);
     return check_launch("decode_combine");
 }
 
