@@ -362,14 +362,26 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(const chronos_l
     __shared__ float red[kMidThreads / 32];
     __shared__ float g_s;
     const int pair = blockIdx.x;
-    if (pair >= p.counters[1]) return;
+    // everything that depends on the pair alone is requested at once (the table rows of pairs past the count exist, they
+    // just hold old values): the kernel is a chain of memory round trips, and each one taken out of it is ~0.7 us
+    const int n_pairs = p.counters[1];
+    const int e = p.pair_expert[pair];
+    const int item = p.pair_item[pair], pos = p.pair_pos[pair];
+    if (pair >= n_pairs) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int I = L.inter, E = L.n_experts;
+    // the key entries of the down-input transform of this warp's first stage, fetched now and used after the two barriers
+    uint4 ce0 = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t sw0 = 0u;
+    if (e < E && warp < I / 256) {
+        const int half = lane >> 4, jl = lane & 15;
+        ce0 = *reinterpret_cast<const uint4*>(L.dn_cin + (size_t)e * I + warp * 256 + half * 128 + jl * 8);
+        sw0 = L.dn_cs2[(size_t)e * (I / 32) + warp * 8 + half * 4 + (jl >> 2)] >> ((jl & 3) * 8);
+    }
     {   // the down pass adds the slices of tiles it splits between two CTAs: this pair's output row starts at zero
         float4* y4 = reinterpret_cast<float4*>(p.y1 + (size_t)pair * L.hidden);
         for (int i = tid; i < L.hidden / 4; i += kMidThreads) y4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    const int e = p.pair_expert[pair];
     const float* z1 = p.z1 + (size_t)pair * 2 * I;
     float ss = 0.0f;
     if (e >= E) {  // shared expert: rows in natural order, no healer
@@ -424,11 +436,24 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(const chronos_l
         const float s4[4] = {a4.x * gi, a4.y * gi, a4.z * gi, a4.w * gi};
         store_half4(p.ac + (size_t)pair * I + i, s4);
     }
-    uint8_t* img0 = p.bq_dn + (size_t)p.pair_item[pair] * (I / 256) * 6144;
-    const int pos = p.pair_pos[pair];
+    uint8_t* img0 = p.bq_dn + (size_t)item * (I / 256) * 6144;
     for (int st = warp; st < I / 256; st += kMidThreads / 32) {  // a warp per 256-column stage
         float v[8];
-        transform_dn_stage(L, act_s, e, st, lane, v);
+        if (st == warp && e < E) {  // first stage of the warp: its key entries are already here
+            const uint32_t ent[8] = {ce0.x & 0xffffu, ce0.x >> 16, ce0.y & 0xffffu, ce0.y >> 16,
+                                     ce0.z & 0xffffu, ce0.z >> 16, ce0.w & 0xffffu, ce0.w >> 16};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float av = act_s[ent[i] & 0x7fffu];
+                v[i] = (ent[i] >> 15) ? -av : av;
+            }
+            fwht128_half(v, lane);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if ((sw0 >> i) & 1u) v[i] = -v[i];
+        } else {
+            transform_dn_stage(L, act_s, e, st, lane, v);
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] *= gi;
         quantize_stage_fp4x3<32, 8>(v, lane, img0 + (size_t)st * 6144, pos);
