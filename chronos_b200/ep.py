@@ -127,6 +127,7 @@ class ExpertParallelMoE:
         self.pack_fn = pack_fn or self._pack_cuda
         self.compute_fn = compute_fn or self._compute_cuda
         self.combine_fn = combine_fn or self._combine_cuda
+        self.out_dtype = torch.float32  # dtype of forward()'s result (fp32 sums rounded once); a stack sets its activations' dtype
         self.phase_events = None   # set to [] to record (name, start, end) CUDA events of the next forward
         self._checked: set[tuple] = set()
         # peer stores over NVLink instead of the all-to-all (CUDA ranks of one box with symmetric memory; every rank must
@@ -206,10 +207,10 @@ class ExpertParallelMoE:
     def _combine_cuda(self, back_rows, slot_of, shared_rows, capacity):
         w, block_rows, h = back_rows.shape
         tl = slot_of.shape[0]
-        y = torch.empty((tl, h), dtype=torch.float32, device=back_rows.device)
+        y = torch.empty((tl, h), dtype=self.out_dtype, device=back_rows.device)
         _lib.check(_lib.lib().chronos_b200_ep_combine(back_rows.data_ptr(), _DTYPES[back_rows.dtype], slot_of.data_ptr(),
                                                     shared_rows.data_ptr() if shared_rows is not None else None, tl, h, w, capacity,
-                                                    y.data_ptr(), _lib.DTYPE_F32, block_rows, torch.cuda.current_stream().cuda_stream))
+                                                    y.data_ptr(), _DTYPES[self.out_dtype], block_rows, torch.cuda.current_stream().cuda_stream))
         return y
 
     def _peer_exchange(self, x: torch.Tensor, capacity: int) -> Optional[_PeerExchange]:
@@ -285,7 +286,7 @@ class ExpertParallelMoE:
     # -- the layer ------------------------------------------------------------------------------------------------------
     @torch.no_grad()
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
-        """x_local [Tl, H] (same Tl on every rank) -> y_local fp32 [Tl, H]."""
+        """x_local [Tl, H] (same Tl on every rank) -> y_local [Tl, H] in `out_dtype` (fp32 unless a stack set its own)."""
         tl, h = x_local.shape
         x_local = x_local.contiguous()
         capacity = block_capacity(tl, self.world, self.cfg.top_k, self.capacity_factor)
@@ -294,7 +295,7 @@ class ExpertParallelMoE:
             ids, gates = self.route_fn(x_local)
         if self.world == 1 and self.layer is not None:  # every expert is local: nothing to exchange
             with self._mark("routed_experts"):
-                return self.layer.routed_forward(x_local, ids, gates, with_shared=self.layer.n_shared_experts > 0, out_dtype=torch.float32)
+                return self.layer.routed_forward(x_local, ids, gates, with_shared=self.layer.n_shared_experts > 0, out_dtype=self.out_dtype)
         ex = self._peer_exchange(x_local, capacity)
         if ex is not None:
             return self._forward_peer(ex, x_local, ids, gates, capacity)
@@ -361,6 +362,8 @@ class ExpertParallelStack:
         y = None
         for lay in self.layers:
             x = residual_rmsnorm(h_local, y, None, self.eps)   # h += y of the previous layer; x = norm(h)
+            if h_local.dtype in (torch.bfloat16, torch.float32) and h_local.device.type == "cuda":
+                lay.out_dtype = h_local.dtype                   # the layer's last kernel rounds to the stack's dtype itself
             y = lay(x).to(h_local.dtype)
         residual_rmsnorm(h_local, y, None, self.eps)           # last residual add
         return h_local

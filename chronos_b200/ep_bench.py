@@ -115,6 +115,7 @@ def run(args, n_layers: int, tokens: int, layer_kw: dict, sampler_cls=None) -> d
         from . import _lib
         from .moe import residual_rmsnorm
         lay0 = layers[0]
+        lay0.out_dtype = torch.float32  # the parity record compares the fp32 sums, not the stack's bf16 rounding of them
         x0 = residual_rmsnorm(h0.clone(), None, None, 1e-6)  # what layer 0 sees in the stack
         ids0, gates0 = lay0.route_fn(x0)
         ids_all = torch.empty((world * tl, cfg.top_k), dtype=ids0.dtype, device=dev)

@@ -55,6 +55,7 @@ def _worker(rank: int, world: int, port: int, ret, peer: bool):
 
         x0 = residual_rmsnorm(h_all[rank * tl:(rank + 1) * tl].clone(), None, None, 1e-6)
         ids0, gates0 = layers[0].route_fn(x0)
+        layers[0].out_dtype = torch.float32  # the stack above had switched its layers to its own dtype
         y0 = layers[0](x0)
         par = layer_parity(cfg, layers[0], 3, x0, y0, ids0, gates0, dev, n_sample=6)
         from chronos_b200.ep import _PEER_EXCHANGES
